@@ -1,0 +1,114 @@
+"""ctypes binding of the C-ABI library ``_lib/libpymsst_b200.so``.
+
+The library is the product: every fused op in this package calls it, and there
+is no fallback.  If the library is missing the import of an op raises
+:class:`FusedKernelUnavailable`, mirroring the reference's loader error
+(src/pymsst/training/fused_extension.py:11-19), but it is never swallowed.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libpymsst_b200.so"
+
+F32, F16, BF16 = 0, 1, 2
+_DTYPE_CODES = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16}
+
+_p = ctypes.c_void_p
+_i64 = ctypes.c_int64
+_i = ctypes.c_int
+_pp = ctypes.POINTER(ctypes.c_void_p)
+_pi64 = ctypes.POINTER(ctypes.c_int64)
+
+# name -> (restype, argtypes).  Kept in the order of include/pymsst_b200.h.
+SIGNATURES: dict[str, tuple[object, list[object]]] = {
+    "pmb_version": (ctypes.c_char_p, []),
+    "pmb_last_error": (ctypes.c_char_p, []),
+    "pmb_rms_norm_forward": (_i, [_p, _p, _p, _p, _p, _i64, _i64, _i, _i, _i, _p]),
+    "pmb_rms_norm_backward_workspace_size": (_i64, [_i64, _i64]),
+    "pmb_rms_norm_backward": (_i, [_p, _p, _i, _p, _p, _p, _p, _i64, _i64, _i, _i, _i, _i, _p, _i64, _p]),
+    "pmb_rotary_forward": (_i, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i, _p]),
+    "pmb_rotary_backward": (_i, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i, _p]),
+}
+
+
+class FusedKernelUnavailable(RuntimeError):
+    """The sm_100a kernel library cannot be used (not built, or no CUDA device)."""
+
+
+class KernelError(RuntimeError):
+    """A C-ABI entry point returned a non-zero status."""
+
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+
+def library(path: Path | None = None) -> ctypes.CDLL:
+    """Load (once) and return the C-ABI library with typed entry points."""
+    global _lib
+    with _lock:
+        if _lib is not None and path is None:
+            return _lib
+        target = Path(path) if path is not None else LIB_PATH
+        if not target.is_file():
+            raise FusedKernelUnavailable(
+                f"{target} is missing; build it with `python -m pymsst_b200.build`"
+            )
+        lib = ctypes.CDLL(str(target))
+        for name, (restype, argtypes) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = restype
+            fn.argtypes = argtypes
+        if path is None:
+            _lib = lib
+        return lib
+
+
+def dtype_code(dtype: torch.dtype) -> int:
+    try:
+        return _DTYPE_CODES[dtype]
+    except KeyError as exc:
+        raise TypeError(f"unsupported dtype {dtype}; expected float32, float16 or bfloat16") from exc
+
+
+def stream_handle(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def check(status: int, name: str) -> None:
+    if status != 0:
+        message = library().pmb_last_error().decode("utf-8", "replace")
+        raise KernelError(f"{name} failed with status {status}: {message}")
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def call(name: str, *args) -> None:
+    """Call a status-returning entry point and raise on failure."""
+    check(getattr(library(), name)(*args), name)
+
+
+def require_cuda(*tensors: torch.Tensor | None, name: str) -> torch.device:
+    """Fail loudly unless every tensor is on one CUDA device."""
+    device = None
+    for t in tensors:
+        if t is None:
+            continue
+        if t.device.type != "cuda":
+            raise FusedKernelUnavailable(
+                f"{name}: tensors must be CUDA tensors (got {t.device}); this package has no CPU path"
+            )
+        if device is None:
+            device = t.device
+        elif t.device != device:
+            raise ValueError(f"{name}: tensors are on different devices ({device} and {t.device})")
+    if device is None:
+        raise ValueError(f"{name}: no tensor arguments")
+    return device

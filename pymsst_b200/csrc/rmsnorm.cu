@@ -1,0 +1,410 @@
+// Transformer RMSNorm (F.normalize(x) * sqrt(D) * gamma) forward and backward.
+//
+// One warp owns one row at a time; a lane keeps its slice of the row in
+// registers as 16-byte vectors (8 x 16-bit or 4 x fp32 elements), so x is read
+// exactly once, and the row sum of squares is a warp shuffle reduction.  The
+// backward produces grad_gamma deterministically: each CTA reduces its rows
+// into one fp32 partial row in the caller's workspace, and a second launch
+// sums the partials column-wise (coalesced).  Reference semantics:
+// src/pymsst/training/cuda/fused_band_split.cu:1211-1315 (formulas at
+// :1237-1247 and :1263-1286).
+#include "common.cuh"
+
+namespace pmb {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kMaxBwdBlocks = 4 * 148;
+
+__device__ __forceinline__ float ld_dyn(const void* p, int64_t i, int code) {
+  switch (code) {
+    case PMB_FLOAT16:
+      return __half2float(static_cast<const __half*>(p)[i]);
+    case PMB_BFLOAT16:
+      return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+    default:
+      return static_cast<const float*>(p)[i];
+  }
+}
+
+__device__ __forceinline__ void st_dyn(void* p, int64_t i, int code, float v) {
+  switch (code) {
+    case PMB_FLOAT16:
+      static_cast<__half*>(p)[i] = __float2half_rn(v);
+      break;
+    case PMB_BFLOAT16:
+      static_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+      break;
+    default:
+      static_cast<float*>(p)[i] = v;
+  }
+}
+
+template <typename T, int V>
+struct alignas((sizeof(T) * V) < 16 ? (sizeof(T) * V) : 16) Pack {
+  T v[V];
+};
+
+// ---------------------------------------------------------------- forward
+template <typename Tx, typename To, int V, int NJ>
+__global__ void __launch_bounds__(kThreads)
+    rms_fwd_vec(const Tx* __restrict__ x, const void* __restrict__ gamma, int gcode,
+                To* __restrict__ out, To* __restrict__ normed, float* __restrict__ inv_norm,
+                int64_t rows, int dim) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
+  const int64_t nwarps = (int64_t)gridDim.x * kWarps;
+  const int nvec = dim / V;
+  const float scale = sqrtf((float)dim);
+
+  float g[NJ][V];
+#pragma unroll
+  for (int j = 0; j < NJ; ++j) {
+    const int vi = j * 32 + lane;
+#pragma unroll
+    for (int e = 0; e < V; ++e) g[j][e] = vi < nvec ? ld_dyn(gamma, (int64_t)vi * V + e, gcode) : 0.f;
+  }
+
+  for (int64_t r = warp; r < rows; r += nwarps) {
+    const Tx* xr = x + r * dim;
+    float v[NJ][V];
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) {
+      const int vi = j * 32 + lane;
+      if (vi < nvec) {
+        const Pack<Tx, V> p = *reinterpret_cast<const Pack<Tx, V>*>(xr + (int64_t)vi * V);
+#pragma unroll
+        for (int e = 0; e < V; ++e) {
+          v[j][e] = Elem<Tx>::to_f(p.v[e]);
+          ss += v[j][e] * v[j][e];
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < V; ++e) v[j][e] = 0.f;
+      }
+    }
+    ss = warp_sum(ss);
+    const float inv = 1.0f / fmaxf(sqrtf(ss), 1.0e-12f);
+    if (lane == 0) inv_norm[r] = inv;
+    const float k = inv * scale;
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) {
+      const int vi = j * 32 + lane;
+      if (vi < nvec) {
+        Pack<To, V> po, pn;
+#pragma unroll
+        for (int e = 0; e < V; ++e) {
+          const float n = v[j][e] * k;
+          pn.v[e] = Elem<To>::from_f(n);
+          po.v[e] = Elem<To>::from_f(n * g[j][e]);
+        }
+        *reinterpret_cast<Pack<To, V>*>(out + r * dim + (int64_t)vi * V) = po;
+        if (normed != nullptr) *reinterpret_cast<Pack<To, V>*>(normed + r * dim + (int64_t)vi * V) = pn;
+      }
+    }
+  }
+}
+
+// Any dim / alignment: the row is streamed twice instead of held in registers.
+template <typename Tx, typename To>
+__global__ void __launch_bounds__(kThreads)
+    rms_fwd_generic(const Tx* __restrict__ x, const void* __restrict__ gamma, int gcode,
+                    To* __restrict__ out, To* __restrict__ normed, float* __restrict__ inv_norm,
+                    int64_t rows, int dim) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
+  const int64_t nwarps = (int64_t)gridDim.x * kWarps;
+  const float scale = sqrtf((float)dim);
+  for (int64_t r = warp; r < rows; r += nwarps) {
+    const Tx* xr = x + r * dim;
+    float ss = 0.f;
+    for (int c = lane; c < dim; c += 32) {
+      const float v = Elem<Tx>::to_f(xr[c]);
+      ss += v * v;
+    }
+    ss = warp_sum(ss);
+    const float inv = 1.0f / fmaxf(sqrtf(ss), 1.0e-12f);
+    if (lane == 0) inv_norm[r] = inv;
+    for (int c = lane; c < dim; c += 32) {
+      const float n = Elem<Tx>::to_f(xr[c]) * inv * scale;
+      out[r * dim + c] = Elem<To>::from_f(n * ld_dyn(gamma, c, gcode));
+      if (normed != nullptr) normed[r * dim + c] = Elem<To>::from_f(n);
+    }
+  }
+}
+
+// --------------------------------------------------------------- backward
+template <typename Tg, typename Tdx, int V, int NJ>
+__global__ void __launch_bounds__(kThreads)
+    rms_bwd_vec(const Tg* __restrict__ dy, const Tg* __restrict__ saved, int saved_is_input,
+                const float* __restrict__ inv_norm, const void* __restrict__ gamma, int gcode,
+                Tdx* __restrict__ dx, float* __restrict__ partial, int64_t rows, int dim) {
+  extern __shared__ float red[];  // [kWarps][dim]
+  const int lane = threadIdx.x & 31;
+  const int wib = threadIdx.x >> 5;
+  const int64_t warp = (int64_t)blockIdx.x * kWarps + wib;
+  const int64_t nwarps = (int64_t)gridDim.x * kWarps;
+  const int nvec = dim / V;
+  const float scale = sqrtf((float)dim);
+
+  float g[NJ][V], acc[NJ][V];
+#pragma unroll
+  for (int j = 0; j < NJ; ++j) {
+    const int vi = j * 32 + lane;
+#pragma unroll
+    for (int e = 0; e < V; ++e) {
+      g[j][e] = vi < nvec ? ld_dyn(gamma, (int64_t)vi * V + e, gcode) : 0.f;
+      acc[j][e] = 0.f;
+    }
+  }
+
+  for (int64_t r = warp; r < rows; r += nwarps) {
+    const float inv = inv_norm[r];
+    const float nk = saved_is_input ? inv * scale : 1.0f;
+    float gd[NJ][V], nv[NJ][V];
+    float dot = 0.f;
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) {
+      const int vi = j * 32 + lane;
+      if (vi < nvec) {
+        const Pack<Tg, V> pd = *reinterpret_cast<const Pack<Tg, V>*>(dy + r * dim + (int64_t)vi * V);
+        const Pack<Tg, V> ps = *reinterpret_cast<const Pack<Tg, V>*>(saved + r * dim + (int64_t)vi * V);
+#pragma unroll
+        for (int e = 0; e < V; ++e) {
+          const float d = Elem<Tg>::to_f(pd.v[e]);
+          const float n = Elem<Tg>::to_f(ps.v[e]) * nk;
+          nv[j][e] = n;
+          gd[j][e] = d * g[j][e];
+          dot += gd[j][e] * n;
+          acc[j][e] += d * n;
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < V; ++e) gd[j][e] = nv[j][e] = 0.f;
+      }
+    }
+    dot = warp_sum(dot);
+    if (dx != nullptr) {
+      const float ds = dot / scale;
+#pragma unroll
+      for (int j = 0; j < NJ; ++j) {
+        const int vi = j * 32 + lane;
+        if (vi < nvec) {
+          Pack<Tdx, V> p;
+#pragma unroll
+          for (int e = 0; e < V; ++e) p.v[e] = Elem<Tdx>::from_f(inv * (gd[j][e] * scale - nv[j][e] * ds));
+          *reinterpret_cast<Pack<Tdx, V>*>(dx + r * dim + (int64_t)vi * V) = p;
+        }
+      }
+    }
+  }
+
+#pragma unroll
+  for (int j = 0; j < NJ; ++j) {
+    const int vi = j * 32 + lane;
+    if (vi < nvec) {
+#pragma unroll
+      for (int e = 0; e < V; ++e) red[wib * dim + vi * V + e] = acc[j][e];
+    }
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < dim; c += kThreads) {
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) s += red[w * dim + c];
+    partial[(int64_t)blockIdx.x * dim + c] = s;
+  }
+}
+
+template <typename Tg, typename Tdx>
+__global__ void __launch_bounds__(kThreads)
+    rms_bwd_generic(const Tg* __restrict__ dy, const Tg* __restrict__ saved, int saved_is_input,
+                    const float* __restrict__ inv_norm, const void* __restrict__ gamma, int gcode,
+                    Tdx* __restrict__ dx, float* __restrict__ partial, int64_t rows, int dim) {
+  // Column-parallel partials: each thread owns columns c = tid, tid+256, ...
+  // and walks this CTA's rows; the row dot product is a CTA reduction.
+  __shared__ float sdot[kWarps];
+  const float scale = sqrtf((float)dim);
+  const int lane = threadIdx.x & 31;
+  const int wib = threadIdx.x >> 5;
+  for (int c = threadIdx.x; c < dim; c += kThreads) partial[(int64_t)blockIdx.x * dim + c] = 0.f;
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const float inv = inv_norm[r];
+    const float nk = saved_is_input ? inv * scale : 1.0f;
+    float dot = 0.f;
+    for (int c = threadIdx.x; c < dim; c += kThreads) {
+      const float d = Elem<Tg>::to_f(dy[r * dim + c]);
+      const float n = Elem<Tg>::to_f(saved[r * dim + c]) * nk;
+      dot += d * ld_dyn(gamma, c, gcode) * n;
+      partial[(int64_t)blockIdx.x * dim + c] += d * n;
+    }
+    dot = warp_sum(dot);
+    if (lane == 0) sdot[wib] = dot;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) tot += sdot[w];
+    __syncthreads();
+    if (dx != nullptr) {
+      const float ds = tot / scale;
+      for (int c = threadIdx.x; c < dim; c += kThreads) {
+        const float d = Elem<Tg>::to_f(dy[r * dim + c]);
+        const float n = Elem<Tg>::to_f(saved[r * dim + c]) * nk;
+        dx[r * dim + c] = Elem<Tdx>::from_f(inv * (d * ld_dyn(gamma, c, gcode) * scale - n * ds));
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kThreads)
+    column_sum_kernel(const float* __restrict__ partial, int blocks, int dim, void* __restrict__ out,
+                      int out_code) {
+  const int c = blockIdx.x * kThreads + threadIdx.x;
+  if (c >= dim) return;
+  float s = 0.f;
+  for (int b = 0; b < blocks; ++b) s += partial[(int64_t)b * dim + c];
+  st_dyn(out, c, out_code, s);
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int grid_for_rows(int64_t rows, int64_t cap) {
+  int64_t blocks = (rows + kWarps - 1) / kWarps;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  return (int)blocks;
+}
+
+template <typename Tx, typename To>
+int launch_fwd(const void* x, const void* gamma, int gcode, void* out, void* normed, float* inv,
+               int64_t rows, int64_t dim, cudaStream_t stream) {
+  constexpr int V = 16 / sizeof(Tx);
+  const int grid = grid_for_rows(rows, (int64_t)num_sms() * 16);
+  const int64_t nvec = dim / V;
+  const bool vec_ok = dim % V == 0 && aligned16(x) && aligned16(out) && (normed == nullptr || aligned16(normed)) &&
+                      (dim * (int64_t)sizeof(Tx)) % 16 == 0 && (dim * (int64_t)sizeof(To)) % 16 == 0;
+  const int nj = (int)((nvec + 31) / 32);
+  const Tx* xp = static_cast<const Tx*>(x);
+  To* op = static_cast<To*>(out);
+  To* np = static_cast<To*>(normed);
+  if (vec_ok && nj * 32 * V <= 1024) {
+    if (nj <= 1)
+      rms_fwd_vec<Tx, To, V, 1><<<grid, kThreads, 0, stream>>>(xp, gamma, gcode, op, np, inv, rows, (int)dim);
+    else if (nj <= 2)
+      rms_fwd_vec<Tx, To, V, 2><<<grid, kThreads, 0, stream>>>(xp, gamma, gcode, op, np, inv, rows, (int)dim);
+    else if (nj <= 4)
+      rms_fwd_vec<Tx, To, V, 4><<<grid, kThreads, 0, stream>>>(xp, gamma, gcode, op, np, inv, rows, (int)dim);
+    else if constexpr (V == 4)
+      rms_fwd_vec<Tx, To, V, 8><<<grid, kThreads, 0, stream>>>(xp, gamma, gcode, op, np, inv, rows, (int)dim);
+  } else {
+    rms_fwd_generic<Tx, To><<<grid, kThreads, 0, stream>>>(xp, gamma, gcode, op, np, inv, rows, (int)dim);
+  }
+  PMB_CHECK_LAUNCH("pmb_rms_norm_forward");
+  return PMB_OK;
+}
+
+int bwd_blocks(int64_t rows) { return grid_for_rows(rows, kMaxBwdBlocks); }
+
+template <typename Tg, typename Tdx>
+int launch_bwd(const void* dy, const void* saved, int saved_is_input, const float* inv, const void* gamma,
+               int gcode, void* dx, void* dgamma, int dgcode, int64_t rows, int64_t dim, float* partial,
+               cudaStream_t stream) {
+  constexpr int V = 16 / sizeof(Tg);
+  const int grid = bwd_blocks(rows);
+  const int64_t nvec = dim / V;
+  const bool vec_ok = dim % V == 0 && aligned16(dy) && aligned16(saved) && (dx == nullptr || aligned16(dx)) &&
+                      (dim * (int64_t)sizeof(Tg)) % 16 == 0 && (dim * (int64_t)sizeof(Tdx)) % 16 == 0;
+  const int nj = (int)((nvec + 31) / 32);
+  const Tg* dyp = static_cast<const Tg*>(dy);
+  const Tg* sp = static_cast<const Tg*>(saved);
+  Tdx* dxp = static_cast<Tdx*>(dx);
+  const size_t smem = (size_t)kWarps * dim * sizeof(float);
+  // Register budget: at most 1024 elements of a row per warp in the vector path.
+  if (vec_ok && nj * 32 * V <= 1024 && smem <= 48 * 1024) {
+    if (nj <= 1)
+      rms_bwd_vec<Tg, Tdx, V, 1><<<grid, kThreads, smem, stream>>>(dyp, sp, saved_is_input, inv, gamma, gcode, dxp,
+                                                                   partial, rows, (int)dim);
+    else if (nj <= 2)
+      rms_bwd_vec<Tg, Tdx, V, 2><<<grid, kThreads, smem, stream>>>(dyp, sp, saved_is_input, inv, gamma, gcode, dxp,
+                                                                   partial, rows, (int)dim);
+    else if (nj <= 4)
+      rms_bwd_vec<Tg, Tdx, V, 4><<<grid, kThreads, smem, stream>>>(dyp, sp, saved_is_input, inv, gamma, gcode, dxp,
+                                                                   partial, rows, (int)dim);
+    else if constexpr (V == 4)
+      rms_bwd_vec<Tg, Tdx, V, 8><<<grid, kThreads, smem, stream>>>(dyp, sp, saved_is_input, inv, gamma, gcode, dxp,
+                                                                   partial, rows, (int)dim);
+  } else {
+    rms_bwd_generic<Tg, Tdx><<<grid, kThreads, 0, stream>>>(dyp, sp, saved_is_input, inv, gamma, gcode, dxp,
+                                                            partial, rows, (int)dim);
+  }
+  PMB_CHECK_LAUNCH("pmb_rms_norm_backward");
+  if (dgamma != nullptr) {
+    column_sum_kernel<<<(int)((dim + kThreads - 1) / kThreads), kThreads, 0, stream>>>(partial, grid, (int)dim,
+                                                                                       dgamma, dgcode);
+    PMB_CHECK_LAUNCH("pmb_rms_norm_backward(grad_gamma)");
+  }
+  return PMB_OK;
+}
+
+bool valid_code(int c) { return c == PMB_FLOAT32 || c == PMB_FLOAT16 || c == PMB_BFLOAT16; }
+
+}  // namespace
+}  // namespace pmb
+
+using namespace pmb;
+
+extern "C" int pmb_rms_norm_forward(const void* x, const void* gamma, void* out, void* normed, float* inv_norm,
+                                    int64_t rows, int64_t dim, int x_dtype, int gamma_dtype, int out_dtype,
+                                    void* stream) {
+  clear_error();
+  PMB_REQUIRE(rows >= 0 && dim > 0 && dim <= (1 << 20), "pmb_rms_norm_forward: bad shape rows=%lld dim=%lld",
+              (long long)rows, (long long)dim);
+  PMB_REQUIRE(valid_code(gamma_dtype), "pmb_rms_norm_forward: unsupported gamma dtype %d", gamma_dtype);
+  if (rows == 0) return PMB_OK;
+  PMB_REQUIRE(x && gamma && out && inv_norm, "pmb_rms_norm_forward: NULL tensor argument");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return PMB_DISPATCH(x_dtype, Tx, "pmb_rms_norm_forward", [&] {
+    return PMB_DISPATCH(out_dtype, To, "pmb_rms_norm_forward", [&] {
+      return launch_fwd<Tx, To>(x, gamma, gamma_dtype, out, normed, inv_norm, rows, dim, s);
+    });
+  });
+}
+
+extern "C" int64_t pmb_rms_norm_backward_workspace_size(int64_t rows, int64_t dim) {
+  if (rows <= 0 || dim <= 0) return 0;
+  return (int64_t)bwd_blocks(rows) * dim * (int64_t)sizeof(float);
+}
+
+extern "C" int pmb_rms_norm_backward(const void* grad_out, const void* saved, int saved_is_input,
+                                     const float* inv_norm, const void* gamma, void* grad_x, void* grad_gamma,
+                                     int64_t rows, int64_t dim, int grad_dtype, int gamma_dtype, int grad_x_dtype,
+                                     int grad_gamma_dtype, void* workspace, int64_t workspace_bytes, void* stream) {
+  clear_error();
+  PMB_REQUIRE(rows >= 0 && dim > 0 && dim <= (1 << 20), "pmb_rms_norm_backward: bad shape rows=%lld dim=%lld",
+              (long long)rows, (long long)dim);
+  PMB_REQUIRE(valid_code(gamma_dtype) && valid_code(grad_gamma_dtype),
+              "pmb_rms_norm_backward: unsupported gamma/grad_gamma dtype");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (rows == 0) {
+    if (grad_gamma != nullptr) {
+      PMB_CHECK_CUDA(cudaMemsetAsync(grad_gamma, 0, dim * dtype_size(grad_gamma_dtype), s), "pmb_rms_norm_backward");
+    }
+    return PMB_OK;
+  }
+  PMB_REQUIRE(grad_out && saved && inv_norm && gamma, "pmb_rms_norm_backward: NULL tensor argument");
+  const int64_t need = pmb_rms_norm_backward_workspace_size(rows, dim);
+  if (workspace_bytes < need || workspace == nullptr) {
+    set_error("pmb_rms_norm_backward: workspace of %lld bytes is smaller than the %lld required",
+              (long long)workspace_bytes, (long long)need);
+    return PMB_ERR_WORKSPACE;
+  }
+  float* partial = static_cast<float*>(workspace);
+  return PMB_DISPATCH(grad_dtype, Tg, "pmb_rms_norm_backward", [&] {
+    return PMB_DISPATCH(grad_x_dtype, Tdx, "pmb_rms_norm_backward", [&] {
+      return launch_bwd<Tg, Tdx>(grad_out, saved, saved_is_input, inv_norm, gamma, gamma_dtype, grad_x, grad_gamma,
+                                 grad_gamma_dtype, rows, dim, partial, s);
+    });
+  });
+}
