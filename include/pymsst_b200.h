@@ -51,6 +51,10 @@ extern "C" {
 #define PMB_ERR_ALIGNMENT (-4)
 #define PMB_ERR_WORKSPACE (-5)
 
+/* activation codes (grouped linear epilogue) */
+#define PMB_ACT_NONE 0
+#define PMB_ACT_TANH 1
+
 /* Largest band count accepted by the ragged (per-band) kernels. */
 #define PMB_MAX_BANDS 128
 
@@ -110,6 +114,166 @@ PMB_API int pmb_rotary_forward(const void* t, const void* cos, const void* sin, 
 PMB_API int pmb_rotary_backward(const void* grad_out, const void* cos, const void* sin, void* grad_t,
                         int64_t batch, int64_t seq_len, int64_t heads, int64_t dim, int dtype,
                         void* stream);
+
+/* ------------------------------------------------------------------------
+ * BandSplit forward: per-band RMSNorm + per-band Linear(I_b -> O).
+ * Band b covers features [off_b, off_b + widths[b]) of a row, off_b the
+ * prefix sum of widths.  Element (row m, band b, feature i) of x is read at
+ * element offset
+ *   m*x_stride_row + (off_b + i)*x_stride_feat          if x_stride_band < 0
+ *                                                        (ragged layout),
+ *   m*x_stride_row + b*x_stride_band + i*x_stride_feat   otherwise (grouped
+ *                                                        layout, equal widths).
+ * Per band (host arrays of device pointers): gammas[b] [I_b],
+ * weights[b] [O, I_b] row-major, biases (array may be NULL; entries may be
+ * NULL) [O].  Outputs: out [rows, num_bands, O]; normed [rows, total]
+ * (nullable) = x*inv*sqrt(I_b); inv_norm fp32 [rows, num_bands].
+ * x, out, normed are in `dtype`; the per-band parameters (and, in the
+ * backward, their gradients) are in `param_dtype`, which is `dtype` or fp32
+ * (fp32 master weights read directly under mixed precision).
+ * Replaces band_split_forward (.cpp:141-170; .cu:14-123) and
+ * band_split_ragged_forward (.cpp:271-314; .cu:590-739).
+ * ---------------------------------------------------------------------- */
+PMB_API int pmb_band_split_forward(const void* x, int64_t rows, int64_t x_stride_row, int64_t x_stride_band,
+                                   int64_t x_stride_feat, int num_bands, const int64_t* widths,
+                                   const void* const* gammas, const void* const* weights,
+                                   const void* const* biases, int64_t out_features, void* out, void* normed,
+                                   float* inv_norm, int dtype, int param_dtype, void* stream);
+
+/* Scratch bytes for pmb_band_split_backward (need_grad_x: grad_x requested). */
+PMB_API int64_t pmb_band_split_backward_workspace_size(int64_t rows, int num_bands, const int64_t* widths,
+                                                       int64_t out_features, int need_grad_x);
+
+/*
+ * BandSplit backward from grad_out [rows, num_bands, O], normed
+ * [rows, total] and inv_norm [rows, num_bands]:
+ *   grad_weights[b] [O, I_b] = grad_out_b^T (normed_b * gamma_b)
+ *   grad_gammas[b]  [I_b]    = sum_m (grad_out_b W_b)[m,:] * normed_b[m,:]
+ *   grad_biases[b]  [O]      = sum_m grad_out_b[m,:]      (array may be NULL)
+ *   grad_x [rows, total]     = RMSNorm input gradient    (nullable: skipped)
+ * All reductions are deterministic (no atomics).
+ * Replaces band_split_backward / _v2 / _v3 (.cpp:172-269; .cu:126-587) and
+ * band_split_ragged_backward (.cpp:316-356; .cu:742-1003).
+ */
+PMB_API int pmb_band_split_backward(const void* grad_out, const void* normed, const float* inv_norm, int64_t rows,
+                                    int num_bands, const int64_t* widths, const void* const* gammas,
+                                    const void* const* weights, int64_t out_features, void* grad_x,
+                                    void* const* grad_gammas, void* const* grad_weights, void* const* grad_biases,
+                                    int dtype, int param_dtype, void* workspace, int64_t workspace_bytes,
+                                    void* stream);
+
+/* ------------------------------------------------------------------------
+ * For every remaining band-wise entry point, `dtype` types the activations
+ * and `param_dtype` the weights / biases and their gradients; param_dtype is
+ * `dtype` (reference convention) or fp32 (mixed precision on fp32 masters).
+ *
+ * Grouped linear, groups of equal shape (MaskEstimator hidden layers):
+ *   out[m, g, :] = act(x[m, g, :] W[g]^T + bias[g]),  act = none | tanh
+ * x element (m, g, i) at m*x_stride_row + g*x_stride_group + i*x_stride_feat;
+ * weight [G, O, I], bias [G, O] (nullable), out [rows, G, O].
+ * Replaces grouped_linear_forward (.cpp:358-388; .cu:1006-1074), and with
+ * activation = PMB_ACT_TANH fuses the hidden-layer Tanh that the reference
+ * applies separately (fused_roformer.py:527-553).
+ * ---------------------------------------------------------------------- */
+PMB_API int pmb_grouped_linear_forward(const void* x, int64_t rows, int64_t groups, int64_t in_features,
+                                       int64_t out_features, int64_t x_stride_row, int64_t x_stride_group,
+                                       int64_t x_stride_feat, const void* weight, const void* bias, void* out,
+                                       int activation, int dtype, int param_dtype, void* stream);
+PMB_API int64_t pmb_grouped_linear_backward_workspace_size(int64_t rows, int64_t groups, int64_t out_features);
+/*
+ * Backward of pmb_grouped_linear_forward for contiguous x [rows, G, I]:
+ * `out` is the forward output (needed for tanh'), grad_x nullable,
+ * grad_bias nullable.  (No reference counterpart: the reference's hidden
+ * layers backpropagate through torch einsum, fused_roformer.py:1042-1048.)
+ */
+PMB_API int pmb_grouped_linear_backward(const void* grad_out, const void* x, const void* out, int64_t rows,
+                                        int64_t groups, int64_t in_features, int64_t out_features,
+                                        const void* weight, void* grad_x, void* grad_weight, void* grad_bias,
+                                        int activation, int dtype, int param_dtype, void* workspace,
+                                        int64_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
+ * MaskEstimator final layer: per-band Linear(H -> 2*I_b) + GLU.
+ * x [rows, num_bands, H]; weights[b] [2*I_b, H]; bias [2*total];
+ *   pre[m, 2*off_b + j] = x[m,b,:] . W_b[j,:] + bias[2*off_b + j]
+ *   out[m, off_b + l]   = pre[m, 2*off_b + l] * sigmoid(pre[m, 2*off_b + I_b + l])
+ * out [rows, total], pre [rows, 2*total] (saved for the backward).
+ * Replaces mask_estimator_final_direct_forward / mask_estimator_final_forward
+ * (.cpp:560-693; .cu:2284-2420, .cu:2516-2553, .cu:2706-2760).
+ * ---------------------------------------------------------------------- */
+PMB_API int pmb_mask_estimator_final_forward(const void* x, int64_t rows, int num_bands, int64_t hidden,
+                                             const int64_t* widths, const void* const* weights, const void* bias,
+                                             void* out, void* pre, int dtype, int param_dtype, void* stream);
+PMB_API int64_t pmb_mask_estimator_final_backward_workspace_size(int64_t rows, int num_bands, const int64_t* widths);
+/*
+ * Backward: grad_out [rows, total] -> grad_x [rows, num_bands, H],
+ * grad_bias [2*total], grad_weights[b] [2*I_b, H].
+ * Replaces mask_estimator_final_direct_backward / mask_estimator_final_backward
+ * (.cpp:591-729; .cu:2556-2704, .cu:2422-2513, .cu:2762-2851).
+ */
+PMB_API int pmb_mask_estimator_final_backward(const void* grad_out, const void* x, const void* pre, int64_t rows,
+                                              int num_bands, int64_t hidden, const int64_t* widths,
+                                              const void* const* weights, void* grad_x, void* grad_bias,
+                                              void* const* grad_weights, int dtype, int param_dtype,
+                                              void* workspace, int64_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Attention output gate (per head):
+ *   gate[r, h] = sigmoid(x[r,:] . weight[h,:] + bias[h])      [rows, H]
+ *   out[r, h*Dh + d] = attn(r, h, d) * gate[r, h]              [rows, H*Dh]
+ * attn element (r, h, d), r = bi*seq_len + n, at
+ *   bi*attn_stride_batch + n*attn_stride_seq + h*attn_stride_head + d,
+ * so the [batch, H, seq, Dh] attention output is read in place.
+ * x [rows, dim], weight [H, dim], bias [H]; H <= 16.
+ * Replaces attention_gate_forward (.cpp:539-561; .cu:1778-1824, .cu:1922-1970).
+ * ---------------------------------------------------------------------- */
+PMB_API int pmb_attention_gate_forward(const void* attn, int64_t seq_len, int64_t attn_stride_batch,
+                                       int64_t attn_stride_seq, int64_t attn_stride_head, const void* x,
+                                       const void* weight, const void* bias, int64_t rows, int64_t heads,
+                                       int64_t dim_head, int64_t dim, void* out, void* gate, int dtype,
+                                       int param_dtype, void* stream);
+PMB_API int64_t pmb_attention_gate_backward_workspace_size(int64_t rows, int64_t heads, int64_t dim);
+/*
+ * Backward: grad_out [rows, H*Dh] -> grad_attn (written with the attn
+ * strides), grad_x [rows, dim], grad_weight [H, dim], grad_bias [H].
+ * Replaces attention_gate_backward (.cpp:563-591; .cu:1826-1920, .cu:1972-2036).
+ */
+PMB_API int pmb_attention_gate_backward(const void* grad_out, const void* attn, int64_t seq_len,
+                                        int64_t attn_stride_batch, int64_t attn_stride_seq,
+                                        int64_t attn_stride_head, const void* x, const void* weight,
+                                        const void* gate, int64_t rows, int64_t heads, int64_t dim_head,
+                                        int64_t dim, void* grad_attn, void* grad_x, void* grad_weight,
+                                        void* grad_bias, int dtype, int param_dtype, void* workspace,
+                                        int64_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Band index kernels between the STFT and the band feature layouts
+ * (Mel-band RoFormer overlapping bands; identity index for BS-RoFormer).
+ *   stft  fp32 [B, S, F, T, 2]  (torch.stft of [B*S, L] audio, as real)
+ *   feats      [B, T, J, 2]     J = pairs, index[j] = f*S + s (int32)
+ *   inv_ptr int32 [F*S + 1], inv_idx int32 [J]: CSR inverse of index.
+ * gather:    feats[b,t,j,:] = stft[b, s_j, f_j, t, :]
+ * recombine: out[b,n,s,f,t] = (stft[b,s,f,t] if multiply_stft else 1) *
+ *            sum_{j in inv(f*S+s)} mask[b,n,t,j] / max(count, 1e-8)   (complex)
+ * (pymss-core MelBandRoformer gather `stft_repr[batch, freq_indices]` and
+ * scatter_add_ / num_bands_per_freq average, which have no pymsst CUDA
+ * counterpart; reached via fused_roformer.py:827-873.)
+ * ---------------------------------------------------------------------- */
+PMB_API int pmb_band_gather_forward(const float* stft, const int* index, int64_t batch, int64_t channels,
+                                    int64_t freqs, int64_t frames, int64_t pairs, void* x, int x_dtype,
+                                    void* stream);
+PMB_API int pmb_band_gather_backward(const void* grad_x, const int* inv_ptr, const int* inv_idx, int64_t batch,
+                                     int64_t channels, int64_t freqs, int64_t frames, int64_t pairs,
+                                     float* grad_stft, int x_dtype, void* stream);
+PMB_API int pmb_band_recombine_forward(const void* mask, const float* stft, const int* inv_ptr,
+                                       const int* inv_idx, int64_t batch, int64_t stems, int64_t channels,
+                                       int64_t freqs, int64_t frames, int64_t pairs, int multiply_stft,
+                                       float* out, int mask_dtype, void* stream);
+/* grad_mask [B, N, T, J, 2] from grad_out [B, N, S, F, T, 2] (fp32). */
+PMB_API int pmb_band_recombine_backward(const float* grad_out, const float* stft, const int* index,
+                                        const int* inv_ptr, int64_t batch, int64_t stems, int64_t channels,
+                                        int64_t freqs, int64_t frames, int64_t pairs, int multiply_stft,
+                                        void* grad_mask, int mask_dtype, void* stream);
 
 #ifdef __cplusplus
 }

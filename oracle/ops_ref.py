@@ -194,3 +194,14 @@ def mask_estimator_final_backward(grad_out, x, pre, weights, dim_inputs, dim_off
 
 
 mask_estimator_final_direct_backward = mask_estimator_final_backward
+
+
+# Reference names that differ only in dtype handling map to the same formulas.
+rms_norm_forward_fp32_gamma = rms_norm_forward
+rms_norm_backward_fp32_gamma = rms_norm_backward
+rms_norm_forward_mixed = rms_norm_forward
+
+
+def rms_norm_backward_mixed(grad_out, normed, inv_norm, gamma, x_meta=None):
+    """.cu:1628-1691 (grad_x is cast to x_meta's dtype by the caller)."""
+    return rms_norm_backward(grad_out, normed, inv_norm, gamma)

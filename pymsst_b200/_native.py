@@ -33,6 +33,30 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "pmb_rms_norm_backward": (_i, [_p, _p, _i, _p, _p, _p, _p, _i64, _i64, _i, _i, _i, _i, _p, _i64, _p]),
     "pmb_rotary_forward": (_i, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i, _p]),
     "pmb_rotary_backward": (_i, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i, _p]),
+    "pmb_band_split_forward": (
+        _i, [_p, _i64, _i64, _i64, _i64, _i, _pi64, _pp, _pp, _pp, _i64, _p, _p, _p, _i, _i, _p]),
+    "pmb_band_split_backward_workspace_size": (_i64, [_i64, _i, _pi64, _i64, _i]),
+    "pmb_band_split_backward": (
+        _i, [_p, _p, _p, _i64, _i, _pi64, _pp, _pp, _i64, _p, _pp, _pp, _pp, _i, _i, _p, _i64, _p]),
+    "pmb_grouped_linear_forward": (
+        _i, [_p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _i, _i, _i, _p]),
+    "pmb_grouped_linear_backward_workspace_size": (_i64, [_i64, _i64, _i64]),
+    "pmb_grouped_linear_backward": (
+        _i, [_p, _p, _p, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _i, _i, _i, _p, _i64, _p]),
+    "pmb_mask_estimator_final_forward": (_i, [_p, _i64, _i, _i64, _pi64, _pp, _p, _p, _p, _i, _i, _p]),
+    "pmb_mask_estimator_final_backward_workspace_size": (_i64, [_i64, _i, _pi64]),
+    "pmb_mask_estimator_final_backward": (
+        _i, [_p, _p, _p, _i64, _i, _i64, _pi64, _pp, _p, _p, _pp, _i, _i, _p, _i64, _p]),
+    "pmb_attention_gate_forward": (
+        _i, [_p, _i64, _i64, _i64, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _p, _i, _i, _p]),
+    "pmb_attention_gate_backward_workspace_size": (_i64, [_i64, _i64, _i64]),
+    "pmb_attention_gate_backward": (
+        _i, [_p, _p, _i64, _i64, _i64, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _i, _i, _p, _i64,
+             _p]),
+    "pmb_band_gather_forward": (_i, [_p, _p, _i64, _i64, _i64, _i64, _i64, _p, _i, _p]),
+    "pmb_band_gather_backward": (_i, [_p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p, _i, _p]),
+    "pmb_band_recombine_forward": (_i, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i, _p, _i, _p]),
+    "pmb_band_recombine_backward": (_i, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i, _p, _i, _p]),
 }
 
 
@@ -93,6 +117,28 @@ def ptr(t: torch.Tensor | None) -> int | None:
 def call(name: str, *args) -> None:
     """Call a status-returning entry point and raise on failure."""
     check(getattr(library(), name)(*args), name)
+
+
+def i64_array(values) -> ctypes.Array:
+    values = [int(v) for v in values]
+    return (ctypes.c_int64 * len(values))(*values)
+
+
+def ptr_array(values) -> ctypes.Array:
+    """Host array of device pointers (ints or tensors; None becomes NULL)."""
+    out = []
+    for v in values:
+        if v is None:
+            out.append(None)
+        elif isinstance(v, torch.Tensor):
+            out.append(v.data_ptr())
+        else:
+            out.append(int(v))
+    return (ctypes.c_void_p * len(out))(*out)
+
+
+def workspace(nbytes: int, device: torch.device) -> torch.Tensor:
+    return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=device)
 
 
 def require_cuda(*tensors: torch.Tensor | None, name: str) -> torch.device:

@@ -66,7 +66,7 @@ __global__ void __launch_bounds__(kThreads)
 }
 
 // tab.ptr0 = gamma_b [I_b], ptr1 = W_b [O, I_b], ptr2 = bias_b [O] (may be NULL)
-template <typename T, bool KCONTIG>
+template <typename T, typename TP, bool KCONTIG>
 __global__ void __launch_bounds__(simt::kThreads)
     band_split_fwd_gemm(const T* __restrict__ x, int64_t rows, XLayout lx, BandTable tab, int64_t O,
                         const float* __restrict__ inv_norm, T* __restrict__ out) {
@@ -81,10 +81,10 @@ __global__ void __launch_bounds__(simt::kThreads)
     sm.a_row_scale[r] = (m0 + r < rows) ? inv_norm[(int64_t)(m0 + r) * tab.count + b] * s : 0.f;
   __syncthreads();
   float acc[simt::TM][simt::TN];
-  simt::mainloop<T, T, KCONTIG, true, T>(sm, x + lx.base(tab, b), lx.s_row, lx.s_feat,
-                                         static_cast<const T*>(tab.ptr1[b]), w, 1, m0, (int)rows, n0, (int)O, (int)w,
-                                         true, static_cast<const T*>(tab.ptr0[b]), acc);
-  const T* bias = static_cast<const T*>(tab.ptr2[b]);
+  simt::mainloop<T, TP, KCONTIG, true, TP>(sm, x + lx.base(tab, b), lx.s_row, lx.s_feat,
+                                           static_cast<const TP*>(tab.ptr1[b]), w, 1, m0, (int)rows, n0, (int)O,
+                                           (int)w, true, tab.ptr0[b], acc);
+  const TP* bias = static_cast<const TP*>(tab.ptr2[b]);
 #pragma unroll
   for (int i = 0; i < simt::TM; ++i) {
     const int m = m0 + simt::row_of(i);
@@ -94,7 +94,7 @@ __global__ void __launch_bounds__(simt::kThreads)
       const int n = n0 + simt::col_of(j);
       if (n >= O) continue;
       float v = acc[i][j];
-      if (bias != nullptr) v += Elem<T>::to_f(bias[n]);
+      if (bias != nullptr) v += Elem<TP>::to_f(bias[n]);
       out[((int64_t)m * tab.count + b) * O + n] = Elem<T>::from_f(v);
     }
   }
@@ -103,7 +103,7 @@ __global__ void __launch_bounds__(simt::kThreads)
 // G-GEMM: G[o, i] = sum_m dY[m,b,o] normed[m, off_b + i].  Epilogue writes
 // grad_W = G * gamma and a per-o-tile partial of grad_gamma (fp32 workspace).
 // tab.ptr0 = gamma_b, ptr1 = W_b, ptr2 = grad_W_b.
-template <typename T>
+template <typename T, typename TP>
 __global__ void __launch_bounds__(simt::kThreads)
     band_split_bwd_weight(const T* __restrict__ dy, const T* __restrict__ normed, int64_t rows, BandTable tab,
                           int64_t O, float* __restrict__ dgamma_partial) {
@@ -120,22 +120,22 @@ __global__ void __launch_bounds__(simt::kThreads)
   float acc[simt::TM][simt::TN];
   simt::mainloop<T, T, false, false, T>(sm, dy + (int64_t)b * O, 1, nbO, normed + tab.off[b], 1, tab.total, m0,
                                         (int)O, n0, (int)w, (int)rows, false, nullptr, acc);
-  const T* gamma = static_cast<const T*>(tab.ptr0[b]);
-  const T* W = static_cast<const T*>(tab.ptr1[b]);
-  T* gW = static_cast<T*>(const_cast<void*>(tab.ptr2[b]));
+  const TP* gamma = static_cast<const TP*>(tab.ptr0[b]);
+  const TP* W = static_cast<const TP*>(tab.ptr1[b]);
+  TP* gW = static_cast<TP*>(const_cast<void*>(tab.ptr2[b]));
   float colpart[simt::TN];
 #pragma unroll
   for (int j = 0; j < simt::TN; ++j) {
     const int i = n0 + simt::col_of(j);
     colpart[j] = 0.f;
     if (i >= w) continue;
-    const float g = Elem<T>::to_f(gamma[i]);
+    const float g = Elem<TP>::to_f(gamma[i]);
 #pragma unroll
     for (int ii = 0; ii < simt::TM; ++ii) {
       const int o = m0 + simt::row_of(ii);
       if (o >= O) continue;
-      gW[(int64_t)o * w + i] = Elem<T>::from_f(acc[ii][j] * g);
-      colpart[j] += Elem<T>::to_f(W[(int64_t)o * w + i]) * acc[ii][j];
+      gW[(int64_t)o * w + i] = Elem<TP>::from_f(acc[ii][j] * g);
+      colpart[j] += Elem<TP>::to_f(W[(int64_t)o * w + i]) * acc[ii][j];
     }
   }
   const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
@@ -153,7 +153,7 @@ __global__ void __launch_bounds__(simt::kThreads)
 }
 
 // gs[m, off_b + i] = sum_o dY[m,b,o] W_b[o, i]   (fp32 workspace)
-template <typename T>
+template <typename T, typename TP>
 __global__ void __launch_bounds__(simt::kThreads)
     band_split_bwd_gs(const T* __restrict__ dy, int64_t rows, BandTable tab, int64_t O, float* __restrict__ gs) {
   __shared__ simt::Smem sm;
@@ -164,9 +164,9 @@ __global__ void __launch_bounds__(simt::kThreads)
   const int n0 = (blockIdx.x % nti) * simt::BN;
   if (n0 >= w) return;
   float acc[simt::TM][simt::TN];
-  simt::mainloop<T, T, true, false, T>(sm, dy + (int64_t)b * O, (int64_t)tab.count * O, 1,
-                                       static_cast<const T*>(tab.ptr1[b]), 1, w, m0, (int)rows, n0, (int)w, (int)O,
-                                       false, nullptr, acc);
+  simt::mainloop<T, TP, true, false>(sm, dy + (int64_t)b * O, (int64_t)tab.count * O, 1,
+                                     static_cast<const TP*>(tab.ptr1[b]), 1, w, m0, (int)rows, n0, (int)w, (int)O,
+                                     false, nullptr, acc);
 #pragma unroll
   for (int ii = 0; ii < simt::TM; ++ii) {
     const int m = m0 + simt::row_of(ii);
@@ -179,7 +179,7 @@ __global__ void __launch_bounds__(simt::kThreads)
   }
 }
 
-template <typename T>
+template <typename T, typename TP>
 __global__ void __launch_bounds__(kThreads)
     band_split_bwd_input(const float* __restrict__ gs, const T* __restrict__ normed, const float* __restrict__ inv_norm,
                          int64_t rows, BandTable tab, T* __restrict__ grad_x) {
@@ -190,15 +190,15 @@ __global__ void __launch_bounds__(kThreads)
     const int b = (int)(p % tab.count);
     const int64_t w = tab.off[b + 1] - tab.off[b];
     const float s = sqrtf((float)w);
-    const T* gamma = static_cast<const T*>(tab.ptr0[b]);
+    const TP* gamma = static_cast<const TP*>(tab.ptr0[b]);
     const int64_t base = r * tab.total + tab.off[b];
     float dot = 0.f;
-    for (int64_t i = lane; i < w; i += 32) dot += gs[base + i] * Elem<T>::to_f(gamma[i]) * Elem<T>::to_f(normed[base + i]);
+    for (int64_t i = lane; i < w; i += 32) dot += gs[base + i] * Elem<TP>::to_f(gamma[i]) * Elem<T>::to_f(normed[base + i]);
     dot = warp_sum(dot);
     const float inv = inv_norm[r * tab.count + b];
     const float ds = dot / s;
     for (int64_t i = lane; i < w; i += 32) {
-      const float gn = gs[base + i] * Elem<T>::to_f(gamma[i]);
+      const float gn = gs[base + i] * Elem<TP>::to_f(gamma[i]);
       grad_x[base + i] = Elem<T>::from_f(inv * (gn * s - Elem<T>::to_f(normed[base + i]) * ds));
     }
   }
@@ -228,7 +228,7 @@ int grid_pairs(int64_t pairs) {
   return (int)(g < 1 ? 1 : g);
 }
 
-template <typename T>
+template <typename T, typename TP>
 int fwd_impl(const void* x, int64_t rows, XLayout lx, const BandTable& tab, int64_t O, void* out, void* normed,
              float* inv_norm, cudaStream_t stream) {
   band_norm_kernel<T><<<grid_pairs(rows * tab.count), kThreads, 0, stream>>>(
@@ -236,43 +236,43 @@ int fwd_impl(const void* x, int64_t rows, XLayout lx, const BandTable& tab, int6
   PMB_CHECK_LAUNCH("pmb_band_split_forward(norm)");
   dim3 grid(simt::tiles(rows, simt::BM) * simt::tiles(O, simt::BN), tab.count);
   if (lx.s_feat == 1)
-    band_split_fwd_gemm<T, true><<<grid, simt::kThreads, 0, stream>>>(static_cast<const T*>(x), rows, lx, tab, O,
-                                                                       inv_norm, static_cast<T*>(out));
+    band_split_fwd_gemm<T, TP, true><<<grid, simt::kThreads, 0, stream>>>(static_cast<const T*>(x), rows, lx, tab,
+                                                                           O, inv_norm, static_cast<T*>(out));
   else
-    band_split_fwd_gemm<T, false><<<grid, simt::kThreads, 0, stream>>>(static_cast<const T*>(x), rows, lx, tab, O,
-                                                                        inv_norm, static_cast<T*>(out));
+    band_split_fwd_gemm<T, TP, false><<<grid, simt::kThreads, 0, stream>>>(static_cast<const T*>(x), rows, lx, tab,
+                                                                            O, inv_norm, static_cast<T*>(out));
   PMB_CHECK_LAUNCH("pmb_band_split_forward(gemm)");
   return PMB_OK;
 }
 
-template <typename T>
+template <typename T, typename TP>
 int bwd_impl(const void* dy, const void* normed, const float* inv_norm, int64_t rows, const BandTable& wtab,
              const BandTable& gtab, const BandTable& btab, int64_t O, void* grad_x, char* ws, const BwdWorkspace& L,
-             int code, cudaStream_t stream) {
+             int pcode, cudaStream_t stream) {
   float* dgp = reinterpret_cast<float*>(ws + L.dgamma_partial_off);
   float* dbp = reinterpret_cast<float*>(ws + L.db_partial_off);
   float* gs = reinterpret_cast<float*>(ws + L.gs_off);
   const int nti = simt::tiles(wtab.max_width, simt::BN);
   dim3 gw(L.o_tiles * nti, wtab.count);
-  band_split_bwd_weight<T><<<gw, simt::kThreads, 0, stream>>>(static_cast<const T*>(dy), static_cast<const T*>(normed),
+  band_split_bwd_weight<T, TP><<<gw, simt::kThreads, 0, stream>>>(static_cast<const T*>(dy), static_cast<const T*>(normed),
                                                                rows, wtab, O, dgp);
   PMB_CHECK_LAUNCH("pmb_band_split_backward(weight)");
   red::colsum_finalize_bands<<<(int)((wtab.total + 255) / 256), red::kThreads, 0, stream>>>(dgp, L.o_tiles, wtab.total,
-                                                                                             gtab, code);
+                                                                                             gtab, pcode);
   PMB_CHECK_LAUNCH("pmb_band_split_backward(gamma)");
   if (btab.count > 0) {
     const int64_t cols = (int64_t)wtab.count * O;
     dim3 gp((int)((cols + 255) / 256), L.row_chunks);
     red::colsum_partial<T><<<gp, red::kThreads, 0, stream>>>(static_cast<const T*>(dy), rows, cols, cols, dbp);
     red::colsum_finalize_bands<<<(int)((cols + 255) / 256), red::kThreads, 0, stream>>>(dbp, L.row_chunks, cols, btab,
-                                                                                         code);
+                                                                                         pcode);
     PMB_CHECK_LAUNCH("pmb_band_split_backward(bias)");
   }
   if (grad_x != nullptr) {
     dim3 gg(simt::tiles(rows, simt::BM) * nti, wtab.count);
-    band_split_bwd_gs<T><<<gg, simt::kThreads, 0, stream>>>(static_cast<const T*>(dy), rows, wtab, O, gs);
+    band_split_bwd_gs<T, TP><<<gg, simt::kThreads, 0, stream>>>(static_cast<const T*>(dy), rows, wtab, O, gs);
     PMB_CHECK_LAUNCH("pmb_band_split_backward(gs)");
-    band_split_bwd_input<T><<<grid_pairs(rows * wtab.count), kThreads, 0, stream>>>(
+    band_split_bwd_input<T, TP><<<grid_pairs(rows * wtab.count), kThreads, 0, stream>>>(
         gs, static_cast<const T*>(normed), inv_norm, rows, wtab, static_cast<T*>(grad_x));
     PMB_CHECK_LAUNCH("pmb_band_split_backward(input)");
   }
@@ -288,7 +288,7 @@ extern "C" int pmb_band_split_forward(const void* x, int64_t rows, int64_t x_str
                                       int64_t x_stride_feat, int num_bands, const int64_t* widths,
                                       const void* const* gammas, const void* const* weights,
                                       const void* const* biases, int64_t out_features, void* out, void* normed,
-                                      float* inv_norm, int dtype, void* stream) {
+                                      float* inv_norm, int dtype, int param_dtype, void* stream) {
   clear_error();
   const char* name = "pmb_band_split_forward";
   BandTable tab;
@@ -304,7 +304,8 @@ extern "C" int pmb_band_split_forward(const void* x, int64_t rows, int64_t x_str
               "%s: a band stride requires equal band widths", name);
   XLayout lx{x_stride_row, x_stride_band, x_stride_feat};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  return PMB_DISPATCH(dtype, T, name, [&] { return fwd_impl<T>(x, rows, lx, tab, out_features, out, normed, inv_norm, s); });
+  return PMB_DISPATCH_PARAM(dtype, param_dtype, T, TP, name,
+                            [&] { return fwd_impl<T, TP>(x, rows, lx, tab, out_features, out, normed, inv_norm, s); });
 }
 
 extern "C" int64_t pmb_band_split_backward_workspace_size(int64_t rows, int num_bands, const int64_t* widths,
@@ -319,7 +320,8 @@ extern "C" int pmb_band_split_backward(const void* grad_out, const void* normed,
                                        int num_bands, const int64_t* widths, const void* const* gammas,
                                        const void* const* weights, int64_t out_features, void* grad_x,
                                        void* const* grad_gammas, void* const* grad_weights, void* const* grad_biases,
-                                       int dtype, void* workspace, int64_t workspace_bytes, void* stream) {
+                                       int dtype, int param_dtype, void* workspace, int64_t workspace_bytes,
+                                       void* stream) {
   clear_error();
   const char* name = "pmb_band_split_backward";
   BandTable wtab, gtab, btab;
@@ -347,7 +349,8 @@ extern "C" int pmb_band_split_backward(const void* grad_out, const void* normed,
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (rows == 0) {
     // Zero-row batch: every gradient is zero.
-    const int es = dtype_size(dtype);
+    const int es = dtype_size(param_dtype);
+    PMB_REQUIRE(es > 0, "%s: unsupported parameter dtype %d", name, param_dtype);
     for (int b = 0; b < num_bands; ++b) {
       const int64_t w = wtab.off[b + 1] - wtab.off[b];
       PMB_CHECK_CUDA(cudaMemsetAsync(const_cast<void*>(wtab.ptr2[b]), 0, w * out_features * es, s), name);
@@ -357,8 +360,8 @@ extern "C" int pmb_band_split_backward(const void* grad_out, const void* normed,
     return PMB_OK;
   }
   PMB_REQUIRE(grad_out && normed && inv_norm, "%s: NULL tensor argument", name);
-  return PMB_DISPATCH(dtype, T, name, [&] {
-    return bwd_impl<T>(grad_out, normed, inv_norm, rows, wtab, gtab, btab, out_features, grad_x,
-                       static_cast<char*>(workspace), L, dtype, s);
+  return PMB_DISPATCH_PARAM(dtype, param_dtype, T, TP, name, [&] {
+    return bwd_impl<T, TP>(grad_out, normed, inv_norm, rows, wtab, gtab, btab, out_features, grad_x,
+                           static_cast<char*>(workspace), L, param_dtype, s);
   });
 }

@@ -121,6 +121,26 @@ void clear_error();
     }                                                                  \
   }()
 
+// Dispatch (activation dtype, parameter dtype): parameters either share the
+// activation dtype or are fp32 (master weights used directly under mixed
+// precision).
+#define PMB_DISPATCH_PARAM(code, pcode, T, TP, name, ...)                                     \
+  [&]() -> int {                                                                              \
+    if ((pcode) != (code) && (pcode) != PMB_FLOAT32) {                                        \
+      ::pmb::set_error("%s: parameter dtype %d must equal the activation dtype or be fp32", \
+                       name, pcode);                                                          \
+      return PMB_ERR_UNSUPPORTED_DTYPE;                                                       \
+    }                                                                                         \
+    return PMB_DISPATCH(code, T, name, [&] {                                                  \
+      if ((pcode) == PMB_FLOAT32) {                                                           \
+        using TP = float;                                                                     \
+        return __VA_ARGS__();                                                                 \
+      }                                                                                       \
+      using TP = T;                                                                           \
+      return __VA_ARGS__();                                                                   \
+    });                                                                                       \
+  }()
+
 // ---------------------------------------------------------------------------
 // Reductions.
 // ---------------------------------------------------------------------------

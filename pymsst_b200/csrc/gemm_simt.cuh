@@ -51,13 +51,14 @@ __device__ __forceinline__ void load_tile(float (*dst)[ROWS + 1], const T* __res
 }
 
 // Accumulate one BM x BN tile over k in [0, K).  Optional A transforms:
-// a_row_scale (smem, BM entries, multiplies row r) and a_k_scale (global,
-// K entries of type TKS, multiplies column k).
+// a_row_scale (smem, BM entries, multiplies row r) and a_k_scale_ptr (global,
+// K entries of type TKS, multiplies column k; NULL = none).
 template <typename TA, typename TB, bool A_KCONTIG, bool B_KCONTIG, typename TKS = float>
 __device__ __forceinline__ void mainloop(Smem& sm, const TA* __restrict__ A, int64_t sa_m, int64_t sa_k,
                                          const TB* __restrict__ B, int64_t sb_n, int64_t sb_k, int m0, int m_lim,
                                          int n0, int n_lim, int K, bool use_row_scale,
-                                         const TKS* __restrict__ a_k_scale, float (&acc)[TM][TN]) {
+                                         const void* __restrict__ a_k_scale_ptr, float (&acc)[TM][TN]) {
+  const TKS* a_k_scale = static_cast<const TKS*>(a_k_scale_ptr);
   const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
 #pragma unroll
   for (int i = 0; i < TM; ++i)
@@ -95,7 +96,7 @@ __device__ __forceinline__ void mainloop(Smem& sm, const TA* __restrict__ A, int
 __device__ __forceinline__ int row_of(int i) { return threadIdx.x / 16 + 16 * i; }
 __device__ __forceinline__ int col_of(int j) { return threadIdx.x % 16 + 16 * j; }
 
-inline int tiles(int64_t n, int t) { return (int)((n + t - 1) / t); }
+__host__ __device__ inline int tiles(int64_t n, int t) { return (int)((n + t - 1) / t); }
 
 }  // namespace simt
 }  // namespace pmb

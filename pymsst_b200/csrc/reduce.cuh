@@ -7,6 +7,7 @@
 
 namespace pmb {
 namespace red {
+namespace {  // internal linkage: each translation unit owns its copy
 
 constexpr int kThreads = 256;
 constexpr int kRowsPerChunk = 64;
@@ -64,5 +65,6 @@ __global__ void __launch_bounds__(kThreads)
   store_dyn(const_cast<void*>(table.ptr0[b]), c - table.off[b], out_code, s);
 }
 
+}  // namespace
 }  // namespace red
 }  // namespace pmb

@@ -208,6 +208,485 @@ def rotary_backward(grad_out, cos, sin):
     return _rotary("pmb_rotary_backward", grad_out, cos, sin)
 
 
+# --------------------------------------------------------------- BandSplit
+def _elsize(t: torch.Tensor) -> int:
+    return t.element_size()
+
+
+def _rows_ptrs(base: torch.Tensor, count: int, step_elems: int) -> list[int]:
+    return [base.data_ptr() + g * step_elems * _elsize(base) for g in range(count)]
+
+
+def band_split_forward_into(x, rows, strides, widths, gammas, weights, biases, out_features, out, normed, inv_norm,
+                            param_dtype=None, name="band_split_forward"):
+    """Low-level call: per-band pointer lists, caller-allocated outputs."""
+    device = x.device
+    with torch.cuda.device(device):
+        nat.call(
+            "pmb_band_split_forward", x.data_ptr(), rows, strides[0], strides[1], strides[2], len(widths),
+            nat.i64_array(widths), nat.ptr_array(gammas), nat.ptr_array(weights),
+            None if biases is None else nat.ptr_array(biases), out_features, out.data_ptr(),
+            nat.ptr(normed), inv_norm.data_ptr(), nat.dtype_code(x.dtype), nat.dtype_code(param_dtype or x.dtype),
+            nat.stream_handle(device),
+        )
+
+
+def band_split_backward_into(grad_out, normed, inv_norm, widths, gammas, weights, out_features, grad_x,
+                             grad_gammas, grad_weights, grad_biases, param_dtype=None, name="band_split_backward"):
+    device = grad_out.device
+    rows = grad_out.shape[0]
+    lib = nat.library()
+    warr = nat.i64_array(widths)
+    ws_bytes = int(lib.pmb_band_split_backward_workspace_size(rows, len(widths), warr, out_features,
+                                                              int(grad_x is not None)))
+    ws = nat.workspace(ws_bytes, device)
+    with torch.cuda.device(device):
+        nat.call(
+            "pmb_band_split_backward", grad_out.data_ptr(), normed.data_ptr(), inv_norm.data_ptr(), rows,
+            len(widths), warr, nat.ptr_array(gammas), nat.ptr_array(weights), out_features, nat.ptr(grad_x),
+            nat.ptr_array(grad_gammas), nat.ptr_array(grad_weights),
+            None if grad_biases is None else nat.ptr_array(grad_biases), nat.dtype_code(grad_out.dtype),
+            nat.dtype_code(param_dtype or grad_out.dtype), ws.data_ptr(), ws_bytes, nat.stream_handle(device),
+        )
+
+
+def band_split_forward(x, gamma, weight, bias=None):
+    """Grouped BandSplit forward; reference .cpp:141-170 -> (out, normed, inv_norm)."""
+    _check(x.is_cuda, "x must be a CUDA tensor")
+    _check(gamma.is_cuda, "gamma must be a CUDA tensor")
+    _check(weight.is_cuda, "weight must be a CUDA tensor")
+    if bias is not None:
+        _check(bias.is_cuda, "bias must be a CUDA tensor")
+    _check(x.dim() == 3, "x must have shape [M, G, I]")
+    _check(gamma.dim() == 2, "gamma must have shape [G, I]")
+    _check(weight.dim() == 3, "weight must have shape [G, O, I]")
+    _check(gamma.size(0) == x.size(1), "gamma group dimension must match x")
+    _check(gamma.size(1) == x.size(2), "gamma input dimension must match x")
+    _check(weight.size(0) == x.size(1), "weight group dimension must match x")
+    _check(weight.size(2) == x.size(2), "weight input dimension must match x")
+    if bias is not None:
+        _check(bias.dim() == 2, "bias must have shape [G, O]")
+        _check(bias.size(0) == x.size(1), "bias group dimension must match x")
+        _check(bias.size(1) == weight.size(1), "bias output dimension must match weight")
+        _check(bias.dtype == x.dtype, "bias dtype must match x")
+    _check(gamma.dtype == x.dtype, "gamma dtype must match x")
+    _check(weight.dtype == x.dtype, "weight dtype must match x")
+    nat.require_cuda(x, gamma, weight, bias, name="band_split_forward")
+    m, g, i = x.shape
+    o = weight.shape[1]
+    gamma, weight = _contig(gamma), _contig(weight)
+    bias = None if bias is None else _contig(bias)
+    out = torch.empty(m, g, o, dtype=x.dtype, device=x.device)
+    normed = torch.empty(m, g, i, dtype=x.dtype, device=x.device)
+    inv = torch.empty(m, g, dtype=torch.float32, device=x.device)
+    band_split_forward_into(
+        x, m, (x.stride(0), x.stride(1), x.stride(2)), [i] * g, _rows_ptrs(gamma, g, i), _rows_ptrs(weight, g, o * i),
+        None if bias is None else _rows_ptrs(bias, g, o), o, out, normed, inv,
+    )
+    return out, normed, inv
+
+
+def _band_split_backward_grouped(grad_out, normed, inv_norm, gamma, weight, has_bias):
+    _check(grad_out.is_cuda, "grad_out must be a CUDA tensor")
+    _check(normed.is_cuda, "normed must be a CUDA tensor")
+    _check(inv_norm.is_cuda, "inv_norm must be a CUDA tensor")
+    _check(gamma.is_cuda, "gamma must be a CUDA tensor")
+    _check(weight.is_cuda, "weight must be a CUDA tensor")
+    _check(grad_out.dim() == 3, "grad_out must have shape [M, G, O]")
+    _check(normed.dim() == 3, "normed must have shape [M, G, I]")
+    _check(inv_norm.dim() == 2, "inv_norm must have shape [M, G]")
+    _check(gamma.dim() == 2, "gamma must have shape [G, I]")
+    _check(weight.dim() == 3, "weight must have shape [G, O, I]")
+    _check(normed.size(0) == grad_out.size(0), "normed M must match grad_out")
+    _check(normed.size(1) == grad_out.size(1), "normed G must match grad_out")
+    _check(inv_norm.size(0) == grad_out.size(0), "inv_norm M must match grad_out")
+    _check(inv_norm.size(1) == grad_out.size(1), "inv_norm G must match grad_out")
+    _check(gamma.size(0) == grad_out.size(1), "gamma G must match grad_out")
+    _check(gamma.size(1) == normed.size(2), "gamma I must match normed")
+    _check(weight.size(0) == grad_out.size(1), "weight G must match grad_out")
+    _check(weight.size(1) == grad_out.size(2), "weight O must match grad_out")
+    _check(weight.size(2) == normed.size(2), "weight I must match normed")
+    _check(normed.dtype == grad_out.dtype, "normed dtype must match grad_out")
+    _check(gamma.dtype == grad_out.dtype, "gamma dtype must match grad_out")
+    _check(weight.dtype == grad_out.dtype, "weight dtype must match grad_out")
+    _check(inv_norm.dtype == torch.float32, "inv_norm must be float32")
+    nat.require_cuda(grad_out, normed, inv_norm, gamma, weight, name="band_split_backward")
+    m, g, o = grad_out.shape
+    i = normed.shape[2]
+    grad_out, normed, inv_norm = _contig(grad_out), _contig(normed), _contig(inv_norm)
+    gamma, weight = _contig(gamma), _contig(weight)
+    grad_x = torch.empty_like(normed)
+    grad_gamma = torch.empty_like(gamma)
+    grad_weight = torch.empty_like(weight)
+    grad_bias = torch.empty(g, o, dtype=grad_out.dtype, device=grad_out.device) if has_bias else None
+    band_split_backward_into(
+        grad_out, normed, inv_norm, [i] * g, _rows_ptrs(gamma, g, i), _rows_ptrs(weight, g, o * i), o, grad_x,
+        _rows_ptrs(grad_gamma, g, i), _rows_ptrs(grad_weight, g, o * i),
+        None if grad_bias is None else _rows_ptrs(grad_bias, g, o),
+    )
+    return grad_x, grad_gamma, grad_weight, grad_bias
+
+
+def band_split_backward(grad_out, normed, inv_norm, gamma, weight, has_bias):
+    """Reference .cpp:172-203 -> (grad_x, grad_gamma, grad_weight, grad_bias|None)."""
+    return _band_split_backward_grouped(grad_out, normed, inv_norm, gamma, weight, has_bias)
+
+
+def band_split_backward_v2(grad_out, normed, inv_norm, gamma, weight, has_bias):
+    """Reference .cpp:205-236 (same values as v1)."""
+    return _band_split_backward_grouped(grad_out, normed, inv_norm, gamma, weight, has_bias)
+
+
+def band_split_backward_v3(grad_out, normed, inv_norm, gamma, weight, has_bias):
+    """Reference .cpp:238-269 (same values as v1)."""
+    return _band_split_backward_grouped(grad_out, normed, inv_norm, gamma, weight, has_bias)
+
+
+def _check_offsets(dim_offsets, dim_inputs, count):
+    _check(dim_offsets.dim() == 1, "dim_offsets must be 1D")
+    _check(dim_offsets.dtype == torch.int64, "dim_offsets must be int64")
+    _check(dim_offsets.size(0) == count + 1, "dim_offsets length must be band count + 1")
+
+
+def band_split_ragged_forward(x, gammas, weights, biases, dim_inputs, dim_offsets):
+    """Reference .cpp:271-314 -> (out [M,nb,O], normed [M,total], inv_norm [M,nb])."""
+    _check(x.is_cuda, "x must be a CUDA tensor")
+    _check(dim_offsets.is_cuda, "dim_offsets must be a CUDA tensor")
+    _check(x.dim() == 2, "x must have shape [M, total]")
+    _check(len(gammas) == len(weights), "gammas length must match weights length")
+    _check(len(biases) == len(weights), "biases length must match weights length")
+    _check(len(dim_inputs) == len(weights), "dim_inputs length must match weights length")
+    _check(len(weights) > 0, "weights must not be empty")
+    _check_offsets(dim_offsets, dim_inputs, len(weights))
+    o = weights[0].size(0)
+    for gamma, weight, bias, w in zip(gammas, weights, biases, dim_inputs):
+        _check(gamma.dim() == 1, "gamma must have shape [I]")
+        _check(weight.dim() == 2, "weight must have shape [O, I]")
+        _check(bias.dim() == 1, "bias must have shape [O]")
+        _check(gamma.size(0) == w, "gamma dimension must match dim_inputs")
+        _check(weight.size(0) == o, "all weights must share output dimension")
+        _check(weight.size(1) == w, "weight input dimension must match dim_inputs")
+        _check(bias.size(0) == o, "bias output dimension must match weight")
+        _check(gamma.dtype == x.dtype, "gamma dtype must match x")
+        _check(weight.dtype == x.dtype, "weight dtype must match x")
+        _check(bias.dtype == x.dtype, "bias dtype must match x")
+    _check(x.size(1) == sum(int(w) for w in dim_inputs), "x total dimension must match dim_inputs")
+    nat.require_cuda(x, *gammas, *weights, *biases, name="band_split_ragged_forward")
+    x = _contig(x)
+    gammas = [_contig(t) for t in gammas]
+    weights = [_contig(t) for t in weights]
+    biases = [_contig(t) for t in biases]
+    m, total = x.shape
+    nb = len(weights)
+    out = torch.empty(m, nb, o, dtype=x.dtype, device=x.device)
+    normed = torch.empty(m, total, dtype=x.dtype, device=x.device)
+    inv = torch.empty(m, nb, dtype=torch.float32, device=x.device)
+    band_split_forward_into(x, m, (total, -1, 1), dim_inputs, gammas, weights, biases, o, out, normed, inv)
+    return out, normed, inv
+
+
+def band_split_ragged_backward(grad_out, normed, inv_norm, gammas, weights, dim_inputs, dim_offsets):
+    """Reference .cpp:316-356 -> [grad_x, *grad_gammas, *grad_weights, *grad_biases]."""
+    _check(grad_out.is_cuda, "grad_out must be a CUDA tensor")
+    _check(grad_out.dim() == 3, "grad_out must have shape [M, B, O]")
+    _check(normed.dim() == 2, "normed must have shape [M, total]")
+    _check(inv_norm.dim() == 2, "inv_norm must have shape [M, B]")
+    _check(len(gammas) == len(weights), "gammas length must match weights length")
+    _check(len(dim_inputs) == len(weights), "dim_inputs length must match weights length")
+    _check(len(weights) > 0, "weights must not be empty")
+    _check_offsets(dim_offsets, dim_inputs, len(weights))
+    _check(normed.size(0) == grad_out.size(0), "normed M must match grad_out")
+    _check(inv_norm.size(0) == grad_out.size(0), "inv_norm M must match grad_out")
+    _check(inv_norm.size(1) == grad_out.size(1), "inv_norm band count must match grad_out")
+    _check(len(weights) == grad_out.size(1), "weights length must match grad_out band count")
+    _check(normed.dtype == grad_out.dtype, "normed dtype must match grad_out")
+    _check(inv_norm.dtype == torch.float32, "inv_norm must be float32")
+    _check(normed.size(1) == sum(int(w) for w in dim_inputs), "normed total dimension must match dim_inputs")
+    nat.require_cuda(grad_out, normed, inv_norm, *gammas, *weights, name="band_split_ragged_backward")
+    o = grad_out.size(2)
+    grad_out, normed, inv_norm = _contig(grad_out), _contig(normed), _contig(inv_norm)
+    gammas = [_contig(t) for t in gammas]
+    weights = [_contig(t) for t in weights]
+    grad_x = torch.empty_like(normed)
+    grad_gammas = [torch.empty_like(t) for t in gammas]
+    grad_weights = [torch.empty_like(t) for t in weights]
+    grad_biases = [torch.empty(o, dtype=grad_out.dtype, device=grad_out.device) for _ in weights]
+    band_split_backward_into(grad_out, normed, inv_norm, dim_inputs, gammas, weights, o, grad_x, grad_gammas,
+                             grad_weights, grad_biases)
+    return [grad_x, *grad_gammas, *grad_weights, *grad_biases]
+
+
+# ---------------------------------------------------------- grouped linear
+def grouped_linear_forward(x, weight, bias=None, activation: int = 0):
+    """Reference .cpp:358-388 (x [M,G,I] any strides) -> out [M,G,O]."""
+    _check(x.is_cuda, "x must be a CUDA tensor")
+    _check(weight.is_cuda, "weight must be a CUDA tensor")
+    _check(x.dim() == 3, "x must have shape [M, G, I]")
+    _check(weight.dim() == 3, "weight must have shape [G, O, I]")
+    _check(weight.size(0) == x.size(1), "weight group dimension must match x")
+    _check(weight.size(2) == x.size(2), "weight input dimension must match x")
+    if bias is not None:
+        _check(bias.dim() == 2, "bias must have shape [G, O]")
+        _check(bias.size(0) == x.size(1), "bias group dimension must match x")
+        _check(bias.size(1) == weight.size(1), "bias output dimension must match weight")
+        _check(bias.dtype == x.dtype, "bias dtype must match x")
+    _check(weight.dtype == x.dtype, "weight dtype must match x")
+    device = nat.require_cuda(x, weight, bias, name="grouped_linear_forward")
+    m, g, i = x.shape
+    o = weight.shape[1]
+    weight = _contig(weight)
+    bias = None if bias is None else _contig(bias)
+    out = torch.empty(m, g, o, dtype=x.dtype, device=device)
+    with torch.cuda.device(device):
+        nat.call(
+            "pmb_grouped_linear_forward", x.data_ptr(), m, g, i, o, x.stride(0), x.stride(1), x.stride(2),
+            weight.data_ptr(), nat.ptr(bias), out.data_ptr(), activation, nat.dtype_code(x.dtype),
+            nat.dtype_code(weight.dtype), nat.stream_handle(device),
+        )
+    return out
+
+
+def grouped_linear_backward(grad_out, x, out, weight, activation: int = 0, need_grad_x: bool = True,
+                            has_bias: bool = True):
+    """Backward of :func:`grouped_linear_forward` -> (grad_x|None, grad_weight, grad_bias|None)."""
+    device = nat.require_cuda(grad_out, x, out, weight, name="grouped_linear_backward")
+    grad_out, x, weight = _contig(grad_out), _contig(x), _contig(weight)
+    out = None if out is None else _contig(out)
+    m, g, i = x.shape
+    o = weight.shape[1]
+    grad_x = torch.empty_like(x) if need_grad_x else None
+    grad_weight = torch.empty_like(weight)
+    grad_bias = torch.empty(g, o, dtype=weight.dtype, device=device) if has_bias else None
+    lib = nat.library()
+    ws_bytes = int(lib.pmb_grouped_linear_backward_workspace_size(m, g, o))
+    ws = nat.workspace(ws_bytes, device)
+    with torch.cuda.device(device):
+        nat.call(
+            "pmb_grouped_linear_backward", grad_out.data_ptr(), x.data_ptr(), nat.ptr(out), m, g, i, o,
+            weight.data_ptr(), nat.ptr(grad_x), grad_weight.data_ptr(), nat.ptr(grad_bias), activation,
+            nat.dtype_code(x.dtype), nat.dtype_code(weight.dtype), ws.data_ptr(), ws_bytes, nat.stream_handle(device),
+        )
+    return grad_x, grad_weight, grad_bias
+
+
+# ----------------------------------------------------------- attention gate
+def attention_gate_forward(attn, x, weight, bias):
+    """Reference .cpp:539-561 -> (out [M,H*DH], gate [M,H], attn, x)."""
+    _check(attn.is_cuda, "attn must be a CUDA tensor")
+    _check(x.is_cuda, "x must be a CUDA tensor")
+    _check(weight.is_cuda, "weight must be a CUDA tensor")
+    _check(bias.is_cuda, "bias must be a CUDA tensor")
+    _check(attn.dim() == 3, "attn must have shape [M, H, DH]")
+    _check(x.dim() == 2, "x must have shape [M, D]")
+    _check(weight.dim() == 2, "weight must have shape [H, D]")
+    _check(bias.dim() == 1, "bias must have shape [H]")
+    _check(attn.size(0) == x.size(0), "attn and x row counts must match")
+    _check(attn.size(1) == weight.size(0), "attn heads must match weight")
+    _check(weight.size(1) == x.size(1), "weight input dimension must match x")
+    _check(bias.size(0) == weight.size(0), "bias heads must match weight")
+    _check(x.dtype == attn.dtype, "x dtype must match attn")
+    _check(weight.dtype == attn.dtype, "weight dtype must match attn")
+    _check(bias.dtype == attn.dtype, "bias dtype must match attn")
+    device = nat.require_cuda(attn, x, weight, bias, name="attention_gate_forward")
+    attn, x, weight, bias = _contig(attn), _contig(x), _contig(weight), _contig(bias)
+    rows, heads, dh = attn.shape
+    out = torch.empty(rows, heads * dh, dtype=attn.dtype, device=device)
+    gate = torch.empty(rows, heads, dtype=attn.dtype, device=device)
+    with torch.cuda.device(device):
+        nat.call(
+            "pmb_attention_gate_forward", attn.data_ptr(), 1, heads * dh, 0, dh, x.data_ptr(), weight.data_ptr(),
+            bias.data_ptr(), rows, heads, dh, x.shape[1], out.data_ptr(), gate.data_ptr(),
+            nat.dtype_code(attn.dtype), nat.dtype_code(weight.dtype), nat.stream_handle(device),
+        )
+    return out, gate, attn, x
+
+
+def attention_gate_backward(grad_out, attn, x, weight, gate):
+    """Reference .cpp:563-591 -> (grad_attn, grad_x, grad_weight, grad_bias)."""
+    _check(grad_out.dim() == 2, "grad_out must have shape [M, H*DH]")
+    _check(attn.dim() == 3, "attn must have shape [M, H, DH]")
+    _check(x.dim() == 2, "x must have shape [M, D]")
+    _check(weight.dim() == 2, "weight must have shape [H, D]")
+    _check(gate.dim() == 2, "gate must have shape [M, H]")
+    _check(grad_out.size(0) == attn.size(0), "grad_out rows must match attn")
+    _check(grad_out.size(1) == attn.size(1) * attn.size(2), "grad_out columns must match flattened attn")
+    _check(attn.size(0) == x.size(0), "attn and x row counts must match")
+    _check(attn.size(1) == weight.size(0), "attn heads must match weight")
+    _check(weight.size(1) == x.size(1), "weight input dimension must match x")
+    _check(gate.size(0) == attn.size(0), "gate rows must match attn")
+    _check(gate.size(1) == attn.size(1), "gate heads must match attn")
+    for t, n in ((attn, "attn"), (x, "x"), (weight, "weight"), (gate, "gate")):
+        _check(t.dtype == grad_out.dtype, f"{n} dtype must match grad_out")
+    device = nat.require_cuda(grad_out, attn, x, weight, gate, name="attention_gate_backward")
+    grad_out, attn, x, weight, gate = map(_contig, (grad_out, attn, x, weight, gate))
+    rows, heads, dh = attn.shape
+    dim = x.shape[1]
+    grad_attn = torch.empty_like(attn)
+    grad_x = torch.empty_like(x)
+    grad_weight = torch.empty_like(weight)
+    grad_bias = torch.empty(heads, dtype=grad_out.dtype, device=device)
+    lib = nat.library()
+    ws_bytes = int(lib.pmb_attention_gate_backward_workspace_size(rows, heads, dim))
+    ws = nat.workspace(ws_bytes, device)
+    with torch.cuda.device(device):
+        nat.call(
+            "pmb_attention_gate_backward", grad_out.data_ptr(), attn.data_ptr(), 1, heads * dh, 0, dh,
+            x.data_ptr(), weight.data_ptr(), gate.data_ptr(), rows, heads, dh, dim, grad_attn.data_ptr(),
+            grad_x.data_ptr(), grad_weight.data_ptr(), grad_bias.data_ptr(), nat.dtype_code(grad_out.dtype),
+            nat.dtype_code(weight.dtype), ws.data_ptr(), ws_bytes, nat.stream_handle(device),
+        )
+    return grad_attn, grad_x, grad_weight, grad_bias
+
+
+# ------------------------------------------------- MaskEstimator final + GLU
+def _check_mask_forward(x, weights, bias, dim_inputs, dim_offsets):
+    _check(x.is_cuda, "x must be a CUDA tensor")
+    _check(bias.is_cuda, "bias must be a CUDA tensor")
+    _check(dim_offsets.is_cuda, "dim_offsets must be a CUDA tensor")
+    _check(x.dim() == 3, "x must have shape [M, G, H]")
+    _check(bias.dim() == 1, "bias must have shape [2 * total]")
+    _check(len(weights) == x.size(1), "weights length must match band count")
+    _check(len(dim_inputs) == len(weights), "dim_inputs length must match weights length")
+    _check_offsets(dim_offsets, dim_inputs, len(weights))
+    _check(bias.size(0) == 2 * sum(int(w) for w in dim_inputs), "bias dimension must match dim_inputs")
+    _check(bias.dtype == x.dtype, "bias dtype must match x")
+    for weight, w in zip(weights, dim_inputs):
+        _check(weight.dim() == 2, "weight must have shape [2 * O, H]")
+        _check(weight.size(1) == x.size(2), "weight hidden dimension must match x")
+        _check(weight.size(0) == int(w) * 2, "weight output dimension must match dim_inputs")
+        _check(weight.dtype == x.dtype, "weight dtype must match x")
+
+
+def mask_estimator_final_forward_into(x, weights, bias, dim_inputs, out, pre):
+    device = x.device
+    rows, nb, hidden = x.shape
+    with torch.cuda.device(device):
+        nat.call(
+            "pmb_mask_estimator_final_forward", x.data_ptr(), rows, nb, hidden, nat.i64_array(dim_inputs),
+            nat.ptr_array(weights), bias.data_ptr(), out.data_ptr(), pre.data_ptr(), nat.dtype_code(x.dtype),
+            nat.dtype_code(bias.dtype), nat.stream_handle(device),
+        )
+
+
+def mask_estimator_final_backward_into(grad_out, x, pre, weights, dim_inputs, grad_x, grad_bias, grad_weights):
+    device = grad_out.device
+    rows, nb, hidden = x.shape
+    warr = nat.i64_array(dim_inputs)
+    lib = nat.library()
+    ws_bytes = int(lib.pmb_mask_estimator_final_backward_workspace_size(rows, nb, warr))
+    ws = nat.workspace(ws_bytes, device)
+    with torch.cuda.device(device):
+        nat.call(
+            "pmb_mask_estimator_final_backward", grad_out.data_ptr(), x.data_ptr(), pre.data_ptr(), rows, nb,
+            hidden, warr, nat.ptr_array(weights), grad_x.data_ptr(), grad_bias.data_ptr(),
+            nat.ptr_array(grad_weights), nat.dtype_code(grad_out.dtype), nat.dtype_code(grad_bias.dtype), ws.data_ptr(),
+            ws_bytes, nat.stream_handle(device),
+        )
+
+
+def mask_estimator_final_forward(x, weights, bias, dim_inputs, dim_offsets):
+    """Reference .cpp:560-589 ("grouped") -> (out [M,total], pre [M,2*total], x)."""
+    _check_mask_forward(x, weights, bias, dim_inputs, dim_offsets)
+    nat.require_cuda(x, bias, *weights, name="mask_estimator_final_forward")
+    x, bias = _contig(x), _contig(bias)
+    weights = [_contig(w) for w in weights]
+    total = sum(int(w) for w in dim_inputs)
+    out = torch.empty(x.shape[0], total, dtype=x.dtype, device=x.device)
+    pre = torch.empty(x.shape[0], 2 * total, dtype=x.dtype, device=x.device)
+    mask_estimator_final_forward_into(x, weights, bias, dim_inputs, out, pre)
+    return out, pre, x
+
+
+def mask_estimator_final_backward(grad_out, x, pre, weights, dim_inputs, dim_offsets):
+    """Reference .cpp:591-625 -> [grad_x, grad_bias, *grad_weights]."""
+    _check(grad_out.dim() == 2, "grad_out must have shape [M, total]")
+    _check(x.dim() == 3, "x must have shape [M, G, H]")
+    _check(pre.dim() == 2, "pre must have shape [M, 2 * total]")
+    _check(grad_out.size(0) == x.size(0), "grad_out M must match x")
+    _check(pre.size(0) == x.size(0), "pre M must match x")
+    _check(pre.size(1) == grad_out.size(1) * 2, "pre total dimension must be twice grad_out")
+    _check_offsets(dim_offsets, dim_inputs, x.size(1))
+    _check(len(weights) == x.size(1), "weights length must match band count")
+    _check(grad_out.dtype == x.dtype, "grad_out dtype must match x")
+    _check(pre.dtype == x.dtype, "pre dtype must match x")
+    nat.require_cuda(grad_out, x, pre, *weights, name="mask_estimator_final_backward")
+    grad_out, x, pre = _contig(grad_out), _contig(x), _contig(pre)
+    weights = [_contig(w) for w in weights]
+    grad_x = torch.empty_like(x)
+    grad_bias = torch.empty(pre.shape[1], dtype=grad_out.dtype, device=grad_out.device)
+    grad_weights = [torch.empty_like(w) for w in weights]
+    mask_estimator_final_backward_into(grad_out, x, pre, weights, dim_inputs, grad_x, grad_bias, grad_weights)
+    return [grad_x, grad_bias, *grad_weights]
+
+
+def mask_estimator_final_direct_forward(x, weights, bias, dim_inputs, dim_offsets):
+    """Reference .cpp:660-693 ("direct"); same kernels as the grouped form."""
+    return mask_estimator_final_forward(x, weights, bias, dim_inputs, dim_offsets)
+
+
+def mask_estimator_final_direct_backward(grad_out, x, pre, weights, dim_inputs, dim_offsets):
+    """Reference .cpp:695-729 ("direct"); same kernels as the grouped form."""
+    return mask_estimator_final_backward(grad_out, x, pre, weights, dim_inputs, dim_offsets)
+
+
+# ------------------------------------------------------- band index kernels
+def band_gather(stft: torch.Tensor, tables: dict, out_dtype: torch.dtype = torch.float32) -> torch.Tensor:
+    """stft fp32 [B,S,F,T,2] -> band features [B,T,J*2] (``tables`` from BandIndex.device_tables)."""
+    device = nat.require_cuda(stft, name="band_gather")
+    _check(stft.dtype == torch.float32 and stft.dim() == 5 and stft.shape[-1] == 2, "stft must be fp32 [B,S,F,T,2]")
+    stft = _contig(stft)
+    b, s, f, t, _ = stft.shape
+    j = tables["index"].numel()
+    x = torch.empty(b, t, j * 2, dtype=out_dtype, device=device)
+    with torch.cuda.device(device):
+        nat.call("pmb_band_gather_forward", stft.data_ptr(), tables["index"].data_ptr(), b, s, f, t, j, x.data_ptr(),
+                 nat.dtype_code(out_dtype), nat.stream_handle(device))
+    return x
+
+
+def band_gather_backward(grad_x: torch.Tensor, tables: dict, channels: int, freqs: int) -> torch.Tensor:
+    device = nat.require_cuda(grad_x, name="band_gather_backward")
+    grad_x = _contig(grad_x)
+    b, t, j2 = grad_x.shape
+    grad = torch.empty(b, channels, freqs, t, 2, dtype=torch.float32, device=device)
+    with torch.cuda.device(device):
+        nat.call("pmb_band_gather_backward", grad_x.data_ptr(), tables["inv_ptr"].data_ptr(),
+                 tables["inv_idx"].data_ptr(), b, channels, freqs, t, j2 // 2, grad.data_ptr(),
+                 nat.dtype_code(grad_x.dtype), nat.stream_handle(device))
+    return grad
+
+
+def band_recombine(mask: torch.Tensor, stft: torch.Tensor | None, tables: dict, channels: int, freqs: int,
+                   multiply: bool = True) -> torch.Tensor:
+    """mask [B,N,T,J*2] (+ stft [B,S,F,T,2]) -> masked STFT fp32 [B,N,S,F,T,2]."""
+    device = nat.require_cuda(mask, stft, name="band_recombine")
+    mask = _contig(mask)
+    b, n, t, j2 = mask.shape
+    if multiply:
+        _check(stft is not None and stft.dtype == torch.float32, "stft must be fp32 [B,S,F,T,2]")
+        stft = _contig(stft)
+    out = torch.empty(b, n, channels, freqs, t, 2, dtype=torch.float32, device=device)
+    with torch.cuda.device(device):
+        nat.call("pmb_band_recombine_forward", mask.data_ptr(), nat.ptr(stft if multiply else None),
+                 tables["inv_ptr"].data_ptr(), tables["inv_idx"].data_ptr(), b, n, channels, freqs, t, j2 // 2,
+                 int(multiply), out.data_ptr(), nat.dtype_code(mask.dtype), nat.stream_handle(device))
+    return out
+
+
+def band_recombine_backward(grad_out: torch.Tensor, stft: torch.Tensor | None, tables: dict,
+                            mask_dtype: torch.dtype = torch.float32, multiply: bool = True) -> torch.Tensor:
+    device = nat.require_cuda(grad_out, stft, name="band_recombine_backward")
+    grad_out = _contig(grad_out).float()
+    b, n, s, f, t, _ = grad_out.shape
+    j = tables["index"].numel()
+    grad_mask = torch.empty(b, n, t, j * 2, dtype=mask_dtype, device=device)
+    with torch.cuda.device(device):
+        nat.call("pmb_band_recombine_backward", grad_out.data_ptr(), nat.ptr(_contig(stft) if multiply else None),
+                 tables["index"].data_ptr(), tables["inv_ptr"].data_ptr(), b, n, s, f, t, j, int(multiply),
+                 grad_mask.data_ptr(), nat.dtype_code(mask_dtype), nat.stream_handle(device))
+    return grad_mask
+
+
 #: The reference-compatible operator namespace (``extension=ops``).
 ops = SimpleNamespace(
     rms_norm_forward=rms_norm_forward,
@@ -218,6 +697,19 @@ ops = SimpleNamespace(
     rms_norm_backward_mixed=rms_norm_backward_mixed,
     rotary_forward=rotary_forward,
     rotary_backward=rotary_backward,
+    band_split_forward=band_split_forward,
+    band_split_backward=band_split_backward,
+    band_split_backward_v2=band_split_backward_v2,
+    band_split_backward_v3=band_split_backward_v3,
+    band_split_ragged_forward=band_split_ragged_forward,
+    band_split_ragged_backward=band_split_ragged_backward,
+    grouped_linear_forward=grouped_linear_forward,
+    attention_gate_forward=attention_gate_forward,
+    attention_gate_backward=attention_gate_backward,
+    mask_estimator_final_forward=mask_estimator_final_forward,
+    mask_estimator_final_backward=mask_estimator_final_backward,
+    mask_estimator_final_direct_forward=mask_estimator_final_direct_forward,
+    mask_estimator_final_direct_backward=mask_estimator_final_direct_backward,
 )
 
 
@@ -229,6 +721,11 @@ def load_fused_band_split_extension() -> SimpleNamespace:
     return ops
 
 
-__all__ = ["ops", "load_fused_band_split_extension", "rms_norm_backward_into"] + [
+__all__ = [
+    "ops", "load_fused_band_split_extension", "rms_norm_backward_into", "band_split_forward_into",
+    "band_split_backward_into", "grouped_linear_backward", "mask_estimator_final_forward_into",
+    "mask_estimator_final_backward_into", "band_gather", "band_gather_backward", "band_recombine",
+    "band_recombine_backward",
+] + [
     name for name in vars(ops)
 ]
