@@ -64,6 +64,9 @@ PMB_API const char* pmb_version(void);
 /* Message describing the last failed call on this host thread ("" if none). */
 PMB_API const char* pmb_last_error(void);
 
+/* Number of kernels this library has launched in the process so far. */
+PMB_API uint64_t pmb_launch_count(void);
+
 /* ------------------------------------------------------------------------
  * RMSNorm over the last dimension (transformer RMSNorm, F.normalize form):
  *   inv_norm[r] = 1 / max(||x[r,:]||_2, 1e-12)
@@ -168,52 +171,57 @@ PMB_API int pmb_band_split_backward(const void* grad_out, const void* normed, co
  * `dtype` (reference convention) or fp32 (mixed precision on fp32 masters).
  *
  * Grouped linear, groups of equal shape (MaskEstimator hidden layers):
- *   out[m, g, :] = act(x[m, g, :] W[g]^T + bias[g]),  act = none | tanh
+ *   out[m, g, :] = act(x[m, g, :] W_g^T + bias_g),  act = none | tanh
  * x element (m, g, i) at m*x_stride_row + g*x_stride_group + i*x_stride_feat;
- * weight [G, O, I], bias [G, O] (nullable), out [rows, G, O].
+ * weights[g] [O, I], biases[g] [O] (array may be NULL), out [rows, G, O];
+ * G <= PMB_MAX_BANDS (per-group pointers, as the per-band Linear modules
+ * hold them; a packed [G, O, I] weight is passed as G row pointers).
  * Replaces grouped_linear_forward (.cpp:358-388; .cu:1006-1074), and with
  * activation = PMB_ACT_TANH fuses the hidden-layer Tanh that the reference
  * applies separately (fused_roformer.py:527-553).
  * ---------------------------------------------------------------------- */
 PMB_API int pmb_grouped_linear_forward(const void* x, int64_t rows, int64_t groups, int64_t in_features,
                                        int64_t out_features, int64_t x_stride_row, int64_t x_stride_group,
-                                       int64_t x_stride_feat, const void* weight, const void* bias, void* out,
-                                       int activation, int dtype, int param_dtype, void* stream);
+                                       int64_t x_stride_feat, const void* const* weights,
+                                       const void* const* biases, void* out, int activation, int dtype,
+                                       int param_dtype, void* stream);
 PMB_API int64_t pmb_grouped_linear_backward_workspace_size(int64_t rows, int64_t groups, int64_t out_features);
 /*
  * Backward of pmb_grouped_linear_forward for contiguous x [rows, G, I]:
  * `out` is the forward output (needed for tanh'), grad_x nullable,
- * grad_bias nullable.  (No reference counterpart: the reference's hidden
+ * grad_weights[g] [O, I], grad_biases (array nullable) [O].  (No reference counterpart: the reference's hidden
  * layers backpropagate through torch einsum, fused_roformer.py:1042-1048.)
  */
 PMB_API int pmb_grouped_linear_backward(const void* grad_out, const void* x, const void* out, int64_t rows,
                                         int64_t groups, int64_t in_features, int64_t out_features,
-                                        const void* weight, void* grad_x, void* grad_weight, void* grad_bias,
-                                        int activation, int dtype, int param_dtype, void* workspace,
-                                        int64_t workspace_bytes, void* stream);
+                                        const void* const* weights, void* grad_x, void* const* grad_weights,
+                                        void* const* grad_biases, int activation, int dtype, int param_dtype,
+                                        void* workspace, int64_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------
  * MaskEstimator final layer: per-band Linear(H -> 2*I_b) + GLU.
- * x [rows, num_bands, H]; weights[b] [2*I_b, H]; bias [2*total];
- *   pre[m, 2*off_b + j] = x[m,b,:] . W_b[j,:] + bias[2*off_b + j]
+ * x [rows, num_bands, H]; weights[b] [2*I_b, H]; biases[b] [2*I_b]
+ * (the reference's flat [2*total] bias is passed as per-band pointers);
+ *   pre[m, 2*off_b + j] = x[m,b,:] . W_b[j,:] + bias_b[j]
  *   out[m, off_b + l]   = pre[m, 2*off_b + l] * sigmoid(pre[m, 2*off_b + I_b + l])
  * out [rows, total], pre [rows, 2*total] (saved for the backward).
  * Replaces mask_estimator_final_direct_forward / mask_estimator_final_forward
  * (.cpp:560-693; .cu:2284-2420, .cu:2516-2553, .cu:2706-2760).
  * ---------------------------------------------------------------------- */
 PMB_API int pmb_mask_estimator_final_forward(const void* x, int64_t rows, int num_bands, int64_t hidden,
-                                             const int64_t* widths, const void* const* weights, const void* bias,
-                                             void* out, void* pre, int dtype, int param_dtype, void* stream);
+                                             const int64_t* widths, const void* const* weights,
+                                             const void* const* biases, void* out, void* pre, int dtype,
+                                             int param_dtype, void* stream);
 PMB_API int64_t pmb_mask_estimator_final_backward_workspace_size(int64_t rows, int num_bands, const int64_t* widths);
 /*
  * Backward: grad_out [rows, total] -> grad_x [rows, num_bands, H],
- * grad_bias [2*total], grad_weights[b] [2*I_b, H].
+ * grad_biases[b] [2*I_b], grad_weights[b] [2*I_b, H].
  * Replaces mask_estimator_final_direct_backward / mask_estimator_final_backward
  * (.cpp:591-729; .cu:2556-2704, .cu:2422-2513, .cu:2762-2851).
  */
 PMB_API int pmb_mask_estimator_final_backward(const void* grad_out, const void* x, const void* pre, int64_t rows,
                                               int num_bands, int64_t hidden, const int64_t* widths,
-                                              const void* const* weights, void* grad_x, void* grad_bias,
+                                              const void* const* weights, void* grad_x, void* const* grad_biases,
                                               void* const* grad_weights, int dtype, int param_dtype,
                                               void* workspace, int64_t workspace_bytes, void* stream);
 
@@ -274,6 +282,23 @@ PMB_API int pmb_band_recombine_backward(const float* grad_out, const float* stft
                                         const int* inv_ptr, int64_t batch, int64_t stems, int64_t channels,
                                         int64_t freqs, int64_t frames, int64_t pairs, int multiply_stft,
                                         void* grad_mask, int mask_dtype, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Attention input projection split with rotary embedding (training path).
+ *   qkv [B*N, 3, H, Dh] (= x W_qkv^T)  ->  q, k, v [B, H, N, Dh]
+ * q and k are rotated (if rotate_qk) by cos/sin fp32 [N, Dh/2]:
+ *   (e, o) -> (e c - o s, o c + e s)   on interleaved pairs.
+ * merge is the backward: grad_q/k/v [B, H, N, Dh] -> grad_qkv [B*N, 3*H*Dh]
+ * with the inverse rotation.  Replaces qkv_to_bnhd + rotary_forward /
+ * rotary_backward on q and k (fused_roformer.py:710-732, 793-818;
+ * .cu:1077-1168) with one pass each way.
+ * ---------------------------------------------------------------------- */
+PMB_API int pmb_qkv_rotary_split(const void* qkv, const float* cos, const float* sin, int64_t batch,
+                                 int64_t seq_len, int64_t heads, int64_t dim_head, void* q, void* k, void* v,
+                                 int rotate_qk, int dtype, void* stream);
+PMB_API int pmb_qkv_rotary_merge(const void* grad_q, const void* grad_k, const void* grad_v, const float* cos,
+                                 const float* sin, int64_t batch, int64_t seq_len, int64_t heads,
+                                 int64_t dim_head, void* grad_qkv, int rotate_qk, int dtype, void* stream);
 
 #ifdef __cplusplus
 }

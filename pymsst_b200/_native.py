@@ -28,6 +28,7 @@ _pi64 = ctypes.POINTER(ctypes.c_int64)
 SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "pmb_version": (ctypes.c_char_p, []),
     "pmb_last_error": (ctypes.c_char_p, []),
+    "pmb_launch_count": (ctypes.c_uint64, []),
     "pmb_rms_norm_forward": (_i, [_p, _p, _p, _p, _p, _i64, _i64, _i, _i, _i, _p]),
     "pmb_rms_norm_backward_workspace_size": (_i64, [_i64, _i64]),
     "pmb_rms_norm_backward": (_i, [_p, _p, _i, _p, _p, _p, _p, _i64, _i64, _i, _i, _i, _i, _p, _i64, _p]),
@@ -39,14 +40,14 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "pmb_band_split_backward": (
         _i, [_p, _p, _p, _i64, _i, _pi64, _pp, _pp, _i64, _p, _pp, _pp, _pp, _i, _i, _p, _i64, _p]),
     "pmb_grouped_linear_forward": (
-        _i, [_p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _i, _i, _i, _p]),
+        _i, [_p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _pp, _pp, _p, _i, _i, _i, _p]),
     "pmb_grouped_linear_backward_workspace_size": (_i64, [_i64, _i64, _i64]),
     "pmb_grouped_linear_backward": (
-        _i, [_p, _p, _p, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _i, _i, _i, _p, _i64, _p]),
-    "pmb_mask_estimator_final_forward": (_i, [_p, _i64, _i, _i64, _pi64, _pp, _p, _p, _p, _i, _i, _p]),
+        _i, [_p, _p, _p, _i64, _i64, _i64, _i64, _pp, _p, _pp, _pp, _i, _i, _i, _p, _i64, _p]),
+    "pmb_mask_estimator_final_forward": (_i, [_p, _i64, _i, _i64, _pi64, _pp, _pp, _p, _p, _i, _i, _p]),
     "pmb_mask_estimator_final_backward_workspace_size": (_i64, [_i64, _i, _pi64]),
     "pmb_mask_estimator_final_backward": (
-        _i, [_p, _p, _p, _i64, _i, _i64, _pi64, _pp, _p, _p, _pp, _i, _i, _p, _i64, _p]),
+        _i, [_p, _p, _p, _i64, _i, _i64, _pi64, _pp, _p, _pp, _pp, _i, _i, _p, _i64, _p]),
     "pmb_attention_gate_forward": (
         _i, [_p, _i64, _i64, _i64, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _p, _i, _i, _p]),
     "pmb_attention_gate_backward_workspace_size": (_i64, [_i64, _i64, _i64]),
@@ -57,6 +58,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "pmb_band_gather_backward": (_i, [_p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p, _i, _p]),
     "pmb_band_recombine_forward": (_i, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i, _p, _i, _p]),
     "pmb_band_recombine_backward": (_i, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i, _p, _i, _p]),
+    "pmb_qkv_rotary_split": (_i, [_p, _p, _p, _i64, _i64, _i64, _i64, _p, _p, _p, _i, _i, _p]),
+    "pmb_qkv_rotary_merge": (_i, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _i, _i, _p]),
 }
 
 

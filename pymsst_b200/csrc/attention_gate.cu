@@ -250,6 +250,7 @@ extern "C" int pmb_attention_gate_backward(const void* grad_out, const void* att
     dim3 gp((cols + kThreads - 1) / kThreads, nch);
     gate_bwd_weight_partial<T><<<gp, kThreads, 0, s>>>(ggp, static_cast<const T*>(x), rows, (int)heads, (int)dim,
                                                        partial);
+    PMB_CHECK_LAUNCH(name);
     gate_bwd_weight_finalize<TP><<<(cols + kThreads - 1) / kThreads, kThreads, 0, s>>>(
         partial, nch, (int)heads, (int)dim, static_cast<TP*>(grad_weight), static_cast<TP*>(grad_bias));
     PMB_CHECK_LAUNCH(name);

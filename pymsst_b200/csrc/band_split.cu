@@ -264,6 +264,7 @@ int bwd_impl(const void* dy, const void* normed, const float* inv_norm, int64_t 
     const int64_t cols = (int64_t)wtab.count * O;
     dim3 gp((int)((cols + 255) / 256), L.row_chunks);
     red::colsum_partial<T><<<gp, red::kThreads, 0, stream>>>(static_cast<const T*>(dy), rows, cols, cols, dbp);
+    PMB_CHECK_LAUNCH("pmb_band_split_backward(bias partial)");
     red::colsum_finalize_bands<<<(int)((cols + 255) / 256), red::kThreads, 0, stream>>>(dbp, L.row_chunks, cols, btab,
                                                                                          pcode);
     PMB_CHECK_LAUNCH("pmb_band_split_backward(bias)");

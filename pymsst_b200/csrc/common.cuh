@@ -72,6 +72,8 @@ inline int dtype_size(int code) {
 // ---------------------------------------------------------------------------
 void set_error(const char* fmt, ...);
 void clear_error();
+// Counts kernel launches made by this library (read by pmb_launch_count()).
+void count_launch();
 
 #define PMB_REQUIRE(cond, ...)                  \
   do {                                          \
@@ -81,8 +83,10 @@ void clear_error();
     }                                           \
   } while (0)
 
+// Every kernel launch in the library is followed by exactly one of these.
 #define PMB_CHECK_LAUNCH(name)                                                        \
   do {                                                                                \
+    ::pmb::count_launch();                                                            \
     cudaError_t err__ = cudaGetLastError();                                           \
     if (err__ != cudaSuccess) {                                                       \
       ::pmb::set_error("%s: kernel launch failed: %s", name, cudaGetErrorString(err__)); \

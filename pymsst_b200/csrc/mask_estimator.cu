@@ -14,6 +14,8 @@
 #include "gemm_simt.cuh"
 #include "reduce.cuh"
 
+#include <vector>
+
 namespace pmb {
 namespace {
 
@@ -23,10 +25,10 @@ __device__ __forceinline__ float sigmoidf_(float v) { return 1.0f / (1.0f + expf
 
 // ------------------------------------------------------ final layer (GLU)
 // tab.ptr0 = W_b [2w, H]
+// tab.ptr1 = bias_b [2w]
 template <typename T, typename TP>
 __global__ void __launch_bounds__(simt::kThreads)
-    final_fwd_gemm(const T* __restrict__ x, int64_t rows, int64_t H, BandTable tab, const TP* __restrict__ bias,
-                   T* __restrict__ pre) {
+    final_fwd_gemm(const T* __restrict__ x, int64_t rows, int64_t H, BandTable tab, T* __restrict__ pre) {
   __shared__ simt::Smem sm;
   const int b = blockIdx.y;
   const int64_t w2 = 2 * (tab.off[b + 1] - tab.off[b]);
@@ -40,6 +42,7 @@ __global__ void __launch_bounds__(simt::kThreads)
                                      false, nullptr, acc);
   const int64_t c0 = 2 * tab.off[b];
   const int64_t ld = 2 * tab.total;
+  const TP* bias = static_cast<const TP*>(tab.ptr1[b]);
 #pragma unroll
   for (int i = 0; i < simt::TM; ++i) {
     const int m = m0 + simt::row_of(i);
@@ -48,7 +51,7 @@ __global__ void __launch_bounds__(simt::kThreads)
     for (int j = 0; j < simt::TN; ++j) {
       const int n = n0 + simt::col_of(j);
       if (n >= w2) continue;
-      pre[(int64_t)m * ld + c0 + n] = Elem<T>::from_f(acc[i][j] + Elem<TP>::to_f(bias[c0 + n]));
+      pre[(int64_t)m * ld + c0 + n] = Elem<T>::from_f(acc[i][j] + Elem<TP>::to_f(bias[n]));
     }
   }
 }
@@ -145,19 +148,20 @@ struct GL {
   int64_t xs_m, xs_g, xs_i;
 };
 
+// tab.ptr0 = W_g [O, I], tab.ptr1 = bias_g [O] (may be NULL)
 template <typename T, typename TP, bool KCONTIG>
 __global__ void __launch_bounds__(simt::kThreads)
-    grouped_fwd(const T* __restrict__ x, GL p, const TP* __restrict__ W, const TP* __restrict__ bias,
-                T* __restrict__ out, int act) {
+    grouped_fwd(const T* __restrict__ x, GL p, BandTable tab, T* __restrict__ out, int act) {
   __shared__ simt::Smem sm;
   const int g = blockIdx.y;
+  const TP* W = static_cast<const TP*>(tab.ptr0[g]);
+  const TP* bias = static_cast<const TP*>(tab.ptr1[g]);
   const int ntn = simt::tiles(p.out_f, simt::BN);
   const int m0 = (blockIdx.x / ntn) * simt::BM;
   const int n0 = (blockIdx.x % ntn) * simt::BN;
   float acc[simt::TM][simt::TN];
-  simt::mainloop<T, TP, KCONTIG, true>(sm, x + g * p.xs_g, p.xs_m, p.xs_i, W + (int64_t)g * p.out_f * p.in_f,
-                                        p.in_f, 1, m0, (int)p.rows, n0, (int)p.out_f, (int)p.in_f, false, nullptr,
-                                        acc);
+  simt::mainloop<T, TP, KCONTIG, true>(sm, x + g * p.xs_g, p.xs_m, p.xs_i, W, p.in_f, 1, m0, (int)p.rows, n0,
+                                        (int)p.out_f, (int)p.in_f, false, nullptr, acc);
 #pragma unroll
   for (int i = 0; i < simt::TM; ++i) {
     const int m = m0 + simt::row_of(i);
@@ -167,7 +171,7 @@ __global__ void __launch_bounds__(simt::kThreads)
       const int o = n0 + simt::col_of(j);
       if (o >= p.out_f) continue;
       float v = acc[i][j];
-      if (bias != nullptr) v += Elem<TP>::to_f(bias[(int64_t)g * p.out_f + o]);
+      if (bias != nullptr) v += Elem<TP>::to_f(bias[o]);
       if (act == PMB_ACT_TANH) v = tanhf(v);
       out[((int64_t)m * p.groups + g) * p.out_f + o] = Elem<T>::from_f(v);
     }
@@ -189,16 +193,16 @@ __global__ void __launch_bounds__(kThreads)
 
 template <typename T, typename TP>
 __global__ void __launch_bounds__(simt::kThreads)
-    grouped_bwd_x(const float* __restrict__ dpre, GL p, const TP* __restrict__ W, T* __restrict__ grad_x) {
+    grouped_bwd_x(const float* __restrict__ dpre, GL p, BandTable tab, T* __restrict__ grad_x) {
   __shared__ simt::Smem sm;
   const int g = blockIdx.y;
+  const TP* W = static_cast<const TP*>(tab.ptr0[g]);
   const int ntn = simt::tiles(p.in_f, simt::BN);
   const int m0 = (blockIdx.x / ntn) * simt::BM;
   const int n0 = (blockIdx.x % ntn) * simt::BN;
   float acc[simt::TM][simt::TN];
-  simt::mainloop<float, TP, true, false>(sm, dpre + g * p.out_f, p.groups * p.out_f, 1,
-                                        W + (int64_t)g * p.out_f * p.in_f, 1, p.in_f, m0, (int)p.rows, n0,
-                                        (int)p.in_f, (int)p.out_f, false, nullptr, acc);
+  simt::mainloop<float, TP, true, false>(sm, dpre + g * p.out_f, p.groups * p.out_f, 1, W, 1, p.in_f, m0,
+                                         (int)p.rows, n0, (int)p.in_f, (int)p.out_f, false, nullptr, acc);
 #pragma unroll
   for (int i = 0; i < simt::TM; ++i) {
     const int m = m0 + simt::row_of(i);
@@ -213,9 +217,10 @@ __global__ void __launch_bounds__(simt::kThreads)
 
 template <typename T, typename TP>
 __global__ void __launch_bounds__(simt::kThreads)
-    grouped_bwd_w(const float* __restrict__ dpre, const T* __restrict__ x, GL p, TP* __restrict__ grad_w) {
+    grouped_bwd_w(const float* __restrict__ dpre, const T* __restrict__ x, GL p, BandTable tab) {
   __shared__ simt::Smem sm;
   const int g = blockIdx.y;
+  TP* grad_w = static_cast<TP*>(const_cast<void*>(tab.ptr2[g]));
   const int ntn = simt::tiles(p.in_f, simt::BN);
   const int m0 = (blockIdx.x / ntn) * simt::BM;  // over o
   const int n0 = (blockIdx.x % ntn) * simt::BN;  // over i
@@ -229,7 +234,7 @@ __global__ void __launch_bounds__(simt::kThreads)
 #pragma unroll
     for (int j = 0; j < simt::TN; ++j) {
       const int c = n0 + simt::col_of(j);
-      if (c < p.in_f) grad_w[((int64_t)g * p.out_f + o) * p.in_f + c] = Elem<TP>::from_f(acc[i][j]);
+      if (c < p.in_f) grad_w[(int64_t)o * p.in_f + c] = Elem<TP>::from_f(acc[i][j]);
     }
   }
 }
@@ -250,22 +255,24 @@ using namespace pmb;
 
 // --------------------------------------------------------------- final layer
 extern "C" int pmb_mask_estimator_final_forward(const void* x, int64_t rows, int num_bands, int64_t hidden,
-                                                const int64_t* widths, const void* const* weights, const void* bias,
-                                                void* out, void* pre, int dtype, int param_dtype, void* stream) {
+                                                const int64_t* widths, const void* const* weights,
+                                                const void* const* biases, void* out, void* pre, int dtype,
+                                                int param_dtype, void* stream) {
   clear_error();
   const char* name = "pmb_mask_estimator_final_forward";
   BandTable tab;
-  int st = make_band_table(tab, num_bands, widths, weights, nullptr, nullptr, name);
+  int st = make_band_table(tab, num_bands, widths, weights, biases, nullptr, name);
   if (st) return st;
   PMB_REQUIRE(rows >= 0 && hidden > 0, "%s: bad shape", name);
   if (rows == 0) return PMB_OK;
-  PMB_REQUIRE(x && bias && out && pre && weights, "%s: NULL tensor argument", name);
-  for (int b = 0; b < num_bands; ++b) PMB_REQUIRE(tab.ptr0[b], "%s: band %d weight is NULL", name, b);
+  PMB_REQUIRE(x && biases && out && pre && weights, "%s: NULL tensor argument", name);
+  for (int b = 0; b < num_bands; ++b)
+    PMB_REQUIRE(tab.ptr0[b] && tab.ptr1[b], "%s: band %d weight or bias is NULL", name, b);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return PMB_DISPATCH_PARAM(dtype, param_dtype, T, TP, name, [&] {
     dim3 grid(simt::tiles(rows, simt::BM) * simt::tiles(2 * (int64_t)tab.max_width, simt::BN), num_bands);
     final_fwd_gemm<T, TP><<<grid, simt::kThreads, 0, s>>>(static_cast<const T*>(x), rows, hidden, tab,
-                                                           static_cast<const TP*>(bias), static_cast<T*>(pre));
+                                                           static_cast<T*>(pre));
     PMB_CHECK_LAUNCH(name);
     glu_fwd<T><<<elementwise_grid(rows * tab.total), kThreads, 0, s>>>(static_cast<const T*>(pre), rows, tab,
                                                                         static_cast<T*>(out));
@@ -284,24 +291,32 @@ extern "C" int64_t pmb_mask_estimator_final_backward_workspace_size(int64_t rows
 
 extern "C" int pmb_mask_estimator_final_backward(const void* grad_out, const void* x, const void* pre, int64_t rows,
                                                  int num_bands, int64_t hidden, const int64_t* widths,
-                                                 const void* const* weights, void* grad_x, void* grad_bias,
+                                                 const void* const* weights, void* grad_x, void* const* grad_biases,
                                                  void* const* grad_weights, int dtype, int param_dtype,
                                                  void* workspace, int64_t workspace_bytes, void* stream) {
   clear_error();
   const char* name = "pmb_mask_estimator_final_backward";
-  BandTable tab;
+  BandTable tab, btab;
   int st = make_band_table(tab, num_bands, widths, weights, (const void* const*)grad_weights, nullptr, name);
   if (st) return st;
   PMB_REQUIRE(rows >= 0 && hidden > 0, "%s: bad shape", name);
-  PMB_REQUIRE(weights && grad_weights && grad_bias && grad_x, "%s: NULL argument", name);
-  for (int b = 0; b < num_bands; ++b) PMB_REQUIRE(tab.ptr0[b] && tab.ptr1[b], "%s: band %d pointer is NULL", name, b);
+  PMB_REQUIRE(weights && grad_weights && grad_biases && grad_x, "%s: NULL argument", name);
+  {
+    std::vector<int64_t> w2(num_bands);
+    for (int b = 0; b < num_bands; ++b) w2[b] = 2 * widths[b];
+    st = make_band_table(btab, num_bands, w2.data(), (const void* const*)grad_biases, nullptr, nullptr, name);
+    if (st) return st;
+  }
+  for (int b = 0; b < num_bands; ++b)
+    PMB_REQUIRE(tab.ptr0[b] && tab.ptr1[b] && btab.ptr0[b], "%s: band %d pointer is NULL", name, b);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int es = dtype_size(param_dtype);
   PMB_REQUIRE(es > 0, "%s: unsupported parameter dtype %d", name, param_dtype);
   if (rows == 0) {
-    PMB_CHECK_CUDA(cudaMemsetAsync(grad_bias, 0, 2 * tab.total * es, s), name);
-    for (int b = 0; b < num_bands; ++b)
+    for (int b = 0; b < num_bands; ++b) {
+      PMB_CHECK_CUDA(cudaMemsetAsync(grad_biases[b], 0, 2 * (tab.off[b + 1] - tab.off[b]) * es, s), name);
       PMB_CHECK_CUDA(cudaMemsetAsync(grad_weights[b], 0, 2 * (tab.off[b + 1] - tab.off[b]) * hidden * es, s), name);
+    }
     return PMB_OK;
   }
   PMB_REQUIRE(grad_out && x && pre, "%s: NULL tensor argument", name);
@@ -320,8 +335,9 @@ extern "C" int pmb_mask_estimator_final_backward(const void* grad_out, const voi
     const int64_t cols = 2 * tab.total;
     dim3 gpart((int)((cols + 255) / 256), red::chunks(rows));
     red::colsum_partial<float><<<gpart, red::kThreads, 0, s>>>(gp, rows, cols, cols, partial);
-    red::colsum_finalize<<<(int)((cols + 255) / 256), red::kThreads, 0, s>>>(partial, red::chunks(rows), cols,
-                                                                             grad_bias, param_dtype);
+    PMB_CHECK_LAUNCH(name);
+    red::colsum_finalize_bands<<<(int)((cols + 255) / 256), red::kThreads, 0, s>>>(partial, red::chunks(rows), cols,
+                                                                                   btab, param_dtype);
     PMB_CHECK_LAUNCH(name);
     dim3 gx(simt::tiles(rows, simt::BM) * simt::tiles(hidden, simt::BN), num_bands);
     final_bwd_x<T, TP><<<gx, simt::kThreads, 0, s>>>(gp, rows, hidden, tab, static_cast<T*>(grad_x));
@@ -336,30 +352,34 @@ extern "C" int pmb_mask_estimator_final_backward(const void* grad_out, const voi
 // ------------------------------------------------------------ grouped linear
 extern "C" int pmb_grouped_linear_forward(const void* x, int64_t rows, int64_t groups, int64_t in_features,
                                           int64_t out_features, int64_t x_stride_row, int64_t x_stride_group,
-                                          int64_t x_stride_feat, const void* weight, const void* bias, void* out,
-                                          int activation, int dtype, int param_dtype, void* stream) {
+                                          int64_t x_stride_feat, const void* const* weights,
+                                          const void* const* biases, void* out, int activation, int dtype,
+                                          int param_dtype, void* stream) {
   clear_error();
   const char* name = "pmb_grouped_linear_forward";
-  PMB_REQUIRE(rows >= 0 && groups > 0 && groups <= 65535 && in_features > 0 && out_features > 0,
-              "%s: bad shape", name);
+  PMB_REQUIRE(rows >= 0 && groups > 0 && groups <= kMaxBands && in_features > 0 && out_features > 0,
+              "%s: bad shape (groups must be 1..%d)", name, kMaxBands);
+  BandTable tab;
+  {
+    std::vector<int64_t> ow(groups, out_features);
+    int st = make_band_table(tab, (int)groups, ow.data(), weights, biases, nullptr, name);
+    if (st) return st;
+  }
   PMB_REQUIRE(activation == PMB_ACT_NONE || activation == PMB_ACT_TANH, "%s: unknown activation %d", name,
               activation);
   if (rows == 0) return PMB_OK;
-  PMB_REQUIRE(x && weight && out, "%s: NULL tensor argument", name);
+  PMB_REQUIRE(x && weights && out, "%s: NULL tensor argument", name);
+  for (int g = 0; g < groups; ++g) PMB_REQUIRE(tab.ptr0[g], "%s: group %d weight is NULL", name, g);
   GL p{rows, groups, in_features, out_features, x_stride_row, x_stride_group, x_stride_feat};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return PMB_DISPATCH_PARAM(dtype, param_dtype, T, TP, name, [&] {
     dim3 grid(simt::tiles(rows, simt::BM) * simt::tiles(out_features, simt::BN), (unsigned)groups);
     if (x_stride_feat == 1)
-      grouped_fwd<T, TP, true><<<grid, simt::kThreads, 0, s>>>(static_cast<const T*>(x), p,
-                                                               static_cast<const TP*>(weight),
-                                                               static_cast<const TP*>(bias), static_cast<T*>(out),
-                                                               activation);
+      grouped_fwd<T, TP, true><<<grid, simt::kThreads, 0, s>>>(static_cast<const T*>(x), p, tab,
+                                                               static_cast<T*>(out), activation);
     else
-      grouped_fwd<T, TP, false><<<grid, simt::kThreads, 0, s>>>(static_cast<const T*>(x), p,
-                                                                static_cast<const TP*>(weight),
-                                                                static_cast<const TP*>(bias), static_cast<T*>(out),
-                                                                activation);
+      grouped_fwd<T, TP, false><<<grid, simt::kThreads, 0, s>>>(static_cast<const T*>(x), p, tab,
+                                                                static_cast<T*>(out), activation);
     PMB_CHECK_LAUNCH(name);
     return PMB_OK;
   });
@@ -373,24 +393,40 @@ extern "C" int64_t pmb_grouped_linear_backward_workspace_size(int64_t rows, int6
 
 extern "C" int pmb_grouped_linear_backward(const void* grad_out, const void* x, const void* out, int64_t rows,
                                            int64_t groups, int64_t in_features, int64_t out_features,
-                                           const void* weight, void* grad_x, void* grad_weight, void* grad_bias,
-                                           int activation, int dtype, int param_dtype, void* workspace,
-                                           int64_t workspace_bytes, void* stream) {
+                                           const void* const* weights, void* grad_x, void* const* grad_weights,
+                                           void* const* grad_biases, int activation, int dtype, int param_dtype,
+                                           void* workspace, int64_t workspace_bytes, void* stream) {
   clear_error();
   const char* name = "pmb_grouped_linear_backward";
-  PMB_REQUIRE(rows >= 0 && groups > 0 && groups <= 65535 && in_features > 0 && out_features > 0,
-              "%s: bad shape", name);
+  PMB_REQUIRE(rows >= 0 && groups > 0 && groups <= kMaxBands && in_features > 0 && out_features > 0,
+              "%s: bad shape (groups must be 1..%d)", name, kMaxBands);
+  BandTable tab, btab;
+  {
+    std::vector<int64_t> ow(groups, out_features);
+    int st = make_band_table(tab, (int)groups, ow.data(), weights, nullptr, (const void* const*)grad_weights, name);
+    if (st) return st;
+    btab.count = 0;
+    if (grad_biases != nullptr) {
+      st = make_band_table(btab, (int)groups, ow.data(), (const void* const*)grad_biases, nullptr, nullptr, name);
+      if (st) return st;
+    }
+  }
   PMB_REQUIRE(activation == PMB_ACT_NONE || activation == PMB_ACT_TANH, "%s: unknown activation %d", name,
               activation);
-  PMB_REQUIRE(weight && grad_weight, "%s: NULL argument", name);
+  PMB_REQUIRE(weights && grad_weights, "%s: NULL argument", name);
+  for (int g = 0; g < groups; ++g)
+    PMB_REQUIRE(tab.ptr0[g] && tab.ptr2[g] && (btab.count == 0 || btab.ptr0[g]), "%s: group %d pointer is NULL",
+                name, g);
   PMB_REQUIRE(activation != PMB_ACT_TANH || out != nullptr || rows == 0, "%s: tanh backward needs `out`", name);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int es = dtype_size(param_dtype);
   PMB_REQUIRE(es > 0, "%s: unsupported parameter dtype %d", name, param_dtype);
   const int64_t cols = groups * out_features;
   if (rows == 0) {
-    PMB_CHECK_CUDA(cudaMemsetAsync(grad_weight, 0, cols * in_features * es, s), name);
-    if (grad_bias) PMB_CHECK_CUDA(cudaMemsetAsync(grad_bias, 0, cols * es, s), name);
+    for (int g = 0; g < groups; ++g) {
+      PMB_CHECK_CUDA(cudaMemsetAsync(grad_weights[g], 0, out_features * in_features * es, s), name);
+      if (btab.count) PMB_CHECK_CUDA(cudaMemsetAsync(grad_biases[g], 0, out_features * es, s), name);
+    }
     return PMB_OK;
   }
   PMB_REQUIRE(grad_out && x, "%s: NULL tensor argument", name);
@@ -408,22 +444,21 @@ extern "C" int pmb_grouped_linear_backward(const void* grad_out, const void* x, 
                                                                   static_cast<const T*>(out), rows * cols, activation,
                                                                   dpre);
     PMB_CHECK_LAUNCH(name);
-    if (grad_bias != nullptr) {
+    if (btab.count > 0) {
       dim3 gpart((int)((cols + 255) / 256), red::chunks(rows));
       red::colsum_partial<float><<<gpart, red::kThreads, 0, s>>>(dpre, rows, cols, cols, partial);
-      red::colsum_finalize<<<(int)((cols + 255) / 256), red::kThreads, 0, s>>>(partial, red::chunks(rows), cols,
-                                                                               grad_bias, param_dtype);
+      PMB_CHECK_LAUNCH(name);
+      red::colsum_finalize_bands<<<(int)((cols + 255) / 256), red::kThreads, 0, s>>>(partial, red::chunks(rows), cols,
+                                                                                     btab, param_dtype);
       PMB_CHECK_LAUNCH(name);
     }
     if (grad_x != nullptr) {
       dim3 gx(simt::tiles(rows, simt::BM) * simt::tiles(in_features, simt::BN), (unsigned)groups);
-      grouped_bwd_x<T, TP><<<gx, simt::kThreads, 0, s>>>(dpre, p, static_cast<const TP*>(weight),
-                                                         static_cast<T*>(grad_x));
+      grouped_bwd_x<T, TP><<<gx, simt::kThreads, 0, s>>>(dpre, p, tab, static_cast<T*>(grad_x));
       PMB_CHECK_LAUNCH(name);
     }
     dim3 gw(simt::tiles(out_features, simt::BM) * simt::tiles(in_features, simt::BN), (unsigned)groups);
-    grouped_bwd_w<T, TP><<<gw, simt::kThreads, 0, s>>>(dpre, static_cast<const T*>(x), p,
-                                                       static_cast<TP*>(grad_weight));
+    grouped_bwd_w<T, TP><<<gw, simt::kThreads, 0, s>>>(dpre, static_cast<const T*>(x), p, tab);
     PMB_CHECK_LAUNCH(name);
     return PMB_OK;
   });

@@ -1,0 +1,128 @@
+// Split of the attention input projection into the attention layout, with the
+// rotary embedding applied to q and k on the way (forward), and the inverse
+// (backward): one memory pass each, so q/k make no separate rotary round trip.
+//
+//   qkv [B*N, 3, H, Dh]  (x W_qkv^T, the 'b n (qkv h d)' layout)
+//   q, k, v [B, H, N, Dh] (the layout scaled-dot-product attention takes)
+//   rotation of interleaved pairs by angle table cos/sin fp32 [N, Dh/2]:
+//     (e, o) -> (e c - o s, o c + e s);  backward (e, o) -> (e c + o s, o c - e s)
+// Reference semantics: rotary .cu:1077-1128 applied to q/k after
+// qkv_to_bnhd (src/pymsst/training/fused_roformer.py:710-732, 793-818);
+// the angles follow rotary-embedding-torch: theta_i = n / 10000^(2i/Dh).
+#include "common.cuh"
+
+namespace pmb {
+namespace {
+
+constexpr int kThreads = 256;
+
+template <typename T, int P>
+struct alignas((sizeof(T) * 2 * P) < 16 ? (sizeof(T) * 2 * P) : 16) Chunk {
+  T v[2 * P];
+};
+
+struct QkvDims {
+  int64_t B, N;
+  int H, Dh;
+};
+
+template <typename T, int P, bool BACKWARD>
+__global__ void __launch_bounds__(kThreads)
+    qkv_rotary_kernel(T* __restrict__ qkv, const float* __restrict__ cosv, const float* __restrict__ sinv, QkvDims d,
+                      T* __restrict__ q, T* __restrict__ k, T* __restrict__ v, int rotate_qk, int64_t units) {
+  const int gph = d.Dh / (2 * P);
+  const int half = d.Dh / 2;
+  for (int64_t u = (int64_t)blockIdx.x * kThreads + threadIdx.x; u < units; u += (int64_t)gridDim.x * kThreads) {
+    const int grp = (int)(u % gph);
+    int64_t rest = u / gph;
+    const int h = (int)(rest % d.H);
+    rest /= d.H;
+    const int which = (int)(rest % 3);
+    const int64_t row = rest / 3;
+    const int64_t b = row / d.N, n = row % d.N;
+    T* packed = qkv + ((row * 3 + which) * d.H + h) * d.Dh + grp * 2 * P;
+    T* base = which == 0 ? q : (which == 1 ? k : v);
+    T* split = base + ((b * d.H + h) * d.N + n) * d.Dh + grp * 2 * P;
+    const Chunk<T, P> in = *reinterpret_cast<const Chunk<T, P>*>(BACKWARD ? split : packed);
+    Chunk<T, P> out;
+    if (which < 2 && rotate_qk) {
+#pragma unroll
+      for (int p = 0; p < P; ++p) {
+        const float c = cosv[n * half + grp * P + p];
+        const float s = BACKWARD ? -sinv[n * half + grp * P + p] : sinv[n * half + grp * P + p];
+        const float e = Elem<T>::to_f(in.v[2 * p]), o = Elem<T>::to_f(in.v[2 * p + 1]);
+        out.v[2 * p] = Elem<T>::from_f(e * c - o * s);
+        out.v[2 * p + 1] = Elem<T>::from_f(o * c + e * s);
+      }
+    } else {
+      out = in;
+    }
+    *reinterpret_cast<Chunk<T, P>*>(BACKWARD ? packed : split) = out;
+  }
+}
+
+template <typename T, bool BACKWARD>
+int launch(void* qkv, const float* cosv, const float* sinv, QkvDims d, void* q, void* k, void* v, int rotate,
+           cudaStream_t stream, const char* name) {
+  const uintptr_t al = reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(q) |
+                       reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v);
+  constexpr int P = sizeof(T) == 2 ? 4 : 2;  // 16-byte chunks
+  const bool vec = (d.Dh % (2 * P)) == 0 && (al % 16) == 0;
+  const int64_t pairs_per_row = 3LL * d.H * (d.Dh / 2);
+  const int64_t cap = (int64_t)num_sms() * 32;
+  auto grid_for = [&](int64_t units) {
+    int64_t g = (units + kThreads - 1) / kThreads;
+    if (g > cap) g = cap;
+    return (int)(g < 1 ? 1 : g);
+  };
+  if (vec) {
+    const int64_t units = d.B * d.N * pairs_per_row / P;
+    qkv_rotary_kernel<T, P, BACKWARD><<<grid_for(units), kThreads, 0, stream>>>(
+        static_cast<T*>(qkv), cosv, sinv, d, static_cast<T*>(q), static_cast<T*>(k), static_cast<T*>(v), rotate, units);
+  } else {
+    const int64_t units = d.B * d.N * pairs_per_row;
+    qkv_rotary_kernel<T, 1, BACKWARD><<<grid_for(units), kThreads, 0, stream>>>(
+        static_cast<T*>(qkv), cosv, sinv, d, static_cast<T*>(q), static_cast<T*>(k), static_cast<T*>(v), rotate, units);
+  }
+  PMB_CHECK_LAUNCH(name);
+  return PMB_OK;
+}
+
+}  // namespace
+}  // namespace pmb
+
+using namespace pmb;
+
+extern "C" int pmb_qkv_rotary_split(const void* qkv, const float* cos, const float* sin, int64_t batch,
+                                    int64_t seq_len, int64_t heads, int64_t dim_head, void* q, void* k, void* v,
+                                    int rotate_qk, int dtype, void* stream) {
+  clear_error();
+  const char* name = "pmb_qkv_rotary_split";
+  PMB_REQUIRE(batch >= 0 && seq_len >= 0 && heads > 0 && dim_head > 0 && dim_head % 2 == 0,
+              "%s: bad shape (dim_head must be even)", name);
+  if (batch * seq_len == 0) return PMB_OK;
+  PMB_REQUIRE(qkv && q && k && v && (!rotate_qk || (cos && sin)), "%s: NULL tensor argument", name);
+  QkvDims d{batch, seq_len, (int)heads, (int)dim_head};
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return PMB_DISPATCH(dtype, T, name, [&] {
+    return launch<T, false>(const_cast<void*>(qkv), cos, sin, d, q, k, v, rotate_qk, s, name);
+  });
+}
+
+extern "C" int pmb_qkv_rotary_merge(const void* grad_q, const void* grad_k, const void* grad_v, const float* cos,
+                                    const float* sin, int64_t batch, int64_t seq_len, int64_t heads,
+                                    int64_t dim_head, void* grad_qkv, int rotate_qk, int dtype, void* stream) {
+  clear_error();
+  const char* name = "pmb_qkv_rotary_merge";
+  PMB_REQUIRE(batch >= 0 && seq_len >= 0 && heads > 0 && dim_head > 0 && dim_head % 2 == 0,
+              "%s: bad shape (dim_head must be even)", name);
+  if (batch * seq_len == 0) return PMB_OK;
+  PMB_REQUIRE(grad_q && grad_k && grad_v && grad_qkv && (!rotate_qk || (cos && sin)), "%s: NULL tensor argument",
+              name);
+  QkvDims d{batch, seq_len, (int)heads, (int)dim_head};
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return PMB_DISPATCH(dtype, T, name, [&] {
+    return launch<T, true>(grad_qkv, cos, sin, d, const_cast<void*>(grad_q), const_cast<void*>(grad_k),
+                           const_cast<void*>(grad_v), rotate_qk, s, name);
+  });
+}

@@ -1,4 +1,5 @@
 // Error channel and small shared host utilities of the C ABI.
+#include <atomic>
 #include <cstring>
 
 #include "common.cuh"
@@ -15,6 +16,10 @@ void set_error(const char* fmt, ...) {
 }
 
 void clear_error() { g_last_error[0] = 0; }
+
+static std::atomic<uint64_t> g_launches{0};
+
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 int make_band_table(BandTable& t, int count, const int64_t* widths, const void* const* p0,
                     const void* const* p1, const void* const* p2, const char* name) {
@@ -55,5 +60,7 @@ extern "C" {
 const char* pmb_version(void) { return "0.1.0"; }
 
 const char* pmb_last_error(void) { return pmb::g_last_error; }
+
+uint64_t pmb_launch_count(void) { return pmb::g_launches.load(std::memory_order_relaxed); }
 
 }  // extern "C"

@@ -431,17 +431,28 @@ def grouped_linear_forward(x, weight, bias=None, activation: int = 0):
         _check(bias.size(1) == weight.size(1), "bias output dimension must match weight")
         _check(bias.dtype == x.dtype, "bias dtype must match x")
     _check(weight.dtype == x.dtype, "weight dtype must match x")
-    device = nat.require_cuda(x, weight, bias, name="grouped_linear_forward")
-    m, g, i = x.shape
-    o = weight.shape[1]
+    nat.require_cuda(x, weight, bias, name="grouped_linear_forward")
+    g = x.shape[1]
+    o, i = weight.shape[1], weight.shape[2]
     weight = _contig(weight)
     bias = None if bias is None else _contig(bias)
-    out = torch.empty(m, g, o, dtype=x.dtype, device=device)
+    return grouped_linear_forward_lists(
+        x, _rows_ptrs(weight, g, o * i), None if bias is None else _rows_ptrs(bias, g, o), o, weight.dtype, activation
+    )
+
+
+def grouped_linear_forward_lists(x, weights, biases, out_features, param_dtype, activation: int = 0,
+                                 out: torch.Tensor | None = None):
+    """x [M,G,I] (any strides), per-group weight / bias pointers or tensors -> out [M,G,O]."""
+    device = x.device
+    m, g, i = x.shape
+    if out is None:
+        out = torch.empty(m, g, out_features, dtype=x.dtype, device=device)
     with torch.cuda.device(device):
         nat.call(
-            "pmb_grouped_linear_forward", x.data_ptr(), m, g, i, o, x.stride(0), x.stride(1), x.stride(2),
-            weight.data_ptr(), nat.ptr(bias), out.data_ptr(), activation, nat.dtype_code(x.dtype),
-            nat.dtype_code(weight.dtype), nat.stream_handle(device),
+            "pmb_grouped_linear_forward", x.data_ptr(), m, g, i, out_features, x.stride(0), x.stride(1),
+            x.stride(2), nat.ptr_array(weights), None if biases is None else nat.ptr_array(biases), out.data_ptr(),
+            activation, nat.dtype_code(x.dtype), nat.dtype_code(param_dtype), nat.stream_handle(device),
         )
     return out
 
@@ -450,23 +461,35 @@ def grouped_linear_backward(grad_out, x, out, weight, activation: int = 0, need_
                             has_bias: bool = True):
     """Backward of :func:`grouped_linear_forward` -> (grad_x|None, grad_weight, grad_bias|None)."""
     device = nat.require_cuda(grad_out, x, out, weight, name="grouped_linear_backward")
-    grad_out, x, weight = _contig(grad_out), _contig(x), _contig(weight)
-    out = None if out is None else _contig(out)
-    m, g, i = x.shape
-    o = weight.shape[1]
+    weight = _contig(weight)
+    g, o, i = weight.shape
     grad_x = torch.empty_like(x) if need_grad_x else None
     grad_weight = torch.empty_like(weight)
     grad_bias = torch.empty(g, o, dtype=weight.dtype, device=device) if has_bias else None
+    grouped_linear_backward_lists(
+        grad_out, x, out, _rows_ptrs(weight, g, o * i), o, weight.dtype, grad_x, _rows_ptrs(grad_weight, g, o * i),
+        None if grad_bias is None else _rows_ptrs(grad_bias, g, o), activation,
+    )
+    return grad_x, grad_weight, grad_bias
+
+
+def grouped_linear_backward_lists(grad_out, x, out, weights, out_features, param_dtype, grad_x, grad_weights,
+                                  grad_biases, activation: int = 0):
+    """Backward with per-group pointer lists; x/grad_out/out must be contiguous [M,G,*]."""
+    device = grad_out.device
+    grad_out, x = _contig(grad_out), _contig(x)
+    out = None if out is None else _contig(out)
+    m, g, i = x.shape
     lib = nat.library()
-    ws_bytes = int(lib.pmb_grouped_linear_backward_workspace_size(m, g, o))
+    ws_bytes = int(lib.pmb_grouped_linear_backward_workspace_size(m, g, out_features))
     ws = nat.workspace(ws_bytes, device)
     with torch.cuda.device(device):
         nat.call(
-            "pmb_grouped_linear_backward", grad_out.data_ptr(), x.data_ptr(), nat.ptr(out), m, g, i, o,
-            weight.data_ptr(), nat.ptr(grad_x), grad_weight.data_ptr(), nat.ptr(grad_bias), activation,
-            nat.dtype_code(x.dtype), nat.dtype_code(weight.dtype), ws.data_ptr(), ws_bytes, nat.stream_handle(device),
+            "pmb_grouped_linear_backward", grad_out.data_ptr(), x.data_ptr(), nat.ptr(out), m, g, i, out_features,
+            nat.ptr_array(weights), nat.ptr(grad_x), nat.ptr_array(grad_weights),
+            None if grad_biases is None else nat.ptr_array(grad_biases), activation, nat.dtype_code(x.dtype),
+            nat.dtype_code(param_dtype), ws.data_ptr(), ws_bytes, nat.stream_handle(device),
         )
-    return grad_x, grad_weight, grad_bias
 
 
 # ----------------------------------------------------------- attention gate
@@ -557,18 +580,29 @@ def _check_mask_forward(x, weights, bias, dim_inputs, dim_offsets):
         _check(weight.dtype == x.dtype, "weight dtype must match x")
 
 
-def mask_estimator_final_forward_into(x, weights, bias, dim_inputs, out, pre):
+def _flat_band_ptrs(flat: torch.Tensor, dim_inputs, factor: int = 2) -> list[int]:
+    """Per-band pointers into a flat [factor*total] vector."""
+    ptrs, off = [], 0
+    for w in dim_inputs:
+        ptrs.append(flat.data_ptr() + factor * off * flat.element_size())
+        off += int(w)
+    return ptrs
+
+
+def mask_estimator_final_forward_into(x, weights, biases, dim_inputs, out, pre, param_dtype):
+    """Per-band weights / biases (tensors or pointers) -> out [M,total], pre [M,2*total]."""
     device = x.device
     rows, nb, hidden = x.shape
     with torch.cuda.device(device):
         nat.call(
             "pmb_mask_estimator_final_forward", x.data_ptr(), rows, nb, hidden, nat.i64_array(dim_inputs),
-            nat.ptr_array(weights), bias.data_ptr(), out.data_ptr(), pre.data_ptr(), nat.dtype_code(x.dtype),
-            nat.dtype_code(bias.dtype), nat.stream_handle(device),
+            nat.ptr_array(weights), nat.ptr_array(biases), out.data_ptr(), pre.data_ptr(), nat.dtype_code(x.dtype),
+            nat.dtype_code(param_dtype), nat.stream_handle(device),
         )
 
 
-def mask_estimator_final_backward_into(grad_out, x, pre, weights, dim_inputs, grad_x, grad_bias, grad_weights):
+def mask_estimator_final_backward_into(grad_out, x, pre, weights, dim_inputs, grad_x, grad_biases, grad_weights,
+                                       param_dtype):
     device = grad_out.device
     rows, nb, hidden = x.shape
     warr = nat.i64_array(dim_inputs)
@@ -578,8 +612,8 @@ def mask_estimator_final_backward_into(grad_out, x, pre, weights, dim_inputs, gr
     with torch.cuda.device(device):
         nat.call(
             "pmb_mask_estimator_final_backward", grad_out.data_ptr(), x.data_ptr(), pre.data_ptr(), rows, nb,
-            hidden, warr, nat.ptr_array(weights), grad_x.data_ptr(), grad_bias.data_ptr(),
-            nat.ptr_array(grad_weights), nat.dtype_code(grad_out.dtype), nat.dtype_code(grad_bias.dtype), ws.data_ptr(),
+            hidden, warr, nat.ptr_array(weights), grad_x.data_ptr(), nat.ptr_array(grad_biases),
+            nat.ptr_array(grad_weights), nat.dtype_code(grad_out.dtype), nat.dtype_code(param_dtype), ws.data_ptr(),
             ws_bytes, nat.stream_handle(device),
         )
 
@@ -593,7 +627,7 @@ def mask_estimator_final_forward(x, weights, bias, dim_inputs, dim_offsets):
     total = sum(int(w) for w in dim_inputs)
     out = torch.empty(x.shape[0], total, dtype=x.dtype, device=x.device)
     pre = torch.empty(x.shape[0], 2 * total, dtype=x.dtype, device=x.device)
-    mask_estimator_final_forward_into(x, weights, bias, dim_inputs, out, pre)
+    mask_estimator_final_forward_into(x, weights, _flat_band_ptrs(bias, dim_inputs), dim_inputs, out, pre, bias.dtype)
     return out, pre, x
 
 
@@ -615,7 +649,8 @@ def mask_estimator_final_backward(grad_out, x, pre, weights, dim_inputs, dim_off
     grad_x = torch.empty_like(x)
     grad_bias = torch.empty(pre.shape[1], dtype=grad_out.dtype, device=grad_out.device)
     grad_weights = [torch.empty_like(w) for w in weights]
-    mask_estimator_final_backward_into(grad_out, x, pre, weights, dim_inputs, grad_x, grad_bias, grad_weights)
+    mask_estimator_final_backward_into(grad_out, x, pre, weights, dim_inputs, grad_x,
+                                       _flat_band_ptrs(grad_bias, dim_inputs), grad_weights, grad_bias.dtype)
     return [grad_x, grad_bias, *grad_weights]
 
 
@@ -723,7 +758,8 @@ def load_fused_band_split_extension() -> SimpleNamespace:
 
 __all__ = [
     "ops", "load_fused_band_split_extension", "rms_norm_backward_into", "band_split_forward_into",
-    "band_split_backward_into", "grouped_linear_backward", "mask_estimator_final_forward_into",
+    "band_split_backward_into", "grouped_linear_backward", "grouped_linear_forward_lists",
+    "grouped_linear_backward_lists", "mask_estimator_final_forward_into",
     "mask_estimator_final_backward_into", "band_gather", "band_gather_backward", "band_recombine",
     "band_recombine_backward",
 ] + [

@@ -1,0 +1,292 @@
+"""Autograd Functions of the fused training path (the product's hot path).
+
+Each Function calls the sm_100a C-ABI library through :mod:`pymsst_b200._native`;
+there is no CPU or torch fallback (CPU tensors raise
+:class:`~pymsst_b200._native.FusedKernelUnavailable`).  They play the role of
+the reference's autograd wrappers (src/pymsst/training/fused_roformer.py:
+888-1262) for this package's own model modules.
+
+Precision: activations are in the *compute dtype* (fp32, or the autocast
+dtype bf16 / fp16 under ``torch.autocast``); parameters stay fp32 masters and
+are read directly by the kernels (no per-step cast copies); parameter
+gradients are produced in fp32.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _native as nat
+from . import extension as ext
+
+
+def compute_dtype(t: torch.Tensor) -> torch.dtype:
+    if t.device.type == "cuda" and torch.is_autocast_enabled("cuda"):
+        return torch.get_autocast_dtype("cuda")
+    return t.dtype if t.is_floating_point() else torch.float32
+
+
+def _rows(x: torch.Tensor) -> int:
+    return x.numel() // x.shape[-1] if x.shape[-1] else 0
+
+
+# ------------------------------------------------------------------ RMSNorm
+class RMSNormFn(torch.autograd.Function):
+    """y = F.normalize(x) * sqrt(D) * gamma; saves x and the fp32 inverse norms."""
+
+    @staticmethod
+    def forward(ctx, x: torch.Tensor, gamma: torch.Tensor):
+        device = nat.require_cuda(x, gamma, name="RMSNorm")
+        x = x.contiguous()
+        dim = x.shape[-1]
+        rows = _rows(x)
+        out = torch.empty_like(x)
+        inv = torch.empty(rows, dtype=torch.float32, device=device)
+        nat.call(
+            "pmb_rms_norm_forward", x.data_ptr(), gamma.data_ptr(), out.data_ptr(), None, inv.data_ptr(), rows, dim,
+            nat.dtype_code(x.dtype), nat.dtype_code(gamma.dtype), nat.dtype_code(x.dtype), nat.stream_handle(device),
+        )
+        ctx.save_for_backward(x, inv, gamma)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad):
+        x, inv, gamma = ctx.saved_tensors
+        gx, gg = ext.rms_norm_backward_into(
+            grad.to(x.dtype).contiguous(), x, inv, gamma, saved_is_input=True,
+            grad_x_dtype=x.dtype if ctx.needs_input_grad[0] else None, grad_gamma_dtype=gamma.dtype,
+            name="RMSNorm.backward",
+        )
+        return gx, gg
+
+
+# ---------------------------------------------------------------- BandSplit
+class BandSplitFn(torch.autograd.Function):
+    """feats [rows, total] -> [rows, nb, O]; per band RMSNorm + Linear (ragged)."""
+
+    @staticmethod
+    def forward(ctx, x, widths, out_features, *params):
+        nb = len(widths)
+        gammas, weights, biases = params[:nb], params[nb : 2 * nb], params[2 * nb :]
+        nat.require_cuda(x, name="BandSplit")
+        x = x.contiguous()
+        rows, total = x.shape
+        out = torch.empty(rows, nb, out_features, dtype=x.dtype, device=x.device)
+        normed = torch.empty_like(x)
+        inv = torch.empty(rows, nb, dtype=torch.float32, device=x.device)
+        ext.band_split_forward_into(x, rows, (total, -1, 1), widths, gammas, weights, biases, out_features, out,
+                                    normed, inv, param_dtype=weights[0].dtype)
+        ctx.widths = widths
+        ctx.out_features = out_features
+        ctx.save_for_backward(normed, inv, *gammas, *weights)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad):
+        nb = len(ctx.widths)
+        normed, inv, *rest = ctx.saved_tensors
+        gammas, weights = rest[:nb], rest[nb:]
+        grad = grad.to(normed.dtype).contiguous()
+        grad_x = torch.empty_like(normed) if ctx.needs_input_grad[0] else None
+        g_gammas = [torch.empty_like(g) for g in gammas]
+        g_weights = [torch.empty_like(w) for w in weights]
+        g_biases = [torch.empty(ctx.out_features, dtype=weights[0].dtype, device=grad.device) for _ in weights]
+        ext.band_split_backward_into(grad, normed, inv, ctx.widths, gammas, weights, ctx.out_features, grad_x,
+                                     g_gammas, g_weights, g_biases, param_dtype=weights[0].dtype)
+        return (grad_x, None, None, *g_gammas, *g_weights, *g_biases)
+
+
+# ----------------------------------------------------------- MaskEstimator
+class MaskEstimatorFn(torch.autograd.Function):
+    """x [rows, nb, D] -> mask [rows, total]: per band (Linear+Tanh)^L, Linear, GLU.
+
+    params: for each hidden layer, nb weights then nb biases; then the nb
+    final weights and nb final biases.
+    """
+
+    @staticmethod
+    def forward(ctx, x, widths, hidden_layers, *params):
+        nb = len(widths)
+        nat.require_cuda(x, name="MaskEstimator")
+        x = x.contiguous()
+        rows = x.shape[0]
+        pdtype = params[0].dtype
+        acts = [x]
+        h = x
+        for layer in range(hidden_layers):
+            ws = params[2 * nb * layer : 2 * nb * layer + nb]
+            bs = params[2 * nb * layer + nb : 2 * nb * (layer + 1)]
+            h = ext.grouped_linear_forward_lists(h, ws, bs, ws[0].shape[0], pdtype, activation=1)
+            acts.append(h)
+        fw = params[2 * nb * hidden_layers : 2 * nb * hidden_layers + nb]
+        fb = params[2 * nb * hidden_layers + nb :]
+        total = sum(widths)
+        out = torch.empty(rows, total, dtype=x.dtype, device=x.device)
+        pre = torch.empty(rows, 2 * total, dtype=x.dtype, device=x.device)
+        ext.mask_estimator_final_forward_into(h, fw, fb, widths, out, pre, pdtype)
+        ctx.widths = widths
+        ctx.hidden_layers = hidden_layers
+        ctx.save_for_backward(pre, *acts, *params)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad):
+        nb = len(ctx.widths)
+        L = ctx.hidden_layers
+        pre, *rest = ctx.saved_tensors
+        acts, params = rest[: L + 1], rest[L + 1 :]
+        pdtype = params[0].dtype
+        grad = grad.to(pre.dtype).contiguous()
+        fw = params[2 * nb * L : 2 * nb * L + nb]
+        h = acts[-1]
+        grad_h = torch.empty_like(h)
+        g_fw = [torch.empty_like(w) for w in fw]
+        g_fb = [torch.empty(w.shape[0], dtype=pdtype, device=grad.device) for w in fw]
+        ext.mask_estimator_final_backward_into(grad, h, pre, fw, ctx.widths, grad_h, g_fb, g_fw, pdtype)
+        layer_grads = []
+        for layer in reversed(range(L)):
+            ws = params[2 * nb * layer : 2 * nb * layer + nb]
+            x_in, y = acts[layer], acts[layer + 1]
+            need_x = layer > 0 or ctx.needs_input_grad[0]
+            gx = torch.empty_like(x_in) if need_x else None
+            g_w = [torch.empty_like(w) for w in ws]
+            g_b = [torch.empty(w.shape[0], dtype=pdtype, device=grad.device) for w in ws]
+            ext.grouped_linear_backward_lists(grad_h, x_in, y, ws, ws[0].shape[0], pdtype, gx, g_w, g_b, activation=1)
+            layer_grads.append((g_w, g_b))
+            grad_h = gx
+        flat = []
+        for g_w, g_b in reversed(layer_grads):
+            flat.extend(g_w)
+            flat.extend(g_b)
+        flat.extend(g_fw)
+        flat.extend(g_fb)
+        return (grad_h if ctx.needs_input_grad[0] else None, None, None, *flat)
+
+
+# ------------------------------------------------------- attention pieces
+class QKVRotaryFn(torch.autograd.Function):
+    """xn [b, n, D] -> q, k, v [b, h, n, dh]: projection, split, rotary on q/k."""
+
+    @staticmethod
+    def forward(ctx, xn, weight, cos, sin, heads):
+        device = nat.require_cuda(xn, weight, name="QKVRotary")
+        b, n, d = xn.shape
+        dh = weight.shape[0] // (3 * heads)
+        w = weight.to(xn.dtype)
+        x2 = xn.reshape(b * n, d)
+        qkv = torch.matmul(x2, w.t())
+        q = torch.empty(b, heads, n, dh, dtype=xn.dtype, device=device)
+        k = torch.empty_like(q)
+        v = torch.empty_like(q)
+        rotate = int(cos is not None)
+        nat.call(
+            "pmb_qkv_rotary_split", qkv.data_ptr(), nat.ptr(cos), nat.ptr(sin), b, n, heads, dh, q.data_ptr(),
+            k.data_ptr(), v.data_ptr(), rotate, nat.dtype_code(xn.dtype), nat.stream_handle(device),
+        )
+        ctx.heads = heads
+        ctx.weight_dtype = weight.dtype
+        ctx.save_for_backward(x2, w, cos, sin)
+        return q, k, v
+
+    @staticmethod
+    def backward(ctx, gq, gk, gv):
+        x2, w, cos, sin = ctx.saved_tensors
+        heads = ctx.heads
+        device = x2.device
+        ref = next(g for g in (gq, gk, gv) if g is not None)
+        b, _, n, dh = ref.shape
+        gq, gk, gv = (torch.zeros_like(ref) if g is None else g for g in (gq, gk, gv))
+        gq, gk, gv = (g.to(x2.dtype).contiguous() for g in (gq, gk, gv))
+        gqkv = torch.empty(b * n, 3 * heads * dh, dtype=x2.dtype, device=device)
+        nat.call(
+            "pmb_qkv_rotary_merge", gq.data_ptr(), gk.data_ptr(), gv.data_ptr(), nat.ptr(cos), nat.ptr(sin), b, n,
+            heads, dh, gqkv.data_ptr(), int(cos is not None), nat.dtype_code(x2.dtype), nat.stream_handle(device),
+        )
+        gx = torch.matmul(gqkv, w).reshape(b, n, -1) if ctx.needs_input_grad[0] else None
+        gw = torch.matmul(gqkv.t(), x2).to(ctx.weight_dtype) if ctx.needs_input_grad[1] else None
+        return gx, gw, None, None, None
+
+
+class AttentionGateFn(torch.autograd.Function):
+    """attn [b, h, n, dh] (any strides, dh contiguous), xn [b*n, D] -> gated [b*n, h*dh]."""
+
+    @staticmethod
+    def forward(ctx, attn, xn, weight, bias):
+        device = nat.require_cuda(attn, xn, weight, bias, name="AttentionGate")
+        if attn.stride(-1) != 1:
+            attn = attn.contiguous()
+        b, h, n, dh = attn.shape
+        xn = xn.contiguous()
+        rows, dim = xn.shape
+        out = torch.empty(rows, h * dh, dtype=attn.dtype, device=device)
+        gate = torch.empty(rows, h, dtype=attn.dtype, device=device)
+        nat.call(
+            "pmb_attention_gate_forward", attn.data_ptr(), n, attn.stride(0), attn.stride(2), attn.stride(1),
+            xn.data_ptr(), weight.data_ptr(), bias.data_ptr(), rows, h, dh, dim, out.data_ptr(), gate.data_ptr(),
+            nat.dtype_code(attn.dtype), nat.dtype_code(weight.dtype), nat.stream_handle(device),
+        )
+        ctx.save_for_backward(attn, xn, weight, gate)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad):
+        attn, xn, weight, gate = ctx.saved_tensors
+        device = attn.device
+        b, h, n, dh = attn.shape
+        rows, dim = xn.shape
+        grad = grad.to(attn.dtype).contiguous()
+        grad_attn = torch.empty_strided(attn.shape, attn.stride(), dtype=attn.dtype, device=device)
+        grad_x = torch.empty_like(xn)
+        gw = torch.empty_like(weight)
+        gb = torch.empty(h, dtype=weight.dtype, device=device)
+        lib = nat.library()
+        ws_bytes = int(lib.pmb_attention_gate_backward_workspace_size(rows, h, dim))
+        ws = nat.workspace(ws_bytes, device)
+        nat.call(
+            "pmb_attention_gate_backward", grad.data_ptr(), attn.data_ptr(), n, attn.stride(0), attn.stride(2),
+            attn.stride(1), xn.data_ptr(), weight.data_ptr(), gate.data_ptr(), rows, h, dh, dim,
+            grad_attn.data_ptr(), grad_x.data_ptr(), gw.data_ptr(), gb.data_ptr(), nat.dtype_code(attn.dtype),
+            nat.dtype_code(weight.dtype), ws.data_ptr(), ws_bytes, nat.stream_handle(device),
+        )
+        return grad_attn, grad_x, gw, gb
+
+
+# -------------------------------------------------------- band index ops
+class BandGatherFn(torch.autograd.Function):
+    """stft fp32 [B,S,F,T,2] -> band features [B,T,J*2] in out_dtype."""
+
+    @staticmethod
+    def forward(ctx, stft, tables, out_dtype):
+        ctx.tables = tables
+        ctx.shape = stft.shape
+        return ext.band_gather(stft, tables, out_dtype)
+
+    @staticmethod
+    def backward(ctx, grad):
+        _, s, f, _, _ = ctx.shape
+        return ext.band_gather_backward(grad, ctx.tables, s, f), None, None
+
+
+class BandRecombineFn(torch.autograd.Function):
+    """masks [B,N,T,J*2] x stft [B,S,F,T,2] -> masked STFT fp32 [B,N,S,F,T,2] (overlaps averaged)."""
+
+    @staticmethod
+    def forward(ctx, mask, stft, tables):
+        ctx.tables = tables
+        ctx.mask_dtype = mask.dtype
+        ctx.save_for_backward(stft)
+        _, s, f, _, _ = stft.shape
+        return ext.band_recombine(mask, stft, tables, s, f, multiply=True)
+
+    @staticmethod
+    def backward(ctx, grad):
+        (stft,) = ctx.saved_tensors
+        gm = ext.band_recombine_backward(grad, stft, ctx.tables, ctx.mask_dtype, multiply=True)
+        return gm, None, None
+
+
+def rotary_tables(freqs: torch.Tensor, n: int, device: torch.device) -> tuple[torch.Tensor, torch.Tensor]:
+    """fp32 cos/sin [n, dh/2] for positions 0..n-1 (exact fp32 positions)."""
+    pos = torch.arange(n, device=device, dtype=torch.float32)
+    ang = pos[:, None] * freqs.detach().to(device=device, dtype=torch.float32)[None, :]
+    return ang.cos().contiguous(), ang.sin().contiguous()
+
