@@ -67,6 +67,26 @@ PMB_API const char* pmb_last_error(void);
 /* Number of kernels this library has launched in the process so far. */
 PMB_API uint64_t pmb_launch_count(void);
 
+/*
+ * Non-zero if a tensor-core kernel gave up a bounded wait (a pipeline stall
+ * that would otherwise hang the GPU); the value encodes the wait site (low
+ * 16 bits) and block.  reset != 0 clears it.  Synchronises the device.
+ */
+PMB_API unsigned int pmb_umma_timeout(int reset);
+
+/* ------------------------------------------------------------------------
+ * Dense GEMM on the tcgen05 tensor cores (bf16 / fp16 operands, fp32
+ * accumulate):  C[m, n] = act(sum_k A(m, k) B(n, k) + bias[n])
+ * A(m, k) = a[m*lda + k] (a_mn_major = 0) or a[k*lda + m] (a_mn_major = 1);
+ * B(n, k) likewise.  C is written in c_dtype with row stride ldc; bias
+ * (nullable) in bias_dtype.  lda/ldb must give 16-byte aligned rows.
+ * Replaces the dense use of the reference's cuBLAS grouped GEMM
+ * (.cu:2038-2281).
+ * ---------------------------------------------------------------------- */
+PMB_API int pmb_gemm_tc(const void* a, int64_t lda, int a_mn_major, const void* b, int64_t ldb, int b_mn_major,
+                        void* c, int64_t ldc, int c_dtype, const void* bias, int bias_dtype, int activation,
+                        int64_t m, int64_t n, int64_t k, int dtype, void* stream);
+
 /* ------------------------------------------------------------------------
  * RMSNorm over the last dimension (transformer RMSNorm, F.normalize form):
  *   inv_norm[r] = 1 / max(||x[r,:]||_2, 1e-12)
@@ -299,6 +319,37 @@ PMB_API int pmb_qkv_rotary_split(const void* qkv, const float* cos, const float*
 PMB_API int pmb_qkv_rotary_merge(const void* grad_q, const void* grad_k, const void* grad_v, const float* cos,
                                  const float* sin, int64_t batch, int64_t seq_len, int64_t heads,
                                  int64_t dim_head, void* grad_qkv, int rotate_qk, int dtype, void* stream);
+
+/* ------------------------------------------------------------------------
+ * MaskEstimator MLP on the tcgen05 tensor cores (training path, bf16/fp16
+ * activations, fp32 or 16-bit parameters): per band b,
+ *   h_1 = tanh(x_b W_{1,b}^T + b_{1,b}), ..., h_L (hidden_layers of them),
+ *   pre_b = h_L W_{f,b}^T + b_{f,b}  (2*w_b outputs),  out_b = GLU(pre_b).
+ * x [rows, nb, dim]; weights / biases: host arrays of (hidden_layers + 1)*nb
+ * per-band device pointers, layer-major (W [out, in], bias [out]).
+ * Caller-owned buffers, sized by pmb_mask_estimator_tc_sizes (sizes[0..4] =
+ * packed-weight bytes, saved-activation bytes, pre bytes, backward workspace
+ * bytes, packed width P): packed_weights (kept for the backward), acts
+ * [hidden_layers, rows, nb, hidden], pre [rows, P] (GLU pre-activations in a
+ * chunk-interleaved packed layout), out [rows, sum(widths)].
+ * The backward writes per-band parameter gradients (fp32 when param_dtype is
+ * fp32) and, if grad_x is not NULL, grad_x [rows, nb, dim].
+ * Replaces the per-group grouped_linear + mask_estimator_final kernels
+ * (fused_roformer.py:527-583; .cu:1006-1074, :2284-2851) with one launch
+ * per layer for all bands.
+ * ---------------------------------------------------------------------- */
+PMB_API int pmb_mask_estimator_tc_sizes(int64_t rows, int num_bands, int64_t dim, int64_t hidden, int hidden_layers,
+                                        const int64_t* widths, int64_t* sizes);
+PMB_API int pmb_mask_estimator_tc_forward(const void* x, int64_t rows, int num_bands, int64_t dim, int64_t hidden,
+                                          int hidden_layers, const int64_t* widths, const void* const* weights,
+                                          const void* const* biases, void* packed_weights, void* acts, void* pre,
+                                          void* out, int dtype, int param_dtype, void* stream);
+PMB_API int pmb_mask_estimator_tc_backward(const void* grad_out, const void* x, const void* acts, const void* pre,
+                                           const void* packed_weights, int64_t rows, int num_bands, int64_t dim,
+                                           int64_t hidden, int hidden_layers, const int64_t* widths,
+                                           void* const* grad_weights, void* const* grad_biases, void* grad_x,
+                                           int dtype, int param_dtype, void* workspace, int64_t workspace_bytes,
+                                           void* stream);
 
 #ifdef __cplusplus
 }

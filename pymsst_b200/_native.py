@@ -29,6 +29,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "pmb_version": (ctypes.c_char_p, []),
     "pmb_last_error": (ctypes.c_char_p, []),
     "pmb_launch_count": (ctypes.c_uint64, []),
+    "pmb_umma_timeout": (ctypes.c_uint, [_i]),
+    "pmb_gemm_tc": (_i, [_p, _i64, _i, _p, _i64, _i, _p, _i64, _i, _p, _i, _i, _i64, _i64, _i64, _i, _p]),
     "pmb_rms_norm_forward": (_i, [_p, _p, _p, _p, _p, _i64, _i64, _i, _i, _i, _p]),
     "pmb_rms_norm_backward_workspace_size": (_i64, [_i64, _i64]),
     "pmb_rms_norm_backward": (_i, [_p, _p, _i, _p, _p, _p, _p, _i64, _i64, _i, _i, _i, _i, _p, _i64, _p]),
@@ -58,6 +60,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "pmb_band_gather_backward": (_i, [_p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p, _i, _p]),
     "pmb_band_recombine_forward": (_i, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i, _p, _i, _p]),
     "pmb_band_recombine_backward": (_i, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i, _p, _i, _p]),
+    "pmb_mask_estimator_tc_sizes": (_i, [_i64, _i, _i64, _i64, _i, _pi64, _pi64]),
+    "pmb_mask_estimator_tc_forward": (
+        _i, [_p, _i64, _i, _i64, _i64, _i, _pi64, _pp, _pp, _p, _p, _p, _p, _i, _i, _p]),
+    "pmb_mask_estimator_tc_backward": (
+        _i, [_p, _p, _p, _p, _p, _i64, _i, _i64, _i64, _i, _pi64, _pp, _pp, _p, _i, _i, _p, _i64, _p]),
     "pmb_qkv_rotary_split": (_i, [_p, _p, _p, _i64, _i64, _i64, _i64, _p, _p, _p, _i, _i, _p]),
     "pmb_qkv_rotary_merge": (_i, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _i, _i, _p]),
 }
@@ -117,9 +124,48 @@ def ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
 
+# Entry points whose calls are bracketed by CUDA events (see ``time_entries``).
+_TIMED: dict[str, list] = {}
+
+
 def call(name: str, *args) -> None:
     """Call a status-returning entry point and raise on failure."""
+    rec = _TIMED.get(name) if _TIMED else None
+    if rec is None:
+        check(getattr(library(), name)(*args), name)
+        return
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record()
     check(getattr(library(), name)(*args), name)
+    end.record()
+    rec.append((start, end, args))
+
+
+class time_entries:
+    """Context manager: record CUDA events around every call of the given entry
+    points (on the current stream, where the library launches).  ``result()``
+    returns {name: (calls, total_ms, [args of each call])} after a synchronize."""
+
+    def __init__(self, names):
+        self.names = list(names)
+
+    def __enter__(self):
+        for n in self.names:
+            _TIMED[n] = []
+        return self
+
+    def __exit__(self, *exc):
+        self.records = {n: _TIMED.pop(n) for n in self.names}
+        return False
+
+    def result(self) -> dict:
+        torch.cuda.synchronize()
+        out = {}
+        for n, recs in self.records.items():
+            total = sum(s.elapsed_time(e) for s, e, _ in recs)
+            out[n] = (len(recs), total, [a for _, _, a in recs])
+        return out
 
 
 def i64_array(values) -> ctypes.Array:

@@ -53,9 +53,19 @@ int make_band_table(BandTable& t, int count, const int64_t* widths, const void* 
   return PMB_OK;
 }
 
+// Per-translation-unit tcgen05 wait-timeout flags (umma.cuh).
+unsigned int timeout_flag_gemm(int reset);
+unsigned int timeout_flag_mask(int reset);
+
 }  // namespace pmb
 
 extern "C" {
+
+unsigned int pmb_umma_timeout(int reset) {
+  const unsigned int a = pmb::timeout_flag_gemm(reset);
+  const unsigned int b = pmb::timeout_flag_mask(reset);
+  return a ? a : b;
+}
 
 const char* pmb_version(void) { return "0.1.0"; }
 

@@ -1,0 +1,26 @@
+// Host-side TMA tensor-map encoding.  The driver entry point is resolved at
+// run time through the CUDA runtime, so the library has no link-time
+// dependency on libcuda and loads on machines without a GPU.
+#pragma once
+
+#include <cuda.h>
+
+#include "common.cuh"
+
+namespace pmb {
+namespace tma {
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn();
+
+// 3-D map (inner, mid, outer) over a 16-bit tensor with 128-byte swizzle.
+// Strides are in bytes for the mid and outer dimensions.  Returns a status.
+int make_map_3d(CUtensorMap& map, const void* base, int dtype, uint64_t inner, uint64_t mid, uint64_t outer,
+                uint64_t stride_mid_bytes, uint64_t stride_outer_bytes, uint32_t box_inner, uint32_t box_mid,
+                uint32_t box_outer, const char* name);
+
+}  // namespace tma
+}  // namespace pmb

@@ -162,6 +162,65 @@ class MaskEstimatorFn(torch.autograd.Function):
         return (grad_h if ctx.needs_input_grad[0] else None, None, None, *flat)
 
 
+class MaskEstimatorTCFn(torch.autograd.Function):
+    """Tensor-core (tcgen05) MaskEstimator for 16-bit activations; same contract as MaskEstimatorFn."""
+
+    @staticmethod
+    def forward(ctx, x, widths, hidden_layers, hidden, *params):
+        import ctypes
+
+        nb = len(widths)
+        device = nat.require_cuda(x, name="MaskEstimatorTC")
+        x = x.contiguous()
+        rows, _, dim = x.shape
+        warr = nat.i64_array(widths)
+        sizes = (ctypes.c_int64 * 5)()
+        nat.call("pmb_mask_estimator_tc_sizes", rows, nb, dim, hidden, hidden_layers, warr, sizes)
+        packed = torch.empty(max(sizes[0], 1), dtype=torch.uint8, device=device)
+        acts = torch.empty(max(sizes[1], 1), dtype=torch.uint8, device=device)
+        pre = torch.empty(max(sizes[2], 1), dtype=torch.uint8, device=device)
+        total = sum(widths)
+        out = torch.empty(rows, total, dtype=x.dtype, device=device)
+        layers = hidden_layers + 1
+        weights = [params[2 * nb * l + b] for l in range(layers) for b in range(nb)]
+        biases = [params[2 * nb * l + nb + b] for l in range(layers) for b in range(nb)]
+        nat.call(
+            "pmb_mask_estimator_tc_forward", x.data_ptr(), rows, nb, dim, hidden, hidden_layers, warr,
+            nat.ptr_array(weights), nat.ptr_array(biases), packed.data_ptr(), acts.data_ptr(), pre.data_ptr(),
+            out.data_ptr(), nat.dtype_code(x.dtype), nat.dtype_code(params[0].dtype), nat.stream_handle(device),
+        )
+        ctx.meta = (widths, hidden_layers, hidden, int(sizes[3]))
+        ctx.save_for_backward(x, packed, acts, pre, *params)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad):
+        widths, hidden_layers, hidden, ws_bytes = ctx.meta
+        x, packed, acts, pre, *params = ctx.saved_tensors
+        nb = len(widths)
+        rows, _, dim = x.shape
+        device = x.device
+        grad = grad.to(x.dtype).contiguous()
+        grads = [torch.empty_like(p) for p in params]
+        layers = hidden_layers + 1
+        gw = [grads[2 * nb * l + b] for l in range(layers) for b in range(nb)]
+        gb = [grads[2 * nb * l + nb + b] for l in range(layers) for b in range(nb)]
+        grad_x = torch.empty_like(x) if ctx.needs_input_grad[0] else None
+        ws = nat.workspace(ws_bytes, device)
+        nat.call(
+            "pmb_mask_estimator_tc_backward", grad.data_ptr(), x.data_ptr(), acts.data_ptr(), pre.data_ptr(),
+            packed.data_ptr(), rows, nb, dim, hidden, hidden_layers, nat.i64_array(widths), nat.ptr_array(gw),
+            nat.ptr_array(gb), nat.ptr(grad_x), nat.dtype_code(x.dtype), nat.dtype_code(params[0].dtype),
+            ws.data_ptr(), ws_bytes, nat.stream_handle(device),
+        )
+        return (grad_x, None, None, None, *grads)
+
+
+def tensor_core_ok(x: torch.Tensor, *dims: int) -> bool:
+    """16-bit activations and 64-aligned feature widths take the tcgen05 path."""
+    return x.dtype in (torch.bfloat16, torch.float16) and all(d % 64 == 0 for d in dims)
+
+
 # ------------------------------------------------------- attention pieces
 class QKVRotaryFn(torch.autograd.Function):
     """xn [b, n, D] -> q, k, v [b, h, n, dh]: projection, split, rotary on q/k."""

@@ -41,10 +41,12 @@ from .fused import (
     BandRecombineFn,
     BandSplitFn,
     MaskEstimatorFn,
+    MaskEstimatorTCFn,
     QKVRotaryFn,
     RMSNormFn,
     compute_dtype,
     rotary_tables,
+    tensor_core_ok,
 )
 
 DEFAULT_FREQS_PER_BANDS = band_tables.DEFAULT_FREQS_PER_BANDS
@@ -183,7 +185,9 @@ class MaskEstimator(nn.Module):
         super().__init__()
         self.dim_inputs = tuple(int(d) for d in dim_inputs)
         self.hidden_layers = int(hidden_layers)
+        self.dim = dim
         hidden = dim * mlp_expansion_factor
+        self.hidden = hidden
         self.to_freqs = nn.ModuleList(
             [nn.Sequential(MLP(dim, d * 2, hidden, self.hidden_layers), nn.GLU(dim=-1)) for d in self.dim_inputs]
         )
@@ -198,8 +202,12 @@ class MaskEstimator(nn.Module):
 
     def forward(self, x):  # [..., nb, dim] -> [..., total]
         lead = x.shape[:-2]
-        out = MaskEstimatorFn.apply(x.reshape(-1, *x.shape[-2:]), self.dim_inputs, self.hidden_layers,
-                                    *self.ordered_parameters())
+        x2 = x.reshape(-1, *x.shape[-2:])
+        if tensor_core_ok(x2, self.dim, self.hidden):
+            out = MaskEstimatorTCFn.apply(x2, self.dim_inputs, self.hidden_layers, self.hidden,
+                                          *self.ordered_parameters())
+        else:
+            out = MaskEstimatorFn.apply(x2, self.dim_inputs, self.hidden_layers, *self.ordered_parameters())
         return out.reshape(*lead, out.shape[-1])
 
 

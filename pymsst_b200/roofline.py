@@ -1,0 +1,117 @@
+"""Algorithmic work models of the C-ABI entry points, for roofline reporting.
+
+For one call, ``work(name, args)`` returns the algorithmic HBM bytes (every
+operand read once, every result written once) and floating-point operations
+of the op, computed from the call's own arguments.  ``roofline`` turns the
+measured average duration of those calls into the achieved rate against the
+binding roof: HBM bandwidth or the dense bf16 tensor peak, whichever bounds
+the op at its arithmetic intensity.
+"""
+from __future__ import annotations
+
+import json
+from pathlib import Path
+
+ES = {0: 4, 1: 2, 2: 2}
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def load_peaks(path: str | Path | None = None) -> dict:
+    candidates = [Path(path)] if path else []
+    candidates.append(Path(__file__).resolve().parents[1] / "MEASURED_PEAKS.json")
+    for c in candidates:
+        if c.is_file():
+            data = json.loads(c.read_text())
+            return {"hbm_gbs": float(data["hbm_gbs"]), "bf16_tflops": float(data["bf16_tflops"]),
+                    "bf16_tflops_sustained": float(data.get("bf16_tflops_sustained", data["bf16_tflops"])),
+                    "source": "measured"}
+    return dict(FALLBACK_PEAKS)
+
+
+def _widths(ptr, n):
+    return [int(ptr[i]) for i in range(n)]
+
+
+def work(name: str, a: tuple) -> tuple[float, float]:
+    """(bytes, flops) of one call of entry point ``name`` with ctypes args ``a``."""
+    if name == "pmb_rms_norm_forward":
+        rows, dim, xd, gd, od = a[5], a[6], a[7], a[8], a[9]
+        outs = 1 + (a[3] is not None)
+        return rows * dim * (ES[xd] + outs * ES[od]) + 4 * rows + dim * ES[gd], 4.0 * rows * dim
+    if name == "pmb_rms_norm_backward":
+        rows, dim, gd, gmd, gxd = a[7], a[8], a[9], a[10], a[11]
+        return rows * dim * (2 * ES[gd] + (ES[gxd] if a[5] is not None else 0)) + 4 * rows + 2 * dim * ES[gmd], \
+            8.0 * rows * dim
+    if name in ("pmb_qkv_rotary_split", "pmb_qkv_rotary_merge"):
+        b, n, h, dh = (a[3], a[4], a[5], a[6]) if name.endswith("split") else (a[5], a[6], a[7], a[8])
+        dt = a[11]
+        return 2.0 * b * n * 3 * h * dh * ES[dt] + 2 * n * dh // 2 * 4, 6.0 * b * n * 2 * h * dh
+    if name == "pmb_attention_gate_forward":
+        rows, h, dh, dim, dt, pt = a[8], a[9], a[10], a[11], a[14], a[15]
+        return rows * (2 * h * dh + dim + h) * ES[dt] + h * (dim + 1) * ES[pt], 2.0 * rows * h * (dim + dh)
+    if name == "pmb_attention_gate_backward":
+        rows, h, dh, dim, dt, pt = a[9], a[10], a[11], a[12], a[17], a[18]
+        return rows * (3 * h * dh + 2 * dim + h) * ES[dt] + 8 * rows * h + 2 * h * (dim + 1) * ES[pt], \
+            4.0 * rows * h * (dim + dh)
+    if name == "pmb_band_gather_forward":
+        b, s, f, t, j, xd = a[2], a[3], a[4], a[5], a[6], a[8]
+        return b * t * j * 2 * (4 + ES[xd]) + 4 * j, 0.0
+    if name == "pmb_band_recombine_forward":
+        b, n, s, f, t, j, mult, md = a[4], a[5], a[6], a[7], a[8], a[9], a[10], a[12]
+        return b * n * t * j * 2 * ES[md] + (b * s * f * t * 8 if mult else 0) + b * n * s * f * t * 8, \
+            8.0 * b * n * s * f * t
+    if name == "pmb_band_recombine_backward":
+        b, n, s, f, t, j, mult, md = a[4], a[5], a[6], a[7], a[8], a[9], a[10], a[12]
+        return b * n * s * f * t * 8 + (b * s * f * t * 8 if mult else 0) + b * n * t * j * 2 * ES[md], \
+            8.0 * b * n * t * j
+    if name == "pmb_band_split_forward":
+        rows, nb, o, dt, pt = a[1], a[5], a[10], a[14], a[15]
+        total = sum(_widths(a[6], nb))
+        normed = a[12] is not None
+        byt = rows * total * ES[dt] * (1 + normed) + rows * nb * (o * ES[dt] + 4) + (total * (o + 1) + nb * o) * ES[pt]
+        return byt, 2.0 * rows * total * o
+    if name == "pmb_band_split_backward":
+        rows, nb, o, dt, pt = a[3], a[4], a[8], a[13], a[14]
+        total = sum(_widths(a[5], nb))
+        gx = a[9] is not None
+        byt = rows * nb * o * ES[dt] + rows * total * ES[dt] * (1 + gx) + 4 * rows * nb + 2 * (total * (o + 1) + nb * o) * ES[pt]
+        return byt, 2.0 * rows * total * o * (2 if gx else 1)
+    if name == "pmb_grouped_linear_forward":
+        rows, g, i, o, dt, pt = a[1], a[2], a[3], a[4], a[12], a[13]
+        return rows * g * (i + o) * ES[dt] + g * o * (i + 1) * ES[pt], 2.0 * rows * g * i * o
+    if name == "pmb_grouped_linear_backward":
+        rows, g, i, o, dt, pt = a[3], a[4], a[5], a[6], a[13], a[14]
+        gx = a[8] is not None
+        return rows * g * (2 * o + i * (1 + gx)) * ES[dt] + 2 * g * o * (i + 1) * ES[pt], \
+            2.0 * rows * g * i * o * (2 if gx else 1)
+    if name == "pmb_mask_estimator_final_forward":
+        rows, nb, h, dt, pt = a[1], a[2], a[3], a[9], a[10]
+        total = sum(_widths(a[4], nb))
+        return rows * (nb * h + 3 * total) * ES[dt] + 2 * total * (h + 1) * ES[pt], 4.0 * rows * h * total
+    if name == "pmb_mask_estimator_final_backward":
+        rows, nb, h, dt, pt = a[3], a[4], a[5], a[11], a[12]
+        total = sum(_widths(a[6], nb))
+        return rows * (2 * nb * h + 3 * total) * ES[dt] + 2 * 2 * total * (h + 1) * ES[pt], 8.0 * rows * h * total
+    return 0.0, 0.0
+
+
+def roofline(name: str, calls: int, total_ms: float, args_list: list, peaks: dict, traffic=None) -> dict:
+    """Achieved rate of the timed calls against the roof that binds this op."""
+    byt = sum(work(name, a)[0] for a in args_list)
+    flops = sum(work(name, a)[1] for a in args_list)
+    secs = total_ms / 1e3
+    t_hbm = byt / (peaks["hbm_gbs"] * 1e9)
+    t_tc = flops / (peaks["bf16_tflops"] * 1e12)
+    per_launch_ms = total_ms / max(calls, 1)
+    if t_tc > t_hbm:
+        achieved = flops / secs / 1e12
+        return {"bound": "tensor", "achieved": round(achieved, 2), "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                "frac": round(achieved / peaks["bf16_tflops"], 4), "traffic": traffic, "kernel": name,
+                "calls": calls, "ms_per_call": round(per_launch_ms, 4), "peak_source": peaks["source"],
+                "algorithmic_flops_per_call": flops / max(calls, 1)}
+    achieved = byt / secs / 1e9
+    return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+            "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic, "kernel": name, "calls": calls,
+            "ms_per_call": round(per_launch_ms, 4), "peak_source": peaks["source"],
+            "algorithmic_bytes_per_call": byt / max(calls, 1)}
+

@@ -1,0 +1,146 @@
+"""Training step, benchmark configurations and the seeded loss-curve runner.
+
+``Trainer.step`` is one training step of the reference's manual loop
+(src/pymsst/validation/direct_compare.py:358-386): forward with the loss under
+autocast (bf16 / fp16 or off), backward, optional gradient clipping, Adam
+step.  Data parallelism is torch DDP over NCCL (the reference trains with
+Lightning ``strategy="ddp"``, src/pymsst/cli.py:357-372): one process per
+GPU, gradients all-reduced in buckets that overlap the backward.
+``run_loss_curve`` is the ``compare-direct`` analogue: a seeded run that
+records the loss of every step.
+"""
+from __future__ import annotations
+
+import os
+from dataclasses import dataclass, field
+
+import torch
+import torch.distributed as dist
+
+from . import config as cfg
+from . import synthetic
+
+BSR_BASE = dict(dim=192, depth=6, stereo=True, num_stems=1, time_transformer_depth=1, freq_transformer_depth=1,
+                dim_head=64, heads=8, mask_estimator_depth=2, mlp_expansion_factor=4)
+
+
+@dataclass(frozen=True)
+class BenchConfig:
+    """A benchmark workload: model, per-GPU batch, chunk length and precision."""
+
+    name: str
+    model_type: str
+    model: dict
+    batch: int
+    chunk: int
+    amp: torch.dtype | None
+    stems: int = 1
+    lr: float = 1e-4
+    notes: str = ""
+    extra: dict = field(default_factory=dict)
+
+    @property
+    def audio_seconds_per_step(self) -> float:
+        return self.batch * self.chunk / synthetic.SAMPLE_RATE
+
+    @property
+    def frames(self) -> int:
+        return self.chunk // self.model.get("stft_hop_length", 512) + 1
+
+
+CONFIGS = {
+    "config0": BenchConfig("config0", "bs_roformer", BSR_BASE, batch=2, chunk=32768, amp=None,
+                           notes="BS-RoFormer fp32, batch 2 x 32768"),
+    "config1": BenchConfig("config1", "mel_band_roformer",
+                           dict(BSR_BASE, num_bands=60, sample_rate=44100), batch=2, chunk=32768,
+                           amp=torch.bfloat16, notes="Mel-band RoFormer, 60 bands, batch 2 x 32768"),
+    "config3": BenchConfig("config3", "bs_roformer", BSR_BASE, batch=4, chunk=131584, amp=torch.bfloat16,
+                           notes="BS-RoFormer bf16 AMP, chunk 131584 (258 frames), batch 4 per GPU"),
+    "config4": BenchConfig("config4", "bs_roformer", dict(BSR_BASE, dim=384, depth=12, num_stems=4), batch=2,
+                           chunk=352800, amp=torch.bfloat16, stems=4,
+                           notes="BS-RoFormer dim 384 depth 12, 4 stems, chunk 352800, batch 2 per GPU"),
+}
+
+
+def build_model(bench: BenchConfig, seed: int = 0) -> torch.nn.Module:
+    torch.manual_seed(seed)
+    return cfg.build_model(bench.model_type, **bench.model)
+
+
+class Trainer:
+    """Owns the model (optionally DDP-wrapped) and its Adam optimizer."""
+
+    def __init__(self, model: torch.nn.Module, *, lr: float = 1e-4, amp_dtype: torch.dtype | None = None,
+                 grad_clip: float = 0.0, distributed: bool = False, device: torch.device | None = None,
+                 fused_adam: bool = True, bucket_cap_mb: float = 64.0):
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        self.model = model.to(self.device)
+        self.amp_dtype = amp_dtype
+        self.grad_clip = float(grad_clip)
+        self.module = self.model
+        if distributed:
+            from torch.nn.parallel import DistributedDataParallel
+
+            self.module = DistributedDataParallel(
+                self.model, device_ids=[self.device.index], bucket_cap_mb=bucket_cap_mb, gradient_as_bucket_view=True,
+                broadcast_buffers=False,
+            )
+        params = [p for p in self.model.parameters() if p.requires_grad]
+        self.optimizer = torch.optim.Adam(params, lr=lr, fused=fused_adam)
+
+    def step(self, mixture: torch.Tensor, target: torch.Tensor) -> torch.Tensor:
+        """One training step on device tensors; returns the detached loss (device)."""
+        self.optimizer.zero_grad(set_to_none=True)
+        with torch.autocast("cuda", dtype=self.amp_dtype or torch.bfloat16, enabled=self.amp_dtype is not None):
+            loss = self.module(mixture, target)
+        loss.backward()
+        if self.grad_clip:
+            torch.nn.utils.clip_grad_norm_(self.model.parameters(), self.grad_clip)
+        self.optimizer.step()
+        return loss.detach()
+
+    def step_host(self, mixture: torch.Tensor, target: torch.Tensor, loss_out: torch.Tensor | None = None):
+        """Step from host tensors (pinned for async copies); the loss is copied back to ``loss_out``."""
+        mix = mixture.to(self.device, non_blocking=True)
+        tgt = target.to(self.device, non_blocking=True)
+        loss = self.step(mix, tgt)
+        if loss_out is None:
+            return float(loss)
+        loss_out.copy_(loss, non_blocking=True)
+        return loss_out
+
+
+def run_loss_curve(model: torch.nn.Module, batches, *, lr: float = 1e-4, amp_dtype=None,
+                   device: torch.device | None = None, grad_clip: float = 0.0) -> list[float]:
+    """Seeded training run; returns the loss of every step (the compare-direct curve)."""
+    trainer = Trainer(model, lr=lr, amp_dtype=amp_dtype, device=device, grad_clip=grad_clip)
+    losses = []
+    for mix, tgt in batches:
+        losses.append(float(trainer.step(mix.to(trainer.device), tgt.to(trainer.device))))
+    return losses
+
+
+def compare_loss_curves(a: list[float], b: list[float]) -> dict:
+    """Mean / max absolute difference over the overlapping steps (comparison.py:223-241)."""
+    n = min(len(a), len(b))
+    if n == 0:
+        raise ValueError("no overlapping loss points to compare")
+    diffs = [abs(x - y) for x, y in zip(a[:n], b[:n])]
+    return {"compared_points": n, "mean_abs_diff": sum(diffs) / n, "max_abs_diff": max(diffs)}
+
+
+def init_distributed(timeout_s: float = 120.0) -> tuple[int, int, int]:
+    """(rank, world, local_rank) from torchrun's environment; NCCL on CUDA, gloo otherwise."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and not dist.is_initialized():
+        import datetime
+
+        backend = "nccl" if torch.cuda.is_available() else "gloo"
+        if torch.cuda.is_available():
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=timeout_s))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(local)
+    return rank, world, local

@@ -1,0 +1,48 @@
+"""tcgen05 GEMM engine against a float64 reference of the same 16-bit inputs.
+
+Tolerance: fp32 accumulation of bf16/fp16 products; outputs compared with
+rtol 2e-3 and an absolute floor of 2e-3 x sqrt(K) x the operand scale.
+"""
+from __future__ import annotations
+
+import pytest
+import torch
+
+from pymsst_b200 import _native as nat
+
+pytestmark = pytest.mark.gpu
+
+
+def _gemm(a, b, m, n, k, a_mn, b_mn, out_dtype, bias=None, act=0):
+    c = torch.empty(m, n, dtype=out_dtype, device=a.device)
+    nat.call("pmb_gemm_tc", a.data_ptr(), a.stride(0), int(a_mn), b.data_ptr(), b.stride(0), int(b_mn), c.data_ptr(),
+             c.stride(0), nat.dtype_code(out_dtype), nat.ptr(bias), nat.dtype_code(bias.dtype) if bias is not None else 0,
+             act, m, n, k, nat.dtype_code(a.dtype), nat.stream_handle(a.device))
+    return c
+
+
+@pytest.mark.parametrize("m,n,k", [(128, 128, 64), (1000, 192, 768), (130, 70, 100), (4096, 1536, 192), (64, 8, 16)])
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, False), (True, True)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_gemm_tc_matches_reference(cuda_device, m, n, k, a_mn, b_mn, dtype):
+    torch.manual_seed(m + n + k)
+    A = torch.randn(m, k).to(dtype)
+    B = torch.randn(n, k).to(dtype)
+    ref = A.double() @ B.double().t()
+    a = (A.t().contiguous() if a_mn else A).to(cuda_device)
+    b = (B.t().contiguous() if b_mn else B).to(cuda_device)
+    c = _gemm(a, b, m, n, k, a_mn, b_mn, torch.float32)
+    tol = 2e-3 * max(1.0, k ** 0.5)
+    torch.testing.assert_close(c.double().cpu(), ref, rtol=2e-3, atol=tol)
+    assert nat.library().pmb_umma_timeout(1) == 0
+
+
+def test_gemm_tc_bias_tanh_bf16_out(cuda_device):
+    m, n, k = 300, 768, 192
+    A = torch.randn(m, k).to(torch.bfloat16)
+    B = (torch.randn(n, k) / k ** 0.5).to(torch.bfloat16)
+    bias = torch.randn(n)
+    ref = torch.tanh(A.double() @ B.double().t() + bias.double())
+    c = _gemm(A.to(cuda_device), B.to(cuda_device), m, n, k, False, False, torch.bfloat16, bias=bias.to(cuda_device),
+              act=1)
+    torch.testing.assert_close(c.double().cpu(), ref, rtol=1e-2, atol=1e-2)
