@@ -123,6 +123,26 @@ PMB_API int pmb_rms_norm_backward(const void* grad_out, const void* saved, int s
                           int grad_x_dtype, int grad_gamma_dtype, void* workspace,
                           int64_t workspace_bytes, void* stream);
 
+/*
+ * pmb_rms_norm_backward for callers that cannot allocate device memory for
+ * the call (a program binding this C ABI from another language with no
+ * device allocator of its own, or a loop that must not allocate mid-step
+ * because cudaMalloc / cudaFree synchronise the device).  Same arguments and
+ * results as pmb_rms_norm_backward minus the workspace: the grad_gamma
+ * partial sums live in a fixed 2.3 MiB array inside the library, held on
+ * every GPU that loads it until exit.  dim <= 1024 (larger: PMB_ERR_WORKSPACE).
+ * The first call on a device looks up the array's address there; make it
+ * before capturing work on the stream.  All calls on a device share the
+ * array (it keeps the last call's contents; each call rewrites what it
+ * reads), so calls that overlap on the GPU race: issue them in order on one
+ * stream.  No counterpart in the reference.
+ */
+PMB_API int pmb_rms_norm_backward_noalloc(const void* grad_out, const void* saved, int saved_is_input,
+                                          const float* inv_norm, const void* gamma, void* grad_x,
+                                          void* grad_gamma, int64_t rows, int64_t dim, int grad_dtype,
+                                          int gamma_dtype, int grad_x_dtype, int grad_gamma_dtype,
+                                          void* stream);
+
 /* ------------------------------------------------------------------------
  * Interleaved-pair rotary embedding on t[B, N, H, D] (bnhd layout):
  *   (t[2i], t[2i+1]) -> (t[2i] c - t[2i+1] s, t[2i+1] c + t[2i] s),

@@ -8,6 +8,8 @@
 // sums the partials column-wise (coalesced).  Reference semantics:
 // src/pymsst/training/cuda/fused_band_split.cu:1211-1315 (formulas at
 // :1237-1247 and :1263-1286).
+#include <mutex>
+
 #include "common.cuh"
 
 namespace pmb {
@@ -403,6 +405,103 @@ extern "C" int pmb_rms_norm_backward(const void* grad_out, const void* saved, in
   float* partial = static_cast<float*>(workspace);
   return PMB_DISPATCH(grad_dtype, Tg, "pmb_rms_norm_backward", [&] {
     return PMB_DISPATCH(grad_x_dtype, Tdx, "pmb_rms_norm_backward", [&] {
+      return launch_bwd<Tg, Tdx>(grad_out, saved, saved_is_input, inv_norm, gamma, gamma_dtype, grad_x, grad_gamma,
+                                 grad_gamma_dtype, rows, dim, partial, s);
+    });
+  });
+}
+
+// ---------------------------------------------------------------------------
+// RMSNorm backward without a caller-supplied workspace.
+//
+// Some callers of this library cannot allocate device memory for a call: a
+// program that binds the C ABI directly from another language and has no
+// tensor library or device allocator of its own, or a training loop that
+// plans all of its device memory before it starts and must not allocate in
+// the middle of a step (cudaMalloc and cudaFree synchronise the whole
+// device).  For them this variant keeps its scratch -- the per-block partial
+// sums of grad_gamma -- in one fixed array inside the library instead of a
+// workspace argument.  Inputs and outputs are still the caller's.
+//
+// Limits and behaviour:
+//  * the array holds kNoAllocScratchFloats fp32 values (2.3 MiB); every GPU
+//    that loads the library keeps it until the process exits;
+//  * dim may be at most kNoAllocMaxDim (1024); a larger dim is rejected with
+//    PMB_ERR_WORKSPACE before anything is launched;
+//  * the first call on a device looks up the array's address on that device
+//    (cudaGetSymbolAddress) and remembers it, so make that first call before
+//    capturing work on the stream;
+//  * all calls on a device share the array, and it keeps whatever the last
+//    call left in it.  Each call rewrites every partial sum it reads before
+//    reading it, so nothing has to be cleared between calls, but calls whose
+//    kernels overlap on the GPU (other streams, other host threads) race on
+//    the array: issue them in order on one stream.
+// ---------------------------------------------------------------------------
+namespace pmb {
+namespace {
+
+constexpr int64_t kNoAllocMaxDim = 1024;
+constexpr int64_t kNoAllocScratchFloats = (int64_t)kMaxBwdBlocks * kNoAllocMaxDim;
+constexpr int kNoAllocMaxDevices = 64;
+
+static __device__ __align__(256) float g_rms_noalloc_scratch[kNoAllocScratchFloats];
+
+std::mutex g_noalloc_mutex;
+float* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+// Device address of the scratch array on the current device (looked up once
+// per device; the host-side name is only a stand-in for the symbol).
+int noalloc_scratch(float** out, const char* name) {
+  int dev = 0;
+  PMB_CHECK_CUDA(cudaGetDevice(&dev), name);
+  if (dev < 0 || dev >= kNoAllocMaxDevices) {
+    set_error("%s: device ordinal %d is outside the supported range", name, dev);
+    return PMB_ERR_INVALID_ARGUMENT;
+  }
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t err = cudaGetSymbolAddress(&p, g_rms_noalloc_scratch);
+    if (err != cudaSuccess || p == nullptr) {
+      set_error("%s: cudaGetSymbolAddress failed on device %d: %s", name, dev, cudaGetErrorString(err));
+      return PMB_ERR_CUDA;
+    }
+    g_noalloc_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return PMB_OK;
+}
+
+}  // namespace
+}  // namespace pmb
+
+extern "C" int pmb_rms_norm_backward_noalloc(const void* grad_out, const void* saved, int saved_is_input,
+                                             const float* inv_norm, const void* gamma, void* grad_x,
+                                             void* grad_gamma, int64_t rows, int64_t dim, int grad_dtype,
+                                             int gamma_dtype, int grad_x_dtype, int grad_gamma_dtype,
+                                             void* stream) {
+  clear_error();
+  const char* name = "pmb_rms_norm_backward_noalloc";
+  PMB_REQUIRE(rows >= 0 && dim > 0, "%s: bad shape rows=%lld dim=%lld", name, (long long)rows, (long long)dim);
+  if (dim > kNoAllocMaxDim) {
+    set_error("%s: dim %lld exceeds the built-in scratch limit of %lld; use pmb_rms_norm_backward with a workspace",
+              name, (long long)dim, (long long)kNoAllocMaxDim);
+    return PMB_ERR_WORKSPACE;
+  }
+  PMB_REQUIRE(valid_code(gamma_dtype) && valid_code(grad_gamma_dtype), "%s: unsupported gamma/grad_gamma dtype",
+              name);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (rows == 0) {
+    if (grad_gamma != nullptr) PMB_CHECK_CUDA(cudaMemsetAsync(grad_gamma, 0, dim * dtype_size(grad_gamma_dtype), s), name);
+    return PMB_OK;
+  }
+  PMB_REQUIRE(grad_out && saved && inv_norm && gamma, "%s: NULL tensor argument", name);
+  float* partial = nullptr;
+  const int st = noalloc_scratch(&partial, name);
+  if (st) return st;
+  // bwd_blocks(rows) <= kMaxBwdBlocks, so the partial sums fit the array.
+  return PMB_DISPATCH(grad_dtype, Tg, name, [&] {
+    return PMB_DISPATCH(grad_x_dtype, Tdx, name, [&] {
       return launch_bwd<Tg, Tdx>(grad_out, saved, saved_is_input, inv_norm, gamma, gamma_dtype, grad_x, grad_gamma,
                                  grad_gamma_dtype, rows, dim, partial, s);
     });
