@@ -8,6 +8,8 @@
 // r = bi*seq + n, element (r, h, d) at bi*s_b + n*s_n + h*s_h + d.  The gate
 // row product, sigmoid and gating are one warp-per-row pass (the reference
 // uses two launches); the backward writes grad_attn with the attn strides.
+#include <initializer_list>
+
 #include "common.cuh"
 #include "reduce.cuh"
 
@@ -156,6 +158,244 @@ __global__ void __launch_bounds__(kThreads)
     grad_w[h * dim + i] = Elem<TP>::from_f(s);
 }
 
+// ---------------------------------------------------------------------------
+// Tiled path: a CTA takes 32 consecutive rows at a time.  The tile's x rows
+// and the gate weights sit in shared memory; every global access is a 16-byte
+// vector (x, attn, out, grad tensors), so each row costs one pass over its
+// bytes.  The backward keeps the weight / bias gradient partials in
+// registers across all tiles of a persistent CTA (one fp32 partial row per
+// CTA, summed by red::colsum_rows), so it needs no per-row gate-gradient
+// buffer.  Conditions (tiled_ok): 16-byte aligned pointers and strides, dim
+// and Dh multiples of the vector width, Dh / width a power of two <= 32.
+constexpr int kTileRows = 32;
+constexpr int kMaxWPerThread = 12;      // heads * dim <= 256 * 12 in the tiled backward
+constexpr int kMaxTiledBwdBlocks = 592; // partial rows in the workspace
+
+template <typename T>
+struct Vec {
+  static constexpr int N = 16 / sizeof(T);
+  __device__ __forceinline__ static void unpack(const uint4& u, float (&f)[N]) {
+    const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+    for (int i = 0; i < N; ++i) f[i] = Elem<T>::to_f(e[i]);
+  }
+  __device__ __forceinline__ static uint4 pack(const float (&f)[N]) {
+    uint4 u;
+    T* e = reinterpret_cast<T*>(&u);
+#pragma unroll
+    for (int i = 0; i < N; ++i) e[i] = Elem<T>::from_f(f[i]);
+    return u;
+  }
+};
+
+// Shared-memory carve-up common to both directions: gate weights as fp32
+// [H][dim + 4], the x tile [32][dim + V] (row padding keeps 16-byte reads of
+// neighbouring rows on different banks), then two [32][H] fp32 arrays.
+struct TileSmem {
+  int wld, xld;
+  size_t w_bytes, x_bytes, bytes;
+  __host__ __device__ TileSmem(int H, int dim, int V) {
+    wld = dim + 4;
+    xld = dim + V;
+    w_bytes = (size_t)H * wld * 4;
+    x_bytes = (size_t)kTileRows * xld * (16 / V);
+    bytes = w_bytes + x_bytes + 2 * (size_t)kTileRows * H * 4;
+  }
+};
+
+template <typename T, typename TP>
+__device__ __forceinline__ void load_weights_smem(const TP* __restrict__ W, int H, int dim, float* w_s, int wld) {
+  for (int e = threadIdx.x; e < H * dim; e += kThreads) w_s[(e / dim) * wld + e % dim] = Elem<TP>::to_f(W[e]);
+}
+
+template <typename T>
+__device__ __forceinline__ void load_x_tile(const T* __restrict__ x, int64_t r0, int64_t rows, int dim, T* x_s,
+                                            int xld) {
+  constexpr int V = Vec<T>::N;
+  const int vpr = dim / V;
+  for (int v = threadIdx.x; v < kTileRows * vpr; v += kThreads) {
+    const int r = v / vpr, c = (v - r * vpr) * V;
+    uint4 u = make_uint4(0, 0, 0, 0);
+    if (r0 + r < rows) u = *reinterpret_cast<const uint4*>(x + (r0 + r) * dim + c);
+    *reinterpret_cast<uint4*>(x_s + r * xld + c) = u;
+  }
+}
+
+template <typename T, typename TP>
+__global__ void __launch_bounds__(kThreads, 4)
+    gate_fwd_tiled(const T* __restrict__ attn, AttnLayout la, const T* __restrict__ x, const TP* __restrict__ W,
+                   const TP* __restrict__ bias, int64_t rows, int H, int Dh, int dim, T* __restrict__ out,
+                   T* __restrict__ gate) {
+  constexpr int V = Vec<T>::N;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const TileSmem L(H, dim, V);
+  float* w_s = reinterpret_cast<float*>(smem_raw);
+  T* x_s = reinterpret_cast<T*>(smem_raw + L.w_bytes);
+  float* g_s = reinterpret_cast<float*>(smem_raw + L.w_bytes + L.x_bytes);
+  load_weights_smem<T, TP>(W, H, dim, w_s, L.wld);
+  const int vh = Dh / V, vr = H * vh;
+  const int64_t tiles = (rows + kTileRows - 1) / kTileRows;
+  for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+    const int64_t r0 = tile * kTileRows;
+    load_x_tile<T>(x, r0, rows, dim, x_s, L.xld);
+    __syncthreads();
+    for (int p = threadIdx.x; p < kTileRows * H; p += kThreads) {
+      const int r = p / H, h = p - r * H;
+      const T* xr = x_s + r * L.xld;
+      const float* wr = w_s + h * L.wld;
+      float acc = 0.f;
+      for (int i = 0; i < dim; i += V) {
+        float xf[V];
+        Vec<T>::unpack(*reinterpret_cast<const uint4*>(xr + i), xf);
+#pragma unroll
+        for (int q = 0; q < V; q += 4) {
+          const float4 w4 = *reinterpret_cast<const float4*>(wr + i + q);
+          acc += xf[q] * w4.x + xf[q + 1] * w4.y + xf[q + 2] * w4.z + xf[q + 3] * w4.w;
+        }
+      }
+      const float g = round_to<T>(sigmoidf_(acc + Elem<TP>::to_f(bias[h])));
+      g_s[p] = g;
+      if (r0 + r < rows) gate[r0 * H + p] = Elem<T>::from_f(g);
+    }
+    __syncthreads();
+#pragma unroll 4
+    for (int v = threadIdx.x; v < kTileRows * vr; v += kThreads) {
+      const int r = v / vr, c = v - r * vr;
+      if (r0 + r >= rows) continue;
+      const int h = c / vh, d = (c - h * vh) * V;
+      float a[V];
+      Vec<T>::unpack(*reinterpret_cast<const uint4*>(attn + la.row_base(r0 + r) + h * la.s_h + d), a);
+      const float g = g_s[r * H + h];
+#pragma unroll
+      for (int q = 0; q < V; ++q) a[q] *= g;
+      *reinterpret_cast<uint4*>(out + (r0 + r) * (int64_t)vr * V + (int64_t)c * V) = Vec<T>::pack(a);
+    }
+    __syncthreads();
+  }
+}
+
+template <typename T, typename TP>
+__global__ void __launch_bounds__(kThreads, 3)
+    gate_bwd_tiled(const T* __restrict__ grad_out, const T* __restrict__ attn, AttnLayout la,
+                   const T* __restrict__ x, const TP* __restrict__ W, const T* __restrict__ gate, int64_t rows,
+                   int H, int Dh, int dim, T* __restrict__ grad_attn, T* __restrict__ grad_x,
+                   float* __restrict__ partial_w, float* __restrict__ partial_b) {
+  constexpr int V = Vec<T>::N;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const TileSmem L(H, dim, V);
+  float* w_s = reinterpret_cast<float*>(smem_raw);
+  T* x_s = reinterpret_cast<T*>(smem_raw + L.w_bytes);
+  float* g_s = reinterpret_cast<float*>(smem_raw + L.w_bytes + L.x_bytes);
+  float* gp_s = g_s + kTileRows * H;
+  load_weights_smem<T, TP>(W, H, dim, w_s, L.wld);
+  const int vh = Dh / V, vr = H * vh, vpr = dim / V, hd = H * dim;
+  float accw[kMaxWPerThread];
+#pragma unroll
+  for (int j = 0; j < kMaxWPerThread; ++j) accw[j] = 0.f;
+  float accb = 0.f;
+  const int64_t tiles = (rows + kTileRows - 1) / kTileRows;
+  for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+    const int64_t r0 = tile * kTileRows;
+    load_x_tile<T>(x, r0, rows, dim, x_s, L.xld);
+    for (int p = threadIdx.x; p < kTileRows * H; p += kThreads)
+      g_s[p] = r0 + p / H < rows ? Elem<T>::to_f(gate[r0 * H + p]) : 0.f;
+    __syncthreads();
+    // grad_attn = grad_out * gate; per (row, head) sum of grad_out * attn
+    // over the head's vh consecutive vectors, reduced across vh lanes.
+    // Trip counts are warp-uniform (kTileRows * vr is a multiple of 32).
+#pragma unroll 2
+    for (int v = threadIdx.x; v < kTileRows * vr; v += kThreads) {
+      const int r = v / vr, c = v - r * vr;
+      const int h = c / vh, d = (c - h * vh) * V;
+      float part = 0.f;
+      if (r0 + r < rows) {
+        const int64_t ai = la.row_base(r0 + r) + h * la.s_h + d;
+        float go[V], a[V];
+        Vec<T>::unpack(*reinterpret_cast<const uint4*>(grad_out + (r0 + r) * (int64_t)vr * V + (int64_t)c * V), go);
+        Vec<T>::unpack(*reinterpret_cast<const uint4*>(attn + ai), a);
+        const float g = g_s[r * H + h];
+#pragma unroll
+        for (int q = 0; q < V; ++q) {
+          part += go[q] * a[q];
+          a[q] = go[q] * g;
+        }
+        *reinterpret_cast<uint4*>(grad_attn + ai) = Vec<T>::pack(a);
+      }
+      for (int o = vh >> 1; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+      if ((c & (vh - 1)) == 0) {
+        const float g = g_s[r * H + h];
+        gp_s[r * H + h] = part * g * (1.0f - g);
+      }
+    }
+    __syncthreads();
+    // grad_x[r, i] = sum_h gp[r, h] W[h, i]
+    for (int v = threadIdx.x; v < kTileRows * vpr; v += kThreads) {
+      const int r = v / vpr, i = (v - r * vpr) * V;
+      if (r0 + r >= rows) continue;
+      float acc[V];
+#pragma unroll
+      for (int q = 0; q < V; ++q) acc[q] = 0.f;
+      for (int h = 0; h < H; ++h) {
+        const float gp = gp_s[r * H + h];
+        const float* wr = w_s + h * L.wld + i;
+#pragma unroll
+        for (int q = 0; q < V; q += 4) {
+          const float4 w4 = *reinterpret_cast<const float4*>(wr + q);
+          acc[q] += gp * w4.x;
+          acc[q + 1] += gp * w4.y;
+          acc[q + 2] += gp * w4.z;
+          acc[q + 3] += gp * w4.w;
+        }
+      }
+      *reinterpret_cast<uint4*>(grad_x + (r0 + r) * dim + i) = Vec<T>::pack(acc);
+    }
+    // grad_W[h, i] += sum_r gp[r, h] x[r, i]; grad_b[h] += sum_r gp[r, h]
+    // (rows past the end have gp = 0 and x = 0).
+#pragma unroll
+    for (int j = 0; j < kMaxWPerThread; ++j) {
+      const int e = threadIdx.x + j * kThreads;
+      if (e < hd) {
+        const int h = e / dim, i = e - h * dim;
+        float acc = accw[j];
+#pragma unroll 8
+        for (int r = 0; r < kTileRows; ++r) acc += gp_s[r * H + h] * Elem<T>::to_f(x_s[r * L.xld + i]);
+        accw[j] = acc;
+      }
+    }
+    if (threadIdx.x < H)
+      for (int r = 0; r < kTileRows; ++r) accb += gp_s[r * H + threadIdx.x];
+    __syncthreads();
+  }
+#pragma unroll
+  for (int j = 0; j < kMaxWPerThread; ++j) {
+    const int e = threadIdx.x + j * kThreads;
+    if (e < hd) partial_w[(int64_t)blockIdx.x * hd + e] = accw[j];
+  }
+  if (threadIdx.x < H) partial_b[(int64_t)blockIdx.x * H + threadIdx.x] = accb;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// Whether the tiled kernels apply (vector width V = 16 / element size).
+bool tiled_ok(int es, const AttnLayout& la, int64_t H, int64_t Dh, int64_t dim, std::initializer_list<const void*> ptrs) {
+  const int V = 16 / es;
+  if (dim % V != 0 || Dh % V != 0) return false;
+  const int64_t vh = Dh / V;
+  if (vh > 32 || (vh & (vh - 1)) != 0) return false;
+  if (la.s_b % V != 0 || la.s_n % V != 0 || la.s_h % V != 0) return false;
+  for (const void* p : ptrs)
+    if (!aligned16(p)) return false;
+  return TileSmem((int)H, (int)dim, V).bytes <= 200 * 1024;
+}
+
+int tiled_grid(int64_t rows, int per_sm, int cap) {
+  const int64_t tiles = (rows + kTileRows - 1) / kTileRows;
+  int64_t g = (int64_t)num_sms() * per_sm;
+  if (g > cap) g = cap;
+  if (g > tiles) g = tiles;
+  return (int)(g < 1 ? 1 : g);
+}
+
 int row_grid(int64_t rows) {
   int64_t g = (rows + kWarps - 1) / kWarps;
   const int64_t cap = (int64_t)num_sms() * 16;
@@ -187,6 +427,18 @@ extern "C" int pmb_attention_gate_forward(const void* attn, int64_t seq_len, int
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const size_t smem = (size_t)heads * dim * sizeof(float);
   return PMB_DISPATCH_PARAM(dtype, param_dtype, T, TP, name, [&] {
+    if (tiled_ok(sizeof(T), la, heads, dim_head, dim, {attn, x, out})) {
+      const size_t tsm = TileSmem((int)heads, (int)dim, Vec<T>::N).bytes;
+      if (tsm > 48 * 1024)
+        PMB_CHECK_CUDA(
+            cudaFuncSetAttribute(gate_fwd_tiled<T, TP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tsm), name);
+      gate_fwd_tiled<T, TP><<<tiled_grid(rows, 8, 1 << 20), kThreads, tsm, s>>>(
+          static_cast<const T*>(attn), la, static_cast<const T*>(x), static_cast<const TP*>(weight),
+          static_cast<const TP*>(bias), rows, (int)heads, (int)dim_head, (int)dim, static_cast<T*>(out),
+          static_cast<T*>(gate));
+      PMB_CHECK_LAUNCH(name);
+      return PMB_OK;
+    }
     if (smem > 48 * 1024)
       PMB_CHECK_CUDA(cudaFuncSetAttribute(gate_fwd<T, TP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                      name);
@@ -201,7 +453,10 @@ extern "C" int pmb_attention_gate_forward(const void* attn, int64_t seq_len, int
 
 extern "C" int64_t pmb_attention_gate_backward_workspace_size(int64_t rows, int64_t heads, int64_t dim) {
   if (rows <= 0 || heads <= 0 || dim <= 0) return 0;
-  return align256(rows * heads * 4) + align256(chunks_of(rows) * heads * (dim + 1) * 4);
+  const int64_t rowwise = align256(rows * heads * 4) + align256(chunks_of(rows) * heads * (dim + 1) * 4);
+  const int64_t tiled = align256((int64_t)kMaxTiledBwdBlocks * heads * dim * 4) +
+                        align256((int64_t)kMaxTiledBwdBlocks * heads * 4);
+  return rowwise > tiled ? rowwise : tiled;
 }
 
 extern "C" int pmb_attention_gate_backward(const void* grad_out, const void* attn, int64_t seq_len,
@@ -237,6 +492,29 @@ extern "C" int pmb_attention_gate_backward(const void* grad_out, const void* att
   AttnLayout la{seq_len, attn_stride_batch, attn_stride_seq, attn_stride_head};
   const size_t smem = (size_t)heads * dim * sizeof(float);
   return PMB_DISPATCH_PARAM(dtype, param_dtype, T, TP, name, [&] {
+    if (heads * dim <= kThreads * kMaxWPerThread &&
+        tiled_ok(sizeof(T), la, heads, dim_head, dim, {grad_out, attn, x, grad_attn, grad_x})) {
+      const size_t tsm = TileSmem((int)heads, (int)dim, Vec<T>::N).bytes;
+      if (tsm > 48 * 1024)
+        PMB_CHECK_CUDA(
+            cudaFuncSetAttribute(gate_bwd_tiled<T, TP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tsm), name);
+      const int grid = tiled_grid(rows, 4, kMaxTiledBwdBlocks);
+      float* pw = static_cast<float*>(workspace);
+      float* pb = reinterpret_cast<float*>(static_cast<char*>(workspace) +
+                                           align256((int64_t)kMaxTiledBwdBlocks * heads * dim * 4));
+      gate_bwd_tiled<T, TP><<<grid, kThreads, tsm, s>>>(
+          static_cast<const T*>(grad_out), static_cast<const T*>(attn), la, static_cast<const T*>(x),
+          static_cast<const TP*>(weight), static_cast<const T*>(gate), rows, (int)heads, (int)dim_head, (int)dim,
+          static_cast<T*>(grad_attn), static_cast<T*>(grad_x), pw, pb);
+      PMB_CHECK_LAUNCH(name);
+      red::colsum_rows<<<(int)((heads * dim + 31) / 32), red::kThreads, 0, s>>>(pw, grid, heads * dim, grad_weight,
+                                                                               Elem<TP>::code);
+      PMB_CHECK_LAUNCH(name);
+      red::colsum_rows<<<(int)((heads + 31) / 32), red::kThreads, 0, s>>>(pb, grid, heads, grad_bias,
+                                                                         Elem<TP>::code);
+      PMB_CHECK_LAUNCH(name);
+      return PMB_OK;
+    }
     if (smem > 48 * 1024)
       PMB_CHECK_CUDA(
           cudaFuncSetAttribute(gate_bwd_rows<T, TP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem), name);

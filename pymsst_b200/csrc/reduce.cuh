@@ -65,6 +65,28 @@ __global__ void __launch_bounds__(kThreads)
   store_dyn(const_cast<void*>(table.ptr0[b]), c - table.off[b], out_code, s);
 }
 
+// Column sums of a [nrows, cols] fp32 partial matrix with many rows: each CTA
+// covers 32 columns; its 8 warps stride over the rows (coalesced 128-byte
+// row segments) and the per-warp sums are combined in shared memory.
+// Launch: grid ceil(cols / 32), 256 threads.  out[c] stored as out_code.
+__global__ void __launch_bounds__(kThreads)
+    colsum_rows(const float* __restrict__ partial, int nrows, int64_t cols, void* __restrict__ out, int out_code) {
+  __shared__ float red_s[8][33];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t c = (int64_t)blockIdx.x * 32 + lane;
+  float s = 0.f;
+  if (c < cols)
+    for (int r = warp; r < nrows; r += 8) s += partial[(int64_t)r * cols + c];
+  red_s[warp][lane] = s;
+  __syncthreads();
+  if (warp == 0 && c < cols) {
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) t += red_s[w][lane];
+    store_dyn(out, c, out_code, t);
+  }
+}
+
 }  // namespace
 }  // namespace red
 }  // namespace pmb

@@ -11,6 +11,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "reduce.cuh"
 
 namespace pmb {
 namespace {
@@ -260,16 +261,6 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
-__global__ void __launch_bounds__(kThreads)
-    column_sum_kernel(const float* __restrict__ partial, int blocks, int dim, void* __restrict__ out,
-                      int out_code) {
-  const int c = blockIdx.x * kThreads + threadIdx.x;
-  if (c >= dim) return;
-  float s = 0.f;
-  for (int b = 0; b < blocks; ++b) s += partial[(int64_t)b * dim + c];
-  st_dyn(out, c, out_code, s);
-}
-
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 int grid_for_rows(int64_t rows, int64_t cap) {
@@ -343,8 +334,7 @@ int launch_bwd(const void* dy, const void* saved, int saved_is_input, const floa
   }
   PMB_CHECK_LAUNCH("pmb_rms_norm_backward");
   if (dgamma != nullptr) {
-    column_sum_kernel<<<(int)((dim + kThreads - 1) / kThreads), kThreads, 0, stream>>>(partial, grid, (int)dim,
-                                                                                       dgamma, dgcode);
+    red::colsum_rows<<<(int)((dim + 31) / 32), red::kThreads, 0, stream>>>(partial, grid, dim, dgamma, dgcode);
     PMB_CHECK_LAUNCH("pmb_rms_norm_backward(grad_gamma)");
   }
   return PMB_OK;

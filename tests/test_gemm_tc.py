@@ -21,6 +21,15 @@ def _gemm(a, b, m, n, k, a_mn, b_mn, out_dtype, bias=None, act=0):
     return c
 
 
+def _padded(t, device):
+    """Copy of a 2-D tensor whose row stride is rounded up to 8 elements
+    (16 bytes), the alignment TMA needs; ragged shapes stay ragged."""
+    ld = (t.shape[1] + 7) // 8 * 8
+    store = torch.zeros(t.shape[0], ld, dtype=t.dtype)
+    store[:, : t.shape[1]] = t
+    return store.to(device)[:, : t.shape[1]]
+
+
 @pytest.mark.parametrize("m,n,k", [(128, 128, 64), (1000, 192, 768), (130, 70, 100), (4096, 1536, 192), (64, 8, 16)])
 @pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, False), (True, True)])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
@@ -29,8 +38,8 @@ def test_gemm_tc_matches_reference(cuda_device, m, n, k, a_mn, b_mn, dtype):
     A = torch.randn(m, k).to(dtype)
     B = torch.randn(n, k).to(dtype)
     ref = A.double() @ B.double().t()
-    a = (A.t().contiguous() if a_mn else A).to(cuda_device)
-    b = (B.t().contiguous() if b_mn else B).to(cuda_device)
+    a = _padded(A.t() if a_mn else A, cuda_device)
+    b = _padded(B.t() if b_mn else B, cuda_device)
     c = _gemm(a, b, m, n, k, a_mn, b_mn, torch.float32)
     tol = 2e-3 * max(1.0, k ** 0.5)
     torch.testing.assert_close(c.double().cpu(), ref, rtol=2e-3, atol=tol)
@@ -46,3 +55,11 @@ def test_gemm_tc_bias_tanh_bf16_out(cuda_device):
     c = _gemm(A.to(cuda_device), B.to(cuda_device), m, n, k, False, False, torch.bfloat16, bias=bias.to(cuda_device),
               act=1)
     torch.testing.assert_close(c.double().cpu(), ref, rtol=1e-2, atol=1e-2)
+
+
+def test_gemm_tc_rejects_unaligned_stride(cuda_device):
+    a = torch.randn(130, 100, device=cuda_device).to(torch.bfloat16)
+    c = torch.empty(130, 130, device=cuda_device)
+    st = nat.library().pmb_gemm_tc(a.data_ptr(), 100, 0, a.data_ptr(), 100, 0, c.data_ptr(), 130, 0, None, 0, 0,
+                                   130, 130, 100, nat.dtype_code(a.dtype), nat.stream_handle(a.device))
+    assert st == -4 and b"16-byte" in nat.library().pmb_last_error()
