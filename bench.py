@@ -51,7 +51,8 @@ TIMED_ENTRIES = [
     "pmb_attention_gate_forward", "pmb_attention_gate_backward", "pmb_band_gather_forward",
     "pmb_band_recombine_forward", "pmb_band_recombine_backward", "pmb_band_split_forward",
     "pmb_band_split_backward", "pmb_grouped_linear_forward", "pmb_grouped_linear_backward",
-    "pmb_mask_estimator_final_forward", "pmb_mask_estimator_final_backward",
+    "pmb_mask_estimator_final_forward", "pmb_mask_estimator_final_backward", "pmb_mask_estimator_tc_forward",
+    "pmb_mask_estimator_tc_backward", "pmb_gemm_tc",
 ]
 
 
@@ -63,6 +64,8 @@ def parse():
     p.add_argument("--config", default="config3", choices=sorted(CONFIGS))
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--profile-range", action="store_true",
+                   help="bracket the timed steps with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
     p.add_argument("--traffic-json", default=str(REPO / "profiles" / "traffic.json"),
                    help="per-kernel ncu DRAM bytes per launch (written from an ncu capture)")
     return p.parse_args()
@@ -209,11 +212,15 @@ def run_ours(args, rank: int, world: int, local: int):
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     with nat.time_entries(TIMED_ENTRIES) as timer:
+        if args.profile_range:
+            torch.cuda.cudart().cudaProfilerStart()
         start.record(stream)
         for i in range(args.steps):
             trainer.step(*dev[i % pool])
         end.record(stream)
         barrier()
+        if args.profile_range:
+            torch.cuda.cudart().cudaProfilerStop()
     launches = nat.library().pmb_launch_count() - launches0
     value_ms = start.elapsed_time(end)
 

@@ -87,6 +87,21 @@ PMB_API int pmb_gemm_tc(const void* a, int64_t lda, int a_mn_major, const void* 
                         void* c, int64_t ldc, int c_dtype, const void* bias, int bias_dtype, int activation,
                         int64_t m, int64_t n, int64_t k, int dtype, void* stream);
 
+/*
+ * Weight-gradient GEMM on the tensor cores: C[m, n] = sum_k A[k*lda + m] *
+ * B[k*ldb + n] (both operands row-major with K as the row index, e.g. an
+ * output gradient and the layer input over the batch rows), written in
+ * c_dtype with row stride ldc.  K is split into slices whose fp32 partials
+ * are summed in a fixed order (deterministic); workspace of
+ * pmb_gemm_tc_wgrad_workspace_size(m, n, k) bytes (0 when no split).
+ * Replaces the weight-gradient use of the reference's cuBLAS grouped GEMM
+ * (.cu:2038-2281) for dense layers.
+ */
+PMB_API int64_t pmb_gemm_tc_wgrad_workspace_size(int64_t m, int64_t n, int64_t k);
+PMB_API int pmb_gemm_tc_wgrad(const void* a, int64_t lda, const void* b, int64_t ldb, int64_t m, int64_t n,
+                              int64_t k, void* c, int64_t ldc, int c_dtype, int dtype, void* workspace,
+                              int64_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------------------------
  * RMSNorm over the last dimension (transformer RMSNorm, F.normalize form):
  *   inv_norm[r] = 1 / max(||x[r,:]||_2, 1e-12)
@@ -329,7 +344,9 @@ PMB_API int pmb_band_recombine_backward(const float* grad_out, const float* stft
  * q and k are rotated (if rotate_qk) by cos/sin fp32 [N, Dh/2]:
  *   (e, o) -> (e c - o s, o c + e s)   on interleaved pairs.
  * merge is the backward: grad_q/k/v [B, H, N, Dh] -> grad_qkv [B*N, 3*H*Dh]
- * with the inverse rotation.  Replaces qkv_to_bnhd + rotary_forward /
+ * with the inverse rotation; the three gradients share the element strides
+ * (stride_batch, stride_head, stride_seq) with Dh contiguous, so both the
+ * [B, H, N, Dh] and the [B, N, H, Dh] layouts are read in place.  Replaces qkv_to_bnhd + rotary_forward /
  * rotary_backward on q and k (fused_roformer.py:710-732, 793-818;
  * .cu:1077-1168) with one pass each way.
  * ---------------------------------------------------------------------- */
@@ -338,7 +355,68 @@ PMB_API int pmb_qkv_rotary_split(const void* qkv, const float* cos, const float*
                                  int rotate_qk, int dtype, void* stream);
 PMB_API int pmb_qkv_rotary_merge(const void* grad_q, const void* grad_k, const void* grad_v, const float* cos,
                                  const float* sin, int64_t batch, int64_t seq_len, int64_t heads,
-                                 int64_t dim_head, void* grad_qkv, int rotate_qk, int dtype, void* stream);
+                                 int64_t dim_head, void* grad_qkv, int rotate_qk, int dtype, int64_t stride_batch,
+                                 int64_t stride_head, int64_t stride_seq, void* stream);
+
+/*
+ * Attention input projection with the rotary embedding fused into the GEMM
+ * epilogue (bf16 / fp16, tcgen05): x [B*N, dim] and weight [3*H*Dh, dim] in
+ * the activation dtype; q, k, v each [B*N, H*Dh] (= the [B, N, H, Dh]
+ * layout) = the three thirds of x weight^T, q and k rotated as in
+ * pmb_qkv_rotary_split (each projection value rounded to the activation
+ * dtype before rotation).  The angle tables are TRANSPOSED here:
+ * cos_t / sin_t fp32 [Dh/2, N].  dim % 8 == 0, Dh % 32 == 0.  The backward
+ * is pmb_qkv_rotary_merge (which reads this layout in place) plus the two
+ * projection GEMMs.  Replaces to_qkv + qkv_to_bnhd + rotary_forward
+ * (fused_roformer.py:710-732, 793-818; .cu:1077-1128).
+ */
+PMB_API int pmb_qkv_linear_rotary_forward(const void* x, const void* weight, const float* cos_t,
+                                          const float* sin_t, int64_t batch, int64_t seq_len, int64_t dim,
+                                          int64_t heads, int64_t dim_head, void* q, void* k, void* v,
+                                          int rotate_qk, int dtype, void* stream);
+
+/* ------------------------------------------------------------------------
+ * GELU (exact erf form of torch.nn.GELU()) and column sums for the
+ * transformer feed-forward block, 16-bit or fp32 tensors:
+ *   pmb_gelu_forward:  y = x * Phi(x) over n elements (16-byte aligned).
+ *   pmb_gelu_backward: grad_in = grad_out * (Phi(x) + x phi(x)) on [rows,
+ *     cols]; with grad_bias non-NULL also its column sums (the bias gradient
+ *     of the Linear before the GELU) in bias_dtype.
+ *   pmb_column_sum:    out[c] = sum_r x[r, c] (a Linear's bias gradient).
+ * cols must be a multiple of 16 bytes' worth of elements; workspace of
+ * pmb_rows_pass_workspace_size(rows, cols) bytes.  No counterpart in the
+ * reference's extension (torch runs GELU and the bias reductions there).
+ * ---------------------------------------------------------------------- */
+PMB_API int pmb_gelu_forward(const void* x, void* y, int64_t n, int dtype, void* stream);
+PMB_API int64_t pmb_rows_pass_workspace_size(int64_t rows, int64_t cols);
+PMB_API int pmb_gelu_backward(const void* grad_out, const void* x, void* grad_in, int64_t rows, int64_t cols,
+                              void* grad_bias, int bias_dtype, int dtype, void* workspace, int64_t workspace_bytes,
+                              void* stream);
+PMB_API int pmb_column_sum(const void* x, int64_t rows, int64_t cols, void* out, int out_dtype, int dtype,
+                           void* workspace, int64_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Transformer feed-forward block on the tcgen05 tensor cores (bf16 / fp16
+ * activations; parameters fp32 or the activation dtype):
+ *   pre = x w1^T + b1,  act = gelu(pre) (exact erf form),  out = act w2^T + b2
+ * x [rows, dim]; w1 [hidden, dim] and w2 [dim, hidden] in the activation
+ * dtype (operands of the tensor cores); b1, b2 in param_dtype.  pre and act
+ * [rows, hidden] are saved for the backward.  The backward writes grad_x
+ * (nullable, activation dtype) and the four parameter gradients in
+ * param_dtype, using a workspace of
+ * pmb_feed_forward_backward_workspace_size bytes.  dim, hidden % 8 == 0.
+ * No counterpart in the reference's extension: the reference runs this
+ * block of every transformer layer through torch (Linear, GELU, Linear).
+ * ---------------------------------------------------------------------- */
+PMB_API int pmb_feed_forward_forward(const void* x, const void* w1, const void* b1, const void* w2, const void* b2,
+                                     int64_t rows, int64_t dim, int64_t hidden, void* pre, void* act, void* out,
+                                     int dtype, int param_dtype, void* stream);
+PMB_API int64_t pmb_feed_forward_backward_workspace_size(int64_t rows, int64_t dim, int64_t hidden, int dtype);
+PMB_API int pmb_feed_forward_backward(const void* grad_out, const void* x, const void* pre, const void* act,
+                                      const void* w1, const void* w2, int64_t rows, int64_t dim, int64_t hidden,
+                                      void* grad_x, void* grad_w1, void* grad_b1, void* grad_w2, void* grad_b2,
+                                      int dtype, int param_dtype, void* workspace, int64_t workspace_bytes,
+                                      void* stream);
 
 /* ------------------------------------------------------------------------
  * MaskEstimator MLP on the tcgen05 tensor cores (training path, bf16/fp16

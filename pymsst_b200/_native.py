@@ -31,6 +31,18 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "pmb_launch_count": (ctypes.c_uint64, []),
     "pmb_umma_timeout": (ctypes.c_uint, [_i]),
     "pmb_gemm_tc": (_i, [_p, _i64, _i, _p, _i64, _i, _p, _i64, _i, _p, _i, _i, _i64, _i64, _i64, _i, _p]),
+    "pmb_gemm_tc_wgrad_workspace_size": (_i64, [_i64, _i64, _i64]),
+    "pmb_gemm_tc_wgrad": (_i, [_p, _i64, _p, _i64, _i64, _i64, _i64, _p, _i64, _i, _i, _p, _i64, _p]),
+    "pmb_qkv_linear_rotary_forward": (
+        _i, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _i, _i, _p]),
+    "pmb_feed_forward_forward": (_i, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _p, _p, _p, _i, _i, _p]),
+    "pmb_feed_forward_backward_workspace_size": (_i64, [_i64, _i64, _i64, _i]),
+    "pmb_feed_forward_backward": (
+        _i, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _p, _p, _p, _p, _p, _i, _i, _p, _i64, _p]),
+    "pmb_gelu_forward": (_i, [_p, _p, _i64, _i, _p]),
+    "pmb_rows_pass_workspace_size": (_i64, [_i64, _i64]),
+    "pmb_gelu_backward": (_i, [_p, _p, _p, _i64, _i64, _p, _i, _i, _p, _i64, _p]),
+    "pmb_column_sum": (_i, [_p, _i64, _i64, _p, _i, _i, _p, _i64, _p]),
     "pmb_rms_norm_forward": (_i, [_p, _p, _p, _p, _p, _i64, _i64, _i, _i, _i, _p]),
     "pmb_rms_norm_backward_workspace_size": (_i64, [_i64, _i64]),
     "pmb_rms_norm_backward": (_i, [_p, _p, _i, _p, _p, _p, _p, _i64, _i64, _i, _i, _i, _i, _p, _i64, _p]),
@@ -67,7 +79,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "pmb_mask_estimator_tc_backward": (
         _i, [_p, _p, _p, _p, _p, _i64, _i, _i64, _i64, _i, _pi64, _pp, _pp, _p, _i, _i, _p, _i64, _p]),
     "pmb_qkv_rotary_split": (_i, [_p, _p, _p, _i64, _i64, _i64, _i64, _p, _p, _p, _i, _i, _p]),
-    "pmb_qkv_rotary_merge": (_i, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _i, _i, _p]),
+    "pmb_qkv_rotary_merge": (_i, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _i, _i, _i64, _i64, _i64, _p]),
 }
 
 

@@ -507,10 +507,10 @@ extern "C" int pmb_attention_gate_backward(const void* grad_out, const void* att
           static_cast<const TP*>(weight), static_cast<const T*>(gate), rows, (int)heads, (int)dim_head, (int)dim,
           static_cast<T*>(grad_attn), static_cast<T*>(grad_x), pw, pb);
       PMB_CHECK_LAUNCH(name);
-      red::colsum_rows<<<(int)((heads * dim + 31) / 32), red::kThreads, 0, s>>>(pw, grid, heads * dim, grad_weight,
+      red::colsum_rows<<<red::colsum_rows_grid(heads * dim), red::kThreads, 0, s>>>(pw, grid, heads * dim, grad_weight,
                                                                                Elem<TP>::code);
       PMB_CHECK_LAUNCH(name);
-      red::colsum_rows<<<(int)((heads + 31) / 32), red::kThreads, 0, s>>>(pb, grid, heads, grad_bias,
+      red::colsum_rows<<<red::colsum_rows_grid(heads), red::kThreads, 0, s>>>(pb, grid, heads, grad_bias,
                                                                          Elem<TP>::code);
       PMB_CHECK_LAUNCH(name);
       return PMB_OK;

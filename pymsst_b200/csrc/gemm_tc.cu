@@ -5,8 +5,7 @@
 // A(m, k) = A[m*lda + k] (K-major) or A[k*lda + m] (MN-major); same for B.
 // Replaces the reference's cuBLAS grouped-GEMM planner for the dense case
 // (src/pymsst/training/cuda/fused_band_split.cu:2038-2281).
-#include "gemm_umma.cuh"
-#include "tma.cuh"
+#include "dense_gemm.cuh"
 
 namespace pmb {
 // This unit's tcgen05 timeout flag (see umma.cuh).
@@ -58,82 +57,6 @@ int make_map_3d(CUtensorMap& map, const void* base, int dtype, uint64_t inner, u
 
 }  // namespace tma
 
-namespace {
-
-__device__ __forceinline__ void store_dyn(void* p, int64_t i, int code, float v) {
-  switch (code) {
-    case PMB_FLOAT16:
-      static_cast<__half*>(p)[i] = __float2half_rn(v);
-      break;
-    case PMB_BFLOAT16:
-      static_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
-      break;
-    default:
-      static_cast<float*>(p)[i] = v;
-  }
-}
-
-__device__ __forceinline__ float load_dyn(const void* p, int64_t i, int code) {
-  switch (code) {
-    case PMB_FLOAT16:
-      return __half2float(static_cast<const __half*>(p)[i]);
-    case PMB_BFLOAT16:
-      return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
-    default:
-      return static_cast<const float*>(p)[i];
-  }
-}
-
-struct DenseEpi {
-  void* c;
-  int64_t ldc;
-  int c_dtype;
-  const void* bias;
-  int bias_dtype;
-  int act;
-  template <int BN>
-  __device__ void run(const ugemm::Plan&, const ugemm::TileCtx& t) const {
-#pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 32) {
-      float v[32];
-      umma::tmem_ld32(t.taddr + c0, v);
-      if (!t.row_valid) continue;
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const int n = c0 + j;
-        if (n >= t.n_valid) break;
-        float x = v[j];
-        if (bias) x += load_dyn(bias, t.n0 + n, bias_dtype);
-        if (act == PMB_ACT_TANH) x = tanhf(x);
-        store_dyn(c, (int64_t)t.row * ldc + t.n0 + n, c_dtype, x);
-      }
-    }
-  }
-};
-
-template <int BN, int STAGES, bool A_MN, bool B_MN>
-int launch_dense(const CUtensorMap& ma, const CUtensorMap& mb, ugemm::Plan& plan, const DenseEpi& epi, int fp16,
-                 cudaStream_t stream, const char* name) {
-  const int tiles = ugemm::build_plan(plan, BN);
-  if (tiles == 0) return PMB_OK;
-  auto kern = ugemm::umma_gemm_kernel<BN, STAGES, A_MN, B_MN, DenseEpi>;
-  const int smem = ugemm::smem_bytes<BN, STAGES>();
-  PMB_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem), name);
-  kern<<<tiles, ugemm::kThreads, smem, stream>>>(ma, mb, plan, epi, fp16);
-  PMB_CHECK_LAUNCH(name);
-  return PMB_OK;
-}
-
-template <int BN, int STAGES>
-int dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ma, const CUtensorMap& mb, ugemm::Plan& plan,
-                   const DenseEpi& epi, int fp16, cudaStream_t s, const char* name) {
-  if (!a_mn && !b_mn) return launch_dense<BN, STAGES, false, false>(ma, mb, plan, epi, fp16, s, name);
-  if (!a_mn && b_mn) return launch_dense<BN, STAGES, false, true>(ma, mb, plan, epi, fp16, s, name);
-  if (a_mn && !b_mn) return launch_dense<BN, STAGES, true, false>(ma, mb, plan, epi, fp16, s, name);
-  return launch_dense<BN, STAGES, true, true>(ma, mb, plan, epi, fp16, s, name);
-}
-
-}  // namespace
 }  // namespace pmb
 
 using namespace pmb;
@@ -149,25 +72,25 @@ extern "C" int pmb_gemm_tc(const void* a, int64_t lda, int a_mn_major, const voi
   PMB_REQUIRE(activation == PMB_ACT_NONE || activation == PMB_ACT_TANH, "%s: unknown activation", name);
   if (m == 0 || n == 0) return PMB_OK;
   PMB_REQUIRE(a && b && c, "%s: NULL tensor argument", name);
-  const int bn = n >= 128 ? 128 : 64;
-  CUtensorMap ma, mb;
-  int st;
-  if (!a_mn_major)
-    st = tma::make_map_3d(ma, a, dtype, k, 1, m, lda * 2, lda * 2, 64, 1, ugemm::BM, name);
-  else
-    st = tma::make_map_3d(ma, a, dtype, m, 1, k, lda * 2, lda * 2, 64, 1, 64, name);
-  if (st) return st;
-  if (!b_mn_major)
-    st = tma::make_map_3d(mb, b, dtype, k, 1, n, ldb * 2, ldb * 2, 64, 1, bn, name);
-  else
-    st = tma::make_map_3d(mb, b, dtype, n, 1, k, ldb * 2, ldb * 2, 64, 1, 64, name);
-  if (st) return st;
-  ugemm::Plan plan;
-  plan.num_groups = 1;
-  plan.g[0] = ugemm::Group{(int)m, (int)n, (int)k, 0, 0, 0, 0, 0, 0};
-  DenseEpi epi{c, ldc, c_dtype, bias, bias_dtype, activation};
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int fp16 = dtype == PMB_FLOAT16;
-  if (bn == 128) return dispatch_major<128, 4>(a_mn_major, b_mn_major, ma, mb, plan, epi, fp16, s, name);
-  return dispatch_major<64, 6>(a_mn_major, b_mn_major, ma, mb, plan, epi, fp16, s, name);
+  return dense::gemm(a, lda, a_mn_major != 0, b, ldb, b_mn_major != 0, c, ldc, c_dtype, bias, bias_dtype, activation,
+                     m, n, k, dtype, static_cast<cudaStream_t>(stream), name);
+}
+
+extern "C" int64_t pmb_gemm_tc_wgrad_workspace_size(int64_t m, int64_t n, int64_t k) {
+  return dense::wgrad_workspace(m, n, k);
+}
+
+extern "C" int pmb_gemm_tc_wgrad(const void* a, int64_t lda, const void* b, int64_t ldb, int64_t m, int64_t n,
+                                 int64_t k, void* c, int64_t ldc, int c_dtype, int dtype, void* workspace,
+                                 int64_t workspace_bytes, void* stream) {
+  clear_error();
+  const char* name = "pmb_gemm_tc_wgrad";
+  PMB_REQUIRE(dtype == PMB_BFLOAT16 || dtype == PMB_FLOAT16, "%s: operands must be bf16 or fp16", name);
+  PMB_REQUIRE(m >= 0 && n >= 0 && k >= 0 && m < (1ll << 31) && n < (1ll << 31) && k < (1ll << 31), "%s: bad shape",
+              name);
+  PMB_REQUIRE(dtype_size(c_dtype) > 0, "%s: unsupported output dtype %d", name, c_dtype);
+  if (m == 0 || n == 0) return PMB_OK;
+  PMB_REQUIRE(c && (k == 0 || (a && b)), "%s: NULL tensor argument", name);
+  return dense::wgrad(a, lda, b, ldb, m, n, k, c, ldc, c_dtype, dtype, workspace, workspace_bytes,
+                      static_cast<cudaStream_t>(stream), name);
 }

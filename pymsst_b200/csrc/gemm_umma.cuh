@@ -8,14 +8,26 @@
 // per 64-wide MN chunk.  Groups carry offsets into the maps, so one launch
 // covers all bands of a ragged / grouped layer.
 //
-// CTA = 128 threads.  Warp 0 lane 0 issues TMA into a STAGES-deep shared
-// memory ring (full/empty mbarriers); warp 1 lane 0 issues tcgen05.mma
-// (M = 128, N = BN, K = 16 per instruction) into a TMEM accumulator of BN
-// fp32 columns and commits stage releases; after the last k-block all four
-// warps drain the accumulator with tcgen05.ld (warp w owns rows 32w..32w+31,
-// one row per thread) and run the epilogue functor.  All waits are bounded
-// (umma.cuh); on a timeout the CTA skips the remaining work, frees its TMEM
-// and exits, leaving the site in g_umma_timeout.
+// Persistent, warp-specialised CTA of 448 threads, one per SM; CTA i takes
+// tiles i, i + grid, ... (tiles enumerated group by group, N fastest, so the
+// CTAs in flight share their A rows through L2):
+//   warp 0 (one lane)   TMA producer into a STAGES-deep shared-memory ring
+//                       (full / empty mbarriers, running across tiles);
+//   warp 1 (one lane)   tcgen05.mma issuer (M = 128, N = BN, K = 16 per
+//                       instruction) into one of two TMEM accumulators of BN
+//                       fp32 columns; commits ring-slot releases and, after a
+//                       tile's last k-block, the accumulator-full barrier;
+//   warps 2..13         epilogue: drain the accumulator with tcgen05.ld (warp
+//                       w reads TMEM lanes 32*(w%4).., one row per thread;
+//                       the kSubs = 3 warps of a lane quarter take every
+//                       third 32-column chunk), run the epilogue functor,
+//                       release the accumulator.
+// Two accumulators let the epilogue of tile i overlap the mainloop of tile
+// i+1.  Epilogues write through a per-warp shared-memory staging block so
+// global stores are 16-byte vectors along rows (warp_store below).
+//
+// All waits are bounded (umma.cuh); on a timeout the CTA stops issuing work,
+// frees its TMEM and exits, leaving the site in g_umma_timeout.
 #pragma once
 
 #include "umma.cuh"
@@ -25,11 +37,16 @@ namespace ugemm {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int kThreads = 128;
+constexpr int kSubs = 3;                 // epilogue warps per TMEM lane quarter
+constexpr int kEpiWarps = 4 * kSubs;
+constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kMaxGroups = PMB_MAX_BANDS;
+// Per-warp staging block: 32 rows x (32 fp32 + 16 bytes of padding).
+constexpr int kStageRowBytes = 32 * 4 + 16;
+constexpr int kStageWarpBytes = 32 * kStageRowBytes;
 
 struct Group {
-  int m, n, k;             // problem size of this group
+  int m, n, k;                  // problem size of this group
   int a_inner, a_mid, a_outer;  // offsets added to A's TMA coordinates
   int b_inner, b_mid, b_outer;  // offsets added to B's TMA coordinates
 };
@@ -41,13 +58,14 @@ struct Plan {
   Group g[kMaxGroups];
 };
 
-// Host: per-group tile counts for a given BN.
+// Host: per-group tile counts for a given BN (groups with an empty M, N or K
+// contribute no tiles; callers clear such outputs themselves).
 inline int build_plan(Plan& p, int bn) {
   p.total_tiles = 0;
   p.tile_start[0] = 0;
   for (int i = 0; i < p.num_groups; ++i) {
     const Group& g = p.g[i];
-    const int t = (g.m <= 0 || g.n <= 0) ? 0 : ((g.m + BM - 1) / BM) * ((g.n + bn - 1) / bn);
+    const int t = (g.m <= 0 || g.n <= 0 || g.k <= 0) ? 0 : ((g.m + BM - 1) / BM) * ((g.n + bn - 1) / bn);
     p.total_tiles += t;
     p.tile_start[i + 1] = p.total_tiles;
   }
@@ -61,24 +79,152 @@ struct Config {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr uint32_t IDESC_BF16 = umma::idesc_f16(true, A_MN, B_MN, BM, BN);
   static constexpr uint32_t IDESC_F16 = umma::idesc_f16(false, A_MN, B_MN, BM, BN);
-  static constexpr uint32_t TMEM_COLS = BN < 32 ? 32 : BN;
+  static constexpr uint32_t TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;  // two accumulators
 };
 
 template <int BN, int STAGES>
 constexpr int smem_bytes() {
-  return STAGES * (BM * BK * 2 + BN * BK * 2) + 1024 /*alignment slack*/ + 256 /*barriers*/;
+  return STAGES * (BM * BK * 2 + BN * BK * 2) + kEpiWarps * kStageWarpBytes + 1024 /*alignment slack*/ +
+         256 /*barriers*/;
 }
 
-// Per-thread view handed to epilogues: the accumulator row this thread owns.
+// Per-warp view handed to epilogues.  Each thread owns one accumulator row;
+// the warp owns 32 consecutive rows starting at row0.
 struct TileCtx {
   int group;
-  int m0, n0;       // tile origin within the group
-  int row;          // m0 + thread's row
-  bool row_valid;   // row < group m
-  int n_valid;      // columns of this tile inside the group (<= BN)
-  uint32_t taddr;   // TMEM address of this thread's row, column 0 of the tile
+  int sub;         // this warp's share of the columns: 32-column chunks c with c % kSubs == sub
+  int m0, n0;      // tile origin within the group
+  int row0;        // first row of this warp
+  int row;         // this thread's row (row0 + lane)
+  bool row_valid;  // row < group m
+  int rows_valid;  // rows of this warp inside the group (0..32)
+  int n_valid;     // columns of this tile inside the group (<= BN)
+  uint32_t taddr;  // TMEM address of this thread's row, column 0 of the tile
+  uint8_t* stage;  // this warp's staging block (kStageWarpBytes)
 };
 
+// Locate tile `tile` of the plan: group, M / N origin.
+__device__ __forceinline__ void locate(const Plan& plan, int tile, int bn, int& gi, int& m0, int& n0) {
+  int lo = 0, hi = plan.num_groups - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (plan.tile_start[mid] <= tile) lo = mid; else hi = mid - 1;
+  }
+  gi = lo;
+  const Group& G = plan.g[gi];
+  const int local = tile - plan.tile_start[gi];
+  const int ntn = (G.n + bn - 1) / bn;
+  m0 = (local / ntn) * BM;
+  n0 = (local % ntn) * bn;
+}
+
+// ------------------------------------------------------- epilogue helpers
+// Store a 32 x 32 block held one row per lane (v = this lane's 32 values):
+// dst points at the block's (row 0, column 0), rows `ld` elements apart.
+// The block is staged in shared memory and written back as 16-byte vectors
+// along rows when dst, ld allow it, else element by element (coalesced
+// along columns).  Whole warp; rows_valid / cols_valid clip the block.
+template <typename T>
+__device__ __forceinline__ void warp_store(uint8_t* stage, const float (&v)[32], T* dst, int64_t ld,
+                                           int rows_valid, int cols_valid) {
+  const int lane = threadIdx.x & 31;
+  T* srow = reinterpret_cast<T*>(stage + lane * kStageRowBytes);
+  {
+    T pack[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) pack[j] = Elem<T>::from_f(v[j]);
+#pragma unroll
+    for (int q = 0; q < 32 * (int)sizeof(T) / 16; ++q)
+      reinterpret_cast<uint4*>(srow)[q] = reinterpret_cast<const uint4*>(pack)[q];
+  }
+  __syncwarp();
+  const bool vec = cols_valid == 32 &&
+                   ((reinterpret_cast<uintptr_t>(dst) | (uintptr_t)(ld * (int64_t)sizeof(T))) & 15) == 0;
+  if (vec) {
+    constexpr int CPR = 32 * sizeof(T) / 16;  // 16-byte chunks per row
+#pragma unroll
+    for (int i = lane; i < 32 * CPR; i += 32) {
+      const int r = i / CPR, q = i % CPR;
+      if (r < rows_valid)
+        reinterpret_cast<uint4*>(dst + (int64_t)r * ld)[q] =
+            *reinterpret_cast<const uint4*>(stage + r * kStageRowBytes + q * 16);
+    }
+  } else {
+#pragma unroll 4
+    for (int r = 0; r < rows_valid; ++r)
+      if (lane < cols_valid)
+        dst[(int64_t)r * ld + lane] = reinterpret_cast<const T*>(stage + r * kStageRowBytes)[lane];
+  }
+  __syncwarp();
+}
+
+// Same, with an arbitrary destination per row: each lane passes the address
+// of its own row's first column (nullptr = row skipped).
+template <typename T>
+__device__ __forceinline__ void warp_store_rows(uint8_t* stage, const float (&v)[32], T* my_row, int cols_valid) {
+  const int lane = threadIdx.x & 31;
+  T* srow = reinterpret_cast<T*>(stage + lane * kStageRowBytes);
+  {
+    T pack[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) pack[j] = Elem<T>::from_f(v[j]);
+#pragma unroll
+    for (int q = 0; q < 32 * (int)sizeof(T) / 16; ++q)
+      reinterpret_cast<uint4*>(srow)[q] = reinterpret_cast<const uint4*>(pack)[q];
+  }
+  __syncwarp();
+  const bool vec = __all_sync(0xffffffffu, (reinterpret_cast<uintptr_t>(my_row) & 15) == 0) && cols_valid == 32;
+  const unsigned long long mine = reinterpret_cast<unsigned long long>(my_row);
+  if (vec) {
+    constexpr int CPR = 32 * sizeof(T) / 16;
+#pragma unroll
+    for (int i = lane; i < 32 * CPR; i += 32) {
+      const int r = i / CPR, q = i % CPR;
+      T* row = reinterpret_cast<T*>(__shfl_sync(0xffffffffu, mine, r));
+      if (row != nullptr)
+        reinterpret_cast<uint4*>(row)[q] = *reinterpret_cast<const uint4*>(stage + r * kStageRowBytes + q * 16);
+    }
+  } else {
+#pragma unroll 4
+    for (int r = 0; r < 32; ++r) {
+      T* row = reinterpret_cast<T*>(__shfl_sync(0xffffffffu, mine, r));
+      if (row != nullptr && lane < cols_valid) row[lane] = reinterpret_cast<const T*>(stage + r * kStageRowBytes)[lane];
+    }
+  }
+  __syncwarp();
+}
+
+// Load a 32 x 32 block (same addressing as warp_store) and return this lane's
+// row as floats; positions outside the clip read 0.
+template <typename T>
+__device__ __forceinline__ void warp_load(uint8_t* stage, const T* src, int64_t ld, int rows_valid, int cols_valid,
+                                          float (&v)[32]) {
+  const int lane = threadIdx.x & 31;
+  const bool vec = cols_valid == 32 &&
+                   ((reinterpret_cast<uintptr_t>(src) | (uintptr_t)(ld * (int64_t)sizeof(T))) & 15) == 0;
+  if (vec) {
+    constexpr int CPR = 32 * sizeof(T) / 16;
+#pragma unroll
+    for (int i = lane; i < 32 * CPR; i += 32) {
+      const int r = i / CPR, q = i % CPR;
+      uint4 u = make_uint4(0, 0, 0, 0);
+      if (r < rows_valid) u = reinterpret_cast<const uint4*>(src + (int64_t)r * ld)[q];
+      *reinterpret_cast<uint4*>(stage + r * kStageRowBytes + q * 16) = u;
+    }
+  } else {
+#pragma unroll 4
+    for (int r = 0; r < 32; ++r)
+      reinterpret_cast<T*>(stage + r * kStageRowBytes)[lane] =
+          (r < rows_valid && lane < cols_valid) ? src[(int64_t)r * ld + lane] : Elem<T>::from_f(0.f);
+  }
+  __syncwarp();
+  const T* srow = reinterpret_cast<const T*>(stage + lane * kStageRowBytes);
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = Elem<T>::to_f(srow[j]);
+  __syncwarp();
+}
+
+// ------------------------------------------------------------------ kernel
 template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi>
 __global__ void __launch_bounds__(kThreads, 1)
     umma_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -86,130 +232,176 @@ __global__ void __launch_bounds__(kThreads, 1)
   using C = Config<BN, A_MN, B_MN>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES);
+  uint8_t* staging = smem + STAGES * C::STAGE_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(staging + kEpiWarps * kStageWarpBytes);
   uint64_t* empty = full + STAGES;
-  uint64_t* accum = empty + STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
-  __shared__ int abort_flag;
+  uint64_t* tfull = empty + STAGES;  // [2] accumulator ready (MMA -> epilogue)
+  uint64_t* tempty = tfull + 2;      // [2] accumulator drained (epilogue -> MMA)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  __shared__ volatile int abort_flag;
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-
-  // ---- locate this CTA's tile
-  const int tile = blockIdx.x;
-  int lo = 0, hi = plan.num_groups - 1;
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (plan.tile_start[mid] <= tile) lo = mid; else hi = mid - 1;
-  }
-  const int gi = lo;
-  const Group& G = plan.g[gi];
-  const int local = tile - plan.tile_start[gi];
-  const int ntn = (G.n + BN - 1) / BN;
-  const int m0 = (local / ntn) * BM;
-  const int n0 = (local % ntn) * BN;
-  const int kblocks = (G.k + BK - 1) / BK;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       umma::mbar_init(&full[s], 1);
       umma::mbar_init(&empty[s], 1);
     }
-    umma::mbar_init(accum, 1);
+    for (int b = 0; b < 2; ++b) {
+      umma::mbar_init(&tfull[b], 1);
+      umma::mbar_init(&tempty[b], kEpiWarps);
+    }
     umma::fence_barrier_init();
     abort_flag = 0;
     umma::tma_prefetch(&tmA);
     umma::tma_prefetch(&tmB);
   }
-  if (warp == 0) umma::tmem_alloc(tmem_slot, C::TMEM_COLS);
+  if (warp == 1) umma::tmem_alloc(tmem_slot, C::TMEM_COLS);
   umma::tc_fence_before();
   __syncthreads();
   umma::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0 && lane == 0) {
-    // ---------------- TMA producer
-    for (int kb = 0; kb < kblocks; ++kb) {
-      const int s = kb % STAGES;
-      const uint32_t round = kb / STAGES;
-      if (!umma::mbar_wait(&empty[s], (round & 1) ^ 1, 1)) {
-        atomicExch(&abort_flag, 1);
-        break;
-      }
-      uint8_t* a_dst = smem + s * C::STAGE_BYTES;
-      uint8_t* b_dst = a_dst + C::A_BYTES;
-      umma::mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
-      const int k0 = kb * BK;
-      if (!A_MN) {
-        umma::tma_load_3d(a_dst, &tmA, &full[s], k0 + G.a_inner, G.a_mid, m0 + G.a_outer);
-      } else {
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer
+      uint32_t it = 0;
+      for (int tile = blockIdx.x; tile < plan.total_tiles && !abort_flag; tile += gridDim.x) {
+        int gi, m0, n0;
+        locate(plan, tile, BN, gi, m0, n0);
+        const Group& G = plan.g[gi];
+        const int kblocks = (G.k + BK - 1) / BK;
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t round = it / STAGES;
+          if (!umma::mbar_wait(&empty[s], (round & 1) ^ 1, 1)) {
+            abort_flag = 1;
+            break;
+          }
+          uint8_t* a_dst = smem + s * C::STAGE_BYTES;
+          uint8_t* b_dst = a_dst + C::A_BYTES;
+          umma::mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
+          const int k0 = kb * BK;
+          if (!A_MN) {
+            umma::tma_load_3d(a_dst, &tmA, &full[s], k0 + G.a_inner, G.a_mid, m0 + G.a_outer);
+          } else {
 #pragma unroll
-        for (int c = 0; c < BM / 64; ++c)
-          umma::tma_load_3d(a_dst + c * 64 * BK * 2, &tmA, &full[s], m0 + c * 64 + G.a_inner, G.a_mid,
-                            k0 + G.a_outer);
-      }
-      if (!B_MN) {
-        umma::tma_load_3d(b_dst, &tmB, &full[s], k0 + G.b_inner, G.b_mid, n0 + G.b_outer);
-      } else {
+            for (int c = 0; c < BM / 64; ++c)
+              umma::tma_load_3d(a_dst + c * 64 * BK * 2, &tmA, &full[s], m0 + c * 64 + G.a_inner, G.a_mid,
+                                k0 + G.a_outer);
+          }
+          if (!B_MN) {
+            umma::tma_load_3d(b_dst, &tmB, &full[s], k0 + G.b_inner, G.b_mid, n0 + G.b_outer);
+          } else {
 #pragma unroll
-        for (int c = 0; c < BN / 64; ++c)
-          umma::tma_load_3d(b_dst + c * 64 * BK * 2, &tmB, &full[s], n0 + c * 64 + G.b_inner, G.b_mid,
-                            k0 + G.b_outer);
+            for (int c = 0; c < BN / 64; ++c)
+              umma::tma_load_3d(b_dst + c * 64 * BK * 2, &tmB, &full[s], n0 + c * 64 + G.b_inner, G.b_mid,
+                                k0 + G.b_outer);
+          }
+        }
       }
     }
-  } else if (warp == 1 && lane == 0) {
-    // ---------------- MMA issuer
-    const uint32_t idesc = fp16 ? C::IDESC_F16 : C::IDESC_BF16;
-    bool ok = true;
-    for (int kb = 0; kb < kblocks; ++kb) {
-      const int s = kb % STAGES;
-      const uint32_t round = kb / STAGES;
-      if (!umma::mbar_wait(&full[s], round & 1, 2)) {
-        atomicExch(&abort_flag, 1);
-        ok = false;
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer
+      const uint32_t idesc = fp16 ? C::IDESC_F16 : C::IDESC_BF16;
+      uint32_t it = 0, local = 0;
+      for (int tile = blockIdx.x; tile < plan.total_tiles && !abort_flag; tile += gridDim.x, ++local) {
+        int gi, m0, n0;
+        locate(plan, tile, BN, gi, m0, n0);
+        const int kblocks = (plan.g[gi].k + BK - 1) / BK;
+        const uint32_t buf = local & 1, use = local >> 1;
+        if (!umma::mbar_wait(&tempty[buf], (use & 1) ^ 1, 4)) {
+          abort_flag = 1;
+          break;
+        }
+        umma::tc_fence_after();
+        const uint32_t acc = tmem + buf * BN;
+        bool ok = true;
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t round = it / STAGES;
+          if (!umma::mbar_wait(&full[s], round & 1, 2)) {
+            abort_flag = 1;
+            ok = false;
+            break;
+          }
+          umma::tc_fence_after();
+          const uint32_t a_base = umma::smem_u32(smem + s * C::STAGE_BYTES);
+          const uint32_t b_base = a_base + C::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            uint64_t da, db;
+            if (!A_MN)
+              da = umma::smem_desc_sw128(a_base + kk * 32, 16, 1024);
+            else
+              da = umma::smem_desc_sw128(a_base + kk * 16 * 128, 64 * BK * 2, 1024);
+            if (!B_MN)
+              db = umma::smem_desc_sw128(b_base + kk * 32, 16, 1024);
+            else
+              db = umma::smem_desc_sw128(b_base + kk * 16 * 128, 64 * BK * 2, 1024);
+            umma::mma_f16(acc, da, db, idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          umma::mma_commit(&empty[s]);
+        }
+        if (ok)
+          umma::mma_commit(&tfull[buf]);
+        else
+          umma::mbar_arrive(&tfull[buf]);  // release the epilogue; it sees the abort flag
+        if (!ok) break;
+      }
+    }
+  } else {
+    // ---------------- epilogue warps
+    const int quarter = warp & 3;
+    const int sub = (warp - 2) / 4;
+    uint8_t* stage = staging + (warp - 2) * kStageWarpBytes;
+    uint32_t local = 0;
+    for (int tile = blockIdx.x; tile < plan.total_tiles; tile += gridDim.x, ++local) {
+      if (abort_flag) break;
+      int gi, m0, n0;
+      locate(plan, tile, BN, gi, m0, n0);
+      const Group& G = plan.g[gi];
+      const uint32_t buf = local & 1, use = local >> 1;
+      if (!umma::mbar_wait(&tfull[buf], use & 1, 3)) {
+        abort_flag = 1;
         break;
       }
       umma::tc_fence_after();
-      const uint32_t a_base = umma::smem_u32(smem + s * C::STAGE_BYTES);
-      const uint32_t b_base = a_base + C::A_BYTES;
-#pragma unroll
-      for (int kk = 0; kk < BK / 16; ++kk) {
-        uint64_t da, db;
-        if (!A_MN)
-          da = umma::smem_desc_sw128(a_base + kk * 32, 16, 1024);
-        else
-          da = umma::smem_desc_sw128(a_base + kk * 16 * 128, 64 * BK * 2, 1024);
-        if (!B_MN)
-          db = umma::smem_desc_sw128(b_base + kk * 32, 16, 1024);
-        else
-          db = umma::smem_desc_sw128(b_base + kk * 16 * 128, 64 * BK * 2, 1024);
-        umma::mma_f16(tmem, da, db, idesc, (kb | kk) != 0 ? 1u : 0u);
+      __syncwarp();
+      if (!abort_flag) {
+        TileCtx t;
+        t.group = gi;
+        t.sub = sub;
+        t.m0 = m0;
+        t.n0 = n0;
+        t.row0 = m0 + quarter * 32;
+        t.row = t.row0 + lane;
+        t.row_valid = t.row < G.m;
+        t.rows_valid = max(0, min(32, G.m - t.row0));
+        t.n_valid = min(BN, G.n - n0);
+        t.taddr = tmem + buf * BN + ((uint32_t)(quarter * 32) << 16);
+        t.stage = stage;
+        epi.template run<BN>(plan, t);
       }
-      umma::mma_commit(&empty[s]);
+      umma::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) umma::mbar_arrive(&tempty[buf]);
     }
-    if (ok) umma::mma_commit(accum);
-    else umma::mbar_arrive(accum);  // release the epilogue; results are discarded
   }
   __syncwarp();
-
-  // ---------------- epilogue (all 4 warps)
-  const bool done = umma::mbar_wait(accum, 0, 3);
-  umma::tc_fence_after();
-  if (!done) atomicExch(&abort_flag, 1);
-  __syncthreads();
-  if (!abort_flag && kblocks > 0) {
-    TileCtx t;
-    t.group = gi;
-    t.m0 = m0;
-    t.n0 = n0;
-    t.row = m0 + warp * 32 + lane;
-    t.row_valid = t.row < G.m;
-    t.n_valid = min(BN, G.n - n0);
-    t.taddr = tmem + ((uint32_t)(warp * 32) << 16);
-    epi.template run<BN>(plan, t);
-  }
   umma::tc_fence_before();
   __syncthreads();
-  if (warp == 0) umma::tmem_dealloc(tmem, C::TMEM_COLS);
+  if (warp == 1) {
+    umma::tc_fence_after();
+    umma::tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+// Host: persistent grid for a plan (one CTA per SM at most).
+inline int persistent_grid(int tiles) {
+  const int sms = num_sms();
+  return tiles < sms ? tiles : sms;
 }
 
 }  // namespace ugemm

@@ -97,28 +97,22 @@ struct TanhEpi {
   T* out;
   int64_t ld;  // nb * H
   int h;
-  const BandInfo* info_unused;
   const void* bias[kMaxBands];
   template <int BNT>
   __device__ void run(const ugemm::Plan&, const ugemm::TileCtx& t) const {
-    T* o = out + (int64_t)t.row * ld + (int64_t)t.group * h + t.n0;
+    T* o = out + (int64_t)t.row0 * ld + (int64_t)t.group * h + t.n0;
     const TP* bp = static_cast<const TP*>(bias[t.group]) + t.n0;
+    const int lane = threadIdx.x & 31;
 #pragma unroll 1
-    for (int c0 = 0; c0 < BNT; c0 += 32) {
+    for (int c0 = 32 * t.sub; c0 < BNT; c0 += 32 * ugemm::kSubs) {
+      if (c0 >= t.n_valid) break;
+      const int ncols = min(32, t.n_valid - c0);
       float v[32];
       umma::tmem_ld32(t.taddr + c0, v);
-      if (!t.row_valid) continue;
-      if (c0 + 32 <= t.n_valid) {
-        T pack[32];
+      const float bl = lane < ncols ? Elem<TP>::to_f(bp[c0 + lane]) : 0.f;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) pack[j] = Elem<T>::from_f(tanhf(v[j] + Elem<TP>::to_f(bp[c0 + j])));
-        uint4* dst = reinterpret_cast<uint4*>(o + c0);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) dst[q] = reinterpret_cast<const uint4*>(pack)[q];
-      } else {
-        for (int j = 0; j < 32 && c0 + j < t.n_valid; ++j)
-          o[c0 + j] = Elem<T>::from_f(tanhf(v[j] + Elem<TP>::to_f(bp[c0 + j])));
-      }
+      for (int j = 0; j < 32; ++j) v[j] = tanhf(v[j] + __shfl_sync(0xffffffffu, bl, j));
+      ugemm::warp_store<T>(t.stage, v, o + c0, ld, t.rows_valid, ncols);
     }
   }
 };
@@ -137,25 +131,29 @@ struct GluEpi {
     const int c = t.n0 / 128;
     const int cw = min(kChunk, w - c * kChunk);
     const TP* bias = static_cast<const TP*>(info.bias[b]);
-    T* o = out + (int64_t)t.row * ld_out + info.off[b] + c * kChunk;
-    T* p = pre + (int64_t)t.row * ld_pre + info.pbase[b] + c * 128;
-#pragma unroll 1
-    for (int h = 0; h < 2; ++h) {  // two 32-wide halves of the 64-output chunk
+    T* o = out + (int64_t)t.row0 * ld_out + info.off[b] + c * kChunk;
+    T* p = pre + (int64_t)t.row0 * ld_pre + info.pbase[b] + c * 128;
+    const int lane = threadIdx.x & 31;
+    {  // this warp's 32-wide half h of the 64-output chunk
+      const int h = t.sub;  // GLU pairs columns h*32.. with 64 + h*32..: two warps of a lane quarter
+      if (h >= 2 || h * 32 >= cw) return;
+      const int ncols = min(32, cw - h * 32);
       float left[32], gate[32];
       umma::tmem_ld32(t.taddr + h * 32, left);
       umma::tmem_ld32(t.taddr + kChunk + h * 32, gate);
-      if (!t.row_valid) continue;
+      const int l0 = c * kChunk + h * 32;
+      const float bl = lane < ncols ? Elem<TP>::to_f(bias[l0 + lane]) : 0.f;
+      const float bg = lane < ncols ? Elem<TP>::to_f(bias[w + l0 + lane]) : 0.f;
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
-        const int jj = h * 32 + j;
-        if (jj >= cw) break;
-        const int l = c * kChunk + jj;
-        const float a = left[j] + Elem<TP>::to_f(bias[l]);
-        const float g = gate[j] + Elem<TP>::to_f(bias[w + l]);
-        p[jj] = Elem<T>::from_f(a);
-        p[kChunk + jj] = Elem<T>::from_f(g);
-        o[jj] = Elem<T>::from_f(a * sigm(g));
+        left[j] += __shfl_sync(0xffffffffu, bl, j);
+        gate[j] += __shfl_sync(0xffffffffu, bg, j);
       }
+      ugemm::warp_store<T>(t.stage, left, p + h * 32, ld_pre, t.rows_valid, ncols);
+      ugemm::warp_store<T>(t.stage, gate, p + kChunk + h * 32, ld_pre, t.rows_valid, ncols);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) left[j] *= sigm(gate[j]);
+      ugemm::warp_store<T>(t.stage, left, o + h * 32, ld_out, t.rows_valid, ncols);
     }
   }
 };
@@ -170,27 +168,28 @@ struct DActEpi {
   int h;
   template <int BNT>
   __device__ void run(const ugemm::Plan&, const ugemm::TileCtx& t) const {
-    const int64_t base = (int64_t)t.row * ld + (int64_t)t.group * h + t.n0;
+    const int64_t base = (int64_t)t.row0 * ld + (int64_t)t.group * h + t.n0;
 #pragma unroll 1
-    for (int c0 = 0; c0 < BNT; c0 += 32) {
+    for (int c0 = 32 * t.sub; c0 < BNT; c0 += 32 * ugemm::kSubs) {
+      if (c0 >= t.n_valid) break;
+      const int ncols = min(32, t.n_valid - c0);
       float v[32];
       umma::tmem_ld32(t.taddr + c0, v);
-      if (!t.row_valid) continue;
-      for (int j = 0; j < 32 && c0 + j < t.n_valid; ++j) {
-        float g = v[j];
-        if (y != nullptr) {
-          const float yy = Elem<T>::to_f(y[base + c0 + j]);
-          g *= 1.0f - yy * yy;
-        }
-        dst[base + c0 + j] = Elem<T>::from_f(g);
+      if (y != nullptr) {
+        float yv[32];
+        ugemm::warp_load<T>(t.stage, y + base + c0, ld, t.rows_valid, ncols, yv);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] *= 1.0f - yv[j] * yv[j];
       }
+      ugemm::warp_store<T>(t.stage, v, dst + base + c0, ld, t.rows_valid, ncols);
     }
   }
 };
 
 // Weight-gradient epilogue into per-band fp32/param-dtype tensors.
 // mode 0: grouped (row m of group b -> grad_b[m, n]); mode 1: packed GLU rows
-// (m = 128c + j -> left/gate source row, skipped past w_b).
+// (m = 128c + j -> left/gate source row, skipped past w_b).  A warp's 32 rows
+// map to 32 consecutive source rows in both modes.
 template <typename TP>
 struct WGradEpi {
   int mode;
@@ -199,20 +198,21 @@ struct WGradEpi {
   template <int BNT>
   __device__ void run(const ugemm::Plan&, const ugemm::TileCtx& t) const {
     const int b = t.group;
-    int srow = t.row;
+    int srow0 = t.row0, nrows = t.rows_valid;
     if (mode == 1) {
-      const int c = t.row / 128, j = t.row % 128;
-      const int l = c * kChunk + (j % kChunk);
-      srow = l < info.w[b] ? (j < kChunk ? l : info.w[b] + l) : -1;
+      const int c = t.row0 / 128, j0 = t.row0 % 128;
+      const int l0 = c * kChunk + (j0 % kChunk);
+      srow0 = j0 < kChunk ? l0 : info.w[b] + l0;
+      nrows = max(0, min(nrows, info.w[b] - l0));
     }
-    TP* g = static_cast<TP*>(info.grad[b]);
+    if (nrows == 0) return;
+    TP* g = static_cast<TP*>(info.grad[b]) + (int64_t)srow0 * cols + t.n0;
 #pragma unroll 1
-    for (int c0 = 0; c0 < BNT; c0 += 32) {
+    for (int c0 = 32 * t.sub; c0 < BNT; c0 += 32 * ugemm::kSubs) {
+      if (c0 >= t.n_valid) break;
       float v[32];
       umma::tmem_ld32(t.taddr + c0, v);
-      if (!t.row_valid || srow < 0) continue;
-      for (int j = 0; j < 32 && c0 + j < t.n_valid; ++j)
-        g[(int64_t)srow * cols + t.n0 + c0 + j] = Elem<TP>::from_f(v[j]);
+      ugemm::warp_store<TP>(t.stage, v, g + c0, cols, nrows, min(32, t.n_valid - c0));
     }
   }
 };
@@ -344,7 +344,7 @@ int run_gemm(const CUtensorMap& ma, const CUtensorMap& mb, ugemm::Plan& plan, co
   auto kern = ugemm::umma_gemm_kernel<BN, STAGES, A_MN, B_MN, Epi>;
   const int smem = ugemm::smem_bytes<BN, STAGES>();
   PMB_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem), name);
-  kern<<<tiles, ugemm::kThreads, smem, s>>>(ma, mb, plan, epi, fp16);
+  kern<<<ugemm::persistent_grid(tiles), ugemm::kThreads, smem, s>>>(ma, mb, plan, epi, fp16);
   PMB_CHECK_LAUNCH(name);
   return PMB_OK;
 }
@@ -391,7 +391,6 @@ int forward_impl(const void* x, const Layout& y, const void* const* weights, con
       epi.out = static_cast<T*>(acts) + (int64_t)l * y.rows * y.nb * y.hidden;
       epi.ld = (int64_t)y.nb * y.hidden;
       epi.h = (int)y.hidden;
-      epi.info_unused = nullptr;
       for (int b = 0; b < y.nb; ++b) epi.bias[b] = biases[(int64_t)l * y.nb + b];
       st = run_gemm<TanhEpi<T, TP>, false, false>(ma, mb, plan, epi, fp16, s, name);
       if (st) return st;

@@ -1,0 +1,99 @@
+// Attention input projection with the rotary embedding in the GEMM epilogue
+// (training path, bf16 / fp16 on the tcgen05 tensor cores).
+//
+//   [q | k | v][r, :] = x[r, :] W^T,  each written as a [B*N, H*Dh] row-major
+//   plane (the [B, N, H, Dh] layout; q, k, v are its [B, H, N, Dh] views, which
+//   the attention kernel reads in place).
+// The epilogue rounds each q / k projection value to the activation dtype (as
+// the stored projection of the unfused path) and rotates the interleaved pairs
+// by the row's position angle; the angle tables are passed transposed
+// ([Dh/2, N]) so the 32 rows of a warp read 32 consecutive positions of one
+// pair (coalesced) instead of 32 scattered table rows.  Stores are 16-byte
+// row vectors.  The projection is written once and never re-read for a split
+// or rotary pass; the backward is pmb_qkv_rotary_merge plus the two
+// projection-gradient GEMMs.
+// Reference semantics: to_qkv projection + qkv_to_bnhd + rotary_forward on
+// q and k (src/pymsst/training/fused_roformer.py:710-732, 793-818;
+// rotary kernels src/pymsst/training/cuda/fused_band_split.cu:1077-1128).
+#include "dense_gemm.cuh"
+
+namespace pmb {
+unsigned int timeout_flag_qkv(int reset) { return umma::flag_reader(reset); }
+
+namespace {
+
+template <typename T>
+struct QkvRotaryEpi {
+  T* plane[3];       // q, k, v: [rows, H*Dh]
+  const float* cos_t;  // [Dh/2, seq]
+  const float* sin_t;
+  int hd, seq, dh, rotate;
+  template <int BN>
+  __device__ void run(const ugemm::Plan&, const ugemm::TileCtx& t) const {
+    // rows past the end still map to a position in [0, seq): table reads stay in bounds
+    const int pos = t.row % seq;
+#pragma unroll 1
+    for (int c0 = 32 * t.sub; c0 < BN; c0 += 32 * ugemm::kSubs) {
+      if (c0 >= t.n_valid) break;
+      const int ncols = min(32, t.n_valid - c0);
+      float v[32];
+      umma::tmem_ld32(t.taddr + c0, v);
+      const int n = t.n0 + c0;
+      const int which = n / hd, col = n - which * hd;
+      if (rotate && which < 2) {
+        const int p0 = (col % dh) / 2;
+        const float* cp = cos_t + (int64_t)p0 * seq + pos;
+        const float* sp = sin_t + (int64_t)p0 * seq + pos;
+#pragma unroll
+        for (int u = 0; u < 16; ++u) {
+          const float c = cp[(int64_t)u * seq], sn = sp[(int64_t)u * seq];
+          const float e = round_to<T>(v[2 * u]), o = round_to<T>(v[2 * u + 1]);
+          v[2 * u] = e * c - o * sn;
+          v[2 * u + 1] = o * c + e * sn;
+        }
+      }
+      T* dst = (which == 0 ? plane[0] : (which == 1 ? plane[1] : plane[2])) + (int64_t)t.row0 * hd + col;
+      ugemm::warp_store<T>(t.stage, v, dst, hd, t.rows_valid, ncols);
+    }
+  }
+};
+
+}  // namespace
+}  // namespace pmb
+
+using namespace pmb;
+
+extern "C" int pmb_qkv_linear_rotary_forward(const void* x, const void* weight, const float* cos_t,
+                                             const float* sin_t, int64_t batch, int64_t seq_len, int64_t dim,
+                                             int64_t heads, int64_t dim_head, void* q, void* k, void* v,
+                                             int rotate_qk, int dtype, void* stream) {
+  clear_error();
+  const char* name = "pmb_qkv_linear_rotary_forward";
+  PMB_REQUIRE(dtype == PMB_BFLOAT16 || dtype == PMB_FLOAT16, "%s: activations must be bf16 or fp16", name);
+  PMB_REQUIRE(batch >= 0 && seq_len >= 0 && dim > 0 && heads > 0 && dim_head > 0, "%s: bad shape", name);
+  PMB_REQUIRE(dim_head % 32 == 0, "%s: dim_head must be a multiple of 32", name);
+  PMB_REQUIRE(dim % 8 == 0, "%s: dim must be a multiple of 8", name);
+  const int64_t rows = batch * seq_len;
+  if (rows == 0) return PMB_OK;
+  PMB_REQUIRE(rows < (1ll << 31) && 3 * heads * dim_head < (1ll << 31), "%s: too large", name);
+  PMB_REQUIRE(x && weight && q && k && v && (!rotate_qk || (cos_t && sin_t)), "%s: NULL tensor argument", name);
+  const int64_t n = 3 * heads * dim_head;
+  const int bn = dense::pick_bn(n);
+  CUtensorMap ma, mb;
+  int st = dense::make_maps(ma, mb, x, dim, false, weight, dim, false, rows, n, dim, bn, dtype, name);
+  if (st) return st;
+  ugemm::Plan plan;
+  plan.num_groups = 1;
+  plan.g[0] = ugemm::Group{(int)rows, (int)n, (int)dim, 0, 0, 0, 0, 0, 0};
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int fp16 = dtype == PMB_FLOAT16;
+  auto run = [&](auto tag) {
+    using T = decltype(tag);
+    QkvRotaryEpi<T> epi{{static_cast<T*>(q), static_cast<T*>(k), static_cast<T*>(v)}, cos_t, sin_t,
+                        (int)(heads * dim_head), (int)seq_len, (int)dim_head, rotate_qk};
+    if (bn == 256) return dense::launch<256, false, false>(ma, mb, plan, epi, fp16, s, name);
+    if (bn == 128) return dense::launch<128, false, false>(ma, mb, plan, epi, fp16, s, name);
+    return dense::launch<64, false, false>(ma, mb, plan, epi, fp16, s, name);
+  };
+  return fp16 ? run(__half()) : run(__nv_bfloat16());
+}

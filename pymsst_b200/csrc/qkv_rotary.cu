@@ -24,6 +24,7 @@ struct alignas((sizeof(T) * 2 * P) < 16 ? (sizeof(T) * 2 * P) : 16) Chunk {
 struct QkvDims {
   int64_t B, N;
   int H, Dh;
+  int64_t s_b, s_h, s_n;  // element strides of q / k / v (d contiguous)
 };
 
 template <typename T, int P, bool BACKWARD>
@@ -42,7 +43,7 @@ __global__ void __launch_bounds__(kThreads)
     const int64_t b = row / d.N, n = row % d.N;
     T* packed = qkv + ((row * 3 + which) * d.H + h) * d.Dh + grp * 2 * P;
     T* base = which == 0 ? q : (which == 1 ? k : v);
-    T* split = base + ((b * d.H + h) * d.N + n) * d.Dh + grp * 2 * P;
+    T* split = base + b * d.s_b + h * d.s_h + n * d.s_n + grp * 2 * P;
     const Chunk<T, P> in = *reinterpret_cast<const Chunk<T, P>*>(BACKWARD ? split : packed);
     Chunk<T, P> out;
     if (which < 2 && rotate_qk) {
@@ -67,7 +68,8 @@ int launch(void* qkv, const float* cosv, const float* sinv, QkvDims d, void* q, 
   const uintptr_t al = reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(q) |
                        reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v);
   constexpr int P = sizeof(T) == 2 ? 4 : 2;  // 16-byte chunks
-  const bool vec = (d.Dh % (2 * P)) == 0 && (al % 16) == 0;
+  const bool vec = (d.Dh % (2 * P)) == 0 && (al % 16) == 0 && d.s_b % (2 * P) == 0 && d.s_h % (2 * P) == 0 &&
+                   d.s_n % (2 * P) == 0;
   const int64_t pairs_per_row = 3LL * d.H * (d.Dh / 2);
   const int64_t cap = (int64_t)num_sms() * 32;
   auto grid_for = [&](int64_t units) {
@@ -102,7 +104,7 @@ extern "C" int pmb_qkv_rotary_split(const void* qkv, const float* cos, const flo
               "%s: bad shape (dim_head must be even)", name);
   if (batch * seq_len == 0) return PMB_OK;
   PMB_REQUIRE(qkv && q && k && v && (!rotate_qk || (cos && sin)), "%s: NULL tensor argument", name);
-  QkvDims d{batch, seq_len, (int)heads, (int)dim_head};
+  QkvDims d{batch, seq_len, (int)heads, (int)dim_head, heads * seq_len * dim_head, seq_len * dim_head, dim_head};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return PMB_DISPATCH(dtype, T, name, [&] {
     return launch<T, false>(const_cast<void*>(qkv), cos, sin, d, q, k, v, rotate_qk, s, name);
@@ -111,7 +113,8 @@ extern "C" int pmb_qkv_rotary_split(const void* qkv, const float* cos, const flo
 
 extern "C" int pmb_qkv_rotary_merge(const void* grad_q, const void* grad_k, const void* grad_v, const float* cos,
                                     const float* sin, int64_t batch, int64_t seq_len, int64_t heads,
-                                    int64_t dim_head, void* grad_qkv, int rotate_qk, int dtype, void* stream) {
+                                    int64_t dim_head, void* grad_qkv, int rotate_qk, int dtype, int64_t stride_batch,
+                                    int64_t stride_head, int64_t stride_seq, void* stream) {
   clear_error();
   const char* name = "pmb_qkv_rotary_merge";
   PMB_REQUIRE(batch >= 0 && seq_len >= 0 && heads > 0 && dim_head > 0 && dim_head % 2 == 0,
@@ -119,7 +122,8 @@ extern "C" int pmb_qkv_rotary_merge(const void* grad_q, const void* grad_k, cons
   if (batch * seq_len == 0) return PMB_OK;
   PMB_REQUIRE(grad_q && grad_k && grad_v && grad_qkv && (!rotate_qk || (cos && sin)), "%s: NULL tensor argument",
               name);
-  QkvDims d{batch, seq_len, (int)heads, (int)dim_head};
+  PMB_REQUIRE(stride_batch >= 0 && stride_head >= 0 && stride_seq >= 0, "%s: bad strides", name);
+  QkvDims d{batch, seq_len, (int)heads, (int)dim_head, stride_batch, stride_head, stride_seq};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return PMB_DISPATCH(dtype, T, name, [&] {
     return launch<T, true>(grad_qkv, cos, sin, d, const_cast<void*>(grad_q), const_cast<void*>(grad_k),

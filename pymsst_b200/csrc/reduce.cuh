@@ -66,24 +66,34 @@ __global__ void __launch_bounds__(kThreads)
 }
 
 // Column sums of a [nrows, cols] fp32 partial matrix with many rows: each CTA
-// covers 32 columns; its 8 warps stride over the rows (coalesced 128-byte
-// row segments) and the per-warp sums are combined in shared memory.
-// Launch: grid ceil(cols / 32), 256 threads.  out[c] stored as out_code.
+// covers 8 columns with 32 row lanes (a warp reads 4 rows x 32 bytes per
+// load, four loads in flight per thread); the row lanes are combined in
+// shared memory in a fixed order.  Launch: grid ceil(cols / 8), 256 threads.
+// out[c] stored as out_code.
+inline int colsum_rows_grid(int64_t cols) { return (int)((cols + 7) / 8); }
+
 __global__ void __launch_bounds__(kThreads)
     colsum_rows(const float* __restrict__ partial, int nrows, int64_t cols, void* __restrict__ out, int out_code) {
-  __shared__ float red_s[8][33];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int64_t c = (int64_t)blockIdx.x * 32 + lane;
+  __shared__ float red_s[32][9];
+  const int cl = threadIdx.x & 7, rl = threadIdx.x >> 3;
+  const int64_t c = (int64_t)blockIdx.x * 8 + cl;
   float s = 0.f;
-  if (c < cols)
-    for (int r = warp; r < nrows; r += 8) s += partial[(int64_t)r * cols + c];
-  red_s[warp][lane] = s;
+  if (c < cols) {
+    int r = rl;
+    for (; r + 96 < nrows; r += 128) {
+      const float a = partial[(int64_t)r * cols + c], b = partial[(int64_t)(r + 32) * cols + c];
+      const float d = partial[(int64_t)(r + 64) * cols + c], e = partial[(int64_t)(r + 96) * cols + c];
+      s += (a + b) + (d + e);
+    }
+    for (; r < nrows; r += 32) s += partial[(int64_t)r * cols + c];
+  }
+  red_s[rl][cl] = s;
   __syncthreads();
-  if (warp == 0 && c < cols) {
+  if (threadIdx.x < 8 && (int64_t)blockIdx.x * 8 + threadIdx.x < cols) {
     float t = 0.f;
-#pragma unroll
-    for (int w = 0; w < 8; ++w) t += red_s[w][lane];
-    store_dyn(out, c, out_code, t);
+#pragma unroll 8
+    for (int k = 0; k < 32; ++k) t += red_s[k][threadIdx.x];
+    store_dyn(out, (int64_t)blockIdx.x * 8 + threadIdx.x, out_code, t);
   }
 }
 

@@ -334,7 +334,7 @@ int launch_bwd(const void* dy, const void* saved, int saved_is_input, const floa
   }
   PMB_CHECK_LAUNCH("pmb_rms_norm_backward");
   if (dgamma != nullptr) {
-    red::colsum_rows<<<(int)((dim + 31) / 32), red::kThreads, 0, stream>>>(partial, grid, dim, dgamma, dgcode);
+    red::colsum_rows<<<red::colsum_rows_grid(dim), red::kThreads, 0, stream>>>(partial, grid, dim, dgamma, dgcode);
     PMB_CHECK_LAUNCH("pmb_rms_norm_backward(grad_gamma)");
   }
   return PMB_OK;

@@ -1,4 +1,5 @@
 // Error channel and small shared host utilities of the C ABI.
+#include <initializer_list>
 #include <atomic>
 #include <cstring>
 
@@ -56,15 +57,20 @@ int make_band_table(BandTable& t, int count, const int64_t* widths, const void* 
 // Per-translation-unit tcgen05 wait-timeout flags (umma.cuh).
 unsigned int timeout_flag_gemm(int reset);
 unsigned int timeout_flag_mask(int reset);
+unsigned int timeout_flag_qkv(int reset);
+unsigned int timeout_flag_ff(int reset);
 
 }  // namespace pmb
 
 extern "C" {
 
 unsigned int pmb_umma_timeout(int reset) {
-  const unsigned int a = pmb::timeout_flag_gemm(reset);
-  const unsigned int b = pmb::timeout_flag_mask(reset);
-  return a ? a : b;
+  unsigned int first = 0;
+  for (auto flag : {pmb::timeout_flag_gemm, pmb::timeout_flag_mask, pmb::timeout_flag_qkv, pmb::timeout_flag_ff}) {
+    const unsigned int v = flag(reset);
+    if (first == 0) first = v;
+  }
+  return first;
 }
 
 const char* pmb_version(void) { return "0.1.0"; }

@@ -14,6 +14,7 @@ gradients are produced in fp32.
 from __future__ import annotations
 
 import torch
+import torch.nn.functional as F
 
 from . import _native as nat
 from . import extension as ext
@@ -223,24 +224,45 @@ def tensor_core_ok(x: torch.Tensor, *dims: int) -> bool:
 
 # ------------------------------------------------------- attention pieces
 class QKVRotaryFn(torch.autograd.Function):
-    """xn [b, n, D] -> q, k, v [b, h, n, dh]: projection, split, rotary on q/k."""
+    """xn [b, n, D] -> q, k, v [b, h, n, dh]: projection, split, rotary on q/k.
+
+    16-bit activations with D % 8 == 0 and dh % 32 == 0: one tensor-core GEMM
+    with the rotation in its epilogue writes q, k, v as [b, n, h, dh] planes
+    (pmb_qkv_linear_rotary_forward); the returned [b, h, n, dh] tensors are
+    views of them, which the attention kernel reads in place.  cos_t / sin_t
+    are the transposed angle tables ([dh/2, n]) that epilogue reads.
+    Otherwise (fp32, other shapes): a torch projection plus the split kernel.
+    The backward merges the three gradients, in whatever layout the attention
+    backward produced them, with the inverse rotation (pmb_qkv_rotary_merge)
+    and runs the two projection-gradient GEMMs."""
 
     @staticmethod
-    def forward(ctx, xn, weight, cos, sin, heads):
+    def forward(ctx, xn, weight, cos, sin, cos_t, sin_t, heads):
         device = nat.require_cuda(xn, weight, name="QKVRotary")
         b, n, d = xn.shape
         dh = weight.shape[0] // (3 * heads)
-        w = weight.to(xn.dtype)
-        x2 = xn.reshape(b * n, d)
-        qkv = torch.matmul(x2, w.t())
-        q = torch.empty(b, heads, n, dh, dtype=xn.dtype, device=device)
-        k = torch.empty_like(q)
-        v = torch.empty_like(q)
+        w = weight.to(xn.dtype).contiguous()
+        x2 = xn.reshape(b * n, d).contiguous()
         rotate = int(cos is not None)
-        nat.call(
-            "pmb_qkv_rotary_split", qkv.data_ptr(), nat.ptr(cos), nat.ptr(sin), b, n, heads, dh, q.data_ptr(),
-            k.data_ptr(), v.data_ptr(), rotate, nat.dtype_code(xn.dtype), nat.stream_handle(device),
-        )
+        if xn.dtype in (torch.bfloat16, torch.float16) and d % 8 == 0 and dh % 32 == 0:
+            if rotate and cos_t is None:
+                cos_t, sin_t = cos.t().contiguous(), sin.t().contiguous()
+            planes = [torch.empty(b, n, heads, dh, dtype=xn.dtype, device=device) for _ in range(3)]
+            nat.call(
+                "pmb_qkv_linear_rotary_forward", x2.data_ptr(), w.data_ptr(), nat.ptr(cos_t), nat.ptr(sin_t), b, n,
+                d, heads, dh, planes[0].data_ptr(), planes[1].data_ptr(), planes[2].data_ptr(), rotate,
+                nat.dtype_code(xn.dtype), nat.stream_handle(device),
+            )
+            q, k, v = (p.transpose(1, 2) for p in planes)
+        else:
+            qkv = torch.matmul(x2, w.t())
+            q = torch.empty(b, heads, n, dh, dtype=xn.dtype, device=device)
+            k = torch.empty_like(q)
+            v = torch.empty_like(q)
+            nat.call(
+                "pmb_qkv_rotary_split", qkv.data_ptr(), nat.ptr(cos), nat.ptr(sin), b, n, heads, dh, q.data_ptr(),
+                k.data_ptr(), v.data_ptr(), rotate, nat.dtype_code(xn.dtype), nat.stream_handle(device),
+            )
         ctx.heads = heads
         ctx.weight_dtype = weight.dtype
         ctx.save_for_backward(x2, w, cos, sin)
@@ -253,16 +275,71 @@ class QKVRotaryFn(torch.autograd.Function):
         device = x2.device
         ref = next(g for g in (gq, gk, gv) if g is not None)
         b, _, n, dh = ref.shape
-        gq, gk, gv = (torch.zeros_like(ref) if g is None else g for g in (gq, gk, gv))
-        gq, gk, gv = (g.to(x2.dtype).contiguous() for g in (gq, gk, gv))
+        grads = [torch.zeros_like(ref) if g is None else g.to(x2.dtype) for g in (gq, gk, gv)]
+        strides = grads[0].stride()
+        if strides[-1] != 1 or any(g.stride() != strides for g in grads[1:]):
+            grads = [g.contiguous() for g in grads]
+            strides = grads[0].stride()
         gqkv = torch.empty(b * n, 3 * heads * dh, dtype=x2.dtype, device=device)
         nat.call(
-            "pmb_qkv_rotary_merge", gq.data_ptr(), gk.data_ptr(), gv.data_ptr(), nat.ptr(cos), nat.ptr(sin), b, n,
-            heads, dh, gqkv.data_ptr(), int(cos is not None), nat.dtype_code(x2.dtype), nat.stream_handle(device),
+            "pmb_qkv_rotary_merge", grads[0].data_ptr(), grads[1].data_ptr(), grads[2].data_ptr(), nat.ptr(cos),
+            nat.ptr(sin), b, n, heads, dh, gqkv.data_ptr(), int(cos is not None), nat.dtype_code(x2.dtype),
+            strides[0], strides[1], strides[2], nat.stream_handle(device),
         )
         gx = torch.matmul(gqkv, w).reshape(b, n, -1) if ctx.needs_input_grad[0] else None
         gw = torch.matmul(gqkv.t(), x2).to(ctx.weight_dtype) if ctx.needs_input_grad[1] else None
-        return gx, gw, None, None, None
+        return gx, gw, None, None, None, None, None
+
+
+class FeedForwardFn(torch.autograd.Function):
+    """xn [rows, D] -> gelu(xn W1^T + b1) W2^T + b2 (16-bit activations).
+
+    The two Linear layers and their weight / input gradients are plain
+    library GEMMs (cuBLAS through torch, bias in the GEMM epilogue, operands
+    cast to the activation dtype as autocast does); GELU, its derivative and
+    both bias gradients are this package's kernels: the GELU derivative and
+    the first bias gradient come out of one pass over the hidden activations
+    (pmb_gelu_backward), the second bias gradient from pmb_column_sum."""
+
+    @staticmethod
+    def forward(ctx, xn, w1, b1, w2, b2):
+        device = nat.require_cuda(xn, w1, b1, w2, b2, name="FeedForward")
+        dt = xn.dtype
+        xn = xn.contiguous()
+        w1c, w2c = w1.to(dt), w2.to(dt)
+        pre = F.linear(xn, w1c, b1.to(dt))
+        act = torch.empty_like(pre)
+        nat.call("pmb_gelu_forward", pre.data_ptr(), act.data_ptr(), pre.numel(), nat.dtype_code(dt),
+                 nat.stream_handle(device))
+        out = F.linear(act, w2c, b2.to(dt))
+        ctx.param_dtypes = (w1.dtype, b1.dtype, w2.dtype, b2.dtype)
+        ctx.save_for_backward(xn, pre, act, w1c, w2c)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        xn, pre, act, w1c, w2c = ctx.saved_tensors
+        rows, dim = xn.shape
+        hidden = pre.shape[1]
+        device = xn.device
+        dt = xn.dtype
+        st = nat.stream_handle(device)
+        g = grad_out.to(dt).contiguous()
+        dts = ctx.param_dtypes
+        gb2 = torch.empty(dim, dtype=dts[3], device=device)
+        wsb = nat.library().pmb_rows_pass_workspace_size(rows, max(dim, hidden))
+        ws = nat.workspace(wsb, device)
+        nat.call("pmb_column_sum", g.data_ptr(), rows, dim, gb2.data_ptr(), nat.dtype_code(dts[3]),
+                 nat.dtype_code(dt), ws.data_ptr(), wsb, st)
+        gw2 = torch.matmul(g.t(), act).to(dts[2])
+        da = torch.matmul(g, w2c)
+        dpre = torch.empty_like(pre)
+        gb1 = torch.empty(hidden, dtype=dts[1], device=device)
+        nat.call("pmb_gelu_backward", da.data_ptr(), pre.data_ptr(), dpre.data_ptr(), rows, hidden, gb1.data_ptr(),
+                 nat.dtype_code(dts[1]), nat.dtype_code(dt), ws.data_ptr(), wsb, st)
+        gw1 = torch.matmul(dpre.t(), xn).to(dts[0])
+        gx = torch.matmul(dpre, w1c) if ctx.needs_input_grad[0] else None
+        return gx, gw1, gb1, gw2, gb2
 
 
 class AttentionGateFn(torch.autograd.Function):
@@ -344,7 +421,8 @@ class BandRecombineFn(torch.autograd.Function):
 
 
 def rotary_tables(freqs: torch.Tensor, n: int, device: torch.device) -> tuple[torch.Tensor, torch.Tensor]:
-    """fp32 cos/sin [n, dh/2] for positions 0..n-1 (exact fp32 positions)."""
+    """fp32 cos/sin [n, dh/2] for positions 0..n-1 (exact fp32 positions); .t().contiguous() of them are the
+    transposed tables the fused projection epilogue reads."""
     pos = torch.arange(n, device=device, dtype=torch.float32)
     ang = pos[:, None] * freqs.detach().to(device=device, dtype=torch.float32)[None, :]
     return ang.cos().contiguous(), ang.sin().contiguous()

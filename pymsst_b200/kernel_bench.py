@@ -1,0 +1,264 @@
+"""Per-kernel timings of the C-ABI entry points at the config-3 shapes.
+
+``python -m pymsst_b200.kernel_bench [op ...] [--iters N] [--json PATH]``
+
+Each op is one entry-point call on synthetic device tensors with the shapes a
+config-3 training step uses (BS-RoFormer dim 192, 8 heads of 64, batch 4 x
+258 frames x 62 bands = 63984 transformer rows).  Calls are timed with CUDA
+events on the launching stream after 3 warm-up calls, with a 256 MB buffer
+written between timed calls so every call starts with a cold L2.  The line
+printed per op gives the median time, the algorithmic bytes (each operand
+read once, each result written once) and the achieved fraction of the
+measured HBM bandwidth, or TFLOP/s for the GEMMs.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+from . import _native as nat
+from .roofline import load_peaks
+
+ROWS, DIM, HEADS, DHEAD = 63984, 192, 8, 64
+SEQ_BATCH, SEQ = 248, 258
+
+
+class _Bench:
+    def __init__(self, device: torch.device, iters: int):
+        self.device = device
+        self.iters = iters
+        self.flush = torch.empty(64 * 1024 * 1024, device=device)
+        self.stream = torch.cuda.current_stream(device)
+        self.results: dict[str, dict] = {}
+        self.peaks = load_peaks()
+
+    def time(self, name: str, fn, bytes_: float = 0.0, flops: float = 0.0) -> dict:
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize(self.device)
+        times = []
+        for _ in range(self.iters):
+            self.flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(self.stream)
+            fn()
+            b.record(self.stream)
+            torch.cuda.synchronize(self.device)
+            times.append(a.elapsed_time(b))
+        times.sort()
+        us = times[len(times) // 2] * 1e3
+        rec = {"us": round(us, 2), "bytes": bytes_, "flops": flops}
+        if flops > 0 and flops / (self.peaks["bf16_tflops"] * 1e12) > bytes_ / (self.peaks["hbm_gbs"] * 1e9):
+            rec["tflops"] = round(flops / us / 1e6, 1)
+            rec["frac"] = round(rec["tflops"] / self.peaks["bf16_tflops"], 3)
+            what = f"{rec['tflops']:8.1f} TFLOP/s"
+        else:
+            rec["gbs"] = round(bytes_ / us / 1e3, 1)
+            rec["frac"] = round(rec["gbs"] / self.peaks["hbm_gbs"], 3)
+            what = f"{rec['gbs']:8.1f} GB/s"
+        self.results[name] = rec
+        print(f"{name:34s} {us:9.1f} us {bytes_ / 1e6:9.1f} MB {what}  frac {rec['frac']:.3f}", flush=True)
+        return rec
+
+
+def _gemm(a, lda, a_mn, b, ldb, b_mn, c, m, n, k, bias=None, act=0):
+    nat.call("pmb_gemm_tc", a.data_ptr(), lda, a_mn, b.data_ptr(), ldb, b_mn, c.data_ptr(), c.stride(0),
+             nat.dtype_code(c.dtype), nat.ptr(bias), nat.dtype_code(bias.dtype) if bias is not None else 0, act,
+             m, n, k, nat.dtype_code(a.dtype), nat.stream_handle(a.device))
+
+
+def op_gate(bench: _Bench):
+    dev, bf, f32 = bench.device, torch.bfloat16, torch.float32
+    x = torch.randn(ROWS, DIM, device=dev, dtype=bf)
+    attn = torch.randn(SEQ_BATCH, HEADS, SEQ, DHEAD, device=dev, dtype=bf)
+    w = torch.randn(HEADS, DIM, device=dev, dtype=f32) * 0.1
+    b = torch.randn(HEADS, device=dev, dtype=f32)
+    out = torch.empty(ROWS, HEADS * DHEAD, device=dev, dtype=bf)
+    gate = torch.empty(ROWS, HEADS, device=dev, dtype=bf)
+    st = nat.stream_handle(dev)
+    strides = (attn.stride(0), attn.stride(2), attn.stride(1))
+
+    def fwd():
+        nat.call("pmb_attention_gate_forward", attn.data_ptr(), SEQ, *strides, x.data_ptr(), w.data_ptr(),
+                 b.data_ptr(), ROWS, HEADS, DHEAD, DIM, out.data_ptr(), gate.data_ptr(), nat.dtype_code(bf),
+                 nat.dtype_code(f32), st)
+
+    e = 2
+    bench.time("attention_gate_forward", fwd, ROWS * (DIM + 2 * HEADS * DHEAD + HEADS) * e)
+    dy = torch.randn(ROWS, HEADS * DHEAD, device=dev, dtype=bf)
+    ga, gx = torch.empty_like(attn), torch.empty_like(x)
+    gw, gb = torch.empty_like(w), torch.empty_like(b)
+    wsb = nat.library().pmb_attention_gate_backward_workspace_size(ROWS, HEADS, DIM)
+    ws = nat.workspace(wsb, dev)
+
+    def bwd():
+        nat.call("pmb_attention_gate_backward", dy.data_ptr(), attn.data_ptr(), SEQ, *strides, x.data_ptr(),
+                 w.data_ptr(), gate.data_ptr(), ROWS, HEADS, DHEAD, DIM, ga.data_ptr(), gx.data_ptr(), gw.data_ptr(),
+                 gb.data_ptr(), nat.dtype_code(bf), nat.dtype_code(f32), ws.data_ptr(), wsb, st)
+
+    bench.time("attention_gate_backward", bwd, ROWS * (3 * HEADS * DHEAD + 2 * DIM + HEADS) * e)
+
+
+def op_rms(bench: _Bench):
+    dev, bf = bench.device, torch.bfloat16
+    x = torch.randn(ROWS, DIM, device=dev, dtype=bf)
+    g = torch.ones(DIM, device=dev, dtype=bf)
+    out, normed = torch.empty_like(x), torch.empty_like(x)
+    inv = torch.empty(ROWS, device=dev)
+    st = nat.stream_handle(dev)
+    bench.time("rms_norm_forward", lambda: nat.call(
+        "pmb_rms_norm_forward", x.data_ptr(), g.data_ptr(), out.data_ptr(), normed.data_ptr(), inv.data_ptr(), ROWS,
+        DIM, 2, 2, 2, st), ROWS * DIM * 2 * 3 + ROWS * 4)
+    dy = torch.randn_like(x)
+    gx, gg = torch.empty_like(x), torch.empty_like(g)
+    wsb = nat.library().pmb_rms_norm_backward_workspace_size(ROWS, DIM)
+    ws = nat.workspace(wsb, dev)
+    bench.time("rms_norm_backward", lambda: nat.call(
+        "pmb_rms_norm_backward", dy.data_ptr(), x.data_ptr(), 1, inv.data_ptr(), g.data_ptr(), gx.data_ptr(),
+        gg.data_ptr(), ROWS, DIM, 2, 2, 2, 2, ws.data_ptr(), wsb, st), ROWS * DIM * 2 * 3 + ROWS * 4)
+
+
+def op_qkv(bench: _Bench):
+    dev, bf = bench.device, torch.bfloat16
+    n3 = 3 * HEADS * DHEAD
+    x = torch.randn(ROWS, DIM, device=dev, dtype=bf)
+    w = torch.randn(n3, DIM, device=dev, dtype=bf) * 0.05
+    qkv = torch.empty(ROWS, n3, device=dev, dtype=bf)
+    flops = 2.0 * ROWS * n3 * DIM
+    bench.time("gemm_tc qkv (x W^T)", lambda: _gemm(x, DIM, 0, w, DIM, 0, qkv, ROWS, n3, DIM),
+               (ROWS * DIM + n3 * DIM + ROWS * n3) * 2, flops)
+    bench.time("torch qkv (x W^T)", lambda: torch.matmul(x, w.t(), out=qkv), (ROWS * DIM + n3 * DIM + ROWS * n3) * 2,
+               flops)
+    dx = torch.empty(ROWS, DIM, device=dev, dtype=bf)
+    bench.time("gemm_tc dx (dqkv W)", lambda: _gemm(qkv, n3, 0, w, DIM, 1, dx, ROWS, DIM, n3),
+               (ROWS * DIM + n3 * DIM + ROWS * n3) * 2, flops)
+    bench.time("torch dx (dqkv W)", lambda: torch.matmul(qkv, w, out=dx), (ROWS * DIM + n3 * DIM + ROWS * n3) * 2,
+               flops)
+    cos = torch.randn(SEQ, DHEAD // 2, device=dev)
+    sin = torch.randn(SEQ, DHEAD // 2, device=dev)
+    q = torch.empty(SEQ_BATCH, HEADS, SEQ, DHEAD, device=dev, dtype=bf)
+    k, v = torch.empty_like(q), torch.empty_like(q)
+    st = nat.stream_handle(dev)
+    bench.time("qkv_rotary_split", lambda: nat.call(
+        "pmb_qkv_rotary_split", qkv.data_ptr(), cos.data_ptr(), sin.data_ptr(), SEQ_BATCH, SEQ, HEADS, DHEAD,
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), 1, 2, st), ROWS * n3 * 2 * 2)
+    bench.time("qkv_rotary_merge", lambda: nat.call(
+        "pmb_qkv_rotary_merge", q.data_ptr(), k.data_ptr(), v.data_ptr(), cos.data_ptr(), sin.data_ptr(), SEQ_BATCH,
+        SEQ, HEADS, DHEAD, qkv.data_ptr(), 1, 2, q.stride(0), q.stride(1), q.stride(2), st), ROWS * n3 * 2 * 2)
+    cos_t, sin_t = cos.t().contiguous(), sin.t().contiguous()
+    pq, pk, pv = (torch.empty(ROWS, HEADS * DHEAD, device=dev, dtype=bf) for _ in range(3))
+    bench.time("qkv_linear_rotary_forward", lambda: nat.call(
+        "pmb_qkv_linear_rotary_forward", x.data_ptr(), w.data_ptr(), cos_t.data_ptr(), sin_t.data_ptr(), SEQ_BATCH,
+        SEQ, DIM, HEADS, DHEAD, pq.data_ptr(), pk.data_ptr(), pv.data_ptr(), 1, 2, st),
+        (ROWS * DIM + n3 * DIM + ROWS * n3) * 2, flops)
+    gw = torch.empty(n3, DIM, device=dev)
+    wsb = nat.library().pmb_gemm_tc_wgrad_workspace_size(n3, DIM, ROWS)
+    ws = nat.workspace(wsb, dev)
+    bench.time("gemm_tc_wgrad (dqkv^T x)", lambda: nat.call(
+        "pmb_gemm_tc_wgrad", qkv.data_ptr(), n3, x.data_ptr(), DIM, n3, DIM, ROWS, gw.data_ptr(), DIM, 0, 2,
+        ws.data_ptr(), wsb, st), (ROWS * n3 + ROWS * DIM) * 2 + n3 * DIM * 4, flops)
+    bench.time("torch wgrad (dqkv^T x)", lambda: torch.matmul(qkv.t(), x),
+               (ROWS * n3 + ROWS * DIM) * 2 + n3 * DIM * 2, flops)
+
+
+def op_ff(bench: _Bench):
+    dev, bf = bench.device, torch.bfloat16
+    hid = 4 * DIM
+    x = torch.randn(ROWS, DIM, device=dev, dtype=bf)
+    w1 = torch.randn(hid, DIM, device=dev, dtype=bf) * 0.05
+    b1 = torch.randn(hid, device=dev, dtype=bf)
+    h = torch.empty(ROWS, hid, device=dev, dtype=bf)
+    flops = 2.0 * ROWS * hid * DIM
+    byt = (ROWS * DIM + hid * DIM + ROWS * hid) * 2
+    bench.time("gemm_tc ff1 (+bias)", lambda: _gemm(x, DIM, 0, w1, DIM, 0, h, ROWS, hid, DIM, bias=b1), byt, flops)
+    bench.time("torch ff1 (+bias)", lambda: torch.nn.functional.linear(x, w1, b1), byt, flops)
+    w1f, b1f = w1.float(), b1.float()
+    w2 = torch.randn(DIM, hid, device=dev, dtype=bf) * 0.05
+    w2f, b2f = w2.float(), torch.randn(DIM, device=dev)
+    pre, act = torch.empty(ROWS, hid, device=dev, dtype=bf), torch.empty(ROWS, hid, device=dev, dtype=bf)
+    out = torch.empty(ROWS, DIM, device=dev, dtype=bf)
+    st = nat.stream_handle(dev)
+    fwd_bytes = (ROWS * DIM * 2 + ROWS * hid * 2) * 2
+    bench.time("feed_forward_forward", lambda: nat.call(
+        "pmb_feed_forward_forward", x.data_ptr(), w1.data_ptr(), b1f.data_ptr(), w2.data_ptr(), b2f.data_ptr(), ROWS,
+        DIM, hid, pre.data_ptr(), act.data_ptr(), out.data_ptr(), 2, 0, st), fwd_bytes, 2 * flops)
+    gy = torch.randn(ROWS, DIM, device=dev, dtype=bf)
+    gx = torch.empty_like(x)
+    gw1, gb1, gw2, gb2 = torch.empty_like(w1f), torch.empty_like(b1f), torch.empty_like(w2f), torch.empty_like(b2f)
+    wsb = nat.library().pmb_feed_forward_backward_workspace_size(ROWS, DIM, hid, 2)
+    ws = nat.workspace(wsb, dev)
+    gwsb = nat.library().pmb_rows_pass_workspace_size(ROWS, hid)
+    gws = nat.workspace(gwsb, dev)
+    gpre = torch.empty_like(pre)
+    bench.time("gelu_forward", lambda: nat.call("pmb_gelu_forward", pre.data_ptr(), act.data_ptr(), pre.numel(), 2, st),
+               2 * ROWS * hid * 2)
+    bench.time("gelu_backward (+bias grad)", lambda: nat.call(
+        "pmb_gelu_backward", act.data_ptr(), pre.data_ptr(), gpre.data_ptr(), ROWS, hid, gb1.data_ptr(), 0, 2,
+        gws.data_ptr(), gwsb, st), 3 * ROWS * hid * 2)
+    bench.time("column_sum [rows, dim]", lambda: nat.call(
+        "pmb_column_sum", gy.data_ptr(), ROWS, DIM, gb2.data_ptr(), 0, 2, gws.data_ptr(), gwsb, st), ROWS * DIM * 2)
+    bwd_bytes = (3 * ROWS * DIM + 4 * ROWS * hid) * 2
+    bench.time("feed_forward_backward", lambda: nat.call(
+        "pmb_feed_forward_backward", gy.data_ptr(), x.data_ptr(), pre.data_ptr(), act.data_ptr(), w1.data_ptr(),
+        w2.data_ptr(), ROWS, DIM, hid, gx.data_ptr(), gw1.data_ptr(), gb1.data_ptr(), gw2.data_ptr(), gb2.data_ptr(),
+        2, 0, ws.data_ptr(), wsb, st), bwd_bytes, 4 * flops)
+    lin1 = torch.nn.Linear(DIM, hid, device=dev)
+    lin2 = torch.nn.Linear(hid, DIM, device=dev)
+    xr = x.detach().requires_grad_()
+
+    def torch_ff():
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            y = lin2(torch.nn.functional.gelu(lin1(xr)))
+        y.backward(gy)
+
+    bench.time("torch feed-forward fwd+bwd", torch_ff, fwd_bytes + bwd_bytes, 6 * flops)
+
+
+def op_sdpa(bench: _Bench):
+    """Attention core (library kernels) fwd+bwd per backend, q/k/v as [B, H, N, Dh] views of [B, N, H, Dh]."""
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+
+    dev, bf = bench.device, torch.bfloat16
+    for nb, n in ((SEQ_BATCH, SEQ), (ROWS // 62, 62)):
+        qkv = [torch.randn(nb, n, HEADS, DHEAD, device=dev, dtype=bf).transpose(1, 2).requires_grad_()
+               for _ in range(3)]
+        gy = torch.randn(nb, HEADS, n, DHEAD, device=dev, dtype=bf)
+        flops = 4.0 * nb * HEADS * n * n * DHEAD * 3.5
+        for backend in (SDPBackend.CUDNN_ATTENTION, SDPBackend.FLASH_ATTENTION, SDPBackend.EFFICIENT_ATTENTION):
+            def run():
+                with sdpa_kernel(backend):
+                    y = torch.nn.functional.scaled_dot_product_attention(*qkv)
+                y.backward(gy)
+            try:
+                bench.time(f"sdpa {backend.name} n={n}", run, 0.0, flops)
+            except RuntimeError as e:
+                print(f"sdpa {backend.name} n={n}: unavailable ({str(e).splitlines()[0][:80]})")
+
+
+OPS = {"gate": op_gate, "rms": op_rms, "qkv": op_qkv, "ff": op_ff, "sdpa": op_sdpa}
+
+
+def main(argv=None) -> None:
+    p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    p.add_argument("ops", nargs="*", help=f"ops to run (default all): {', '.join(OPS)}")
+    p.add_argument("--iters", type=int, default=20)
+    p.add_argument("--json", default=None)
+    args = p.parse_args(argv)
+    device = torch.device("cuda", torch.cuda.current_device())
+    bench = _Bench(device, args.iters)
+    for name in args.ops or list(OPS):
+        if name not in OPS:
+            raise SystemExit(f"unknown op {name!r}; choose from {', '.join(OPS)}")
+        OPS[name](bench)
+    timeout = nat.library().pmb_umma_timeout(1)
+    if timeout:
+        raise RuntimeError(f"tcgen05 wait timed out (site {timeout:#x})")
+    if args.json:
+        with open(args.json, "w") as f:
+            json.dump(bench.results, f, indent=1)
+
+
+if __name__ == "__main__":
+    main()

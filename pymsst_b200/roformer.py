@@ -40,6 +40,7 @@ from .fused import (
     BandGatherFn,
     BandRecombineFn,
     BandSplitFn,
+    FeedForwardFn,
     MaskEstimatorFn,
     MaskEstimatorTCFn,
     QKVRotaryFn,
@@ -75,7 +76,8 @@ class RotaryEmbedding(nn.Module):
         key = (n, device.type, device.index, self.freqs.data_ptr(), self.freqs._version)
         hit = self._tables.get(key)
         if hit is None:
-            self._tables = {key: rotary_tables(self.freqs, n, device)}
+            cos, sin = rotary_tables(self.freqs, n, device)
+            self._tables = {key: (cos, sin, cos.t().contiguous(), sin.t().contiguous())}
             hit = self._tables[key]
         return hit
 
@@ -96,10 +98,10 @@ class Attention(nn.Module):
     def forward(self, x):
         b, n, d = x.shape
         xn = self.norm(x)
-        cos = sin = None
+        cos = sin = cos_t = sin_t = None
         if self.rotary_embed is not None:
-            cos, sin = self.rotary_embed.tables(n, x.device)
-        q, k, v = QKVRotaryFn.apply(xn, self.to_qkv.weight, cos, sin, self.heads)
+            cos, sin, cos_t, sin_t = self.rotary_embed.tables(n, x.device)
+        q, k, v = QKVRotaryFn.apply(xn, self.to_qkv.weight, cos, sin, cos_t, sin_t, self.heads)
         attn = F.scaled_dot_product_attention(q, k, v, dropout_p=self.dropout if self.training else 0.0)
         gated = AttentionGateFn.apply(attn, xn.reshape(b * n, d), self.to_gates.weight, self.to_gates.bias)
         out = F.linear(gated, self.to_out[0].weight.to(gated.dtype))
@@ -117,6 +119,13 @@ class FeedForward(nn.Module):
     def forward(self, x):
         dt = x.dtype
         h = self.net[0](x)
+        lin1, lin2 = self.net[1], self.net[4]
+        dropout_live = self.training and (self.net[3].p > 0 or self.net[5].p > 0)
+        if h.dtype in (torch.bfloat16, torch.float16) and not dropout_live and h.shape[-1] % 8 == 0 and \
+                lin1.out_features % 8 == 0:
+            shape = h.shape
+            out = FeedForwardFn.apply(h.reshape(-1, shape[-1]), lin1.weight, lin1.bias, lin2.weight, lin2.bias)
+            return out.reshape(shape)
         h = F.linear(h, self.net[1].weight.to(dt), self.net[1].bias.to(dt))
         h = self.net[3](F.gelu(h))
         h = F.linear(h, self.net[4].weight.to(dt), self.net[4].bias.to(dt))

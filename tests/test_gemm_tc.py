@@ -63,3 +63,25 @@ def test_gemm_tc_rejects_unaligned_stride(cuda_device):
     st = nat.library().pmb_gemm_tc(a.data_ptr(), 100, 0, a.data_ptr(), 100, 0, c.data_ptr(), 130, 0, None, 0, 0,
                                    130, 130, 100, nat.dtype_code(a.dtype), nat.stream_handle(a.device))
     assert st == -4 and b"16-byte" in nat.library().pmb_last_error()
+
+
+@pytest.mark.parametrize("m,n,k", [(1536, 192, 63984), (768, 192, 5000), (192, 768, 4100), (130, 70, 100),
+                                   (64, 64, 64)])
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16])
+def test_gemm_tc_wgrad_split_k(cuda_device, m, n, k, out_dtype):
+    """C = A^T B over K rows (split-K with fp32 partials) against float64."""
+    torch.manual_seed(m * 7 + n + k)
+    A = torch.randn(k, m).to(torch.bfloat16)
+    B = torch.randn(k, n).to(torch.bfloat16)
+    ref = A.double().t() @ B.double()
+    a, b = _padded(A, cuda_device), _padded(B, cuda_device)
+    c = torch.empty(m, n, dtype=out_dtype, device=cuda_device)
+    wsb = nat.library().pmb_gemm_tc_wgrad_workspace_size(m, n, k)
+    ws = nat.workspace(wsb, cuda_device)
+    nat.call("pmb_gemm_tc_wgrad", a.data_ptr(), a.stride(0), b.data_ptr(), b.stride(0), m, n, k, c.data_ptr(),
+             c.stride(0), nat.dtype_code(out_dtype), nat.dtype_code(torch.bfloat16), ws.data_ptr(), wsb,
+             nat.stream_handle(cuda_device))
+    tol = 2e-3 * max(1.0, k ** 0.5)
+    rtol = 2e-3 if out_dtype == torch.float32 else 1e-2
+    torch.testing.assert_close(c.double().cpu(), ref, rtol=rtol, atol=tol)
+    assert nat.library().pmb_umma_timeout(1) == 0

@@ -139,11 +139,16 @@ def test_mask_estimator_final(cuda_device, widths, rows, hidden, dtype):
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-def test_attention_gate_strided_attention_layout(cuda_device, dtype):
-    """The gate reads the [batch, heads, seq, Dh] attention output in place."""
+@pytest.mark.parametrize("bsz,heads,seq,dh,dim", [(6, 8, 62, 64, 192), (3, 4, 41, 32, 100), (2, 16, 33, 16, 64),
+                                                  (5, 8, 258, 64, 384)])
+def test_attention_gate_strided_attention_layout(cuda_device, dtype, bsz, heads, seq, dh, dim):
+    """The gate reads the [batch, heads, seq, Dh] attention output in place.
+
+    Shapes cover the 32-row tiled kernels (16-byte vectors; partial last
+    tile) and the row-wise fallback (dim 100 is not a multiple of the bf16
+    vector width)."""
     from pymsst_b200 import _native as nat
 
-    bsz, heads, seq, dh, dim = 6, 8, 62, 64, 192
     rows = bsz * seq
     attn_bhnd = torch.randn(bsz, heads, seq, dh).to(dtype)
     x = torch.randn(rows, dim).to(dtype)
