@@ -221,6 +221,28 @@ __device__ __forceinline__ void load_x_tile(const T* __restrict__ x, int64_t r0,
   }
 }
 
+// Per-tile row bases of the attention layout (one 64-bit division per row,
+// by 32 threads, instead of one per 16-byte vector).
+__device__ __forceinline__ void load_row_bases(const AttnLayout& la, int64_t r0, int64_t rows, int64_t* rb_s) {
+  if (threadIdx.x < kTileRows) {
+    const int64_t r = r0 + threadIdx.x;
+    rb_s[threadIdx.x] = r < rows ? la.row_base(r) : 0;
+  }
+}
+
+// Thread -> (column vector, first row, row step) over a tile of 32 rows with
+// vr vectors per row: fixed column when vr divides the block, else strided.
+struct ColMap {
+  int c, r_first, r_step;
+  bool fixed;
+  __device__ ColMap(int vr) {
+    fixed = (kThreads % vr) == 0;
+    c = threadIdx.x % vr;
+    r_first = threadIdx.x / vr;
+    r_step = kThreads / vr;
+  }
+};
+
 template <typename T, typename TP>
 __global__ void __launch_bounds__(kThreads, 4)
     gate_fwd_tiled(const T* __restrict__ attn, AttnLayout la, const T* __restrict__ x, const TP* __restrict__ W,
@@ -228,16 +250,20 @@ __global__ void __launch_bounds__(kThreads, 4)
                    T* __restrict__ gate) {
   constexpr int V = Vec<T>::N;
   extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ int64_t rb_s[kTileRows];
   const TileSmem L(H, dim, V);
   float* w_s = reinterpret_cast<float*>(smem_raw);
   T* x_s = reinterpret_cast<T*>(smem_raw + L.w_bytes);
   float* g_s = reinterpret_cast<float*>(smem_raw + L.w_bytes + L.x_bytes);
   load_weights_smem<T, TP>(W, H, dim, w_s, L.wld);
   const int vh = Dh / V, vr = H * vh;
+  const ColMap cm(vr);
+  const int ch = cm.c / vh, cd = (cm.c - ch * vh) * V;
   const int64_t tiles = (rows + kTileRows - 1) / kTileRows;
   for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
     const int64_t r0 = tile * kTileRows;
     load_x_tile<T>(x, r0, rows, dim, x_s, L.xld);
+    load_row_bases(la, r0, rows, rb_s);
     __syncthreads();
     for (int p = threadIdx.x; p < kTileRows * H; p += kThreads) {
       const int r = p / H, h = p - r * H;
@@ -258,17 +284,30 @@ __global__ void __launch_bounds__(kThreads, 4)
       if (r0 + r < rows) gate[r0 * H + p] = Elem<T>::from_f(g);
     }
     __syncthreads();
+    const int nr = rows - r0 < kTileRows ? (int)(rows - r0) : kTileRows;
+    if (cm.fixed) {
+      const int64_t aoff = (int64_t)ch * la.s_h + cd;
+      T* orow = out + r0 * (int64_t)vr * V + (int64_t)cm.c * V;
 #pragma unroll 4
-    for (int v = threadIdx.x; v < kTileRows * vr; v += kThreads) {
-      const int r = v / vr, c = v - r * vr;
-      if (r0 + r >= rows) continue;
-      const int h = c / vh, d = (c - h * vh) * V;
-      float a[V];
-      Vec<T>::unpack(*reinterpret_cast<const uint4*>(attn + la.row_base(r0 + r) + h * la.s_h + d), a);
-      const float g = g_s[r * H + h];
+      for (int r = cm.r_first; r < nr; r += cm.r_step) {
+        float a[V];
+        Vec<T>::unpack(*reinterpret_cast<const uint4*>(attn + rb_s[r] + aoff), a);
+        const float g = g_s[r * H + ch];
 #pragma unroll
-      for (int q = 0; q < V; ++q) a[q] *= g;
-      *reinterpret_cast<uint4*>(out + (r0 + r) * (int64_t)vr * V + (int64_t)c * V) = Vec<T>::pack(a);
+        for (int q = 0; q < V; ++q) a[q] *= g;
+        *reinterpret_cast<uint4*>(orow + (int64_t)r * vr * V) = Vec<T>::pack(a);
+      }
+    } else {
+      for (int v = threadIdx.x; v < nr * vr; v += kThreads) {
+        const int r = v / vr, c = v - r * vr;
+        const int h = c / vh, d = (c - h * vh) * V;
+        float a[V];
+        Vec<T>::unpack(*reinterpret_cast<const uint4*>(attn + rb_s[r] + h * la.s_h + d), a);
+        const float g = g_s[r * H + h];
+#pragma unroll
+        for (int q = 0; q < V; ++q) a[q] *= g;
+        *reinterpret_cast<uint4*>(out + (r0 + r) * (int64_t)vr * V + (int64_t)c * V) = Vec<T>::pack(a);
+      }
     }
     __syncthreads();
   }
@@ -282,13 +321,16 @@ __global__ void __launch_bounds__(kThreads, 3)
                    float* __restrict__ partial_w, float* __restrict__ partial_b) {
   constexpr int V = Vec<T>::N;
   extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ int64_t rb_s[kTileRows];
   const TileSmem L(H, dim, V);
   float* w_s = reinterpret_cast<float*>(smem_raw);
   T* x_s = reinterpret_cast<T*>(smem_raw + L.w_bytes);
   float* g_s = reinterpret_cast<float*>(smem_raw + L.w_bytes + L.x_bytes);
   float* gp_s = g_s + kTileRows * H;
   load_weights_smem<T, TP>(W, H, dim, w_s, L.wld);
-  const int vh = Dh / V, vr = H * vh, vpr = dim / V, hd = H * dim;
+  const int vh = Dh / V, vr = H * vh, hd = H * dim, q4 = dim / 4;
+  const ColMap cm(vr);
+  const int ch = cm.c / vh, cd = (cm.c - ch * vh) * V;
   float accw[kMaxWPerThread];
 #pragma unroll
   for (int j = 0; j < kMaxWPerThread; ++j) accw[j] = 0.f;
@@ -296,58 +338,90 @@ __global__ void __launch_bounds__(kThreads, 3)
   const int64_t tiles = (rows + kTileRows - 1) / kTileRows;
   for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
     const int64_t r0 = tile * kTileRows;
+    const int nr = rows - r0 < kTileRows ? (int)(rows - r0) : kTileRows;
     load_x_tile<T>(x, r0, rows, dim, x_s, L.xld);
-    for (int p = threadIdx.x; p < kTileRows * H; p += kThreads)
-      g_s[p] = r0 + p / H < rows ? Elem<T>::to_f(gate[r0 * H + p]) : 0.f;
+    load_row_bases(la, r0, rows, rb_s);
+    for (int p = threadIdx.x; p < kTileRows * H; p += kThreads) {
+      g_s[p] = p / H < nr ? Elem<T>::to_f(gate[r0 * H + p]) : 0.f;
+      gp_s[p] = 0.f;
+    }
     __syncthreads();
-    // grad_attn = grad_out * gate; per (row, head) sum of grad_out * attn
-    // over the head's vh consecutive vectors, reduced across vh lanes.
-    // Trip counts are warp-uniform (kTileRows * vr is a multiple of 32).
+    // grad_attn = grad_out * gate; per (row, head) sum of grad_out * attn over
+    // the head's vh consecutive vectors, reduced across vh lanes.  Trip counts
+    // are warp-uniform (the lanes of a warp share their rows in the fixed map;
+    // kTileRows * vr is a multiple of 32 in the strided one).
+    if (cm.fixed) {
+      const int64_t aoff = (int64_t)ch * la.s_h + cd;
+      const T* gorow = grad_out + r0 * (int64_t)vr * V + (int64_t)cm.c * V;
 #pragma unroll 2
-    for (int v = threadIdx.x; v < kTileRows * vr; v += kThreads) {
-      const int r = v / vr, c = v - r * vr;
-      const int h = c / vh, d = (c - h * vh) * V;
-      float part = 0.f;
-      if (r0 + r < rows) {
-        const int64_t ai = la.row_base(r0 + r) + h * la.s_h + d;
-        float go[V], a[V];
-        Vec<T>::unpack(*reinterpret_cast<const uint4*>(grad_out + (r0 + r) * (int64_t)vr * V + (int64_t)c * V), go);
-        Vec<T>::unpack(*reinterpret_cast<const uint4*>(attn + ai), a);
-        const float g = g_s[r * H + h];
+      for (int r = cm.r_first; r < kTileRows; r += cm.r_step) {
+        float part = 0.f;
+        if (r < nr) {
+          const int64_t ai = rb_s[r] + aoff;
+          float go[V], a[V];
+          Vec<T>::unpack(*reinterpret_cast<const uint4*>(gorow + (int64_t)r * vr * V), go);
+          Vec<T>::unpack(*reinterpret_cast<const uint4*>(attn + ai), a);
+          const float g = g_s[r * H + ch];
 #pragma unroll
-        for (int q = 0; q < V; ++q) {
-          part += go[q] * a[q];
-          a[q] = go[q] * g;
+          for (int q = 0; q < V; ++q) {
+            part += go[q] * a[q];
+            a[q] = go[q] * g;
+          }
+          *reinterpret_cast<uint4*>(grad_attn + ai) = Vec<T>::pack(a);
         }
-        *reinterpret_cast<uint4*>(grad_attn + ai) = Vec<T>::pack(a);
+        for (int o = vh >> 1; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+        if ((cm.c & (vh - 1)) == 0 && r < nr) {
+          const float g = g_s[r * H + ch];
+          gp_s[r * H + ch] = part * g * (1.0f - g);
+        }
       }
-      for (int o = vh >> 1; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-      if ((c & (vh - 1)) == 0) {
-        const float g = g_s[r * H + h];
-        gp_s[r * H + h] = part * g * (1.0f - g);
+    } else {
+      for (int v = threadIdx.x; v < kTileRows * vr; v += kThreads) {
+        const int r = v / vr, c = v - r * vr;
+        const int h = c / vh, d = (c - h * vh) * V;
+        float part = 0.f;
+        if (r < nr) {
+          const int64_t ai = rb_s[r] + h * la.s_h + d;
+          float go[V], a[V];
+          Vec<T>::unpack(*reinterpret_cast<const uint4*>(grad_out + (r0 + r) * (int64_t)vr * V + (int64_t)c * V),
+                         go);
+          Vec<T>::unpack(*reinterpret_cast<const uint4*>(attn + ai), a);
+          const float g = g_s[r * H + h];
+#pragma unroll
+          for (int q = 0; q < V; ++q) {
+            part += go[q] * a[q];
+            a[q] = go[q] * g;
+          }
+          *reinterpret_cast<uint4*>(grad_attn + ai) = Vec<T>::pack(a);
+        }
+        for (int o = vh >> 1; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+        if ((c & (vh - 1)) == 0 && r < nr) {
+          const float g = g_s[r * H + h];
+          gp_s[r * H + h] = part * g * (1.0f - g);
+        }
       }
     }
     __syncthreads();
-    // grad_x[r, i] = sum_h gp[r, h] W[h, i]
-    for (int v = threadIdx.x; v < kTileRows * vpr; v += kThreads) {
-      const int r = v / vpr, i = (v - r * vpr) * V;
-      if (r0 + r >= rows) continue;
-      float acc[V];
-#pragma unroll
-      for (int q = 0; q < V; ++q) acc[q] = 0.f;
+    // grad_x[r, i..i+3] = sum_h gp[r, h] W[h, i..i+3]
+    for (int v = threadIdx.x; v < nr * q4; v += kThreads) {
+      const int r = v / q4, i = (v - r * q4) * 4;
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
       for (int h = 0; h < H; ++h) {
         const float gp = gp_s[r * H + h];
-        const float* wr = w_s + h * L.wld + i;
-#pragma unroll
-        for (int q = 0; q < V; q += 4) {
-          const float4 w4 = *reinterpret_cast<const float4*>(wr + q);
-          acc[q] += gp * w4.x;
-          acc[q + 1] += gp * w4.y;
-          acc[q + 2] += gp * w4.z;
-          acc[q + 3] += gp * w4.w;
-        }
+        const float4 w4 = *reinterpret_cast<const float4*>(w_s + h * L.wld + i);
+        acc[0] += gp * w4.x;
+        acc[1] += gp * w4.y;
+        acc[2] += gp * w4.z;
+        acc[3] += gp * w4.w;
       }
-      *reinterpret_cast<uint4*>(grad_x + (r0 + r) * dim + i) = Vec<T>::pack(acc);
+      T o4[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) o4[q] = Elem<T>::from_f(acc[q]);
+      T* dst = grad_x + (r0 + r) * dim + i;
+      if (sizeof(T) == 2)
+        *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(o4);
+      else
+        *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(o4);
     }
     // grad_W[h, i] += sum_r gp[r, h] x[r, i]; grad_b[h] += sum_r gp[r, h]
     // (rows past the end have gp = 0 and x = 0).

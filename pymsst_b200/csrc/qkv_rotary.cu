@@ -27,38 +27,51 @@ struct QkvDims {
   int64_t s_b, s_h, s_n;  // element strides of q / k / v (d contiguous)
 };
 
+// One warp per row (b, n) of the packed [B*N, 3, H, Dh] projection; lane l
+// handles the P-pair chunks c = l, l + 32, ... of the row (c indexes
+// (which, h, pair group) in that order).  Index math is 32-bit except the
+// per-row bases; the angle table row n is shared by the whole warp.
 template <typename T, int P, bool BACKWARD>
 __global__ void __launch_bounds__(kThreads)
     qkv_rotary_kernel(T* __restrict__ qkv, const float* __restrict__ cosv, const float* __restrict__ sinv, QkvDims d,
-                      T* __restrict__ q, T* __restrict__ k, T* __restrict__ v, int rotate_qk, int64_t units) {
-  const int gph = d.Dh / (2 * P);
+                      T* __restrict__ q, T* __restrict__ k, T* __restrict__ v, int rotate_qk) {
+  const int gph = d.Dh / (2 * P);         // chunks per head
+  const int cpw = d.H * gph;              // chunks per q / k / v part of a row
+  const int cpr = 3 * cpw;                // chunks per row
   const int half = d.Dh / 2;
-  for (int64_t u = (int64_t)blockIdx.x * kThreads + threadIdx.x; u < units; u += (int64_t)gridDim.x * kThreads) {
-    const int grp = (int)(u % gph);
-    int64_t rest = u / gph;
-    const int h = (int)(rest % d.H);
-    rest /= d.H;
-    const int which = (int)(rest % 3);
-    const int64_t row = rest / 3;
-    const int64_t b = row / d.N, n = row % d.N;
-    T* packed = qkv + ((row * 3 + which) * d.H + h) * d.Dh + grp * 2 * P;
-    T* base = which == 0 ? q : (which == 1 ? k : v);
-    T* split = base + b * d.s_b + h * d.s_h + n * d.s_n + grp * 2 * P;
-    const Chunk<T, P> in = *reinterpret_cast<const Chunk<T, P>*>(BACKWARD ? split : packed);
-    Chunk<T, P> out;
-    if (which < 2 && rotate_qk) {
+  const int lane = threadIdx.x & 31;
+  const int64_t rows = d.B * d.N;
+  const int64_t warps = (int64_t)gridDim.x * (kThreads / 32);
+  for (int64_t row = (int64_t)blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5); row < rows; row += warps) {
+    const int64_t b = row / d.N;
+    const int n = (int)(row - b * d.N);
+    T* prow = qkv + row * (int64_t)cpr * 2 * P;
+    const int64_t sbase = b * d.s_b + (int64_t)n * d.s_n;
+    const float* crow = cosv + (int64_t)n * half;
+    const float* srow = sinv + (int64_t)n * half;
+#pragma unroll 2
+    for (int c = lane; c < cpr; c += 32) {
+      const int which = c / cpw, rem = c - which * cpw;
+      const int h = rem / gph, grp = rem - h * gph;
+      T* base = which == 0 ? q : (which == 1 ? k : v);
+      T* split = base + sbase + (int64_t)h * d.s_h + grp * 2 * P;
+      T* packed = prow + c * 2 * P;
+      const Chunk<T, P> in = *reinterpret_cast<const Chunk<T, P>*>(BACKWARD ? split : packed);
+      Chunk<T, P> out;
+      if (which < 2 && rotate_qk) {
 #pragma unroll
-      for (int p = 0; p < P; ++p) {
-        const float c = cosv[n * half + grp * P + p];
-        const float s = BACKWARD ? -sinv[n * half + grp * P + p] : sinv[n * half + grp * P + p];
-        const float e = Elem<T>::to_f(in.v[2 * p]), o = Elem<T>::to_f(in.v[2 * p + 1]);
-        out.v[2 * p] = Elem<T>::from_f(e * c - o * s);
-        out.v[2 * p + 1] = Elem<T>::from_f(o * c + e * s);
+        for (int p = 0; p < P; ++p) {
+          const float cs = crow[grp * P + p];
+          const float sn = BACKWARD ? -srow[grp * P + p] : srow[grp * P + p];
+          const float e = Elem<T>::to_f(in.v[2 * p]), o = Elem<T>::to_f(in.v[2 * p + 1]);
+          out.v[2 * p] = Elem<T>::from_f(e * cs - o * sn);
+          out.v[2 * p + 1] = Elem<T>::from_f(o * cs + e * sn);
+        }
+      } else {
+        out = in;
       }
-    } else {
-      out = in;
+      *reinterpret_cast<Chunk<T, P>*>(BACKWARD ? packed : split) = out;
     }
-    *reinterpret_cast<Chunk<T, P>*>(BACKWARD ? packed : split) = out;
   }
 }
 
@@ -70,22 +83,16 @@ int launch(void* qkv, const float* cosv, const float* sinv, QkvDims d, void* q, 
   constexpr int P = sizeof(T) == 2 ? 4 : 2;  // 16-byte chunks
   const bool vec = (d.Dh % (2 * P)) == 0 && (al % 16) == 0 && d.s_b % (2 * P) == 0 && d.s_h % (2 * P) == 0 &&
                    d.s_n % (2 * P) == 0;
-  const int64_t pairs_per_row = 3LL * d.H * (d.Dh / 2);
-  const int64_t cap = (int64_t)num_sms() * 32;
-  auto grid_for = [&](int64_t units) {
-    int64_t g = (units + kThreads - 1) / kThreads;
-    if (g > cap) g = cap;
-    return (int)(g < 1 ? 1 : g);
-  };
-  if (vec) {
-    const int64_t units = d.B * d.N * pairs_per_row / P;
-    qkv_rotary_kernel<T, P, BACKWARD><<<grid_for(units), kThreads, 0, stream>>>(
-        static_cast<T*>(qkv), cosv, sinv, d, static_cast<T*>(q), static_cast<T*>(k), static_cast<T*>(v), rotate, units);
-  } else {
-    const int64_t units = d.B * d.N * pairs_per_row;
-    qkv_rotary_kernel<T, 1, BACKWARD><<<grid_for(units), kThreads, 0, stream>>>(
-        static_cast<T*>(qkv), cosv, sinv, d, static_cast<T*>(q), static_cast<T*>(k), static_cast<T*>(v), rotate, units);
-  }
+  int64_t g = (d.B * d.N + kThreads / 32 - 1) / (kThreads / 32);
+  const int64_t cap = (int64_t)num_sms() * 16;
+  if (g > cap) g = cap;
+  if (g < 1) g = 1;
+  if (vec)
+    qkv_rotary_kernel<T, P, BACKWARD><<<(int)g, kThreads, 0, stream>>>(
+        static_cast<T*>(qkv), cosv, sinv, d, static_cast<T*>(q), static_cast<T*>(k), static_cast<T*>(v), rotate);
+  else
+    qkv_rotary_kernel<T, 1, BACKWARD><<<(int)g, kThreads, 0, stream>>>(
+        static_cast<T*>(qkv), cosv, sinv, d, static_cast<T*>(q), static_cast<T*>(k), static_cast<T*>(v), rotate);
   PMB_CHECK_LAUNCH(name);
   return PMB_OK;
 }

@@ -12,8 +12,11 @@
 
 #include "common.cuh"
 #include "reduce.cuh"
+#include "umma.cuh"
 
 namespace pmb {
+unsigned int timeout_flag_rms(int reset) { return umma::flag_reader(reset); }
+
 namespace {
 
 constexpr int kThreads = 256;
@@ -261,6 +264,269 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
+// ------------------------------------------------- bulk-staged (TMA) path
+// Rows are contiguous, so a tile of consecutive rows is one contiguous block:
+// one thread streams tiles into a kStages-deep shared-memory ring with
+// cp.async.bulk (mbarrier completion), keeping up to kStages tiles per CTA in
+// flight without holding registers, and the warps normalise rows out of
+// shared memory.  Persistent CTAs; tiles t = blockIdx.x + i * gridDim.x.
+constexpr int kStages = 4;
+constexpr int kFwdStageBytes = 12288;
+constexpr int kBwdStageBytes = 8192;  // per input (dy, saved)
+
+constexpr int kMaxBulkDim = 1024;  // gamma staged as fp32 after the ring and the barriers
+
+template <int STAGE_BYTES, int INPUTS>
+constexpr int bulk_smem_bytes() {
+  return kStages * STAGE_BYTES * INPUTS + 128 + kMaxBulkDim * 4;
+}
+
+// gamma as fp32 into shared memory (whole CTA; followed by the caller's barrier)
+__device__ __forceinline__ void stage_gamma(const void* gamma, int gcode, int dim, float* g_s) {
+  for (int c = threadIdx.x; c < dim; c += kThreads) g_s[c] = ld_dyn(gamma, c, gcode);
+}
+
+// Lane layout of the bulk kernels: G lanes per row (G = 8, 16 or 32), so a
+// warp works on 32 / G rows at once and every lane is busy; lane l of a row
+// group owns the 16-byte vectors l, l + G, ... (NJ of them).
+template <int G>
+__device__ __forceinline__ float group_sum(float v) {
+#pragma unroll
+  for (int o = G / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+template <typename Tx, typename To, int V, int G, int NJ>
+__global__ void __launch_bounds__(kThreads, 4)
+    rms_fwd_bulk(const Tx* __restrict__ x, const void* __restrict__ gamma, int gcode, To* __restrict__ out,
+                 To* __restrict__ normed, float* __restrict__ inv_norm, int64_t rows, int dim, int rpt) {
+  constexpr int RW = 32 / G;  // rows per warp step
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kFwdStageBytes);
+  float* g_s = reinterpret_cast<float*>(smem + kStages * kFwdStageBytes + 128);
+  const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+  const int gl = lane % G, sub = lane / G;
+  stage_gamma(gamma, gcode, dim, g_s);
+  const int nvec = dim / V;
+  const float scale = sqrtf((float)dim);
+  const int64_t tiles = (rows + rpt - 1) / rpt;
+  if (threadIdx.x == 0) {
+    for (int st = 0; st < kStages; ++st) umma::mbar_init(&full[st], 1);
+    umma::fence_barrier_init();
+  }
+  __syncthreads();
+  auto issue = [&](int64_t tile, int st) {
+    const int64_t r0 = tile * rpt;
+    const int64_t n = rows - r0 < rpt ? rows - r0 : rpt;
+    const uint32_t bytes = (uint32_t)(n * dim * (int64_t)sizeof(Tx));
+    umma::mbar_arrive_expect_tx(&full[st], bytes);
+    umma::bulk_load(smem + st * kFwdStageBytes, x + r0 * dim, bytes, &full[st]);
+  };
+  if (threadIdx.x == 0)
+    for (int st = 0; st < kStages; ++st) {
+      const int64_t t = blockIdx.x + (int64_t)st * gridDim.x;
+      if (t < tiles) issue(t, st);
+    }
+  int it = 0;
+  for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++it) {
+    const int st = it % kStages;
+    if (!umma::mbar_wait(&full[st], (it / kStages) & 1, 0x21)) break;
+    Tx* xs = reinterpret_cast<Tx*>(smem + st * kFwdStageBytes);
+    const int64_t r0 = tile * rpt;
+    const int n = rows - r0 < rpt ? (int)(rows - r0) : rpt;
+    for (int qb = wib * RW; qb < n; qb += kWarps * RW) {
+      const int q = qb + sub;
+      const bool live = q < n;
+      float v[NJ][V];
+      float ss = 0.f;
+#pragma unroll
+      for (int j = 0; j < NJ; ++j) {
+        const int vi = j * G + gl;
+        if (live && vi < nvec) {
+          const Pack<Tx, V> p = *reinterpret_cast<const Pack<Tx, V>*>(xs + q * dim + vi * V);
+#pragma unroll
+          for (int e = 0; e < V; ++e) {
+            v[j][e] = Elem<Tx>::to_f(p.v[e]);
+            ss += v[j][e] * v[j][e];
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < V; ++e) v[j][e] = 0.f;
+        }
+      }
+      ss = group_sum<G>(ss);
+      if (!live) continue;
+      const int64_t r = r0 + q;
+      const float inv = 1.0f / fmaxf(sqrtf(ss), 1.0e-12f);
+      if (gl == 0) inv_norm[r] = inv;
+      const float k = inv * scale;
+#pragma unroll
+      for (int j = 0; j < NJ; ++j) {
+        const int vi = j * G + gl;
+        if (vi < nvec) {
+          Pack<To, V> po, pn;
+          const float* gv = g_s + vi * V;
+#pragma unroll
+          for (int e = 0; e < V; ++e) {
+            const float nrm = v[j][e] * k;
+            pn.v[e] = Elem<To>::from_f(nrm);
+            po.v[e] = Elem<To>::from_f(nrm * gv[e]);
+          }
+          // out goes back over this lane's own x elements (sizeof(To) == sizeof(Tx)) and leaves by bulk store
+          *reinterpret_cast<Pack<To, V>*>(reinterpret_cast<To*>(xs) + q * dim + vi * V) = po;
+          if (normed != nullptr) *reinterpret_cast<Pack<To, V>*>(normed + r * dim + (int64_t)vi * V) = pn;
+        }
+      }
+    }
+    umma::fence_proxy_async_smem();
+    __syncthreads();  // every warp is done with stage st
+    if (threadIdx.x == 0) {
+      umma::bulk_store(out + r0 * dim, xs, (uint32_t)(n * dim * (int64_t)sizeof(To)));
+      umma::bulk_commit();
+      const int64_t nt = tile + (int64_t)kStages * gridDim.x;
+      if (nt < tiles) {
+        umma::bulk_wait_read_all();  // the store has read the stage before the next load refills it
+        issue(nt, st);
+      }
+    }
+  }
+  if (threadIdx.x == 0) umma::bulk_wait_all();
+}
+
+template <typename Tg, typename Tdx, int V, int G, int NJ>
+__global__ void __launch_bounds__(kThreads, 3)
+    rms_bwd_bulk(const Tg* __restrict__ dy, const Tg* __restrict__ saved, int saved_is_input,
+                 const float* __restrict__ inv_norm, const void* __restrict__ gamma, int gcode, Tdx* __restrict__ dx,
+                 float* __restrict__ partial, int64_t rows, int dim, int rpt) {
+  constexpr int RW = 32 / G;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kBwdStageBytes * 2);
+  float* g_s = reinterpret_cast<float*>(smem + kStages * kBwdStageBytes * 2 + 128);
+  float* red = reinterpret_cast<float*>(smem);  // reused after the ring drains: [kWarps * RW][dim]
+  const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+  const int gl = lane % G, sub = lane / G;
+  stage_gamma(gamma, gcode, dim, g_s);
+  const int nvec = dim / V;
+  const float scale = sqrtf((float)dim);
+  const int64_t tiles = (rows + rpt - 1) / rpt;
+  if (threadIdx.x == 0) {
+    for (int st = 0; st < kStages; ++st) umma::mbar_init(&full[st], 1);
+    umma::fence_barrier_init();
+  }
+  __syncthreads();
+  auto issue = [&](int64_t tile, int st) {
+    const int64_t r0 = tile * rpt;
+    const int64_t n = rows - r0 < rpt ? rows - r0 : rpt;
+    const uint32_t bytes = (uint32_t)(n * dim * (int64_t)sizeof(Tg));
+    uint8_t* base = smem + st * kBwdStageBytes * 2;
+    umma::mbar_arrive_expect_tx(&full[st], 2 * bytes);
+    umma::bulk_load(base, dy + r0 * dim, bytes, &full[st]);
+    umma::bulk_load(base + kBwdStageBytes, saved + r0 * dim, bytes, &full[st]);
+  };
+  if (threadIdx.x == 0)
+    for (int st = 0; st < kStages; ++st) {
+      const int64_t t = blockIdx.x + (int64_t)st * gridDim.x;
+      if (t < tiles) issue(t, st);
+    }
+  float acc[NJ][V];
+#pragma unroll
+  for (int j = 0; j < NJ; ++j)
+#pragma unroll
+    for (int e = 0; e < V; ++e) acc[j][e] = 0.f;
+  int it = 0;
+  for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++it) {
+    const int st = it % kStages;
+    const int64_t r0 = tile * rpt;
+    const int n = rows - r0 < rpt ? (int)(rows - r0) : rpt;
+    // this warp's row norms for the tile, one load per lane, before the wait
+    const int qi = wib * RW + (lane / RW) * kWarps * RW + (lane % RW);
+    const float inv_l = qi < n ? inv_norm[r0 + qi] : 0.f;
+    if (!umma::mbar_wait(&full[st], (it / kStages) & 1, 0x22)) break;
+    Tg* ds_ = reinterpret_cast<Tg*>(smem + st * kBwdStageBytes * 2);
+    const Tg* ss_ = reinterpret_cast<const Tg*>(smem + st * kBwdStageBytes * 2 + kBwdStageBytes);
+    int step = 0;
+    for (int qb = wib * RW; qb < n; qb += kWarps * RW, ++step) {
+      const int q = qb + sub;
+      const bool live = q < n;
+      // row q = wib*RW + step*kWarps*RW + sub is held by lane step*RW + sub
+      const float inv = __shfl_sync(0xffffffffu, inv_l, (step * RW + sub) & 31);
+      const float nk = saved_is_input ? inv * scale : 1.0f;
+      // pass 1: row dot product (gamma-weighted) and the grad_gamma terms
+      float dot = 0.f;
+#pragma unroll
+      for (int j = 0; j < NJ; ++j) {
+        const int vi = j * G + gl;
+        if (live && vi < nvec) {
+          const Pack<Tg, V> pd = *reinterpret_cast<const Pack<Tg, V>*>(ds_ + q * dim + vi * V);
+          const Pack<Tg, V> ps = *reinterpret_cast<const Pack<Tg, V>*>(ss_ + q * dim + vi * V);
+          const float* gv = g_s + vi * V;
+#pragma unroll
+          for (int e = 0; e < V; ++e) {
+            const float d = Elem<Tg>::to_f(pd.v[e]);
+            const float nn = Elem<Tg>::to_f(ps.v[e]) * nk;
+            dot += d * gv[e] * nn;
+            acc[j][e] += d * nn;
+          }
+        }
+      }
+      dot = group_sum<G>(dot);
+      // pass 2: grad_x from the staged row again
+      if (dx != nullptr && live) {
+        const float dsc = dot / scale;
+#pragma unroll
+        for (int j = 0; j < NJ; ++j) {
+          const int vi = j * G + gl;
+          if (vi < nvec) {
+            const Pack<Tg, V> pd = *reinterpret_cast<const Pack<Tg, V>*>(ds_ + q * dim + vi * V);
+            const Pack<Tg, V> ps = *reinterpret_cast<const Pack<Tg, V>*>(ss_ + q * dim + vi * V);
+            const float* gv = g_s + vi * V;
+            Pack<Tdx, V> p;
+#pragma unroll
+            for (int e = 0; e < V; ++e) {
+              const float d = Elem<Tg>::to_f(pd.v[e]);
+              const float nn = Elem<Tg>::to_f(ps.v[e]) * nk;
+              p.v[e] = Elem<Tdx>::from_f(inv * (d * gv[e] * scale - nn * dsc));
+            }
+            // dx goes back over this lane's own dy elements (sizeof(Tdx) == sizeof(Tg)), bulk-stored below
+            *reinterpret_cast<Pack<Tdx, V>*>(reinterpret_cast<Tdx*>(ds_) + q * dim + vi * V) = p;
+          }
+        }
+      }
+    }
+    umma::fence_proxy_async_smem();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      if (dx != nullptr) {
+        umma::bulk_store(dx + r0 * dim, ds_, (uint32_t)(n * dim * (int64_t)sizeof(Tdx)));
+        umma::bulk_commit();
+      }
+      const int64_t nt = tile + (int64_t)kStages * gridDim.x;
+      if (nt < tiles) {
+        if (dx != nullptr) umma::bulk_wait_read_all();
+        issue(nt, st);
+      }
+    }
+  }
+  if (threadIdx.x == 0) umma::bulk_wait_read_all();
+  // every stage has been consumed and read by its store; reuse the ring for
+  // the cross-warp reduction of the grad_gamma partials
+  __syncthreads();
+#pragma unroll
+  for (int j = 0; j < NJ; ++j) {
+    const int vi = j * G + gl;
+    if (vi < nvec) {
+#pragma unroll
+      for (int e = 0; e < V; ++e) red[(wib * RW + sub) * dim + vi * V + e] = acc[j][e];
+    }
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < dim; c += kThreads) {
+    float s2 = 0.f;
+    for (int w = 0; w < kWarps * RW; ++w) s2 += red[w * dim + c];
+    partial[(int64_t)blockIdx.x * dim + c] = s2;
+  }
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 int grid_for_rows(int64_t rows, int64_t cap) {
@@ -282,7 +548,29 @@ int launch_fwd(const void* x, const void* gamma, int gcode, void* out, void* nor
   const Tx* xp = static_cast<const Tx*>(x);
   To* op = static_cast<To*>(out);
   To* np = static_cast<To*>(normed);
-  if (vec_ok && nj * 32 * V <= 1024) {
+  const int64_t row_bytes = dim * (int64_t)sizeof(Tx);
+  if (vec_ok && sizeof(Tx) == sizeof(To) && dim <= kMaxBulkDim && row_bytes <= kFwdStageBytes) {
+    const int rpt = (int)(kFwdStageBytes / row_bytes);
+    const int64_t tiles = (rows + rpt - 1) / rpt;
+    int g = (int)(tiles < (int64_t)num_sms() * 4 ? tiles : (int64_t)num_sms() * 4);
+    constexpr int smem = bulk_smem_bytes<kFwdStageBytes, 1>();
+    auto go = [&](auto kern) {
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      kern<<<g, kThreads, smem, stream>>>(xp, gamma, gcode, op, np, inv, rows, (int)dim, rpt);
+    };
+    if (nvec <= 8)
+      go(rms_fwd_bulk<Tx, To, V, 8, 1>);
+    else if (nvec <= 24)
+      go(rms_fwd_bulk<Tx, To, V, 8, 3>);
+    else if (nvec <= 48)
+      go(rms_fwd_bulk<Tx, To, V, 16, 3>);
+    else if (nvec <= 64)
+      go(rms_fwd_bulk<Tx, To, V, 32, 2>);
+    else if (nvec <= 128)
+      go(rms_fwd_bulk<Tx, To, V, 32, 4>);
+    else if constexpr (V == 4)
+      go(rms_fwd_bulk<Tx, To, V, 32, 8>);
+  } else if (vec_ok && nj * 32 * V <= 1024) {
     if (nj <= 1)
       rms_fwd_vec<Tx, To, V, 1><<<grid, kThreads, 0, stream>>>(xp, gamma, gcode, op, np, inv, rows, (int)dim);
     else if (nj <= 2)
@@ -314,8 +602,36 @@ int launch_bwd(const void* dy, const void* saved, int saved_is_input, const floa
   const Tg* sp = static_cast<const Tg*>(saved);
   Tdx* dxp = static_cast<Tdx*>(dx);
   const size_t smem = (size_t)kWarps * dim * sizeof(float);
+  int used_grid = grid;  // CTAs writing grad_gamma partial rows
   // Register budget: at most 1024 elements of a row per warp in the vector path.
-  if (vec_ok && nj * 32 * V <= 1024 && smem <= 48 * 1024) {
+  const int64_t row_bytes = dim * (int64_t)sizeof(Tg);
+  if (vec_ok && sizeof(Tg) == sizeof(Tdx) && dim <= kMaxBulkDim && row_bytes <= kBwdStageBytes &&
+      (int64_t)kWarps * 4 * dim * 4 <= (int64_t)kStages * kBwdStageBytes * 2) {
+    const int rpt = (int)(kBwdStageBytes / row_bytes);
+    const int64_t tiles = (rows + rpt - 1) / rpt;
+    int64_t g = (int64_t)num_sms() * 3;  // 3 CTAs of 64 KB shared memory per SM
+    if (g > kMaxBwdBlocks) g = kMaxBwdBlocks;
+    if (g > tiles) g = tiles;
+    used_grid = (int)g;
+    constexpr int bsm = bulk_smem_bytes<kBwdStageBytes, 2>();
+    auto go = [&](auto kern) {
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bsm);
+      kern<<<used_grid, kThreads, bsm, stream>>>(dyp, sp, saved_is_input, inv, gamma, gcode, dxp, partial, rows,
+                                                 (int)dim, rpt);
+    };
+    if (nvec <= 8)
+      go(rms_bwd_bulk<Tg, Tdx, V, 8, 1>);
+    else if (nvec <= 24)
+      go(rms_bwd_bulk<Tg, Tdx, V, 8, 3>);
+    else if (nvec <= 48)
+      go(rms_bwd_bulk<Tg, Tdx, V, 16, 3>);
+    else if (nvec <= 64)
+      go(rms_bwd_bulk<Tg, Tdx, V, 32, 2>);
+    else if (nvec <= 128)
+      go(rms_bwd_bulk<Tg, Tdx, V, 32, 4>);
+    else if constexpr (V == 4)
+      go(rms_bwd_bulk<Tg, Tdx, V, 32, 8>);
+  } else if (vec_ok && nj * 32 * V <= 1024 && smem <= 48 * 1024) {
     if (nj <= 1)
       rms_bwd_vec<Tg, Tdx, V, 1><<<grid, kThreads, smem, stream>>>(dyp, sp, saved_is_input, inv, gamma, gcode, dxp,
                                                                    partial, rows, (int)dim);
@@ -334,7 +650,8 @@ int launch_bwd(const void* dy, const void* saved, int saved_is_input, const floa
   }
   PMB_CHECK_LAUNCH("pmb_rms_norm_backward");
   if (dgamma != nullptr) {
-    red::colsum_rows<<<red::colsum_rows_grid(dim), red::kThreads, 0, stream>>>(partial, grid, dim, dgamma, dgcode);
+    red::colsum_rows<<<red::colsum_rows_grid(dim), red::kThreads, 0, stream>>>(partial, used_grid, dim, dgamma,
+                                                                               dgcode);
     PMB_CHECK_LAUNCH("pmb_rms_norm_backward(grad_gamma)");
   }
   return PMB_OK;
