@@ -419,6 +419,35 @@ PMB_API int pmb_feed_forward_backward(const void* grad_out, const void* x, const
                                       void* stream);
 
 /* ------------------------------------------------------------------------
+ * BandSplit on the tcgen05 tensor cores (bf16 / fp16 activations; fp32 or
+ * activation-dtype parameters), same math as pmb_band_split_forward:
+ *   out[m, b, :] = (x_b * inv * sqrt(w_b) * gamma_b) W_b^T + bias_b.
+ * `normed_padded` [rows, Kp] holds the normalised band features with every
+ * band padded with zeros to a multiple of 64 columns (Kp = sizes[3]); it and
+ * inv_norm [rows, nb] are saved for the backward.  `packed_weights` [O, Kp]
+ * holds W_b * gamma_b in the activation dtype (written by the forward).
+ * The backward produces the parameter gradients (grad_biases nullable); the
+ * band features' own gradient is not produced (use pmb_band_split_backward
+ * when the input needs one).  pmb_band_split_tc_sizes fills sizes[0..3] =
+ * packed-weight bytes, normed_padded bytes, backward workspace bytes, Kp.
+ * out_features % 8 == 0.  Replaces the ragged band split's forward / weight
+ * backward (.cu:590-1003).
+ * ---------------------------------------------------------------------- */
+PMB_API int pmb_band_split_tc_sizes(int64_t rows, int num_bands, const int64_t* widths, int64_t out_features,
+                                    int dtype, int64_t* sizes);
+PMB_API int pmb_band_split_tc_forward(const void* x, int64_t rows, int64_t x_stride_row, int64_t x_stride_band,
+                                      int64_t x_stride_feat, int num_bands, const int64_t* widths,
+                                      const void* const* gammas, const void* const* weights,
+                                      const void* const* biases, int64_t out_features, void* packed_weights,
+                                      void* normed_padded, float* inv_norm, void* out, int dtype, int param_dtype,
+                                      void* stream);
+PMB_API int pmb_band_split_tc_backward(const void* grad_out, const void* normed_padded, int64_t rows,
+                                       int num_bands, const int64_t* widths, const void* const* gammas,
+                                       const void* const* weights, int64_t out_features, void* const* grad_gammas,
+                                       void* const* grad_weights, void* const* grad_biases, int dtype,
+                                       int param_dtype, void* workspace, int64_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
  * MaskEstimator MLP on the tcgen05 tensor cores (training path, bf16/fp16
  * activations, fp32 or 16-bit parameters): per band b,
  *   h_1 = tanh(x_b W_{1,b}^T + b_{1,b}), ..., h_L (hidden_layers of them),

@@ -43,6 +43,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "pmb_rows_pass_workspace_size": (_i64, [_i64, _i64]),
     "pmb_gelu_backward": (_i, [_p, _p, _p, _i64, _i64, _p, _i, _i, _p, _i64, _p]),
     "pmb_column_sum": (_i, [_p, _i64, _i64, _p, _i, _i, _p, _i64, _p]),
+    "pmb_band_split_tc_sizes": (_i, [_i64, _i, _p, _i64, _i, _p]),
+    "pmb_band_split_tc_forward": (
+        _i, [_p, _i64, _i64, _i64, _i64, _i, _p, _p, _p, _p, _i64, _p, _p, _p, _p, _i, _i, _p]),
+    "pmb_band_split_tc_backward": (
+        _i, [_p, _p, _i64, _i, _p, _p, _p, _i64, _p, _p, _p, _i, _i, _p, _i64, _p]),
     "pmb_rms_norm_forward": (_i, [_p, _p, _p, _p, _p, _i64, _i64, _i, _i, _i, _p]),
     "pmb_rms_norm_backward_workspace_size": (_i64, [_i64, _i64]),
     "pmb_rms_norm_backward": (_i, [_p, _p, _i, _p, _p, _p, _p, _i64, _i64, _i, _i, _i, _i, _p, _i64, _p]),

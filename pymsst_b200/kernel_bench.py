@@ -237,7 +237,54 @@ def op_sdpa(bench: _Bench):
                 print(f"sdpa {backend.name} n={n}: unavailable ({str(e).splitlines()[0][:80]})")
 
 
-OPS = {"gate": op_gate, "rms": op_rms, "qkv": op_qkv, "ff": op_ff, "sdpa": op_sdpa}
+def op_band(bench: _Bench):
+    """BandSplit (config-3 bands: 62 bands over 1025 stereo complex bins, 1032 rows, D = 192)."""
+    import ctypes
+
+    from .bands import DEFAULT_FREQS_PER_BANDS
+
+    dev, bf = bench.device, torch.bfloat16
+    widths = [4 * f for f in DEFAULT_FREQS_PER_BANDS]
+    nb, total, rows, D = len(widths), sum(widths), 1032, DIM
+    x = torch.randn(rows, total, device=dev, dtype=bf)
+    gam = [torch.ones(w, device=dev) for w in widths]
+    wts = [torch.randn(D, w, device=dev) / w ** 0.5 for w in widths]
+    bss = [torch.zeros(D, device=dev) for _ in widths]
+    warr = nat.i64_array(widths)
+    sizes = (ctypes.c_int64 * 4)()
+    nat.call("pmb_band_split_tc_sizes", rows, nb, warr, D, 2, sizes)
+    packed = nat.workspace(sizes[0], dev)
+    normed_p = torch.empty(rows, int(sizes[3]), device=dev, dtype=bf)
+    inv = torch.empty(rows, nb, device=dev)
+    out = torch.empty(rows, nb, D, device=dev, dtype=bf)
+    st = nat.stream_handle(dev)
+    pg, pw, pb = nat.ptr_array(gam), nat.ptr_array(wts), nat.ptr_array(bss)
+    flops = 2.0 * rows * total * D
+    byt = rows * total * 2 * 2 + total * D * 4 + rows * nb * D * 2
+    bench.time("band_split_tc_forward", lambda: nat.call(
+        "pmb_band_split_tc_forward", x.data_ptr(), rows, total, -1, 1, nb, warr, pg, pw, pb, D, packed.data_ptr(),
+        normed_p.data_ptr(), inv.data_ptr(), out.data_ptr(), 2, 0, st), byt, flops)
+    normed = torch.empty_like(x)
+    bench.time("band_split_forward (SIMT)", lambda: nat.call(
+        "pmb_band_split_forward", x.data_ptr(), rows, total, -1, 1, nb, warr, pg, pw, pb, D, out.data_ptr(),
+        normed.data_ptr(), inv.data_ptr(), 2, 0, st), byt, flops)
+    gy = torch.randn(rows, nb, D, device=dev, dtype=bf)
+    gg = [torch.empty_like(g) for g in gam]
+    gw = [torch.empty_like(w) for w in wts]
+    gb = [torch.empty_like(b) for b in bss]
+    ws = nat.workspace(sizes[2], dev)
+    bbyt = rows * nb * D * 2 + rows * total * 2 + total * D * 4 * 2
+    bench.time("band_split_tc_backward", lambda: nat.call(
+        "pmb_band_split_tc_backward", gy.data_ptr(), normed_p.data_ptr(), rows, nb, warr, pg, pw, D,
+        nat.ptr_array(gg), nat.ptr_array(gw), nat.ptr_array(gb), 2, 0, ws.data_ptr(), sizes[2], st), bbyt, flops)
+    swsb = nat.library().pmb_band_split_backward_workspace_size(rows, nb, warr, D, 0)
+    sws = nat.workspace(swsb, dev)
+    bench.time("band_split_backward (SIMT)", lambda: nat.call(
+        "pmb_band_split_backward", gy.data_ptr(), normed.data_ptr(), inv.data_ptr(), rows, nb, warr, pg, pw, D, None,
+        nat.ptr_array(gg), nat.ptr_array(gw), nat.ptr_array(gb), 2, 0, sws.data_ptr(), swsb, st), bbyt, flops)
+
+
+OPS = {"gate": op_gate, "band": op_band, "rms": op_rms, "qkv": op_qkv, "ff": op_ff, "sdpa": op_sdpa}
 
 
 def main(argv=None) -> None:
