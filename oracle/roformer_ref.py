@@ -58,7 +58,7 @@ class RotaryEmbedding(nn.Module):
 
     def rotate(self, t):  # t [..., n, d]
         n = t.shape[-2]
-        ang = torch.arange(n, dtype=self.freqs.dtype)[:, None] * self.freqs[None, :]
+        ang = torch.arange(n, dtype=self.freqs.dtype, device=self.freqs.device)[:, None] * self.freqs[None, :]
         cos, sin = ang.cos().to(t.dtype), ang.sin().to(t.dtype)
         e, o = t[..., 0::2], t[..., 1::2]
         return torch.stack((e * cos - o * sin, o * cos + e * sin), dim=-1).flatten(-2)

@@ -97,25 +97,61 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
-// packed[n, poff_b + k] = W_b[n, k] * gamma_b[k] (k < w_b), else 0.
+// Contiguous features (s_feat == 1, ragged): one CTA per row.  The row is
+// staged in shared memory with 4-byte loads (rows need not be 16-byte
+// aligned), then warp w handles bands w, w + 8, ...: sum of squares from
+// shared memory, and the padded normalised segment written with coalesced
+// stores.
+template <typename T>
+__global__ void __launch_bounds__(kThreads)
+    norm_padded_rows(const T* __restrict__ x, int64_t rows, int64_t s_row, BandCols bc, T* __restrict__ normed_p,
+                     float* __restrict__ inv_norm) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  T* xs = reinterpret_cast<T*>(smem_raw);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const T* xr = x + r * s_row;
+    // total is even for 16-bit bands of 4-element multiples; copy pairs when aligned
+    if ((reinterpret_cast<uintptr_t>(xr) & 3) == 0 && (bc.total & 1) == 0) {
+      const uint32_t* src = reinterpret_cast<const uint32_t*>(xr);
+      uint32_t* dst = reinterpret_cast<uint32_t*>(xs);
+      for (int i = threadIdx.x; i < bc.total / 2; i += kThreads) dst[i] = src[i];
+    } else {
+      for (int i = threadIdx.x; i < bc.total; i += kThreads) xs[i] = xr[i];
+    }
+    __syncthreads();
+    for (int b = warp; b < bc.nb; b += kThreads / 32) {
+      const int w = bc.w[b];
+      const T* xb = xs + bc.off[b];
+      float ss = 0.f;
+      for (int i = lane; i < w; i += 32) {
+        const float v = Elem<T>::to_f(xb[i]);
+        ss += v * v;
+      }
+      ss = warp_sum(ss);
+      const float inv = 1.0f / fmaxf(sqrtf(ss), 1.0e-12f);
+      if (lane == 0) inv_norm[r * bc.nb + b] = inv;
+      const float k = inv * sqrtf((float)w);
+      T* nb_ = normed_p + r * bc.total_p + bc.poff[b];
+      for (int i = lane; i < bc.kp[b]; i += 32) nb_[i] = Elem<T>::from_f(i < w ? Elem<T>::to_f(xb[i]) * k : 0.f);
+    }
+    __syncthreads();
+  }
+}
+
+// packed[n, poff_b + k] for band b = blockIdx.y: threads over k, rows n strided.
 template <typename T, typename TP>
 __global__ void __launch_bounds__(kThreads)
-    pack_weights(BandTable tab, BandCols bc, int64_t O, T* __restrict__ packed) {
-  const int64_t n_el = O * bc.total_p;
-  for (int64_t e = (int64_t)blockIdx.x * kThreads + threadIdx.x; e < n_el; e += (int64_t)gridDim.x * kThreads) {
-    const int64_t n = e / bc.total_p;
-    const int c = (int)(e - n * bc.total_p);
-    int lo = 0, hi = bc.nb - 1;
-    while (lo < hi) {
-      const int mid = (lo + hi + 1) >> 1;
-      if (bc.poff[mid] <= c) lo = mid; else hi = mid - 1;
-    }
-    const int b = lo, k = c - bc.poff[b];
-    float v = 0.f;
-    if (k < bc.w[b])
-      v = Elem<TP>::to_f(static_cast<const TP*>(tab.ptr1[b])[n * bc.w[b] + k]) *
-          Elem<TP>::to_f(static_cast<const TP*>(tab.ptr0[b])[k]);
-    packed[e] = Elem<T>::from_f(v);
+    pack_weights_band(BandTable tab, BandCols bc, int64_t O, T* __restrict__ packed) {
+  const int b = blockIdx.y;
+  const int w = bc.w[b], kp = bc.kp[b];
+  const TP* W = static_cast<const TP*>(tab.ptr1[b]);
+  const TP* g = static_cast<const TP*>(tab.ptr0[b]);
+  for (int64_t e = (int64_t)blockIdx.x * kThreads + threadIdx.x; e < O * kp; e += (int64_t)gridDim.x * kThreads) {
+    const int64_t n = e / kp;
+    const int k = (int)(e - n * kp);
+    const float v = k < w ? Elem<TP>::to_f(W[n * w + k]) * Elem<TP>::to_f(g[k]) : 0.f;
+    packed[n * bc.total_p + bc.poff[b] + k] = Elem<T>::from_f(v);
   }
 }
 
@@ -292,11 +328,25 @@ extern "C" int pmb_band_split_tc_forward(const void* x, int64_t rows, int64_t x_
       set_error("%s: fp32 activations are not supported", name);
       return PMB_ERR_UNSUPPORTED_DTYPE;
     } else {
-      norm_padded<T><<<grid_for(rows * num_bands, kThreads / 32), kThreads, 0, s>>>(
-          static_cast<const T*>(x), rows, lx, bc, static_cast<T*>(normed_padded), inv_norm);
+      const size_t row_smem = (size_t)bc.total * sizeof(T);
+      if (x_stride_band < 0 && x_stride_feat == 1 && row_smem <= 96 * 1024) {
+        if (row_smem > 48 * 1024)
+          PMB_CHECK_CUDA(cudaFuncSetAttribute(norm_padded_rows<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              (int)row_smem),
+                         name);
+        const int g = (int)(rows < (int64_t)num_sms() * 8 ? rows : (int64_t)num_sms() * 8);
+        norm_padded_rows<T><<<g, kThreads, row_smem, s>>>(static_cast<const T*>(x), rows, x_stride_row, bc,
+                                                            static_cast<T*>(normed_padded), inv_norm);
+      } else {
+        norm_padded<T><<<grid_for(rows * num_bands, kThreads / 32), kThreads, 0, s>>>(
+            static_cast<const T*>(x), rows, lx, bc, static_cast<T*>(normed_padded), inv_norm);
+      }
       PMB_CHECK_LAUNCH(name);
-      pack_weights<T, TP><<<grid_for(out_features * bc.total_p, kThreads), kThreads, 0, s>>>(
-          tab, bc, out_features, static_cast<T*>(packed_weights));
+      {
+        int bx = (int)((out_features * 64 + kThreads - 1) / kThreads);
+        dim3 pg((unsigned)(bx < 1 ? 1 : bx), (unsigned)num_bands);
+        pack_weights_band<T, TP><<<pg, kThreads, 0, s>>>(tab, bc, out_features, static_cast<T*>(packed_weights));
+      }
       PMB_CHECK_LAUNCH(name);
       CUtensorMap ma, mb;
       constexpr int BN = 256;

@@ -90,3 +90,18 @@ def test_config0_autocast_within_two_percent(cuda_device, dtype):
         ref_stems = ref(mix)
     rel = float((stems.float().cpu() - ref_stems).norm() / ref_stems.norm())
     assert rel < 2e-2, rel
+
+
+def test_loss_curve_100_steps_fp32(cuda_device):
+    """100-step seeded training run (Adam, fp32): the fused model's loss curve against the oracle model's on the
+    same weights and batches: mean abs diff <= 3.5e-5, max abs diff <= 1.7e-3 (the compare-direct bar)."""
+    from pymsst_b200.train import compare_loss_curves, run_loss_curve
+
+    ours, ref = _models("bs_roformer", CONFIG0_BSR, cuda_device)
+    batches = [synthetic.make_batch(1, 32768, seed=100 + i) for i in range(4)]
+    steps = [batches[i % len(batches)] for i in range(100)]
+    ours_curve = run_loss_curve(ours, steps, lr=1e-4, device=cuda_device)
+    ref_curve = run_loss_curve(ref.to(cuda_device), steps, lr=1e-4, device=cuda_device)
+    cmp = compare_loss_curves(ours_curve, ref_curve)
+    assert cmp["compared_points"] == 100
+    assert cmp["mean_abs_diff"] <= 3.5e-5 and cmp["max_abs_diff"] <= 1.7e-3, cmp
