@@ -42,7 +42,7 @@ sys.path.insert(0, str(REPO))
 from pymsst_b200 import _native as nat  # noqa: E402
 from pymsst_b200 import roofline as rl  # noqa: E402
 from pymsst_b200 import synthetic  # noqa: E402
-from pymsst_b200.train import CONFIGS, Trainer, build_model, init_distributed  # noqa: E402
+from pymsst_b200.train import CONFIGS, Trainer, build_model, init_distributed, max_over_ranks  # noqa: E402
 
 METRIC = "BSR train audio-sec/sec"
 UNIT = "audio-s/s"
@@ -236,10 +236,7 @@ def run_ours(args, rank: int, world: int, local: int):
     e2e_ms = e_start.elapsed_time(e_end)
     clocks = sampler.stop() if sampler else None
 
-    times = torch.tensor([value_ms, e2e_ms], dtype=torch.float64, device=device)
-    if world > 1:
-        dist.all_reduce(times, op=dist.ReduceOp.MAX)
-    value_ms, e2e_ms = float(times[0]), float(times[1])
+    value_ms, e2e_ms = max_over_ranks([value_ms, e2e_ms], device)
     audio_job = bench.audio_seconds_per_step * world * args.steps
     result = timer.result()
     if rank != 0:

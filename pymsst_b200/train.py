@@ -82,11 +82,11 @@ class Trainer:
             from torch.nn.parallel import DistributedDataParallel
 
             self.module = DistributedDataParallel(
-                self.model, device_ids=[self.device.index], bucket_cap_mb=bucket_cap_mb, gradient_as_bucket_view=True,
-                broadcast_buffers=False,
+                self.model, device_ids=[self.device.index] if self.device.type == "cuda" else None,
+                bucket_cap_mb=bucket_cap_mb, gradient_as_bucket_view=True, broadcast_buffers=False,
             )
         params = [p for p in self.model.parameters() if p.requires_grad]
-        self.optimizer = torch.optim.Adam(params, lr=lr, fused=fused_adam)
+        self.optimizer = torch.optim.Adam(params, lr=lr, fused=fused_adam and self.device.type == "cuda")
 
     def step(self, mixture: torch.Tensor, target: torch.Tensor) -> torch.Tensor:
         """One training step on device tensors; returns the detached loss (device)."""
@@ -127,6 +127,14 @@ def compare_loss_curves(a: list[float], b: list[float]) -> dict:
         raise ValueError("no overlapping loss points to compare")
     diffs = [abs(x - y) for x, y in zip(a[:n], b[:n])]
     return {"compared_points": n, "mean_abs_diff": sum(diffs) / n, "max_abs_diff": max(diffs)}
+
+
+def max_over_ranks(values: list[float], device: torch.device) -> list[float]:
+    """Element-wise max of per-rank timings (the job's time is its slowest rank's)."""
+    t = torch.tensor(values, dtype=torch.float64, device=device)
+    if dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(v) for v in t.cpu()]
 
 
 def init_distributed(timeout_s: float = 120.0) -> tuple[int, int, int]:
