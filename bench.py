@@ -64,6 +64,11 @@ def parse():
     p.add_argument("--config", default="config3", choices=sorted(CONFIGS))
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--bucket-mb", type=float, default=1024.0,
+                   help="DDP gradient bucket size (MB); the default puts all gradients in one bucket reduced after "
+                        "the backward, which keeps NCCL off the SMs while the persistent kernels run")
+    p.add_argument("--eager", action="store_true",
+                   help="launch every kernel from Python each step instead of replaying the captured step graph")
     p.add_argument("--profile-range", action="store_true",
                    help="bracket the timed steps with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
     p.add_argument("--traffic-json", default=str(REPO / "profiles" / "traffic.json"),
@@ -188,7 +193,8 @@ def run_ours(args, rank: int, world: int, local: int):
     torch.backends.cuda.matmul.allow_tf32 = False
     torch.backends.cudnn.allow_tf32 = False
     model = build_model(bench, seed=0)
-    trainer = Trainer(model, lr=bench.lr, amp_dtype=bench.amp, distributed=world > 1, device=device)
+    trainer = Trainer(model, lr=bench.lr, amp_dtype=bench.amp, distributed=world > 1, device=device,
+                      bucket_cap_mb=args.bucket_mb, cuda_graph=not args.eager)
     pool = 2
     host = [synthetic.make_batch(bench.batch, bench.chunk, seed=1000 * rank + i, stems=bench.stems) for i in range(pool)]
     host = [(m.pin_memory(), t.pin_memory()) for m, t in host]
@@ -211,17 +217,19 @@ def run_ours(args, rank: int, world: int, local: int):
     launches0 = nat.library().pmb_launch_count()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
-    with nat.time_entries(TIMED_ENTRIES) as timer:
-        if args.profile_range:
-            torch.cuda.cudart().cudaProfilerStart()
-        start.record(stream)
-        for i in range(args.steps):
-            trainer.step(*dev[i % pool])
-        end.record(stream)
-        barrier()
-        if args.profile_range:
-            torch.cuda.cudart().cudaProfilerStop()
-    launches = nat.library().pmb_launch_count() - launches0
+    if args.profile_range:
+        torch.cuda.cudart().cudaProfilerStart()
+    start.record(stream)
+    for i in range(args.steps):
+        trainer.step(*dev[i % pool])
+    end.record(stream)
+    barrier()
+    if args.profile_range:
+        torch.cuda.cudart().cudaProfilerStop()
+    if trainer.cuda_graph:
+        launches = trainer.launches_per_step * args.steps
+    else:
+        launches = nat.library().pmb_launch_count() - launches0
     value_ms = start.elapsed_time(end)
 
     # end to end through the step API from pinned host buffers
@@ -235,6 +243,15 @@ def run_ours(args, rank: int, world: int, local: int):
     barrier()
     e2e_ms = e_start.elapsed_time(e_end)
     clocks = sampler.stop() if sampler else None
+
+    # per-kernel durations for the roofline: the same forward/backward launched eagerly, each entry point
+    # bracketed by CUDA events on its stream (graph replays launch the kernels without the host calls)
+    barrier()
+    with nat.time_entries(TIMED_ENTRIES) as timer:
+        for i in range(args.steps):
+            trainer.optimizer.zero_grad(set_to_none=True)
+            trainer._forward_backward(*dev[i % pool])
+        barrier()
 
     value_ms, e2e_ms = max_over_ranks([value_ms, e2e_ms], device)
     audio_job = bench.audio_seconds_per_step * world * args.steps
@@ -264,6 +281,7 @@ def run_ours(args, rank: int, world: int, local: int):
         "e2e": {"value": round(audio_job / (e2e_ms / 1e3), 3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": 4},
         "gpu_launches": int(launches),
+        "step_launch": "cuda graph replay" if trainer.cuda_graph else "eager",
         "roofline": roof,
         "fused_op_ms": per_entry,
         "clocks": clocks,

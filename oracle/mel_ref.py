@@ -91,9 +91,10 @@ def recombine(mask: torch.Tensor, stft: torch.Tensor, index: torch.Tensor, multi
     b, s, f, t, _ = stft.shape
     n = mask.shape[1]
     m = mask.reshape(b, n, t, -1, 2).permute(0, 1, 3, 2, 4)  # [B,N,J,T,2]
-    summed = torch.zeros(b, n, f * s, t, 2, dtype=mask.dtype)
+    summed = torch.zeros(b, n, f * s, t, 2, dtype=mask.dtype, device=mask.device)
     summed.index_add_(2, index, m)
-    count = torch.zeros(f * s, dtype=mask.dtype).index_add_(0, index, torch.ones(index.numel(), dtype=mask.dtype))
+    count = torch.zeros(f * s, dtype=mask.dtype, device=mask.device).index_add_(
+        0, index, torch.ones(index.numel(), dtype=mask.dtype, device=mask.device))
     avg = summed / count.clamp_min(1e-8)[None, None, :, None, None]
     avg = avg.reshape(b, n, f, s, t, 2).permute(0, 1, 3, 2, 4, 5)  # [B,N,S,F,T,2]
     if not multiply:

@@ -53,6 +53,28 @@ from .fused import (
 DEFAULT_FREQS_PER_BANDS = band_tables.DEFAULT_FREQS_PER_BANDS
 
 
+def _istft_overlap_add(z, n_fft, hop, window, normalized, length):
+    """Inverse STFT (center=True, onesided) as torch.istft computes it -- inverse real FFT of each frame,
+    window, overlap-add, division by the overlap-added squared window, centre trim -- without torch.istft's
+    host-side check of the window envelope, so a captured CUDA graph can contain it.  z [B, F, T] complex."""
+    frames = torch.fft.irfft(z, n=n_fft, dim=-2, norm="ortho" if normalized else "backward")  # [B, n_fft, T]
+    win = window
+    if win.shape[0] < n_fft:
+        left = (n_fft - win.shape[0]) // 2
+        win = F.pad(win, (left, n_fft - win.shape[0] - left))
+    t = frames.shape[-1]
+    total = n_fft + hop * (t - 1)
+    y = F.fold(frames * win[:, None], output_size=(1, total), kernel_size=(1, n_fft), stride=(1, hop))
+    env = F.fold((win * win)[:, None].expand(n_fft, t)[None], output_size=(1, total), kernel_size=(1, n_fft),
+                 stride=(1, hop))
+    start = n_fft // 2
+    end = start + length if length is not None else total - n_fft // 2
+    y = y.reshape(y.shape[0], total)[:, start:end] / env.reshape(total)[start:end]
+    if length is not None and y.shape[-1] < length:
+        y = F.pad(y, (0, length - y.shape[-1]))
+    return y
+
+
 class RMSNorm(nn.Module):
     def __init__(self, dim: int):
         super().__init__()
@@ -320,7 +342,8 @@ class _Roformer(nn.Module):
         b, n, s, f, t, _ = spec.shape
         z = torch.view_as_complex(spec.reshape(b * n * s, f, t, 2))
         with torch.autocast("cuda", enabled=False):
-            audio = torch.istft(z, **self.stft_kwargs, window=window, return_complex=False, length=length)
+            audio = _istft_overlap_add(z, self.stft_kwargs["n_fft"], self.stft_kwargs["hop_length"], window,
+                                       self.stft_kwargs["normalized"], length)
         audio = audio.reshape(b, n, s, -1)
         return audio[:, 0] if n == 1 else audio
 

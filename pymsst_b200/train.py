@@ -68,17 +68,31 @@ def build_model(bench: BenchConfig, seed: int = 0) -> torch.nn.Module:
 
 
 class Trainer:
-    """Owns the model (optionally DDP-wrapped) and its Adam optimizer."""
+    """Owns the model (optionally data-parallel) and its Adam optimizer.
+
+    ``cuda_graph=True`` captures the whole training step (forward, backward,
+    gradient all-reduce, Adam) once into a CUDA graph and replays it; the
+    step is then free of per-kernel host launch cost, which otherwise bounds
+    a training step of this size.  The first call runs three untimed
+    forward/backward passes on its batch (no parameter update) so every
+    library plan and cached table exists before the capture, initialises the
+    Adam state with an update of zero, and then captures; every call,
+    including the first, applies exactly one Adam update.  With more than one
+    rank the graph all-reduces the flattened gradients itself (one NCCL call,
+    mean over ranks) instead of wrapping the model in DDP.  Input shapes must
+    stay fixed; the returned loss tensor is overwritten by the next step."""
 
     def __init__(self, model: torch.nn.Module, *, lr: float = 1e-4, amp_dtype: torch.dtype | None = None,
                  grad_clip: float = 0.0, distributed: bool = False, device: torch.device | None = None,
-                 fused_adam: bool = True, bucket_cap_mb: float = 64.0):
+                 fused_adam: bool = True, bucket_cap_mb: float = 64.0, cuda_graph: bool = False):
         self.device = device or torch.device("cuda", torch.cuda.current_device())
         self.model = model.to(self.device)
         self.amp_dtype = amp_dtype
         self.grad_clip = float(grad_clip)
         self.module = self.model
-        if distributed:
+        self.distributed = distributed
+        self.cuda_graph = bool(cuda_graph) and self.device.type == "cuda"
+        if distributed and not self.cuda_graph:
             from torch.nn.parallel import DistributedDataParallel
 
             self.module = DistributedDataParallel(
@@ -86,24 +100,106 @@ class Trainer:
                 bucket_cap_mb=bucket_cap_mb, gradient_as_bucket_view=True, broadcast_buffers=False,
             )
         params = [p for p in self.model.parameters() if p.requires_grad]
-        self.optimizer = torch.optim.Adam(params, lr=lr, fused=fused_adam and self.device.type == "cuda")
+        self.params = params
+        on_cuda = self.device.type == "cuda"
+        self.optimizer = torch.optim.Adam(params, lr=lr, fused=fused_adam and on_cuda,
+                                          capturable=self.cuda_graph)
+        self._graph = None
+        self._static = None
+        self.launches_per_step = None  # this package's kernels in one captured step
 
-    def step(self, mixture: torch.Tensor, target: torch.Tensor) -> torch.Tensor:
-        """One training step on device tensors; returns the detached loss (device)."""
-        self.optimizer.zero_grad(set_to_none=True)
-        with torch.autocast("cuda", dtype=self.amp_dtype or torch.bfloat16, enabled=self.amp_dtype is not None):
+    # ------------------------------------------------------------- eager
+    def _forward_backward(self, mixture, target):
+        with torch.autocast("cuda", dtype=self.amp_dtype or torch.bfloat16, enabled=self.amp_dtype is not None,
+                            cache_enabled=not self.cuda_graph):
             loss = self.module(mixture, target)
         loss.backward()
+        return loss
+
+    def _allreduce_grads(self):
+        import torch.distributed as dist
+
+        grads = [p.grad for p in self.params if p.grad is not None]
+        flat = torch.cat([g.reshape(-1) for g in grads])
+        dist.all_reduce(flat)
+        flat.div_(dist.get_world_size())
+        off = 0
+        for g in grads:
+            n = g.numel()
+            g.copy_(flat[off:off + n].view_as(g))
+            off += n
+
+    def _update(self):
         if self.grad_clip:
             torch.nn.utils.clip_grad_norm_(self.model.parameters(), self.grad_clip)
         self.optimizer.step()
+
+    def step(self, mixture: torch.Tensor, target: torch.Tensor) -> torch.Tensor:
+        """One training step on device tensors; returns the detached loss (device)."""
+        if self.cuda_graph:
+            return self._graph_step(mixture, target)
+        self.optimizer.zero_grad(set_to_none=True)
+        loss = self._forward_backward(mixture, target)
+        self._update()
         return loss.detach()
+
+    # ------------------------------------------------------------- graph
+    def _capture(self, mixture, target):
+        from . import _native as nat
+
+        static_mix, static_tgt = mixture.clone(), target.clone()
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                self.optimizer.zero_grad(set_to_none=True)
+                self._forward_backward(static_mix, static_tgt)
+                if self.distributed:
+                    self._allreduce_grads()
+            # Adam state (moments, device step counters) created by an update of zero
+            for p in self.params:
+                p.grad = torch.zeros_like(p)
+            self.optimizer.step()
+            for group in self.optimizer.param_groups:
+                for p in group["params"]:
+                    st = self.optimizer.state[p]
+                    if "step" in st:
+                        st["step"].zero_()
+        torch.cuda.current_stream(self.device).wait_stream(side)
+        self.optimizer.zero_grad(set_to_none=True)
+        graph = torch.cuda.CUDAGraph()
+        before = nat.library().pmb_launch_count()
+        with torch.cuda.graph(graph):
+            loss = self._forward_backward(static_mix, static_tgt)
+            if self.distributed:
+                self._allreduce_grads()
+            self._update()
+        self.launches_per_step = int(nat.library().pmb_launch_count() - before)
+        self._graph = graph
+        self._static = (static_mix, static_tgt, loss.detach())
+
+    def _graph_step(self, mixture, target):
+        if self._graph is None:
+            self._capture(mixture, target)
+        static_mix, static_tgt, loss = self._static
+        if mixture.data_ptr() != static_mix.data_ptr():
+            static_mix.copy_(mixture, non_blocking=True)
+        if target.data_ptr() != static_tgt.data_ptr():
+            static_tgt.copy_(target, non_blocking=True)
+        self._graph.replay()
+        return loss
 
     def step_host(self, mixture: torch.Tensor, target: torch.Tensor, loss_out: torch.Tensor | None = None):
         """Step from host tensors (pinned for async copies); the loss is copied back to ``loss_out``."""
-        mix = mixture.to(self.device, non_blocking=True)
-        tgt = target.to(self.device, non_blocking=True)
-        loss = self.step(mix, tgt)
+        if self.cuda_graph and self._static is not None:
+            static_mix, static_tgt, _ = self._static
+            static_mix.copy_(mixture, non_blocking=True)
+            static_tgt.copy_(target, non_blocking=True)
+            loss = self._graph_step(static_mix, static_tgt)
+        else:
+            mix = mixture.to(self.device, non_blocking=True)
+            tgt = target.to(self.device, non_blocking=True)
+            loss = self.step(mix, tgt)
         if loss_out is None:
             return float(loss)
         loss_out.copy_(loss, non_blocking=True)
