@@ -52,7 +52,8 @@ TIMED_ENTRIES = [
     "pmb_band_recombine_forward", "pmb_band_recombine_backward", "pmb_band_split_forward",
     "pmb_band_split_backward", "pmb_grouped_linear_forward", "pmb_grouped_linear_backward",
     "pmb_mask_estimator_final_forward", "pmb_mask_estimator_final_backward", "pmb_mask_estimator_tc_forward",
-    "pmb_mask_estimator_tc_backward", "pmb_gemm_tc",
+    "pmb_mask_estimator_tc_backward", "pmb_gemm_tc", "pmb_qkv_linear_rotary_forward", "pmb_band_split_tc_forward",
+    "pmb_band_split_tc_backward", "pmb_gelu_forward", "pmb_gelu_backward", "pmb_column_sum",
 ]
 
 

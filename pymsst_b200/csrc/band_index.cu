@@ -18,106 +18,90 @@
 //              out = stft * m  (complex product)
 // For BS-RoFormer the index is the identity (non-overlapping bands).
 //
-// A CTA covers kTT = 4 consecutive frames so that every global access moves
-// at least 32 contiguous bytes (4 frames x 8-byte complex values); the
-// recombine stages the 4 mask rows in shared memory and reduces the
-// overlapping contributions there.
+// The STFT-side tensors are contiguous along frames, the feature-side ones
+// along j, so every kernel works on frame-contiguous runs:
+//   gather forward / recombine backward (one value per feature j): a CTA
+//     stages a 32 (j) x 32 (frame) tile in shared memory -- rows read along
+//     frames for each j's (f, s), written back along j -- so both sides move
+//     full 128-byte lines;
+//   gather backward / recombine forward (a sum over the features j that read
+//     pair (f, s)): a warp owns one pair and 32 consecutive frames, walks the
+//     pair's feature list (warp-uniform, in CSR order, so the sum order is
+//     fixed and the result deterministic) and writes 32 frames contiguously;
+//     the feature-side reads are frame-strided but the [B, T, J] features
+//     stay resident in the 126 MB L2.
 #include "common.cuh"
 
 namespace pmb {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kTT = 4;
 
 struct Dims {
   int64_t B, S, F, T, J, N;
 };
 
+constexpr int kTile = 32;
+
+// x[b, t, j, :] = stft[b, s_j, f_j, t, :]: CTA = 32 j x 32 frames of one batch item.
 template <typename T>
 __global__ void __launch_bounds__(kThreads)
     gather_fwd(const float* __restrict__ stft, const int* __restrict__ index, Dims d, T* __restrict__ x) {
-  const int64_t tiles_t = (d.T + kTT - 1) / kTT;
-  const int64_t b = blockIdx.x / tiles_t;
-  const int64_t t0 = (blockIdx.x % tiles_t) * kTT;
-  for (int64_t e = threadIdx.x; e < d.J * kTT; e += kThreads) {
-    const int tt = (int)(e % kTT);
-    const int64_t j = e / kTT;
-    const int64_t t = t0 + tt;
-    if (t >= d.T) continue;
-    const int fs = index[j];
-    const int64_t f = fs / d.S, s = fs % d.S;
-    const float2 v = *reinterpret_cast<const float2*>(stft + ((((b * d.S + s) * d.F + f) * d.T + t) << 1));
-    T* dst = x + ((b * d.T + t) * d.J + j) * 2;
-    dst[0] = Elem<T>::from_f(v.x);
-    dst[1] = Elem<T>::from_f(v.y);
+  __shared__ float2 tile[kTile][kTile + 1];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int64_t j0 = (int64_t)blockIdx.x * kTile, t0 = (int64_t)blockIdx.y * kTile, b = blockIdx.z;
+  for (int jj = ty; jj < kTile; jj += kThreads / 32) {
+    const int64_t j = j0 + jj, t = t0 + tx;
+    if (j < d.J && t < d.T) {
+      const int fs = index[j];
+      const int64_t f = fs / d.S, s = fs - f * d.S;
+      tile[jj][tx] = *reinterpret_cast<const float2*>(stft + ((((b * d.S + s) * d.F + f) * d.T + t) << 1));
+    }
+  }
+  __syncthreads();
+  for (int tt = ty; tt < kTile; tt += kThreads / 32) {
+    const int64_t t = t0 + tt, j = j0 + tx;
+    if (j < d.J && t < d.T) {
+      const float2 v = tile[tx][tt];
+      T* dst = x + ((b * d.T + t) * d.J + j) * 2;
+      dst[0] = Elem<T>::from_f(v.x);
+      dst[1] = Elem<T>::from_f(v.y);
+    }
   }
 }
 
-// grad_stft[b,s,f,t,c] = sum_{j in inv(f*S+s)} grad_x[b,t,j,c]
-template <typename T>
+// Pair-major sum over a pair's features for 32 frames: warp = one (f, s) pair.
+// MODE 0 (gather backward): out = sum_j src[b, t, j].
+// MODE 1 (recombine forward): out = (stft *) sum_j src[bn, t, j] / count.
+template <typename T, int MODE>
 __global__ void __launch_bounds__(kThreads)
-    gather_bwd(const T* __restrict__ gx, const int* __restrict__ inv_ptr, const int* __restrict__ inv_idx, Dims d,
-               float* __restrict__ gstft) {
-  extern __shared__ float rows[];  // [kTT][J*2]
-  const int64_t tiles_t = (d.T + kTT - 1) / kTT;
-  const int64_t b = blockIdx.x / tiles_t;
-  const int64_t t0 = (blockIdx.x % tiles_t) * kTT;
-  for (int64_t e = threadIdx.x; e < kTT * d.J * 2; e += kThreads) {
-    const int64_t tt = e / (d.J * 2), q = e % (d.J * 2);
-    rows[e] = (t0 + tt < d.T) ? Elem<T>::to_f(gx[(b * d.T + t0 + tt) * d.J * 2 + q]) : 0.f;
-  }
-  __syncthreads();
+    pair_sum(const T* __restrict__ src, const float* __restrict__ stft, const int* __restrict__ inv_ptr,
+             const int* __restrict__ inv_idx, Dims d, int multiply, float* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
   const int64_t FS = d.F * d.S;
-  for (int64_t e = threadIdx.x; e < FS * kTT; e += kThreads) {
-    const int tt = (int)(e % kTT);
-    const int64_t fs = e / kTT;
-    if (t0 + tt >= d.T) continue;
-    float re = 0.f, im = 0.f;
-    for (int k = inv_ptr[fs]; k < inv_ptr[fs + 1]; ++k) {
-      const int j = inv_idx[k];
-      re += rows[tt * d.J * 2 + 2 * j];
-      im += rows[tt * d.J * 2 + 2 * j + 1];
-    }
-    const int64_t f = fs / d.S, s = fs % d.S;
-    *reinterpret_cast<float2*>(gstft + ((((b * d.S + s) * d.F + f) * d.T + t0 + tt) << 1)) = make_float2(re, im);
+  const int64_t fs = (int64_t)blockIdx.y * (kThreads / 32) + (threadIdx.x >> 5);
+  const int64_t t = (int64_t)blockIdx.x * 32 + lane;
+  const int64_t bn = blockIdx.z;  // b (MODE 0) or b * N + n (MODE 1)
+  if (fs >= FS || t >= d.T) return;
+  const int k0 = inv_ptr[fs], k1 = inv_ptr[fs + 1];
+  const T* row = src + (bn * d.T + t) * d.J * 2;
+  float re = 0.f, im = 0.f;
+  for (int k = k0; k < k1; ++k) {
+    const int j = inv_idx[k];
+    re += Elem<T>::to_f(row[2 * j]);
+    im += Elem<T>::to_f(row[2 * j + 1]);
   }
-}
-
-// out[b,n,s,f,t] = (multiply ? stft[b,s,f,t] : 1) * sum_{j in inv} mask[b,n,t,j] / count
-template <typename T>
-__global__ void __launch_bounds__(kThreads)
-    recombine_fwd(const T* __restrict__ mask, const float* __restrict__ stft, const int* __restrict__ inv_ptr,
-                  const int* __restrict__ inv_idx, Dims d, int multiply, float* __restrict__ out) {
-  extern __shared__ float rows[];  // [kTT][J*2]
-  const int64_t tiles_t = (d.T + kTT - 1) / kTT;
-  const int64_t bn = blockIdx.x / tiles_t;  // b * N + n
-  const int64_t b = bn / d.N;
-  const int64_t t0 = (blockIdx.x % tiles_t) * kTT;
-  for (int64_t e = threadIdx.x; e < kTT * d.J * 2; e += kThreads) {
-    const int64_t tt = e / (d.J * 2), q = e % (d.J * 2);
-    rows[e] = (t0 + tt < d.T) ? Elem<T>::to_f(mask[(bn * d.T + t0 + tt) * d.J * 2 + q]) : 0.f;
-  }
-  __syncthreads();
-  const int64_t FS = d.F * d.S;
-  for (int64_t e = threadIdx.x; e < FS * kTT; e += kThreads) {
-    const int tt = (int)(e % kTT);
-    const int64_t fs = e / kTT;
-    const int64_t t = t0 + tt;
-    if (t >= d.T) continue;
-    const int k0 = inv_ptr[fs], k1 = inv_ptr[fs + 1];
-    float mr = 0.f, mi = 0.f;
-    for (int k = k0; k < k1; ++k) {
-      const int j = inv_idx[k];
-      mr += rows[tt * d.J * 2 + 2 * j];
-      mi += rows[tt * d.J * 2 + 2 * j + 1];
-    }
+  const int64_t f = fs / d.S, s = fs - f * d.S;
+  float2 o;
+  if (MODE == 0) {
+    o = make_float2(re, im);
+    *reinterpret_cast<float2*>(out + ((((bn * d.S + s) * d.F + f) * d.T + t) << 1)) = o;
+  } else {
     const float cnt = fmaxf((float)(k1 - k0), 1.0e-8f);
-    mr /= cnt;
-    mi /= cnt;
-    const int64_t f = fs / d.S, s = fs % d.S;
-    float2 o = make_float2(mr, mi);
+    const float mr = re / cnt, mi = im / cnt;
+    o = make_float2(mr, mi);
     if (multiply) {
+      const int64_t b = bn / d.N;
       const float2 v = *reinterpret_cast<const float2*>(stft + ((((b * d.S + s) * d.F + f) * d.T + t) << 1));
       o = make_float2(v.x * mr - v.y * mi, v.x * mi + v.y * mr);
     }
@@ -125,52 +109,44 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
-// grad_mask[b,n,t,j] = conj-chain of out = stft * avg:  g_avg = g * conj(stft)
-// (or g when multiply == 0), divided by count(index[j]).
+// grad_mask[b,n,t,j] = (g * conj(stft) or g) / count(index[j]), g = grad_out[b,n,s_j,f_j,t]:
+// CTA = 32 j x 32 frames, staged like gather_fwd.
 template <typename T>
 __global__ void __launch_bounds__(kThreads)
     recombine_bwd(const float* __restrict__ gout, const float* __restrict__ stft, const int* __restrict__ index,
                   const int* __restrict__ inv_ptr, Dims d, int multiply, T* __restrict__ gmask) {
-  const int64_t tiles_t = (d.T + kTT - 1) / kTT;
-  const int64_t bn = blockIdx.x / tiles_t;
+  __shared__ float2 tile[kTile][kTile + 1];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int64_t j0 = (int64_t)blockIdx.x * kTile, t0 = (int64_t)blockIdx.y * kTile, bn = blockIdx.z;
   const int64_t b = bn / d.N;
-  const int64_t t0 = (blockIdx.x % tiles_t) * kTT;
-  for (int64_t e = threadIdx.x; e < d.J * kTT; e += kThreads) {
-    const int tt = (int)(e % kTT);
-    const int64_t j = e / kTT;
-    const int64_t t = t0 + tt;
-    if (t >= d.T) continue;
-    const int fs = index[j];
-    const int64_t f = fs / d.S, s = fs % d.S;
-    const float cnt = fmaxf((float)(inv_ptr[fs + 1] - inv_ptr[fs]), 1.0e-8f);
-    const float2 g = *reinterpret_cast<const float2*>(gout + (((((bn * d.S + s) * d.F + f) * d.T) + t) << 1));
-    float2 r = g;
-    if (multiply) {
-      const float2 v = *reinterpret_cast<const float2*>(stft + ((((b * d.S + s) * d.F + f) * d.T + t) << 1));
-      r = make_float2(g.x * v.x + g.y * v.y, g.y * v.x - g.x * v.y);
+  for (int jj = ty; jj < kTile; jj += kThreads / 32) {
+    const int64_t j = j0 + jj, t = t0 + tx;
+    if (j < d.J && t < d.T) {
+      const int fs = index[j];
+      const int64_t f = fs / d.S, s = fs - f * d.S;
+      const float cnt = fmaxf((float)(inv_ptr[fs + 1] - inv_ptr[fs]), 1.0e-8f);
+      const float2 g = *reinterpret_cast<const float2*>(gout + (((((bn * d.S + s) * d.F + f) * d.T) + t) << 1));
+      float2 r = g;
+      if (multiply) {
+        const float2 v = *reinterpret_cast<const float2*>(stft + ((((b * d.S + s) * d.F + f) * d.T + t) << 1));
+        r = make_float2(g.x * v.x + g.y * v.y, g.y * v.x - g.x * v.y);
+      }
+      tile[jj][tx] = make_float2(r.x / cnt, r.y / cnt);
     }
-    T* dst = gmask + ((bn * d.T + t) * d.J + j) * 2;
-    dst[0] = Elem<T>::from_f(r.x / cnt);
-    dst[1] = Elem<T>::from_f(r.y / cnt);
+  }
+  __syncthreads();
+  for (int tt = ty; tt < kTile; tt += kThreads / 32) {
+    const int64_t t = t0 + tt, j = j0 + tx;
+    if (j < d.J && t < d.T) {
+      const float2 v = tile[tx][tt];
+      T* dst = gmask + ((bn * d.T + t) * d.J + j) * 2;
+      dst[0] = Elem<T>::from_f(v.x);
+      dst[1] = Elem<T>::from_f(v.y);
+    }
   }
 }
 
 bool check_dims(const Dims& d) { return d.B >= 0 && d.S > 0 && d.F > 0 && d.T >= 0 && d.J > 0 && d.N > 0; }
-
-int set_smem(const void* fn, size_t bytes, const char* name) {
-  if (bytes > 227 * 1024) {
-    set_error("%s: %zu bytes of staged rows exceed shared memory (J too large)", name, bytes);
-    return PMB_ERR_INVALID_ARGUMENT;
-  }
-  if (bytes > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
-    if (e != cudaSuccess) {
-      set_error("%s: cudaFuncSetAttribute failed: %s", name, cudaGetErrorString(e));
-      return PMB_ERR_CUDA;
-    }
-  }
-  return PMB_OK;
-}
 
 }  // namespace
 }  // namespace pmb
@@ -188,9 +164,9 @@ extern "C" int pmb_band_gather_forward(const float* stft, const int* index, int6
   PMB_REQUIRE(stft && index && x, "%s: NULL tensor argument", name);
   PMB_REQUIRE((reinterpret_cast<uintptr_t>(stft) & 7) == 0, "%s: stft must be 8-byte aligned", name);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int64_t grid = batch * ((frames + kTT - 1) / kTT);
+  const dim3 grid((unsigned)((pairs + kTile - 1) / kTile), (unsigned)((frames + kTile - 1) / kTile), (unsigned)batch);
   return PMB_DISPATCH(x_dtype, T, name, [&] {
-    gather_fwd<T><<<(unsigned)grid, kThreads, 0, s>>>(stft, index, d, static_cast<T*>(x));
+    gather_fwd<T><<<grid, kThreads, 0, s>>>(stft, index, d, static_cast<T*>(x));
     PMB_CHECK_LAUNCH(name);
     return PMB_OK;
   });
@@ -207,13 +183,11 @@ extern "C" int pmb_band_gather_backward(const void* grad_x, const int* inv_ptr, 
   PMB_REQUIRE(grad_x && inv_ptr && inv_idx && grad_stft, "%s: NULL tensor argument", name);
   PMB_REQUIRE((reinterpret_cast<uintptr_t>(grad_stft) & 7) == 0, "%s: grad_stft must be 8-byte aligned", name);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const size_t smem = (size_t)kTT * pairs * 2 * sizeof(float);
-  const int64_t grid = batch * ((frames + kTT - 1) / kTT);
+  const dim3 grid((unsigned)((frames + 31) / 32), (unsigned)((freqs * channels + kThreads / 32 - 1) / (kThreads / 32)),
+                  (unsigned)batch);
   return PMB_DISPATCH(x_dtype, T, name, [&] {
-    int st = set_smem((const void*)gather_bwd<T>, smem, name);
-    if (st) return st;
-    gather_bwd<T><<<(unsigned)grid, kThreads, smem, s>>>(static_cast<const T*>(grad_x), inv_ptr, inv_idx, d,
-                                                          grad_stft);
+    pair_sum<T, 0><<<grid, kThreads, 0, s>>>(static_cast<const T*>(grad_x), nullptr, inv_ptr, inv_idx, d, 0,
+                                             grad_stft);
     PMB_CHECK_LAUNCH(name);
     return PMB_OK;
   });
@@ -232,13 +206,11 @@ extern "C" int pmb_band_recombine_forward(const void* mask, const float* stft, c
   PMB_REQUIRE((reinterpret_cast<uintptr_t>(out) & 7) == 0 && (reinterpret_cast<uintptr_t>(stft) & 7) == 0,
               "%s: stft/out must be 8-byte aligned", name);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const size_t smem = (size_t)kTT * pairs * 2 * sizeof(float);
-  const int64_t grid = batch * stems * ((frames + kTT - 1) / kTT);
+  const dim3 grid((unsigned)((frames + 31) / 32), (unsigned)((freqs * channels + kThreads / 32 - 1) / (kThreads / 32)),
+                  (unsigned)(batch * stems));
   return PMB_DISPATCH(mask_dtype, T, name, [&] {
-    int st = set_smem((const void*)recombine_fwd<T>, smem, name);
-    if (st) return st;
-    recombine_fwd<T><<<(unsigned)grid, kThreads, smem, s>>>(static_cast<const T*>(mask), stft, inv_ptr, inv_idx, d,
-                                                             multiply_stft, out);
+    pair_sum<T, 1><<<grid, kThreads, 0, s>>>(static_cast<const T*>(mask), stft, inv_ptr, inv_idx, d, multiply_stft,
+                                             out);
     PMB_CHECK_LAUNCH(name);
     return PMB_OK;
   });
@@ -257,10 +229,11 @@ extern "C" int pmb_band_recombine_backward(const float* grad_out, const float* s
   PMB_REQUIRE((reinterpret_cast<uintptr_t>(grad_out) & 7) == 0 && (reinterpret_cast<uintptr_t>(stft) & 7) == 0,
               "%s: stft/grad_out must be 8-byte aligned", name);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int64_t grid = batch * stems * ((frames + kTT - 1) / kTT);
+  const dim3 grid((unsigned)((pairs + kTile - 1) / kTile), (unsigned)((frames + kTile - 1) / kTile),
+                  (unsigned)(batch * stems));
   return PMB_DISPATCH(mask_dtype, T, name, [&] {
-    recombine_bwd<T><<<(unsigned)grid, kThreads, 0, s>>>(grad_out, stft, index, inv_ptr, d, multiply_stft,
-                                                          static_cast<T*>(grad_mask));
+    recombine_bwd<T><<<grid, kThreads, 0, s>>>(grad_out, stft, index, inv_ptr, d, multiply_stft,
+                                               static_cast<T*>(grad_mask));
     PMB_CHECK_LAUNCH(name);
     return PMB_OK;
   });

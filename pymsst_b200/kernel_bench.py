@@ -284,7 +284,66 @@ def op_band(bench: _Bench):
         nat.ptr_array(gg), nat.ptr_array(gw), nat.ptr_array(gb), 2, 0, sws.data_ptr(), swsb, st), bbyt, flops)
 
 
-OPS = {"gate": op_gate, "band": op_band, "rms": op_rms, "qkv": op_qkv, "ff": op_ff, "sdpa": op_sdpa}
+def op_mel(bench: _Bench):
+    """Mel-band gather / scatter-add-average recombine (60 overlapping mel bands, stereo, batch 4 x 258 frames)."""
+    from . import bands
+    from . import extension as ext
+
+    dev = bench.device
+    index = bands.mel_band_index(44100, 2048, 60, channels=2)
+    tables = index.device_tables(dev)
+    b, t, f = 4, 258, 1025
+    j = int(tables["index"].numel())
+    stft = torch.randn(b, 2, f, t, 2, device=dev)
+    x = ext.band_gather(stft, tables, torch.bfloat16)
+    bench.time("band_gather_forward", lambda: ext.band_gather(stft, tables, torch.bfloat16),
+               b * t * j * 2 * (4 + 2) + 4 * j)
+    gx = torch.randn_like(x)
+    bench.time("band_gather_backward", lambda: ext.band_gather_backward(gx, tables, 2, f),
+               b * t * j * 2 * 2 + b * 2 * f * t * 2 * 4)
+    mask = torch.randn(b, 1, t, j * 2, device=dev, dtype=torch.bfloat16)
+    out = ext.band_recombine(mask, stft, tables, 2, f)
+    bench.time("band_recombine_forward", lambda: ext.band_recombine(mask, stft, tables, 2, f),
+               b * t * j * 2 * 2 + 2 * b * 2 * f * t * 8)
+    go = torch.randn_like(out)
+    bench.time("band_recombine_backward",
+               lambda: ext.band_recombine_backward(go, stft, tables, torch.bfloat16),
+               2 * b * 2 * f * t * 8 + b * t * j * 2 * 2)
+
+
+def op_mask(bench: _Bench):
+    """MaskEstimator on the tensor cores (config 3: 62 bands, dim 192, hidden 768, one hidden layer, 1032 rows)."""
+    from .bands import DEFAULT_FREQS_PER_BANDS
+    from .fused import MaskEstimatorTCFn
+
+    dev = bench.device
+    widths = [2 * 2 * f for f in DEFAULT_FREQS_PER_BANDS]
+    nb, rows, hid = len(widths), 1032, 4 * DIM
+    params = []
+    for w_in, w_out in ((DIM, hid), (hid, None)):
+        outs = [hid] * nb if w_out is not None else [2 * w for w in widths]
+        params += [torch.randn(o, w_in, device=dev) / w_in ** 0.5 for o in outs]
+        params += [torch.zeros(o, device=dev) for o in outs]
+    params = [p.requires_grad_() for p in params]
+    x = torch.randn(rows, nb, DIM, device=dev, dtype=torch.bfloat16)
+    flops = 2.0 * rows * (nb * DIM * hid + hid * 2 * sum(widths))
+    byt = rows * (nb * DIM + nb * hid + 3 * sum(widths)) * 2
+
+    def fwd():
+        with torch.no_grad():
+            MaskEstimatorTCFn.apply(x, widths, 1, hid, *params)
+
+    bench.time("mask_estimator_tc_forward", fwd, byt, flops)
+    xr = x.detach().requires_grad_()
+    gy = torch.randn(rows, sum(widths), device=dev, dtype=torch.bfloat16)
+
+    def fwd_bwd():
+        MaskEstimatorTCFn.apply(xr, widths, 1, hid, *params).backward(gy)
+
+    bench.time("mask_estimator_tc fwd+bwd", fwd_bwd, 3 * byt, 3 * flops)
+
+
+OPS = {"gate": op_gate, "band": op_band, "mel": op_mel, "mask": op_mask, "rms": op_rms, "qkv": op_qkv, "ff": op_ff, "sdpa": op_sdpa}
 
 
 def main(argv=None) -> None:

@@ -92,6 +92,39 @@ def work(name: str, a: tuple) -> tuple[float, float]:
         rows, nb, h, dt, pt = a[3], a[4], a[5], a[11], a[12]
         total = sum(_widths(a[6], nb))
         return rows * (2 * nb * h + 3 * total) * ES[dt] + 2 * 2 * total * (h + 1) * ES[pt], 8.0 * rows * h * total
+    if name == "pmb_qkv_linear_rotary_forward":
+        rows, dim, n, dt = a[4] * a[5], a[6], 3 * a[7] * a[8], a[13]
+        return (rows * dim + n * dim + rows * n) * ES[dt] + 2 * a[5] * a[8] // 2 * 4, 2.0 * rows * n * dim
+    if name == "pmb_band_split_tc_forward":
+        rows, nb, o, dt, pt = a[1], a[5], a[10], a[15], a[16]
+        total = sum(_widths(a[6], nb))
+        byt = 2 * rows * total * ES[dt] + rows * nb * (o * ES[dt] + 4) + (total * (o + 1) + nb * o) * ES[pt]
+        return byt, 2.0 * rows * total * o
+    if name == "pmb_band_split_tc_backward":
+        rows, nb, o, dt, pt = a[2], a[3], a[7], a[11], a[12]
+        total = sum(_widths(a[4], nb))
+        byt = rows * nb * o * ES[dt] + rows * total * ES[dt] + (2 * total * (o + 1) + 2 * nb * o) * ES[pt]
+        return byt, 2.0 * rows * total * o
+    if name in ("pmb_mask_estimator_tc_forward", "pmb_mask_estimator_tc_backward"):
+        fwd = name.endswith("forward")
+        rows, nb, dim, hid, layers = a[1 if fwd else 5], a[2 if fwd else 6], a[3 if fwd else 7], \
+            a[4 if fwd else 8], a[5 if fwd else 9]
+        widths = _widths(a[6 if fwd else 10], nb)
+        dt, pt = (a[13], a[14]) if fwd else (a[14], a[15])
+        total = sum(widths)
+        hin = hid if layers > 0 else dim
+        flops = 2.0 * rows * (nb * dim * hid * (layers > 0) + max(layers - 1, 0) * nb * hid * hid + 2 * total * hin)
+        params = nb * dim * hid * (layers > 0) + max(layers - 1, 0) * nb * hid * hid + 2 * total * hin
+        acts = rows * (nb * dim + layers * nb * hid + 2 * total + total)
+        if fwd:
+            return acts * ES[dt] + params * (ES[pt] + ES[dt]), flops
+        return (acts + rows * total) * ES[dt] + 2 * params * ES[pt], 2 * flops
+    if name == "pmb_gelu_forward":
+        return 2.0 * a[2] * ES[a[3]], 0.0
+    if name == "pmb_gelu_backward":
+        return 3.0 * a[3] * a[4] * ES[a[7]], 0.0
+    if name == "pmb_column_sum":
+        return 1.0 * a[1] * a[2] * ES[a[5]], 0.0
     return 0.0, 0.0
 
 
