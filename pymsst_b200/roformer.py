@@ -53,6 +53,26 @@ from .fused import (
 DEFAULT_FREQS_PER_BANDS = band_tables.DEFAULT_FREQS_PER_BANDS
 
 
+_ENVELOPES: dict = {}
+
+
+def _overlap_add(frames, hop):
+    """frames [B, n, T] -> [B, n + hop * (T - 1)]: frame t added at offset t * hop.  With n a multiple of hop
+    the frames are cut into n / hop hop-long pieces and summed as shifted, zero-padded copies (a few
+    contiguous passes whose backward is a slice); otherwise torch's fold."""
+    b, n, t = frames.shape
+    if n % hop == 0:
+        r = n // hop
+        pieces = frames.transpose(1, 2).reshape(b, t, r, hop)
+        y = None
+        for i in range(r):
+            part = F.pad(pieces[:, :, i, :], (0, 0, i, r - 1 - i))
+            y = part if y is None else y + part
+        return y.reshape(b, (t + r - 1) * hop)
+    total = n + hop * (t - 1)
+    return F.fold(frames, output_size=(1, total), kernel_size=(1, n), stride=(1, hop)).reshape(b, total)
+
+
 def _istft_overlap_add(z, n_fft, hop, window, normalized, length):
     """Inverse STFT (center=True, onesided) as torch.istft computes it -- inverse real FFT of each frame,
     window, overlap-add, division by the overlap-added squared window, centre trim -- without torch.istft's
@@ -64,12 +84,15 @@ def _istft_overlap_add(z, n_fft, hop, window, normalized, length):
         win = F.pad(win, (left, n_fft - win.shape[0] - left))
     t = frames.shape[-1]
     total = n_fft + hop * (t - 1)
-    y = F.fold(frames * win[:, None], output_size=(1, total), kernel_size=(1, n_fft), stride=(1, hop))
-    env = F.fold((win * win)[:, None].expand(n_fft, t)[None], output_size=(1, total), kernel_size=(1, n_fft),
-                 stride=(1, hop))
+    y = _overlap_add(frames * win[:, None], hop)
+    key = (n_fft, hop, t, win.device, win.data_ptr(), win._version)
+    env = _ENVELOPES.get(key)
+    if env is None:  # kept for the process lifetime: a captured step graph reads it on every replay
+        env = _overlap_add((win * win)[None, :, None].expand(1, n_fft, t).contiguous(), hop).reshape(total)
+        _ENVELOPES[key] = env
     start = n_fft // 2
     end = start + length if length is not None else total - n_fft // 2
-    y = y.reshape(y.shape[0], total)[:, start:end] / env.reshape(total)[start:end]
+    y = y[:, start:end] / env[start:end]
     if length is not None and y.shape[-1] < length:
         y = F.pad(y, (0, length - y.shape[-1]))
     return y
