@@ -284,9 +284,11 @@ PMB_API int pmb_mask_estimator_final_backward(const void* grad_out, const void* 
  * Attention output gate (per head):
  *   gate[r, h] = sigmoid(x[r,:] . weight[h,:] + bias[h])      [rows, H]
  *   out[r, h*Dh + d] = attn(r, h, d) * gate[r, h]              [rows, H*Dh]
- * attn element (r, h, d), r = bi*seq_len + n, at
+ * attn element (r, h, d) at
  *   bi*attn_stride_batch + n*attn_stride_seq + h*attn_stride_head + d,
- * so the [batch, H, seq, Dh] attention output is read in place.
+ * with r = (o*seq_len + n)*seq_inner + i and bi = o*seq_inner + i (seq_inner
+ * = 1: r = bi*seq_len + n), so the [batch, H, seq, Dh] attention output is
+ * read in place and x / out may stay in an axial transformer's other order.
  * x [rows, dim], weight [H, dim], bias [H]; H <= 16.
  * Replaces attention_gate_forward (.cpp:539-561; .cu:1778-1824, .cu:1922-1970).
  * ---------------------------------------------------------------------- */
@@ -294,7 +296,7 @@ PMB_API int pmb_attention_gate_forward(const void* attn, int64_t seq_len, int64_
                                        int64_t attn_stride_seq, int64_t attn_stride_head, const void* x,
                                        const void* weight, const void* bias, int64_t rows, int64_t heads,
                                        int64_t dim_head, int64_t dim, void* out, void* gate, int dtype,
-                                       int param_dtype, void* stream);
+                                       int param_dtype, int64_t seq_inner, void* stream);
 PMB_API int64_t pmb_attention_gate_backward_workspace_size(int64_t rows, int64_t heads, int64_t dim);
 /*
  * Backward: grad_out [rows, H*Dh] -> grad_attn (written with the attn
@@ -307,7 +309,7 @@ PMB_API int pmb_attention_gate_backward(const void* grad_out, const void* attn, 
                                         const void* gate, int64_t rows, int64_t heads, int64_t dim_head,
                                         int64_t dim, void* grad_attn, void* grad_x, void* grad_weight,
                                         void* grad_bias, int dtype, int param_dtype, void* workspace,
-                                        int64_t workspace_bytes, void* stream);
+                                        int64_t workspace_bytes, int64_t seq_inner, void* stream);
 
 /* ------------------------------------------------------------------------
  * Band index kernels between the STFT and the band feature layouts
@@ -346,17 +348,21 @@ PMB_API int pmb_band_recombine_backward(const float* grad_out, const float* stft
  * merge is the backward: grad_q/k/v [B, H, N, Dh] -> grad_qkv [B*N, 3*H*Dh]
  * with the inverse rotation; the three gradients share the element strides
  * (stride_batch, stride_head, stride_seq) with Dh contiguous, so both the
- * [B, H, N, Dh] and the [B, N, H, Dh] layouts are read in place.  Replaces qkv_to_bnhd + rotary_forward /
- * rotary_backward on q and k (fused_roformer.py:710-732, 793-818;
- * .cu:1077-1168) with one pass each way.
+ * [B, H, N, Dh] and the [B, N, H, Dh] layouts are read in place.
+ * seq_inner (>= 1, divides B) orders the qkv rows as (outer, position,
+ * inner): sequence = outer * seq_inner + inner index.  1 is the plain
+ * [B, N] row order; an axial transformer passes the other axis' extent so its
+ * activations never need a permuted copy.  Replaces qkv_to_bnhd +
+ * rotary_forward / rotary_backward on q and k (fused_roformer.py:710-732,
+ * 793-818; .cu:1077-1168) with one pass each way.
  * ---------------------------------------------------------------------- */
 PMB_API int pmb_qkv_rotary_split(const void* qkv, const float* cos, const float* sin, int64_t batch,
                                  int64_t seq_len, int64_t heads, int64_t dim_head, void* q, void* k, void* v,
-                                 int rotate_qk, int dtype, void* stream);
+                                 int rotate_qk, int dtype, int64_t seq_inner, void* stream);
 PMB_API int pmb_qkv_rotary_merge(const void* grad_q, const void* grad_k, const void* grad_v, const float* cos,
                                  const float* sin, int64_t batch, int64_t seq_len, int64_t heads,
                                  int64_t dim_head, void* grad_qkv, int rotate_qk, int dtype, int64_t stride_batch,
-                                 int64_t stride_head, int64_t stride_seq, void* stream);
+                                 int64_t stride_head, int64_t stride_seq, int64_t seq_inner, void* stream);
 
 /*
  * Attention input projection with the rotary embedding fused into the GEMM
@@ -365,7 +371,9 @@ PMB_API int pmb_qkv_rotary_merge(const void* grad_q, const void* grad_k, const v
  * layout) = the three thirds of x weight^T, q and k rotated as in
  * pmb_qkv_rotary_split (each projection value rounded to the activation
  * dtype before rotation).  The angle tables are TRANSPOSED here:
- * cos_t / sin_t fp32 [Dh/2, N].  dim % 8 == 0, Dh % 32 == 0.  The backward
+ * cos_t / sin_t fp32 [Dh/2, N].  x rows follow the seq_inner row order of
+ * pmb_qkv_rotary_split; the planes are always [sequence, N, H, Dh].
+ * dim % 8 == 0, Dh % 32 == 0.  The backward
  * is pmb_qkv_rotary_merge (which reads this layout in place) plus the two
  * projection GEMMs.  Replaces to_qkv + qkv_to_bnhd + rotary_forward
  * (fused_roformer.py:710-732, 793-818; .cu:1077-1128).
@@ -373,7 +381,7 @@ PMB_API int pmb_qkv_rotary_merge(const void* grad_q, const void* grad_k, const v
 PMB_API int pmb_qkv_linear_rotary_forward(const void* x, const void* weight, const float* cos_t,
                                           const float* sin_t, int64_t batch, int64_t seq_len, int64_t dim,
                                           int64_t heads, int64_t dim_head, void* q, void* k, void* v,
-                                          int rotate_qk, int dtype, void* stream);
+                                          int rotate_qk, int dtype, int64_t seq_inner, void* stream);
 
 /* ------------------------------------------------------------------------
  * GELU (exact erf form of torch.nn.GELU()) and column sums for the

@@ -34,7 +34,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "pmb_gemm_tc_wgrad_workspace_size": (_i64, [_i64, _i64, _i64]),
     "pmb_gemm_tc_wgrad": (_i, [_p, _i64, _p, _i64, _i64, _i64, _i64, _p, _i64, _i, _i, _p, _i64, _p]),
     "pmb_qkv_linear_rotary_forward": (
-        _i, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _i, _i, _p]),
+        _i, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _i, _i, _i64, _p]),
     "pmb_feed_forward_forward": (_i, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _p, _p, _p, _i, _i, _p]),
     "pmb_feed_forward_backward_workspace_size": (_i64, [_i64, _i64, _i64, _i]),
     "pmb_feed_forward_backward": (
@@ -69,11 +69,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "pmb_mask_estimator_final_backward": (
         _i, [_p, _p, _p, _i64, _i, _i64, _pi64, _pp, _p, _pp, _pp, _i, _i, _p, _i64, _p]),
     "pmb_attention_gate_forward": (
-        _i, [_p, _i64, _i64, _i64, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _p, _i, _i, _p]),
+        _i, [_p, _i64, _i64, _i64, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _p, _i, _i, _i64, _p]),
     "pmb_attention_gate_backward_workspace_size": (_i64, [_i64, _i64, _i64]),
     "pmb_attention_gate_backward": (
         _i, [_p, _p, _i64, _i64, _i64, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _i, _i, _p, _i64,
-             _p]),
+             _i64, _p]),
     "pmb_band_gather_forward": (_i, [_p, _p, _i64, _i64, _i64, _i64, _i64, _p, _i, _p]),
     "pmb_band_gather_backward": (_i, [_p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p, _i, _p]),
     "pmb_band_recombine_forward": (_i, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i, _p, _i, _p]),
@@ -83,8 +83,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         _i, [_p, _i64, _i, _i64, _i64, _i, _pi64, _pp, _pp, _p, _p, _p, _p, _i, _i, _p]),
     "pmb_mask_estimator_tc_backward": (
         _i, [_p, _p, _p, _p, _p, _i64, _i, _i64, _i64, _i, _pi64, _pp, _pp, _p, _i, _i, _p, _i64, _p]),
-    "pmb_qkv_rotary_split": (_i, [_p, _p, _p, _i64, _i64, _i64, _i64, _p, _p, _p, _i, _i, _p]),
-    "pmb_qkv_rotary_merge": (_i, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _i, _i, _i64, _i64, _i64, _p]),
+    "pmb_qkv_rotary_split": (_i, [_p, _p, _p, _i64, _i64, _i64, _i64, _p, _p, _p, _i, _i, _i64, _p]),
+    "pmb_qkv_rotary_merge": (_i, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _i, _i, _i64, _i64, _i64, _i64, _p]),
 }
 
 

@@ -21,9 +21,17 @@ constexpr int kWarps = kThreads / 32;
 constexpr int kMaxHeads = 16;
 constexpr int kRowsPerChunk = 256;
 
+// Row r of x / out is token (sequence, position) of the attention output:
+// rows are ordered (outer, position, inner) -- inner = 1 is the plain
+// [sequences, seq] order; inner > 1 lets an axial transformer keep its input
+// in the other axis' order (sequence = outer * inner + inner index).
 struct AttnLayout {
-  int64_t seq, s_b, s_n, s_h;
-  __device__ __forceinline__ int64_t row_base(int64_t r) const { return (r / seq) * s_b + (r % seq) * s_n; }
+  int64_t seq, s_b, s_n, s_h, inner;
+  __device__ __forceinline__ int64_t row_base(int64_t r) const {
+    const int64_t q = r / inner, ii = r - q * inner;
+    const int64_t o = q / seq, pos = q - o * seq;
+    return (o * inner + ii) * s_b + pos * s_n;
+  }
 };
 
 __device__ __forceinline__ float sigmoidf_(float v) { return 1.0f / (1.0f + expf(-v)); }
@@ -489,7 +497,7 @@ extern "C" int pmb_attention_gate_forward(const void* attn, int64_t seq_len, int
                                           int64_t attn_stride_seq, int64_t attn_stride_head, const void* x,
                                           const void* weight, const void* bias, int64_t rows, int64_t heads,
                                           int64_t dim_head, int64_t dim, void* out, void* gate, int dtype,
-                                          int param_dtype, void* stream) {
+                                          int param_dtype, int64_t seq_inner, void* stream) {
   clear_error();
   const char* name = "pmb_attention_gate_forward";
   PMB_REQUIRE(rows >= 0 && heads > 0 && heads <= kMaxHeads && dim_head > 0 && dim > 0 && seq_len > 0,
@@ -497,7 +505,8 @@ extern "C" int pmb_attention_gate_forward(const void* attn, int64_t seq_len, int
   PMB_REQUIRE(heads * dim * 4 <= 96 * 1024, "%s: heads*dim too large", name);
   if (rows == 0) return PMB_OK;
   PMB_REQUIRE(attn && x && weight && bias && out && gate, "%s: NULL tensor argument", name);
-  AttnLayout la{seq_len, attn_stride_batch, attn_stride_seq, attn_stride_head};
+  PMB_REQUIRE(seq_inner > 0, "%s: seq_inner must be positive", name);
+  AttnLayout la{seq_len, attn_stride_batch, attn_stride_seq, attn_stride_head, seq_inner};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const size_t smem = (size_t)heads * dim * sizeof(float);
   return PMB_DISPATCH_PARAM(dtype, param_dtype, T, TP, name, [&] {
@@ -539,7 +548,7 @@ extern "C" int pmb_attention_gate_backward(const void* grad_out, const void* att
                                            const void* gate, int64_t rows, int64_t heads, int64_t dim_head,
                                            int64_t dim, void* grad_attn, void* grad_x, void* grad_weight,
                                            void* grad_bias, int dtype, int param_dtype, void* workspace,
-                                           int64_t workspace_bytes, void* stream) {
+                                           int64_t workspace_bytes, int64_t seq_inner, void* stream) {
   clear_error();
   const char* name = "pmb_attention_gate_backward";
   PMB_REQUIRE(rows >= 0 && heads > 0 && heads <= kMaxHeads && dim_head > 0 && dim > 0 && seq_len > 0,
@@ -563,7 +572,8 @@ extern "C" int pmb_attention_gate_backward(const void* grad_out, const void* att
   }
   float* ggp = static_cast<float*>(workspace);
   float* partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + align256(rows * heads * 4));
-  AttnLayout la{seq_len, attn_stride_batch, attn_stride_seq, attn_stride_head};
+  PMB_REQUIRE(seq_inner > 0, "%s: seq_inner must be positive", name);
+  AttnLayout la{seq_len, attn_stride_batch, attn_stride_seq, attn_stride_head, seq_inner};
   const size_t smem = (size_t)heads * dim * sizeof(float);
   return PMB_DISPATCH_PARAM(dtype, param_dtype, T, TP, name, [&] {
     if (heads * dim <= kThreads * kMaxWPerThread &&

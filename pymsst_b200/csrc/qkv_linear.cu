@@ -24,14 +24,17 @@ namespace {
 
 template <typename T>
 struct QkvRotaryEpi {
-  T* plane[3];       // q, k, v: [rows, H*Dh]
+  T* plane[3];         // q, k, v: [sequences * seq, H*Dh]
   const float* cos_t;  // [Dh/2, seq]
   const float* sin_t;
-  int hd, seq, dh, rotate;
+  int hd, seq, dh, rotate, inner;
   template <int BN>
   __device__ void run(const ugemm::Plan&, const ugemm::TileCtx& t) const {
-    // rows past the end still map to a position in [0, seq): table reads stay in bounds
-    const int pos = t.row % seq;
+    // x row r = (outer, position, inner index); its plane row is (outer * inner + inner index) * seq + position.
+    // Rows past the end still map to a position in [0, seq): table reads stay in bounds.
+    const int q_ = t.row / inner, ii = t.row - q_ * inner;
+    const int o = q_ / seq, pos = q_ - o * seq;
+    const int64_t prow = (int64_t)(o * inner + ii) * seq + pos;
 #pragma unroll 1
     for (int c0 = 32 * t.sub; c0 < BN; c0 += 32 * ugemm::kSubs) {
       if (c0 >= t.n_valid) break;
@@ -47,13 +50,18 @@ struct QkvRotaryEpi {
 #pragma unroll
         for (int u = 0; u < 16; ++u) {
           const float c = cp[(int64_t)u * seq], sn = sp[(int64_t)u * seq];
-          const float e = round_to<T>(v[2 * u]), o = round_to<T>(v[2 * u + 1]);
-          v[2 * u] = e * c - o * sn;
-          v[2 * u + 1] = o * c + e * sn;
+          const float e = round_to<T>(v[2 * u]), od = round_to<T>(v[2 * u + 1]);
+          v[2 * u] = e * c - od * sn;
+          v[2 * u + 1] = od * c + e * sn;
         }
       }
-      T* dst = (which == 0 ? plane[0] : (which == 1 ? plane[1] : plane[2])) + (int64_t)t.row0 * hd + col;
-      ugemm::warp_store<T>(t.stage, v, dst, hd, t.rows_valid, ncols);
+      T* base = which == 0 ? plane[0] : (which == 1 ? plane[1] : plane[2]);
+      if (inner == 1) {
+        ugemm::warp_store<T>(t.stage, v, base + (int64_t)t.row0 * hd + col, hd, t.rows_valid, ncols);
+      } else {
+        T* row = t.row_valid ? base + prow * hd + col : nullptr;
+        ugemm::warp_store_rows<T>(t.stage, v, row, ncols);
+      }
     }
   }
 };
@@ -66,7 +74,7 @@ using namespace pmb;
 extern "C" int pmb_qkv_linear_rotary_forward(const void* x, const void* weight, const float* cos_t,
                                              const float* sin_t, int64_t batch, int64_t seq_len, int64_t dim,
                                              int64_t heads, int64_t dim_head, void* q, void* k, void* v,
-                                             int rotate_qk, int dtype, void* stream) {
+                                             int rotate_qk, int dtype, int64_t seq_inner, void* stream) {
   clear_error();
   const char* name = "pmb_qkv_linear_rotary_forward";
   PMB_REQUIRE(dtype == PMB_BFLOAT16 || dtype == PMB_FLOAT16, "%s: activations must be bf16 or fp16", name);
@@ -77,6 +85,7 @@ extern "C" int pmb_qkv_linear_rotary_forward(const void* x, const void* weight, 
   if (rows == 0) return PMB_OK;
   PMB_REQUIRE(rows < (1ll << 31) && 3 * heads * dim_head < (1ll << 31), "%s: too large", name);
   PMB_REQUIRE(x && weight && q && k && v && (!rotate_qk || (cos_t && sin_t)), "%s: NULL tensor argument", name);
+  PMB_REQUIRE(seq_inner > 0 && batch % seq_inner == 0, "%s: batch must be a multiple of seq_inner", name);
   const int64_t n = 3 * heads * dim_head;
   const int bn = dense::pick_bn(n);
   CUtensorMap ma, mb;
@@ -90,7 +99,7 @@ extern "C" int pmb_qkv_linear_rotary_forward(const void* x, const void* weight, 
   auto run = [&](auto tag) {
     using T = decltype(tag);
     QkvRotaryEpi<T> epi{{static_cast<T*>(q), static_cast<T*>(k), static_cast<T*>(v)}, cos_t, sin_t,
-                        (int)(heads * dim_head), (int)seq_len, (int)dim_head, rotate_qk};
+                        (int)(heads * dim_head), (int)seq_len, (int)dim_head, rotate_qk, (int)seq_inner};
     if (bn == 256) return dense::launch<256, false, false>(ma, mb, plan, epi, fp16, s, name);
     if (bn == 128) return dense::launch<128, false, false>(ma, mb, plan, epi, fp16, s, name);
     return dense::launch<64, false, false>(ma, mb, plan, epi, fp16, s, name);

@@ -25,6 +25,7 @@ struct QkvDims {
   int64_t B, N;
   int H, Dh;
   int64_t s_b, s_h, s_n;  // element strides of q / k / v (d contiguous)
+  int64_t inner;          // rows ordered (outer, position, inner); sequence = outer * inner + inner index
 };
 
 // One warp per row (b, n) of the packed [B*N, 3, H, Dh] projection; lane l
@@ -43,8 +44,10 @@ __global__ void __launch_bounds__(kThreads)
   const int64_t rows = d.B * d.N;
   const int64_t warps = (int64_t)gridDim.x * (kThreads / 32);
   for (int64_t row = (int64_t)blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5); row < rows; row += warps) {
-    const int64_t b = row / d.N;
-    const int n = (int)(row - b * d.N);
+    const int64_t q_ = row / d.inner, ii = row - q_ * d.inner;
+    const int64_t o = q_ / d.N;
+    const int n = (int)(q_ - o * d.N);
+    const int64_t b = o * d.inner + ii;
     T* prow = qkv + row * (int64_t)cpr * 2 * P;
     const int64_t sbase = b * d.s_b + (int64_t)n * d.s_n;
     const float* crow = cosv + (int64_t)n * half;
@@ -104,14 +107,16 @@ using namespace pmb;
 
 extern "C" int pmb_qkv_rotary_split(const void* qkv, const float* cos, const float* sin, int64_t batch,
                                     int64_t seq_len, int64_t heads, int64_t dim_head, void* q, void* k, void* v,
-                                    int rotate_qk, int dtype, void* stream) {
+                                    int rotate_qk, int dtype, int64_t seq_inner, void* stream) {
   clear_error();
   const char* name = "pmb_qkv_rotary_split";
   PMB_REQUIRE(batch >= 0 && seq_len >= 0 && heads > 0 && dim_head > 0 && dim_head % 2 == 0,
               "%s: bad shape (dim_head must be even)", name);
   if (batch * seq_len == 0) return PMB_OK;
   PMB_REQUIRE(qkv && q && k && v && (!rotate_qk || (cos && sin)), "%s: NULL tensor argument", name);
-  QkvDims d{batch, seq_len, (int)heads, (int)dim_head, heads * seq_len * dim_head, seq_len * dim_head, dim_head};
+  PMB_REQUIRE(seq_inner > 0 && batch % seq_inner == 0, "%s: batch must be a multiple of seq_inner", name);
+  QkvDims d{batch, seq_len, (int)heads, (int)dim_head, heads * seq_len * dim_head, seq_len * dim_head, dim_head,
+            seq_inner};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return PMB_DISPATCH(dtype, T, name, [&] {
     return launch<T, false>(const_cast<void*>(qkv), cos, sin, d, q, k, v, rotate_qk, s, name);
@@ -121,7 +126,7 @@ extern "C" int pmb_qkv_rotary_split(const void* qkv, const float* cos, const flo
 extern "C" int pmb_qkv_rotary_merge(const void* grad_q, const void* grad_k, const void* grad_v, const float* cos,
                                     const float* sin, int64_t batch, int64_t seq_len, int64_t heads,
                                     int64_t dim_head, void* grad_qkv, int rotate_qk, int dtype, int64_t stride_batch,
-                                    int64_t stride_head, int64_t stride_seq, void* stream) {
+                                    int64_t stride_head, int64_t stride_seq, int64_t seq_inner, void* stream) {
   clear_error();
   const char* name = "pmb_qkv_rotary_merge";
   PMB_REQUIRE(batch >= 0 && seq_len >= 0 && heads > 0 && dim_head > 0 && dim_head % 2 == 0,
@@ -130,7 +135,8 @@ extern "C" int pmb_qkv_rotary_merge(const void* grad_q, const void* grad_k, cons
   PMB_REQUIRE(grad_q && grad_k && grad_v && grad_qkv && (!rotate_qk || (cos && sin)), "%s: NULL tensor argument",
               name);
   PMB_REQUIRE(stride_batch >= 0 && stride_head >= 0 && stride_seq >= 0, "%s: bad strides", name);
-  QkvDims d{batch, seq_len, (int)heads, (int)dim_head, stride_batch, stride_head, stride_seq};
+  PMB_REQUIRE(seq_inner > 0 && batch % seq_inner == 0, "%s: batch must be a multiple of seq_inner", name);
+  QkvDims d{batch, seq_len, (int)heads, (int)dim_head, stride_batch, stride_head, stride_seq, seq_inner};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return PMB_DISPATCH(dtype, T, name, [&] {
     return launch<T, true>(grad_qkv, cos, sin, d, const_cast<void*>(grad_q), const_cast<void*>(grad_k),

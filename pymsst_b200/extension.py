@@ -519,7 +519,7 @@ def attention_gate_forward(attn, x, weight, bias):
         nat.call(
             "pmb_attention_gate_forward", attn.data_ptr(), 1, heads * dh, 0, dh, x.data_ptr(), weight.data_ptr(),
             bias.data_ptr(), rows, heads, dh, x.shape[1], out.data_ptr(), gate.data_ptr(),
-            nat.dtype_code(attn.dtype), nat.dtype_code(weight.dtype), nat.stream_handle(device),
+            nat.dtype_code(attn.dtype), nat.dtype_code(weight.dtype), 1, nat.stream_handle(device),
         )
     return out, gate, attn, x
 
@@ -556,7 +556,7 @@ def attention_gate_backward(grad_out, attn, x, weight, gate):
             "pmb_attention_gate_backward", grad_out.data_ptr(), attn.data_ptr(), 1, heads * dh, 0, dh,
             x.data_ptr(), weight.data_ptr(), gate.data_ptr(), rows, heads, dh, dim, grad_attn.data_ptr(),
             grad_x.data_ptr(), grad_weight.data_ptr(), grad_bias.data_ptr(), nat.dtype_code(grad_out.dtype),
-            nat.dtype_code(weight.dtype), ws.data_ptr(), ws_bytes, nat.stream_handle(device),
+            nat.dtype_code(weight.dtype), ws.data_ptr(), ws_bytes, 1, nat.stream_handle(device),
         )
     return grad_attn, grad_x, grad_weight, grad_bias
 

@@ -269,6 +269,11 @@ def tensor_core_ok(x: torch.Tensor, *dims: int) -> bool:
 class QKVRotaryFn(torch.autograd.Function):
     """xn [b, n, D] -> q, k, v [b, h, n, dh]: projection, split, rotary on q/k.
 
+    ``inner`` > 1: the b*n rows of xn are ordered (outer, position, inner)
+    rather than (sequence, position) -- sequence = outer * inner + inner
+    index -- so an axial transformer passes its activations without a
+    permuted copy; q, k, v are always in sequence order.
+
     16-bit activations with D % 8 == 0 and dh % 32 == 0: one tensor-core GEMM
     with the rotation in its epilogue writes q, k, v as [b, n, h, dh] planes
     (pmb_qkv_linear_rotary_forward); the returned [b, h, n, dh] tensors are
@@ -280,7 +285,7 @@ class QKVRotaryFn(torch.autograd.Function):
     and runs the two projection-gradient GEMMs."""
 
     @staticmethod
-    def forward(ctx, xn, weight, cos, sin, cos_t, sin_t, heads):
+    def forward(ctx, xn, weight, cos, sin, cos_t, sin_t, heads, inner=1):
         device = nat.require_cuda(xn, weight, name="QKVRotary")
         b, n, d = xn.shape
         dh = weight.shape[0] // (3 * heads)
@@ -294,7 +299,7 @@ class QKVRotaryFn(torch.autograd.Function):
             nat.call(
                 "pmb_qkv_linear_rotary_forward", x2.data_ptr(), w.data_ptr(), nat.ptr(cos_t), nat.ptr(sin_t), b, n,
                 d, heads, dh, planes[0].data_ptr(), planes[1].data_ptr(), planes[2].data_ptr(), rotate,
-                nat.dtype_code(xn.dtype), nat.stream_handle(device),
+                nat.dtype_code(xn.dtype), inner, nat.stream_handle(device),
             )
             q, k, v = (p.transpose(1, 2) for p in planes)
         else:
@@ -304,9 +309,10 @@ class QKVRotaryFn(torch.autograd.Function):
             v = torch.empty_like(q)
             nat.call(
                 "pmb_qkv_rotary_split", qkv.data_ptr(), nat.ptr(cos), nat.ptr(sin), b, n, heads, dh, q.data_ptr(),
-                k.data_ptr(), v.data_ptr(), rotate, nat.dtype_code(xn.dtype), nat.stream_handle(device),
+                k.data_ptr(), v.data_ptr(), rotate, nat.dtype_code(xn.dtype), inner, nat.stream_handle(device),
             )
         ctx.heads = heads
+        ctx.inner = inner
         ctx.weight_dtype = weight.dtype
         ctx.save_for_backward(x2, w, cos, sin)
         return q, k, v
@@ -327,11 +333,11 @@ class QKVRotaryFn(torch.autograd.Function):
         nat.call(
             "pmb_qkv_rotary_merge", grads[0].data_ptr(), grads[1].data_ptr(), grads[2].data_ptr(), nat.ptr(cos),
             nat.ptr(sin), b, n, heads, dh, gqkv.data_ptr(), int(cos is not None), nat.dtype_code(x2.dtype),
-            strides[0], strides[1], strides[2], nat.stream_handle(device),
+            strides[0], strides[1], strides[2], ctx.inner, nat.stream_handle(device),
         )
         gx = torch.matmul(gqkv, w).reshape(b, n, -1) if ctx.needs_input_grad[0] else None
         gw = torch.matmul(gqkv.t(), x2).to(ctx.weight_dtype) if ctx.needs_input_grad[1] else None
-        return gx, gw, None, None, None, None, None
+        return gx, gw, None, None, None, None, None, None
 
 
 class FeedForwardFn(torch.autograd.Function):
@@ -386,10 +392,11 @@ class FeedForwardFn(torch.autograd.Function):
 
 
 class AttentionGateFn(torch.autograd.Function):
-    """attn [b, h, n, dh] (any strides, dh contiguous), xn [b*n, D] -> gated [b*n, h*dh]."""
+    """attn [b, h, n, dh] (any strides, dh contiguous), xn [b*n, D] -> gated [b*n, h*dh]; the rows of xn and of
+    the result follow the ``inner`` row order of QKVRotaryFn."""
 
     @staticmethod
-    def forward(ctx, attn, xn, weight, bias):
+    def forward(ctx, attn, xn, weight, bias, inner=1):
         device = nat.require_cuda(attn, xn, weight, bias, name="AttentionGate")
         if attn.stride(-1) != 1:
             attn = attn.contiguous()
@@ -401,8 +408,9 @@ class AttentionGateFn(torch.autograd.Function):
         nat.call(
             "pmb_attention_gate_forward", attn.data_ptr(), n, attn.stride(0), attn.stride(2), attn.stride(1),
             xn.data_ptr(), weight.data_ptr(), bias.data_ptr(), rows, h, dh, dim, out.data_ptr(), gate.data_ptr(),
-            nat.dtype_code(attn.dtype), nat.dtype_code(weight.dtype), nat.stream_handle(device),
+            nat.dtype_code(attn.dtype), nat.dtype_code(weight.dtype), inner, nat.stream_handle(device),
         )
+        ctx.inner = inner
         ctx.save_for_backward(attn, xn, weight, gate)
         return out
 
@@ -424,9 +432,9 @@ class AttentionGateFn(torch.autograd.Function):
             "pmb_attention_gate_backward", grad.data_ptr(), attn.data_ptr(), n, attn.stride(0), attn.stride(2),
             attn.stride(1), xn.data_ptr(), weight.data_ptr(), gate.data_ptr(), rows, h, dh, dim,
             grad_attn.data_ptr(), grad_x.data_ptr(), gw.data_ptr(), gb.data_ptr(), nat.dtype_code(attn.dtype),
-            nat.dtype_code(weight.dtype), ws.data_ptr(), ws_bytes, nat.stream_handle(device),
+            nat.dtype_code(weight.dtype), ws.data_ptr(), ws_bytes, ctx.inner, nat.stream_handle(device),
         )
-        return grad_attn, grad_x, gw, gb
+        return grad_attn, grad_x, gw, gb, None
 
 
 # -------------------------------------------------------- band index ops

@@ -83,7 +83,7 @@ def op_gate(bench: _Bench):
     def fwd():
         nat.call("pmb_attention_gate_forward", attn.data_ptr(), SEQ, *strides, x.data_ptr(), w.data_ptr(),
                  b.data_ptr(), ROWS, HEADS, DHEAD, DIM, out.data_ptr(), gate.data_ptr(), nat.dtype_code(bf),
-                 nat.dtype_code(f32), st)
+                 nat.dtype_code(f32), 1, st)
 
     e = 2
     bench.time("attention_gate_forward", fwd, ROWS * (DIM + 2 * HEADS * DHEAD + HEADS) * e)
@@ -96,7 +96,7 @@ def op_gate(bench: _Bench):
     def bwd():
         nat.call("pmb_attention_gate_backward", dy.data_ptr(), attn.data_ptr(), SEQ, *strides, x.data_ptr(),
                  w.data_ptr(), gate.data_ptr(), ROWS, HEADS, DHEAD, DIM, ga.data_ptr(), gx.data_ptr(), gw.data_ptr(),
-                 gb.data_ptr(), nat.dtype_code(bf), nat.dtype_code(f32), ws.data_ptr(), wsb, st)
+                 gb.data_ptr(), nat.dtype_code(bf), nat.dtype_code(f32), ws.data_ptr(), wsb, 1, st)
 
     bench.time("attention_gate_backward", bwd, ROWS * (3 * HEADS * DHEAD + 2 * DIM + HEADS) * e)
 
@@ -143,15 +143,15 @@ def op_qkv(bench: _Bench):
     st = nat.stream_handle(dev)
     bench.time("qkv_rotary_split", lambda: nat.call(
         "pmb_qkv_rotary_split", qkv.data_ptr(), cos.data_ptr(), sin.data_ptr(), SEQ_BATCH, SEQ, HEADS, DHEAD,
-        q.data_ptr(), k.data_ptr(), v.data_ptr(), 1, 2, st), ROWS * n3 * 2 * 2)
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), 1, 2, 1, st), ROWS * n3 * 2 * 2)
     bench.time("qkv_rotary_merge", lambda: nat.call(
         "pmb_qkv_rotary_merge", q.data_ptr(), k.data_ptr(), v.data_ptr(), cos.data_ptr(), sin.data_ptr(), SEQ_BATCH,
-        SEQ, HEADS, DHEAD, qkv.data_ptr(), 1, 2, q.stride(0), q.stride(1), q.stride(2), st), ROWS * n3 * 2 * 2)
+        SEQ, HEADS, DHEAD, qkv.data_ptr(), 1, 2, q.stride(0), q.stride(1), q.stride(2), 1, st), ROWS * n3 * 2 * 2)
     cos_t, sin_t = cos.t().contiguous(), sin.t().contiguous()
     pq, pk, pv = (torch.empty(ROWS, HEADS * DHEAD, device=dev, dtype=bf) for _ in range(3))
     bench.time("qkv_linear_rotary_forward", lambda: nat.call(
         "pmb_qkv_linear_rotary_forward", x.data_ptr(), w.data_ptr(), cos_t.data_ptr(), sin_t.data_ptr(), SEQ_BATCH,
-        SEQ, DIM, HEADS, DHEAD, pq.data_ptr(), pk.data_ptr(), pv.data_ptr(), 1, 2, st),
+        SEQ, DIM, HEADS, DHEAD, pq.data_ptr(), pk.data_ptr(), pv.data_ptr(), 1, 2, 1, st),
         (ROWS * DIM + n3 * DIM + ROWS * n3) * 2, flops)
     gw = torch.empty(n3, DIM, device=dev)
     wsb = nat.library().pmb_gemm_tc_wgrad_workspace_size(n3, DIM, ROWS)

@@ -158,17 +158,23 @@ class Attention(nn.Module):
         self.to_gates = nn.Linear(dim, heads)
         self.to_out = nn.Sequential(nn.Linear(inner, dim, bias=False), nn.Dropout(dropout))
 
-    def forward(self, x):
-        b, n, d = x.shape
+    def forward(self, x, seq_len=None, inner=1):
+        """x [b, n, d]; or any [..., d] whose rows are ordered (outer, position, inner) with sequences of
+        ``seq_len`` positions (sequence = outer * inner + inner index)."""
+        d = x.shape[-1]
+        n = x.shape[-2] if seq_len is None else seq_len
+        rows = x.numel() // d
+        b = rows // n
         xn = self.norm(x)
         cos = sin = cos_t = sin_t = None
         if self.rotary_embed is not None:
             cos, sin, cos_t, sin_t = self.rotary_embed.tables(n, x.device)
-        q, k, v = QKVRotaryFn.apply(xn, self.to_qkv.weight, cos, sin, cos_t, sin_t, self.heads)
+        q, k, v = QKVRotaryFn.apply(xn.reshape(b, n, d), self.to_qkv.weight, cos, sin, cos_t, sin_t, self.heads,
+                                    inner)
         attn = _attention(q, k, v, self.dropout if self.training else 0.0)
-        gated = AttentionGateFn.apply(attn, xn.reshape(b * n, d), self.to_gates.weight, self.to_gates.bias)
+        gated = AttentionGateFn.apply(attn, xn.reshape(rows, d), self.to_gates.weight, self.to_gates.bias, inner)
         out = F.linear(gated, self.to_out[0].weight.to(gated.dtype))
-        return self.to_out[1](out).reshape(b, n, d)
+        return self.to_out[1](out).reshape(x.shape)
 
 
 class FeedForward(nn.Module):
@@ -214,9 +220,10 @@ class Transformer(nn.Module):
         )
         self.norm = RMSNorm(dim) if norm_output else nn.Identity()
 
-    def forward(self, x):
+    def forward(self, x, seq_len=None, inner=1):
+        """x [b, n, d], or rows in (outer, position, inner) order (see Attention.forward)."""
         for attn, ff in self.layers:
-            x = attn(x) + x
+            x = attn(x, seq_len, inner) + x
             x = ff(x) + x
         return self.norm(x)
 
@@ -355,7 +362,9 @@ class _Roformer(nn.Module):
                 for prev in store:
                     x = x + prev
             b, t, f, d = x.shape
-            x = time_t(x.permute(0, 2, 1, 3).reshape(b * f, t, d)).reshape(b, f, t, d).permute(0, 2, 1, 3)
+            # rows stay in (b, t, f) order for both axes: the time transformer's sequences are (b, f) pairs
+            # over t (inner = f), the frequency transformer's are (b, t) pairs over f
+            x = time_t(x, seq_len=t, inner=f)
             x = freq_t(x.reshape(b * t, f, d)).reshape(b, t, f, d)
             if self.skip_connection:
                 store.append(x)

@@ -162,7 +162,7 @@ def test_attention_gate_strided_attention_layout(cuda_device, dtype, bsz, heads,
     xd, wd, bd = x.to(cuda_device), w.to(cuda_device), b.to(cuda_device)
     nat.call("pmb_attention_gate_forward", a_dev.data_ptr(), seq, a_dev.stride(0), a_dev.stride(2), a_dev.stride(1),
              xd.data_ptr(), wd.data_ptr(), bd.data_ptr(), rows, heads, dh, dim, out.data_ptr(), gate.data_ptr(),
-             nat.dtype_code(dtype), nat.dtype_code(dtype), nat.stream_handle(cuda_device))
+             nat.dtype_code(dtype), nat.dtype_code(dtype), 1, nat.stream_handle(cuda_device))
     _close(out, r_out, dtype, "out")
     _close(gate, r_gate, dtype, "gate")
     dy = torch.randn(rows, heads * dh).to(dtype)
@@ -176,7 +176,7 @@ def test_attention_gate_strided_attention_layout(cuda_device, dtype, bsz, heads,
     nat.call("pmb_attention_gate_backward", dyd.data_ptr(), a_dev.data_ptr(), seq, a_dev.stride(0), a_dev.stride(2),
              a_dev.stride(1), xd.data_ptr(), wd.data_ptr(), gate.data_ptr(), rows, heads, dh, dim,
              grad_attn.data_ptr(), gx.data_ptr(), gw.data_ptr(), gb.data_ptr(), nat.dtype_code(dtype),
-             nat.dtype_code(dtype), ws.data_ptr(), ws_bytes, nat.stream_handle(cuda_device))
+             nat.dtype_code(dtype), ws.data_ptr(), ws_bytes, 1, nat.stream_handle(cuda_device))
     r = ops_ref.attention_gate_backward(dy.double(), attn_rows.double(), x.double(), w.double(),
                                         gate.double().cpu())
     _close(grad_attn.permute(0, 2, 1, 3).reshape(rows, heads, dh), r[0], dtype, "grad_attn")

@@ -76,12 +76,49 @@ def test_qkv_linear_rotary_matches_unfused_split(cuda_device):
     st = nat.stream_handle(cuda_device)
     cos_t, sin_t = cos.t().contiguous(), sin.t().contiguous()
     nat.call("pmb_qkv_linear_rotary_forward", x.data_ptr(), w.data_ptr(), cos_t.data_ptr(), sin_t.data_ptr(), b, n,
-             d, heads, dh, planes[0].data_ptr(), planes[1].data_ptr(), planes[2].data_ptr(), 1, 2, st)
+             d, heads, dh, planes[0].data_ptr(), planes[1].data_ptr(), planes[2].data_ptr(), 1, 2, 1, st)
     split = [torch.empty(b, heads, n, dh, dtype=torch.bfloat16, device=cuda_device) for _ in range(3)]
     qkv = (x.float() @ w.float().t()).to(torch.bfloat16)
     nat.call("pmb_qkv_rotary_split", qkv.data_ptr(), cos.data_ptr(), sin.data_ptr(), b, n, heads, dh,
-             split[0].data_ptr(), split[1].data_ptr(), split[2].data_ptr(), 1, 2, st)
+             split[0].data_ptr(), split[1].data_ptr(), split[2].data_ptr(), 1, 2, 1, st)
     for i in range(3):
         a, e = planes[i].transpose(1, 2).float(), split[i].float()
         bad = ((a - e).abs() > 2 * 2 ** -7 * e.abs().clamp_min(1e-3) + 1e-3).float().mean().item()
         assert bad < 1e-3, f"output {i}: {bad:.2%} of values differ by more than 2 ulps"
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_row_map_matches_permuted_input(cuda_device, dtype):
+    """Rows ordered (outer, position, inner) with inner > 1 give the same q / k / v, gate output and input
+    gradients as the permuted copy in plain (sequence, position) order: the axial transformer's time axis."""
+    from pymsst_b200.fused import AttentionGateFn
+
+    torch.manual_seed(9)
+    b, t, f, d, heads, dh = 2, 37, 6, 64, 2, 32
+    x = torch.randn(b, t, f, d, device=cuda_device).to(dtype)
+    w = (torch.randn(3 * heads * dh, d, device=cuda_device) / d ** 0.5)
+    gw = torch.randn(heads, d, device=cuda_device) * 0.1
+    gb = torch.randn(heads, device=cuda_device)
+    freqs = 1.0 / (10000 ** (torch.arange(0, dh, 2, device=cuda_device).float() / dh))
+    cos, sin = rotary_tables(freqs, t, cuda_device)
+    ct, st = cos.t().contiguous(), sin.t().contiguous()
+
+    def run(inp, inner):
+        inp = inp.detach().requires_grad_()
+        rows = inp.numel() // d
+        q, k, v = QKVRotaryFn.apply(inp.reshape(rows // t, t, d), w, cos, sin, ct, st, heads, inner)
+        attn = q * 0.5 + k * 0.25 + v  # any function of q, k, v in sequence order
+        out = AttentionGateFn.apply(attn, inp.reshape(rows, d), gw, gb, inner)
+        return inp, (q, k, v), out
+
+    xp = x.permute(0, 2, 1, 3).contiguous()  # [b, f, t, d]: plain order, sequences (b, f)
+    a_in, a_qkv, a_out = run(x, f)
+    b_in, b_qkv, b_out = run(xp, 1)
+    for u, v_ in zip(a_qkv, b_qkv):
+        torch.testing.assert_close(u, v_, rtol=0, atol=0)
+    torch.testing.assert_close(a_out.reshape(b, t, f, -1), b_out.reshape(b, f, t, -1).permute(0, 2, 1, 3),
+                               rtol=0, atol=0)
+    g = torch.randn_like(a_out)
+    a_out.backward(g)
+    b_out.backward(g.reshape(b, t, f, -1).permute(0, 2, 1, 3).reshape(b_out.shape))
+    torch.testing.assert_close(a_in.grad, b_in.grad.permute(0, 2, 1, 3), rtol=1e-5, atol=1e-5)
