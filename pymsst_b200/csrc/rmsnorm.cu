@@ -587,6 +587,11 @@ int launch_fwd(const void* x, const void* gamma, int gcode, void* out, void* nor
 }
 
 int bwd_blocks(int64_t rows) { return grid_for_rows(rows, kMaxBwdBlocks); }
+int64_t max_bwd_grid(int64_t rows) { return rows < kMaxBwdBlocks ? rows : kMaxBwdBlocks; }
+
+// Rows per bulk backward tile: a lane prefetches the norm of one row of its
+// warp per step, so a warp covers at most 32 rows and a tile kWarps * 32.
+constexpr int kMaxBwdTileRows = kWarps * 32;
 
 template <typename Tg, typename Tdx>
 int launch_bwd(const void* dy, const void* saved, int saved_is_input, const float* inv, const void* gamma,
@@ -607,7 +612,7 @@ int launch_bwd(const void* dy, const void* saved, int saved_is_input, const floa
   const int64_t row_bytes = dim * (int64_t)sizeof(Tg);
   if (vec_ok && sizeof(Tg) == sizeof(Tdx) && dim <= kMaxBulkDim && row_bytes <= kBwdStageBytes &&
       (int64_t)kWarps * 4 * dim * 4 <= (int64_t)kStages * kBwdStageBytes * 2) {
-    const int rpt = (int)(kBwdStageBytes / row_bytes);
+    const int rpt = (int)(kBwdStageBytes / row_bytes < kMaxBwdTileRows ? kBwdStageBytes / row_bytes : kMaxBwdTileRows);
     const int64_t tiles = (rows + rpt - 1) / rpt;
     int64_t g = (int64_t)num_sms() * 3;  // 3 CTAs of 64 KB shared memory per SM
     if (g > kMaxBwdBlocks) g = kMaxBwdBlocks;
@@ -683,7 +688,9 @@ extern "C" int pmb_rms_norm_forward(const void* x, const void* gamma, void* out,
 
 extern "C" int64_t pmb_rms_norm_backward_workspace_size(int64_t rows, int64_t dim) {
   if (rows <= 0 || dim <= 0) return 0;
-  return (int64_t)bwd_blocks(rows) * dim * (int64_t)sizeof(float);
+  // every backward path launches at most min(rows, kMaxBwdBlocks) CTAs (the
+  // bulk path one per tile of as few as one row), each writing one partial row
+  return max_bwd_grid(rows) * dim * (int64_t)sizeof(float);
 }
 
 extern "C" int pmb_rms_norm_backward(const void* grad_out, const void* saved, int saved_is_input,
@@ -806,7 +813,7 @@ extern "C" int pmb_rms_norm_backward_noalloc(const void* grad_out, const void* s
   float* partial = nullptr;
   const int st = noalloc_scratch(&partial, name);
   if (st) return st;
-  // bwd_blocks(rows) <= kMaxBwdBlocks, so the partial sums fit the array.
+  // every path launches at most kMaxBwdBlocks CTAs, so the partial sums fit the array.
   return PMB_DISPATCH(grad_dtype, Tg, name, [&] {
     return PMB_DISPATCH(grad_x_dtype, Tdx, name, [&] {
       return launch_bwd<Tg, Tdx>(grad_out, saved, saved_is_input, inv_norm, gamma, gamma_dtype, grad_x, grad_gamma,

@@ -120,3 +120,32 @@ def test_rejects_mismatched_arguments(cuda_device):
     c = torch.randn(1, 3, 1, 3, device=cuda_device)
     with pytest.raises(RuntimeError, match="cos sequence dimension must match t"):
         ops.rotary_forward(t, c, c)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("dim", [4, 64, 192, 384, 1024, 1536])
+@pytest.mark.parametrize("rows", [1, 5, 17, 300, 777, 5000])
+def test_rms_norm_backward_stays_inside_workspace(cuda_device, rows, dim, dtype):
+    """The grad_gamma partials fit the advertised workspace for every path:
+    the exact size is followed by a sentinel region that must stay untouched."""
+    from pymsst_b200 import _native as nat
+
+    lib = nat.library()
+    need = int(lib.pmb_rms_norm_backward_workspace_size(rows, dim))
+    guard = 1 << 16
+    buf = torch.full((need + guard,), 0xA5, dtype=torch.uint8, device=cuda_device)
+    dy = torch.randn(rows, dim, device=cuda_device).to(dtype)
+    normed = torch.randn(rows, dim, device=cuda_device).to(dtype)
+    inv = torch.rand(rows, device=cuda_device) + 0.5
+    gamma = (torch.rand(dim, device=cuda_device) + 0.5).to(dtype)
+    gx = torch.empty_like(dy)
+    gg = torch.empty(dim, dtype=dtype, device=cuda_device)
+    code = nat.dtype_code(dtype)
+    nat.call("pmb_rms_norm_backward", dy.data_ptr(), normed.data_ptr(), 0, inv.data_ptr(), gamma.data_ptr(),
+             gx.data_ptr(), gg.data_ptr(), rows, dim, code, code, code, code, buf.data_ptr(), need,
+             nat.stream_handle(cuda_device))
+    assert bool((buf[need:] == 0xA5).all()), "backward wrote past the workspace"
+    r_gx, r_gg = ops_ref.rms_norm_backward(dy.double().cpu(), normed.double().cpu(), inv.double().cpu(),
+                                           gamma.double().cpu())
+    _close(gx, r_gx, dtype)
+    _close(gg, r_gg, dtype, scale=rows ** 0.5)
