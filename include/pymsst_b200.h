@@ -486,6 +486,31 @@ PMB_API int pmb_mask_estimator_tc_backward(const void* grad_out, const void* x, 
                                            int dtype, int param_dtype, void* workspace, int64_t workspace_bytes,
                                            void* stream);
 
+/* ------------------------------------------------------------------------
+ * Attention core of the axial transformers on the tensor cores: softmax(
+ * Q K^T * scale) V per (sequence, head), head dim 64, bf16/fp16, no mask, no
+ * dropout.  q, k, v, o (and grad_out, grad_q, grad_k, grad_v) are
+ * [sequences, seq_len, heads, 64] planes given by a base pointer and three
+ * element strides (sequence, position, head) each, all multiples of 8 with
+ * the 64 head elements contiguous; `strides` holds them plane by plane
+ * (forward: q, k, v, o = 12 values; backward: q, k, v, o, grad_out, grad_q,
+ * grad_k, grad_v = 24 values).  lse: fp32 [sequences * heads, seq_len], the
+ * natural-log row sums written by the forward and read by the backward.
+ * The backward needs pmb_attention_backward_workspace_size bytes of
+ * workspace (the row sums D = rowsum(grad_out * o)) and is deterministic.
+ * Replaces torch.nn.functional.scaled_dot_product_attention in pymss-core's
+ * Attention module, whose backend the reference selects with
+ * cuda_attention_backend (src/pymsst/training/module.py:96-107, :416-425).
+ * ---------------------------------------------------------------------- */
+PMB_API int pmb_attention_forward(const void* q, const void* k, const void* v, void* o, float* lse,
+                                  int64_t sequences, int64_t seq_len, int64_t heads, int64_t dim_head,
+                                  const int64_t* strides, float scale, int dtype, void* stream);
+PMB_API int64_t pmb_attention_backward_workspace_size(int64_t sequences, int64_t seq_len, int64_t heads);
+PMB_API int pmb_attention_backward(const void* q, const void* k, const void* v, const void* o, const void* grad_out,
+                                   const float* lse, void* grad_q, void* grad_k, void* grad_v, int64_t sequences,
+                                   int64_t seq_len, int64_t heads, int64_t dim_head, const int64_t* strides,
+                                   float scale, int dtype, void* workspace, int64_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -21,6 +21,7 @@ _DTYPE_CODES = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16}
 _p = ctypes.c_void_p
 _i64 = ctypes.c_int64
 _i = ctypes.c_int
+_f32 = ctypes.c_float
 _pp = ctypes.POINTER(ctypes.c_void_p)
 _pi64 = ctypes.POINTER(ctypes.c_int64)
 
@@ -85,6 +86,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         _i, [_p, _p, _p, _p, _p, _i64, _i, _i64, _i64, _i, _pi64, _pp, _pp, _p, _i, _i, _p, _i64, _p]),
     "pmb_qkv_rotary_split": (_i, [_p, _p, _p, _i64, _i64, _i64, _i64, _p, _p, _p, _i, _i, _i64, _p]),
     "pmb_qkv_rotary_merge": (_i, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _i, _i, _i64, _i64, _i64, _i64, _p]),
+    "pmb_attention_forward": (_i, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _pi64, _f32, _i, _p]),
+    "pmb_attention_backward_workspace_size": (_i64, [_i64, _i64, _i64]),
+    "pmb_attention_backward": (
+        _i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _pi64, _f32, _i, _p, _i64, _p]),
 }
 
 

@@ -55,6 +55,33 @@ int make_map_3d(CUtensorMap& map, const void* base, int dtype, uint64_t inner, u
   return PMB_OK;
 }
 
+int make_map_4d(CUtensorMap& map, const void* base, int dtype, const uint64_t (&dims)[4],
+                const uint64_t (&stride_bytes)[3], const uint32_t (&box)[4], const char* name) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) {
+    set_error("%s: cuTensorMapEncodeTiled is unavailable (driver too old or no GPU)", name);
+    return PMB_ERR_CUDA;
+  }
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || ((stride_bytes[0] | stride_bytes[1] | stride_bytes[2]) & 15)) {
+    set_error("%s: tensor-core operand needs a 16-byte aligned base and strides", name);
+    return PMB_ERR_ALIGNMENT;
+  }
+  const cuuint64_t d[4] = {dims[0], dims[1], dims[2], dims[3]};
+  const cuuint64_t st[3] = {stride_bytes[0], stride_bytes[1], stride_bytes[2]};
+  const cuuint32_t bx[4] = {box[0], box[1], box[2], box[3]};
+  const cuuint32_t elem[4] = {1, 1, 1, 1};
+  const CUtensorMapDataType t =
+      dtype == PMB_BFLOAT16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const CUresult r = fn(&map, t, 4, const_cast<void*>(base), d, st, bx, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("%s: cuTensorMapEncodeTiled failed (%d) for a 4-D map", name, (int)r);
+    return PMB_ERR_CUDA;
+  }
+  return PMB_OK;
+}
+
 }  // namespace tma
 
 }  // namespace pmb

@@ -61,6 +61,7 @@ unsigned int timeout_flag_qkv(int reset);
 unsigned int timeout_flag_ff(int reset);
 unsigned int timeout_flag_rms(int reset);
 unsigned int timeout_flag_band(int reset);
+unsigned int timeout_flag_attn(int reset);
 
 }  // namespace pmb
 
@@ -69,7 +70,7 @@ extern "C" {
 unsigned int pmb_umma_timeout(int reset) {
   unsigned int first = 0;
   for (auto flag : {pmb::timeout_flag_gemm, pmb::timeout_flag_mask, pmb::timeout_flag_qkv, pmb::timeout_flag_ff, pmb::timeout_flag_rms,
-                    pmb::timeout_flag_band}) {
+                    pmb::timeout_flag_band, pmb::timeout_flag_attn}) {
     const unsigned int v = flag(reset);
     if (first == 0) first = v;
   }

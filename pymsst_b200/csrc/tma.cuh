@@ -22,5 +22,10 @@ int make_map_3d(CUtensorMap& map, const void* base, int dtype, uint64_t inner, u
                 uint64_t stride_mid_bytes, uint64_t stride_outer_bytes, uint32_t box_inner, uint32_t box_mid,
                 uint32_t box_outer, const char* name);
 
+// 4-D map (d0 innermost .. d3) over a 16-bit tensor with 128-byte swizzle;
+// strides in bytes for d1..d3; out-of-range boxes read zeros.
+int make_map_4d(CUtensorMap& map, const void* base, int dtype, const uint64_t (&dims)[4],
+                const uint64_t (&stride_bytes)[3], const uint32_t (&box)[4], const char* name);
+
 }  // namespace tma
 }  // namespace pmb

@@ -437,6 +437,69 @@ class AttentionGateFn(torch.autograd.Function):
         return grad_attn, grad_x, gw, gb, None
 
 
+def _attn_plane(t: torch.Tensor) -> torch.Tensor:
+    """[b, h, n, dh] view whose strides the attention kernels accept (head dim contiguous, 16-byte rows)."""
+    if t.stride(-1) != 1 or any(s % 8 for s in t.stride()[:3]) or t.data_ptr() % 16:
+        t = t.transpose(1, 2).contiguous().transpose(1, 2)
+    return t
+
+
+def _attn_strides(*planes: torch.Tensor) -> list[int]:
+    """(sequence, position, head) element strides of [b, h, n, dh] views, plane by plane."""
+    out: list[int] = []
+    for t in planes:
+        out += [t.stride(0), t.stride(2), t.stride(1)]
+    return out
+
+
+def _bnhd_empty(b, h, n, dh, dtype, device) -> torch.Tensor:
+    return torch.empty(b, n, h, dh, dtype=dtype, device=device).transpose(1, 2)
+
+
+def attention_supported(q: torch.Tensor, dropout_p: float = 0.0) -> bool:
+    """Shapes and types the attention kernels take: CUDA, bf16/fp16, head dim 64, no dropout."""
+    return (q.is_cuda and q.dtype in (torch.bfloat16, torch.float16) and q.dim() == 4 and q.shape[-1] == 64
+            and dropout_p == 0.0)
+
+
+class AttentionFn(torch.autograd.Function):
+    """softmax(q k^T / sqrt(dh)) v for q, k, v [b, h, n, 64] (any strides with the head dim contiguous, such as
+    views of [b, n, h, 64] planes) -> o [b, h, n, 64], a view of a [b, n, h, 64] plane.  Drop-in for
+    F.scaled_dot_product_attention(q, k, v) without mask or dropout; deterministic backward."""
+
+    @staticmethod
+    def forward(ctx, q, k, v):
+        device = nat.require_cuda(q, k, v, name="Attention")
+        q, k, v = _attn_plane(q), _attn_plane(k), _attn_plane(v)
+        b, h, n, dh = q.shape
+        o = _bnhd_empty(b, h, n, dh, q.dtype, device)
+        lse = torch.empty(b * h, n, dtype=torch.float32, device=device)
+        nat.call(
+            "pmb_attention_forward", q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(), b, n, h,
+            dh, nat.i64_array(_attn_strides(q, k, v, o)), dh ** -0.5, nat.dtype_code(q.dtype),
+            nat.stream_handle(device),
+        )
+        ctx.save_for_backward(q, k, v, o, lse)
+        return o
+
+    @staticmethod
+    def backward(ctx, grad):
+        q, k, v, o, lse = ctx.saved_tensors
+        device = q.device
+        b, h, n, dh = q.shape
+        grad = _attn_plane(grad.to(q.dtype))
+        dq, dk, dv = (_bnhd_empty(b, h, n, dh, q.dtype, device) for _ in range(3))
+        ws_bytes = int(nat.library().pmb_attention_backward_workspace_size(b, n, h))
+        ws = nat.workspace(ws_bytes, device)
+        nat.call(
+            "pmb_attention_backward", q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), grad.data_ptr(),
+            lse.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), b, n, h, dh,
+            nat.i64_array(_attn_strides(q, k, v, o, grad, dq, dk, dv)), dh ** -0.5, nat.dtype_code(q.dtype),
+            ws.data_ptr(), ws_bytes, nat.stream_handle(device),
+        )
+        return dq, dk, dv
+
+
 # -------------------------------------------------------- band index ops
 class BandGatherFn(torch.autograd.Function):
     """stft fp32 [B,S,F,T,2] -> band features [B,T,J*2] in out_dtype."""

@@ -237,6 +237,29 @@ def op_sdpa(bench: _Bench):
                 print(f"sdpa {backend.name} n={n}: unavailable ({str(e).splitlines()[0][:80]})")
 
 
+def op_attn(bench: _Bench):
+    """Own attention kernels (fwd, fwd+bwd) on the two axial shapes, q/k/v as views of a packed projection."""
+    from .fused import AttentionFn
+
+    dev, bf = bench.device, torch.bfloat16
+    for nb, n in ((SEQ_BATCH, SEQ), (ROWS // 62, 62)):
+        packed = torch.randn(nb, n, 3, HEADS, DHEAD, device=dev, dtype=bf)
+        qkv = [packed[:, :, i].transpose(1, 2).requires_grad_() for i in range(3)]
+        gy = torch.randn(nb, n, HEADS, DHEAD, device=dev, dtype=bf).transpose(1, 2)
+        fl_f = 4.0 * nb * HEADS * n * n * DHEAD
+        by = 4 * nb * n * HEADS * DHEAD * 2
+
+        def fwd():
+            with torch.no_grad():
+                AttentionFn.apply(*qkv)
+
+        def run():
+            AttentionFn.apply(*qkv).backward(gy)
+
+        bench.time(f"attention fwd n={n}", fwd, by, fl_f)
+        bench.time(f"attention fwd+bwd n={n}", run, by * 3, fl_f * 3.5)
+
+
 def op_band(bench: _Bench):
     """BandSplit (config-3 bands: 62 bands over 1025 stereo complex bins, 1032 rows, D = 192)."""
     import ctypes
@@ -343,7 +366,7 @@ def op_mask(bench: _Bench):
     bench.time("mask_estimator_tc fwd+bwd", fwd_bwd, 3 * byt, 3 * flops)
 
 
-OPS = {"gate": op_gate, "band": op_band, "mel": op_mel, "mask": op_mask, "rms": op_rms, "qkv": op_qkv, "ff": op_ff, "sdpa": op_sdpa}
+OPS = {"gate": op_gate, "band": op_band, "mel": op_mel, "mask": op_mask, "rms": op_rms, "qkv": op_qkv, "ff": op_ff, "sdpa": op_sdpa, "attn": op_attn}
 
 
 def main(argv=None) -> None:

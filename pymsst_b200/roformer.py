@@ -23,8 +23,12 @@ The per-layer hot path runs through :mod:`pymsst_b200.fused`:
 * mask recombination (scatter-add-average) and complex mask product:
   :class:`~pymsst_b200.fused.BandRecombineFn`.
 
-Attention scores use ``F.scaled_dot_product_attention``; the remaining
-projections (feed-forward, attention output) are plain cuBLAS GEMMs.
+* attention core softmax(q k^T / sqrt(dh)) v: :class:`~pymsst_b200.fused.AttentionFn`
+  (16-bit, head dim 64; ``F.scaled_dot_product_attention`` otherwise or when
+  a library backend is selected with ``set_cuda_attention_backend``).
+
+The feed-forward projections and the attention output projection are cuBLAS
+GEMMs (the feed-forward GELU and bias gradients run on this package's kernels).
 There is no CPU path: a forward on CPU tensors raises
 ``FusedKernelUnavailable``.
 """
@@ -36,6 +40,7 @@ from torch import nn
 
 from . import bands as band_tables
 from .fused import (
+    AttentionFn,
     AttentionGateFn,
     BandGatherFn,
     BandRecombineFn,
@@ -47,6 +52,7 @@ from .fused import (
     RMSNormFn,
     compute_dtype,
     rotary_tables,
+    attention_supported,
     tensor_core_ok,
 )
 
@@ -127,21 +133,36 @@ class RotaryEmbedding(nn.Module):
         return hit
 
 
-# Attention-core library kernel per sequence length, from fwd+bwd timings of
-# [B, 8, N, 64] bf16 on B200: cuDNN's fused attention is fastest for the long
-# (time-axis) sequences, the memory-efficient kernel for the short band axis.
+# Library attention kernel per sequence length, used where the own kernels do
+# not apply (fp32, dropout, head dim other than 64) or when a library backend
+# is asked for: from fwd+bwd timings of [B, 8, N, 64] bf16 on B200, cuDNN's
+# fused attention is the fastest library kernel for the long (time-axis)
+# sequences, the memory-efficient kernel for the short band axis.
 _SHORT_SEQ = 128
 
+# Names accepted by Attention.set_cuda_attention_backend: the reference's
+# cuda_attention_backend choices (src/pymsst/cli.py:61) plus "pmb", the
+# attention kernels of this package ("auto" and "default" select them too).
+ATTENTION_BACKENDS = ("auto", "default", "pmb", "cudnn", "efficient", "math", "flash")
 
-def _attention(q, k, v, dropout_p):
-    if q.is_cuda and q.dtype in (torch.bfloat16, torch.float16):
+
+def _attention(q, k, v, dropout_p, backend="auto"):
+    if backend in ("auto", "default", "pmb") and attention_supported(q, dropout_p):
+        return AttentionFn.apply(q, k, v)
+    if q.is_cuda:
         from torch.nn.attention import SDPBackend, sdpa_kernel
 
-        backend = SDPBackend.EFFICIENT_ATTENTION if q.shape[-2] <= _SHORT_SEQ else SDPBackend.CUDNN_ATTENTION
-        order = [backend] + [b for b in (SDPBackend.CUDNN_ATTENTION, SDPBackend.FLASH_ATTENTION,
-                                           SDPBackend.EFFICIENT_ATTENTION, SDPBackend.MATH) if b != backend]
-        with sdpa_kernel(order, set_priority=True):
-            return F.scaled_dot_product_attention(q, k, v, dropout_p=dropout_p)
+        forced = {"cudnn": SDPBackend.CUDNN_ATTENTION, "efficient": SDPBackend.EFFICIENT_ATTENTION,
+                  "math": SDPBackend.MATH, "flash": SDPBackend.FLASH_ATTENTION}.get(backend)
+        if forced is not None:
+            with sdpa_kernel([forced]):
+                return F.scaled_dot_product_attention(q, k, v, dropout_p=dropout_p)
+        if q.dtype in (torch.bfloat16, torch.float16):
+            first = SDPBackend.EFFICIENT_ATTENTION if q.shape[-2] <= _SHORT_SEQ else SDPBackend.CUDNN_ATTENTION
+            order = [first] + [b for b in (SDPBackend.CUDNN_ATTENTION, SDPBackend.FLASH_ATTENTION,
+                                           SDPBackend.EFFICIENT_ATTENTION, SDPBackend.MATH) if b != first]
+            with sdpa_kernel(order, set_priority=True):
+                return F.scaled_dot_product_attention(q, k, v, dropout_p=dropout_p)
     return F.scaled_dot_product_attention(q, k, v, dropout_p=dropout_p)
 
 
@@ -157,6 +178,15 @@ class Attention(nn.Module):
         self.to_qkv = nn.Linear(dim, inner * 3, bias=False)
         self.to_gates = nn.Linear(dim, heads)
         self.to_out = nn.Sequential(nn.Linear(inner, dim, bias=False), nn.Dropout(dropout))
+        self.attention_backend = "auto"
+
+    def set_cuda_attention_backend(self, backend: str) -> None:
+        """Attention kernel choice, the hook the reference's training module calls on every module
+        (src/pymsst/training/module.py:416-425); one of ATTENTION_BACKENDS."""
+        name = str(backend).strip().lower()
+        if name not in ATTENTION_BACKENDS:
+            raise ValueError(f"unknown cuda attention backend {backend!r}; expected one of {ATTENTION_BACKENDS}")
+        self.attention_backend = name
 
     def forward(self, x, seq_len=None, inner=1):
         """x [b, n, d]; or any [..., d] whose rows are ordered (outer, position, inner) with sequences of
@@ -171,7 +201,7 @@ class Attention(nn.Module):
             cos, sin, cos_t, sin_t = self.rotary_embed.tables(n, x.device)
         q, k, v = QKVRotaryFn.apply(xn.reshape(b, n, d), self.to_qkv.weight, cos, sin, cos_t, sin_t, self.heads,
                                     inner)
-        attn = _attention(q, k, v, self.dropout if self.training else 0.0)
+        attn = _attention(q, k, v, self.dropout if self.training else 0.0, self.attention_backend)
         gated = AttentionGateFn.apply(attn, xn.reshape(rows, d), self.to_gates.weight, self.to_gates.bias, inner)
         out = F.linear(gated, self.to_out[0].weight.to(gated.dtype))
         return self.to_out[1](out).reshape(x.shape)
