@@ -494,14 +494,17 @@ PMB_API int pmb_mask_estimator_tc_backward(const void* grad_out, const void* x, 
  * element strides (sequence, position, head) each, all multiples of 8 with
  * the 64 head elements contiguous; `strides` holds them plane by plane
  * (forward: q, k, v, o = 12 values; backward: q, k, v, o, grad_out, grad_q,
- * grad_k, grad_v = 24 values).  lse: fp32 [sequences * heads, seq_len], the
- * natural-log row sums written by the forward and read by the backward.
- * The backward needs pmb_attention_backward_workspace_size bytes of
- * workspace (the row sums D = rowsum(grad_out * o)) and is deterministic.
+ * grad_k, grad_v = 24 values).  lse: fp32 [sequences * heads, ld] with
+ * ld = pmb_attention_row_pitch(seq_len) (seq_len rounded up to a multiple of
+ * 4), 16-byte aligned: the natural-log row sums written by the forward and
+ * read by the backward.  The backward needs
+ * pmb_attention_backward_workspace_size bytes of 16-byte aligned workspace
+ * (the row sums D = rowsum(grad_out * o), same layout) and is deterministic.
  * Replaces torch.nn.functional.scaled_dot_product_attention in pymss-core's
  * Attention module, whose backend the reference selects with
  * cuda_attention_backend (src/pymsst/training/module.py:96-107, :416-425).
  * ---------------------------------------------------------------------- */
+PMB_API int64_t pmb_attention_row_pitch(int64_t seq_len);
 PMB_API int pmb_attention_forward(const void* q, const void* k, const void* v, void* o, float* lse,
                                   int64_t sequences, int64_t seq_len, int64_t heads, int64_t dim_head,
                                   const int64_t* strides, float scale, int dtype, void* stream);

@@ -86,6 +86,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         _i, [_p, _p, _p, _p, _p, _i64, _i, _i64, _i64, _i, _pi64, _pp, _pp, _p, _i, _i, _p, _i64, _p]),
     "pmb_qkv_rotary_split": (_i, [_p, _p, _p, _i64, _i64, _i64, _i64, _p, _p, _p, _i, _i, _i64, _p]),
     "pmb_qkv_rotary_merge": (_i, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _i, _i, _i64, _i64, _i64, _i64, _p]),
+    "pmb_attention_row_pitch": (_i64, [_i64]),
     "pmb_attention_forward": (_i, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _pi64, _f32, _i, _p]),
     "pmb_attention_backward_workspace_size": (_i64, [_i64, _i64, _i64]),
     "pmb_attention_backward": (

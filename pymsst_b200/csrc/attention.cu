@@ -1,28 +1,36 @@
 // Scaled-dot-product attention core of the axial transformers (head dim 64,
-// no mask, no dropout), forward and backward, bf16 / fp16 in, fp32 math.
+// no mask, no dropout), forward and backward on the tcgen05 tensor cores,
+// bf16 / fp16 in, fp32 accumulation and softmax.
 //
 //   S = Q K^T * scale,  P = softmax_rows(S),  O = P V,  lse = log(sum exp S)
 //   backward:  D = rowsum(dO * O),  dP = dO V^T,  dS = P * (dP - D),
 //              dV = P^T dO,  dQ = scale * dS K,  dK = scale * dS^T Q
 //
-// Forward: attn_fwd_tc, a persistent warp-specialised tcgen05 kernel (TMA
-// tiles, S and per-chunk O accumulators in tensor memory, one softmax thread
-// per query row); described above the kernel.
-// Backward: two kernels over 64-row blocks of one (sequence, head), four
-// warps per CTA, each warp owning 16 rows of the block, products on
-// mma.sync m16n8k16 (fp32 accumulators) from ldmatrix fragments:
-//   attn_bwd_dq    query block; computes D for its rows, then streams K/V
-//                  chunks (double-buffered cp.async ring) recomputing P and
-//                  dP and accumulating dQ;
-//   attn_bwd_dkdv  key block; streams Q/dO chunks (with lse and D) and
-//                  accumulates dK and dV for its keys.
-// No atomics: every output row is owned by one thread or warp, so results
+// Three persistent, warp-specialised kernels with the same shape: a work
+// item is 128 rows (queries, or keys for dK/dV) of one (sequence, head); two
+// CTAs per SM take items blockIdx.x, + gridDim.x, ...; 192 threads:
+//   warp 0   TMA producers: lane 0 loads the item's 128-row tiles, lane 1
+//            streams the 64-row chunks of the other operand through a ring
+//            (4-D plane maps: rows >= N read as zeros);
+//   warp 1   lane 0 issues tcgen05.mma (M 128, N 64, K 16 per instruction,
+//            fp32 accumulators in tensor memory);
+//   warps 2..5  one row per thread (TMEM lane = row): softmax / gradient
+//            arithmetic on the accumulators, the 16-bit P / dS operand rows
+//            written to shared memory in the 128-byte-swizzled K-major
+//            layout the MMA reads, and the item's output rows.
+// Each accumulator product uses the staged tiles as they arrive: a K/V, Q or
+// dO tile serves as a K-major operand in one product and as an MN-major
+// operand (N = head dim) in the other.  Chunks are counted across items, so
+// barrier phases run on; every wait is bounded (on a timeout the roles stop,
+// tensor memory is freed and the site is left in the attention timeout
+// flag).  No atomics: each output row is written by one thread, so results
 // are deterministic.  P and dS are rounded to the input type before their
 // products, as torch's fused attention kernels do.
 //
 // Layout: q, k, v, o and their gradients are [sequences, N, H, 64] planes
 // with any sequence / position / head element strides (multiples of 8, the
-// 64 head elements contiguous); lse and D are fp32 [sequences * H, N].
+// 64 head elements contiguous); lse and D are fp32 [sequences * H, ld] with
+// ld = N rounded up to a multiple of 4 (16-byte rows for TMA).
 // Reference semantics: torch.nn.functional.scaled_dot_product_attention with
 // the default scale 1/sqrt(64), as called by the BS-/Mel-RoFormer Attention
 // module of pymss-core (the attention backend the reference selects with
@@ -36,11 +44,12 @@ unsigned int timeout_flag_attn(int reset) { return umma::flag_reader(reset); }
 namespace {
 
 constexpr int kD = 64;          // head dim
-constexpr int kLd = kD + 8;     // shared-memory row pitch in elements (144 bytes)
-constexpr int kBlock = 64;      // rows per CTA block and per streamed chunk (backward)
-constexpr int kWarps = 4;
-constexpr int kThreads = 32 * kWarps;
-constexpr int kTile = kBlock * kLd;  // elements of one staged 64-row tile
+constexpr int BM = 128;         // rows per work item
+constexpr int BN = 64;          // rows per streamed chunk
+constexpr int kThreads = 192;   // TMA warp, MMA warp, 4 row warps
+constexpr int TILE128 = BM * kD * 2;  // 16 KB: 128 rows x 64 16-bit
+constexpr int TILE64 = BN * kD * 2;   // 8 KB
+constexpr uint32_t kTmemCols = 256;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 
@@ -48,205 +57,119 @@ struct Plane {
   int64_t s_b, s_n, s_h;  // element strides of a [sequences, N, H, 64] plane
 };
 
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
-               "r"(valid ? 16 : 0));
-}
-
-__device__ __forceinline__ void cp_async4(void* dst, const void* src, bool valid) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(valid ? 4 : 0));
-}
-
-__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;"); }
-
-template <int N>
-__device__ __forceinline__ void cp_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N));
-}
-
-__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(smem_u32(p)));
-}
-
-__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void* p) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(smem_u32(p)));
-}
-
-// c += a * b for one m16n8k16 tile (fp32 accumulators)
-template <typename T>
-__device__ __forceinline__ void mma(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
-        "{%0, %1, %2, %3};"
-        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-  } else {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
-        "{%0, %1, %2, %3};"
-        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-  }
-}
-
 template <typename T>
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
-  const T a = Elem<T>::from_f(lo), b = Elem<T>::from_f(hi);
-  return (uint32_t)(*reinterpret_cast<const uint16_t*>(&a)) |
-         ((uint32_t)(*reinterpret_cast<const uint16_t*>(&b)) << 16);
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  } else {
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
 }
 
-template <int N>
-__device__ __forceinline__ void zero(float (&a)[N][4]) {
-#pragma unroll
-  for (int i = 0; i < N; ++i) a[i][0] = a[i][1] = a[i][2] = a[i][3] = 0.f;
+// Byte offset of 16-byte chunk ch (elements 8ch..8ch+7) of row r in a
+// 128-byte-swizzled K-major tile of 64-element rows.
+__device__ __forceinline__ uint32_t sw128(int r, int ch) {
+  return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((ch ^ (r & 7)) << 4));
 }
 
-// Rows [row0, row0 + 64) of one (sequence, head) of a plane into a staged
-// tile (cp.async; rows >= N are zero-filled).  The whole CTA.
+// 32 fp32 values -> chunks [c0, c0 + 4) of row r of a 16-bit SW128 tile
 template <typename T>
-__device__ __forceinline__ void load_tile(T* dst, const T* src, int64_t s_n, int row0, int N) {
+__device__ __forceinline__ void put_row32(uint8_t* tile, int r, int c0, const float (&v)[32]) {
 #pragma unroll
-  for (int i = threadIdx.x; i < kBlock * (kD / 8); i += kThreads) {
-    const int r = i >> 3, c = (i & 7) * 8, gr = row0 + r;
-    const bool ok = gr < N;
-    cp_async16(dst + r * kLd + c, src + (ok ? (int64_t)gr * s_n + c : 0), ok);
-  }
+  for (int i = 0; i < 4; ++i)
+    *reinterpret_cast<uint4*>(tile + sw128(r, c0 + i)) =
+        make_uint4(pack2<T>(v[8 * i], v[8 * i + 1]), pack2<T>(v[8 * i + 2], v[8 * i + 3]),
+                   pack2<T>(v[8 * i + 4], v[8 * i + 5]), pack2<T>(v[8 * i + 6], v[8 * i + 7]));
 }
 
-// A fragments of a 16 x 64 row-major slab of a staged tile: a[k-step][4]
+// 64 fp32 values (times mul) -> one 128-byte row of a global plane
 template <typename T>
-__device__ __forceinline__ void load_a(uint32_t (&a)[4][4], const T* slab) {
-  const int lane = threadIdx.x & 31;
-  const int r = (lane & 7) + 8 * ((lane >> 3) & 1), c = 8 * (lane >> 4);
+__device__ __forceinline__ void store_row64(T* dst, const float (&a)[32], const float (&b)[32], float mul) {
 #pragma unroll
-  for (int ks = 0; ks < 4; ++ks) ldsm_x4(a[ks], slab + r * kLd + ks * 16 + c);
+  for (int i = 0; i < 4; ++i)
+    *reinterpret_cast<uint4*>(dst + 8 * i) =
+        make_uint4(pack2<T>(a[8 * i] * mul, a[8 * i + 1] * mul), pack2<T>(a[8 * i + 2] * mul, a[8 * i + 3] * mul),
+                   pack2<T>(a[8 * i + 4] * mul, a[8 * i + 5] * mul), pack2<T>(a[8 * i + 6] * mul, a[8 * i + 7] * mul));
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    *reinterpret_cast<uint4*>(dst + 32 + 8 * i) =
+        make_uint4(pack2<T>(b[8 * i] * mul, b[8 * i + 1] * mul), pack2<T>(b[8 * i + 2] * mul, b[8 * i + 3] * mul),
+                   pack2<T>(b[8 * i + 4] * mul, b[8 * i + 5] * mul), pack2<T>(b[8 * i + 6] * mul, b[8 * i + 7] * mul));
 }
 
-// acc[0..2*NP) (16 x 16*NP) += A (16 x 64, fragments a) * rows^T, where rows
-// are NP*16 consecutive rows of a staged tile starting at `rows` (the n index
-// runs over those rows, k over the 64 columns).
-template <typename T, int NP>
-__device__ __forceinline__ void mma_rows_t(float (&acc)[2 * NP][4], const uint32_t (&a)[4][4], const T* rows) {
-  const int lane = threadIdx.x & 31;
-  const int rr = (lane & 7) + 8 * (lane >> 4), cc = 8 * ((lane >> 3) & 1);
+// D[tmem] (+)= A * B^T over K = 64: A a 128-row K-major SW128 tile; B either
+// a K-major tile (its rows are the N index) or an MN-major one (64 rows of K,
+// the 64 head elements are the N index).
+__device__ __forceinline__ void mma_k64(uint32_t d, uint32_t a_base, uint32_t b_base, bool b_mn, uint32_t idesc,
+                                        bool accumulate) {
 #pragma unroll
-  for (int ks = 0; ks < 4; ++ks) {
-#pragma unroll
-    for (int np = 0; np < NP; ++np) {
-      uint32_t b[4];
-      ldsm_x4(b, rows + (np * 16 + rr) * kLd + ks * 16 + cc);
-      mma<T>(acc[2 * np], a[ks], b[0], b[1]);
-      mma<T>(acc[2 * np + 1], a[ks], b[2], b[3]);
-    }
+  for (int kk = 0; kk < 4; ++kk) {
+    const uint64_t a = umma::smem_desc_sw128(a_base + kk * 32, 16, 1024);
+    const uint64_t b = b_mn ? umma::smem_desc_sw128(b_base + kk * 16 * 128, BN * 128, 1024)
+                            : umma::smem_desc_sw128(b_base + kk * 32, 16, 1024);
+    umma::mma_f16(d, a, b, idesc, (accumulate || kk) ? 1u : 0u);
   }
 }
 
-// acc[0..8) (16 x 64) += A (16 x 16*KS, fragments a) * rows, where rows are
-// 16*KS consecutive rows of a staged tile (the k index runs over those rows,
-// n over the 64 columns).
-template <typename T, int KS>
-__device__ __forceinline__ void mma_rows(float (&acc)[8][4], const uint32_t (&a)[KS][4], const T* rows) {
-  const int lane = threadIdx.x & 31;
-  const int rr = (lane & 7) + 8 * ((lane >> 3) & 1), cc = 8 * (lane >> 4);
-#pragma unroll
-  for (int ks = 0; ks < KS; ++ks) {
-#pragma unroll
-    for (int np = 0; np < 4; ++np) {
-      uint32_t b[4];
-      ldsm_x4_t(b, rows + (ks * 16 + rr) * kLd + np * 16 + cc);
-      mma<T>(acc[2 * np], a[ks], b[0], b[1]);
-      mma<T>(acc[2 * np + 1], a[ks], b[2], b[3]);
-    }
-  }
-}
-
-// C fragments of NT 8-column tiles (16 rows) -> A fragments of NT/2 k-steps
-template <typename T, int NT>
-__device__ __forceinline__ void c_to_a(uint32_t (&a)[NT / 2][4], const float (&c)[NT][4]) {
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
-    a[nt >> 1][(nt & 1) * 2 + 0] = pack2<T>(c[nt][0], c[nt][1]);
-    a[nt >> 1][(nt & 1) * 2 + 1] = pack2<T>(c[nt][2], c[nt][3]);
-  }
-}
-
-// A warp's 16 x 64 accumulator (times `mul`) through its own 16 staged rows
-// to rows [r0, r0 + 16) of a plane (rows >= N skipped), 16-byte segments.
 template <typename T>
-__device__ __forceinline__ void store_rows(const float (&acc)[8][4], float mul, T* stage, T* dst, int64_t s_n, int r0,
-                                           int N) {
-  const int lane = threadIdx.x & 31, g = lane >> 2, tig = lane & 3;
-#pragma unroll
-  for (int nt = 0; nt < 8; ++nt) {
-    const int c = nt * 8 + tig * 2;
-    *reinterpret_cast<uint32_t*>(stage + g * kLd + c) = pack2<T>(acc[nt][0] * mul, acc[nt][1] * mul);
-    *reinterpret_cast<uint32_t*>(stage + (g + 8) * kLd + c) = pack2<T>(acc[nt][2] * mul, acc[nt][3] * mul);
-  }
+struct Idesc {
+  static constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+  static constexpr uint32_t K = umma::idesc_f16(kBf16, false, false, BM, BN);  // B K-major, N = 64 rows
+  static constexpr uint32_t MN = umma::idesc_f16(kBf16, false, true, BM, kD);  // B MN-major, N = head dim
+};
+
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
+  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+}
+
+// Arrive once per row warp on `bar` after this thread's shared / tensor
+// memory accesses (count 4 barriers).
+__device__ __forceinline__ void warp_arrive(uint64_t* bar, bool wrote_smem) {
+  if (wrote_smem) umma::fence_proxy_async_smem();
+  umma::tc_fence_before();
   __syncwarp();
-#pragma unroll
-  for (int it = 0; it < 4; ++it) {
-    const int r = it * 4 + (lane >> 3), c = (lane & 7) * 8;
-    if (r0 + r < N)
-      *reinterpret_cast<uint4*>(dst + (int64_t)(r0 + r) * s_n + c) = *reinterpret_cast<const uint4*>(stage + r * kLd + c);
-  }
+  if ((threadIdx.x & 31) == 0) umma::mbar_arrive(bar);
+}
+
+struct Item {
+  int bh, blk, b, h;
+};
+
+__device__ __forceinline__ Item item_at(int item, int nblk, int H) {
+  Item it;
+  it.bh = item / nblk;
+  it.blk = item - it.bh * nblk;
+  it.b = it.bh / H;
+  it.h = it.bh - it.b * H;
+  return it;
 }
 
 // ---------------------------------------------------------------- forward
-// tcgen05 forward.  Work item = 128 query rows of one (sequence, head);
-// persistent CTAs (two per SM) take items blockIdx.x, + gridDim.x, ...
-//   warp 0 (one lane)  TMA: the item's Q tile (4-D plane map, rows >= N read
-//                      as zeros), then its K/V chunks into a kStages ring;
-//   warp 1 (one lane)  tcgen05.mma: S_c = Q K_c^T into TMEM S[c % 2]
-//                      (M 128, N 64, K 64), and one chunk behind,
-//                      O_c = P_c V_c into TMEM O[c % 2] (V read as an MN-major
-//                      operand straight from its TMA tile);
-//   warps 2..5         softmax, one query row per thread (TMEM lane = row):
-//                      reads S_c, keeps the running max / sum, writes P_c as
-//                      bf16/fp16 into shared memory in the 128-byte-swizzled
-//                      K-major layout the MMA reads, then folds O_{c-1} into
-//                      its fp32 row accumulator (rescaled by the max change)
-//                      and finally writes O and the row lse.
-// Chunks are counted across items, so every barrier phase runs on.  All
-// waits are bounded; on a timeout the roles stop, TMEM is freed and the
-// site is left in the attention timeout flag.
-namespace tcf {
-constexpr int BM = 128;        // query rows per item
-constexpr int BN = 64;         // keys per chunk
-constexpr int kThreads = 192;  // TMA warp, MMA warp, 4 softmax warps
-constexpr int kStages = 3;     // K/V chunk ring
-constexpr int Q_BYTES = BM * kD * 2;
-constexpr int KV_BYTES = BN * kD * 2;
-constexpr int P_BYTES = BM * BN * 2;
-constexpr int OFF_KV = Q_BYTES;
-constexpr int OFF_P = OFF_KV + kStages * 2 * KV_BYTES;
-constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
+// Item = 128 queries.  Lane 0 of warp 0 loads Q, lane 1 streams K/V chunks;
+// the MMA lane issues S_c = Q K_c^T into TMEM S[c % 2] and, one chunk
+// behind, O_c = P_c V_c into TMEM O[c % 2]; the row threads read S_c, keep
+// the running max / sum, write P_c and fold O_{c-1} into their fp32 row
+// accumulators (rescaled by the change of the max), then write O and lse.
+namespace fw {
+constexpr int kStages = 3;
+constexpr int OFF_KV = TILE128;                        // kStages x (K, V)
+constexpr int OFF_P = OFF_KV + kStages * 2 * TILE64;   // 2 x P
+constexpr int OFF_BAR = OFF_P + 2 * BM * BN * 2;
 constexpr int kBars = 2 + 2 * kStages + 8;
-constexpr int SMEM = OFF_BAR + kBars * 8 + 16 + 1024;  // + slack for the 1024-byte alignment
-constexpr uint32_t kTmemCols = 256;                     // S[2] at columns 0, 64; O[2] at 128, 192
+constexpr int SMEM = OFF_BAR + kBars * 8 + 16 + 1024;
 constexpr uint32_t kTmemO = 128;
-}  // namespace tcf
+}  // namespace fw
 
 template <typename T>
-__global__ void __launch_bounds__(tcf::kThreads, 2)
+__global__ void __launch_bounds__(kThreads, 2)
     attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                 const __grid_constant__ CUtensorMap tmV, T* __restrict__ o, float* __restrict__ lse, Plane po, int N,
-                int H, int nqb, int total, float scale) {
-  using namespace tcf;
-  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
-  constexpr uint32_t IDESC_S = umma::idesc_f16(kBf16, false, false, BM, BN);
-  constexpr uint32_t IDESC_O = umma::idesc_f16(kBf16, false, true, BM, kD);
+                int H, int ldl, int nblk, int total, float scale) {
+  using namespace fw;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem = align1024(smem_raw);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
   uint64_t* q_full = bars;
   uint64_t* q_empty = bars + 1;
@@ -283,48 +206,47 @@ __global__ void __launch_bounds__(tcf::kThreads, 2)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    if (lane == 0) {
-      // ------------------------------------------------ TMA producer
+    if (lane == 0) {  // Q tiles
       umma::tma_prefetch(&tmQ);
-      umma::tma_prefetch(&tmK);
-      umma::tma_prefetch(&tmV);
-      uint32_t cc = 0, t = 0;
+      uint32_t t = 0;
       for (int item = blockIdx.x; item < total && !abort_flag; item += gridDim.x, ++t) {
-        const int bh = item / nqb, qb = item - bh * nqb, b = bh / H, h = bh - b * H;
+        const Item it = item_at(item, nblk, H);
         if (!umma::mbar_wait(q_empty, (t & 1) ^ 1, 0x41)) {
           abort_flag = 1;
           break;
         }
-        umma::mbar_arrive_expect_tx(q_full, Q_BYTES);
-        umma::tma_load_4d(smem, &tmQ, q_full, 0, h, qb * BM, b);
+        umma::mbar_arrive_expect_tx(q_full, TILE128);
+        umma::tma_load_4d(smem, &tmQ, q_full, 0, it.h, it.blk * BM, it.b);
+      }
+    } else if (lane == 1) {  // K/V chunks
+      umma::tma_prefetch(&tmK);
+      umma::tma_prefetch(&tmV);
+      uint32_t cc = 0;
+      for (int item = blockIdx.x; item < total && !abort_flag; item += gridDim.x) {
+        const Item it = item_at(item, nblk, H);
         for (int j = 0; j < nch; ++j, ++cc) {
           const int s = cc % kStages;
           if (!umma::mbar_wait(&kv_empty[s], ((cc / kStages) & 1) ^ 1, 0x42)) {
             abort_flag = 1;
             break;
           }
-          uint8_t* dst = smem + OFF_KV + s * 2 * KV_BYTES;
-          umma::mbar_arrive_expect_tx(&kv_full[s], 2 * KV_BYTES);
-          umma::tma_load_4d(dst, &tmK, &kv_full[s], 0, h, j * BN, b);
-          umma::tma_load_4d(dst + KV_BYTES, &tmV, &kv_full[s], 0, h, j * BN, b);
+          uint8_t* dst = smem + OFF_KV + s * 2 * TILE64;
+          umma::mbar_arrive_expect_tx(&kv_full[s], 2 * TILE64);
+          umma::tma_load_4d(dst, &tmK, &kv_full[s], 0, it.h, j * BN, it.b);
+          umma::tma_load_4d(dst + TILE64, &tmV, &kv_full[s], 0, it.h, j * BN, it.b);
         }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      // ------------------------------------------------ MMA issuer
       // O_c = P_c V_c, issued one chunk behind S so that S_{c+1} runs during softmax c
       auto issue_o = [&](uint32_t c) -> bool {
         const int pb = c & 1;
         if (!umma::mbar_wait(&p_full[pb], (c >> 1) & 1, 0x44)) return false;
         if (!umma::mbar_wait(&o_empty[pb], ((c >> 1) & 1) ^ 1, 0x45)) return false;
         umma::tc_fence_after();
-        const uint32_t p_base = umma::smem_u32(smem + OFF_P + pb * P_BYTES);
-        const uint32_t v_base = umma::smem_u32(smem + OFF_KV + (c % kStages) * 2 * KV_BYTES + KV_BYTES);
-#pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk)
-          umma::mma_f16(tmem + kTmemO + pb * kD, umma::smem_desc_sw128(p_base + kk * 32, 16, 1024),
-                        umma::smem_desc_sw128(v_base + kk * 16 * 128, BN * 128, 1024), IDESC_O, kk != 0);
+        mma_k64(tmem + kTmemO + pb * kD, umma::smem_u32(smem + OFF_P + pb * BM * BN * 2),
+                umma::smem_u32(smem + OFF_KV + (c % kStages) * 2 * TILE64 + TILE64), true, Idesc<T>::MN, false);
         umma::mma_commit(&o_full[pb]);
         umma::mma_commit(&kv_empty[c % kStages]);
         return true;
@@ -337,7 +259,6 @@ __global__ void __launch_bounds__(tcf::kThreads, 2)
           break;
         }
         umma::tc_fence_after();
-        const uint32_t q_base = umma::smem_u32(smem);
         for (int j = 0; j < nch; ++j, ++cc) {
           const int s = cc % kStages;
           if (!umma::mbar_wait(&kv_full[s], (cc / kStages) & 1, 0x46)) {
@@ -345,11 +266,8 @@ __global__ void __launch_bounds__(tcf::kThreads, 2)
             break;
           }
           umma::tc_fence_after();
-          const uint32_t k_base = umma::smem_u32(smem + OFF_KV + s * 2 * KV_BYTES);
-#pragma unroll
-          for (int kk = 0; kk < kD / 16; ++kk)
-            umma::mma_f16(tmem + (cc & 1) * BN, umma::smem_desc_sw128(q_base + kk * 32, 16, 1024),
-                          umma::smem_desc_sw128(k_base + kk * 32, 16, 1024), IDESC_S, kk != 0);
+          mma_k64(tmem + (cc & 1) * BN, umma::smem_u32(smem), umma::smem_u32(smem + OFF_KV + s * 2 * TILE64), false,
+                  Idesc<T>::K, false);
           umma::mma_commit(&s_full[cc & 1]);
           if (j == nch - 1) umma::mma_commit(q_empty);
           if (cc > 0 && !issue_o(cc - 1)) {
@@ -362,19 +280,18 @@ __global__ void __launch_bounds__(tcf::kThreads, 2)
       if (!ok) abort_flag = 1;
     }
   } else {
-    // ---------------------------------------------------- softmax warps
     const int quarter = warp & 3, row = quarter * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const float sl2 = scale * kLog2e;
     uint32_t cc = 0;
     for (int item = blockIdx.x; item < total && !abort_flag; item += gridDim.x) {
-      const int bh = item / nqb, qb = item - bh * nqb, b = bh / H, h = bh - b * H;
+      const Item it = item_at(item, nblk, H);
       float m = -INFINITY, l = 0.f, corr_prev = 0.f;
       float acc[kD];
 #pragma unroll
       for (int c = 0; c < kD; ++c) acc[c] = 0.f;
       bool ok = true;
-      // fold O of chunk c into acc (acc * corr + O_c), release the O buffer
+      // acc = acc * corr + O_c; release the O buffer
       auto fold_o = [&](uint32_t c, float corr) -> bool {
         const int ob = c & 1;
         if (!umma::mbar_wait(&o_full[ob], (c >> 1) & 1, 0x48)) return false;
@@ -382,13 +299,11 @@ __global__ void __launch_bounds__(tcf::kThreads, 2)
         float v0[32], v1[32];
         umma::tmem_ld32(tmem + lane_off + kTmemO + ob * kD, v0);
         umma::tmem_ld32(tmem + lane_off + kTmemO + ob * kD + 32, v1);
-        umma::tc_fence_before();
-        __syncwarp();
-        if (lane == 0) umma::mbar_arrive(&o_empty[ob]);
+        warp_arrive(&o_empty[ob], false);
 #pragma unroll
         for (int c2 = 0; c2 < 32; ++c2) {
-          acc[c2] = acc[c2] * corr + v0[c2];
-          acc[32 + c2] = acc[32 + c2] * corr + v1[c2];
+          acc[c2] = fmaf(acc[c2], corr, v0[c2]);
+          acc[32 + c2] = fmaf(acc[32 + c2], corr, v1[c2]);
         }
         return true;
       };
@@ -399,38 +314,39 @@ __global__ void __launch_bounds__(tcf::kThreads, 2)
           break;
         }
         umma::tc_fence_after();
-        float s[BN];
-        umma::tmem_ld32(tmem + lane_off + sb * BN, *reinterpret_cast<float(*)[32]>(&s[0]));
-        umma::tmem_ld32(tmem + lane_off + sb * BN + 32, *reinterpret_cast<float(*)[32]>(&s[32]));
+        float s0[32], s1[32];
+        umma::tmem_ld32(tmem + lane_off + sb * BN, s0);
+        umma::tmem_ld32(tmem + lane_off + sb * BN + 32, s1);
         const int kc = j * BN;
-        float mx = -INFINITY;
+        if (kc + BN > N) {  // keys past the end of the sequence
 #pragma unroll
-        for (int c = 0; c < BN; ++c) {
-          const float v = (kc + c < N) ? s[c] * sl2 : -INFINITY;
-          s[c] = v;
-          mx = fmaxf(mx, v);
-        }
-        const float mn = fmaxf(m, mx);  // finite: every chunk holds a key < N
-        const float corr = exp2f(m - mn);
-        float sum = 0.f;
-        uint8_t* prow = smem + OFF_P + sb * P_BYTES + (row >> 3) * 1024 + (row & 7) * 128;
-#pragma unroll
-        for (int ch = 0; ch < BN / 8; ++ch) {
-          uint32_t w[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float p0 = exp2f(s[ch * 8 + 2 * e] - mn), p1 = exp2f(s[ch * 8 + 2 * e + 1] - mn);
-            sum += p0 + p1;
-            w[e] = pack2<T>(p0, p1);
+          for (int c = 0; c < 32; ++c) {
+            if (kc + c >= N) s0[c] = -INFINITY;
+            if (kc + 32 + c >= N) s1[c] = -INFINITY;
           }
-          *reinterpret_cast<uint4*>(prow + ((ch ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
         }
-        l = l * corr + sum;
+        float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+        for (int c = 0; c < 32; c += 4) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) mx4[e] = fmaxf(mx4[e], fmaxf(s0[c + e], s1[c + e]));
+        }
+        // the scale is positive, so the max of the raw scores gives the max of the scaled ones
+        const float mn = fmaxf(m, fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * sl2);  // finite
+        const float corr = exp2f(m - mn);
+        float sum4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          s0[c] = exp2f(fmaf(s0[c], sl2, -mn));
+          s1[c] = exp2f(fmaf(s1[c], sl2, -mn));
+          sum4[c & 3] += s0[c] + s1[c];
+        }
+        l = fmaf(l, corr, (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
         m = mn;
-        umma::fence_proxy_async_smem();
-        umma::tc_fence_before();
-        __syncwarp();
-        if (lane == 0) umma::mbar_arrive(&p_full[sb]);
+        uint8_t* ptile = smem + OFF_P + sb * BM * BN * 2;
+        put_row32<T>(ptile, row, 0, s0);
+        put_row32<T>(ptile, row, 4, s1);
+        warp_arrive(&p_full[sb], true);
         if (j > 0 && !fold_o(cc - 1, corr_prev)) {
           ok = false;
           break;
@@ -442,20 +358,16 @@ __global__ void __launch_bounds__(tcf::kThreads, 2)
         abort_flag = 1;
         break;
       }
-      const int r = qb * BM + row;
+      const int r = it.blk * BM + row;
       if (r < N) {
-        const float inv = 1.f / l;
-        T* dst = o + b * po.s_b + h * po.s_h + (int64_t)r * po.s_n;
+        float a0[32], a1[32];
 #pragma unroll
-        for (int ch = 0; ch < kD / 8; ++ch) {
-          uint4 u;
-          u.x = pack2<T>(acc[ch * 8 + 0] * inv, acc[ch * 8 + 1] * inv);
-          u.y = pack2<T>(acc[ch * 8 + 2] * inv, acc[ch * 8 + 3] * inv);
-          u.z = pack2<T>(acc[ch * 8 + 4] * inv, acc[ch * 8 + 5] * inv);
-          u.w = pack2<T>(acc[ch * 8 + 6] * inv, acc[ch * 8 + 7] * inv);
-          *reinterpret_cast<uint4*>(dst + ch * 8) = u;
+        for (int c = 0; c < 32; ++c) {
+          a0[c] = acc[c];
+          a1[c] = acc[32 + c];
         }
-        lse[(int64_t)bh * N + r] = (m + log2f(l)) * kLn2;
+        store_row64<T>(o + it.b * po.s_b + it.h * po.s_h + (int64_t)r * po.s_n, a0, a1, 1.f / l);
+        lse[(int64_t)it.bh * ldl + r] = (m + log2f(l)) * kLn2;
       }
     }
   }
@@ -463,215 +375,426 @@ __global__ void __launch_bounds__(tcf::kThreads, 2)
   __syncthreads();
   if (warp == 0) {
     umma::tc_fence_after();
-    umma::tmem_dealloc(tmem, tcf::kTmemCols);
+    umma::tmem_dealloc(tmem, kTmemCols);
   }
 }
 
 // ------------------------------------------------------------ backward: dQ
+// Item = 128 queries.  Lane 0 of warp 0 loads the Q and dO tiles, lane 1
+// streams K/V chunks.  Per chunk the MMA lane issues S = Q K_c^T and
+// dP = dO V_c^T, waits for the row threads' dS_c, and issues dQ += dS_c K_c
+// (K_c as the MN-major operand).  The row threads compute D = rowsum(dO * O)
+// for their query once per item (written out for the dK/dV kernel), then
+// per chunk P = exp2(S * scale * log2e - lse * log2e) and dS = P (dP - D).
+namespace bq {
+constexpr int kStages = 3;
+constexpr int OFF_DO = TILE128;
+constexpr int OFF_KV = 2 * TILE128;
+constexpr int OFF_DS = OFF_KV + kStages * 2 * TILE64;
+constexpr int OFF_BAR = OFF_DS + BM * BN * 2;
+constexpr int kBars = 2 + 2 * kStages + 4;
+constexpr int SMEM = OFF_BAR + kBars * 8 + 16 + 1024;
+constexpr uint32_t kTmemDP = 64, kTmemDQ = 128;
+}  // namespace bq
+
 template <typename T>
-__global__ void __launch_bounds__(kThreads, 4)
-    attn_bwd_dq(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v, const T* __restrict__ o,
-                const T* __restrict__ dout, const float* __restrict__ lse, float* __restrict__ delta,
-                T* __restrict__ dq, Plane pq, Plane pk, Plane pv, Plane po, Plane pdo, Plane pdq, int N, int H,
-                int nqb, float scale) {
-  extern __shared__ __align__(16) uint8_t smem_raw[];
-  T* Qs = reinterpret_cast<T*>(smem_raw);
-  T* Ds = Qs + kTile;      // dO tile
-  T* Ks = Ds + kTile;      // 2 buffers
-  T* Vs = Ks + 2 * kTile;  // 2 buffers
-  const int qb = blockIdx.x % nqb, bh = blockIdx.x / nqb, b = bh / H, h = bh - b * H;
-  const T* kg = k + b * pk.s_b + h * pk.s_h;
-  const T* vg = v + b * pv.s_b + h * pv.s_h;
-  const int q0 = qb * kBlock, nch = (N + kBlock - 1) / kBlock;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, tig = lane & 3;
-  const int r0 = q0 + warp * 16;
-  const bool active = r0 < N;
-  const float sl2 = scale * kLog2e;
-
-  load_tile(Qs, q + b * pq.s_b + h * pq.s_h, pq.s_n, q0, N);
-  load_tile(Ds, dout + b * pdo.s_b + h * pdo.s_h, pdo.s_n, q0, N);
-  cp_commit();
-  load_tile(Ks, kg, pk.s_n, 0, N);
-  load_tile(Vs, vg, pv.s_n, 0, N);
-  cp_commit();
-
-  uint32_t qa[4][4], da[4][4];
-  float lse2[2] = {0.f, 0.f}, dlt[2] = {0.f, 0.f};
-  cp_wait<1>();  // Q and dO tiles
+__global__ void __launch_bounds__(kThreads, 2)
+    attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmDO,
+                   const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                   const T* __restrict__ o, const float* __restrict__ lse, float* __restrict__ delta,
+                   T* __restrict__ dq, Plane po, Plane pdq, int N, int H, int ldl, int nblk, int total, float scale) {
+  using namespace bq;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t* qd_full = bars;
+  uint64_t* qd_empty = bars + 1;
+  uint64_t* kv_full = bars + 2;
+  uint64_t* kv_empty = kv_full + kStages;
+  uint64_t* sd_full = kv_empty + kStages;
+  uint64_t* ds_full = sd_full + 1;
+  uint64_t* dq_full = ds_full + 1;
+  uint64_t* dq_empty = dq_full + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kBars);
+  __shared__ int abort_flag;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nch = (N + BN - 1) / BN;
+  if (threadIdx.x == 0) {
+    umma::mbar_init(qd_full, 1);
+    umma::mbar_init(qd_empty, 1 + 4);  // MMA commit + the row warps' D reads
+    for (int s = 0; s < kStages; ++s) {
+      umma::mbar_init(&kv_full[s], 1);
+      umma::mbar_init(&kv_empty[s], 1);
+    }
+    umma::mbar_init(sd_full, 1);
+    umma::mbar_init(ds_full, 4);
+    umma::mbar_init(dq_full, 1);
+    umma::mbar_init(dq_empty, 4);
+    abort_flag = 0;
+    umma::fence_barrier_init();
+  }
+  if (warp == 0) umma::tmem_alloc(tmem_slot, kTmemCols);
+  umma::tc_fence_before();
   __syncthreads();
-  if (active) {
-    load_a(qa, Qs + warp * 16 * kLd);
-    load_a(da, Ds + warp * 16 * kLd);
-    // D = rowsum(dO * O) of this warp's rows: lane pair (2i, 2i+1) sums row i's halves
-    const int dr = lane >> 1, dh = (lane & 1) * 32;
-    float dpart = 0.f;
-    if (r0 + dr < N) {
-      const T* orow = o + b * po.s_b + h * po.s_h + (int64_t)(r0 + dr) * po.s_n + dh;
-      const T* drow = Ds + (warp * 16 + dr) * kLd + dh;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const uint4 o4 = *reinterpret_cast<const uint4*>(orow + i * 8);
-        const uint4 d4 = *reinterpret_cast<const uint4*>(drow + i * 8);
-        const T* oe = reinterpret_cast<const T*>(&o4);
-        const T* de = reinterpret_cast<const T*>(&d4);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) dpart += Elem<T>::to_f(oe[e]) * Elem<T>::to_f(de[e]);
-      }
-    }
-    dpart += __shfl_xor_sync(0xffffffffu, dpart, 1);
-    if (r0 + dr < N && (lane & 1) == 0) delta[(int64_t)bh * N + r0 + dr] = dpart;
-    dlt[0] = __shfl_sync(0xffffffffu, dpart, 2 * g);
-    dlt[1] = __shfl_sync(0xffffffffu, dpart, 2 * g + 16);
-    const float* lb = lse + (int64_t)bh * N;
-    lse2[0] = r0 + g < N ? lb[r0 + g] * kLog2e : 0.f;
-    lse2[1] = r0 + g + 8 < N ? lb[r0 + g + 8] * kLog2e : 0.f;
-  }
-  float dqacc[8][4];
-  zero(dqacc);
-  for (int j = 0; j < nch; ++j) {
-    const int buf = j & 1;
-    if (j + 1 < nch) {
-      load_tile(Ks + (buf ^ 1) * kTile, kg, pk.s_n, (j + 1) * kBlock, N);
-      load_tile(Vs + (buf ^ 1) * kTile, vg, pv.s_n, (j + 1) * kBlock, N);
-    }
-    cp_commit();
-    cp_wait<1>();
-    __syncthreads();
-    if (active) {
-      const T* Kc = Ks + buf * kTile;
-      const T* Vc = Vs + buf * kTile;
-      const int kc = j * kBlock;
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {  // 32-key halves of the chunk
-        float s[4][4], dp[4][4];
-        zero(s);
-        zero(dp);
-        mma_rows_t<T, 2>(s, qa, Kc + hh * 32 * kLd);
-        mma_rows_t<T, 2>(dp, da, Vc + hh * 32 * kLd);
-        const bool tail = kc + hh * 32 + 32 > N;
-#pragma unroll
-        for (int nt = 0; nt < 4; ++nt) {
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            float p = exp2f(s[nt][e] * sl2 - lse2[e >> 1]);
-            if (tail && kc + hh * 32 + nt * 8 + tig * 2 + (e & 1) >= N) p = 0.f;
-            s[nt][e] = p * (dp[nt][e] - dlt[e >> 1]);  // dS
-          }
+  umma::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {  // Q and dO tiles
+      umma::tma_prefetch(&tmQ);
+      umma::tma_prefetch(&tmDO);
+      uint32_t t = 0;
+      for (int item = blockIdx.x; item < total && !abort_flag; item += gridDim.x, ++t) {
+        const Item it = item_at(item, nblk, H);
+        if (!umma::mbar_wait(qd_empty, (t & 1) ^ 1, 0x51)) {
+          abort_flag = 1;
+          break;
         }
-        uint32_t sa[2][4];
-        c_to_a<T, 4>(sa, s);
-        mma_rows<T, 2>(dqacc, sa, Kc + hh * 32 * kLd);
+        umma::mbar_arrive_expect_tx(qd_full, 2 * TILE128);
+        umma::tma_load_4d(smem, &tmQ, qd_full, 0, it.h, it.blk * BM, it.b);
+        umma::tma_load_4d(smem + OFF_DO, &tmDO, qd_full, 0, it.h, it.blk * BM, it.b);
+      }
+    } else if (lane == 1) {  // K/V chunks
+      umma::tma_prefetch(&tmK);
+      umma::tma_prefetch(&tmV);
+      uint32_t cc = 0;
+      for (int item = blockIdx.x; item < total && !abort_flag; item += gridDim.x) {
+        const Item it = item_at(item, nblk, H);
+        for (int j = 0; j < nch; ++j, ++cc) {
+          const int s = cc % kStages;
+          if (!umma::mbar_wait(&kv_empty[s], ((cc / kStages) & 1) ^ 1, 0x52)) {
+            abort_flag = 1;
+            break;
+          }
+          uint8_t* dst = smem + OFF_KV + s * 2 * TILE64;
+          umma::mbar_arrive_expect_tx(&kv_full[s], 2 * TILE64);
+          umma::tma_load_4d(dst, &tmK, &kv_full[s], 0, it.h, j * BN, it.b);
+          umma::tma_load_4d(dst + TILE64, &tmV, &kv_full[s], 0, it.h, j * BN, it.b);
+        }
       }
     }
-    __syncthreads();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      uint32_t cc = 0, t = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < total && ok && !abort_flag; item += gridDim.x, ++t) {
+        if (!umma::mbar_wait(qd_full, t & 1, 0x53)) {
+          ok = false;
+          break;
+        }
+        umma::tc_fence_after();
+        for (int j = 0; j < nch && ok; ++j, ++cc) {
+          const int s = cc % kStages;
+          if (!umma::mbar_wait(&kv_full[s], (cc / kStages) & 1, 0x54)) {
+            ok = false;
+            break;
+          }
+          umma::tc_fence_after();
+          const uint32_t k_base = umma::smem_u32(smem + OFF_KV + s * 2 * TILE64);
+          mma_k64(tmem, umma::smem_u32(smem), k_base, false, Idesc<T>::K, false);                    // S
+          mma_k64(tmem + kTmemDP, umma::smem_u32(smem + OFF_DO), k_base + TILE64, false, Idesc<T>::K, false);  // dP
+          umma::mma_commit(sd_full);
+          if (j == nch - 1) umma::mma_commit(qd_empty);
+          if (!umma::mbar_wait(ds_full, cc & 1, 0x55) ||
+              (j == 0 && !umma::mbar_wait(dq_empty, (t & 1) ^ 1, 0x56))) {
+            ok = false;
+            break;
+          }
+          umma::tc_fence_after();
+          mma_k64(tmem + kTmemDQ, umma::smem_u32(smem + OFF_DS), k_base, true, Idesc<T>::MN, j > 0);  // dQ += dS K
+          umma::mma_commit(&kv_empty[s]);
+          if (j == nch - 1) umma::mma_commit(dq_full);
+        }
+      }
+      if (!ok) abort_flag = 1;
+    }
+  } else {
+    const int quarter = warp & 3, row = quarter * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const float sl2 = scale * kLog2e;
+    uint32_t cc = 0, t = 0;
+    for (int item = blockIdx.x; item < total && !abort_flag; item += gridDim.x, ++t) {
+      const Item it = item_at(item, nblk, H);
+      const int r = it.blk * BM + row;
+      const bool valid = r < N;
+      uint4 orow[8];
+      float lse2 = 0.f;
+      if (valid) {
+        const T* src = o + it.b * po.s_b + it.h * po.s_h + (int64_t)r * po.s_n;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) orow[i] = *reinterpret_cast<const uint4*>(src + 8 * i);
+        lse2 = lse[(int64_t)it.bh * ldl + r] * kLog2e;
+      }
+      if (!umma::mbar_wait(qd_full, t & 1, 0x57)) {
+        abort_flag = 1;
+        break;
+      }
+      float dsum = 0.f;
+      if (valid) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const uint4 d4 = *reinterpret_cast<const uint4*>(smem + OFF_DO + sw128(row, i));
+          const T* oe = reinterpret_cast<const T*>(&orow[i]);
+          const T* de = reinterpret_cast<const T*>(&d4);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) dsum = fmaf(Elem<T>::to_f(oe[e]), Elem<T>::to_f(de[e]), dsum);
+        }
+        delta[(int64_t)it.bh * ldl + r] = dsum;
+      }
+      warp_arrive(qd_empty, false);
+      bool ok = true;
+      for (int j = 0; j < nch; ++j, ++cc) {
+        if (!umma::mbar_wait(sd_full, cc & 1, 0x58)) {
+          ok = false;
+          break;
+        }
+        umma::tc_fence_after();
+        const int kc = j * BN;
+        const bool tail = kc + BN > N;
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          float s[32], dp[32];
+          umma::tmem_ld32(tmem + lane_off + hf * 32, s);
+          umma::tmem_ld32(tmem + lane_off + kTmemDP + hf * 32, dp);
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            float p = exp2f(fmaf(s[c], sl2, -lse2));
+            if (tail && kc + hf * 32 + c >= N) p = 0.f;  // keys past the end
+            s[c] = p * (dp[c] - dsum);
+          }
+          put_row32<T>(smem + OFF_DS, row, hf * 4, s);
+        }
+        warp_arrive(ds_full, true);
+      }
+      if (!ok || !umma::mbar_wait(dq_full, t & 1, 0x59)) {
+        abort_flag = 1;
+        break;
+      }
+      umma::tc_fence_after();
+      float a0[32], a1[32];
+      umma::tmem_ld32(tmem + lane_off + kTmemDQ, a0);
+      umma::tmem_ld32(tmem + lane_off + kTmemDQ + 32, a1);
+      warp_arrive(dq_empty, false);
+      if (valid) store_row64<T>(dq + it.b * pdq.s_b + it.h * pdq.s_h + (int64_t)r * pdq.s_n, a0, a1, scale);
+    }
   }
-  if (!active) return;
-  store_rows<T>(dqacc, scale, Qs + warp * 16 * kLd, dq + b * pdq.s_b + h * pdq.s_h, pdq.s_n, r0, N);
+  umma::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    umma::tc_fence_after();
+    umma::tmem_dealloc(tmem, kTmemCols);
+  }
 }
 
 // -------------------------------------------------------- backward: dK, dV
+// Item = 128 keys.  Lane 0 of warp 0 loads the K and V tiles, lane 1 streams
+// chunks of 64 queries: Q_c, dO_c and their lse / D slices.  Per chunk the
+// MMA lane issues S^T = K Q_c^T and dP^T = V dO_c^T, waits for the row
+// threads' P^T and dS^T (one key per thread), then dV += P^T dO_c and
+// dK += dS^T Q_c (dO_c and Q_c as MN-major operands); the accumulators stay
+// in tensor memory for the whole item.
+namespace bk {
+constexpr int kStages = 2;
+constexpr int STAGE = 2 * TILE64 + 1024;  // Q, dO, then lse[64] and D[64]
+constexpr int OFF_V = TILE128;
+constexpr int OFF_CH = 2 * TILE128;
+constexpr int OFF_PT = OFF_CH + kStages * STAGE;
+constexpr int OFF_DST = OFF_PT + BM * BN * 2;
+constexpr int OFF_BAR = OFF_DST + BM * BN * 2;
+constexpr int kBars = 2 + 2 * kStages + 4;
+constexpr int SMEM = OFF_BAR + kBars * 8 + 16 + 1024;
+constexpr uint32_t kTmemDPT = 64, kTmemDV = 128, kTmemDK = 192;
+}  // namespace bk
+
 template <typename T>
-__global__ void __launch_bounds__(kThreads, 3)
-    attn_bwd_dkdv(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
-                  const T* __restrict__ dout, const float* __restrict__ lse, const float* __restrict__ delta,
-                  T* __restrict__ dk, T* __restrict__ dv, Plane pq, Plane pk, Plane pv, Plane pdo, Plane pdk,
-                  Plane pdv, int N, int H, int nkb, float scale) {
-  extern __shared__ __align__(16) uint8_t smem_raw[];
-  T* Ks = reinterpret_cast<T*>(smem_raw);
-  T* Vs = Ks + kTile;
-  T* Qs = Vs + kTile;      // 2 buffers
-  T* Os = Qs + 2 * kTile;  // dO, 2 buffers
-  float* Ls = reinterpret_cast<float*>(Os + 2 * kTile);  // [2][64] lse, then [2][64] D
-  const int kb = blockIdx.x % nkb, bh = blockIdx.x / nkb, b = bh / H, h = bh - b * H;
-  const T* qg = q + b * pq.s_b + h * pq.s_h;
-  const T* dog = dout + b * pdo.s_b + h * pdo.s_h;
-  const float* lg = lse + (int64_t)bh * N;
-  const float* dg = delta + (int64_t)bh * N;
-  const int k0 = kb * kBlock, nch = (N + kBlock - 1) / kBlock;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, tig = lane & 3;
-  const int r0 = k0 + warp * 16;
-  const bool active = r0 < N;
-  const float sl2 = scale * kLog2e;
-
-  auto load_rowstats = [&](int buf, int row0) {
-    const int i = threadIdx.x & 63, which = threadIdx.x >> 6;  // 128 threads: 64 lse + 64 D
-    const bool ok = row0 + i < N;
-    const float* src = which ? dg : lg;
-    cp_async4(Ls + (which * 2 + buf) * kBlock + i, src + (ok ? row0 + i : 0), ok);
-  };
-  load_tile(Ks, k + b * pk.s_b + h * pk.s_h, pk.s_n, k0, N);
-  load_tile(Vs, v + b * pv.s_b + h * pv.s_h, pv.s_n, k0, N);
-  load_tile(Qs, qg, pq.s_n, 0, N);
-  load_tile(Os, dog, pdo.s_n, 0, N);
-  load_rowstats(0, 0);
-  cp_commit();
-
-  uint32_t ka[4][4];
-  float dkacc[8][4], dvacc[8][4];
-  zero(dkacc);
-  zero(dvacc);
-  for (int j = 0; j < nch; ++j) {
-    const int buf = j & 1;
-    if (j + 1 < nch) {
-      load_tile(Qs + (buf ^ 1) * kTile, qg, pq.s_n, (j + 1) * kBlock, N);
-      load_tile(Os + (buf ^ 1) * kTile, dog, pdo.s_n, (j + 1) * kBlock, N);
-      load_rowstats(buf ^ 1, (j + 1) * kBlock);
+__global__ void __launch_bounds__(kThreads, 2)
+    attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                     const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmDO,
+                     const __grid_constant__ CUtensorMap tmL, const __grid_constant__ CUtensorMap tmD,
+                     T* __restrict__ dk, T* __restrict__ dv, Plane pdk, Plane pdv, int N, int H, int nblk, int total,
+                     float scale) {
+  using namespace bk;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t* kv_full = bars;
+  uint64_t* kv_empty = bars + 1;
+  uint64_t* ch_full = bars + 2;
+  uint64_t* ch_empty = ch_full + kStages;
+  uint64_t* sd_full = ch_empty + kStages;
+  uint64_t* ps_full = sd_full + 1;
+  uint64_t* acc_full = ps_full + 1;
+  uint64_t* acc_empty = acc_full + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kBars);
+  __shared__ int abort_flag;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nch = (N + BN - 1) / BN;
+  if (threadIdx.x == 0) {
+    umma::mbar_init(kv_full, 1);
+    umma::mbar_init(kv_empty, 1);
+    for (int s = 0; s < kStages; ++s) {
+      umma::mbar_init(&ch_full[s], 1);
+      umma::mbar_init(&ch_empty[s], 1);
     }
-    cp_commit();
-    cp_wait<1>();
-    __syncthreads();
-    if (active) {
-      if (j == 0) load_a(ka, Ks + warp * 16 * kLd);
-      const T* Qc = Qs + buf * kTile;
-      const T* Oc = Os + buf * kTile;
-      const float* lc = Ls + buf * kBlock;
-      const float* dc = Ls + (2 + buf) * kBlock;
-      const int qc = j * kBlock;
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {  // 32-query halves of the chunk
-        float st[4][4], dpt[4][4];
-        zero(st);
-        zero(dpt);
-        mma_rows_t<T, 2>(st, ka, Qc + hh * 32 * kLd);  // S^T: keys x queries
-        {
-          uint32_t va[4][4];  // reloaded from the warp's own V rows: keeps registers for the accumulators
-          load_a(va, Vs + warp * 16 * kLd);
-          mma_rows_t<T, 2>(dpt, va, Oc + hh * 32 * kLd);  // dP^T = V dO^T
+    umma::mbar_init(sd_full, 1);
+    umma::mbar_init(ps_full, 4);
+    umma::mbar_init(acc_full, 1);
+    umma::mbar_init(acc_empty, 4);
+    abort_flag = 0;
+    umma::fence_barrier_init();
+  }
+  if (warp == 0) umma::tmem_alloc(tmem_slot, kTmemCols);
+  umma::tc_fence_before();
+  __syncthreads();
+  umma::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {  // K and V tiles
+      umma::tma_prefetch(&tmK);
+      umma::tma_prefetch(&tmV);
+      uint32_t t = 0;
+      for (int item = blockIdx.x; item < total && !abort_flag; item += gridDim.x, ++t) {
+        const Item it = item_at(item, nblk, H);
+        if (!umma::mbar_wait(kv_empty, (t & 1) ^ 1, 0x61)) {
+          abort_flag = 1;
+          break;
         }
-        const bool tail = qc + hh * 32 + 32 > N;
-#pragma unroll
-        for (int nt = 0; nt < 4; ++nt) {
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int col = hh * 32 + nt * 8 + tig * 2 + e;  // query within the chunk
-            const float ls = lc[col] * kLog2e, dd = dc[col];
-            const bool dead = tail && qc + col >= N;
-#pragma unroll
-            for (int rr = 0; rr < 2; ++rr) {
-              const int idx = rr * 2 + e;
-              const float p = dead ? 0.f : exp2f(st[nt][idx] * sl2 - ls);
-              st[nt][idx] = p;
-              dpt[nt][idx] = p * (dpt[nt][idx] - dd);  // dS^T
-            }
+        umma::mbar_arrive_expect_tx(kv_full, 2 * TILE128);
+        umma::tma_load_4d(smem, &tmK, kv_full, 0, it.h, it.blk * BM, it.b);
+        umma::tma_load_4d(smem + OFF_V, &tmV, kv_full, 0, it.h, it.blk * BM, it.b);
+      }
+    } else if (lane == 1) {  // query chunks
+      umma::tma_prefetch(&tmQ);
+      umma::tma_prefetch(&tmDO);
+      umma::tma_prefetch(&tmL);
+      umma::tma_prefetch(&tmD);
+      uint32_t cc = 0;
+      for (int item = blockIdx.x; item < total && !abort_flag; item += gridDim.x) {
+        const Item it = item_at(item, nblk, H);
+        for (int j = 0; j < nch; ++j, ++cc) {
+          const int s = cc % kStages;
+          if (!umma::mbar_wait(&ch_empty[s], ((cc / kStages) & 1) ^ 1, 0x62)) {
+            abort_flag = 1;
+            break;
           }
+          uint8_t* dst = smem + OFF_CH + s * STAGE;
+          umma::mbar_arrive_expect_tx(&ch_full[s], 2 * TILE64 + 2 * BN * 4);
+          umma::tma_load_4d(dst, &tmQ, &ch_full[s], 0, it.h, j * BN, it.b);
+          umma::tma_load_4d(dst + TILE64, &tmDO, &ch_full[s], 0, it.h, j * BN, it.b);
+          umma::tma_load_2d(dst + 2 * TILE64, &tmL, &ch_full[s], j * BN, it.bh);
+          umma::tma_load_2d(dst + 2 * TILE64 + BN * 4, &tmD, &ch_full[s], j * BN, it.bh);
         }
-        uint32_t pa[2][4], sa[2][4];
-        c_to_a<T, 4>(pa, st);
-        c_to_a<T, 4>(sa, dpt);
-        mma_rows<T, 2>(dvacc, pa, Oc + hh * 32 * kLd);  // dV += P^T dO
-        mma_rows<T, 2>(dkacc, sa, Qc + hh * 32 * kLd);  // dK += dS^T Q
       }
     }
-    __syncthreads();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      uint32_t cc = 0, t = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < total && ok && !abort_flag; item += gridDim.x, ++t) {
+        if (!umma::mbar_wait(kv_full, t & 1, 0x63)) {
+          ok = false;
+          break;
+        }
+        umma::tc_fence_after();
+        for (int j = 0; j < nch && ok; ++j, ++cc) {
+          const int s = cc % kStages;
+          if (!umma::mbar_wait(&ch_full[s], (cc / kStages) & 1, 0x64)) {
+            ok = false;
+            break;
+          }
+          umma::tc_fence_after();
+          const uint32_t q_base = umma::smem_u32(smem + OFF_CH + s * STAGE), do_base = q_base + TILE64;
+          mma_k64(tmem, umma::smem_u32(smem), q_base, false, Idesc<T>::K, false);                  // S^T = K Q^T
+          mma_k64(tmem + kTmemDPT, umma::smem_u32(smem + OFF_V), do_base, false, Idesc<T>::K, false);  // dP^T = V dO^T
+          umma::mma_commit(sd_full);
+          if (j == nch - 1) umma::mma_commit(kv_empty);
+          if (!umma::mbar_wait(ps_full, cc & 1, 0x65) ||
+              (j == 0 && !umma::mbar_wait(acc_empty, (t & 1) ^ 1, 0x66))) {
+            ok = false;
+            break;
+          }
+          umma::tc_fence_after();
+          mma_k64(tmem + kTmemDV, umma::smem_u32(smem + OFF_PT), do_base, true, Idesc<T>::MN, j > 0);   // dV
+          mma_k64(tmem + kTmemDK, umma::smem_u32(smem + OFF_DST), q_base, true, Idesc<T>::MN, j > 0);   // dK
+          umma::mma_commit(&ch_empty[s]);
+          if (j == nch - 1) umma::mma_commit(acc_full);
+        }
+      }
+      if (!ok) abort_flag = 1;
+    }
+  } else {
+    const int quarter = warp & 3, row = quarter * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const float sl2 = scale * kLog2e;
+    uint32_t cc = 0, t = 0;
+    for (int item = blockIdx.x; item < total && !abort_flag; item += gridDim.x, ++t) {
+      const Item it = item_at(item, nblk, H);
+      bool ok = true;
+      for (int j = 0; j < nch; ++j, ++cc) {
+        const int s = cc % kStages;
+        // the lse / D slices are read from the stage: wait for its TMA as well as for the products
+        if (!umma::mbar_wait(&ch_full[s], (cc / kStages) & 1, 0x67) || !umma::mbar_wait(sd_full, cc & 1, 0x68)) {
+          ok = false;
+          break;
+        }
+        umma::tc_fence_after();
+        const float* ls = reinterpret_cast<const float*>(smem + OFF_CH + s * STAGE + 2 * TILE64);
+        const float* ds = ls + BN;
+        const int qc = j * BN;
+        const bool tail = qc + BN > N;
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          float st[32], dpt[32];
+          umma::tmem_ld32(tmem + lane_off + hf * 32, st);
+          umma::tmem_ld32(tmem + lane_off + kTmemDPT + hf * 32, dpt);
+#pragma unroll
+          for (int c4 = 0; c4 < 8; ++c4) {
+            const float4 l4 = *reinterpret_cast<const float4*>(ls + hf * 32 + 4 * c4);
+            const float4 d4 = *reinterpret_cast<const float4*>(ds + hf * 32 + 4 * c4);
+            const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dd[4] = {d4.x, d4.y, d4.z, d4.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int c = 4 * c4 + e;
+              // queries past the end: their lse / D slots hold padding, so select zeros outright
+              const bool dead = tail && qc + hf * 32 + c >= N;
+              const float p = dead ? 0.f : exp2f(fmaf(st[c], sl2, -lv[e] * kLog2e));
+              st[c] = p;
+              dpt[c] = dead ? 0.f : p * (dpt[c] - dd[e]);
+            }
+          }
+          put_row32<T>(smem + OFF_PT, row, hf * 4, st);
+          put_row32<T>(smem + OFF_DST, row, hf * 4, dpt);
+        }
+        warp_arrive(ps_full, true);
+      }
+      if (!ok || !umma::mbar_wait(acc_full, t & 1, 0x69)) {
+        abort_flag = 1;
+        break;
+      }
+      umma::tc_fence_after();
+      float v0[32], v1[32], k0[32], k1[32];
+      umma::tmem_ld32(tmem + lane_off + kTmemDV, v0);
+      umma::tmem_ld32(tmem + lane_off + kTmemDV + 32, v1);
+      umma::tmem_ld32(tmem + lane_off + kTmemDK, k0);
+      umma::tmem_ld32(tmem + lane_off + kTmemDK + 32, k1);
+      warp_arrive(acc_empty, false);
+      const int r = it.blk * BM + row;
+      if (r < N) {
+        store_row64<T>(dv + it.b * pdv.s_b + it.h * pdv.s_h + (int64_t)r * pdv.s_n, v0, v1, 1.f);
+        store_row64<T>(dk + it.b * pdk.s_b + it.h * pdk.s_h + (int64_t)r * pdk.s_n, k0, k1, scale);
+      }
+    }
   }
-  if (!active) return;
-  store_rows<T>(dkacc, scale, Ks + warp * 16 * kLd, dk + b * pdk.s_b + h * pdk.s_h, pdk.s_n, r0, N);
-  store_rows<T>(dvacc, 1.f, Vs + warp * 16 * kLd, dv + b * pdv.s_b + h * pdv.s_h, pdv.s_n, r0, N);
+  umma::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    umma::tc_fence_after();
+    umma::tmem_dealloc(tmem, kTmemCols);
+  }
 }
 
-constexpr size_t kDqSmem = (size_t)6 * kTile * 2;
-constexpr size_t kDkdvSmem = (size_t)6 * kTile * 2 + 4 * kBlock * 4;
-
+// ------------------------------------------------------------------ host
 bool plane_ok(const void* p, const Plane& pl) {
   return p != nullptr && (reinterpret_cast<uintptr_t>(p) & 15) == 0 && pl.s_b % 8 == 0 && pl.s_n % 8 == 0 &&
          pl.s_h % 8 == 0;
@@ -679,28 +802,55 @@ bool plane_ok(const void* p, const Plane& pl) {
 
 Plane plane_at(const int64_t* strides, int i) { return Plane{strides[3 * i], strides[3 * i + 1], strides[3 * i + 2]}; }
 
+int64_t row_pitch(int64_t seq_len) { return (seq_len + 3) / 4 * 4; }
+
 int check_shape(const char* name, int dtype, int64_t sequences, int64_t seq_len, int64_t heads, int64_t dim_head) {
   PMB_REQUIRE(dtype == PMB_BFLOAT16 || dtype == PMB_FLOAT16, "%s: bf16 or fp16 only (dtype %d)", name, dtype);
   PMB_REQUIRE(dim_head == kD, "%s: dim_head must be %d (got %lld)", name, kD, (long long)dim_head);
   PMB_REQUIRE(sequences >= 0 && heads > 0 && seq_len > 0 && seq_len <= (1 << 24), "%s: bad shape", name);
-  PMB_REQUIRE(sequences * heads * ((seq_len + kBlock - 1) / kBlock) < ((int64_t)1 << 31), "%s: grid too large",
-              name);
+  PMB_REQUIRE(sequences * heads * ((seq_len + BM - 1) / BM) < ((int64_t)1 << 31) && sequences * heads < (1 << 30),
+              "%s: too many sequences", name);
   return PMB_OK;
 }
 
+// Strides of a plane as the TMA map takes them: the stride of a dimension of
+// extent 1 is never used, so it is replaced by the extent of the one inside.
+Plane tma_strides(const Plane& pl, int64_t sequences, int N, int H) {
+  Plane t = pl;
+  if (H == 1) t.s_h = kD;
+  if (N == 1) t.s_n = (int64_t)H * t.s_h;
+  if (sequences == 1) t.s_b = (int64_t)N * t.s_n;
+  return t;
+}
+
+// The TMA map (64, H, N, sequences) needs strides that do not overlap:
+// head >= 64 elements, position >= H heads, sequence >= N positions.
+bool plane_order_ok(const Plane& pl, int64_t sequences, int N, int H) {
+  const Plane t = tma_strides(pl, sequences, N, H);
+  return t.s_h >= kD && t.s_n >= (int64_t)H * t.s_h && t.s_b >= (int64_t)N * t.s_n;
+}
+
 // TMA map over one [sequences, N, H, 64] plane: dims (64, H, N, sequences), box (64, 1, rows, 1)
-int plane_map(CUtensorMap& map, const void* base, const Plane& pl, int dtype, int64_t sequences, int N, int H,
+int plane_map(CUtensorMap& map, const void* base, const Plane& pl_in, int dtype, int64_t sequences, int N, int H,
               int rows, const char* name) {
+  const Plane pl = tma_strides(pl_in, sequences, N, H);
   const uint64_t dims[4] = {(uint64_t)kD, (uint64_t)H, (uint64_t)N, (uint64_t)sequences};
   const uint64_t strides[3] = {(uint64_t)pl.s_h * 2, (uint64_t)pl.s_n * 2, (uint64_t)pl.s_b * 2};
   const uint32_t box[4] = {(uint32_t)kD, 1, (uint32_t)rows, 1};
   return tma::make_map_4d(map, base, dtype, dims, strides, box, name);
 }
 
+int grid_for(int64_t total) {
+  int64_t g = (int64_t)num_sms() * 2;
+  return (int)(g < total ? g : total);
+}
+
 }  // namespace
 }  // namespace pmb
 
 using namespace pmb;
+
+extern "C" int64_t pmb_attention_row_pitch(int64_t seq_len) { return seq_len > 0 ? row_pitch(seq_len) : 0; }
 
 extern "C" int pmb_attention_forward(const void* q, const void* k, const void* v, void* o, float* lse,
                                      int64_t sequences, int64_t seq_len, int64_t heads, int64_t dim_head,
@@ -714,21 +864,22 @@ extern "C" int pmb_attention_forward(const void* q, const void* k, const void* v
               po = plane_at(strides, 3);
   PMB_REQUIRE(plane_ok(q, pq) && plane_ok(k, pk) && plane_ok(v, pv) && plane_ok(o, po),
               "%s: planes must be non-NULL, 16-byte aligned, with strides that are multiples of 8", name);
-  const int N = (int)seq_len, H = (int)heads, nqb = (N + tcf::BM - 1) / tcf::BM;
-  const int64_t total = sequences * heads * nqb;
-  PMB_REQUIRE(total < ((int64_t)1 << 31), "%s: too many sequences", name);
+  const int N = (int)seq_len, H = (int)heads, nblk = (N + BM - 1) / BM;
+  const int64_t total = sequences * heads * nblk;
+  PMB_REQUIRE(plane_order_ok(pq, sequences, N, H) && plane_order_ok(pk, sequences, N, H) &&
+                  plane_order_ok(pv, sequences, N, H),
+              "%s: q, k, v strides must not overlap (head >= 64, position >= heads * head, sequence >= seq_len * "
+              "position)", name);
   CUtensorMap mq, mk, mv;
-  if (int st = plane_map(mq, q, pq, dtype, sequences, N, H, tcf::BM, name)) return st;
-  if (int st = plane_map(mk, k, pk, dtype, sequences, N, H, tcf::BN, name)) return st;
-  if (int st = plane_map(mv, v, pv, dtype, sequences, N, H, tcf::BN, name)) return st;
-  int64_t grid = (int64_t)num_sms() * 2;
-  if (grid > total) grid = total;
+  if (int st = plane_map(mq, q, pq, dtype, sequences, N, H, BM, name)) return st;
+  if (int st = plane_map(mk, k, pk, dtype, sequences, N, H, BN, name)) return st;
+  if (int st = plane_map(mv, v, pv, dtype, sequences, N, H, BN, name)) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   auto run = [&](auto tag) {
     using T = decltype(tag);
-    PMB_CHECK_CUDA(cudaFuncSetAttribute(attn_fwd_tc<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, tcf::SMEM), name);
-    attn_fwd_tc<T><<<(unsigned)grid, tcf::kThreads, tcf::SMEM, s>>>(mq, mk, mv, static_cast<T*>(o), lse, po, N, H,
-                                                                     nqb, (int)total, scale);
+    PMB_CHECK_CUDA(cudaFuncSetAttribute(attn_fwd_tc<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, fw::SMEM), name);
+    attn_fwd_tc<T><<<grid_for(total), kThreads, fw::SMEM, s>>>(mq, mk, mv, static_cast<T*>(o), lse, po, N, H,
+                                                               (int)row_pitch(N), nblk, (int)total, scale);
     PMB_CHECK_LAUNCH(name);
     return PMB_OK;
   };
@@ -737,7 +888,7 @@ extern "C" int pmb_attention_forward(const void* q, const void* k, const void* v
 
 extern "C" int64_t pmb_attention_backward_workspace_size(int64_t sequences, int64_t seq_len, int64_t heads) {
   if (sequences <= 0 || seq_len <= 0 || heads <= 0) return 0;
-  return (sequences * heads * seq_len * 4 + 255) / 256 * 256;
+  return (sequences * heads * row_pitch(seq_len) * 4 + 255) / 256 * 256;
 }
 
 extern "C" int pmb_attention_backward(const void* q, const void* k, const void* v, const void* o,
@@ -756,31 +907,47 @@ extern "C" int pmb_attention_backward(const void* q, const void* k, const void* 
               (long long)need);
     return PMB_ERR_WORKSPACE;
   }
+  PMB_REQUIRE((reinterpret_cast<uintptr_t>(lse) & 15) == 0 && (reinterpret_cast<uintptr_t>(workspace) & 15) == 0,
+              "%s: lse and workspace must be 16-byte aligned", name);
   const Plane pq = plane_at(strides, 0), pk = plane_at(strides, 1), pv = plane_at(strides, 2),
               po = plane_at(strides, 3), pdo = plane_at(strides, 4), pdq = plane_at(strides, 5),
               pdk = plane_at(strides, 6), pdv = plane_at(strides, 7);
   PMB_REQUIRE(plane_ok(q, pq) && plane_ok(k, pk) && plane_ok(v, pv) && plane_ok(o, po) && plane_ok(grad_out, pdo) &&
                   plane_ok(grad_q, pdq) && plane_ok(grad_k, pdk) && plane_ok(grad_v, pdv),
               "%s: planes must be non-NULL, 16-byte aligned, with strides that are multiples of 8", name);
-  const int N = (int)seq_len, nb = (N + kBlock - 1) / kBlock;
-  const unsigned grid = (unsigned)(sequences * heads * nb);
+  const int N = (int)seq_len, H = (int)heads, nblk = (N + BM - 1) / BM;
+  const int64_t total = sequences * heads * nblk, ldl = row_pitch(N), rows = sequences * heads;
+  PMB_REQUIRE(plane_order_ok(pq, sequences, N, H) && plane_order_ok(pk, sequences, N, H) &&
+                  plane_order_ok(pv, sequences, N, H) && plane_order_ok(pdo, sequences, N, H),
+              "%s: q, k, v, grad_out strides must not overlap (head >= 64, position >= heads * head, sequence >= "
+              "seq_len * position)", name);
   float* delta = static_cast<float*>(workspace);
+  CUtensorMap mq128, mdo128, mk64, mv64, mk128, mv128, mq64, mdo64, ml, md;
+  if (int st = plane_map(mq128, q, pq, dtype, sequences, N, H, BM, name)) return st;
+  if (int st = plane_map(mdo128, grad_out, pdo, dtype, sequences, N, H, BM, name)) return st;
+  if (int st = plane_map(mk64, k, pk, dtype, sequences, N, H, BN, name)) return st;
+  if (int st = plane_map(mv64, v, pv, dtype, sequences, N, H, BN, name)) return st;
+  if (int st = plane_map(mk128, k, pk, dtype, sequences, N, H, BM, name)) return st;
+  if (int st = plane_map(mv128, v, pv, dtype, sequences, N, H, BM, name)) return st;
+  if (int st = plane_map(mq64, q, pq, dtype, sequences, N, H, BN, name)) return st;
+  if (int st = plane_map(mdo64, grad_out, pdo, dtype, sequences, N, H, BN, name)) return st;
+  if (int st = tma::make_map_rows_f32(ml, lse, ldl, rows, ldl * 4, BN, name)) return st;
+  if (int st = tma::make_map_rows_f32(md, delta, ldl, rows, ldl * 4, BN, name)) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int grid = grid_for(total);
   auto run = [&](auto tag) {
     using T = decltype(tag);
-    PMB_CHECK_CUDA(cudaFuncSetAttribute(attn_bwd_dq<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDqSmem),
+    PMB_CHECK_CUDA(cudaFuncSetAttribute(attn_bwd_dq_tc<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, bq::SMEM),
                    name);
     PMB_CHECK_CUDA(
-        cudaFuncSetAttribute(attn_bwd_dkdv<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDkdvSmem), name);
-    attn_bwd_dq<T><<<grid, kThreads, kDqSmem, s>>>(
-        static_cast<const T*>(q), static_cast<const T*>(k), static_cast<const T*>(v), static_cast<const T*>(o),
-        static_cast<const T*>(grad_out), lse, delta, static_cast<T*>(grad_q), pq, pk, pv, po, pdo, pdq, N,
-        (int)heads, nb, scale);
+        cudaFuncSetAttribute(attn_bwd_dkdv_tc<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, bk::SMEM), name);
+    attn_bwd_dq_tc<T><<<grid, kThreads, bq::SMEM, s>>>(mq128, mdo128, mk64, mv64, static_cast<const T*>(o), lse,
+                                                        delta, static_cast<T*>(grad_q), po, pdq, N, H, (int)ldl, nblk,
+                                                        (int)total, scale);
     PMB_CHECK_LAUNCH(name);
-    attn_bwd_dkdv<T><<<grid, kThreads, kDkdvSmem, s>>>(
-        static_cast<const T*>(q), static_cast<const T*>(k), static_cast<const T*>(v), static_cast<const T*>(grad_out),
-        lse, delta, static_cast<T*>(grad_k), static_cast<T*>(grad_v), pq, pk, pv, pdo, pdk, pdv, N, (int)heads, nb,
-        scale);
+    attn_bwd_dkdv_tc<T><<<grid, kThreads, bk::SMEM, s>>>(mk128, mv128, mq64, mdo64, ml, md, static_cast<T*>(grad_k),
+                                                          static_cast<T*>(grad_v), pdk, pdv, N, H, nblk, (int)total,
+                                                          scale);
     PMB_CHECK_LAUNCH(name);
     return PMB_OK;
   };

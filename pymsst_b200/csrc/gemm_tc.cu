@@ -13,7 +13,17 @@ unsigned int timeout_flag_gemm(int reset) { return umma::flag_reader(reset); }
 
 namespace tma {
 
+// The encoder is a driver call and needs a current context on the calling
+// thread.  A thread that has not used the runtime yet (an autograd worker
+// that reaches a backward op first, a thread of another language's FFI) has
+// none, so bind the current device's primary context first.
+static void bind_context() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaSetDevice(dev) != cudaSuccess) cudaGetLastError();
+}
+
 EncodeTiledFn encode_fn() {
+  bind_context();
   static EncodeTiledFn fn = nullptr;
   if (fn == nullptr) {
     void* p = nullptr;
@@ -77,6 +87,31 @@ int make_map_4d(CUtensorMap& map, const void* base, int dtype, const uint64_t (&
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     set_error("%s: cuTensorMapEncodeTiled failed (%d) for a 4-D map", name, (int)r);
+    return PMB_ERR_CUDA;
+  }
+  return PMB_OK;
+}
+
+int make_map_rows_f32(CUtensorMap& map, const void* base, uint64_t cols, uint64_t rows, uint64_t pitch_bytes,
+                      uint32_t box_cols, const char* name) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) {
+    set_error("%s: cuTensorMapEncodeTiled is unavailable (driver too old or no GPU)", name);
+    return PMB_ERR_CUDA;
+  }
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (pitch_bytes & 15) != 0) {
+    set_error("%s: fp32 row map needs a 16-byte aligned base and pitch", name);
+    return PMB_ERR_ALIGNMENT;
+  }
+  const cuuint64_t d[2] = {cols, rows};
+  const cuuint64_t st[1] = {pitch_bytes};
+  const cuuint32_t bx[2] = {box_cols, 1};
+  const cuuint32_t elem[2] = {1, 1};
+  const CUresult r = fn(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), d, st, bx, elem,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("%s: cuTensorMapEncodeTiled failed (%d) for an fp32 row map", name, (int)r);
     return PMB_ERR_CUDA;
   }
   return PMB_OK;

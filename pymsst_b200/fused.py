@@ -292,6 +292,9 @@ class QKVRotaryFn(torch.autograd.Function):
         w = weight.to(xn.dtype).contiguous()
         x2 = xn.reshape(b * n, d).contiguous()
         rotate = int(cos is not None)
+        if rotate and (tuple(cos.shape) != (n, dh // 2) or tuple(sin.shape) != (n, dh // 2)):
+            raise ValueError(f"QKVRotary: angle tables must be [{n}, {dh // 2}] (rotation of the whole head), "
+                             f"got {tuple(cos.shape)} and {tuple(sin.shape)}")
         if xn.dtype in (torch.bfloat16, torch.float16) and d % 8 == 0 and dh % 32 == 0:
             if rotate and cos_t is None:
                 cos_t, sin_t = cos.t().contiguous(), sin.t().contiguous()
@@ -401,7 +404,8 @@ class AttentionGateFn(torch.autograd.Function):
         if attn.stride(-1) != 1:
             attn = attn.contiguous()
         b, h, n, dh = attn.shape
-        xn = xn.contiguous()
+        ctx.x_dtype = xn.dtype
+        xn = xn.to(attn.dtype).contiguous()  # the kernel reads attn and xn in one activation type
         rows, dim = xn.shape
         out = torch.empty(rows, h * dh, dtype=attn.dtype, device=device)
         gate = torch.empty(rows, h, dtype=attn.dtype, device=device)
@@ -434,12 +438,21 @@ class AttentionGateFn(torch.autograd.Function):
             grad_attn.data_ptr(), grad_x.data_ptr(), gw.data_ptr(), gb.data_ptr(), nat.dtype_code(attn.dtype),
             nat.dtype_code(weight.dtype), ws.data_ptr(), ws_bytes, ctx.inner, nat.stream_handle(device),
         )
-        return grad_attn, grad_x, gw, gb, None
+        return grad_attn, grad_x.to(ctx.x_dtype), gw, gb, None
 
 
 def _attn_plane(t: torch.Tensor) -> torch.Tensor:
-    """[b, h, n, dh] view whose strides the attention kernels accept (head dim contiguous, 16-byte rows)."""
-    if t.stride(-1) != 1 or any(s % 8 for s in t.stride()[:3]) or t.data_ptr() % 16:
+    """[b, h, n, dh] view whose strides the attention kernels accept: head dim contiguous, 16-byte rows, and the
+    non-overlapping order of a [b, n, h, dh] plane (head >= dh, position >= h heads, sequence >= n positions;
+    size-1 dimensions are free); anything else is copied into such a plane."""
+    b, h, n, dh = t.shape
+    sb, sh, sn, sd = t.stride()
+    sh = dh if h == 1 else sh
+    sn = h * sh if n == 1 else sn
+    sb = n * sn if b == 1 else sb
+    ok = (sd == 1 and t.data_ptr() % 16 == 0 and not any(s % 8 for s in t.stride()[:3])
+          and sh >= dh and sn >= h * sh and sb >= n * sn)
+    if not ok:
         t = t.transpose(1, 2).contiguous().transpose(1, 2)
     return t
 
@@ -473,7 +486,7 @@ class AttentionFn(torch.autograd.Function):
         q, k, v = _attn_plane(q), _attn_plane(k), _attn_plane(v)
         b, h, n, dh = q.shape
         o = _bnhd_empty(b, h, n, dh, q.dtype, device)
-        lse = torch.empty(b * h, n, dtype=torch.float32, device=device)
+        lse = torch.empty(b * h, (n + 3) // 4 * 4, dtype=torch.float32, device=device)  # rows padded to 16 bytes
         nat.call(
             "pmb_attention_forward", q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(), b, n, h,
             dh, nat.i64_array(_attn_strides(q, k, v, o)), dh ** -0.5, nat.dtype_code(q.dtype),

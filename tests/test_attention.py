@@ -51,7 +51,7 @@ def test_attention_matches_float64(cuda_device, n, dtype):
     qd, kd, vd = (t.detach().double().requires_grad_() for t in (q, k, v))
     od, lsed = _ref(qd, kd, vd)
     assert _rel(o, od) < 2e-2
-    lse = o.grad_fn.saved_tensors[4].view(b, h, n)
+    lse = o.grad_fn.saved_tensors[4][:, :n].reshape(b, h, n)
     torch.testing.assert_close(lse.double(), lsed.detach(), rtol=1e-4, atol=1e-4)
 
     go = torch.randn(b, h, n, 64, generator=torch.Generator().manual_seed(7)).to(dtype).to(cuda_device)
@@ -128,8 +128,8 @@ def test_model_attention_backends_agree(cuda_device):
     from pymsst_b200.roformer import Attention, RotaryEmbedding
 
     torch.manual_seed(0)
-    attn = Attention(192, heads=8, dim_head=64, rotary_embed=RotaryEmbedding(dim=32)).to(cuda_device)
-    x = torch.randn(6, 62, 192, device=cuda_device)
+    attn = Attention(192, heads=8, dim_head=64, rotary_embed=RotaryEmbedding(64)).to(cuda_device)
+    x = torch.randn(6, 62, 192, device=cuda_device).to(torch.bfloat16)  # transformer inputs are 16-bit under AMP
     outs = {}
     for backend in ("pmb", "efficient"):
         attn.set_cuda_attention_backend(backend)
@@ -167,10 +167,22 @@ def test_attention_rejects_unaligned_strides():
     assert st != 0 and "multiples of 8" in lib.pmb_last_error().decode()
 
 
+def test_attention_rejects_overlapping_plane_order():
+    """[b, h, n, 64]-ordered strides (position stride below heads * head stride) are refused by the C ABI;
+    AttentionFn copies such tensors into a [b, n, h, 64] plane first."""
+    lib = _lib()
+    n, h = 8, 2
+    strides = nat.i64_array([h * n * 64, 64, n * 64] * 4)  # (sequence, position, head) of a bhnd tensor
+    st = lib.pmb_attention_forward(4096, 4096, 4096, 4096, 4096, 2, n, h, 64, strides, ctypes.c_float(0.125),
+                                   nat.BF16, None)
+    assert st != 0 and "must not overlap" in lib.pmb_last_error().decode()
+
+
 def test_attention_backward_workspace_size():
     lib = _lib()
     assert lib.pmb_attention_backward_workspace_size(0, 8, 8) == 0
-    assert lib.pmb_attention_backward_workspace_size(3, 65, 2) >= 3 * 65 * 2 * 4
+    assert lib.pmb_attention_row_pitch(65) == 68 and lib.pmb_attention_row_pitch(64) == 64
+    assert lib.pmb_attention_backward_workspace_size(3, 65, 2) >= 3 * 2 * 68 * 4
 
 
 def test_set_cuda_attention_backend_hook():
@@ -186,3 +198,13 @@ def test_set_cuda_attention_backend_hook():
             m.set_cuda_attention_backend(name)
     with pytest.raises(ValueError):
         setters[0].set_cuda_attention_backend("bogus")
+
+
+@pytest.mark.gpu
+def test_partial_rotary_tables_are_rejected(cuda_device):
+    """The fused projection rotates whole heads; a shorter angle table is refused, not read past its end."""
+    from pymsst_b200.roformer import Attention, RotaryEmbedding
+
+    attn = Attention(192, heads=8, dim_head=64, rotary_embed=RotaryEmbedding(32)).to(cuda_device)
+    with pytest.raises(ValueError, match="angle tables"):
+        attn(torch.randn(2, 62, 192, device=cuda_device).to(torch.bfloat16))
