@@ -379,26 +379,78 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
 }
 
+// ---------------------------------------------------------------- backward
+// Both backward kernels run 8 row warps: warp w (2..9) reads TMEM lane
+// quarter w % 4 and owns columns [32 h, 32 h + 32) of its row, h = (w-2)/4,
+// so two threads share each row and every thread's chain is half as long.
+constexpr int kRowWarpsBwd = 8;
+constexpr int kBwdThreads = 64 + 32 * kRowWarpsBwd;
+
+// 32 columns of this warp's TMEM lane quarter, without waiting: the values
+// are valid after tmem_wait(), which also orders their uses after the wait.
+__device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+// Register dependency on all 32 values (an empty statement the compiler
+// cannot move the values' uses ahead of).
+__device__ __forceinline__ void tie32(uint32_t (&r)[32]) {
+  asm volatile(""
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                 "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                 "+r"(r[29]), "+r"(r[30]), "+r"(r[31]));
+}
+
+// Wait for this thread's outstanding tcgen05.ld and tie both arrays after it.
+__device__ __forceinline__ void tmem_wait2(uint32_t (&a)[32], uint32_t (&b)[32]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+  tie32(a);
+  tie32(b);
+}
+
+// 32 fp32 values (times mul) -> 64 bytes of a global row
+template <typename T>
+__device__ __forceinline__ void store_row32(T* dst, const uint32_t (&a)[32], float mul) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float* f = reinterpret_cast<const float*>(a) + 8 * i;
+    *reinterpret_cast<uint4*>(dst + 8 * i) =
+        make_uint4(pack2<T>(f[0] * mul, f[1] * mul), pack2<T>(f[2] * mul, f[3] * mul),
+                   pack2<T>(f[4] * mul, f[5] * mul), pack2<T>(f[6] * mul, f[7] * mul));
+  }
+}
+
 // ------------------------------------------------------------ backward: dQ
 // Item = 128 queries.  Lane 0 of warp 0 loads the Q and dO tiles, lane 1
 // streams K/V chunks.  Per chunk the MMA lane issues S = Q K_c^T and
 // dP = dO V_c^T, waits for the row threads' dS_c, and issues dQ += dS_c K_c
 // (K_c as the MN-major operand).  The row threads compute D = rowsum(dO * O)
-// for their query once per item (written out for the dK/dV kernel), then
-// per chunk P = exp2(S * scale * log2e - lse * log2e) and dS = P (dP - D).
+// for their query once per item (each half-row thread one half, combined
+// through shared memory; written out for the dK/dV kernel), then per chunk
+// P = exp2(S * scale * log2e - lse * log2e) and dS = P (dP - D).
 namespace bq {
 constexpr int kStages = 3;
 constexpr int OFF_DO = TILE128;
 constexpr int OFF_KV = 2 * TILE128;
 constexpr int OFF_DS = OFF_KV + kStages * 2 * TILE64;
 constexpr int OFF_BAR = OFF_DS + BM * BN * 2;
-constexpr int kBars = 2 + 2 * kStages + 4;
-constexpr int SMEM = OFF_BAR + kBars * 8 + 16 + 1024;
+constexpr int kBars = 2 + 2 * kStages + 5;
+constexpr int OFF_X = OFF_BAR + 256;  // [2][128] fp32 partial row sums of D
+constexpr int SMEM = OFF_X + 2 * BM * 4 + 1024;
 constexpr uint32_t kTmemDP = 64, kTmemDQ = 128;
 }  // namespace bq
 
 template <typename T>
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(kBwdThreads, 2)
     attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmDO,
                    const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                    const T* __restrict__ o, const float* __restrict__ lse, float* __restrict__ delta,
@@ -415,21 +467,24 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint64_t* ds_full = sd_full + 1;
   uint64_t* dq_full = ds_full + 1;
   uint64_t* dq_empty = dq_full + 1;
+  uint64_t* x_full = dq_empty + 1;  // both halves of every row's D partial are in xs
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kBars);
+  float* xs = reinterpret_cast<float*>(smem + OFF_X);
   __shared__ int abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nch = (N + BN - 1) / BN;
   if (threadIdx.x == 0) {
     umma::mbar_init(qd_full, 1);
-    umma::mbar_init(qd_empty, 1 + 4);  // MMA commit + the row warps' D reads
+    umma::mbar_init(qd_empty, 1 + kRowWarpsBwd);  // MMA commit + the row warps' D reads
     for (int s = 0; s < kStages; ++s) {
       umma::mbar_init(&kv_full[s], 1);
       umma::mbar_init(&kv_empty[s], 1);
     }
     umma::mbar_init(sd_full, 1);
-    umma::mbar_init(ds_full, 4);
+    umma::mbar_init(ds_full, kRowWarpsBwd);
     umma::mbar_init(dq_full, 1);
-    umma::mbar_init(dq_empty, 4);
+    umma::mbar_init(dq_empty, kRowWarpsBwd);
+    umma::mbar_init(x_full, kRowWarpsBwd);
     abort_flag = 0;
     umma::fence_barrier_init();
   }
@@ -509,7 +564,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (!ok) abort_flag = 1;
     }
   } else {
-    const int quarter = warp & 3, row = quarter * 32 + lane;
+    const int quarter = warp & 3, half = (warp - 2) >> 2, row = quarter * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const float sl2 = scale * kLog2e;
     uint32_t cc = 0, t = 0;
@@ -517,30 +572,32 @@ __global__ void __launch_bounds__(kThreads, 2)
       const Item it = item_at(item, nblk, H);
       const int r = it.blk * BM + row;
       const bool valid = r < N;
-      uint4 orow[8];
-      float lse2 = 0.f;
-      if (valid) {
-        const T* src = o + it.b * po.s_b + it.h * po.s_h + (int64_t)r * po.s_n;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) orow[i] = *reinterpret_cast<const uint4*>(src + 8 * i);
-        lse2 = lse[(int64_t)it.bh * ldl + r] * kLog2e;
-      }
       if (!umma::mbar_wait(qd_full, t & 1, 0x57)) {
         abort_flag = 1;
         break;
       }
-      float dsum = 0.f;
+      float part = 0.f, lse2 = 0.f;
       if (valid) {
+        const T* src = o + it.b * po.s_b + it.h * po.s_h + (int64_t)r * po.s_n + half * 32;
+        lse2 = lse[(int64_t)it.bh * ldl + r] * kLog2e;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const uint4 d4 = *reinterpret_cast<const uint4*>(smem + OFF_DO + sw128(row, i));
-          const T* oe = reinterpret_cast<const T*>(&orow[i]);
+        for (int i = 0; i < 4; ++i) {
+          const uint4 o4 = *reinterpret_cast<const uint4*>(src + 8 * i);
+          const uint4 d4 = *reinterpret_cast<const uint4*>(smem + OFF_DO + sw128(row, half * 4 + i));
+          const T* oe = reinterpret_cast<const T*>(&o4);
           const T* de = reinterpret_cast<const T*>(&d4);
 #pragma unroll
-          for (int e = 0; e < 8; ++e) dsum = fmaf(Elem<T>::to_f(oe[e]), Elem<T>::to_f(de[e]), dsum);
+          for (int e = 0; e < 8; ++e) part = fmaf(Elem<T>::to_f(oe[e]), Elem<T>::to_f(de[e]), part);
         }
-        delta[(int64_t)it.bh * ldl + r] = dsum;
       }
+      xs[half * BM + row] = part;
+      warp_arrive(x_full, false);
+      if (!umma::mbar_wait(x_full, t & 1, 0x5a)) {
+        abort_flag = 1;
+        break;
+      }
+      const float dsum = xs[row] + xs[BM + row];
+      if (valid && half == 0) delta[(int64_t)it.bh * ldl + r] = dsum;
       warp_arrive(qd_empty, false);
       bool ok = true;
       for (int j = 0; j < nch; ++j, ++cc) {
@@ -549,21 +606,20 @@ __global__ void __launch_bounds__(kThreads, 2)
           break;
         }
         umma::tc_fence_after();
-        const int kc = j * BN;
-        const bool tail = kc + BN > N;
+        uint32_t su[32], du[32];
+        tmem_ld32_nowait(tmem + lane_off + half * 32, su);
+        tmem_ld32_nowait(tmem + lane_off + kTmemDP + half * 32, du);
+        tmem_wait2(su, du);
+        const int k0 = j * BN + half * 32;
+        const bool tail = k0 + 32 > N;
+        float(&ds)[32] = *reinterpret_cast<float(*)[32]>(&su);  // dS overwrites S in place
 #pragma unroll
-        for (int hf = 0; hf < 2; ++hf) {
-          float s[32], dp[32];
-          umma::tmem_ld32(tmem + lane_off + hf * 32, s);
-          umma::tmem_ld32(tmem + lane_off + kTmemDP + hf * 32, dp);
-#pragma unroll
-          for (int c = 0; c < 32; ++c) {
-            float p = exp2f(fmaf(s[c], sl2, -lse2));
-            if (tail && kc + hf * 32 + c >= N) p = 0.f;  // keys past the end
-            s[c] = p * (dp[c] - dsum);
-          }
-          put_row32<T>(smem + OFF_DS, row, hf * 4, s);
+        for (int c = 0; c < 32; ++c) {
+          float p = exp2f(fmaf(__uint_as_float(su[c]), sl2, -lse2));
+          if (tail && k0 + c >= N) p = 0.f;  // keys past the end
+          ds[c] = p * (__uint_as_float(du[c]) - dsum);
         }
+        put_row32<T>(smem + OFF_DS, row, half * 4, ds);
         warp_arrive(ds_full, true);
       }
       if (!ok || !umma::mbar_wait(dq_full, t & 1, 0x59)) {
@@ -571,11 +627,12 @@ __global__ void __launch_bounds__(kThreads, 2)
         break;
       }
       umma::tc_fence_after();
-      float a0[32], a1[32];
-      umma::tmem_ld32(tmem + lane_off + kTmemDQ, a0);
-      umma::tmem_ld32(tmem + lane_off + kTmemDQ + 32, a1);
+      uint32_t a0[32];
+      tmem_ld32_nowait(tmem + lane_off + kTmemDQ + half * 32, a0);
+      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+      tie32(a0);
       warp_arrive(dq_empty, false);
-      if (valid) store_row64<T>(dq + it.b * pdq.s_b + it.h * pdq.s_h + (int64_t)r * pdq.s_n, a0, a1, scale);
+      if (valid) store_row32<T>(dq + it.b * pdq.s_b + it.h * pdq.s_h + (int64_t)r * pdq.s_n + half * 32, a0, scale);
     }
   }
   umma::tc_fence_before();
@@ -590,7 +647,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 // Item = 128 keys.  Lane 0 of warp 0 loads the K and V tiles, lane 1 streams
 // chunks of 64 queries: Q_c, dO_c and their lse / D slices.  Per chunk the
 // MMA lane issues S^T = K Q_c^T and dP^T = V dO_c^T, waits for the row
-// threads' P^T and dS^T (one key per thread), then dV += P^T dO_c and
+// threads' P^T and dS^T (one key per thread pair), then dV += P^T dO_c and
 // dK += dS^T Q_c (dO_c and Q_c as MN-major operands); the accumulators stay
 // in tensor memory for the whole item.
 namespace bk {
@@ -607,7 +664,7 @@ constexpr uint32_t kTmemDPT = 64, kTmemDV = 128, kTmemDK = 192;
 }  // namespace bk
 
 template <typename T>
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(kBwdThreads, 2)
     attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                      const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmDO,
                      const __grid_constant__ CUtensorMap tmL, const __grid_constant__ CUtensorMap tmD,
@@ -637,9 +694,9 @@ __global__ void __launch_bounds__(kThreads, 2)
       umma::mbar_init(&ch_empty[s], 1);
     }
     umma::mbar_init(sd_full, 1);
-    umma::mbar_init(ps_full, 4);
+    umma::mbar_init(ps_full, kRowWarpsBwd);
     umma::mbar_init(acc_full, 1);
-    umma::mbar_init(acc_empty, 4);
+    umma::mbar_init(acc_empty, kRowWarpsBwd);
     abort_flag = 0;
     umma::fence_barrier_init();
   }
@@ -724,7 +781,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (!ok) abort_flag = 1;
     }
   } else {
-    const int quarter = warp & 3, row = quarter * 32 + lane;
+    const int quarter = warp & 3, half = (warp - 2) >> 2, row = quarter * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const float sl2 = scale * kLog2e;
     uint32_t cc = 0, t = 0;
@@ -739,33 +796,33 @@ __global__ void __launch_bounds__(kThreads, 2)
           break;
         }
         umma::tc_fence_after();
-        const float* ls = reinterpret_cast<const float*>(smem + OFF_CH + s * STAGE + 2 * TILE64);
+        uint32_t su[32], du[32];
+        tmem_ld32_nowait(tmem + lane_off + half * 32, su);
+        tmem_ld32_nowait(tmem + lane_off + kTmemDPT + half * 32, du);
+        const float* ls = reinterpret_cast<const float*>(smem + OFF_CH + s * STAGE + 2 * TILE64) + half * 32;
         const float* ds = ls + BN;
-        const int qc = j * BN;
-        const bool tail = qc + BN > N;
+        const int q0 = j * BN + half * 32;
+        const bool tail = q0 + 32 > N;
+        tmem_wait2(su, du);
+        float(&pt)[32] = *reinterpret_cast<float(*)[32]>(&su);   // P^T overwrites S^T in place
+        float(&dst)[32] = *reinterpret_cast<float(*)[32]>(&du);  // dS^T overwrites dP^T in place
 #pragma unroll
-        for (int hf = 0; hf < 2; ++hf) {
-          float st[32], dpt[32];
-          umma::tmem_ld32(tmem + lane_off + hf * 32, st);
-          umma::tmem_ld32(tmem + lane_off + kTmemDPT + hf * 32, dpt);
+        for (int c4 = 0; c4 < 8; ++c4) {
+          const float4 l4 = *reinterpret_cast<const float4*>(ls + 4 * c4);
+          const float4 d4 = *reinterpret_cast<const float4*>(ds + 4 * c4);
+          const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dd[4] = {d4.x, d4.y, d4.z, d4.w};
 #pragma unroll
-          for (int c4 = 0; c4 < 8; ++c4) {
-            const float4 l4 = *reinterpret_cast<const float4*>(ls + hf * 32 + 4 * c4);
-            const float4 d4 = *reinterpret_cast<const float4*>(ds + hf * 32 + 4 * c4);
-            const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dd[4] = {d4.x, d4.y, d4.z, d4.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int c = 4 * c4 + e;
-              // queries past the end: their lse / D slots hold padding, so select zeros outright
-              const bool dead = tail && qc + hf * 32 + c >= N;
-              const float p = dead ? 0.f : exp2f(fmaf(st[c], sl2, -lv[e] * kLog2e));
-              st[c] = p;
-              dpt[c] = dead ? 0.f : p * (dpt[c] - dd[e]);
-            }
+          for (int e = 0; e < 4; ++e) {
+            const int c = 4 * c4 + e;
+            // queries past the end: their lse / D slots hold padding, so select zeros outright
+            const bool dead = tail && q0 + c >= N;
+            const float p = dead ? 0.f : exp2f(fmaf(__uint_as_float(su[c]), sl2, -lv[e] * kLog2e));
+            pt[c] = p;
+            dst[c] = dead ? 0.f : p * (__uint_as_float(du[c]) - dd[e]);
           }
-          put_row32<T>(smem + OFF_PT, row, hf * 4, st);
-          put_row32<T>(smem + OFF_DST, row, hf * 4, dpt);
         }
+        put_row32<T>(smem + OFF_PT, row, half * 4, pt);
+        put_row32<T>(smem + OFF_DST, row, half * 4, dst);
         warp_arrive(ps_full, true);
       }
       if (!ok || !umma::mbar_wait(acc_full, t & 1, 0x69)) {
@@ -773,16 +830,15 @@ __global__ void __launch_bounds__(kThreads, 2)
         break;
       }
       umma::tc_fence_after();
-      float v0[32], v1[32], k0[32], k1[32];
-      umma::tmem_ld32(tmem + lane_off + kTmemDV, v0);
-      umma::tmem_ld32(tmem + lane_off + kTmemDV + 32, v1);
-      umma::tmem_ld32(tmem + lane_off + kTmemDK, k0);
-      umma::tmem_ld32(tmem + lane_off + kTmemDK + 32, k1);
+      uint32_t vv[32], kv[32];
+      tmem_ld32_nowait(tmem + lane_off + kTmemDV + half * 32, vv);
+      tmem_ld32_nowait(tmem + lane_off + kTmemDK + half * 32, kv);
+      tmem_wait2(vv, kv);
       warp_arrive(acc_empty, false);
       const int r = it.blk * BM + row;
       if (r < N) {
-        store_row64<T>(dv + it.b * pdv.s_b + it.h * pdv.s_h + (int64_t)r * pdv.s_n, v0, v1, 1.f);
-        store_row64<T>(dk + it.b * pdk.s_b + it.h * pdk.s_h + (int64_t)r * pdk.s_n, k0, k1, scale);
+        store_row32<T>(dv + it.b * pdv.s_b + it.h * pdv.s_h + (int64_t)r * pdv.s_n + half * 32, vv, 1.f);
+        store_row32<T>(dk + it.b * pdk.s_b + it.h * pdk.s_h + (int64_t)r * pdk.s_n + half * 32, kv, scale);
       }
     }
   }
@@ -941,11 +997,11 @@ extern "C" int pmb_attention_backward(const void* q, const void* k, const void* 
                    name);
     PMB_CHECK_CUDA(
         cudaFuncSetAttribute(attn_bwd_dkdv_tc<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, bk::SMEM), name);
-    attn_bwd_dq_tc<T><<<grid, kThreads, bq::SMEM, s>>>(mq128, mdo128, mk64, mv64, static_cast<const T*>(o), lse,
+    attn_bwd_dq_tc<T><<<grid, kBwdThreads, bq::SMEM, s>>>(mq128, mdo128, mk64, mv64, static_cast<const T*>(o), lse,
                                                         delta, static_cast<T*>(grad_q), po, pdq, N, H, (int)ldl, nblk,
                                                         (int)total, scale);
     PMB_CHECK_LAUNCH(name);
-    attn_bwd_dkdv_tc<T><<<grid, kThreads, bk::SMEM, s>>>(mk128, mv128, mq64, mdo64, ml, md, static_cast<T*>(grad_k),
+    attn_bwd_dkdv_tc<T><<<grid, kBwdThreads, bk::SMEM, s>>>(mk128, mv128, mq64, mdo64, ml, md, static_cast<T*>(grad_k),
                                                           static_cast<T*>(grad_v), pdk, pdv, N, H, nblk, (int)total,
                                                           scale);
     PMB_CHECK_LAUNCH(name);
