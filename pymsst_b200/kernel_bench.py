@@ -26,16 +26,17 @@ SEQ_BATCH, SEQ = 248, 258
 
 
 class _Bench:
-    def __init__(self, device: torch.device, iters: int):
+    def __init__(self, device: torch.device, iters: int, warmup: int = 3):
         self.device = device
         self.iters = iters
+        self.warmup = warmup
         self.flush = torch.empty(64 * 1024 * 1024, device=device)
         self.stream = torch.cuda.current_stream(device)
         self.results: dict[str, dict] = {}
         self.peaks = load_peaks()
 
     def time(self, name: str, fn, bytes_: float = 0.0, flops: float = 0.0) -> dict:
-        for _ in range(3):
+        for _ in range(self.warmup):
             fn()
         torch.cuda.synchronize(self.device)
         times = []
@@ -373,10 +374,12 @@ def main(argv=None) -> None:
     p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     p.add_argument("ops", nargs="*", help=f"ops to run (default all): {', '.join(OPS)}")
     p.add_argument("--iters", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=3, help="untimed calls per op before timing (0 with --iters 1 "
+                   "launches each kernel once, for profiler captures)")
     p.add_argument("--json", default=None)
     args = p.parse_args(argv)
     device = torch.device("cuda", torch.cuda.current_device())
-    bench = _Bench(device, args.iters)
+    bench = _Bench(device, max(args.iters, 1), args.warmup)
     for name in args.ops or list(OPS):
         if name not in OPS:
             raise SystemExit(f"unknown op {name!r}; choose from {', '.join(OPS)}")
