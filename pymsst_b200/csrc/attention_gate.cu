@@ -456,6 +456,305 @@ __global__ void __launch_bounds__(kThreads, 3)
   if (threadIdx.x < H) partial_b[(int64_t)blockIdx.x * H + threadIdx.x] = accb;
 }
 
+// ------------------------------------------------- streamed kernels
+// When a row's heads are contiguous in attn (head stride = Dh) each attention
+// row is one 16-byte aligned block of H*Dh elements.  The streamed kernels
+// keep kStreamStages - 1 tiles of kStreamRows rows in flight while they work
+// on the current one: every thread issues 16-byte cp.async copies of its share
+// of a later tile (attention rows through per-tile row bases, grad_out, x rows
+// padded by 16 bytes so neighbouring rows sit on different banks, gate) into a
+// shared-memory ring, and the per-thread async groups are waited with
+// cp.async.wait_group -- no spin waits.  The arithmetic is that of the tiled
+// kernels above; results leave with 16-byte stores.
+constexpr int kStreamRows = 8;
+constexpr int kStreamStages = 4;
+
+struct StreamLayout {
+  int hd_b, x_b, g_b, xld, wld;             // bytes per attention / x / gate row; x and W row pitch (elements)
+  int off_at, off_go, off_x, off_g, stage;  // offsets within a stage, stage stride
+  int off_w, off_gp, bytes;                 // after the ring: W fp32 [H][wld], gp fp32 [rows][H]
+  __host__ __device__ StreamLayout(int H, int Dh, int dim, int es, bool bwd) {
+    hd_b = H * Dh * es;
+    x_b = dim * es;
+    g_b = H * es;
+    xld = dim + 16 / es;
+    wld = dim + 4;
+    off_at = 0;
+    off_go = off_at + kStreamRows * hd_b;
+    off_x = off_go + (bwd ? kStreamRows * hd_b : 0);
+    off_g = off_x + kStreamRows * xld * es;
+    stage = (off_g + (bwd ? kStreamRows * g_b : 0) + 127) / 128 * 128;
+    off_w = kStreamStages * stage;
+    off_gp = off_w + H * wld * 4;
+    bytes = off_gp + kStreamRows * H * 4;
+  }
+};
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+               "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// This thread's share of one tile's copies (n rows from r0; rb = row bases).
+template <typename T>
+__device__ __forceinline__ void load_tile_async(uint8_t* base, const StreamLayout& L, const int64_t* rb,
+                                                const T* attn, const T* x, const T* grad_out, const T* gate,
+                                                int64_t r0, int n, int H, int dim) {
+  constexpr int V = Vec<T>::N;
+  const int va = L.hd_b / 16, vx = L.x_b / 16;
+  for (int v = threadIdx.x; v < n * va; v += kThreads) {
+    const int r = v / va, c = v - r * va;
+    cp_async16(base + L.off_at + r * L.hd_b + c * 16, attn + rb[r] + (int64_t)c * V);
+    if (grad_out) cp_async16(base + L.off_go + r * L.hd_b + c * 16, grad_out + (r0 + r) * (int64_t)(va * V) + c * V);
+  }
+  for (int v = threadIdx.x; v < n * vx; v += kThreads) {
+    const int r = v / vx, c = v - r * vx;
+    cp_async16(base + L.off_x + r * L.xld * (int)sizeof(T) + c * 16, x + (r0 + r) * dim + (int64_t)c * V);
+  }
+  if (gate)
+    for (int v = threadIdx.x; v < n * (L.g_b / 16); v += kThreads)
+      cp_async16(base + L.off_g + v * 16, gate + r0 * H + (int64_t)v * V);
+}
+
+template <typename TP>
+__device__ __forceinline__ void load_weights_stream(const TP* __restrict__ W, int H, int dim, float* w_s, int wld) {
+  for (int e = threadIdx.x; e < H * dim; e += kThreads) w_s[(e / dim) * wld + e % dim] = Elem<TP>::to_f(W[e]);
+}
+
+// Ring driver shared by both directions: before tile `it` is worked on, the
+// tile kStreamStages - 1 ahead is put in flight.  `rb_s` holds each stage's
+// row bases (written by the first kStreamRows threads).
+struct StreamRing {
+  int64_t rows, tiles;
+  __device__ int rows_of(int64_t t) const {
+    const int64_t left = rows - t * kStreamRows;
+    return (int)(left < kStreamRows ? left : kStreamRows);
+  }
+};
+
+// Fixed thread -> work maps of the streamed kernels (16-bit types, 8-element
+// chunks).  vr 16-byte vectors per attention row divide the 256 threads, so a
+// thread keeps one column vector and walks rows r0 + t / vr, + 256 / vr, ...
+// grad_x / grad_W work is in (row or head) x 8-column chunks, at most
+// kMaxChunkItems per thread.
+constexpr int kMaxChunkItems = 2;
+
+template <typename T, typename TP>
+__global__ void __launch_bounds__(kThreads, 3)
+    gate_fwd_stream(const T* __restrict__ attn, AttnLayout la, const T* __restrict__ x, const TP* __restrict__ W,
+                    const TP* __restrict__ bias, int64_t rows, int H, int Dh, int dim, T* __restrict__ out,
+                    T* __restrict__ gate) {
+  constexpr int V = Vec<T>::N;  // 8
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ int64_t rb_s[kStreamStages][kStreamRows];
+  const StreamLayout L(H, Dh, dim, sizeof(T), false);
+  float* w_s = reinterpret_cast<float*>(smem + L.off_w);
+  float* g_s = reinterpret_cast<float*>(smem + L.off_gp);
+  load_weights_stream<TP>(W, H, dim, w_s, L.wld);
+  const StreamRing ring{rows, (rows + kStreamRows - 1) / kStreamRows};
+  auto prefetch = [&](int64_t t, int st) {  // whole CTA; ends with a commit (empty when t is past the end)
+    if (t < ring.tiles) {
+      const int n = ring.rows_of(t);
+      if (threadIdx.x < kStreamRows) rb_s[st][threadIdx.x] = threadIdx.x < n ? la.row_base(t * kStreamRows + threadIdx.x) : 0;
+      __syncthreads();
+      load_tile_async<T>(smem + st * L.stage, L, rb_s[st], attn, x, (const T*)nullptr, (const T*)nullptr,
+                         t * kStreamRows, n, H, dim);
+    }
+    cp_commit();
+  };
+  for (int s = 0; s < kStreamStages - 1; ++s) prefetch(blockIdx.x + (int64_t)s * gridDim.x, s);
+  const int vh = Dh / V, vr = H * vh, nck = dim / V;
+  // logits: 4 threads per (row, head), each a quarter of the 8-element chunks
+  const int lp = threadIdx.x >> 2, lq = threadIdx.x & 3, lr = lp / H, lh = lp - lr * H;
+  const float lbias = lp < kStreamRows * H ? Elem<TP>::to_f(bias[lh]) : 0.f;
+  // gating: fixed column vector, rows c_r0, + c_rs, ...
+  const int cc = threadIdx.x % vr, c_r0 = threadIdx.x / vr, c_rs = kThreads / vr, ch = cc / vh;
+  int it = 0;
+  for (int64_t tile = blockIdx.x; tile < ring.tiles; tile += gridDim.x, ++it) {
+    const int st = it % kStreamStages;
+    prefetch(tile + (int64_t)(kStreamStages - 1) * gridDim.x, (it + kStreamStages - 1) % kStreamStages);
+    cp_wait<kStreamStages - 1>();
+    __syncthreads();  // this tile's copies from every thread have landed
+    const int64_t r0 = tile * kStreamRows;
+    const int n = ring.rows_of(tile);
+    const uint8_t* base = smem + st * L.stage;
+    const T* at_s = reinterpret_cast<const T*>(base + L.off_at);
+    const T* x_s = reinterpret_cast<const T*>(base + L.off_x);
+    if (lp < kStreamRows * H) {  // warp-uniform: kStreamRows * H * 4 is a multiple of 32
+      const T* xr = x_s + lr * L.xld;
+      const float* wr = w_s + lh * L.wld;
+      float acc = 0.f;
+      for (int k = lq; k < nck; k += 4) {
+        float xf[V];
+        Vec<T>::unpack(*reinterpret_cast<const uint4*>(xr + k * V), xf);
+        const float4 w0 = *reinterpret_cast<const float4*>(wr + k * V);
+        const float4 w1 = *reinterpret_cast<const float4*>(wr + k * V + 4);
+        acc += xf[0] * w0.x + xf[1] * w0.y + xf[2] * w0.z + xf[3] * w0.w + xf[4] * w1.x + xf[5] * w1.y +
+               xf[6] * w1.z + xf[7] * w1.w;
+      }
+      acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+      acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+      if (lq == 0 && lr < n) {
+        const float g = round_to<T>(sigmoidf_(acc + lbias));
+        g_s[lp] = g;
+        gate[r0 * H + lp] = Elem<T>::from_f(g);
+      }
+    }
+    __syncthreads();
+    for (int r = c_r0; r < n; r += c_rs) {
+      float a[V];
+      Vec<T>::unpack(*reinterpret_cast<const uint4*>(at_s + r * vr * V + cc * V), a);
+      const float g = g_s[r * H + ch];
+#pragma unroll
+      for (int q = 0; q < V; ++q) a[q] *= g;
+      *reinterpret_cast<uint4*>(out + (r0 + r) * (int64_t)vr * V + (int64_t)cc * V) = Vec<T>::pack(a);
+    }
+    __syncthreads();  // stage st and g_s are free
+  }
+  cp_wait<0>();
+}
+
+template <typename T, typename TP>
+__global__ void __launch_bounds__(kThreads, 2)
+    gate_bwd_stream(const T* __restrict__ grad_out, const T* __restrict__ attn, AttnLayout la,
+                    const T* __restrict__ x, const TP* __restrict__ W, const T* __restrict__ gate, int64_t rows,
+                    int H, int Dh, int dim, T* __restrict__ grad_attn, T* __restrict__ grad_x,
+                    float* __restrict__ partial_w, float* __restrict__ partial_b) {
+  constexpr int V = Vec<T>::N;  // 8
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ int64_t rb_s[kStreamStages][kStreamRows];
+  const StreamLayout L(H, Dh, dim, sizeof(T), true);
+  float* w_s = reinterpret_cast<float*>(smem + L.off_w);
+  float* gp_s = reinterpret_cast<float*>(smem + L.off_gp);
+  load_weights_stream<TP>(W, H, dim, w_s, L.wld);
+  const StreamRing ring{rows, (rows + kStreamRows - 1) / kStreamRows};
+  auto prefetch = [&](int64_t t, int st) {
+    if (t < ring.tiles) {
+      const int n = ring.rows_of(t);
+      if (threadIdx.x < kStreamRows) rb_s[st][threadIdx.x] = threadIdx.x < n ? la.row_base(t * kStreamRows + threadIdx.x) : 0;
+      __syncthreads();
+      load_tile_async<T>(smem + st * L.stage, L, rb_s[st], attn, x, grad_out, gate, t * kStreamRows, n, H, dim);
+    }
+    cp_commit();
+  };
+  for (int s = 0; s < kStreamStages - 1; ++s) prefetch(blockIdx.x + (int64_t)s * gridDim.x, s);
+  const int vh = Dh / V, vr = H * vh, nck = dim / V;
+  // grad_attn / gate gradient: fixed column vector cc (head ch), rows c_r0, + c_rs, ...
+  const int cc = threadIdx.x % vr, c_r0 = threadIdx.x / vr, c_rs = kThreads / vr, ch = cc / vh;
+  // grad_x items (row, chunk) and grad_W items (head, chunk): item = threadIdx.x + j * kThreads
+  int xr_[kMaxChunkItems], xk_[kMaxChunkItems], wh_[kMaxChunkItems], wk_[kMaxChunkItems];
+#pragma unroll
+  for (int j = 0; j < kMaxChunkItems; ++j) {
+    const int item = threadIdx.x + j * kThreads;
+    xr_[j] = item / nck;
+    xk_[j] = item - xr_[j] * nck;
+    wh_[j] = item < H * nck ? item / nck : H;  // H: no item
+    wk_[j] = item - (item / nck) * nck;
+  }
+  float accw[kMaxChunkItems][V];
+#pragma unroll
+  for (int j = 0; j < kMaxChunkItems; ++j)
+#pragma unroll
+    for (int q = 0; q < V; ++q) accw[j][q] = 0.f;
+  float accb = 0.f;
+  int it = 0;
+  for (int64_t tile = blockIdx.x; tile < ring.tiles; tile += gridDim.x, ++it) {
+    const int st = it % kStreamStages;
+    prefetch(tile + (int64_t)(kStreamStages - 1) * gridDim.x, (it + kStreamStages - 1) % kStreamStages);
+    cp_wait<kStreamStages - 1>();
+    __syncthreads();
+    const int64_t r0 = tile * kStreamRows;
+    const int n = ring.rows_of(tile);
+    const uint8_t* base = smem + st * L.stage;
+    const T* go_s = reinterpret_cast<const T*>(base + L.off_go);
+    const T* at_s = reinterpret_cast<const T*>(base + L.off_at);
+    const T* x_s = reinterpret_cast<const T*>(base + L.off_x);
+    const T* g_in = reinterpret_cast<const T*>(base + L.off_g);
+    const int64_t* rb = rb_s[st];
+    // grad_attn = grad_out * gate, and per (row, head) the gate-logit gradient
+    // sum(grad_out * attn) * g (1 - g), reduced over the head's vh lanes.  The
+    // trip count c_r0 < kStreamRows is warp-uniform (vr >= 32 or vr | 32).
+    for (int r = c_r0; r < kStreamRows; r += c_rs) {
+      float part = 0.f;
+      if (r < n) {
+        float go[V], a[V];
+        Vec<T>::unpack(*reinterpret_cast<const uint4*>(go_s + r * vr * V + cc * V), go);
+        Vec<T>::unpack(*reinterpret_cast<const uint4*>(at_s + r * vr * V + cc * V), a);
+        const float g = Elem<T>::to_f(g_in[r * H + ch]);
+#pragma unroll
+        for (int q = 0; q < V; ++q) {
+          part += go[q] * a[q];
+          a[q] = go[q] * g;
+        }
+        *reinterpret_cast<uint4*>(grad_attn + rb[r] + (int64_t)cc * V) = Vec<T>::pack(a);
+      }
+      for (int o = vh >> 1; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+      if ((cc & (vh - 1)) == 0 && r < n) {
+        const float g = Elem<T>::to_f(g_in[r * H + ch]);
+        gp_s[r * H + ch] = part * g * (1.0f - g);
+      }
+    }
+    __syncthreads();
+    // grad_x[r, 8k..8k+7] = sum_h gp[r, h] W[h, 8k..8k+7]
+#pragma unroll
+    for (int j = 0; j < kMaxChunkItems; ++j) {
+      const int r = xr_[j], k = xk_[j];
+      if (r < n) {
+        float acc[V];
+#pragma unroll
+        for (int q = 0; q < V; ++q) acc[q] = 0.f;
+        for (int h = 0; h < H; ++h) {
+          const float gp = gp_s[r * H + h];
+          const float4 w0 = *reinterpret_cast<const float4*>(w_s + h * L.wld + k * V);
+          const float4 w1 = *reinterpret_cast<const float4*>(w_s + h * L.wld + k * V + 4);
+          acc[0] += gp * w0.x;
+          acc[1] += gp * w0.y;
+          acc[2] += gp * w0.z;
+          acc[3] += gp * w0.w;
+          acc[4] += gp * w1.x;
+          acc[5] += gp * w1.y;
+          acc[6] += gp * w1.z;
+          acc[7] += gp * w1.w;
+        }
+        *reinterpret_cast<uint4*>(grad_x + (r0 + r) * dim + (int64_t)k * V) = Vec<T>::pack(acc);
+      }
+    }
+    // grad_W[h, 8k..8k+7] += sum_r gp[r, h] x[r, 8k..8k+7]; grad_b[h] += sum_r gp[r, h]
+#pragma unroll
+    for (int j = 0; j < kMaxChunkItems; ++j) {
+      const int h = wh_[j], k = wk_[j];
+      if (h < H) {
+        for (int r = 0; r < n; ++r) {
+          const float gp = gp_s[r * H + h];
+          float xf[V];
+          Vec<T>::unpack(*reinterpret_cast<const uint4*>(x_s + r * L.xld + k * V), xf);
+#pragma unroll
+          for (int q = 0; q < V; ++q) accw[j][q] += gp * xf[q];
+        }
+      }
+    }
+    if (threadIdx.x < H)
+      for (int r = 0; r < n; ++r) accb += gp_s[r * H + threadIdx.x];
+    __syncthreads();  // stage st and gp_s are free
+  }
+  cp_wait<0>();
+#pragma unroll
+  for (int j = 0; j < kMaxChunkItems; ++j) {
+    const int h = wh_[j], k = wk_[j];
+    if (h < H) {
+#pragma unroll
+      for (int q = 0; q < V; ++q) partial_w[(int64_t)blockIdx.x * H * dim + h * dim + k * V + q] = accw[j][q];
+    }
+  }
+  if (threadIdx.x < H) partial_b[(int64_t)blockIdx.x * H + threadIdx.x] = accb;
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 // Whether the tiled kernels apply (vector width V = 16 / element size).
@@ -468,6 +767,32 @@ bool tiled_ok(int es, const AttnLayout& la, int64_t H, int64_t Dh, int64_t dim, 
   for (const void* p : ptrs)
     if (!aligned16(p)) return false;
   return TileSmem((int)H, (int)dim, V).bytes <= 200 * 1024;
+}
+
+// Whether the streamed kernels apply: contiguous heads in attn (head
+// stride = Dh), 16-byte aligned rows of every streamed tensor, whole head
+// vectors, and a shared-memory layout that fits two CTAs per SM.
+bool stream_ok(int es, const AttnLayout& la, int64_t H, int64_t Dh, int64_t dim, bool bwd,
+               std::initializer_list<const void*> ptrs) {
+  if (es != 2) return false;  // 16-bit activations: 8-element chunks
+  const int V = 8;
+  if (la.s_h != Dh || dim % V != 0 || Dh % V != 0 || (H * es) % 16 != 0) return false;
+  const int64_t vh = Dh / V, vr = H * vh, nck = dim / V;
+  // fixed maps: vr a power of two that divides the block, head vectors in one warp, logits in one pass,
+  // grad_x / grad_W items within kMaxChunkItems per thread
+  if (vh > 32 || (vh & (vh - 1)) != 0 || (vr & (vr - 1)) != 0 || vr > kThreads) return false;
+  if ((int64_t)kStreamRows * H * 4 > kThreads) return false;
+  if (kStreamRows * nck > kThreads * kMaxChunkItems || H * nck > kThreads * kMaxChunkItems) return false;
+  if (la.s_b % V != 0 || la.s_n % V != 0) return false;
+  for (const void* p : ptrs)
+    if (!aligned16(p)) return false;
+  return StreamLayout((int)H, (int)Dh, (int)dim, es, bwd).bytes <= 110 * 1024;
+}
+
+int stream_grid(int64_t rows, int per_sm) {
+  const int64_t tiles = (rows + kStreamRows - 1) / kStreamRows;
+  const int64_t g = (int64_t)num_sms() * per_sm;
+  return (int)(g < tiles ? g : (tiles < 1 ? 1 : tiles));
 }
 
 int tiled_grid(int64_t rows, int per_sm, int cap) {
@@ -510,6 +835,17 @@ extern "C" int pmb_attention_gate_forward(const void* attn, int64_t seq_len, int
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const size_t smem = (size_t)heads * dim * sizeof(float);
   return PMB_DISPATCH_PARAM(dtype, param_dtype, T, TP, name, [&] {
+    if (stream_ok(sizeof(T), la, heads, dim_head, dim, false, {attn, x, out, gate})) {
+      const int bsm = StreamLayout((int)heads, (int)dim_head, (int)dim, sizeof(T), false).bytes;
+      PMB_CHECK_CUDA(cudaFuncSetAttribute(gate_fwd_stream<T, TP>, cudaFuncAttributeMaxDynamicSharedMemorySize, bsm),
+                     name);
+      gate_fwd_stream<T, TP><<<stream_grid(rows, 3), kThreads, bsm, s>>>(
+          static_cast<const T*>(attn), la, static_cast<const T*>(x), static_cast<const TP*>(weight),
+          static_cast<const TP*>(bias), rows, (int)heads, (int)dim_head, (int)dim, static_cast<T*>(out),
+          static_cast<T*>(gate));
+      PMB_CHECK_LAUNCH(name);
+      return PMB_OK;
+    }
     if (tiled_ok(sizeof(T), la, heads, dim_head, dim, {attn, x, out})) {
       const size_t tsm = TileSmem((int)heads, (int)dim, Vec<T>::N).bytes;
       if (tsm > 48 * 1024)
@@ -576,6 +912,27 @@ extern "C" int pmb_attention_gate_backward(const void* grad_out, const void* att
   AttnLayout la{seq_len, attn_stride_batch, attn_stride_seq, attn_stride_head, seq_inner};
   const size_t smem = (size_t)heads * dim * sizeof(float);
   return PMB_DISPATCH_PARAM(dtype, param_dtype, T, TP, name, [&] {
+    if (stream_ok(sizeof(T), la, heads, dim_head, dim, true, {grad_out, attn, x, gate, grad_attn, grad_x})) {
+      const int bsm = StreamLayout((int)heads, (int)dim_head, (int)dim, sizeof(T), true).bytes;
+      PMB_CHECK_CUDA(cudaFuncSetAttribute(gate_bwd_stream<T, TP>, cudaFuncAttributeMaxDynamicSharedMemorySize, bsm),
+                     name);
+      const int grid = stream_grid(rows, 2);  // <= 2 x SMs <= kMaxTiledBwdBlocks partial rows
+      float* pw = static_cast<float*>(workspace);
+      float* pb = reinterpret_cast<float*>(static_cast<char*>(workspace) +
+                                           align256((int64_t)kMaxTiledBwdBlocks * heads * dim * 4));
+      gate_bwd_stream<T, TP><<<grid, kThreads, bsm, s>>>(
+          static_cast<const T*>(grad_out), static_cast<const T*>(attn), la, static_cast<const T*>(x),
+          static_cast<const TP*>(weight), static_cast<const T*>(gate), rows, (int)heads, (int)dim_head, (int)dim,
+          static_cast<T*>(grad_attn), static_cast<T*>(grad_x), pw, pb);
+      PMB_CHECK_LAUNCH(name);
+      red::colsum_rows<<<red::colsum_rows_grid(heads * dim), red::kThreads, 0, s>>>(pw, grid, heads * dim, grad_weight,
+                                                                               Elem<TP>::code);
+      PMB_CHECK_LAUNCH(name);
+      red::colsum_rows<<<red::colsum_rows_grid(heads), red::kThreads, 0, s>>>(pb, grid, heads, grad_bias,
+                                                                         Elem<TP>::code);
+      PMB_CHECK_LAUNCH(name);
+      return PMB_OK;
+    }
     if (heads * dim <= kThreads * kMaxWPerThread &&
         tiled_ok(sizeof(T), la, heads, dim_head, dim, {grad_out, attn, x, grad_attn, grad_x})) {
       const size_t tsm = TileSmem((int)heads, (int)dim, Vec<T>::N).bytes;

@@ -330,7 +330,8 @@ __global__ void __launch_bounds__(kThreads, 4)
   int it = 0;
   for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++it) {
     const int st = it % kStages;
-    if (!umma::mbar_wait(&full[st], (it / kStages) & 1, 0x21)) break;
+    // every thread takes the same decision, so no thread is left at a barrier
+    if (__syncthreads_or(!umma::mbar_wait(&full[st], (it / kStages) & 1, 0x21))) break;
     Tx* xs = reinterpret_cast<Tx*>(smem + st * kFwdStageBytes);
     const int64_t r0 = tile * rpt;
     const int n = rows - r0 < rpt ? (int)(rows - r0) : rpt;
@@ -441,7 +442,8 @@ __global__ void __launch_bounds__(kThreads, 3)
     // this warp's row norms for the tile, one load per lane, before the wait
     const int qi = wib * RW + (lane / RW) * kWarps * RW + (lane % RW);
     const float inv_l = qi < n ? inv_norm[r0 + qi] : 0.f;
-    if (!umma::mbar_wait(&full[st], (it / kStages) & 1, 0x22)) break;
+    // every thread takes the same decision, so no thread is left at a barrier
+    if (__syncthreads_or(!umma::mbar_wait(&full[st], (it / kStages) & 1, 0x22))) break;
     Tg* ds_ = reinterpret_cast<Tg*>(smem + st * kBwdStageBytes * 2);
     const Tg* ss_ = reinterpret_cast<const Tg*>(smem + st * kBwdStageBytes * 2 + kBwdStageBytes);
     int step = 0;

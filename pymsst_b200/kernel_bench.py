@@ -73,7 +73,8 @@ def _gemm(a, lda, a_mn, b, ldb, b_mn, c, m, n, k, bias=None, act=0):
 def op_gate(bench: _Bench):
     dev, bf, f32 = bench.device, torch.bfloat16, torch.float32
     x = torch.randn(ROWS, DIM, device=dev, dtype=bf)
-    attn = torch.randn(SEQ_BATCH, HEADS, SEQ, DHEAD, device=dev, dtype=bf)
+    # [b, h, n, dh] view of a [b, n, h, dh] plane, the layout the attention kernels write
+    attn = torch.randn(SEQ_BATCH, SEQ, HEADS, DHEAD, device=dev, dtype=bf).transpose(1, 2)
     w = torch.randn(HEADS, DIM, device=dev, dtype=f32) * 0.1
     b = torch.randn(HEADS, device=dev, dtype=f32)
     out = torch.empty(ROWS, HEADS * DHEAD, device=dev, dtype=bf)

@@ -138,25 +138,30 @@ def test_mask_estimator_final(cuda_device, widths, rows, hidden, dtype):
         _close(a, e, dtype, f"grad[{k}]")
 
 
+@pytest.mark.parametrize("layout", ["bhnd", "bnhd"])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize("bsz,heads,seq,dh,dim", [(6, 8, 62, 64, 192), (3, 4, 41, 32, 100), (2, 16, 33, 16, 64),
                                                   (5, 8, 258, 64, 384)])
-def test_attention_gate_strided_attention_layout(cuda_device, dtype, bsz, heads, seq, dh, dim):
-    """The gate reads the [batch, heads, seq, Dh] attention output in place.
+def test_attention_gate_strided_attention_layout(cuda_device, dtype, bsz, heads, seq, dh, dim, layout):
+    """The gate reads the [batch, heads, seq, Dh] attention output in place, stored either as such ("bhnd") or as
+    the [batch, seq, heads, Dh] planes the attention kernels write ("bnhd", heads contiguous).
 
-    Shapes cover the 32-row tiled kernels (16-byte vectors; partial last
-    tile) and the row-wise fallback (dim 100 is not a multiple of the bf16
-    vector width)."""
+    Shapes cover the streamed kernels (bnhd with 16-byte gate rows: cp.async ring of 8-row tiles, partial last
+    tile), the 32-row tiled kernels (bhnd, and bnhd with 4 heads) and the row-wise fallback (dim 100 is not a
+    multiple of the bf16 vector width)."""
     from pymsst_b200 import _native as nat
 
     rows = bsz * seq
-    attn_bhnd = torch.randn(bsz, heads, seq, dh).to(dtype)
+    if layout == "bhnd":
+        attn_bhnd = torch.randn(bsz, heads, seq, dh).to(dtype)
+    else:
+        attn_bhnd = torch.randn(bsz, seq, heads, dh).to(dtype).transpose(1, 2)
     x = torch.randn(rows, dim).to(dtype)
     w = (torch.randn(heads, dim) * 0.1).to(dtype)
     b = torch.randn(heads).to(dtype)
     attn_rows = attn_bhnd.permute(0, 2, 1, 3).reshape(rows, heads, dh)
     r_out, r_gate, _, _ = ops_ref.attention_gate_forward(attn_rows.double(), x.double(), w.double(), b.double())
-    a_dev = attn_bhnd.to(cuda_device)
+    a_dev = attn_bhnd.to(cuda_device)  # keeps the layout's strides
     out = torch.empty(rows, heads * dh, dtype=dtype, device=cuda_device)
     gate = torch.empty(rows, heads, dtype=dtype, device=cuda_device)
     xd, wd, bd = x.to(cuda_device), w.to(cuda_device), b.to(cuda_device)

@@ -87,14 +87,16 @@ def test_qkv_linear_rotary_matches_unfused_split(cuda_device):
         assert bad < 1e-3, f"output {i}: {bad:.2%} of values differ by more than 2 ulps"
 
 
+@pytest.mark.parametrize("heads,dh", [(2, 32), (8, 64)])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
-def test_row_map_matches_permuted_input(cuda_device, dtype):
+def test_row_map_matches_permuted_input(cuda_device, dtype, heads, dh):
     """Rows ordered (outer, position, inner) with inner > 1 give the same q / k / v, gate output and input
-    gradients as the permuted copy in plain (sequence, position) order: the axial transformer's time axis."""
+    gradients as the permuted copy in plain (sequence, position) order: the axial transformer's time axis.
+    8 heads of 64 run the streamed gate kernels, 2 heads of 32 the tiled ones."""
     from pymsst_b200.fused import AttentionGateFn
 
     torch.manual_seed(9)
-    b, t, f, d, heads, dh = 2, 37, 6, 64, 2, 32
+    b, t, f, d = 2, 37, 6, 64
     x = torch.randn(b, t, f, d, device=cuda_device).to(dtype)
     w = (torch.randn(3 * heads * dh, d, device=cuda_device) / d ** 0.5)
     gw = torch.randn(heads, d, device=cuda_device) * 0.1
