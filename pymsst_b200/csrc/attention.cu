@@ -429,24 +429,87 @@ __device__ __forceinline__ void store_row32(T* dst, const uint32_t (&a)[32], flo
   }
 }
 
+// 16 columns of this warp's TMEM lane quarter, without waiting (see tmem_wait16).
+__device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tie16(uint32_t (&r)[16]) {
+  asm volatile(""
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15]));
+}
+
+__device__ __forceinline__ void tmem_wait16(uint32_t (&a)[16], uint32_t (&b)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+  tie16(a);
+  tie16(b);
+}
+
+// 16 fp32 values -> chunks c0, c0 + 1 of row r of a 16-bit SW128 tile
+template <typename T>
+__device__ __forceinline__ void put_row16(uint8_t* tile, int r, int c0, const float* v) {
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+    *reinterpret_cast<uint4*>(tile + sw128(r, c0 + i)) =
+        make_uint4(pack2<T>(v[8 * i], v[8 * i + 1]), pack2<T>(v[8 * i + 2], v[8 * i + 3]),
+                   pack2<T>(v[8 * i + 4], v[8 * i + 5]), pack2<T>(v[8 * i + 6], v[8 * i + 7]));
+}
+
+// D[tmem] (+)= A * B^T over K = 16 * ksteps: A a 128-row K-major SW128 tile
+// (128-byte rows, the first 32 * ksteps bytes of each used), B K-major (its
+// rows are the N index) or MN-major (rows are K, the 64 head elements N).
+__device__ __forceinline__ void mma_k(uint32_t d, uint32_t a_base, uint32_t b_base, bool b_mn, uint32_t idesc,
+                                      bool accumulate, int ksteps) {
+  for (int kk = 0; kk < ksteps; ++kk) {
+    const uint64_t a = umma::smem_desc_sw128(a_base + kk * 32, 16, 1024);
+    const uint64_t b = b_mn ? umma::smem_desc_sw128(b_base + kk * 16 * 128, BN * 128, 1024)
+                            : umma::smem_desc_sw128(b_base + kk * 32, 16, 1024);
+    umma::mma_f16(d, a, b, idesc, (accumulate || kk) ? 1u : 0u);
+  }
+}
+
+// Backward chunks are 32 rows: S / dP (or their transposes) are then 32 TMEM
+// columns each, so two buffers of both plus the 64-column accumulators fit in
+// 256 columns, and the next chunk's products run while the row threads work
+// on the current one.  The row threads' 16-bit operand tile (dS, or P^T and
+// dS^T) is single-buffered: a thread writes chunk c's rows only after the
+// products that read chunk c-1's have completed (the *_free barriers).
+constexpr int CB = 32;                // rows per backward chunk
+constexpr int CTILE = CB * kD * 2;    // 4 KB
+
+template <typename T>
+struct IdescB {
+  static constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+  static constexpr uint32_t K32 = umma::idesc_f16(kBf16, false, false, BM, CB);  // N = 32 chunk rows
+  static constexpr uint32_t MN = umma::idesc_f16(kBf16, false, true, BM, kD);    // N = head dim
+};
+
 // ------------------------------------------------------------ backward: dQ
 // Item = 128 queries.  Lane 0 of warp 0 loads the Q and dO tiles, lane 1
-// streams K/V chunks.  Per chunk the MMA lane issues S = Q K_c^T and
-// dP = dO V_c^T, waits for the row threads' dS_c, and issues dQ += dS_c K_c
-// (K_c as the MN-major operand).  The row threads compute D = rowsum(dO * O)
-// for their query once per item (each half-row thread one half, combined
-// through shared memory; written out for the dK/dV kernel), then per chunk
+// streams 32-key K/V chunks through a 4-deep ring.  The MMA lane keeps S and
+// dP one chunk ahead (S_c = Q K_c^T, dP_c = dO V_c^T into TMEM buffer c % 2)
+// and, once the row threads have written dS_c, issues dQ += dS_c K_c (K_c as
+// the MN-major operand).  The row threads compute D = rowsum(dO * O) for
+// their query once per item (two half-row threads combined through shared
+// memory; written out for the dK/dV kernel), then per chunk
 // P = exp2(S * scale * log2e - lse * log2e) and dS = P (dP - D).
 namespace bq {
-constexpr int kStages = 3;
+constexpr int kStages = 4;
 constexpr int OFF_DO = TILE128;
-constexpr int OFF_KV = 2 * TILE128;
-constexpr int OFF_DS = OFF_KV + kStages * 2 * TILE64;
-constexpr int OFF_BAR = OFF_DS + BM * BN * 2;
-constexpr int kBars = 2 + 2 * kStages + 5;
-constexpr int OFF_X = OFF_BAR + 256;  // [2][128] fp32 partial row sums of D
+constexpr int OFF_KV = 2 * TILE128;                    // kStages x (K 4 KB, V 4 KB)
+constexpr int OFF_DS = OFF_KV + kStages * 2 * CTILE;   // dS: 128 rows x 128 bytes (first 64 used)
+constexpr int OFF_BAR = OFF_DS + TILE128;
+constexpr int kBars = 2 + 2 * kStages + 4 + 2 + 3;
+constexpr int OFF_X = OFF_BAR + 256;                   // [2][128] fp32 partial row sums of D
 constexpr int SMEM = OFF_X + 2 * BM * 4 + 1024;
-constexpr uint32_t kTmemDP = 64, kTmemDQ = 128;
+constexpr uint32_t kTmemDP = 64, kTmemDQ = 128;       // S[2] at 0, 32; dP[2] at 64, 96
 }  // namespace bq
 
 template <typename T>
@@ -463,16 +526,18 @@ __global__ void __launch_bounds__(kBwdThreads, 2)
   uint64_t* qd_empty = bars + 1;
   uint64_t* kv_full = bars + 2;
   uint64_t* kv_empty = kv_full + kStages;
-  uint64_t* sd_full = kv_empty + kStages;
-  uint64_t* ds_full = sd_full + 1;
-  uint64_t* dq_full = ds_full + 1;
+  uint64_t* sd_full = kv_empty + kStages;  // [2]
+  uint64_t* s_free = sd_full + 2;          // [2]
+  uint64_t* ds_full = s_free + 2;
+  uint64_t* ds_free = ds_full + 1;
+  uint64_t* dq_full = ds_free + 1;
   uint64_t* dq_empty = dq_full + 1;
-  uint64_t* x_full = dq_empty + 1;  // both halves of every row's D partial are in xs
+  uint64_t* x_full = dq_empty + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kBars);
   float* xs = reinterpret_cast<float*>(smem + OFF_X);
   __shared__ int abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nch = (N + BN - 1) / BN;
+  const int nch = (N + CB - 1) / CB;
   if (threadIdx.x == 0) {
     umma::mbar_init(qd_full, 1);
     umma::mbar_init(qd_empty, 1 + kRowWarpsBwd);  // MMA commit + the row warps' D reads
@@ -480,8 +545,12 @@ __global__ void __launch_bounds__(kBwdThreads, 2)
       umma::mbar_init(&kv_full[s], 1);
       umma::mbar_init(&kv_empty[s], 1);
     }
-    umma::mbar_init(sd_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      umma::mbar_init(&sd_full[b], 1);
+      umma::mbar_init(&s_free[b], kRowWarpsBwd);
+    }
     umma::mbar_init(ds_full, kRowWarpsBwd);
+    umma::mbar_init(ds_free, 1);
     umma::mbar_init(dq_full, 1);
     umma::mbar_init(dq_empty, kRowWarpsBwd);
     umma::mbar_init(x_full, kRowWarpsBwd);
@@ -521,43 +590,51 @@ __global__ void __launch_bounds__(kBwdThreads, 2)
             abort_flag = 1;
             break;
           }
-          uint8_t* dst = smem + OFF_KV + s * 2 * TILE64;
-          umma::mbar_arrive_expect_tx(&kv_full[s], 2 * TILE64);
-          umma::tma_load_4d(dst, &tmK, &kv_full[s], 0, it.h, j * BN, it.b);
-          umma::tma_load_4d(dst + TILE64, &tmV, &kv_full[s], 0, it.h, j * BN, it.b);
+          uint8_t* dst = smem + OFF_KV + s * 2 * CTILE;
+          umma::mbar_arrive_expect_tx(&kv_full[s], 2 * CTILE);
+          umma::tma_load_4d(dst, &tmK, &kv_full[s], 0, it.h, j * CB, it.b);
+          umma::tma_load_4d(dst + CTILE, &tmV, &kv_full[s], 0, it.h, j * CB, it.b);
         }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
+      // S_c, dP_c into TMEM buffer c % 2
+      auto issue_s = [&](uint32_t c, bool last) -> bool {
+        const int s = c % kStages, b = c & 1;
+        if (!umma::mbar_wait(&kv_full[s], (c / kStages) & 1, 0x54)) return false;
+        if (!umma::mbar_wait(&s_free[b], ((c >> 1) & 1) ^ 1, 0x5b)) return false;
+        umma::tc_fence_after();
+        const uint32_t k_base = umma::smem_u32(smem + OFF_KV + s * 2 * CTILE);
+        mma_k(tmem + b * CB, umma::smem_u32(smem), k_base, false, IdescB<T>::K32, false, 4);                  // S
+        mma_k(tmem + kTmemDP + b * CB, umma::smem_u32(smem + OFF_DO), k_base + CTILE, false, IdescB<T>::K32,  // dP
+              false, 4);
+        umma::mma_commit(&sd_full[b]);
+        if (last) umma::mma_commit(qd_empty);
+        return true;
+      };
       uint32_t cc = 0, t = 0;
       bool ok = true;
       for (int item = blockIdx.x; item < total && ok && !abort_flag; item += gridDim.x, ++t) {
-        if (!umma::mbar_wait(qd_full, t & 1, 0x53)) {
+        if (!umma::mbar_wait(qd_full, t & 1, 0x53) || !issue_s(cc, nch == 1)) {
           ok = false;
           break;
         }
-        umma::tc_fence_after();
-        for (int j = 0; j < nch && ok; ++j, ++cc) {
-          const int s = cc % kStages;
-          if (!umma::mbar_wait(&kv_full[s], (cc / kStages) & 1, 0x54)) {
+        for (int j = 0; j < nch; ++j, ++cc) {
+          if (j + 1 < nch && !issue_s(cc + 1, j + 2 == nch)) {
             ok = false;
             break;
           }
-          umma::tc_fence_after();
-          const uint32_t k_base = umma::smem_u32(smem + OFF_KV + s * 2 * TILE64);
-          mma_k64(tmem, umma::smem_u32(smem), k_base, false, Idesc<T>::K, false);                    // S
-          mma_k64(tmem + kTmemDP, umma::smem_u32(smem + OFF_DO), k_base + TILE64, false, Idesc<T>::K, false);  // dP
-          umma::mma_commit(sd_full);
-          if (j == nch - 1) umma::mma_commit(qd_empty);
           if (!umma::mbar_wait(ds_full, cc & 1, 0x55) ||
               (j == 0 && !umma::mbar_wait(dq_empty, (t & 1) ^ 1, 0x56))) {
             ok = false;
             break;
           }
           umma::tc_fence_after();
-          mma_k64(tmem + kTmemDQ, umma::smem_u32(smem + OFF_DS), k_base, true, Idesc<T>::MN, j > 0);  // dQ += dS K
-          umma::mma_commit(&kv_empty[s]);
+          const uint32_t k_base = umma::smem_u32(smem + OFF_KV + (cc % kStages) * 2 * CTILE);
+          mma_k(tmem + kTmemDQ, umma::smem_u32(smem + OFF_DS), k_base, true, IdescB<T>::MN, j > 0, 2);  // dQ += dS K
+          umma::mma_commit(ds_free);
+          umma::mma_commit(&kv_empty[cc % kStages]);
           if (j == nch - 1) umma::mma_commit(dq_full);
         }
       }
@@ -572,17 +649,24 @@ __global__ void __launch_bounds__(kBwdThreads, 2)
       const Item it = item_at(item, nblk, H);
       const int r = it.blk * BM + row;
       const bool valid = r < N;
+      // this row's half of O and its lse, loaded while the tiles are still in flight
+      uint4 orow[4] = {};
+      float lse2 = 0.f;
+      if (valid) {
+        const T* src = o + it.b * po.s_b + it.h * po.s_h + (int64_t)r * po.s_n + half * 32;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) orow[i] = *reinterpret_cast<const uint4*>(src + 8 * i);
+        lse2 = lse[(int64_t)it.bh * ldl + r] * kLog2e;
+      }
       if (!umma::mbar_wait(qd_full, t & 1, 0x57)) {
         abort_flag = 1;
         break;
       }
-      float part = 0.f, lse2 = 0.f;
+      float part = 0.f;
       if (valid) {
-        const T* src = o + it.b * po.s_b + it.h * po.s_h + (int64_t)r * po.s_n + half * 32;
-        lse2 = lse[(int64_t)it.bh * ldl + r] * kLog2e;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const uint4 o4 = *reinterpret_cast<const uint4*>(src + 8 * i);
+          const uint4 o4 = orow[i];
           const uint4 d4 = *reinterpret_cast<const uint4*>(smem + OFF_DO + sw128(row, half * 4 + i));
           const T* oe = reinterpret_cast<const T*>(&o4);
           const T* de = reinterpret_cast<const T*>(&d4);
@@ -601,25 +685,32 @@ __global__ void __launch_bounds__(kBwdThreads, 2)
       warp_arrive(qd_empty, false);
       bool ok = true;
       for (int j = 0; j < nch; ++j, ++cc) {
-        if (!umma::mbar_wait(sd_full, cc & 1, 0x58)) {
+        const int b = cc & 1;
+        if (!umma::mbar_wait(&sd_full[b], (cc >> 1) & 1, 0x58)) {
           ok = false;
           break;
         }
         umma::tc_fence_after();
-        uint32_t su[32], du[32];
-        tmem_ld32_nowait(tmem + lane_off + half * 32, su);
-        tmem_ld32_nowait(tmem + lane_off + kTmemDP + half * 32, du);
-        tmem_wait2(su, du);
-        const int k0 = j * BN + half * 32;
-        const bool tail = k0 + 32 > N;
-        float(&ds)[32] = *reinterpret_cast<float(*)[32]>(&su);  // dS overwrites S in place
+        uint32_t su[16], du[16];
+        tmem_ld16_nowait(tmem + lane_off + b * CB + half * 16, su);
+        tmem_ld16_nowait(tmem + lane_off + kTmemDP + b * CB + half * 16, du);
+        tmem_wait16(su, du);
+        warp_arrive(&s_free[b], false);  // the next-but-one chunk may overwrite this TMEM buffer
+        const int k0 = j * CB + half * 16;
+        const bool tail = k0 + 16 > N;
+        float* ds = reinterpret_cast<float*>(su);  // dS overwrites S in place
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
+        for (int c = 0; c < 16; ++c) {
           float p = exp2f(fmaf(__uint_as_float(su[c]), sl2, -lse2));
           if (tail && k0 + c >= N) p = 0.f;  // keys past the end
           ds[c] = p * (__uint_as_float(du[c]) - dsum);
         }
-        put_row32<T>(smem + OFF_DS, row, half * 4, ds);
+        // the dQ product of the previous chunk has read the dS tile
+        if (!umma::mbar_wait(ds_free, (cc & 1) ^ 1, 0x5c)) {
+          ok = false;
+          break;
+        }
+        put_row16<T>(smem + OFF_DS, row, half * 2, ds);
         warp_arrive(ds_full, true);
       }
       if (!ok || !umma::mbar_wait(dq_full, t & 1, 0x59)) {
@@ -645,22 +736,23 @@ __global__ void __launch_bounds__(kBwdThreads, 2)
 
 // -------------------------------------------------------- backward: dK, dV
 // Item = 128 keys.  Lane 0 of warp 0 loads the K and V tiles, lane 1 streams
-// chunks of 64 queries: Q_c, dO_c and their lse / D slices.  Per chunk the
-// MMA lane issues S^T = K Q_c^T and dP^T = V dO_c^T, waits for the row
-// threads' P^T and dS^T (one key per thread pair), then dV += P^T dO_c and
-// dK += dS^T Q_c (dO_c and Q_c as MN-major operands); the accumulators stay
-// in tensor memory for the whole item.
+// chunks of 32 queries -- Q_c, dO_c and their lse / D slices -- through a
+// 4-deep ring.  The MMA lane keeps S^T = K Q_c^T and dP^T = V dO_c^T one
+// chunk ahead (TMEM buffer c % 2) and, once the row threads have written
+// P^T and dS^T (one key per thread pair), issues dV += P^T dO_c and
+// dK += dS^T Q_c (dO_c and Q_c as MN-major operands); the accumulators stay in
+// tensor memory for the whole item.
 namespace bk {
-constexpr int kStages = 2;
-constexpr int STAGE = 2 * TILE64 + 1024;  // Q, dO, then lse[64] and D[64]
+constexpr int kStages = 4;
+constexpr int STAGE = 2 * CTILE + 1024;  // Q, dO, then lse[32] and D[32] (1024-aligned stride)
 constexpr int OFF_V = TILE128;
 constexpr int OFF_CH = 2 * TILE128;
-constexpr int OFF_PT = OFF_CH + kStages * STAGE;
-constexpr int OFF_DST = OFF_PT + BM * BN * 2;
-constexpr int OFF_BAR = OFF_DST + BM * BN * 2;
-constexpr int kBars = 2 + 2 * kStages + 4;
+constexpr int OFF_PT = OFF_CH + kStages * STAGE;  // P^T, dS^T: 128 rows x 128 bytes (first 64 used)
+constexpr int OFF_DST = OFF_PT + TILE128;
+constexpr int OFF_BAR = OFF_DST + TILE128;
+constexpr int kBars = 2 + 2 * kStages + 4 + 4;
 constexpr int SMEM = OFF_BAR + kBars * 8 + 16 + 1024;
-constexpr uint32_t kTmemDPT = 64, kTmemDV = 128, kTmemDK = 192;
+constexpr uint32_t kTmemDPT = 64, kTmemDV = 128, kTmemDK = 192;  // S^T[2] at 0, 32; dP^T[2] at 64, 96
 }  // namespace bk
 
 template <typename T>
@@ -678,14 +770,16 @@ __global__ void __launch_bounds__(kBwdThreads, 2)
   uint64_t* kv_empty = bars + 1;
   uint64_t* ch_full = bars + 2;
   uint64_t* ch_empty = ch_full + kStages;
-  uint64_t* sd_full = ch_empty + kStages;
-  uint64_t* ps_full = sd_full + 1;
-  uint64_t* acc_full = ps_full + 1;
+  uint64_t* sd_full = ch_empty + kStages;  // [2]
+  uint64_t* s_free = sd_full + 2;          // [2]
+  uint64_t* ps_full = s_free + 2;
+  uint64_t* pt_free = ps_full + 1;
+  uint64_t* acc_full = pt_free + 1;
   uint64_t* acc_empty = acc_full + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kBars);
   __shared__ int abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nch = (N + BN - 1) / BN;
+  const int nch = (N + CB - 1) / CB;
   if (threadIdx.x == 0) {
     umma::mbar_init(kv_full, 1);
     umma::mbar_init(kv_empty, 1);
@@ -693,8 +787,12 @@ __global__ void __launch_bounds__(kBwdThreads, 2)
       umma::mbar_init(&ch_full[s], 1);
       umma::mbar_init(&ch_empty[s], 1);
     }
-    umma::mbar_init(sd_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      umma::mbar_init(&sd_full[b], 1);
+      umma::mbar_init(&s_free[b], kRowWarpsBwd);
+    }
     umma::mbar_init(ps_full, kRowWarpsBwd);
+    umma::mbar_init(pt_free, 1);
     umma::mbar_init(acc_full, 1);
     umma::mbar_init(acc_empty, kRowWarpsBwd);
     abort_flag = 0;
@@ -736,45 +834,52 @@ __global__ void __launch_bounds__(kBwdThreads, 2)
             break;
           }
           uint8_t* dst = smem + OFF_CH + s * STAGE;
-          umma::mbar_arrive_expect_tx(&ch_full[s], 2 * TILE64 + 2 * BN * 4);
-          umma::tma_load_4d(dst, &tmQ, &ch_full[s], 0, it.h, j * BN, it.b);
-          umma::tma_load_4d(dst + TILE64, &tmDO, &ch_full[s], 0, it.h, j * BN, it.b);
-          umma::tma_load_2d(dst + 2 * TILE64, &tmL, &ch_full[s], j * BN, it.bh);
-          umma::tma_load_2d(dst + 2 * TILE64 + BN * 4, &tmD, &ch_full[s], j * BN, it.bh);
+          umma::mbar_arrive_expect_tx(&ch_full[s], 2 * CTILE + 2 * CB * 4);
+          umma::tma_load_4d(dst, &tmQ, &ch_full[s], 0, it.h, j * CB, it.b);
+          umma::tma_load_4d(dst + CTILE, &tmDO, &ch_full[s], 0, it.h, j * CB, it.b);
+          umma::tma_load_2d(dst + 2 * CTILE, &tmL, &ch_full[s], j * CB, it.bh);
+          umma::tma_load_2d(dst + 2 * CTILE + CB * 4, &tmD, &ch_full[s], j * CB, it.bh);
         }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
+      auto issue_s = [&](uint32_t c, bool last) -> bool {
+        const int s = c % kStages, b = c & 1;
+        if (!umma::mbar_wait(&ch_full[s], (c / kStages) & 1, 0x64)) return false;
+        if (!umma::mbar_wait(&s_free[b], ((c >> 1) & 1) ^ 1, 0x6b)) return false;
+        umma::tc_fence_after();
+        const uint32_t q_base = umma::smem_u32(smem + OFF_CH + s * STAGE);
+        mma_k(tmem + b * CB, umma::smem_u32(smem), q_base, false, IdescB<T>::K32, false, 4);                 // S^T
+        mma_k(tmem + kTmemDPT + b * CB, umma::smem_u32(smem + OFF_V), q_base + CTILE, false, IdescB<T>::K32,  // dP^T
+              false, 4);
+        umma::mma_commit(&sd_full[b]);
+        if (last) umma::mma_commit(kv_empty);
+        return true;
+      };
       uint32_t cc = 0, t = 0;
       bool ok = true;
       for (int item = blockIdx.x; item < total && ok && !abort_flag; item += gridDim.x, ++t) {
-        if (!umma::mbar_wait(kv_full, t & 1, 0x63)) {
+        if (!umma::mbar_wait(kv_full, t & 1, 0x63) || !issue_s(cc, nch == 1)) {
           ok = false;
           break;
         }
-        umma::tc_fence_after();
-        for (int j = 0; j < nch && ok; ++j, ++cc) {
-          const int s = cc % kStages;
-          if (!umma::mbar_wait(&ch_full[s], (cc / kStages) & 1, 0x64)) {
+        for (int j = 0; j < nch; ++j, ++cc) {
+          if (j + 1 < nch && !issue_s(cc + 1, j + 2 == nch)) {
             ok = false;
             break;
           }
-          umma::tc_fence_after();
-          const uint32_t q_base = umma::smem_u32(smem + OFF_CH + s * STAGE), do_base = q_base + TILE64;
-          mma_k64(tmem, umma::smem_u32(smem), q_base, false, Idesc<T>::K, false);                  // S^T = K Q^T
-          mma_k64(tmem + kTmemDPT, umma::smem_u32(smem + OFF_V), do_base, false, Idesc<T>::K, false);  // dP^T = V dO^T
-          umma::mma_commit(sd_full);
-          if (j == nch - 1) umma::mma_commit(kv_empty);
           if (!umma::mbar_wait(ps_full, cc & 1, 0x65) ||
               (j == 0 && !umma::mbar_wait(acc_empty, (t & 1) ^ 1, 0x66))) {
             ok = false;
             break;
           }
           umma::tc_fence_after();
-          mma_k64(tmem + kTmemDV, umma::smem_u32(smem + OFF_PT), do_base, true, Idesc<T>::MN, j > 0);   // dV
-          mma_k64(tmem + kTmemDK, umma::smem_u32(smem + OFF_DST), q_base, true, Idesc<T>::MN, j > 0);   // dK
-          umma::mma_commit(&ch_empty[s]);
+          const uint32_t q_base = umma::smem_u32(smem + OFF_CH + (cc % kStages) * STAGE);
+          mma_k(tmem + kTmemDV, umma::smem_u32(smem + OFF_PT), q_base + CTILE, true, IdescB<T>::MN, j > 0, 2);  // dV
+          mma_k(tmem + kTmemDK, umma::smem_u32(smem + OFF_DST), q_base, true, IdescB<T>::MN, j > 0, 2);        // dK
+          umma::mma_commit(pt_free);
+          umma::mma_commit(&ch_empty[cc % kStages]);
           if (j == nch - 1) umma::mma_commit(acc_full);
         }
       }
@@ -789,27 +894,29 @@ __global__ void __launch_bounds__(kBwdThreads, 2)
       const Item it = item_at(item, nblk, H);
       bool ok = true;
       for (int j = 0; j < nch; ++j, ++cc) {
-        const int s = cc % kStages;
+        const int s = cc % kStages, b = cc & 1;
         // the lse / D slices are read from the stage: wait for its TMA as well as for the products
-        if (!umma::mbar_wait(&ch_full[s], (cc / kStages) & 1, 0x67) || !umma::mbar_wait(sd_full, cc & 1, 0x68)) {
+        if (!umma::mbar_wait(&ch_full[s], (cc / kStages) & 1, 0x67) ||
+            !umma::mbar_wait(&sd_full[b], (cc >> 1) & 1, 0x68)) {
           ok = false;
           break;
         }
         umma::tc_fence_after();
-        uint32_t su[32], du[32];
-        tmem_ld32_nowait(tmem + lane_off + half * 32, su);
-        tmem_ld32_nowait(tmem + lane_off + kTmemDPT + half * 32, du);
-        const float* ls = reinterpret_cast<const float*>(smem + OFF_CH + s * STAGE + 2 * TILE64) + half * 32;
-        const float* ds = ls + BN;
-        const int q0 = j * BN + half * 32;
-        const bool tail = q0 + 32 > N;
-        tmem_wait2(su, du);
-        float(&pt)[32] = *reinterpret_cast<float(*)[32]>(&su);   // P^T overwrites S^T in place
-        float(&dst)[32] = *reinterpret_cast<float(*)[32]>(&du);  // dS^T overwrites dP^T in place
+        uint32_t su[16], du[16];
+        tmem_ld16_nowait(tmem + lane_off + b * CB + half * 16, su);
+        tmem_ld16_nowait(tmem + lane_off + kTmemDPT + b * CB + half * 16, du);
+        const float* ls = reinterpret_cast<const float*>(smem + OFF_CH + s * STAGE + 2 * CTILE) + half * 16;
+        const float* dd_s = ls + CB;
+        const int q0 = j * CB + half * 16;
+        const bool tail = q0 + 16 > N;
+        tmem_wait16(su, du);
+        warp_arrive(&s_free[b], false);
+        float* pt = reinterpret_cast<float*>(su);   // P^T overwrites S^T in place
+        float* dst = reinterpret_cast<float*>(du);  // dS^T overwrites dP^T in place
 #pragma unroll
-        for (int c4 = 0; c4 < 8; ++c4) {
+        for (int c4 = 0; c4 < 4; ++c4) {
           const float4 l4 = *reinterpret_cast<const float4*>(ls + 4 * c4);
-          const float4 d4 = *reinterpret_cast<const float4*>(ds + 4 * c4);
+          const float4 d4 = *reinterpret_cast<const float4*>(dd_s + 4 * c4);
           const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dd[4] = {d4.x, d4.y, d4.z, d4.w};
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
@@ -821,8 +928,13 @@ __global__ void __launch_bounds__(kBwdThreads, 2)
             dst[c] = dead ? 0.f : p * (__uint_as_float(du[c]) - dd[e]);
           }
         }
-        put_row32<T>(smem + OFF_PT, row, half * 4, pt);
-        put_row32<T>(smem + OFF_DST, row, half * 4, dst);
+        // the dV / dK products of the previous chunk have read the operand tiles
+        if (!umma::mbar_wait(pt_free, (cc & 1) ^ 1, 0x6c)) {
+          ok = false;
+          break;
+        }
+        put_row16<T>(smem + OFF_PT, row, half * 2, pt);
+        put_row16<T>(smem + OFF_DST, row, half * 2, dst);
         warp_arrive(ps_full, true);
       }
       if (!ok || !umma::mbar_wait(acc_full, t & 1, 0x69)) {
@@ -978,17 +1090,17 @@ extern "C" int pmb_attention_backward(const void* q, const void* k, const void* 
               "%s: q, k, v, grad_out strides must not overlap (head >= 64, position >= heads * head, sequence >= "
               "seq_len * position)", name);
   float* delta = static_cast<float*>(workspace);
-  CUtensorMap mq128, mdo128, mk64, mv64, mk128, mv128, mq64, mdo64, ml, md;
+  CUtensorMap mq128, mdo128, mk64, mv64, mk128, mv128, mq64, mdo64, ml, md;  // *64: 32-row chunk maps
   if (int st = plane_map(mq128, q, pq, dtype, sequences, N, H, BM, name)) return st;
   if (int st = plane_map(mdo128, grad_out, pdo, dtype, sequences, N, H, BM, name)) return st;
-  if (int st = plane_map(mk64, k, pk, dtype, sequences, N, H, BN, name)) return st;
-  if (int st = plane_map(mv64, v, pv, dtype, sequences, N, H, BN, name)) return st;
+  if (int st = plane_map(mk64, k, pk, dtype, sequences, N, H, CB, name)) return st;
+  if (int st = plane_map(mv64, v, pv, dtype, sequences, N, H, CB, name)) return st;
   if (int st = plane_map(mk128, k, pk, dtype, sequences, N, H, BM, name)) return st;
   if (int st = plane_map(mv128, v, pv, dtype, sequences, N, H, BM, name)) return st;
-  if (int st = plane_map(mq64, q, pq, dtype, sequences, N, H, BN, name)) return st;
-  if (int st = plane_map(mdo64, grad_out, pdo, dtype, sequences, N, H, BN, name)) return st;
-  if (int st = tma::make_map_rows_f32(ml, lse, ldl, rows, ldl * 4, BN, name)) return st;
-  if (int st = tma::make_map_rows_f32(md, delta, ldl, rows, ldl * 4, BN, name)) return st;
+  if (int st = plane_map(mq64, q, pq, dtype, sequences, N, H, CB, name)) return st;
+  if (int st = plane_map(mdo64, grad_out, pdo, dtype, sequences, N, H, CB, name)) return st;
+  if (int st = tma::make_map_rows_f32(ml, lse, ldl, rows, ldl * 4, CB, name)) return st;
+  if (int st = tma::make_map_rows_f32(md, delta, ldl, rows, ldl * 4, CB, name)) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int grid = grid_for(total);
   auto run = [&](auto tag) {
