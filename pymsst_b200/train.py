@@ -123,11 +123,9 @@ class Trainer:
         flat = torch.cat([g.reshape(-1) for g in grads])
         dist.all_reduce(flat)
         flat.div_(dist.get_world_size())
-        off = 0
-        for g in grads:
-            n = g.numel()
-            g.copy_(flat[off:off + n].view_as(g))
-            off += n
+        # back into the gradients with multi-tensor copies (a handful of launches, not one per parameter)
+        parts = flat.split([g.numel() for g in grads])
+        torch._foreach_copy_(grads, [v.view_as(g) for v, g in zip(parts, grads)])
 
     def _update(self):
         if self.grad_clip:
