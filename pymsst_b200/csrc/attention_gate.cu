@@ -467,7 +467,7 @@ __global__ void __launch_bounds__(kThreads, 3)
 // cp.async.wait_group -- no spin waits.  The arithmetic is that of the tiled
 // kernels above; results leave with 16-byte stores.
 constexpr int kStreamRows = 8;
-constexpr int kStreamStages = 4;
+constexpr int kStreamStages = 3;
 
 struct StreamLayout {
   int hd_b, x_b, g_b, xld, wld;             // bytes per attention / x / gate row; x and W row pitch (elements)
@@ -552,23 +552,27 @@ __global__ void __launch_bounds__(kThreads, 3)
                     T* __restrict__ gate) {
   constexpr int V = Vec<T>::N;  // 8
   extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ int64_t rb_s[kStreamStages][kStreamRows];
+  __shared__ int64_t rb_s[kStreamStages + 1][kStreamRows];
   const StreamLayout L(H, Dh, dim, sizeof(T), false);
   float* w_s = reinterpret_cast<float*>(smem + L.off_w);
   float* g_s = reinterpret_cast<float*>(smem + L.off_gp);
   load_weights_stream<TP>(W, H, dim, w_s, L.wld);
   const StreamRing ring{rows, (rows + kStreamRows - 1) / kStreamRows};
-  auto prefetch = [&](int64_t t, int st) {  // whole CTA; ends with a commit (empty when t is past the end)
-    if (t < ring.tiles) {
-      const int n = ring.rows_of(t);
-      if (threadIdx.x < kStreamRows) rb_s[st][threadIdx.x] = threadIdx.x < n ? la.row_base(t * kStreamRows + threadIdx.x) : 0;
-      __syncthreads();
-      load_tile_async<T>(smem + st * L.stage, L, rb_s[st], attn, x, (const T*)nullptr, (const T*)nullptr,
-                         t * kStreamRows, n, H, dim);
-    }
+  // row bases of the tile of iteration k live in slot k % (kStreamStages + 1); they are computed one
+  // iteration before that tile is put in flight, so the copies need no barrier of their own
+  auto bases = [&](int64_t t, int slot) {
+    if (threadIdx.x < kStreamRows)
+      rb_s[slot][threadIdx.x] = (t < ring.tiles && threadIdx.x < ring.rows_of(t)) ? la.row_base(t * kStreamRows + threadIdx.x) : 0;
+  };
+  auto prefetch = [&](int64_t t, int st, int slot) {  // whole CTA; ends with a commit (empty past the end)
+    if (t < ring.tiles)
+      load_tile_async<T>(smem + st * L.stage, L, rb_s[slot], attn, x, (const T*)nullptr, (const T*)nullptr,
+                         t * kStreamRows, ring.rows_of(t), H, dim);
     cp_commit();
   };
-  for (int s = 0; s < kStreamStages - 1; ++s) prefetch(blockIdx.x + (int64_t)s * gridDim.x, s);
+  for (int s = 0; s < kStreamStages; ++s) bases(blockIdx.x + (int64_t)s * gridDim.x, s);
+  __syncthreads();
+  for (int s = 0; s < kStreamStages - 1; ++s) prefetch(blockIdx.x + (int64_t)s * gridDim.x, s, s);
   const int vh = Dh / V, vr = H * vh, nck = dim / V;
   // logits: 4 threads per (row, head), each a quarter of the 8-element chunks
   const int lp = threadIdx.x >> 2, lq = threadIdx.x & 3, lr = lp / H, lh = lp - lr * H;
@@ -578,7 +582,8 @@ __global__ void __launch_bounds__(kThreads, 3)
   int it = 0;
   for (int64_t tile = blockIdx.x; tile < ring.tiles; tile += gridDim.x, ++it) {
     const int st = it % kStreamStages;
-    prefetch(tile + (int64_t)(kStreamStages - 1) * gridDim.x, (it + kStreamStages - 1) % kStreamStages);
+    prefetch(tile + (int64_t)(kStreamStages - 1) * gridDim.x, (it + kStreamStages - 1) % kStreamStages,
+             (it + kStreamStages - 1) % (kStreamStages + 1));
     cp_wait<kStreamStages - 1>();
     __syncthreads();  // this tile's copies from every thread have landed
     const int64_t r0 = tile * kStreamRows;
@@ -586,6 +591,7 @@ __global__ void __launch_bounds__(kThreads, 3)
     const uint8_t* base = smem + st * L.stage;
     const T* at_s = reinterpret_cast<const T*>(base + L.off_at);
     const T* x_s = reinterpret_cast<const T*>(base + L.off_x);
+    bases(tile + (int64_t)kStreamStages * gridDim.x, (it + kStreamStages) % (kStreamStages + 1));
     if (lp < kStreamRows * H) {  // warp-uniform: kStreamRows * H * 4 is a multiple of 32
       const T* xr = x_s + lr * L.xld;
       const float* wr = w_s + lh * L.wld;
@@ -621,29 +627,32 @@ __global__ void __launch_bounds__(kThreads, 3)
 }
 
 template <typename T, typename TP>
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(kThreads, 3)
     gate_bwd_stream(const T* __restrict__ grad_out, const T* __restrict__ attn, AttnLayout la,
                     const T* __restrict__ x, const TP* __restrict__ W, const T* __restrict__ gate, int64_t rows,
                     int H, int Dh, int dim, T* __restrict__ grad_attn, T* __restrict__ grad_x,
                     float* __restrict__ partial_w, float* __restrict__ partial_b) {
   constexpr int V = Vec<T>::N;  // 8
   extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ int64_t rb_s[kStreamStages][kStreamRows];
+  __shared__ int64_t rb_s[kStreamStages + 1][kStreamRows];
   const StreamLayout L(H, Dh, dim, sizeof(T), true);
   float* w_s = reinterpret_cast<float*>(smem + L.off_w);
   float* gp_s = reinterpret_cast<float*>(smem + L.off_gp);
   load_weights_stream<TP>(W, H, dim, w_s, L.wld);
   const StreamRing ring{rows, (rows + kStreamRows - 1) / kStreamRows};
-  auto prefetch = [&](int64_t t, int st) {
-    if (t < ring.tiles) {
-      const int n = ring.rows_of(t);
-      if (threadIdx.x < kStreamRows) rb_s[st][threadIdx.x] = threadIdx.x < n ? la.row_base(t * kStreamRows + threadIdx.x) : 0;
-      __syncthreads();
-      load_tile_async<T>(smem + st * L.stage, L, rb_s[st], attn, x, grad_out, gate, t * kStreamRows, n, H, dim);
-    }
+  auto bases = [&](int64_t t, int slot) {  // see gate_fwd_stream
+    if (threadIdx.x < kStreamRows)
+      rb_s[slot][threadIdx.x] = (t < ring.tiles && threadIdx.x < ring.rows_of(t)) ? la.row_base(t * kStreamRows + threadIdx.x) : 0;
+  };
+  auto prefetch = [&](int64_t t, int st, int slot) {
+    if (t < ring.tiles)
+      load_tile_async<T>(smem + st * L.stage, L, rb_s[slot], attn, x, grad_out, gate, t * kStreamRows,
+                         ring.rows_of(t), H, dim);
     cp_commit();
   };
-  for (int s = 0; s < kStreamStages - 1; ++s) prefetch(blockIdx.x + (int64_t)s * gridDim.x, s);
+  for (int s = 0; s < kStreamStages; ++s) bases(blockIdx.x + (int64_t)s * gridDim.x, s);
+  __syncthreads();
+  for (int s = 0; s < kStreamStages - 1; ++s) prefetch(blockIdx.x + (int64_t)s * gridDim.x, s, s);
   const int vh = Dh / V, vr = H * vh, nck = dim / V;
   // grad_attn / gate gradient: fixed column vector cc (head ch), rows c_r0, + c_rs, ...
   const int cc = threadIdx.x % vr, c_r0 = threadIdx.x / vr, c_rs = kThreads / vr, ch = cc / vh;
@@ -666,7 +675,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   int it = 0;
   for (int64_t tile = blockIdx.x; tile < ring.tiles; tile += gridDim.x, ++it) {
     const int st = it % kStreamStages;
-    prefetch(tile + (int64_t)(kStreamStages - 1) * gridDim.x, (it + kStreamStages - 1) % kStreamStages);
+    prefetch(tile + (int64_t)(kStreamStages - 1) * gridDim.x, (it + kStreamStages - 1) % kStreamStages,
+             (it + kStreamStages - 1) % (kStreamStages + 1));
     cp_wait<kStreamStages - 1>();
     __syncthreads();
     const int64_t r0 = tile * kStreamRows;
@@ -676,7 +686,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     const T* at_s = reinterpret_cast<const T*>(base + L.off_at);
     const T* x_s = reinterpret_cast<const T*>(base + L.off_x);
     const T* g_in = reinterpret_cast<const T*>(base + L.off_g);
-    const int64_t* rb = rb_s[st];
+    const int64_t* rb = rb_s[it % (kStreamStages + 1)];
+    bases(tile + (int64_t)kStreamStages * gridDim.x, (it + kStreamStages) % (kStreamStages + 1));
     // grad_attn = grad_out * gate, and per (row, head) the gate-logit gradient
     // sum(grad_out * attn) * g (1 - g), reduced over the head's vh lanes.  The
     // trip count c_r0 < kStreamRows is warp-uniform (vr >= 32 or vr | 32).
@@ -916,7 +927,7 @@ extern "C" int pmb_attention_gate_backward(const void* grad_out, const void* att
       const int bsm = StreamLayout((int)heads, (int)dim_head, (int)dim, sizeof(T), true).bytes;
       PMB_CHECK_CUDA(cudaFuncSetAttribute(gate_bwd_stream<T, TP>, cudaFuncAttributeMaxDynamicSharedMemorySize, bsm),
                      name);
-      const int grid = stream_grid(rows, 2);  // <= 2 x SMs <= kMaxTiledBwdBlocks partial rows
+      const int grid = stream_grid(rows, 3);  // <= 3 x SMs <= kMaxTiledBwdBlocks partial rows
       float* pw = static_cast<float*>(workspace);
       float* pb = reinterpret_cast<float*>(static_cast<char*>(workspace) +
                                            align256((int64_t)kMaxTiledBwdBlocks * heads * dim * 4));
