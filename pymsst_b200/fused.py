@@ -513,6 +513,41 @@ class AttentionFn(torch.autograd.Function):
         return dq, dk, dv
 
 
+class STFTFramesFn(torch.autograd.Function):
+    """x [B, L] fp32 -> windowed frames [B, T, n_fft] of the centred, reflect-padded signal, as torch.stft frames
+    it (window: n_fft values, zero-padded as torch.stft pads a shorter window).  The backward is one
+    deterministic overlap-add per sample with the reflection folded in (pmb_stft_frames_backward) instead of
+    torch's atomic index_add and reflection-pad backward."""
+
+    @staticmethod
+    def forward(ctx, x, window, n_fft, hop):
+        device = nat.require_cuda(x, window, name="STFTFrames")
+        pad = n_fft // 2
+        xp = F.pad(x[:, None], (pad, pad), mode="reflect")[:, 0]
+        frames = xp.unfold(-1, n_fft, hop) * window
+        ctx.save_for_backward(window)
+        ctx.meta = (x.shape[-1], n_fft, hop, device)
+        return frames
+
+    @staticmethod
+    def backward(ctx, grad):
+        (window,) = ctx.saved_tensors
+        length, n_fft, hop, device = ctx.meta
+        g = grad.float().contiguous()
+        b, t, _ = g.shape
+        gx = torch.empty(b, length, dtype=torch.float32, device=device)
+        nat.call("pmb_stft_frames_backward", g.data_ptr(), window.data_ptr(), gx.data_ptr(), b, length, n_fft, hop, t,
+                 nat.stream_handle(device))
+        return gx, None, None, None
+
+
+def stft_loss_spectrum(x: torch.Tensor, n_fft: int, hop: int, window: torch.Tensor, normalized: bool) -> torch.Tensor:
+    """torch.stft(x, n_fft, hop, window=window, center=True, pad_mode="reflect", onesided, return_complex) for
+    fp32 CUDA x [B, L], as [B, T, F] (frames first); window already zero-padded to n_fft."""
+    frames = STFTFramesFn.apply(x, window, n_fft, hop)
+    return torch.fft.rfft(frames, dim=-1, norm="ortho" if normalized else "backward")
+
+
 # -------------------------------------------------------- band index ops
 class BandGatherFn(torch.autograd.Function):
     """stft fp32 [B,S,F,T,2] -> band features [B,T,J*2] in out_dtype."""

@@ -54,6 +54,7 @@ from .fused import (
     compute_dtype,
     rotary_tables,
     attention_supported,
+    stft_loss_spectrum,
     tensor_core_ok,
 )
 
@@ -373,6 +374,16 @@ class _Roformer(nn.Module):
             w = self._windows[key] = torch.hann_window(n, device=device)
         return w
 
+    def _loss_window(self, win: int, n_fft: int, device: torch.device) -> torch.Tensor:
+        """Hann window of `win` samples zero-padded to n_fft as torch.stft pads it (centred)."""
+        key = ("loss", win, n_fft, device.type, device.index)
+        w = self._windows.get(key)
+        if w is None:
+            base = self._window(win, device)
+            left = (n_fft - win) // 2
+            w = self._windows[key] = F.pad(base, (left, n_fft - win - left)).contiguous()
+        return w
+
     def _tables(self, device: torch.device) -> dict:
         key = (device.type, device.index)
         t = self._device_tables.get(key)
@@ -425,10 +436,19 @@ class _Roformer(nn.Module):
             loss = F.l1_loss(recon, target)
             res = 0.0
             for win in self.multi_stft_resolutions_window_sizes:
-                kw = dict(n_fft=max(win, self.multi_stft_n_fft), win_length=win, return_complex=True,
-                          window=self._window(win, recon.device), **self.multi_stft_kwargs)
-                ry = torch.stft(recon.reshape(-1, recon.shape[-1]), **kw)
-                ty = torch.stft(target.reshape(-1, target.shape[-1]), **kw)
+                n_fft = max(win, self.multi_stft_n_fft)
+                if recon.is_cuda:
+                    # torch.stft's framing with an overlap-add backward of this package (same spectra, frames
+                    # first); the L1 mean does not depend on the layout
+                    window = self._loss_window(win, n_fft, recon.device)
+                    hop, norm = self.multi_stft_kwargs["hop_length"], self.multi_stft_kwargs["normalized"]
+                    ry = stft_loss_spectrum(recon.reshape(-1, recon.shape[-1]), n_fft, hop, window, norm)
+                    ty = stft_loss_spectrum(target.reshape(-1, target.shape[-1]), n_fft, hop, window, norm)
+                else:
+                    kw = dict(n_fft=n_fft, win_length=win, return_complex=True,
+                              window=self._window(win, recon.device), **self.multi_stft_kwargs)
+                    ry = torch.stft(recon.reshape(-1, recon.shape[-1]), **kw)
+                    ty = torch.stft(target.reshape(-1, target.shape[-1]), **kw)
                 res = res + F.l1_loss(ry, ty)
         return loss + res * self.multi_stft_resolution_loss_weight
 

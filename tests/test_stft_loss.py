@@ -1,0 +1,81 @@
+"""STFT framing of the multi-resolution STFT loss (STFTFramesFn / pmb_stft_frames_backward) against torch.stft.
+
+The forward is torch.stft's own framing (reflect padding, unfold, window, real FFT), so spectra agree to fp32
+rounding; the backward replaces torch's atomic index_add / reflection-pad backward with one overlap-add per
+sample, so input gradients agree to fp32 summation-order differences (1e-5 relative to the largest).
+"""
+from __future__ import annotations
+
+import ctypes
+
+import pytest
+import torch
+
+from pymsst_b200 import _native as nat
+
+HOP = 147
+
+
+def _window(win, n_fft, device):
+    w = torch.hann_window(win, device=device)
+    left = (n_fft - win) // 2
+    return torch.nn.functional.pad(w, (left, n_fft - win - left)).contiguous()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("win", [4096, 2048, 1024, 512, 256])
+@pytest.mark.parametrize("length", [131584, 5000, 1025])
+def test_stft_frames_match_torch_stft(cuda_device, win, length):
+    from pymsst_b200.fused import stft_loss_spectrum
+
+    n_fft = max(win, 2048)
+    if n_fft // 2 >= length:
+        pytest.skip("reflect padding needs n_fft / 2 < length")
+    g = torch.Generator().manual_seed(win + length)
+    x = torch.randn(3, length, generator=g).to(cuda_device)
+    t = torch.randn(3, length, generator=g).to(cuda_device)
+    w_small = torch.hann_window(win, device=cuda_device)
+
+    xa = x.clone().requires_grad_()
+    ours = stft_loss_spectrum(xa, n_fft, HOP, _window(win, n_fft, cuda_device), False)
+    ref_x = x.clone().requires_grad_()
+    ref = torch.stft(ref_x, n_fft=n_fft, hop_length=HOP, win_length=win, window=w_small, return_complex=True)
+    assert ours.shape == ref.transpose(1, 2).shape
+    torch.testing.assert_close(ours, ref.transpose(1, 2), rtol=1e-5, atol=1e-4)
+
+    target_ref = torch.stft(t, n_fft=n_fft, hop_length=HOP, win_length=win, window=w_small, return_complex=True)
+    torch.nn.functional.l1_loss(ours, target_ref.transpose(1, 2)).backward()
+    torch.nn.functional.l1_loss(ref, target_ref).backward()
+    err = (xa.grad - ref_x.grad).abs().max() / ref_x.grad.abs().max()
+    assert float(err) < 1e-5, float(err)
+
+
+@pytest.mark.gpu
+def test_stft_frames_backward_is_deterministic(cuda_device):
+    from pymsst_b200.fused import stft_loss_spectrum
+
+    x = torch.randn(2, 20000, device=cuda_device)
+    grads = []
+    for _ in range(2):
+        xa = x.clone().requires_grad_()
+        stft_loss_spectrum(xa, 4096, HOP, _window(4096, 4096, cuda_device), False).abs().sum().backward()
+        grads.append(xa.grad)
+    assert torch.equal(grads[0], grads[1])
+
+
+# ------------------------------------------------------------- host side (CPU)
+def _lib():
+    try:
+        return nat.library()
+    except nat.FusedKernelUnavailable as e:  # pragma: no cover - library not built
+        pytest.skip(str(e))
+
+
+@pytest.mark.parametrize(
+    "length, n_fft, frames, message",
+    [(1000, 2048, 1, "reflect padding"), (10000, 2048, 5, "frame count")],
+)
+def test_stft_frames_backward_rejects_bad_shapes(length, n_fft, frames, message):
+    lib = _lib()
+    st = lib.pmb_stft_frames_backward(None, None, None, 1, length, n_fft, HOP, frames, None)
+    assert st != 0 and message in lib.pmb_last_error().decode()
