@@ -102,7 +102,27 @@ class Trainer:
         params = [p for p in self.model.parameters() if p.requires_grad]
         self.params = params
         on_cuda = self.device.type == "cuda"
-        self.optimizer = torch.optim.Adam(params, lr=lr, fused=fused_adam and on_cuda,
+        self.flat_param = self.flat_grad = None
+        opt_params = params
+        if self.cuda_graph and params and all(p.dtype == torch.float32 for p in params):
+            # one flat fp32 parameter buffer (the parameters become views of it) and one flat gradient buffer:
+            # Adam then updates a single tensor instead of hundreds of small ones, and the all-reduce works
+            # on the flat gradients in place
+            total = sum(p.numel() for p in params)
+            self.flat_param = torch.empty(total, dtype=torch.float32, device=self.device)
+            self.flat_grad = torch.zeros(total, dtype=torch.float32, device=self.device)
+            off = 0
+            self._grad_views = []
+            with torch.no_grad():
+                for p in params:
+                    n = p.numel()
+                    self.flat_param[off:off + n].copy_(p.reshape(-1))
+                    p.data = self.flat_param[off:off + n].view_as(p)
+                    self._grad_views.append(self.flat_grad[off:off + n].view_as(p))
+                    off += n
+            self.flat_param.grad = self.flat_grad
+            opt_params = [self.flat_param]
+        self.optimizer = torch.optim.Adam(opt_params, lr=lr, fused=fused_adam and on_cuda,
                                           capturable=self.cuda_graph)
         self._graph = None
         self._static = None
@@ -116,9 +136,19 @@ class Trainer:
         loss.backward()
         return loss
 
+    def _gather_flat_grads(self):
+        """Per-parameter gradients into the flat gradient buffer (multi-tensor copies); parameters that got
+        no gradient keep zeros there."""
+        pairs = [(v, p.grad) for v, p in zip(self._grad_views, self.params) if p.grad is not None]
+        torch._foreach_copy_([v for v, _ in pairs], [g for _, g in pairs])
+
     def _allreduce_grads(self):
         import torch.distributed as dist
 
+        if self.flat_grad is not None:
+            dist.all_reduce(self.flat_grad)
+            self.flat_grad.div_(dist.get_world_size())
+            return
         grads = [p.grad for p in self.params if p.grad is not None]
         flat = torch.cat([g.reshape(-1) for g in grads])
         dist.all_reduce(flat)
@@ -129,7 +159,10 @@ class Trainer:
 
     def _update(self):
         if self.grad_clip:
-            torch.nn.utils.clip_grad_norm_(self.model.parameters(), self.grad_clip)
+            if self.flat_param is not None:
+                torch.nn.utils.clip_grad_norm_([self.flat_param], self.grad_clip)
+            else:
+                torch.nn.utils.clip_grad_norm_(self.model.parameters(), self.grad_clip)
         self.optimizer.step()
 
     def step(self, mixture: torch.Tensor, target: torch.Tensor) -> torch.Tensor:
@@ -150,13 +183,18 @@ class Trainer:
         side.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(side):
             for _ in range(3):
-                self.optimizer.zero_grad(set_to_none=True)
+                self._zero_grads()
                 self._forward_backward(static_mix, static_tgt)
+                if self.flat_grad is not None:
+                    self._gather_flat_grads()
                 if self.distributed:
                     self._allreduce_grads()
             # Adam state (moments, device step counters) created by an update of zero
-            for p in self.params:
-                p.grad = torch.zeros_like(p)
+            if self.flat_grad is not None:
+                self.flat_grad.zero_()
+            else:
+                for p in self.params:
+                    p.grad = torch.zeros_like(p)
             self.optimizer.step()
             for group in self.optimizer.param_groups:
                 for p in group["params"]:
@@ -164,17 +202,25 @@ class Trainer:
                     if "step" in st:
                         st["step"].zero_()
         torch.cuda.current_stream(self.device).wait_stream(side)
-        self.optimizer.zero_grad(set_to_none=True)
+        self._zero_grads()
         graph = torch.cuda.CUDAGraph()
         before = nat.library().pmb_launch_count()
         with torch.cuda.graph(graph):
             loss = self._forward_backward(static_mix, static_tgt)
+            if self.flat_grad is not None:
+                self._gather_flat_grads()
             if self.distributed:
                 self._allreduce_grads()
             self._update()
         self.launches_per_step = int(nat.library().pmb_launch_count() - before)
         self._graph = graph
         self._static = (static_mix, static_tgt, loss.detach())
+
+    def _zero_grads(self):
+        """Drop the per-parameter gradients (the backward allocates fresh ones); the flat buffer, when there
+        is one, stays attached to the optimizer's single tensor."""
+        for p in self.params:
+            p.grad = None
 
     def _graph_step(self, mixture, target):
         if self._graph is None:
