@@ -515,16 +515,19 @@ PMB_API int pmb_attention_backward(const void* q, const void* k, const void* v, 
                                    float scale, int dtype, void* workspace, int64_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------
- * Backward of the STFT framing of the multi-resolution STFT loss:
- * torch.stft (center=True, reflect padding by n_fft/2) frames x [batch,
- * length] into frames [batch, frames, n_fft] = reflect_pad(x)[f*hop + k] *
- * window[k]; given the frames' gradient (fp32, contiguous) and the window
+ * STFT framing of the multi-resolution STFT loss: torch.stft (center=True,
+ * reflect padding by n_fft/2) frames x [batch, length] into frames [batch,
+ * frames, n_fft] = reflect_pad(x)[f*hop + k] * window[k].  The forward
+ * writes those frames (fp32; window and frames 16-byte aligned, n_fft a
+ * multiple of 4); the backward, given the frames' gradient (fp32, contiguous) and the window
  * (fp32, n_fft values, zero-padded to n_fft as torch.stft pads it), writes
  * grad_x [batch, length] (fp32): one overlap-add per sample, deterministic.
  * frames must equal 1 + (length + 2*(n_fft/2) - n_fft) / hop.  Replaces
  * torch.stft's index_add / reflection-pad backward in pymss-core's
  * multi_stft_resolution_loss (reached from src/pymsst/training/module.py:221-224).
  * ---------------------------------------------------------------------- */
+PMB_API int pmb_stft_frames_forward(const float* x, const float* window, float* frames, int64_t batch,
+                                    int64_t length, int64_t n_fft, int64_t hop, int64_t num_frames, void* stream);
 PMB_API int pmb_stft_frames_backward(const float* grad_frames, const float* window, float* grad_x, int64_t batch,
                                      int64_t length, int64_t n_fft, int64_t hop, int64_t frames, void* stream);
 

@@ -1,4 +1,4 @@
-// Backward of the STFT framing used by the multi-resolution STFT loss.
+// STFT framing of the multi-resolution STFT loss, forward and backward.
 //
 // torch.stft (center=True, reflect padding) frames the signal as
 //   xp = reflect_pad(x, n/2),  frame[f, k] = xp[f*hop + k] * w[k]   (k < n)
@@ -50,10 +50,61 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
+// frames[b, t, k] = reflect_pad(x)[t*hop + k] * w[k] for k in a group of 4
+// (one 16-byte store); groups where the (zero-padded) window is zero are
+// written as zeros without reading x.
+__global__ void __launch_bounds__(kThreads)
+    stft_frames_fwd(const float* __restrict__ x, const float* __restrict__ window, float* __restrict__ frames,
+                    int64_t batch, int64_t L, int n, int hop, int T) {
+  const int64_t pad = n / 2, groups = n / 4, per_b = (int64_t)T * groups;
+  for (int64_t idx = (int64_t)blockIdx.x * kThreads + threadIdx.x; idx < batch * per_b;
+       idx += (int64_t)gridDim.x * kThreads) {
+    const int64_t b = idx / per_b, r = idx - b * per_b, t = r / groups;
+    const int k0 = (int)(r - t * groups) * 4;
+    const float4 w4 = *reinterpret_cast<const float4*>(window + k0);
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (w4.x != 0.f || w4.y != 0.f || w4.z != 0.f || w4.w != 0.f) {
+      const float* xb = x + b * L;
+      float v[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        int64_t j = t * hop + k0 + q - pad;
+        if (j < 0) j = -j;
+        if (j >= L) j = 2 * (L - 1) - j;
+        v[q] = xb[j];
+      }
+      o = make_float4(v[0] * w4.x, v[1] * w4.y, v[2] * w4.z, v[3] * w4.w);
+    }
+    *reinterpret_cast<float4*>(frames + idx * 4) = o;
+  }
+}
+
 }  // namespace
 }  // namespace pmb
 
 using namespace pmb;
+
+extern "C" int pmb_stft_frames_forward(const float* x, const float* window, float* frames, int64_t batch,
+                                       int64_t length, int64_t n_fft, int64_t hop, int64_t num_frames, void* stream) {
+  clear_error();
+  const char* name = "pmb_stft_frames_forward";
+  PMB_REQUIRE(batch >= 0 && length > 0 && n_fft > 0 && hop > 0 && num_frames > 0, "%s: bad shape", name);
+  PMB_REQUIRE(n_fft % 4 == 0, "%s: n_fft must be a multiple of 4", name);
+  PMB_REQUIRE(n_fft / 2 < length, "%s: reflect padding needs n_fft / 2 < length", name);
+  PMB_REQUIRE(num_frames == 1 + (length + 2 * (n_fft / 2) - n_fft) / hop, "%s: frame count does not match", name);
+  PMB_REQUIRE(n_fft < (1 << 30) && num_frames < (1 << 30), "%s: too large", name);
+  if (batch == 0) return PMB_OK;
+  PMB_REQUIRE(x && window && frames, "%s: NULL argument", name);
+  PMB_REQUIRE(((reinterpret_cast<uintptr_t>(window) | reinterpret_cast<uintptr_t>(frames)) & 15) == 0,
+              "%s: window and frames must be 16-byte aligned", name);
+  int64_t g = (batch * num_frames * (n_fft / 4) + kThreads - 1) / kThreads;
+  const int64_t cap = (int64_t)num_sms() * 16;
+  if (g > cap) g = cap;
+  stft_frames_fwd<<<(unsigned)g, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      x, window, frames, batch, length, (int)n_fft, (int)hop, (int)num_frames);
+  PMB_CHECK_LAUNCH(name);
+  return PMB_OK;
+}
 
 extern "C" int pmb_stft_frames_backward(const float* grad_frames, const float* window, float* grad_x, int64_t batch,
                                         int64_t length, int64_t n_fft, int64_t hop, int64_t frames, void* stream) {

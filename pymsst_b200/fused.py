@@ -515,16 +515,19 @@ class AttentionFn(torch.autograd.Function):
 
 class STFTFramesFn(torch.autograd.Function):
     """x [B, L] fp32 -> windowed frames [B, T, n_fft] of the centred, reflect-padded signal, as torch.stft frames
-    it (window: n_fft values, zero-padded as torch.stft pads a shorter window).  The backward is one
-    deterministic overlap-add per sample with the reflection folded in (pmb_stft_frames_backward) instead of
-    torch's atomic index_add and reflection-pad backward."""
+    it (window: n_fft values, zero-padded as torch.stft pads a shorter window).  Forward: one kernel writes the
+    frames (pmb_stft_frames_forward).  Backward: one deterministic overlap-add per sample with the reflection
+    folded in (pmb_stft_frames_backward) instead of torch's atomic index_add and reflection-pad backward."""
 
     @staticmethod
     def forward(ctx, x, window, n_fft, hop):
         device = nat.require_cuda(x, window, name="STFTFrames")
-        pad = n_fft // 2
-        xp = F.pad(x[:, None], (pad, pad), mode="reflect")[:, 0]
-        frames = xp.unfold(-1, n_fft, hop) * window
+        x = x.float().contiguous()
+        b, length = x.shape
+        t = 1 + (length + 2 * (n_fft // 2) - n_fft) // hop
+        frames = torch.empty(b, t, n_fft, dtype=torch.float32, device=device)
+        nat.call("pmb_stft_frames_forward", x.data_ptr(), window.data_ptr(), frames.data_ptr(), b, length, n_fft, hop,
+                 t, nat.stream_handle(device))
         ctx.save_for_backward(window)
         ctx.meta = (x.shape[-1], n_fft, hop, device)
         return frames

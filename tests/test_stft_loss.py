@@ -75,7 +75,8 @@ def _lib():
     "length, n_fft, frames, message",
     [(1000, 2048, 1, "reflect padding"), (10000, 2048, 5, "frame count")],
 )
-def test_stft_frames_backward_rejects_bad_shapes(length, n_fft, frames, message):
+@pytest.mark.parametrize("entry", ["pmb_stft_frames_forward", "pmb_stft_frames_backward"])
+def test_stft_frames_rejects_bad_shapes(entry, length, n_fft, frames, message):
     lib = _lib()
-    st = lib.pmb_stft_frames_backward(None, None, None, 1, length, n_fft, HOP, frames, None)
+    st = getattr(lib, entry)(None, None, None, 1, length, n_fft, HOP, frames, None)
     assert st != 0 and message in lib.pmb_last_error().decode()
