@@ -23,10 +23,10 @@ The per-layer hot path runs through :mod:`pymsst_b200.fused`:
 * mask recombination (scatter-add-average) and complex mask product:
   :class:`~pymsst_b200.fused.BandRecombineFn`.
 
-* attention core softmax(q k^T / sqrt(dh)) v: ``F.scaled_dot_product_attention``
-  (cuDNN / memory-efficient kernels by sequence length) or, with
-  ``set_cuda_attention_backend("pmb")``, :class:`~pymsst_b200.fused.AttentionFn`
-  (tcgen05 kernels; 16-bit, head dim 64).
+* attention core softmax(q k^T / sqrt(dh)) v: :class:`~pymsst_b200.fused.AttentionFn`
+  (tcgen05 kernels; 16-bit, head dim 64) on the band axis, cuDNN's
+  ``F.scaled_dot_product_attention`` on the longer time axis; any backend can
+  be forced with ``set_cuda_attention_backend``.
 
 The feed-forward projections and the attention output projection are cuBLAS
 GEMMs (the feed-forward GELU and bias gradients run on this package's kernels).
@@ -144,15 +144,17 @@ _SHORT_SEQ = 128
 
 # Names accepted by Attention.set_cuda_attention_backend: the reference's
 # cuda_attention_backend choices (src/pymsst/cli.py:61) plus "pmb", this
-# package's tcgen05 attention kernels.  "auto" / "default" take the faster
-# path per shape as measured on B200 for the axial shapes (bf16, 8 heads of
-# 64, fwd + bwd): the library kernels, cuDNN at 258 positions and the
-# memory-efficient kernel at 62, are still ahead of the own kernels there.
+# package's tcgen05 attention kernels.  "auto" / "default" take, per shape,
+# the path measured on B200 for the axial shapes (bf16, 8 heads of 64,
+# fwd + bwd): the own kernels up to _SHORT_SEQ positions (band axis, level
+# with the memory-efficient kernel and deterministic), cuDNN above (time
+# axis, where it is still ahead of the own backward).
 ATTENTION_BACKENDS = ("auto", "default", "pmb", "cudnn", "efficient", "math", "flash")
 
 
 def _attention(q, k, v, dropout_p, backend="auto"):
-    if backend == "pmb" and attention_supported(q, dropout_p):
+    if attention_supported(q, dropout_p) and (
+            backend == "pmb" or (backend in ("auto", "default") and q.shape[-2] <= _SHORT_SEQ)):
         return AttentionFn.apply(q, k, v)
     if q.is_cuda:
         from torch.nn.attention import SDPBackend, sdpa_kernel
