@@ -195,9 +195,10 @@ class Attention(nn.Module):
             raise ValueError(f"unknown cuda attention backend {backend!r}; expected one of {ATTENTION_BACKENDS}")
         self.attention_backend = name
 
-    def forward(self, x, seq_len=None, inner=1):
+    def forward(self, x, seq_len=None, inner=1, residual=None):
         """x [b, n, d]; or any [..., d] whose rows are ordered (outer, position, inner) with sequences of
-        ``seq_len`` positions (sequence = outer * inner + inner index)."""
+        ``seq_len`` positions (sequence = outer * inner + inner index).  With ``residual`` (same shape as x)
+        the block returns residual + attention(x), the addition done by the output projection GEMM."""
         d = x.shape[-1]
         n = x.shape[-2] if seq_len is None else seq_len
         rows = x.numel() // d
@@ -210,8 +211,14 @@ class Attention(nn.Module):
                                     inner)
         attn = _attention(q, k, v, self.dropout if self.training else 0.0, self.attention_backend)
         gated = AttentionGateFn.apply(attn, xn.reshape(rows, d), self.to_gates.weight, self.to_gates.bias, inner)
-        out = F.linear(gated, self.to_out[0].weight.to(gated.dtype))
-        return self.to_out[1](out).reshape(x.shape)
+        w_out = self.to_out[0].weight.to(gated.dtype)
+        drop = self.to_out[1]
+        if residual is not None and (not self.training or drop.p == 0.0):
+            # residual + gated W^T in one GEMM (C = residual, beta = 1)
+            res = residual.reshape(rows, d).to(gated.dtype)
+            return torch.addmm(res, gated, w_out.t()).reshape(x.shape)
+        out = drop(F.linear(gated, w_out)).reshape(x.shape)
+        return out if residual is None else out + residual
 
 
 class FeedForward(nn.Module):
@@ -260,7 +267,7 @@ class Transformer(nn.Module):
     def forward(self, x, seq_len=None, inner=1):
         """x [b, n, d], or rows in (outer, position, inner) order (see Attention.forward)."""
         for attn, ff in self.layers:
-            x = attn(x, seq_len, inner) + x
+            x = attn(x, seq_len, inner, residual=x)
             x = ff(x) + x
         return self.norm(x)
 
