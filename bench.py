@@ -54,6 +54,7 @@ TIMED_ENTRIES = [
     "pmb_mask_estimator_final_forward", "pmb_mask_estimator_final_backward", "pmb_mask_estimator_tc_forward",
     "pmb_mask_estimator_tc_backward", "pmb_gemm_tc", "pmb_qkv_linear_rotary_forward", "pmb_band_split_tc_forward",
     "pmb_band_split_tc_backward", "pmb_gelu_forward", "pmb_gelu_backward", "pmb_column_sum",
+    "pmb_attention_forward", "pmb_attention_backward", "pmb_stft_frames_forward", "pmb_stft_frames_backward",
 ]
 
 
@@ -250,7 +251,7 @@ def run_ours(args, rank: int, world: int, local: int):
     barrier()
     with nat.time_entries(TIMED_ENTRIES) as timer:
         for i in range(args.steps):
-            trainer.optimizer.zero_grad(set_to_none=True)
+            trainer._zero_grads()
             trainer._forward_backward(*dev[i % pool])
         barrier()
 

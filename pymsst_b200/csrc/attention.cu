@@ -8,16 +8,19 @@
 //
 // Three persistent, warp-specialised kernels with the same shape: a work
 // item is 128 rows (queries, or keys for dK/dV) of one (sequence, head); two
-// CTAs per SM take items blockIdx.x, + gridDim.x, ...; 192 threads:
+// CTAs per SM take items blockIdx.x, + gridDim.x, ...:
 //   warp 0   TMA producers: lane 0 loads the item's 128-row tiles, lane 1
-//            streams the 64-row chunks of the other operand through a ring
-//            (4-D plane maps: rows >= N read as zeros);
-//   warp 1   lane 0 issues tcgen05.mma (M 128, N 64, K 16 per instruction,
-//            fp32 accumulators in tensor memory);
-//   warps 2..5  one row per thread (TMEM lane = row): softmax / gradient
+//            streams the chunks of the other operand through a ring (4-D
+//            plane maps: rows >= N read as zeros) -- 64-row chunks in the
+//            forward, 32-row chunks in the backward;
+//   warp 1   lane 0 issues tcgen05.mma (M 128, K 16 per instruction, fp32
+//            accumulators in tensor memory);
+//   row warps  the TMEM lane of a thread is its row: softmax / gradient
 //            arithmetic on the accumulators, the 16-bit P / dS operand rows
 //            written to shared memory in the 128-byte-swizzled K-major
-//            layout the MMA reads, and the item's output rows.
+//            layout the MMA reads, and the item's output rows.  The forward
+//            has 4 row warps (one thread per row); the backward 8 (two
+//            threads per row, half the columns each).
 // Each accumulator product uses the staged tiles as they arrive: a K/V, Q or
 // dO tile serves as a K-major operand in one product and as an MN-major
 // operand (N = head dim) in the other.  Chunks are counted across items, so

@@ -119,6 +119,18 @@ def work(name: str, a: tuple) -> tuple[float, float]:
         if fwd:
             return acts * ES[dt] + params * (ES[pt] + ES[dt]), flops
         return (acts + rows * total) * ES[dt] + 2 * params * ES[pt], 2 * flops
+    if name == "pmb_attention_forward":
+        seqs, n, h, dh, dt = a[5], a[6], a[7], a[8], a[11]
+        plane = seqs * n * h * dh * ES[dt]
+        return 4.0 * plane + 4.0 * seqs * h * n, 4.0 * seqs * h * n * n * dh
+    if name == "pmb_attention_backward":
+        seqs, n, h, dh, dt = a[9], a[10], a[11], a[12], a[15]
+        plane = seqs * n * h * dh * ES[dt]
+        # q, k, v, o, dO read; dQ, dK, dV written; lse read, D written and read back
+        return 8.0 * plane + 12.0 * seqs * h * n, 10.0 * seqs * h * n * n * dh
+    if name in ("pmb_stft_frames_forward", "pmb_stft_frames_backward"):
+        b, length, n_fft, frames = a[3], a[4], a[5], a[7]
+        return 4.0 * (b * length + b * frames * n_fft + n_fft), 1.0 * b * frames * n_fft
     if name == "pmb_gelu_forward":
         return 2.0 * a[2] * ES[a[3]], 0.0
     if name == "pmb_gelu_backward":
