@@ -23,60 +23,70 @@ namespace {
 
 constexpr int kThreads = 256;
 
-__device__ __forceinline__ float frames_sum(const float* __restrict__ g, const float* __restrict__ w, int64_t p,
-                                            int n, int hop, int T) {
-  int64_t f_lo = p - n + 1 > 0 ? (p - n + hop) / hop : 0;  // ceil((p - n + 1) / hop)
-  int64_t f_hi = p / hop;
+// Sum over the frames f with 0 <= p - f*hop < n of g[f][p - f*hop] * w[.],
+// four frames per step with independent accumulators (the loads of a step
+// are in flight together).  p, n, hop and the frame offsets fit in 32 bits.
+__device__ __forceinline__ float frames_sum(const float* __restrict__ g, const float* __restrict__ w, int p, int n,
+                                            int hop, int T) {
+  const int f_lo = p - n + 1 > 0 ? (p - n + hop) / hop : 0;  // ceil((p - n + 1) / hop)
+  int f_hi = p / hop;
   if (f_hi > T - 1) f_hi = T - 1;
-  float acc = 0.f;
-  for (int64_t f = f_lo; f <= f_hi; ++f) {
-    const int k = (int)(p - f * hop);
-    acc = fmaf(g[f * n + k], w[k], acc);
+  float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+  int f = f_lo;
+  for (; f + 3 <= f_hi; f += 4) {
+    const int k0 = p - f * hop;
+    const float g0 = g[f * n + k0], g1 = g[(f + 1) * n + k0 - hop], g2 = g[(f + 2) * n + k0 - 2 * hop],
+                g3 = g[(f + 3) * n + k0 - 3 * hop];
+    a0 = fmaf(g0, w[k0], a0);
+    a1 = fmaf(g1, w[k0 - hop], a1);
+    a2 = fmaf(g2, w[k0 - 2 * hop], a2);
+    a3 = fmaf(g3, w[k0 - 3 * hop], a3);
   }
-  return acc;
+  for (; f <= f_hi; ++f) {
+    const int k = p - f * hop;
+    a0 = fmaf(g[f * n + k], w[k], a0);
+  }
+  return (a0 + a1) + (a2 + a3);
 }
 
+// grid (samples / 256, batch): one thread per input sample
 __global__ void __launch_bounds__(kThreads)
     stft_frames_bwd(const float* __restrict__ grad_frames, const float* __restrict__ window, float* __restrict__ grad_x,
-                    int64_t batch, int64_t L, int n, int hop, int T) {
-  const int64_t pad = n / 2;
-  for (int64_t idx = (int64_t)blockIdx.x * kThreads + threadIdx.x; idx < batch * L; idx += (int64_t)gridDim.x * kThreads) {
-    const int64_t b = idx / L, i = idx - b * L;
-    const float* g = grad_frames + b * (int64_t)T * n;
-    float acc = frames_sum(g, window, i + pad, n, hop, T);
-    if (i >= 1 && i <= pad) acc += frames_sum(g, window, pad - i, n, hop, T);                       // left mirror
-    if (i <= L - 2 && i >= L - 1 - pad) acc += frames_sum(g, window, pad + 2 * (L - 1) - i, n, hop, T);  // right mirror
-    grad_x[idx] = acc;
-  }
+                    int L, int n, int hop, int T) {
+  const int i = blockIdx.x * kThreads + threadIdx.x;
+  if (i >= L) return;
+  const int pad = n / 2;
+  const float* g = grad_frames + (int64_t)blockIdx.y * T * n;
+  float acc = frames_sum(g, window, i + pad, n, hop, T);
+  if (i >= 1 && i <= pad) acc += frames_sum(g, window, pad - i, n, hop, T);                    // left mirror
+  if (i <= L - 2 && i >= L - 1 - pad) acc += frames_sum(g, window, pad + 2 * (L - 1) - i, n, hop, T);  // right mirror
+  grad_x[(int64_t)blockIdx.y * L + i] = acc;
 }
 
-// frames[b, t, k] = reflect_pad(x)[t*hop + k] * w[k] for k in a group of 4
-// (one 16-byte store); groups where the (zero-padded) window is zero are
-// written as zeros without reading x.
+// grid (batch * frames, groups / 256): frames[b, t, k] = reflect_pad(x)[t*hop + k] * w[k] for k in a group
+// of 4 (one 16-byte store); groups where the (zero-padded) window is zero are written as zeros without
+// reading x.
 __global__ void __launch_bounds__(kThreads)
-    stft_frames_fwd(const float* __restrict__ x, const float* __restrict__ window, float* __restrict__ frames,
-                    int64_t batch, int64_t L, int n, int hop, int T) {
-  const int64_t pad = n / 2, groups = n / 4, per_b = (int64_t)T * groups;
-  for (int64_t idx = (int64_t)blockIdx.x * kThreads + threadIdx.x; idx < batch * per_b;
-       idx += (int64_t)gridDim.x * kThreads) {
-    const int64_t b = idx / per_b, r = idx - b * per_b, t = r / groups;
-    const int k0 = (int)(r - t * groups) * 4;
-    const float4 w4 = *reinterpret_cast<const float4*>(window + k0);
-    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (w4.x != 0.f || w4.y != 0.f || w4.z != 0.f || w4.w != 0.f) {
-      const float* xb = x + b * L;
-      float v[4];
+    stft_frames_fwd(const float* __restrict__ x, const float* __restrict__ window, float* __restrict__ frames, int L,
+                    int n, int hop, int T) {
+  const int grp = blockIdx.y * kThreads + threadIdx.x;
+  if (grp >= n / 4) return;
+  const int bt = blockIdx.x, b = bt / T, t = bt - b * T, k0 = grp * 4;
+  const float4 w4 = *reinterpret_cast<const float4*>(window + k0);
+  float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (w4.x != 0.f || w4.y != 0.f || w4.z != 0.f || w4.w != 0.f) {
+    const float* xb = x + (int64_t)b * L;
+    float v[4];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        int64_t j = t * hop + k0 + q - pad;
-        if (j < 0) j = -j;
-        if (j >= L) j = 2 * (L - 1) - j;
-        v[q] = xb[j];
-      }
-      o = make_float4(v[0] * w4.x, v[1] * w4.y, v[2] * w4.z, v[3] * w4.w);
+    for (int q = 0; q < 4; ++q) {
+      int j = t * hop + k0 + q - n / 2;
+      if (j < 0) j = -j;
+      if (j >= L) j = 2 * (L - 1) - j;
+      v[q] = xb[j];
     }
-    *reinterpret_cast<float4*>(frames + idx * 4) = o;
+    o = make_float4(v[0] * w4.x, v[1] * w4.y, v[2] * w4.z, v[3] * w4.w);
   }
+  *reinterpret_cast<float4*>(frames + (int64_t)bt * n + k0) = o;
 }
 
 }  // namespace
@@ -97,11 +107,12 @@ extern "C" int pmb_stft_frames_forward(const float* x, const float* window, floa
   PMB_REQUIRE(x && window && frames, "%s: NULL argument", name);
   PMB_REQUIRE(((reinterpret_cast<uintptr_t>(window) | reinterpret_cast<uintptr_t>(frames)) & 15) == 0,
               "%s: window and frames must be 16-byte aligned", name);
-  int64_t g = (batch * num_frames * (n_fft / 4) + kThreads - 1) / kThreads;
-  const int64_t cap = (int64_t)num_sms() * 16;
-  if (g > cap) g = cap;
-  stft_frames_fwd<<<(unsigned)g, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      x, window, frames, batch, length, (int)n_fft, (int)hop, (int)num_frames);
+  PMB_REQUIRE(batch * num_frames < ((int64_t)1 << 31) && n_fft / 4 <= 65535LL * kThreads && length < (1 << 30) &&
+                  num_frames * n_fft < ((int64_t)1 << 31),
+              "%s: too large", name);
+  const dim3 grid((unsigned)(batch * num_frames), (unsigned)((n_fft / 4 + kThreads - 1) / kThreads));
+  stft_frames_fwd<<<grid, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(x, window, frames, (int)length,
+                                                                            (int)n_fft, (int)hop, (int)num_frames);
   PMB_CHECK_LAUNCH(name);
   return PMB_OK;
 }
@@ -116,11 +127,10 @@ extern "C" int pmb_stft_frames_backward(const float* grad_frames, const float* w
   PMB_REQUIRE(n_fft < (1 << 30) && frames < (1 << 30), "%s: too large", name);
   if (batch == 0) return PMB_OK;
   PMB_REQUIRE(grad_frames && window && grad_x, "%s: NULL argument", name);
-  int64_t g = (batch * length + kThreads - 1) / kThreads;
-  const int64_t cap = (int64_t)num_sms() * 16;
-  if (g > cap) g = cap;
-  stft_frames_bwd<<<(unsigned)g, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      grad_frames, window, grad_x, batch, length, (int)n_fft, (int)hop, (int)frames);
+  PMB_REQUIRE(batch <= 65535 && length < (1 << 30) && frames * n_fft < ((int64_t)1 << 31), "%s: too large", name);
+  const dim3 grid((unsigned)((length + kThreads - 1) / kThreads), (unsigned)batch);
+  stft_frames_bwd<<<grid, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(grad_frames, window, grad_x, (int)length,
+                                                                            (int)n_fft, (int)hop, (int)frames);
   PMB_CHECK_LAUNCH(name);
   return PMB_OK;
 }
