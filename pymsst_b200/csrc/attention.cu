@@ -965,6 +965,562 @@ __global__ void __launch_bounds__(kBwdThreads, 2)
   }
 }
 
+// ------------------------------------------------- forward, short sequences
+// N <= 128: every key of a (sequence, head) fits one 128-column S tile, so
+// the softmax needs no running rescale.  Item = one sequence (N > 64) or two
+// (N <= 64, rows 0-63 and 64-127, the cross-sequence blocks masked), as in
+// the one-pass backward below.  Lane 0 of warp 0 loads Q, K, V (two 64-row
+// boxes each) into a 2-deep stage ring; the MMA lane issues S = Q K^T
+// (N = 128) and, once the row threads have written P over the stage's Q and
+// K tiles (both consumed by S), O = P V (V as the MN-major operand, K = 128
+// keys), then the next item's S; the row threads (one query row each) take
+// the row max and sum, write P, and write O / l and lse.  2 CTAs per SM.
+namespace fs {
+constexpr int kStages = 2;
+constexpr int OFF_K = TILE128, OFF_V = 2 * TILE128;
+constexpr int STAGE = 3 * TILE128;  // Q, K, V; P (two 64-key blocks) later over Q and K
+constexpr int OFF_BAR = kStages * STAGE;
+constexpr int kBars = 2 * kStages + 6;
+constexpr int SMEM = OFF_BAR + 128 + 1024;
+constexpr uint32_t kTmemO = 128;  // S: columns 0-127, O: 128-191
+}  // namespace fs
+
+template <typename T>
+struct IdescF {
+  static constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+  static constexpr uint32_t S = umma::idesc_f16(kBf16, false, false, BM, BM);  // N = 128 queries or keys, B K-major
+  static constexpr uint32_t G = umma::idesc_f16(kBf16, false, true, BM, kD);   // B MN-major, N = head dim
+  static constexpr uint32_t Q = umma::idesc_f16(kBf16, true, true, BM, kD);    // A MN-major as well
+};
+
+template <typename T, bool kPack>
+__global__ void __launch_bounds__(kThreads, 2)
+    attn_fwd_short_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                      const __grid_constant__ CUtensorMap tmV, T* __restrict__ o, float* __restrict__ lse, Plane po,
+                      int sequences, int N, int H, int ldl, int total, float scale) {
+  using namespace fs;
+  constexpr bool pack = kPack;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + kStages;
+  uint64_t* s_full = empty + kStages;
+  uint64_t* s_free = s_full + 1;
+  uint64_t* p_full = s_free + 1;
+  uint64_t* o_full = p_full + 1;
+  uint64_t* o_empty = o_full + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kBars);
+  __shared__ int abort_flag;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      umma::mbar_init(&full[s], 1);
+      umma::mbar_init(&empty[s], 1);
+    }
+    umma::mbar_init(s_full, 1);
+    umma::mbar_init(s_free, 4);
+    umma::mbar_init(p_full, 4);
+    umma::mbar_init(o_full, 1);
+    umma::mbar_init(o_empty, 4);
+    abort_flag = 0;
+    umma::fence_barrier_init();
+  }
+  if (warp == 0) umma::tmem_alloc(tmem_slot, kTmemCols);
+  umma::tc_fence_before();
+  __syncthreads();
+  umma::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      umma::tma_prefetch(&tmQ);
+      umma::tma_prefetch(&tmK);
+      umma::tma_prefetch(&tmV);
+      uint32_t t = 0;
+      for (int item = blockIdx.x; item < total && !abort_flag; item += gridDim.x, ++t) {
+        const int st = t % kStages, p = item / H, h = item - p * H;
+        if (!umma::mbar_wait(&empty[st], ((t / kStages) & 1) ^ 1, 0x81)) {
+          abort_flag = 1;
+          break;
+        }
+        uint8_t* base = smem + st * STAGE;
+        umma::mbar_arrive_expect_tx(&full[st], STAGE);
+#pragma unroll
+        for (int slot = 0; slot < 2; ++slot) {
+          const int seq = pack ? 2 * p + slot : p, pos = pack ? 0 : 64 * slot;  // past the end: zeros
+          const int off = slot * 64 * 128;
+          umma::tma_load_4d(base + off, &tmQ, &full[st], 0, h, pos, seq);
+          umma::tma_load_4d(base + OFF_K + off, &tmK, &full[st], 0, h, pos, seq);
+          umma::tma_load_4d(base + OFF_V + off, &tmV, &full[st], 0, h, pos, seq);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      auto issue_s = [&](uint32_t t) -> bool {
+        const int st = t % kStages;
+        if (!umma::mbar_wait(&full[st], (t / kStages) & 1, 0x82)) return false;
+        if (!umma::mbar_wait(s_free, (t & 1) ^ 1, 0x83)) return false;
+        umma::tc_fence_after();
+        const uint32_t base = umma::smem_u32(smem + st * STAGE);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          umma::mma_f16(tmem, umma::smem_desc_sw128(base + kk * 32, 16, 1024),
+                        umma::smem_desc_sw128(base + OFF_K + kk * 32, 16, 1024), IdescF<T>::S, kk ? 1u : 0u);
+        umma::mma_commit(s_full);
+        return true;
+      };
+      uint32_t t = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < total && !abort_flag; item += gridDim.x, ++t) {
+        if ((t == 0 && !issue_s(0)) || !umma::mbar_wait(p_full, t & 1, 0x84) ||
+            !umma::mbar_wait(o_empty, (t & 1) ^ 1, 0x85)) {
+          ok = false;
+          break;
+        }
+        umma::tc_fence_after();
+        const int st = t % kStages;
+        const uint32_t base = umma::smem_u32(smem + st * STAGE);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)  // K = 128 keys: P block kk / 4 sits over Q (0) or K (1)
+          umma::mma_f16(tmem + kTmemO, umma::smem_desc_sw128(base + (kk >> 2) * TILE128 + (kk & 3) * 32, 16, 1024),
+                        umma::smem_desc_sw128(base + OFF_V + kk * 16 * 128, TILE128, 1024), IdescF<T>::G,
+                        kk ? 1u : 0u);
+        umma::mma_commit(o_full);
+        umma::mma_commit(&empty[st]);
+        if (item + (int)gridDim.x < total && !issue_s(t + 1)) {
+          ok = false;
+          break;
+        }
+      }
+      if (!ok) abort_flag = 1;
+    }
+  } else {
+    const int quarter = warp & 3, row = quarter * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const float sl2 = scale * kLog2e;
+    const int slot = pack ? row >> 6 : 0, pos = pack ? row & 63 : row;
+    uint32_t t = 0;
+    for (int item = blockIdx.x; item < total && !abort_flag; item += gridDim.x, ++t) {
+      const int st = t % kStages, p = item / H, h = item - p * H;
+      const int seq = pack ? 2 * p + slot : p;
+      uint8_t* base = smem + st * STAGE;
+      if (!umma::mbar_wait(s_full, t & 1, 0x86)) {
+        abort_flag = 1;
+        break;
+      }
+      umma::tc_fence_after();
+      float m, l;
+      if constexpr (pack) {
+        // the 64 keys of this row's own sequence; the other block of P is written as zeros
+        uint32_t a[32], b[32];
+        tmem_ld32_nowait(tmem + lane_off + slot * 64, a);
+        tmem_ld32_nowait(tmem + lane_off + slot * 64 + 32, b);
+        tmem_wait2(a, b);
+        warp_arrive(s_free, false);
+        float* s0 = reinterpret_cast<float*>(a);
+        float* s1 = reinterpret_cast<float*>(b);
+        float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          if (c >= N) s0[c] = -INFINITY;  // keys past the end (N >= 1: key 0 always exists)
+          if (32 + c >= N) s1[c] = -INFINITY;
+          mx4[c & 3] = fmaxf(mx4[c & 3], fmaxf(s0[c], s1[c]));
+        }
+        m = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * sl2;  // scale > 0
+        float sum4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          s0[c] = exp2f(fmaf(s0[c], sl2, -m));
+          s1[c] = exp2f(fmaf(s1[c], sl2, -m));
+          sum4[c & 3] += s0[c] + s1[c];
+        }
+        l = (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
+        uint8_t* own = base + slot * TILE128;
+        put_row32<T>(own, row, 0, *reinterpret_cast<float(*)[32]>(s0));
+        put_row32<T>(own, row, 4, *reinterpret_cast<float(*)[32]>(s1));
+        uint8_t* other = base + (1 - slot) * TILE128;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) *reinterpret_cast<uint4*>(other + sw128(row, i)) = make_uint4(0, 0, 0, 0);
+      } else {
+        // 128 keys: the max from a first read of the four 32-column groups, then P from a second read
+        float mx = -INFINITY;
+#pragma unroll 1
+        for (int g = 0; g < 4; ++g) {
+          uint32_t a[32];
+          tmem_ld32_nowait(tmem + lane_off + g * 32, a);
+          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+          tie32(a);
+#pragma unroll
+          for (int c = 0; c < 32; ++c)
+            if (g * 32 + c < N) mx = fmaxf(mx, __uint_as_float(a[c]));
+        }
+        m = mx * sl2;
+        l = 0.f;
+#pragma unroll 1
+        for (int g = 0; g < 4; ++g) {
+          uint32_t a[32];
+          tmem_ld32_nowait(tmem + lane_off + g * 32, a);
+          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+          tie32(a);
+          if (g == 3) warp_arrive(s_free, false);
+          float* pv = reinterpret_cast<float*>(a);
+          float sum4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            pv[c] = g * 32 + c < N ? exp2f(fmaf(pv[c], sl2, -m)) : 0.f;
+            sum4[c & 3] += pv[c];
+          }
+          l += (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
+          put_row32<T>(base + (g >> 1) * TILE128, row, (g & 1) * 4, *reinterpret_cast<float(*)[32]>(pv));
+        }
+      }
+      warp_arrive(p_full, true);
+      if (!umma::mbar_wait(o_full, t & 1, 0x87)) {
+        abort_flag = 1;
+        break;
+      }
+      umma::tc_fence_after();
+      uint32_t oa[32], ob[32];
+      tmem_ld32_nowait(tmem + lane_off + kTmemO, oa);
+      tmem_ld32_nowait(tmem + lane_off + kTmemO + 32, ob);
+      tmem_wait2(oa, ob);
+      warp_arrive(o_empty, false);
+      if (seq < sequences && pos < N) {
+        store_row64<T>(o + seq * po.s_b + h * po.s_h + (int64_t)pos * po.s_n,
+                       *reinterpret_cast<float(*)[32]>(oa), *reinterpret_cast<float(*)[32]>(ob), 1.f / l);
+        lse[((int64_t)seq * H + h) * ldl + pos] = (m + log2f(l)) * kLn2;
+      }
+    }
+  }
+  umma::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    umma::tc_fence_after();
+    umma::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ----------------------------------------------- backward, short sequences
+// N <= 128: one work item holds every key and every query of one head of
+// one sequence -- of two sequences when N <= 64, in rows 0-63 and 64-127, so
+// that the 62-position band-axis sequences fill the 128 TMEM lanes -- and one
+// CTA computes all three gradients in a single pass over the inputs.  Lane 0
+// of warp 0 loads Q, K, V, dO and O (two 64-row boxes each) into a 2-deep
+// stage ring.  The MMA lane issues S^T = K Q^T and dP^T = V dO^T (keys are
+// the TMEM lanes, the 128 queries the columns) and, once the row threads
+// have written P^T and dS^T, dV = P^T dO, dK = dS^T Q and dQ = dS K, then
+// the next item's S^T and dP^T (the TMEM columns are free by then) -- the
+// last reads the dS^T tile as an MN-major A operand, so dS is never
+// transposed.  Row threads: D = rowsum(dO * O) for their query row from the
+// staged tiles (two half-row threads combined through shared memory), P^T
+// and dS^T for their key over half of its queries, then the three output
+// rows of their TMEM lane (dV, dK of a key; dQ of a query).  In a packed
+// pair the cross-sequence blocks of P^T and dS^T are zeroed once and never
+// written again.
+namespace bf {
+constexpr int kStages = 2;
+constexpr int OFF_K = TILE128, OFF_V = 2 * TILE128, OFF_DO = 3 * TILE128, OFF_O = 4 * TILE128;
+constexpr int STAGE = 5 * TILE128;  // Q, K, V, dO, O
+constexpr int kBars = 2 * kStages + 6;
+constexpr uint32_t kTmemDPT = 128, kTmemDV = 256, kTmemDK = 320, kTmemDQ = 384, kCols = 512;
+// P^T and dS^T: 128 keys x 128 queries as two 64-query SW128 blocks, the
+// second kBlk bytes after the first.  In a packed pair rows 64-127 of block 0
+// and rows 0-63 of block 1 are both the zero cross-sequence part, so the
+// blocks overlap there: 24 KB per operand instead of 32, which leaves room
+// for a second D / lse buffer (the next item's D is computed while the
+// current item's gradient products run).
+template <bool kPack>
+struct Layout {
+  static constexpr int kBlk = kPack ? TILE128 / 2 : TILE128;
+  static constexpr int kOp = kBlk + TILE128;
+  static constexpr int OFF_PT = kStages * STAGE;
+  static constexpr int OFF_DST = OFF_PT + kOp;
+  static constexpr int OFF_BAR = OFF_DST + kOp;
+  static constexpr int OFF_X = OFF_BAR + 128;  // per buffer: [2][128] partial D, then [128] lse * log2e
+  static constexpr int kXBufs = kPack ? 2 : 1;
+  static constexpr int kXBytes = 3 * BM * 4;
+  static constexpr int SMEM = OFF_X + kXBufs * kXBytes + 1024;
+  static_assert(SMEM <= 232448 - 64, "fused backward shared memory");
+};
+}  // namespace bf
+
+template <typename T, bool kPack>
+__global__ void __launch_bounds__(kBwdThreads, 1)
+    attn_bwd_fused_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                      const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                      const __grid_constant__ CUtensorMap tmO, const float* __restrict__ lse, T* __restrict__ dq,
+                      T* __restrict__ dk, T* __restrict__ dv, Plane pdq, Plane pdk, Plane pdv, int sequences, int N,
+                      int H, int ldl, int total, float scale) {
+  using namespace bf;
+  using L = Layout<kPack>;
+  constexpr bool pack = kPack;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + kStages;
+  uint64_t* sd_full = empty + kStages;
+  uint64_t* s_free = sd_full + 1;
+  uint64_t* x_full = s_free + 1;
+  uint64_t* ps_full = x_full + 1;
+  uint64_t* acc_full = ps_full + 1;
+  uint64_t* acc_empty = acc_full + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kBars);
+  float* xbuf = reinterpret_cast<float*>(smem + L::OFF_X);
+  __shared__ int abort_flag;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      umma::mbar_init(&full[s], 1);
+      umma::mbar_init(&empty[s], 1);
+    }
+    umma::mbar_init(sd_full, 1);
+    umma::mbar_init(s_free, kRowWarpsBwd);
+    umma::mbar_init(x_full, kRowWarpsBwd);
+    umma::mbar_init(ps_full, kRowWarpsBwd);
+    umma::mbar_init(acc_full, 1);
+    umma::mbar_init(acc_empty, kRowWarpsBwd);
+    abort_flag = 0;
+    umma::fence_barrier_init();
+  }
+  if (warp == 0) umma::tmem_alloc(tmem_slot, kCols);
+  umma::tc_fence_before();
+  __syncthreads();
+  umma::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      umma::tma_prefetch(&tmQ);
+      umma::tma_prefetch(&tmK);
+      umma::tma_prefetch(&tmV);
+      umma::tma_prefetch(&tmDO);
+      umma::tma_prefetch(&tmO);
+      uint32_t t = 0;
+      for (int item = blockIdx.x; item < total && !abort_flag; item += gridDim.x, ++t) {
+        const int st = t % kStages, p = item / H, h = item - p * H;
+        if (!umma::mbar_wait(&empty[st], ((t / kStages) & 1) ^ 1, 0x71)) {
+          abort_flag = 1;
+          break;
+        }
+        uint8_t* base = smem + st * STAGE;
+        umma::mbar_arrive_expect_tx(&full[st], STAGE);
+#pragma unroll
+        for (int slot = 0; slot < 2; ++slot) {
+          // rows 64 * slot.. of the tiles: the slot's sequence (packed) or positions 64.. (one sequence);
+          // a sequence index past the end (odd count, packed) reads zeros
+          const int seq = pack ? 2 * p + slot : p, pos = pack ? 0 : 64 * slot;
+          const int off = slot * 64 * 128;
+          umma::tma_load_4d(base + off, &tmQ, &full[st], 0, h, pos, seq);
+          umma::tma_load_4d(base + OFF_K + off, &tmK, &full[st], 0, h, pos, seq);
+          umma::tma_load_4d(base + OFF_V + off, &tmV, &full[st], 0, h, pos, seq);
+          umma::tma_load_4d(base + OFF_DO + off, &tmDO, &full[st], 0, h, pos, seq);
+          umma::tma_load_4d(base + OFF_O + off, &tmO, &full[st], 0, h, pos, seq);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      auto issue_s = [&](uint32_t t) -> bool {  // S^T, dP^T of the item's t-th stage
+        const int st = t % kStages;
+        if (!umma::mbar_wait(&full[st], (t / kStages) & 1, 0x72)) return false;
+        if (!umma::mbar_wait(s_free, (t & 1) ^ 1, 0x73)) return false;
+        umma::tc_fence_after();
+        const uint32_t base = umma::smem_u32(smem + st * STAGE);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          umma::mma_f16(tmem, umma::smem_desc_sw128(base + OFF_K + kk * 32, 16, 1024),
+                        umma::smem_desc_sw128(base + kk * 32, 16, 1024), IdescF<T>::S, kk ? 1u : 0u);
+          umma::mma_f16(tmem + kTmemDPT, umma::smem_desc_sw128(base + OFF_V + kk * 32, 16, 1024),
+                        umma::smem_desc_sw128(base + OFF_DO + kk * 32, 16, 1024), IdescF<T>::S, kk ? 1u : 0u);
+        }
+        umma::mma_commit(sd_full);
+        return true;
+      };
+      const uint32_t pt = umma::smem_u32(smem + L::OFF_PT), dst = umma::smem_u32(smem + L::OFF_DST);
+      uint32_t t = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < total && !abort_flag; item += gridDim.x, ++t) {
+        if ((t == 0 && !issue_s(0)) || !umma::mbar_wait(ps_full, t & 1, 0x74) ||
+            !umma::mbar_wait(acc_empty, (t & 1) ^ 1, 0x75)) {
+          ok = false;
+          break;
+        }
+        umma::tc_fence_after();
+        const int st = t % kStages;
+        const uint32_t base = umma::smem_u32(smem + st * STAGE);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {  // K = 128 queries (dV, dK) or keys (dQ), 16 per instruction
+          const uint32_t a_k = (kk >> 2) * L::kBlk + (kk & 3) * 32, b_mn = kk * 16 * 128;
+          const uint32_t acc = kk ? 1u : 0u;
+          umma::mma_f16(tmem + kTmemDV, umma::smem_desc_sw128(pt + a_k, 16, 1024),
+                        umma::smem_desc_sw128(base + OFF_DO + b_mn, TILE128, 1024), IdescF<T>::G, acc);
+          umma::mma_f16(tmem + kTmemDK, umma::smem_desc_sw128(dst + a_k, 16, 1024),
+                        umma::smem_desc_sw128(base + b_mn, TILE128, 1024), IdescF<T>::G, acc);
+          // dS^T as the MN-major A operand: its two 64-query blocks are kBlk apart
+          umma::mma_f16(tmem + kTmemDQ, umma::smem_desc_sw128(dst + b_mn, L::kBlk, 1024),
+                        umma::smem_desc_sw128(base + OFF_K + b_mn, TILE128, 1024), IdescF<T>::Q, acc);
+        }
+        umma::mma_commit(acc_full);
+        umma::mma_commit(&empty[st]);
+        // the next item's S^T / dP^T only now: it waits for that item's tiles, the gradients above must not
+        if (item + (int)gridDim.x < total && !issue_s(t + 1)) {
+          ok = false;
+          break;
+        }
+      }
+      if (!ok) abort_flag = 1;
+    }
+  } else {
+    const int quarter = warp & 3, half = (warp - 2) >> 2, row = quarter * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const float sl2 = scale * kLog2e;
+    // Row `row` of every tile: sequence slot and position.  Packed pairs never
+    // write the other sequence's block of P^T / dS^T (the shared zero part of
+    // the two blocks): zero it once.
+    const int slot = pack ? row >> 6 : 0, pos = pack ? row & 63 : row;
+    if (pack) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t off = (1 - slot) * L::kBlk + sw128(row, half * 4 + i);
+        *reinterpret_cast<uint4*>(smem + L::OFF_PT + off) = make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(smem + L::OFF_DST + off) = make_uint4(0, 0, 0, 0);
+      }
+    }
+    // query columns of this thread: packed, 32 of its own sequence's block; otherwise 64 in two passes
+    constexpr int npass = pack ? 1 : 2;
+    const int col0 = pack ? slot * 64 + half * 32 : half * 64;
+    auto seq_of = [&](int64_t item) { return pack ? 2 * (int)(item / H) + slot : (int)(item / H); };
+    // lse of query `row` of an item (half 0 threads), read an item before it is staged
+    auto lse_of = [&](int64_t item) -> float {
+      const int seq = seq_of(item), h = (int)(item % H);
+      return item < total && half == 0 && seq < sequences && pos < N ? lse[((int64_t)seq * H + h) * ldl + pos] : 0.f;
+    };
+    // D partial of query `row` over head elements [32 half, 32 half + 32) and its lse * log2e into buffer xb
+    // (all row warps, then the exchange); returns false on a timeout
+    auto stage_d = [&](uint32_t tt, int64_t item, float lse_v, float* xb) -> bool {
+      const int st = tt % kStages;
+      if (!umma::mbar_wait(&full[st], (tt / kStages) & 1, 0x76)) return false;
+      const uint8_t* base = smem + st * STAGE;
+      float part = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint4 o4 = *reinterpret_cast<const uint4*>(base + OFF_O + sw128(row, half * 4 + i));
+        const uint4 d4 = *reinterpret_cast<const uint4*>(base + OFF_DO + sw128(row, half * 4 + i));
+        const T* oe = reinterpret_cast<const T*>(&o4);
+        const T* de = reinterpret_cast<const T*>(&d4);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) part = fmaf(Elem<T>::to_f(oe[e]), Elem<T>::to_f(de[e]), part);
+      }
+      xb[half * BM + row] = part;
+      if (half == 0) xb[2 * BM + row] = seq_of(item) < sequences && pos < N ? lse_v * kLog2e : 0.f;
+      warp_arrive(x_full, false);
+      return umma::mbar_wait(x_full, tt & 1, 0x77);
+    };
+    float lse_pf = lse_of(blockIdx.x);
+    bool ok = true;
+    if (pack && (int)blockIdx.x < total) {  // packed: D of item t + 1 is staged while item t's products run
+      ok = stage_d(0, blockIdx.x, lse_pf, xbuf);
+      lse_pf = lse_of((int64_t)blockIdx.x + gridDim.x);
+    }
+    uint32_t t = 0;
+    for (int item = blockIdx.x; ok && item < total && !abort_flag; item += gridDim.x, ++t) {
+      const int h = item % H, seq = seq_of(item);
+      const bool valid = seq < sequences && pos < N;  // as a key and as a query
+      float* xb = xbuf + (pack ? (t & 1) : 0) * 3 * BM;
+      if (!pack) {
+        if (!stage_d(t, item, lse_pf, xb)) {
+          ok = false;
+          break;
+        }
+        lse_pf = lse_of((int64_t)item + gridDim.x);
+      }
+      const float* xs = xb;
+      const float* ls = xb + 2 * BM;
+      if (!umma::mbar_wait(sd_full, t & 1, 0x78)) {
+        ok = false;
+        break;
+      }
+      umma::tc_fence_after();
+#pragma unroll
+      for (int ps = 0; ps < npass; ++ps) {
+        const int q0 = col0 + ps * 32;          // first query column of this pass
+        const int qpos0 = pack ? q0 & 63 : q0;  // its position in the sequence
+        uint32_t su[32], du[32];
+        tmem_ld32_nowait(tmem + lane_off + q0, su);
+        tmem_ld32_nowait(tmem + lane_off + kTmemDPT + q0, du);
+        tmem_wait2(su, du);
+        // after the last pass's loads the next item's S^T / dP^T may overwrite these TMEM columns
+        if (ps == npass - 1) warp_arrive(s_free, false);
+        float* pv = reinterpret_cast<float*>(su);   // P^T overwrites S^T in place
+        float* dsv = reinterpret_cast<float*>(du);  // dS^T overwrites dP^T in place
+#pragma unroll
+        for (int c4 = 0; c4 < 8; ++c4) {
+          const float4 l4 = *reinterpret_cast<const float4*>(ls + q0 + 4 * c4);
+          const float4 x0 = *reinterpret_cast<const float4*>(xs + q0 + 4 * c4);
+          const float4 x1 = *reinterpret_cast<const float4*>(xs + BM + q0 + 4 * c4);
+          const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
+          const float dd[4] = {x0.x + x1.x, x0.y + x1.y, x0.z + x1.z, x0.w + x1.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int c = 4 * c4 + e;
+            // the key (this row) and the query must both exist; padding rows give zeros
+            const bool live = valid && qpos0 + c < N;
+            const float pr = live ? exp2f(fmaf(__uint_as_float(su[c]), sl2, -lv[e])) : 0.f;
+            pv[c] = pr;
+            dsv[c] = live ? pr * (__uint_as_float(du[c]) - dd[e]) : 0.f;
+          }
+        }
+        // the previous item's gradient products have completed (its acc_full was waited), so the tiles are free
+        const int blk = (q0 >> 6) * L::kBlk;
+        put_row32<T>(smem + L::OFF_PT + blk, row, (q0 & 63) >> 3, *reinterpret_cast<float(*)[32]>(pv));
+        put_row32<T>(smem + L::OFF_DST + blk, row, (q0 & 63) >> 3, *reinterpret_cast<float(*)[32]>(dsv));
+      }
+      warp_arrive(ps_full, true);
+      if (pack && item + (int64_t)gridDim.x < total) {
+        // every row warp has finished this item's softmax (ps_full waited by the MMA lane before acc_full, and
+        // the other buffer's last readers were item t - 1's): stage the next item's D now
+        if (!stage_d(t + 1, (int64_t)item + gridDim.x, lse_pf, xbuf + ((t + 1) & 1) * 3 * BM)) {
+          ok = false;
+          break;
+        }
+        lse_pf = lse_of((int64_t)item + 2 * (int64_t)gridDim.x);
+      }
+      if (!umma::mbar_wait(acc_full, t & 1, 0x79)) {
+        ok = false;
+        break;
+      }
+      umma::tc_fence_after();
+      uint32_t gv[32], gk[32], gq[32];
+      tmem_ld32_nowait(tmem + lane_off + kTmemDV + half * 32, gv);
+      tmem_ld32_nowait(tmem + lane_off + kTmemDK + half * 32, gk);
+      tmem_ld32_nowait(tmem + lane_off + kTmemDQ + half * 32, gq);
+      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+      tie32(gv);
+      tie32(gk);
+      tie32(gq);
+      warp_arrive(acc_empty, false);
+      if (valid) {
+        const int64_t rv = seq * pdv.s_b + h * pdv.s_h + (int64_t)pos * pdv.s_n + half * 32;
+        const int64_t rk = seq * pdk.s_b + h * pdk.s_h + (int64_t)pos * pdk.s_n + half * 32;
+        const int64_t rq = seq * pdq.s_b + h * pdq.s_h + (int64_t)pos * pdq.s_n + half * 32;
+        store_row32<T>(dv + rv, gv, 1.f);
+        store_row32<T>(dk + rk, gk, scale);
+        store_row32<T>(dq + rq, gq, scale);
+      }
+    }
+    if (!ok) abort_flag = 1;
+  }
+  umma::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    umma::tc_fence_after();
+    umma::tmem_dealloc(tmem, kCols);
+  }
+}
+
 // ------------------------------------------------------------------ host
 bool plane_ok(const void* p, const Plane& pl) {
   return p != nullptr && (reinterpret_cast<uintptr_t>(p) & 15) == 0 && pl.s_b % 8 == 0 && pl.s_n % 8 == 0 &&
@@ -1042,10 +1598,28 @@ extern "C" int pmb_attention_forward(const void* q, const void* k, const void* v
               "%s: q, k, v strides must not overlap (head >= 64, position >= heads * head, sequence >= seq_len * "
               "position)", name);
   CUtensorMap mq, mk, mv;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (N <= BM) {
+    // every key in one S tile; two sequences per item when N <= 64
+    const bool pack = N <= 64;
+    const int64_t items = (pack ? (sequences + 1) / 2 : sequences) * heads;
+    if (int st = plane_map(mq, q, pq, dtype, sequences, N, H, 64, name)) return st;
+    if (int st = plane_map(mk, k, pk, dtype, sequences, N, H, 64, name)) return st;
+    if (int st = plane_map(mv, v, pv, dtype, sequences, N, H, 64, name)) return st;
+    auto run = [&](auto tag) {
+      using T = decltype(tag);
+      auto kernel = pack ? attn_fwd_short_tc<T, true> : attn_fwd_short_tc<T, false>;
+      PMB_CHECK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fs::SMEM), name);
+      kernel<<<grid_for(items), kThreads, fs::SMEM, s>>>(mq, mk, mv, static_cast<T*>(o), lse, po, (int)sequences, N,
+                                                         H, (int)row_pitch(N), (int)items, scale);
+      PMB_CHECK_LAUNCH(name);
+      return PMB_OK;
+    };
+    return dtype == PMB_BFLOAT16 ? run(__nv_bfloat16()) : run(__half());
+  }
   if (int st = plane_map(mq, q, pq, dtype, sequences, N, H, BM, name)) return st;
   if (int st = plane_map(mk, k, pk, dtype, sequences, N, H, BN, name)) return st;
   if (int st = plane_map(mv, v, pv, dtype, sequences, N, H, BN, name)) return st;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   auto run = [&](auto tag) {
     using T = decltype(tag);
     PMB_CHECK_CUDA(cudaFuncSetAttribute(attn_fwd_tc<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, fw::SMEM), name);
@@ -1092,6 +1666,31 @@ extern "C" int pmb_attention_backward(const void* q, const void* k, const void* 
                   plane_order_ok(pv, sequences, N, H) && plane_order_ok(pdo, sequences, N, H),
               "%s: q, k, v, grad_out strides must not overlap (head >= 64, position >= heads * head, sequence >= "
               "seq_len * position)", name);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (N <= BM && plane_order_ok(po, sequences, N, H)) {
+    // one pass: every key and query of a (sequence, head) -- two sequences when N <= 64 -- in one work item
+    const bool pack = N <= 64;
+    const int64_t items = (pack ? (sequences + 1) / 2 : sequences) * heads;
+    CUtensorMap mq, mk, mv, mdo, mo;
+    if (int st = plane_map(mq, q, pq, dtype, sequences, N, H, 64, name)) return st;
+    if (int st = plane_map(mk, k, pk, dtype, sequences, N, H, 64, name)) return st;
+    if (int st = plane_map(mv, v, pv, dtype, sequences, N, H, 64, name)) return st;
+    if (int st = plane_map(mdo, grad_out, pdo, dtype, sequences, N, H, 64, name)) return st;
+    if (int st = plane_map(mo, o, po, dtype, sequences, N, H, 64, name)) return st;
+    const int grid = (int)(items < num_sms() ? items : num_sms());
+    auto run = [&](auto tag) {
+      using T = decltype(tag);
+      auto kernel = pack ? attn_bwd_fused_tc<T, true> : attn_bwd_fused_tc<T, false>;
+      const int smem = pack ? bf::Layout<true>::SMEM : bf::Layout<false>::SMEM;
+      PMB_CHECK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem), name);
+      kernel<<<grid, kBwdThreads, smem, s>>>(mq, mk, mv, mdo, mo, lse, static_cast<T*>(grad_q),
+                                                 static_cast<T*>(grad_k), static_cast<T*>(grad_v), pdq, pdk, pdv,
+                                                 (int)sequences, N, H, (int)ldl, (int)items, scale);
+      PMB_CHECK_LAUNCH(name);
+      return PMB_OK;
+    };
+    return dtype == PMB_BFLOAT16 ? run(__nv_bfloat16()) : run(__half());
+  }
   float* delta = static_cast<float*>(workspace);
   CUtensorMap mq128, mdo128, mk64, mv64, mk128, mv128, mq64, mdo64, ml, md;  // *64: 32-row chunk maps
   if (int st = plane_map(mq128, q, pq, dtype, sequences, N, H, BM, name)) return st;
@@ -1104,7 +1703,6 @@ extern "C" int pmb_attention_backward(const void* q, const void* k, const void* 
   if (int st = plane_map(mdo64, grad_out, pdo, dtype, sequences, N, H, CB, name)) return st;
   if (int st = tma::make_map_rows_f32(ml, lse, ldl, rows, ldl * 4, CB, name)) return st;
   if (int st = tma::make_map_rows_f32(md, delta, ldl, rows, ldl * 4, CB, name)) return st;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int grid = grid_for(total);
   auto run = [&](auto tag) {
     using T = decltype(tag);

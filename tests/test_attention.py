@@ -80,10 +80,11 @@ def test_attention_agrees_with_sdpa(cuda_device, n):
 
 
 @pytest.mark.gpu
-def test_attention_is_deterministic(cuda_device):
+@pytest.mark.parametrize("n", [62, 200])
+def test_attention_is_deterministic(cuda_device, n):
     from pymsst_b200.fused import AttentionFn
 
-    q, k, v = _qkv(2, 200, 4, torch.bfloat16, cuda_device, seed=11)
+    q, k, v = _qkv(3, n, 4, torch.bfloat16, cuda_device, seed=11)
     o1 = AttentionFn.apply(q, k, v)
     o2 = AttentionFn.apply(q, k, v)
     assert torch.equal(o1, o2)
@@ -106,6 +107,25 @@ def test_attention_many_items_per_cta(cuda_device):
     idx = [0, 1, 149, 298, 299]
     od, _ = _ref(*(t.detach()[idx].double() for t in (q, k, v)))
     assert _rel(o[idx], od) < 2e-2
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("n", [62, 100])
+def test_attention_backward_many_items_per_cta(cuda_device, n):
+    """Short sequences take the one-pass backward (every key and query of a head in one item; two sequences per
+    item up to 64 positions): more items than CTAs, an odd sequence count, gradients checked on a sample."""
+    from pymsst_b200.fused import AttentionFn
+
+    q, k, v = _qkv(301, n, 4, torch.bfloat16, cuda_device, seed=17)
+    o = AttentionFn.apply(q, k, v)
+    go = torch.randn(o.shape, generator=torch.Generator().manual_seed(3)).to(o.dtype).to(cuda_device)
+    grads = torch.autograd.grad(o, (q, k, v), go)
+    idx = [0, 1, 150, 299, 300]
+    qd, kd, vd = (t.detach()[idx].double().requires_grad_() for t in (q, k, v))
+    od, _ = _ref(qd, kd, vd)
+    refs = torch.autograd.grad(od, (qd, kd, vd), go[idx].double())
+    for got, want in zip(grads, refs):
+        assert _rel(got[idx], want) < 2e-2, _rel(got[idx], want)
 
 
 @pytest.mark.gpu
