@@ -21,6 +21,58 @@ constexpr int kRowsPerBlock = 128;
 __device__ __forceinline__ float phi_cdf(float v) { return 0.5f * (1.0f + erff(v * 0.70710678118654752f)); }
 __device__ __forceinline__ float phi_pdf(float v) { return 0.39894228040143268f * expf(-0.5f * v * v); }
 
+// 16-bit paths.  Phi(x) = 1 / (1 + 2^(-x H(x^2 / 5.5^2))) with H the degree-9
+// polynomial fitted by pymsst_b200/gelu_fit.py to log2(Phi / (1 - Phi)) / x
+// on [0, 5.5] (uniform relative error of the exponent, so of x Phi(x) on both
+// sides of zero); beyond |x| = 5.5 Phi saturates to 0 / 1, as fp32 erf has
+// already rounded to -1 / 1 there.  Two MUFU operations (ex2.approx,
+// rcp.approx) and 14 FMA-pipe ones per value instead of erff's longer
+// sequence, which made these passes issue-bound.  Over every finite bf16
+// input the rounded GELU equals the exact one (float64) rounded; fp16 differs
+// in 32 of 63488 inputs by one unit in the last place.  fp32 keeps erff.
+__constant__ float kPhiH[10] = {2.302230358e+00f, 3.169386864e+00f, -3.889901191e-02f, -4.928254604e+00f,
+                                1.236330509e+01f, -1.772161293e+01f, 1.614952087e+01f, -9.167760849e+00f,
+                                2.937237978e+00f, -4.014779925e-01f};
+
+__device__ __forceinline__ float ex2_approx(float v) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(v));
+  return r;
+}
+
+__device__ __forceinline__ float rcp_approx(float v) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(v));
+  return r;
+}
+
+__device__ __forceinline__ float phi_cdf_fast(float x) {
+  const float t = x * x;
+  const float s = t * (1.0f / 30.25f);
+  float h = kPhiH[9];
+#pragma unroll
+  for (int i = 8; i >= 0; --i) h = fmaf(h, s, kPhiH[i]);
+  h = t > 30.25f ? 1e4f : h;  // |x| > 5.5: the exponent overflows to +-inf, Phi to 0 / 1
+  return rcp_approx(1.0f + ex2_approx(-x * h));
+}
+
+// phi(x) = exp(-x^2 / 2) / sqrt(2 pi) through ex2.approx
+__device__ __forceinline__ float phi_pdf_fast(float x) {
+  return 0.39894228040143268f * ex2_approx(x * x * -0.72134752044448170f);  // -log2(e) / 2
+}
+
+template <typename T>
+__device__ __forceinline__ float gelu_of(float v) {
+  if constexpr (sizeof(T) == 2) return v * phi_cdf_fast(v);
+  else return v * phi_cdf(v);
+}
+
+template <typename T>
+__device__ __forceinline__ float gelu_grad_of(float v) {
+  if constexpr (sizeof(T) == 2) return phi_cdf_fast(v) + v * phi_pdf_fast(v);
+  else return phi_cdf(v) + v * phi_pdf(v);
+}
+
 template <typename T>
 struct V8 {
   static constexpr int N = 16 / sizeof(T);
@@ -34,16 +86,13 @@ __global__ void __launch_bounds__(256) gelu_fwd_kernel(const T* __restrict__ x, 
     uint4 u = reinterpret_cast<const uint4*>(x)[i];
     T* e = reinterpret_cast<T*>(&u);
 #pragma unroll
-    for (int j = 0; j < N; ++j) {
-      const float v = Elem<T>::to_f(e[j]);
-      e[j] = Elem<T>::from_f(v * phi_cdf(v));
-    }
+    for (int j = 0; j < N; ++j) e[j] = Elem<T>::from_f(gelu_of<T>(Elem<T>::to_f(e[j])));
     reinterpret_cast<uint4*>(y)[i] = u;
   }
   // tail (n not a multiple of the vector width)
   for (int64_t i = nv * N + (int64_t)blockIdx.x * 256 + threadIdx.x; i < n; i += (int64_t)gridDim.x * 256) {
     const float v = Elem<T>::to_f(x[i]);
-    y[i] = Elem<T>::from_f(v * phi_cdf(v));
+    y[i] = Elem<T>::from_f(gelu_of<T>(v));
   }
 }
 
@@ -53,7 +102,7 @@ __global__ void __launch_bounds__(256) gelu_fwd_kernel(const T* __restrict__ x, 
 // column sums of the stored gx.  Requires cols % N == 0 and 16-byte aligned
 // rows (checked by the host).
 template <typename T, int MODE>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, 3)
     rows_pass(const T* __restrict__ gy, const T* __restrict__ x, int64_t rows, int64_t cols, T* __restrict__ gx,
               float* __restrict__ partial) {
   constexpr int N = V8<T>::N;
@@ -66,28 +115,37 @@ __global__ void __launch_bounds__(256)
   for (int j = 0; j < N; ++j) acc[j] = 0.f;
   if (c < cols) {
     const int64_t r1 = r0 + kRowsPerBlock < rows ? r0 + kRowsPerBlock : rows;
-#pragma unroll 2
-    for (int64_t r = r0 + warp; r < r1; r += 8) {
-      const int64_t off = r * cols + c;
-      if (MODE == 0) {
-        const uint4 u = *reinterpret_cast<const uint4*>(x + off);
-        const T* e = reinterpret_cast<const T*>(&u);
+    constexpr int U = 4;  // rows of this warp in flight before any arithmetic
+    for (int64_t rb = r0 + warp; rb < r1; rb += 8 * U) {
+      uint4 ux[U], ug[U];
 #pragma unroll
-        for (int j = 0; j < N; ++j) acc[j] += Elem<T>::to_f(e[j]);
-      } else {
-        const uint4 ug = *reinterpret_cast<const uint4*>(gy + off);
-        const uint4 ux = *reinterpret_cast<const uint4*>(x + off);
-        const T* g = reinterpret_cast<const T*>(&ug);
-        const T* e = reinterpret_cast<const T*>(&ux);
-        uint4 uo;
-        T* o = reinterpret_cast<T*>(&uo);
-#pragma unroll
-        for (int j = 0; j < N; ++j) {
-          const float v = Elem<T>::to_f(e[j]);
-          o[j] = Elem<T>::from_f(Elem<T>::to_f(g[j]) * (phi_cdf(v) + v * phi_pdf(v)));
-          acc[j] += Elem<T>::to_f(o[j]);
+      for (int k = 0; k < U; ++k) {
+        const int64_t r = rb + 8 * k;
+        if (r < r1) {
+          ux[k] = *reinterpret_cast<const uint4*>(x + r * cols + c);
+          if (MODE == 1) ug[k] = *reinterpret_cast<const uint4*>(gy + r * cols + c);
         }
-        *reinterpret_cast<uint4*>(gx + off) = uo;
+      }
+#pragma unroll
+      for (int k = 0; k < U; ++k) {
+        const int64_t r = rb + 8 * k;
+        if (r >= r1) break;
+        const T* e = reinterpret_cast<const T*>(&ux[k]);
+        if (MODE == 0) {
+#pragma unroll
+          for (int j = 0; j < N; ++j) acc[j] += Elem<T>::to_f(e[j]);
+        } else {
+          const T* g = reinterpret_cast<const T*>(&ug[k]);
+          uint4 uo;
+          T* o = reinterpret_cast<T*>(&uo);
+#pragma unroll
+          for (int j = 0; j < N; ++j) {
+            const float v = Elem<T>::to_f(e[j]);
+            o[j] = Elem<T>::from_f(Elem<T>::to_f(g[j]) * gelu_grad_of<T>(v));
+            acc[j] += Elem<T>::to_f(o[j]);
+          }
+          *reinterpret_cast<uint4*>(gx + r * cols + c) = uo;
+        }
       }
     }
   }

@@ -7,6 +7,7 @@ bias gradients (long column sums) within 1e-2 relative.
 """
 from __future__ import annotations
 
+import numpy as np
 import pytest
 import torch
 
@@ -85,3 +86,36 @@ def test_gelu_kernels_match_torch(cuda_device, dtype):
     nat.call("pmb_column_sum", gy.data_ptr(), rows, cols, cs.data_ptr(), 0, nat.dtype_code(dtype), ws.data_ptr(),
              wsb, st)
     torch.testing.assert_close(cs.double(), gy.double().sum(0), rtol=1e-5, atol=1e-4)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_gelu_every_16bit_input(cuda_device, dtype):
+    """Every finite 16-bit value through the 16-bit GELU path (logistic form of the normal CDF, csrc/gelu.cu):
+    forward and derivative within one unit in the last place of torch's erf GELU, equal for almost all."""
+    x = torch.arange(0, 65536, dtype=torch.int32).to(torch.int16).view(dtype)
+    x = x[torch.isfinite(x.float())]
+    x = x[: x.numel() // 8 * 8].reshape(-1, 8).to(cuda_device)
+    rows, cols = x.shape
+    st = nat.stream_handle(cuda_device)
+    ulp = {torch.bfloat16: 2 ** -8, torch.float16: 2 ** -11}[dtype]
+
+    def check(got, want):
+        got, want = got.float(), want.float()
+        diff = (got - want).abs()
+        assert bool((diff <= want.abs() * 2 * ulp + 1e-6).all()), float(diff.max())
+        assert int((diff > 0).sum()) <= 0.01 * want.numel(), int((diff > 0).sum())
+
+    y = torch.empty_like(x)
+    nat.call("pmb_gelu_forward", x.data_ptr(), y.data_ptr(), x.numel(), nat.dtype_code(dtype), st)
+    check(y, torch.nn.functional.gelu(x))
+    xr = x.clone().requires_grad_()
+    gy = torch.ones_like(x)
+    torch.nn.functional.gelu(xr).backward(gy)
+    gx = torch.empty_like(x)
+    wsb = nat.library().pmb_rows_pass_workspace_size(rows, cols)
+    ws = nat.workspace(wsb, cuda_device)
+    nat.call("pmb_gelu_backward", gy.data_ptr(), x.data_ptr(), gx.data_ptr(), rows, cols, None, 0,
+             nat.dtype_code(dtype), ws.data_ptr(), wsb, st)
+    check(gx, xr.grad)
+
