@@ -766,7 +766,217 @@ __global__ void __launch_bounds__(kThreads, 3)
   if (threadIdx.x < H) partial_b[(int64_t)blockIdx.x * H + threadIdx.x] = accb;
 }
 
+// ---------------------------------------------------------------------------
+// Warp-per-row path for the model's own shape (8 heads x 64, 16-bit
+// activations, dim <= 256 in 8-element chunks): one warp owns a whole row;
+// lane l holds elements 16l..16l+15 of the 512-wide attention row (head
+// l / 4) and, for l < dim / 8, the 8-element chunk l of x.  Each lane forms
+// the 8 head dot products over its x chunk (W from shared memory); a
+// transposing butterfly (4 + 2 + 1 + 1 + 1 shuffles) leaves head h's sum in
+// lanes 4h..4h+3 -- the lanes holding that head's attention values -- so the
+// gate needs no broadcast.  The backward reduces the gate gradient over the
+// 4 lanes of a head, broadcasts the 8 values for grad_x, and keeps the
+// W / bias gradient partials in registers across the warp's rows (one fp32
+// partial row per CTA; the warps are combined in shared memory in a fixed
+// order, so results are deterministic).  No block barrier inside the row
+// loop; every global access is a 16-byte vector; the forward issues a row's
+// loads one row ahead.
+constexpr int kWH = 8, kWDh = 64, kWMaxDim = 256;
+
+// Row base in 32-bit arithmetic (callers check rows, inner * seq < 2^31).
+__device__ __forceinline__ int64_t row_base32(const AttnLayout& la, int64_t r) {
+  const uint32_t ur = (uint32_t)r, inner = (uint32_t)la.inner, seq = (uint32_t)la.seq;
+  const uint32_t q = ur / inner, ii = ur - q * inner;
+  const uint32_t o = q / seq, pos = q - o * seq;
+  return (int64_t)(o * inner + ii) * la.s_b + (int64_t)pos * la.s_n;
+}
+
+// d[h] summed over the 32 lanes; lane l receives the sum for head (l >> 2) & 7.
+__device__ __forceinline__ float head_sums(const float (&d)[kWH]) {
+  const int lane = threadIdx.x & 31;
+  const bool b16 = lane & 16, b8 = lane & 8, b4 = lane & 4;
+  float e4[4], e2[2];
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+    e4[k] = (b16 ? d[4 + k] : d[k]) + __shfl_xor_sync(0xffffffffu, b16 ? d[k] : d[4 + k], 16);
+#pragma unroll
+  for (int k = 0; k < 2; ++k)
+    e2[k] = (b8 ? e4[2 + k] : e4[k]) + __shfl_xor_sync(0xffffffffu, b8 ? e4[k] : e4[2 + k], 8);
+  float e = (b4 ? e2[1] : e2[0]) + __shfl_xor_sync(0xffffffffu, b4 ? e2[0] : e2[1], 4);
+  e += __shfl_xor_sync(0xffffffffu, e, 2);
+  e += __shfl_xor_sync(0xffffffffu, e, 1);
+  return e;
+}
+
+// This lane's 8 fp32 gate weights of head h for its x chunk.
+__device__ __forceinline__ void w_chunk(const float* w_s, int dim, int h, int lane, float (&w)[8]) {
+  const float4 u = *reinterpret_cast<const float4*>(w_s + h * dim + 8 * lane);
+  const float4 v = *reinterpret_cast<const float4*>(w_s + h * dim + 8 * lane + 4);
+  w[0] = u.x; w[1] = u.y; w[2] = u.z; w[3] = u.w;
+  w[4] = v.x; w[5] = v.y; w[6] = v.z; w[7] = v.w;
+}
+
+template <typename T, typename TP>
+__global__ void __launch_bounds__(kThreads, 3)
+    gate_fwd_warp(const T* __restrict__ attn, AttnLayout la, const T* __restrict__ x, const TP* __restrict__ W,
+                  const TP* __restrict__ bias, int64_t rows, int dim, T* __restrict__ out, T* __restrict__ gate) {
+  __shared__ __align__(16) float w_s[kWH * kWMaxDim];  // [h][dim]
+  for (int e = threadIdx.x; e < kWH * dim; e += kThreads) w_s[e] = Elem<TP>::to_f(W[e]);
+  __syncthreads();
+  const int lane = threadIdx.x & 31, head = lane >> 2;
+  const bool has_x = lane < (dim >> 3);
+  const float bh = Elem<TP>::to_f(bias[head]);
+  const int64_t step = (int64_t)gridDim.x * kWarps;
+  auto load = [&](int64_t rr, uint4& xv, uint4& a0, uint4& a1) {
+    if (rr < rows) {
+      if (has_x) xv = reinterpret_cast<const uint4*>(x + rr * dim)[lane];
+      const uint4* ap = reinterpret_cast<const uint4*>(attn + row_base32(la, rr)) + 2 * lane;
+      a0 = ap[0];
+      a1 = ap[1];
+    }
+  };
+  int64_t r = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
+  uint4 xv = make_uint4(0, 0, 0, 0), a0 = xv, a1 = xv;
+  load(r, xv, a0, a1);
+  for (; r < rows; r += step) {
+    uint4 nx = make_uint4(0, 0, 0, 0), n0 = nx, n1 = nx;
+    load(r + step, nx, n0, n1);  // the next row's loads go out before this row's arithmetic
+    float d[kWH];
+#pragma unroll
+    for (int h = 0; h < kWH; ++h) d[h] = 0.f;
+    if (has_x) {
+      float xf[8];
+      Vec<T>::unpack(xv, xf);
+#pragma unroll
+      for (int h = 0; h < kWH; ++h) {
+        float w[8];
+        w_chunk(w_s, dim, h, lane, w);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) d[h] = fmaf(xf[j], w[j], d[h]);
+      }
+    }
+    const float g = round_to<T>(sigmoidf_(head_sums(d) + bh));
+    if ((lane & 3) == 0) gate[r * kWH + head] = Elem<T>::from_f(g);
+    float a[8];
+    uint4* op = reinterpret_cast<uint4*>(out + r * (kWH * kWDh)) + 2 * lane;
+    Vec<T>::unpack(a0, a);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) a[j] *= g;
+    op[0] = Vec<T>::pack(a);
+    Vec<T>::unpack(a1, a);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) a[j] *= g;
+    op[1] = Vec<T>::pack(a);
+    xv = nx;
+    a0 = n0;
+    a1 = n1;
+  }
+}
+
+template <typename T, typename TP>
+__global__ void __launch_bounds__(kThreads, 2)
+    gate_bwd_warp(const T* __restrict__ grad_out, const T* __restrict__ attn, AttnLayout la,
+                  const T* __restrict__ x, const TP* __restrict__ W, const T* __restrict__ gate, int64_t rows,
+                  int dim, T* __restrict__ grad_attn, T* __restrict__ grad_x, float* __restrict__ partial_w,
+                  float* __restrict__ partial_b) {
+  extern __shared__ __align__(16) float smem_f[];  // w_s [8][dim], then [kWarps][8][dim] + [kWarps][8] partials
+  float* w_s = smem_f;
+  for (int e = threadIdx.x; e < kWH * dim; e += kThreads) w_s[e] = Elem<TP>::to_f(W[e]);
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, head = lane >> 2;
+  const bool has_x = lane < (dim >> 3);
+  float acc[kWH][8];  // grad_W[h][8 lane + j] over this warp's rows
+#pragma unroll
+  for (int h = 0; h < kWH; ++h)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[h][j] = 0.f;
+  float accb = 0.f;  // grad_b[head] (lanes 4h)
+  for (int64_t r = (int64_t)blockIdx.x * kWarps + warp; r < rows; r += (int64_t)gridDim.x * kWarps) {
+    const int64_t ab = row_base32(la, r);
+    const uint4* gp_in = reinterpret_cast<const uint4*>(grad_out + r * (kWH * kWDh)) + 2 * lane;
+    const uint4* ap = reinterpret_cast<const uint4*>(attn + ab) + 2 * lane;
+    const uint4 go0 = gp_in[0], go1 = gp_in[1], at0 = ap[0], at1 = ap[1];
+    const uint4 xv = has_x ? reinterpret_cast<const uint4*>(x + r * dim)[lane] : make_uint4(0, 0, 0, 0);
+    const float gv = Elem<T>::to_f(gate[r * kWH + head]);
+    // grad_attn = grad_out * gate, and this lane's share of sum_d grad_out * attn
+    float part = 0.f;
+    uint4* gap = reinterpret_cast<uint4*>(grad_attn + ab) + 2 * lane;
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      float go[8], at[8];
+      Vec<T>::unpack(q ? go1 : go0, go);
+      Vec<T>::unpack(q ? at1 : at0, at);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        part = fmaf(go[j], at[j], part);
+        go[j] *= gv;
+      }
+      gap[q] = Vec<T>::pack(go);
+    }
+    part += __shfl_xor_sync(0xffffffffu, part, 1);
+    part += __shfl_xor_sync(0xffffffffu, part, 2);
+    const float gpv = part * gv * (1.0f - gv);  // gate-logit gradient of this lane's head
+    if ((lane & 3) == 0) accb += gpv;
+    float gph[kWH];
+#pragma unroll
+    for (int h = 0; h < kWH; ++h) gph[h] = __shfl_sync(0xffffffffu, gpv, 4 * h);
+    if (has_x) {
+      float xf[8], gx[8];
+      Vec<T>::unpack(xv, xf);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) gx[j] = 0.f;
+#pragma unroll
+      for (int h = 0; h < kWH; ++h) {
+        float w[8];
+        w_chunk(w_s, dim, h, lane, w);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          gx[j] = fmaf(gph[h], w[j], gx[j]);
+          acc[h][j] = fmaf(gph[h], xf[j], acc[h][j]);
+        }
+      }
+      reinterpret_cast<uint4*>(grad_x + r * dim)[lane] = Vec<T>::pack(gx);
+    }
+  }
+  // the CTA's warps combined in warp order: one partial row per CTA
+  float* red_w = smem_f + kWH * dim;
+  float* red_b = red_w + kWarps * kWH * dim;
+  if (has_x) {
+#pragma unroll
+    for (int h = 0; h < kWH; ++h)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) red_w[(warp * kWH + h) * dim + 8 * lane + j] = acc[h][j];
+  }
+  if ((lane & 3) == 0) red_b[warp * kWH + head] = accb;
+  __syncthreads();
+  for (int e = threadIdx.x; e < kWH * dim; e += kThreads) {
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) s += red_w[w * kWH * dim + e];
+    partial_w[(int64_t)blockIdx.x * kWH * dim + e] = s;
+  }
+  if (threadIdx.x < kWH) {
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) s += red_b[w * kWH + threadIdx.x];
+    partial_b[(int64_t)blockIdx.x * kWH + threadIdx.x] = s;
+  }
+}
+
+int warp_bwd_smem(int dim) { return (kWH * dim + kWarps * kWH * dim + kWarps * kWH) * 4; }
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// Whether the warp-per-row kernels apply.
+bool warp_ok(int es, const AttnLayout& la, int64_t rows, int64_t H, int64_t Dh, int64_t dim,
+             std::initializer_list<const void*> ptrs) {
+  if (es != 2 || H != kWH || Dh != kWDh || la.s_h != kWDh || dim % 8 != 0 || dim > kWMaxDim) return false;
+  if (la.s_b % 8 != 0 || la.s_n % 8 != 0) return false;
+  if (rows >= (int64_t)1 << 31 || la.inner * la.seq >= (int64_t)1 << 31) return false;
+  for (const void* p : ptrs)
+    if (!aligned16(p)) return false;
+  return true;
+}
 
 // Whether the tiled kernels apply (vector width V = 16 / element size).
 bool tiled_ok(int es, const AttnLayout& la, int64_t H, int64_t Dh, int64_t dim, std::initializer_list<const void*> ptrs) {
@@ -846,6 +1056,16 @@ extern "C" int pmb_attention_gate_forward(const void* attn, int64_t seq_len, int
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const size_t smem = (size_t)heads * dim * sizeof(float);
   return PMB_DISPATCH_PARAM(dtype, param_dtype, T, TP, name, [&] {
+    if constexpr (sizeof(T) == 2) {
+      if (warp_ok(sizeof(T), la, rows, heads, dim_head, dim, {attn, x, out, gate})) {
+        const int64_t want = (rows + kWarps - 1) / kWarps, cap = (int64_t)num_sms() * 3;
+        gate_fwd_warp<T, TP><<<(int)(want < cap ? want : cap), kThreads, 0, s>>>(
+            static_cast<const T*>(attn), la, static_cast<const T*>(x), static_cast<const TP*>(weight),
+            static_cast<const TP*>(bias), rows, (int)dim, static_cast<T*>(out), static_cast<T*>(gate));
+        PMB_CHECK_LAUNCH(name);
+        return PMB_OK;
+      }
+    }
     if (stream_ok(sizeof(T), la, heads, dim_head, dim, false, {attn, x, out, gate})) {
       const int bsm = StreamLayout((int)heads, (int)dim_head, (int)dim, sizeof(T), false).bytes;
       PMB_CHECK_CUDA(cudaFuncSetAttribute(gate_fwd_stream<T, TP>, cudaFuncAttributeMaxDynamicSharedMemorySize, bsm),
@@ -923,6 +1143,30 @@ extern "C" int pmb_attention_gate_backward(const void* grad_out, const void* att
   AttnLayout la{seq_len, attn_stride_batch, attn_stride_seq, attn_stride_head, seq_inner};
   const size_t smem = (size_t)heads * dim * sizeof(float);
   return PMB_DISPATCH_PARAM(dtype, param_dtype, T, TP, name, [&] {
+    if constexpr (sizeof(T) == 2) {
+      if (warp_ok(sizeof(T), la, rows, heads, dim_head, dim, {grad_out, attn, x, gate, grad_attn, grad_x})) {
+        const int bsm = warp_bwd_smem((int)dim);
+        PMB_CHECK_CUDA(cudaFuncSetAttribute(gate_bwd_warp<T, TP>, cudaFuncAttributeMaxDynamicSharedMemorySize, bsm),
+                       name);
+        const int64_t want = (rows + kWarps - 1) / kWarps, cap = (int64_t)num_sms() * 2;  // <= kMaxTiledBwdBlocks
+        const int grid = (int)(want < cap ? want : cap);
+        float* pw = static_cast<float*>(workspace);
+        float* pb = reinterpret_cast<float*>(static_cast<char*>(workspace) +
+                                             align256((int64_t)kMaxTiledBwdBlocks * heads * dim * 4));
+        gate_bwd_warp<T, TP><<<grid, kThreads, bsm, s>>>(
+            static_cast<const T*>(grad_out), static_cast<const T*>(attn), la, static_cast<const T*>(x),
+            static_cast<const TP*>(weight), static_cast<const T*>(gate), rows, (int)dim, static_cast<T*>(grad_attn),
+            static_cast<T*>(grad_x), pw, pb);
+        PMB_CHECK_LAUNCH(name);
+        red::colsum_rows<<<red::colsum_rows_grid(heads * dim), red::kThreads, 0, s>>>(pw, grid, heads * dim, grad_weight,
+                                                                                 Elem<TP>::code);
+        PMB_CHECK_LAUNCH(name);
+        red::colsum_rows<<<red::colsum_rows_grid(heads), red::kThreads, 0, s>>>(pb, grid, heads, grad_bias,
+                                                                           Elem<TP>::code);
+        PMB_CHECK_LAUNCH(name);
+        return PMB_OK;
+      }
+    }
     if (stream_ok(sizeof(T), la, heads, dim_head, dim, true, {grad_out, attn, x, gate, grad_attn, grad_x})) {
       const int bsm = StreamLayout((int)heads, (int)dim_head, (int)dim, sizeof(T), true).bytes;
       PMB_CHECK_CUDA(cudaFuncSetAttribute(gate_bwd_stream<T, TP>, cudaFuncAttributeMaxDynamicSharedMemorySize, bsm),

@@ -141,14 +141,14 @@ def test_mask_estimator_final(cuda_device, widths, rows, hidden, dtype):
 @pytest.mark.parametrize("layout", ["bhnd", "bnhd"])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize("bsz,heads,seq,dh,dim", [(6, 8, 62, 64, 192), (3, 4, 41, 32, 100), (2, 16, 33, 16, 64),
-                                                  (5, 8, 258, 64, 384)])
+                                                  (5, 8, 258, 64, 384), (7, 8, 62, 64, 256)])
 def test_attention_gate_strided_attention_layout(cuda_device, dtype, bsz, heads, seq, dh, dim, layout):
     """The gate reads the [batch, heads, seq, Dh] attention output in place, stored either as such ("bhnd") or as
     the [batch, seq, heads, Dh] planes the attention kernels write ("bnhd", heads contiguous).
 
-    Shapes cover the streamed kernels (bnhd with 16-byte gate rows: cp.async ring of 8-row tiles, partial last
-    tile), the 32-row tiled kernels (bhnd, and bnhd with 4 heads) and the row-wise fallback (dim 100 is not a
-    multiple of the bf16 vector width)."""
+    Shapes cover the warp-per-row kernels (bnhd, 16-bit, 8 heads x 64, dim <= 256), the streamed kernels (bnhd
+    with dim 384: cp.async ring of 8-row tiles, partial last tile), the 32-row tiled kernels (bhnd, and bnhd with
+    4 heads) and the row-wise fallback (dim 100 is not a multiple of the bf16 vector width)."""
     from pymsst_b200 import _native as nat
 
     rows = bsz * seq
