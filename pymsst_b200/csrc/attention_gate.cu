@@ -780,7 +780,8 @@ __global__ void __launch_bounds__(kThreads, 3)
 // partial row per CTA; the warps are combined in shared memory in a fixed
 // order, so results are deterministic).  No block barrier inside the row
 // loop; every global access is a 16-byte vector; the forward issues a row's
-// loads one row ahead.
+// loads one row ahead (in the backward, whose W-gradient partials take 64
+// registers, the same prefetch measured slower).
 constexpr int kWH = 8, kWDh = 64, kWMaxDim = 256;
 
 // Row base in 32-bit arithmetic (callers check rows, inner * seq < 2^31).
@@ -808,10 +809,28 @@ __device__ __forceinline__ float head_sums(const float (&d)[kWH]) {
   return e;
 }
 
+// Gate weights in shared memory as fp32 float4 slices ordered (head, half, lane): lane l's weights
+// W[h][8l + 4q .. 8l + 4q + 3] are float4 number (2h + q) * 32 + l, so each of a warp's 16-byte loads
+// reads 512 contiguous bytes (no bank conflicts).  kWH * 2 * 32 float4 = 8 KB.
+template <typename TP>
+__device__ __forceinline__ void load_w_lanes(const TP* __restrict__ W, int dim, float4* w4) {
+  for (int e = threadIdx.x; e < kWH * 2 * 32; e += kThreads) {
+    const int l = e & 31, hq = e >> 5, h = hq >> 1, c0 = 8 * l + 4 * (hq & 1);
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (c0 < dim) {
+      v.x = Elem<TP>::to_f(W[h * dim + c0]);
+      v.y = Elem<TP>::to_f(W[h * dim + c0 + 1]);
+      v.z = Elem<TP>::to_f(W[h * dim + c0 + 2]);
+      v.w = Elem<TP>::to_f(W[h * dim + c0 + 3]);
+    }
+    w4[e] = v;
+  }
+}
+
 // This lane's 8 fp32 gate weights of head h for its x chunk.
-__device__ __forceinline__ void w_chunk(const float* w_s, int dim, int h, int lane, float (&w)[8]) {
-  const float4 u = *reinterpret_cast<const float4*>(w_s + h * dim + 8 * lane);
-  const float4 v = *reinterpret_cast<const float4*>(w_s + h * dim + 8 * lane + 4);
+__device__ __forceinline__ void w_chunk(const float4* w4, int h, int lane, float (&w)[8]) {
+  const float4 u = w4[(2 * h) * 32 + lane];
+  const float4 v = w4[(2 * h + 1) * 32 + lane];
   w[0] = u.x; w[1] = u.y; w[2] = u.z; w[3] = u.w;
   w[4] = v.x; w[5] = v.y; w[6] = v.z; w[7] = v.w;
 }
@@ -820,8 +839,8 @@ template <typename T, typename TP>
 __global__ void __launch_bounds__(kThreads, 3)
     gate_fwd_warp(const T* __restrict__ attn, AttnLayout la, const T* __restrict__ x, const TP* __restrict__ W,
                   const TP* __restrict__ bias, int64_t rows, int dim, T* __restrict__ out, T* __restrict__ gate) {
-  __shared__ __align__(16) float w_s[kWH * kWMaxDim];  // [h][dim]
-  for (int e = threadIdx.x; e < kWH * dim; e += kThreads) w_s[e] = Elem<TP>::to_f(W[e]);
+  __shared__ float4 w4[kWH * 2 * 32];
+  load_w_lanes<TP>(W, dim, w4);
   __syncthreads();
   const int lane = threadIdx.x & 31, head = lane >> 2;
   const bool has_x = lane < (dim >> 3);
@@ -850,7 +869,7 @@ __global__ void __launch_bounds__(kThreads, 3)
 #pragma unroll
       for (int h = 0; h < kWH; ++h) {
         float w[8];
-        w_chunk(w_s, dim, h, lane, w);
+        w_chunk(w4, h, lane, w);
 #pragma unroll
         for (int j = 0; j < 8; ++j) d[h] = fmaf(xf[j], w[j], d[h]);
       }
@@ -879,9 +898,9 @@ __global__ void __launch_bounds__(kThreads, 2)
                   const T* __restrict__ x, const TP* __restrict__ W, const T* __restrict__ gate, int64_t rows,
                   int dim, T* __restrict__ grad_attn, T* __restrict__ grad_x, float* __restrict__ partial_w,
                   float* __restrict__ partial_b) {
-  extern __shared__ __align__(16) float smem_f[];  // w_s [8][dim], then [kWarps][8][dim] + [kWarps][8] partials
-  float* w_s = smem_f;
-  for (int e = threadIdx.x; e < kWH * dim; e += kThreads) w_s[e] = Elem<TP>::to_f(W[e]);
+  extern __shared__ __align__(16) float smem_f[];  // w4 (8 KB), then [kWarps][8][dim] + [kWarps][8] partials
+  float4* w4 = reinterpret_cast<float4*>(smem_f);
+  load_w_lanes<TP>(W, dim, w4);
   __syncthreads();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, head = lane >> 2;
   const bool has_x = lane < (dim >> 3);
@@ -928,7 +947,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
       for (int h = 0; h < kWH; ++h) {
         float w[8];
-        w_chunk(w_s, dim, h, lane, w);
+        w_chunk(w4, h, lane, w);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           gx[j] = fmaf(gph[h], w[j], gx[j]);
@@ -939,7 +958,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
   }
   // the CTA's warps combined in warp order: one partial row per CTA
-  float* red_w = smem_f + kWH * dim;
+  float* red_w = smem_f + kWH * 2 * 32 * 4;
   float* red_b = red_w + kWarps * kWH * dim;
   if (has_x) {
 #pragma unroll
@@ -963,7 +982,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
 }
 
-int warp_bwd_smem(int dim) { return (kWH * dim + kWarps * kWH * dim + kWarps * kWH) * 4; }
+int warp_bwd_smem(int dim) { return (kWH * 2 * 32 * 4 + kWarps * kWH * dim + kWarps * kWH) * 4; }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
