@@ -544,11 +544,43 @@ class STFTFramesFn(torch.autograd.Function):
         return gx, None, None, None
 
 
+_INVERSE_NORM = {"backward": "forward", "ortho": "ortho", "forward": "backward"}
+_HALF_BINS: dict = {}
+
+
+class RealFFTFn(torch.autograd.Function):
+    """torch.fft.rfft over the last dimension, with a shorter backward.
+
+    For y_k = sum_n x_n e^(-2 pi i k n / N) over the onesided bins k = 0..N/2 and torch's gradient convention
+    (g = dL/dRe y + i dL/dIm y), dL/dx_n = Re sum_k g_k e^(+2 pi i k n / N).  An inverse real FFT counts every
+    bin strictly between 0 and N/2 twice, so that sum is irfft(h) with those bins of g halved and the
+    normalisation swapped.  torch's own backward instead zero-pads g to all N bins, runs a complex FFT and
+    returns the strided real part (copied again by the framing backward): one multiply and a half-size
+    c2r transform replace a memset, a copy, a full c2c transform and the real-part copy."""
+
+    @staticmethod
+    def forward(ctx, x, norm):
+        ctx.n = x.shape[-1]
+        ctx.norm = norm
+        return torch.fft.rfft(x, dim=-1, norm=norm)
+
+    @staticmethod
+    def backward(ctx, g):
+        n = ctx.n
+        key = (n, g.device)
+        w = _HALF_BINS.get(key)
+        if w is None:
+            w = torch.ones(n // 2 + 1, device=g.device)
+            w[1 : (n - 1) // 2 + 1] = 0.5
+            _HALF_BINS[key] = w
+        return torch.fft.irfft(g * w, n=n, dim=-1, norm=_INVERSE_NORM[ctx.norm]), None
+
+
 def stft_loss_spectrum(x: torch.Tensor, n_fft: int, hop: int, window: torch.Tensor, normalized: bool) -> torch.Tensor:
     """torch.stft(x, n_fft, hop, window=window, center=True, pad_mode="reflect", onesided, return_complex) for
     fp32 CUDA x [B, L], as [B, T, F] (frames first); window already zero-padded to n_fft."""
     frames = STFTFramesFn.apply(x, window, n_fft, hop)
-    return torch.fft.rfft(frames, dim=-1, norm="ortho" if normalized else "backward")
+    return RealFFTFn.apply(frames, "ortho" if normalized else "backward")
 
 
 # -------------------------------------------------------- band index ops

@@ -80,3 +80,19 @@ def test_stft_frames_rejects_bad_shapes(entry, length, n_fft, frames, message):
     lib = _lib()
     st = getattr(lib, entry)(None, None, None, 1, length, n_fft, HOP, frames, None)
     assert st != 0 and message in lib.pmb_last_error().decode()
+
+
+@pytest.mark.parametrize("n", [16, 17, 2048])
+@pytest.mark.parametrize("norm", ["backward", "ortho", "forward"])
+def test_real_fft_backward_matches_torch(n, norm):
+    """RealFFTFn's backward (half-weighted inner bins through an inverse real FFT) equals torch's rfft backward
+    (zero-padded complex FFT) in float64, for even and odd lengths and every normalisation."""
+    from pymsst_b200.fused import RealFFTFn
+
+    g = torch.Generator().manual_seed(n)
+    x = torch.randn(3, 5, n, dtype=torch.float64, generator=g, requires_grad=True)
+    gy = torch.randn(3, 5, n // 2 + 1, dtype=torch.complex128, generator=g)
+    want, = torch.autograd.grad(torch.fft.rfft(x, norm=norm), x, gy)
+    got, = torch.autograd.grad(RealFFTFn.apply(x, norm), x, gy)
+    assert got.is_contiguous()
+    torch.testing.assert_close(got, want, rtol=1e-12, atol=1e-12)
