@@ -73,8 +73,9 @@ def parse():
                    help="launch every kernel from Python each step instead of replaying the captured step graph")
     p.add_argument("--profile-range", action="store_true",
                    help="bracket the timed steps with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
-    p.add_argument("--traffic-json", default=str(REPO / "profiles" / "traffic.json"),
-                   help="per-kernel ncu DRAM bytes per launch (written from an ncu capture)")
+    p.add_argument("--traffic-json", default="",
+                   help="per-kernel ncu DRAM bytes per launch, {config: {entry: bytes}} (default: the measured "
+                        "table in pymsst_b200.roofline)")
     return p.parse_args()
 
 
@@ -262,10 +263,9 @@ def run_ours(args, rank: int, world: int, local: int):
         return
 
     peaks = rl.load_peaks()
-    traffic = {}
-    tpath = Path(args.traffic_json)
-    if tpath.is_file():
-        traffic = json.loads(tpath.read_text()).get(bench.name, {})
+    traffic = rl.MEASURED_TRAFFIC.get(bench.name, {})
+    if args.traffic_json:
+        traffic = json.loads(Path(args.traffic_json).read_text()).get(bench.name, {})
     per_entry = {n: round(ms, 3) for n, (c, ms, _) in sorted(result.items(), key=lambda kv: -kv[1][1]) if c}
     top = max(result.items(), key=lambda kv: kv[1][1])
     name, (calls, total_ms, arglist) = top

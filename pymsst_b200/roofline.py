@@ -140,6 +140,25 @@ def work(name: str, a: tuple) -> tuple[float, float]:
     return 0.0, 0.0
 
 
+# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) of each entry's main kernel, from one
+# `ncu --set full --clock-control none` capture of that kernel on the config-3 shapes
+# (`python -m pymsst_b200.kernel_bench <op> --iters 2 --warmup 1`; the attention entries on the band-axis
+# shape the step runs them on).  Writes that still sit in the 126 MB L2 when a kernel ends are not counted,
+# so traffic can read below the algorithmic bytes; well above them would mean re-reads.
+MEASURED_TRAFFIC = {
+    "config3": {
+        "pmb_qkv_linear_rotary_forward": 168.3e6,
+        "pmb_attention_forward": 235.2e6,
+        "pmb_attention_backward": 483.7e6,
+        "pmb_attention_gate_forward": 118.5e6,
+        "pmb_attention_gate_backward": 216.1e6,
+        "pmb_rms_norm_forward": 26.1e6,
+        "pmb_rms_norm_backward": 50.4e6,
+        "pmb_gelu_forward": 152.6e6,
+    },
+}
+
+
 def roofline(name: str, calls: int, total_ms: float, args_list: list, peaks: dict, traffic=None) -> dict:
     """Achieved rate of the timed calls against the roof that binds this op."""
     byt = sum(work(name, a)[0] for a in args_list)
