@@ -266,6 +266,41 @@ def tensor_core_ok(x: torch.Tensor, *dims: int) -> bool:
 
 
 # ------------------------------------------------------- attention pieces
+def lowp_weight(p: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    """Parameter ``p`` in the activation type ``dtype``: inside the trainer's own forward / backward, its
+    low-precision mirror of the parameters (the same values p.to(dtype) gives, made for all parameters by one
+    copy kernel at the start of that step instead of one cast kernel per weight); anywhere else p.to(dtype).
+    The trainer opens that scope only right after refreshing the mirror, so a mirror older than the
+    parameters is never handed out (a captured optimizer update does not move version counters, so those
+    cannot tell)."""
+    half = getattr(p, "_pmb_half", None)
+    live = getattr(p, "_pmb_half_live", None)
+    if half is not None and live is not None and live[0] and half.dtype == dtype:
+        return half
+    return p.to(dtype)
+
+
+class OutProjFn(torch.autograd.Function):
+    """residual + gated W^T in one GEMM (torch.addmm with the residual as C), W in the activation type; the
+    gradients are those autograd gives through W.to(dtype), with the same products: grad_gated = g W,
+    grad_W = (gated^T g)^T cast to W's type, grad_residual = g."""
+
+    @staticmethod
+    def forward(ctx, res, gated, w):
+        wl = lowp_weight(w, gated.dtype)
+        ctx.w_dtype = w.dtype
+        ctx.save_for_backward(gated, wl)
+        return torch.addmm(res, gated, wl.t())
+
+    @staticmethod
+    def backward(ctx, g):
+        gated, wl = ctx.saved_tensors
+        g_gated = g.mm(wl) if ctx.needs_input_grad[1] else None
+        # the product autograd forms for addmm's second operand (gated^T g), transposed back: same rounding
+        g_w = gated.t().mm(g).t().to(ctx.w_dtype) if ctx.needs_input_grad[2] else None
+        return g, g_gated, g_w
+
+
 class QKVRotaryFn(torch.autograd.Function):
     """xn [b, n, D] -> q, k, v [b, h, n, dh]: projection, split, rotary on q/k.
 
@@ -289,7 +324,7 @@ class QKVRotaryFn(torch.autograd.Function):
         device = nat.require_cuda(xn, weight, name="QKVRotary")
         b, n, d = xn.shape
         dh = weight.shape[0] // (3 * heads)
-        w = weight.to(xn.dtype).contiguous()
+        w = lowp_weight(weight, xn.dtype).contiguous()
         x2 = xn.reshape(b * n, d).contiguous()
         rotate = int(cos is not None)
         if rotate and (tuple(cos.shape) != (n, dh // 2) or tuple(sin.shape) != (n, dh // 2)):
@@ -358,12 +393,12 @@ class FeedForwardFn(torch.autograd.Function):
         device = nat.require_cuda(xn, w1, b1, w2, b2, name="FeedForward")
         dt = xn.dtype
         xn = xn.contiguous()
-        w1c, w2c = w1.to(dt), w2.to(dt)
-        pre = F.linear(xn, w1c, b1.to(dt))
+        w1c, w2c = lowp_weight(w1, dt), lowp_weight(w2, dt)
+        pre = F.linear(xn, w1c, lowp_weight(b1, dt))
         act = torch.empty_like(pre)
         nat.call("pmb_gelu_forward", pre.data_ptr(), act.data_ptr(), pre.numel(), nat.dtype_code(dt),
                  nat.stream_handle(device))
-        out = F.linear(act, w2c, b2.to(dt))
+        out = F.linear(act, w2c, lowp_weight(b2, dt))
         ctx.param_dtypes = (w1.dtype, b1.dtype, w2.dtype, b2.dtype)
         ctx.save_for_backward(xn, pre, act, w1c, w2c)
         return out

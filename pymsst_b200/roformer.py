@@ -49,6 +49,7 @@ from .fused import (
     FeedForwardFn,
     MaskEstimatorFn,
     MaskEstimatorTCFn,
+    OutProjFn,
     QKVRotaryFn,
     RMSNormFn,
     compute_dtype,
@@ -211,13 +212,12 @@ class Attention(nn.Module):
                                     inner)
         attn = _attention(q, k, v, self.dropout if self.training else 0.0, self.attention_backend)
         gated = AttentionGateFn.apply(attn, xn.reshape(rows, d), self.to_gates.weight, self.to_gates.bias, inner)
-        w_out = self.to_out[0].weight.to(gated.dtype)
         drop = self.to_out[1]
         if residual is not None and (not self.training or drop.p == 0.0):
             # residual + gated W^T in one GEMM (C = residual, beta = 1)
             res = residual.reshape(rows, d).to(gated.dtype)
-            return torch.addmm(res, gated, w_out.t()).reshape(x.shape)
-        out = drop(F.linear(gated, w_out)).reshape(x.shape)
+            return OutProjFn.apply(res, gated, self.to_out[0].weight).reshape(x.shape)
+        out = drop(F.linear(gated, self.to_out[0].weight.to(gated.dtype))).reshape(x.shape)
         return out if residual is None else out + residual
 
 

@@ -102,26 +102,40 @@ class Trainer:
         params = [p for p in self.model.parameters() if p.requires_grad]
         self.params = params
         on_cuda = self.device.type == "cuda"
-        self.flat_param = self.flat_grad = None
+        self.flat_param = self.flat_grad = self.flat_half = None
+        self._half_live = [False]  # True only inside _forward_backward, after the mirror's refresh
         opt_params = params
         if self.cuda_graph and params and all(p.dtype == torch.float32 for p in params):
             # one flat fp32 parameter buffer (the parameters become views of it) and one flat gradient buffer:
             # Adam then updates a single tensor instead of hundreds of small ones, and the all-reduce works
             # on the flat gradients in place
-            total = sum(p.numel() for p in params)
-            self.flat_param = torch.empty(total, dtype=torch.float32, device=self.device)
+            # every parameter starts on a 128-element boundary (512 bytes fp32, 256 bytes in the 16-bit
+            # mirror below), as a fresh allocation would: libraries pick their kernels by operand alignment,
+            # and a view at an odd offset would get a different (differently rounded) GEMM than the
+            # per-step cast it replaces.  The padding holds zeros, which Adam leaves at zero.
+            offsets = []
+            total = 0
+            for p in params:
+                offsets.append(total)
+                total += (p.numel() + 127) // 128 * 128
+            self.flat_param = torch.zeros(total, dtype=torch.float32, device=self.device)
             self.flat_grad = torch.zeros(total, dtype=torch.float32, device=self.device)
-            off = 0
             self._grad_views = []
             with torch.no_grad():
-                for p in params:
+                for p, off in zip(params, offsets):
                     n = p.numel()
                     self.flat_param[off:off + n].copy_(p.reshape(-1))
                     p.data = self.flat_param[off:off + n].view_as(p)
                     self._grad_views.append(self.flat_grad[off:off + n].view_as(p))
-                    off += n
             self.flat_param.grad = self.flat_grad
             opt_params = [self.flat_param]
+            if amp_dtype in (torch.bfloat16, torch.float16):
+                # the parameters in the activation type, refreshed by one copy kernel per step (the fused ops
+                # read them through fused.lowp_weight instead of casting each weight with its own kernel)
+                self.flat_half = torch.zeros(total, dtype=amp_dtype, device=self.device)
+                for p, off in zip(params, offsets):
+                    p._pmb_half = self.flat_half[off:off + p.numel()].view_as(p)
+                    p._pmb_half_live = self._half_live
         self.optimizer = torch.optim.Adam(opt_params, lr=lr, fused=fused_adam and on_cuda,
                                           capturable=self.cuda_graph)
         self._graph = None
@@ -130,10 +144,19 @@ class Trainer:
 
     # ------------------------------------------------------------- eager
     def _forward_backward(self, mixture, target):
-        with torch.autocast("cuda", dtype=self.amp_dtype or torch.bfloat16, enabled=self.amp_dtype is not None,
-                            cache_enabled=not self.cuda_graph):
-            loss = self.module(mixture, target)
-        loss.backward()
+        if self.flat_half is not None:
+            # this step's low-precision mirror of the parameters (one kernel), served by fused.lowp_weight
+            # only within this forward / backward
+            with torch.no_grad():
+                self.flat_half.copy_(self.flat_param)
+            self._half_live[0] = True
+        try:
+            with torch.autocast("cuda", dtype=self.amp_dtype or torch.bfloat16, enabled=self.amp_dtype is not None,
+                                cache_enabled=not self.cuda_graph):
+                loss = self.module(mixture, target)
+            loss.backward()
+        finally:
+            self._half_live[0] = False
         return loss
 
     def _gather_flat_grads(self):

@@ -139,3 +139,10 @@ def test_cuda_graph_trainer_matches_eager(cuda_device):
     assert graph.launches_per_step and graph.launches_per_step > 0
     for (name, a), b in zip(ours.named_parameters(), twin.parameters()):
         torch.testing.assert_close(a, b, rtol=2e-2, atol=1e-4, msg=lambda m: f"{name}: {m}")
+    # the graph trainer's low-precision parameter mirror (refreshed inside the captured step) is never handed
+    # out stale: after the updates every parameter reads as its own fresh cast
+    from pymsst_b200.fused import lowp_weight
+
+    assert graph.flat_half is not None
+    for name, p in twin.named_parameters():
+        assert torch.equal(lowp_weight(p, torch.bfloat16), p.detach().to(torch.bfloat16)), name
