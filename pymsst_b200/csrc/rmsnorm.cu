@@ -34,19 +34,6 @@ __device__ __forceinline__ float ld_dyn(const void* p, int64_t i, int code) {
   }
 }
 
-__device__ __forceinline__ void st_dyn(void* p, int64_t i, int code, float v) {
-  switch (code) {
-    case PMB_FLOAT16:
-      static_cast<__half*>(p)[i] = __float2half_rn(v);
-      break;
-    case PMB_BFLOAT16:
-      static_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
-      break;
-    default:
-      static_cast<float*>(p)[i] = v;
-  }
-}
-
 template <typename T, int V>
 struct alignas((sizeof(T) * V) < 16 ? (sizeof(T) * V) : 16) Pack {
   T v[V];
