@@ -1,6 +1,8 @@
 """Per-kernel timings of the C-ABI entry points at the config-3 shapes.
 
-``python -m pymsst_b200.kernel_bench [op ...] [--iters N] [--json PATH]``
+``python -m pymsst_b200.kernel_bench [op ...] [--iters N] [--json PATH]``;
+``--sweep`` runs the config-2 kernel sweep instead (isolated kernels up to
+tensors well beyond L2, bf16 and fp32: ``sweep_cases``).
 
 Each op is one entry-point call on synthetic device tensors with the shapes a
 config-3 training step uses (BS-RoFormer dim 192, 8 heads of 64, batch 4 x
@@ -264,13 +266,18 @@ def op_attn(bench: _Bench):
 
 def op_band(bench: _Bench):
     """BandSplit (config-3 bands: 62 bands over 1025 stereo complex bins, 1032 rows, D = 192)."""
+    _op_band_rows(bench, 1032)
+
+
+def _op_band_rows(bench: _Bench, rows: int):
     import ctypes
 
     from .bands import DEFAULT_FREQS_PER_BANDS
 
     dev, bf = bench.device, torch.bfloat16
     widths = [4 * f for f in DEFAULT_FREQS_PER_BANDS]
-    nb, total, rows, D = len(widths), sum(widths), 1032, DIM
+    nb, total, D = len(widths), sum(widths), DIM
+    sfx = "" if rows == 1032 else f" [{rows} rows]"
     x = torch.randn(rows, total, device=dev, dtype=bf)
     gam = [torch.ones(w, device=dev) for w in widths]
     wts = [torch.randn(D, w, device=dev) / w ** 0.5 for w in widths]
@@ -286,11 +293,11 @@ def op_band(bench: _Bench):
     pg, pw, pb = nat.ptr_array(gam), nat.ptr_array(wts), nat.ptr_array(bss)
     flops = 2.0 * rows * total * D
     byt = rows * total * 2 * 2 + total * D * 4 + rows * nb * D * 2
-    bench.time("band_split_tc_forward", lambda: nat.call(
+    bench.time("band_split_tc_forward" + sfx, lambda: nat.call(
         "pmb_band_split_tc_forward", x.data_ptr(), rows, total, -1, 1, nb, warr, pg, pw, pb, D, packed.data_ptr(),
         normed_p.data_ptr(), inv.data_ptr(), out.data_ptr(), 2, 0, st), byt, flops)
     normed = torch.empty_like(x)
-    bench.time("band_split_forward (SIMT)", lambda: nat.call(
+    bench.time("band_split_forward (SIMT)" + sfx, lambda: nat.call(
         "pmb_band_split_forward", x.data_ptr(), rows, total, -1, 1, nb, warr, pg, pw, pb, D, out.data_ptr(),
         normed.data_ptr(), inv.data_ptr(), 2, 0, st), byt, flops)
     gy = torch.randn(rows, nb, D, device=dev, dtype=bf)
@@ -299,39 +306,44 @@ def op_band(bench: _Bench):
     gb = [torch.empty_like(b) for b in bss]
     ws = nat.workspace(sizes[2], dev)
     bbyt = rows * nb * D * 2 + rows * total * 2 + total * D * 4 * 2
-    bench.time("band_split_tc_backward", lambda: nat.call(
+    bench.time("band_split_tc_backward" + sfx, lambda: nat.call(
         "pmb_band_split_tc_backward", gy.data_ptr(), normed_p.data_ptr(), rows, nb, warr, pg, pw, D,
         nat.ptr_array(gg), nat.ptr_array(gw), nat.ptr_array(gb), 2, 0, ws.data_ptr(), sizes[2], st), bbyt, flops)
     swsb = nat.library().pmb_band_split_backward_workspace_size(rows, nb, warr, D, 0)
     sws = nat.workspace(swsb, dev)
-    bench.time("band_split_backward (SIMT)", lambda: nat.call(
+    bench.time("band_split_backward (SIMT)" + sfx, lambda: nat.call(
         "pmb_band_split_backward", gy.data_ptr(), normed.data_ptr(), inv.data_ptr(), rows, nb, warr, pg, pw, D, None,
         nat.ptr_array(gg), nat.ptr_array(gw), nat.ptr_array(gb), 2, 0, sws.data_ptr(), swsb, st), bbyt, flops)
 
 
 def op_mel(bench: _Bench):
     """Mel-band gather / scatter-add-average recombine (60 overlapping mel bands, stereo, batch 4 x 258 frames)."""
+    _op_mel_shape(bench, 4, 258)
+
+
+def _op_mel_shape(bench: _Bench, b: int, t: int):
     from . import bands
     from . import extension as ext
 
     dev = bench.device
     index = bands.mel_band_index(44100, 2048, 60, channels=2)
     tables = index.device_tables(dev)
-    b, t, f = 4, 258, 1025
+    f = 1025
+    sfx = "" if (b, t) == (4, 258) else f" [{b}x2, {f}, {t}]"
     j = int(tables["index"].numel())
     stft = torch.randn(b, 2, f, t, 2, device=dev)
     x = ext.band_gather(stft, tables, torch.bfloat16)
-    bench.time("band_gather_forward", lambda: ext.band_gather(stft, tables, torch.bfloat16),
+    bench.time("band_gather_forward" + sfx, lambda: ext.band_gather(stft, tables, torch.bfloat16),
                b * t * j * 2 * (4 + 2) + 4 * j)
     gx = torch.randn_like(x)
-    bench.time("band_gather_backward", lambda: ext.band_gather_backward(gx, tables, 2, f),
+    bench.time("band_gather_backward" + sfx, lambda: ext.band_gather_backward(gx, tables, 2, f),
                b * t * j * 2 * 2 + b * 2 * f * t * 2 * 4)
     mask = torch.randn(b, 1, t, j * 2, device=dev, dtype=torch.bfloat16)
     out = ext.band_recombine(mask, stft, tables, 2, f)
-    bench.time("band_recombine_forward", lambda: ext.band_recombine(mask, stft, tables, 2, f),
+    bench.time("band_recombine_forward" + sfx, lambda: ext.band_recombine(mask, stft, tables, 2, f),
                b * t * j * 2 * 2 + 2 * b * 2 * f * t * 8)
     go = torch.randn_like(out)
-    bench.time("band_recombine_backward",
+    bench.time("band_recombine_backward" + sfx,
                lambda: ext.band_recombine_backward(go, stft, tables, torch.bfloat16),
                2 * b * 2 * f * t * 8 + b * t * j * 2 * 2)
 
@@ -371,6 +383,80 @@ def op_mask(bench: _Bench):
 OPS = {"gate": op_gate, "band": op_band, "mel": op_mel, "mask": op_mask, "rms": op_rms, "qkv": op_qkv, "ff": op_ff, "sdpa": op_sdpa, "attn": op_attn}
 
 
+# ---------------------------------------------------------------------------
+# Config-2 sweep: the hot kernels in isolation, up to tensors well beyond the 126 MB
+# L2 (which is flushed between timed calls in any case), random normal inputs (seed 0), bf16 and fp32 where the
+# kernel takes both.
+def sweep_cases() -> list[tuple[str, dict]]:
+    """(op, shape) cases of the sweep, in run order; pure host logic (tests check it without a GPU)."""
+    cases = []
+    for dtype in ("bf16", "fp32"):
+        for dim in (192, 384):
+            for bf, t in ((62, 1024), (496, 1024)):  # B·F rows of T frames: one and eight batch items of 62 bands
+                cases.append(("rms", {"dtype": dtype, "rows": bf * t, "dim": dim}))
+    for dtype in ("bf16", "fp32"):
+        for n, b in ((62, 2048), (1024, 128)):  # [B, N, 8, 64]: 2048 x 62 and 128 x 1024 positions
+            cases.append(("rotary", {"dtype": dtype, "batch": b, "seq": n, "heads": 8, "dim": 64}))
+    cases.append(("band", {"rows": 8 * 1024}))  # ragged BandSplit, 62 bands -> 192, M = 8 x 1024 rows
+    cases.append(("mel", {"batch": 4, "frames": 1024}))  # [8 = 4 x stereo, 1025, 1024] complex
+    return cases
+
+
+_TORCH_DT = {"bf16": torch.bfloat16, "fp32": torch.float32}
+
+
+def _sweep_rms(bench: _Bench, dtype: str, rows: int, dim: int):
+    dev, dt = bench.device, _TORCH_DT[dtype]
+    code, es = nat.dtype_code(dt), torch.tensor([], dtype=dt).element_size()
+    x = torch.randn(rows, dim, device=dev, dtype=dt)
+    g = torch.ones(dim, device=dev, dtype=dt)
+    out, normed = torch.empty_like(x), torch.empty_like(x)
+    inv = torch.empty(rows, device=dev)
+    st = nat.stream_handle(dev)
+    tag = f"{dtype} [{rows}, {dim}]"
+    bench.time(f"rms fwd {tag}", lambda: nat.call(
+        "pmb_rms_norm_forward", x.data_ptr(), g.data_ptr(), out.data_ptr(), normed.data_ptr(), inv.data_ptr(), rows,
+        dim, code, code, code, st), rows * dim * es * 3 + rows * 4)
+    dy = torch.randn_like(x)
+    gx, gg = torch.empty_like(x), torch.empty_like(g)
+    wsb = nat.library().pmb_rms_norm_backward_workspace_size(rows, dim)
+    ws = nat.workspace(wsb, dev)
+    bench.time(f"rms bwd {tag}", lambda: nat.call(
+        "pmb_rms_norm_backward", dy.data_ptr(), x.data_ptr(), 1, inv.data_ptr(), g.data_ptr(), gx.data_ptr(),
+        gg.data_ptr(), rows, dim, code, code, code, code, ws.data_ptr(), wsb, st), rows * dim * es * 3 + rows * 4)
+
+
+def _sweep_rotary(bench: _Bench, dtype: str, batch: int, seq: int, heads: int, dim: int):
+    dev, dt = bench.device, _TORCH_DT[dtype]
+    code, es = nat.dtype_code(dt), torch.tensor([], dtype=dt).element_size()
+    t = torch.randn(batch, seq, heads, dim, device=dev, dtype=dt)
+    cos = torch.randn(seq, dim // 2, device=dev, dtype=dt)
+    sin = torch.randn(seq, dim // 2, device=dev, dtype=dt)
+    out = torch.empty_like(t)
+    st = nat.stream_handle(dev)
+    byt = 2 * t.numel() * es + 2 * seq * (dim // 2) * es
+    tag = f"{dtype} [{batch}, {seq}, {heads}, {dim}]"
+    bench.time(f"rotary fwd {tag}", lambda: nat.call(
+        "pmb_rotary_forward", t.data_ptr(), cos.data_ptr(), sin.data_ptr(), out.data_ptr(), batch, seq, heads, dim,
+        code, st), byt)
+    bench.time(f"rotary bwd {tag}", lambda: nat.call(
+        "pmb_rotary_backward", out.data_ptr(), cos.data_ptr(), sin.data_ptr(), t.data_ptr(), batch, seq, heads, dim,
+        code, st), byt)
+
+
+def run_sweep(bench: _Bench) -> None:
+    torch.manual_seed(0)
+    for op, shape in sweep_cases():
+        if op == "rms":
+            _sweep_rms(bench, **shape)
+        elif op == "rotary":
+            _sweep_rotary(bench, **shape)
+        elif op == "band":
+            _op_band_rows(bench, shape["rows"])
+        elif op == "mel":
+            _op_mel_shape(bench, shape["batch"], shape["frames"])
+
+
 def main(argv=None) -> None:
     p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     p.add_argument("ops", nargs="*", help=f"ops to run (default all): {', '.join(OPS)}")
@@ -378,10 +464,15 @@ def main(argv=None) -> None:
     p.add_argument("--warmup", type=int, default=3, help="untimed calls per op before timing (0 with --iters 1 "
                    "launches each kernel once, for profiler captures)")
     p.add_argument("--json", default=None)
+    p.add_argument("--sweep", action="store_true",
+                   help="run the config-2 kernel sweep (RMSNorm, rotary, BandSplit, mel at sizes beyond L2) "
+                        "instead of the config-3 ops")
     args = p.parse_args(argv)
     device = torch.device("cuda", torch.cuda.current_device())
     bench = _Bench(device, max(args.iters, 1), args.warmup)
-    for name in args.ops or list(OPS):
+    if args.sweep:
+        run_sweep(bench)
+    for name in ([] if args.sweep else args.ops or list(OPS)):
         if name not in OPS:
             raise SystemExit(f"unknown op {name!r}; choose from {', '.join(OPS)}")
         OPS[name](bench)
