@@ -6,9 +6,13 @@
 //   backward:  D = rowsum(dO * O),  dP = dO V^T,  dS = P * (dP - D),
 //              dV = P^T dO,  dQ = scale * dS K,  dK = scale * dS^T Q
 //
-// Three persistent, warp-specialised kernels with the same shape: a work
-// item is 128 rows (queries, or keys for dK/dV) of one (sequence, head); two
-// CTAs per SM take items blockIdx.x, + gridDim.x, ...:
+// Sequences of up to 128 positions (the band axis) take two single-tile
+// kernels, described at "forward, short sequences" / "backward, short
+// sequences" below: every key of an item fits one 128 x 128 S tile (two
+// sequences per item when N <= 64), the backward is one pass for dQ, dK and
+// dV.  Longer sequences take three persistent, warp-specialised kernels with
+// the same shape: a work item is 128 rows (queries, or keys for dK/dV) of one
+// (sequence, head); two CTAs per SM take items blockIdx.x, + gridDim.x, ...:
 //   warp 0   TMA producers: lane 0 loads the item's 128-row tiles, lane 1
 //            streams the chunks of the other operand through a ring (4-D
 //            plane maps: rows >= N read as zeros) -- 64-row chunks in the
