@@ -3,8 +3,9 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config config3] [--impl ours|reference]
 
 N > 1 runs under ``torch.distributed.run`` (one rank per GPU, NCCL); every rank
-trains on its own seeded synthetic batch (weak scaling) and gradients are
-all-reduced by DDP.  Rank 0 prints one JSON line:
+trains on its own seeded synthetic batch (weak scaling) and the captured step
+all-reduces the flat gradient buffer over NCCL (mean over ranks).  Rank 0
+prints one JSON line:
 
 * ``value``: whole-job audio-seconds/s with inputs resident in HBM (device
   time of K steps, CUDA events, max over ranks);
@@ -13,13 +14,15 @@ all-reduced by DDP.  Rank 0 prints one JSON line:
   the timed region);
 * ``roofline``: the dominant fused op of this package, timed with CUDA events
   around its calls during the timed steps, against the measured peaks;
-* ``cpu_baseline``: the CPU oracle (the reference semantics in PyTorch) on a
-  bounded sample of the same workload, on this machine's host cores;
+* ``cpu_baseline``: the CPU oracle (the reference semantics in PyTorch, fp32)
+  on a bounded sample of the same workload (the benchmark's batch, five timed
+  steps), on this machine's host cores;
 * ``clocks``: nvidia-smi samples taken during the timed region.
 
 ``--impl reference`` times the reference's CPU implementation of the path
 (the oracle port: the reference's CUDA extension has no model, and its model
-package pymss-core is not installed) on a bounded sample per step, rank 0 only.
+package pymss-core is not installed) at the benchmark's per-GPU batch, K
+timed steps, rank 0 only.
 """
 from __future__ import annotations
 
@@ -67,8 +70,12 @@ def parse():
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--bucket-mb", type=float, default=1024.0,
-                   help="DDP gradient bucket size (MB); the default puts all gradients in one bucket reduced after "
-                        "the backward, which keeps NCCL off the SMs while the persistent kernels run")
+                   help="gradient all-reduce bucket size (MB) of --overlap-allreduce and of the eager DDP path; the "
+                        "default puts all gradients in one bucket reduced after the backward, which keeps NCCL off "
+                        "the SMs while the persistent kernels run")
+    p.add_argument("--overlap-allreduce", action="store_true",
+                   help="N > 1: all-reduce the flat gradients in buckets launched from gradient hooks during the "
+                        "backward (bucket size --bucket-mb) instead of once after it")
     p.add_argument("--eager", action="store_true",
                    help="launch every kernel from Python each step instead of replaying the captured step graph")
     p.add_argument("--profile-range", action="store_true",
@@ -174,15 +181,25 @@ def cpu_oracle_rate(bench, steps: int, warmup: int, batch: int = 1) -> dict:
                       f"median of {steps} steps after {warmup} warm-up ({per_step:.2f} s/step); CPU {cpu_name}"}
 
 
+def bench_config(bench, world: int) -> dict:
+    """The ``config`` object of both arms' JSON lines."""
+    return {"workload": bench.name, "model": bench.model_type, "global_batch": bench.batch * world,
+            "per_gpu_batch": bench.batch, "chunk_samples": bench.chunk, "frames": bench.frames,
+            "parallelism": f"dp{world}", "note": bench.notes,
+            "l2": "no flush: a step's activations (several GB) exceed the 126 MB L2"}
+
+
 def run_reference(args, rank: int, world: int):
+    """The reference's CPU path of the step (fused backend off: fp32 PyTorch) on this box's host cores, at the
+    benchmark's own per-GPU batch; rank 0 only (one CPU sample stands for the job)."""
     if rank != 0:
         return
     bench = CONFIGS[args.config]
-    base = cpu_oracle_rate(bench, steps=max(1, args.steps), warmup=max(0, args.warmup))
+    base = cpu_oracle_rate(bench, steps=max(1, args.steps), warmup=min(max(0, args.warmup), 3), batch=bench.batch)
     line = {
         "impl": "reference", "metric": METRIC, "value": base["value"], "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "f32", "data": "synthetic", "config": {"workload": bench.name, "note": bench.notes},
+        "dtype": "f32", "data": "synthetic", "config": bench_config(bench, 1),
         "cpu_baseline": base,
         "e2e": {"value": base["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -197,7 +214,8 @@ def run_ours(args, rank: int, world: int, local: int):
     torch.backends.cudnn.allow_tf32 = False
     model = build_model(bench, seed=0)
     trainer = Trainer(model, lr=bench.lr, amp_dtype=bench.amp, distributed=world > 1, device=device,
-                      bucket_cap_mb=args.bucket_mb, cuda_graph=not args.eager)
+                      bucket_cap_mb=args.bucket_mb, cuda_graph=not args.eager,
+                      overlap_allreduce=args.overlap_allreduce)
     pool = 2
     host = [synthetic.make_batch(bench.batch, bench.chunk, seed=1000 * rank + i, stems=bench.stems) for i in range(pool)]
     host = [(m.pin_memory(), t.pin_memory()) for m, t in host]
@@ -247,18 +265,35 @@ def run_ours(args, rank: int, world: int, local: int):
     e2e_ms = e_start.elapsed_time(e_end)
     clocks = sampler.stop() if sampler else None
 
-    # per-kernel durations for the roofline: the same forward/backward launched eagerly, each entry point
-    # bracketed by CUDA events on its stream (graph replays launch the kernels without the host calls)
+    # per-kernel durations for the roofline: each entry point bracketed by CUDA events on its stream.  Graph
+    # mode: the step's forward/backward captured once more with the events as graph nodes and replayed K times,
+    # so the times are device times inside the replayed step; eager mode: the eager forward/backward.
     barrier()
-    with nat.time_entries(TIMED_ENTRIES) as timer:
-        for i in range(args.steps):
-            trainer._zero_grads()
-            trainer._forward_backward(*dev[i % pool])
-        barrier()
+    calls_ms: dict = {}
+    if trainer.cuda_graph:
+        with nat.time_entries(TIMED_ENTRIES, external=True) as timer:
+            prof = trainer.profile_graph()
+        for _ in range(args.steps):
+            prof.replay()
+            for n, (c, ms, a) in timer.result().items():
+                tot = calls_ms.setdefault(n, [0, 0.0, []])
+                tot[0] += c
+                tot[1] += ms
+                tot[2] += a
+        del prof
+    else:
+        with nat.time_entries(TIMED_ENTRIES) as timer:
+            for i in range(args.steps):
+                trainer._zero_grads()
+                trainer._forward_backward(*dev[i % pool])
+            barrier()
+        calls_ms = {n: list(v) for n, v in timer.result().items()}
+    barrier()
 
+    trainer.check_kernels()  # no tensor-core wait ran out during the timed or profiled steps
     value_ms, e2e_ms = max_over_ranks([value_ms, e2e_ms], device)
     audio_job = bench.audio_seconds_per_step * world * args.steps
-    result = timer.result()
+    result = {n: tuple(v) for n, v in calls_ms.items()}
     if rank != 0:
         return
 
@@ -269,17 +304,16 @@ def run_ours(args, rank: int, world: int, local: int):
     per_entry = {n: round(ms, 3) for n, (c, ms, _) in sorted(result.items(), key=lambda kv: -kv[1][1]) if c}
     top = max(result.items(), key=lambda kv: kv[1][1])
     name, (calls, total_ms, arglist) = top
-    roof = rl.roofline(name, calls, total_ms, arglist, peaks, traffic=traffic.get(name))
+    roof = rl.roofline(name, calls, total_ms, arglist, peaks, traffic=traffic.get(name), in_step=True)
+    roof["timing"] = ("CUDA events as graph nodes around each call, in K replays of the captured step's "
+                      "forward/backward" if trainer.cuda_graph else "CUDA events around each call of K eager steps")
 
     line = {
         "metric": METRIC, "value": round(audio_job / (value_ms / 1e3), 3), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(value_ms / args.steps, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": {torch.bfloat16: "bf16", torch.float16: "f16", None: "f32"}[bench.amp], "data": "synthetic",
-        "config": {"workload": bench.name, "model": bench.model_type, "global_batch": bench.batch * world,
-                   "per_gpu_batch": bench.batch, "chunk_samples": bench.chunk, "frames": bench.frames,
-                   "parallelism": f"dp{world}", "note": bench.notes,
-                   "l2": "no flush: a step's activations (several GB) exceed the 126 MB L2"},
+        "config": bench_config(bench, world),
         "e2e": {"value": round(audio_job / (e2e_ms / 1e3), 3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": 4},
         "gpu_launches": int(launches),
@@ -289,7 +323,7 @@ def run_ours(args, rank: int, world: int, local: int):
         "clocks": clocks,
     }
     if world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_oracle_rate(bench, steps=2, warmup=1)
+        line["cpu_baseline"] = cpu_oracle_rate(bench, steps=5, warmup=1, batch=bench.batch)
     print(json.dumps(line), flush=True)
 
 

@@ -317,7 +317,9 @@ PMB_API int pmb_attention_gate_backward(const void* grad_out, const void* attn, 
  *   stft  fp32 [B, S, F, T, 2]  (torch.stft of [B*S, L] audio, as real)
  *   feats      [B, T, J, 2]     J = pairs, index[j] = f*S + s (int32)
  *   inv_ptr int32 [F*S + 1], inv_idx int32 [J]: CSR inverse of index.
- * gather:    feats[b,t,j,:] = stft[b, s_j, f_j, t, :]
+ * gather:    feats[b,t,j,:] = stft[b, s_j, f_j, t, :]; the gather's rows (one
+ *            per (b, t)) are x_ld elements apart (0 = 2 J; a multiple of 8
+ *            gives the 16-byte rows pmb_band_split_tc_forward reads in place)
  * recombine: out[b,n,s,f,t] = (stft[b,s,f,t] if multiply_stft else 1) *
  *            sum_{j in inv(f*S+s)} mask[b,n,t,j] / max(count, 1e-8)   (complex)
  * (pymss-core MelBandRoformer gather `stft_repr[batch, freq_indices]` and
@@ -325,8 +327,8 @@ PMB_API int pmb_attention_gate_backward(const void* grad_out, const void* attn, 
  * counterpart; reached via fused_roformer.py:827-873.)
  * ---------------------------------------------------------------------- */
 PMB_API int pmb_band_gather_forward(const float* stft, const int* index, int64_t batch, int64_t channels,
-                                    int64_t freqs, int64_t frames, int64_t pairs, void* x, int x_dtype,
-                                    void* stream);
+                                    int64_t freqs, int64_t frames, int64_t pairs, void* x, int64_t x_ld,
+                                    int x_dtype, void* stream);
 PMB_API int pmb_band_gather_backward(const void* grad_x, const int* inv_ptr, const int* inv_idx, int64_t batch,
                                      int64_t channels, int64_t freqs, int64_t frames, int64_t pairs,
                                      float* grad_stft, int x_dtype, void* stream);
@@ -429,28 +431,29 @@ PMB_API int pmb_feed_forward_backward(const void* grad_out, const void* x, const
 /* ------------------------------------------------------------------------
  * BandSplit on the tcgen05 tensor cores (bf16 / fp16 activations; fp32 or
  * activation-dtype parameters), same math as pmb_band_split_forward:
- *   out[m, b, :] = (x_b * inv * sqrt(w_b) * gamma_b) W_b^T + bias_b.
- * `normed_padded` [rows, Kp] holds the normalised band features with every
- * band padded with zeros to a multiple of 64 columns (Kp = sizes[3]); it and
- * inv_norm [rows, nb] are saved for the backward.  `packed_weights` [O, Kp]
- * holds W_b * gamma_b in the activation dtype (written by the forward).
- * The backward produces the parameter gradients (grad_biases nullable); the
- * band features' own gradient is not produced (use pmb_band_split_backward
- * when the input needs one).  pmb_band_split_tc_sizes fills sizes[0..3] =
- * packed-weight bytes, normed_padded bytes, backward workspace bytes, Kp.
- * out_features % 8 == 0.  Replaces the ragged band split's forward / weight
- * backward (.cu:590-1003).
+ *   out[m, b, :] = (x_b * inv * sqrt(w_b) * gamma_b) W_b^T + bias_b,
+ * computed as s[m, b] * (x_b (W_b * gamma_b)^T) + bias_b with the row scale
+ * s = inv * sqrt(w_b) applied in the GEMM epilogue, so x is read in place.
+ * x [rows, total] with row stride x_ld: x 16-byte aligned and x_ld a multiple
+ * of sizes[2] (8) elements, >= total.  inv_norm [rows, nb] fp32 is written by
+ * the forward and read by the backward (with x).  `packed_weights` (sizes[0]
+ * bytes) receives W_b * gamma_b in the activation dtype, bands whose columns
+ * share one 64-wide k-block packed block-diagonally into one weight group.
+ * The backward produces the parameter gradients (grad_biases nullable) and
+ * needs a 256-byte aligned workspace of sizes[1] bytes; the band features'
+ * own gradient is not produced (use pmb_band_split_backward when the input
+ * needs one).  sizes[3] = number of weight groups.  out_features must be a
+ * multiple of 64.  Replaces the ragged band split's forward / weight backward
+ * (.cu:590-1003).
  * ---------------------------------------------------------------------- */
 PMB_API int pmb_band_split_tc_sizes(int64_t rows, int num_bands, const int64_t* widths, int64_t out_features,
                                     int dtype, int64_t* sizes);
-PMB_API int pmb_band_split_tc_forward(const void* x, int64_t rows, int64_t x_stride_row, int64_t x_stride_band,
-                                      int64_t x_stride_feat, int num_bands, const int64_t* widths,
-                                      const void* const* gammas, const void* const* weights,
+PMB_API int pmb_band_split_tc_forward(const void* x, int64_t rows, int64_t x_ld, int num_bands,
+                                      const int64_t* widths, const void* const* gammas, const void* const* weights,
                                       const void* const* biases, int64_t out_features, void* packed_weights,
-                                      void* normed_padded, float* inv_norm, void* out, int dtype, int param_dtype,
-                                      void* stream);
-PMB_API int pmb_band_split_tc_backward(const void* grad_out, const void* normed_padded, int64_t rows,
-                                       int num_bands, const int64_t* widths, const void* const* gammas,
+                                      float* inv_norm, void* out, int dtype, int param_dtype, void* stream);
+PMB_API int pmb_band_split_tc_backward(const void* grad_out, const void* x, int64_t x_ld, const float* inv_norm,
+                                       int64_t rows, int num_bands, const int64_t* widths, const void* const* gammas,
                                        const void* const* weights, int64_t out_features, void* const* grad_gammas,
                                        void* const* grad_weights, void* const* grad_biases, int dtype,
                                        int param_dtype, void* workspace, int64_t workspace_bytes, void* stream);

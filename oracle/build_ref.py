@@ -11,7 +11,8 @@ same flags, adding the sm_100a target, and links a Python extension module
 repository.  The module is only imported by ``tests/golden/make_golden.py`` on
 a GPU box to record golden vectors of the reference's kernels.
 
-Usage: ``python oracle/build_ref.py [--reference /path/to/pymsst]``.
+Usage: ``python oracle/build_ref.py --reference /path/to/pymsst`` (or the
+checkout named by the PYMSST_REFERENCE environment variable).
 """
 from __future__ import annotations
 
@@ -25,7 +26,14 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 OUT_DIR = HERE / "_ref"
 MODULE = "pymsst_fused_band_split"
-DEFAULT_REFERENCE = Path(os.environ.get("PYMSST_REFERENCE", "/root/reference"))
+
+
+def reference_checkout(path: str | Path | None = None) -> Path | None:
+    """The reference checkout: ``path`` if given, else $PYMSST_REFERENCE, else None."""
+    if path:
+        return Path(path)
+    env = os.environ.get("PYMSST_REFERENCE")
+    return Path(env) if env else None
 
 
 def _torch_paths():
@@ -38,7 +46,12 @@ def _torch_paths():
     return includes, libs, abi
 
 
-def build(reference: Path = DEFAULT_REFERENCE, verbose: bool = False) -> Path | None:
+def build(reference: str | Path | None = None, verbose: bool = False) -> Path | None:
+    reference = reference_checkout(reference)
+    if reference is None:
+        if verbose:
+            print("no reference checkout given (--reference or PYMSST_REFERENCE); skipping", file=sys.stderr)
+        return None
     cuda_dir = reference / "src" / "pymsst" / "training" / "cuda"
     cpp = cuda_dir / "fused_band_split.cpp"
     cu = cuda_dir / "fused_band_split.cu"
@@ -104,6 +117,6 @@ def load(path: Path | None = None):
 
 if __name__ == "__main__":
     parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    parser.add_argument("--reference", type=Path, default=DEFAULT_REFERENCE)
+    parser.add_argument("--reference", type=Path, default=None)
     args = parser.parse_args()
     print(build(args.reference, verbose=True))

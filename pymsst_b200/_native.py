@@ -46,9 +46,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "pmb_column_sum": (_i, [_p, _i64, _i64, _p, _i, _i, _p, _i64, _p]),
     "pmb_band_split_tc_sizes": (_i, [_i64, _i, _p, _i64, _i, _p]),
     "pmb_band_split_tc_forward": (
-        _i, [_p, _i64, _i64, _i64, _i64, _i, _p, _p, _p, _p, _i64, _p, _p, _p, _p, _i, _i, _p]),
+        _i, [_p, _i64, _i64, _i, _p, _p, _p, _p, _i64, _p, _p, _p, _i, _i, _p]),
     "pmb_band_split_tc_backward": (
-        _i, [_p, _p, _i64, _i, _p, _p, _p, _i64, _p, _p, _p, _i, _i, _p, _i64, _p]),
+        _i, [_p, _p, _i64, _p, _i64, _i, _p, _p, _p, _i64, _p, _p, _p, _i, _i, _p, _i64, _p]),
     "pmb_rms_norm_forward": (_i, [_p, _p, _p, _p, _p, _i64, _i64, _i, _i, _i, _p]),
     "pmb_rms_norm_backward_workspace_size": (_i64, [_i64, _i64]),
     "pmb_rms_norm_backward": (_i, [_p, _p, _i, _p, _p, _p, _p, _i64, _i64, _i, _i, _i, _i, _p, _i64, _p]),
@@ -75,7 +75,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "pmb_attention_gate_backward": (
         _i, [_p, _p, _i64, _i64, _i64, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _i, _i, _p, _i64,
              _i64, _p]),
-    "pmb_band_gather_forward": (_i, [_p, _p, _i64, _i64, _i64, _i64, _i64, _p, _i, _p]),
+    "pmb_band_gather_forward": (_i, [_p, _p, _i64, _i64, _i64, _i64, _i64, _p, _i64, _i, _p]),
     "pmb_band_gather_backward": (_i, [_p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p, _i, _p]),
     "pmb_band_recombine_forward": (_i, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i, _p, _i, _p]),
     "pmb_band_recombine_backward": (_i, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i, _p, _i, _p]),
@@ -152,6 +152,7 @@ def ptr(t: torch.Tensor | None) -> int | None:
 
 # Entry points whose calls are bracketed by CUDA events (see ``time_entries``).
 _TIMED: dict[str, list] = {}
+_TIMED_EXTERNAL = [False]
 
 
 def call(name: str, *args) -> None:
@@ -160,8 +161,8 @@ def call(name: str, *args) -> None:
     if rec is None:
         check(getattr(library(), name)(*args), name)
         return
-    start = torch.cuda.Event(enable_timing=True)
-    end = torch.cuda.Event(enable_timing=True)
+    start = torch.cuda.Event(enable_timing=True, external=_TIMED_EXTERNAL[0])
+    end = torch.cuda.Event(enable_timing=True, external=_TIMED_EXTERNAL[0])
     start.record()
     check(getattr(library(), name)(*args), name)
     end.record()
@@ -171,18 +172,26 @@ def call(name: str, *args) -> None:
 class time_entries:
     """Context manager: record CUDA events around every call of the given entry
     points (on the current stream, where the library launches).  ``result()``
-    returns {name: (calls, total_ms, [args of each call])} after a synchronize."""
+    returns {name: (calls, total_ms, [args of each call])} after a synchronize.
 
-    def __init__(self, names):
+    ``external=True`` makes the events graph nodes when the calls are captured
+    into a CUDA graph: every replay of that graph records them again, so
+    ``result()`` after a replay gives each entry's device time inside the
+    replayed step (no host launch time in it)."""
+
+    def __init__(self, names, external: bool = False):
         self.names = list(names)
+        self.external = bool(external)
 
     def __enter__(self):
         for n in self.names:
             _TIMED[n] = []
+        _TIMED_EXTERNAL[0] = self.external
         return self
 
     def __exit__(self, *exc):
         self.records = {n: _TIMED.pop(n) for n in self.names}
+        _TIMED_EXTERNAL[0] = False
         return False
 
     def result(self) -> dict:

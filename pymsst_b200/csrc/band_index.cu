@@ -43,10 +43,23 @@ struct Dims {
 
 constexpr int kTile = 32;
 
-// x[b, t, j, :] = stft[b, s_j, f_j, t, :]: CTA = 32 j x 32 frames of one batch item.
+// Two consecutive elements (one complex value) stored with one 4- or 8-byte store.
+template <typename T>
+__device__ __forceinline__ void store_pair(T* dst, float re, float im) {
+  if constexpr (sizeof(T) == 2) {
+    T v[2] = {Elem<T>::from_f(re), Elem<T>::from_f(im)};
+    *reinterpret_cast<uint32_t*>(dst) = *reinterpret_cast<const uint32_t*>(v);
+  } else {
+    *reinterpret_cast<float2*>(dst) = make_float2(re, im);
+  }
+}
+
+// x[b, t, j, :] = stft[b, s_j, f_j, t, :]: CTA = 32 j x 32 frames of one batch item; rows of x (one per (b, t))
+// are `ld` elements apart (ld >= 2 J, even).
 template <typename T>
 __global__ void __launch_bounds__(kThreads)
-    gather_fwd(const float* __restrict__ stft, const int* __restrict__ index, Dims d, T* __restrict__ x) {
+    gather_fwd(const float* __restrict__ stft, const int* __restrict__ index, Dims d, int64_t ld,
+               T* __restrict__ x) {
   __shared__ float2 tile[kTile][kTile + 1];
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
   const int64_t j0 = (int64_t)blockIdx.x * kTile, t0 = (int64_t)blockIdx.y * kTile, b = blockIdx.z;
@@ -63,9 +76,7 @@ __global__ void __launch_bounds__(kThreads)
     const int64_t t = t0 + tt, j = j0 + tx;
     if (j < d.J && t < d.T) {
       const float2 v = tile[tx][tt];
-      T* dst = x + ((b * d.T + t) * d.J + j) * 2;
-      dst[0] = Elem<T>::from_f(v.x);
-      dst[1] = Elem<T>::from_f(v.y);
+      store_pair<T>(x + (b * d.T + t) * ld + j * 2, v.x, v.y);
     }
   }
 }
@@ -154,19 +165,24 @@ bool check_dims(const Dims& d) { return d.B >= 0 && d.S > 0 && d.F > 0 && d.T >=
 using namespace pmb;
 
 extern "C" int pmb_band_gather_forward(const float* stft, const int* index, int64_t batch, int64_t channels,
-                                       int64_t freqs, int64_t frames, int64_t pairs, void* x, int x_dtype,
-                                       void* stream) {
+                                       int64_t freqs, int64_t frames, int64_t pairs, void* x, int64_t x_ld,
+                                       int x_dtype, void* stream) {
   clear_error();
   const char* name = "pmb_band_gather_forward";
   Dims d{batch, channels, freqs, frames, pairs, 1};
   PMB_REQUIRE(check_dims(d), "%s: bad shape", name);
+  if (x_ld == 0) x_ld = 2 * pairs;
+  PMB_REQUIRE(x_ld >= 2 * pairs && x_ld % 2 == 0, "%s: row stride %lld must be even and >= %lld", name,
+              (long long)x_ld, (long long)(2 * pairs));
   if (batch * frames == 0) return PMB_OK;
   PMB_REQUIRE(stft && index && x, "%s: NULL tensor argument", name);
   PMB_REQUIRE((reinterpret_cast<uintptr_t>(stft) & 7) == 0, "%s: stft must be 8-byte aligned", name);
+  PMB_REQUIRE((reinterpret_cast<uintptr_t>(x) & (2 * dtype_size(x_dtype) - 1)) == 0,
+              "%s: x must be aligned to one complex value", name);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const dim3 grid((unsigned)((pairs + kTile - 1) / kTile), (unsigned)((frames + kTile - 1) / kTile), (unsigned)batch);
   return PMB_DISPATCH(x_dtype, T, name, [&] {
-    gather_fwd<T><<<grid, kThreads, 0, s>>>(stft, index, d, static_cast<T*>(x));
+    gather_fwd<T><<<grid, kThreads, 0, s>>>(stft, index, d, x_ld, static_cast<T*>(x));
     PMB_CHECK_LAUNCH(name);
     return PMB_OK;
   });

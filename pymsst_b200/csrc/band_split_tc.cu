@@ -1,30 +1,44 @@
 // BandSplit on the tcgen05 tensor cores (bf16 / fp16 activations, fp32 or
 // 16-bit parameters): per band b of width w_b,
-//   normed_b = x_b * inv * sqrt(w_b),  inv = 1 / max(||x_b||, eps)
-//   out[m, b, :] = (normed_b * gamma_b) W_b^T + bias_b
+//   s[m, b] = sqrt(w_b) / max(||x_b[m]||, eps)
+//   out[m, b, :] = s[m, b] * (x_b[m] (W_b * gamma_b)^T) + bias_b
+// which is the reference's (normalise, scale by gamma, Linear) because the
+// per-(row, band) norm is a row scale and commutes with the Linear.
 // Reference semantics: src/pymsst/training/cuda/fused_band_split.cu:590-1003
 // (ragged band split) and :14-247; pure-torch form
 // src/pymsst/training/fused_roformer.py:1265-1271.
 //
-// Layout.  The band features are ragged (w_b = 8 ... 516), so the norm pass
-// writes `normed` in a padded layout P: band b occupies columns
-// [poff_b, poff_b + Kp_b) of a [rows, Kp] matrix, Kp_b = w_b rounded up to 64
-// (the k-block), zero beyond w_b.  Every band then starts on a 128-byte
-// boundary (TMA-aligned) and k-blocks never run into the next band.  The
-// packed weight is (W_b * gamma_b) in the activation dtype in the same column
-// layout, [O, Kp] (the tensor-core B operand), built once per forward and
-// reused by the backward.
+// Input layout.  x [rows, total] is read in place by TMA: its row stride must
+// be a multiple of 8 elements (16 bytes) -- the band gather writes it that
+// way -- and each band's k-range starts at its first column rounded down to a
+// multiple of 8, so every TMA box starts 16-byte aligned whatever the band
+// offsets.  Columns of the box outside the band (the rounding lead, and the
+// rest of the last 64-wide k-block) belong to neighbouring bands or lie past
+// the row end (TMA fills those with zeros); the packed weight holds zeros at
+// those k positions, so they contribute nothing.
 //
-// Forward:  norm pass (inv, normed P), pack pass, one grouped GEMM (group = band:
-//           M = rows, N = O, K = Kp_b) whose epilogue adds the bias and writes
-//           out [rows, nb, O].
-// Backward (the weight side; BandSplit's input is the STFT, which carries no
-// gradient in training, and the row-norm input gradient stays on the exact
-// SIMT path):  G_b = dY_b^T normed_b, a grouped GEMM with M = O, N = Kp_b,
-//           K = rows (both operands MN-major); its epilogue writes
-//           grad_W_b = G_b * gamma_b and per-32-row column partials of
-//           sum_o W_b[o, i] G_b[o, i] (= grad_gamma_b); grad_bias is a column
-//           sum of dY.
+// Weight groups.  Consecutive bands whose columns fit in one 64-wide k-block
+// (the 8- and 16-feature bands of BS-RoFormer) form one group: one A tile
+// x[:, a_g : a_g + 64] feeds all of them, the packed weight of the group is
+// block-diagonal [n_bands * O, 64], and the group's output columns are
+// consecutive columns of out[m, :, :] (bands are adjacent there).  Wider bands
+// are groups of one band with K = their k-range rounded up to 64.
+//
+// Forward (two launches): a prep kernel whose first CTAs compute s[m, b]
+// (row staged as 4-element vectors, per-chunk sums of squares reduced per
+// band in a fixed order) and whose remaining CTAs pack W_b * gamma_b into the
+// grouped weight matrix; then one persistent grouped GEMM (group = weight
+// group, M = rows, N = n_bands * O, K = 64-multiple) whose epilogue scales
+// each row by s[m, b], adds the bias and writes out [rows, nb, O].
+//
+// Backward (the parameter side; BandSplit's input is the STFT, which carries
+// no gradient in training): a prep kernel writes normed = x * s (same strided
+// layout, in the workspace) and per-64-row column partials of dY (bias
+// gradient); one grouped GEMM per band, G_b = dY_b^T normed_b (M = O,
+// N = the band's k-range, K = rows, both operands MN-major), whose epilogue
+// writes grad_W_b = G_b * gamma_b and per-32-row partials of
+// sum_o W_b[o, i] G_b[o, i] (= grad_gamma_b); a finalize kernel sums both
+// partial sets.  Every sum runs in a fixed order (deterministic).
 #include <vector>
 
 #include "gemm_umma.cuh"
@@ -37,244 +51,358 @@ unsigned int timeout_flag_band(int reset) { return umma::flag_reader(reset); }
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kKp = 64;  // band padding unit (= the GEMM k-block)
+constexpr int kRowAlign = 8;     // x row stride alignment in elements (16 bytes)
+constexpr int kMaxGroupBands = 8;
+constexpr int kMaxGroupN = 1536;
 
-struct BandCols {
-  int nb;
-  int w[kMaxBands];     // true widths
-  int off[kMaxBands];   // column offset in the unpadded feature layout
-  int poff[kMaxBands];  // column offset in the padded layout P
-  int kp[kMaxBands];    // padded width
-  int total, total_p;
+struct Layout {
+  int nb, ng, O, total, kpmax, n_total;
+  int w[kMaxBands];        // band widths
+  int off[kMaxBands];      // first feature column of each band
+  int first[kMaxBands + 1];  // group g covers bands [first[g], first[g + 1])
+  int a[kMaxBands];        // first column of group g's k-range (multiple of 8)
+  int kp[kMaxBands];       // k extent of group g (multiple of 64)
+  int row[kMaxBands + 1];  // first row of group g in the packed weight [n_total, kpmax]
 };
 
-BandCols make_cols(int nb, const int64_t* widths) {
-  BandCols c;
-  c.nb = nb;
-  int off = 0, poff = 0;
+Layout make_layout(int nb, const int64_t* widths, int O) {
+  Layout L;
+  L.nb = nb;
+  L.O = O;
+  int off = 0;
   for (int b = 0; b < nb; ++b) {
-    c.w[b] = (int)widths[b];
-    c.off[b] = off;
-    c.poff[b] = poff;
-    c.kp[b] = (c.w[b] + kKp - 1) / kKp * kKp;
-    off += c.w[b];
-    poff += c.kp[b];
+    L.w[b] = (int)widths[b];
+    L.off[b] = off;
+    off += L.w[b];
   }
-  c.total = off;
-  c.total_p = poff;
-  return c;
+  L.total = off;
+  L.ng = 0;
+  L.kpmax = 64;
+  int rows = 0;
+  for (int b = 0; b < nb;) {
+    const int a = L.off[b] & ~(kRowAlign - 1);
+    int e = b + 1;
+    int end = L.off[b] + L.w[b];
+    while (e < nb && L.off[e] + L.w[e] - a <= 64 && e - b < kMaxGroupBands && (e - b + 1) * O <= kMaxGroupN) {
+      end = L.off[e] + L.w[e];
+      ++e;
+    }
+    const int g = L.ng++;
+    L.first[g] = b;
+    L.a[g] = a;
+    L.kp[g] = (end - a + 63) / 64 * 64;
+    L.row[g] = rows;
+    rows += (e - b) * O;
+    if (L.kp[g] > L.kpmax) L.kpmax = L.kp[g];
+    b = e;
+  }
+  L.first[L.ng] = nb;
+  L.row[L.ng] = rows;
+  L.n_total = rows;
+  return L;
 }
 
-struct XLayout {
-  int64_t s_row, s_band, s_feat;  // s_band < 0: ragged (column offset off[b])
+// Elements per vector of the row passes: the largest of 4 / 2 / 1 that
+// divides every band offset and width (so no vector straddles two bands).
+int chunk_elems(const Layout& L) {
+  int g = 4;
+  for (int b = 0; b < L.nb; ++b)
+    while (g > 1 && ((L.off[b] % g) || (L.w[b] % g))) g >>= 1;
+  return g;
+}
+
+template <typename T, int CH>
+struct Vec;
+template <typename T>
+struct Vec<T, 4> {
+  using U = uint2;
+};
+template <typename T>
+struct Vec<T, 2> {
+  using U = uint32_t;
+};
+template <typename T>
+struct Vec<T, 1> {
+  using U = uint16_t;
 };
 
-// One warp per (row, band): inv and the padded normed row segment.
-template <typename T>
+// ------------------------------------------------------------- forward prep
+// CTAs [0, row_ctas): s for rows r = blockIdx.x, + row_ctas, ...
+// CTAs [row_ctas, ...): packed[row_g + n, k] = W_b[o, i] * gamma_b[i] (or 0)
+// for 8 consecutive k per thread.
+template <typename T, typename TP, int CH>
 __global__ void __launch_bounds__(kThreads)
-    norm_padded(const T* __restrict__ x, int64_t rows, XLayout lx, BandCols bc, T* __restrict__ normed_p,
-                float* __restrict__ inv_norm) {
-  const int lane = threadIdx.x & 31;
-  const int64_t pairs = rows * bc.nb;
-  for (int64_t p = (int64_t)blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5); p < pairs;
-       p += (int64_t)gridDim.x * (kThreads / 32)) {
-    const int64_t r = p / bc.nb;
-    const int b = (int)(p - r * bc.nb);
-    const int w = bc.w[b];
-    const T* xb = x + r * lx.s_row + (lx.s_band < 0 ? (int64_t)bc.off[b] * lx.s_feat : (int64_t)b * lx.s_band);
-    float ss = 0.f;
-    for (int i = lane; i < w; i += 32) {
-      const float v = Elem<T>::to_f(xb[i * lx.s_feat]);
-      ss += v * v;
-    }
-    ss = warp_sum(ss);
-    const float inv = 1.0f / fmaxf(sqrtf(ss), 1.0e-12f);
-    if (lane == 0) inv_norm[r * bc.nb + b] = inv;
-    const float k = inv * sqrtf((float)w);
-    T* nb_ = normed_p + r * bc.total_p + bc.poff[b];
-    for (int i = lane; i < bc.kp[b]; i += 32)
-      nb_[i] = Elem<T>::from_f(i < w ? Elem<T>::to_f(xb[i * lx.s_feat]) * k : 0.f);
-  }
-}
-
-// Contiguous features (s_feat == 1, ragged): one CTA per row.  The row is
-// staged in shared memory with 4-byte loads (rows need not be 16-byte
-// aligned), then warp w handles bands w, w + 8, ...: sum of squares from
-// shared memory, and the padded normalised segment written with coalesced
-// stores.
-template <typename T>
-__global__ void __launch_bounds__(kThreads)
-    norm_padded_rows(const T* __restrict__ x, int64_t rows, int64_t s_row, BandCols bc, T* __restrict__ normed_p,
-                     float* __restrict__ inv_norm) {
-  extern __shared__ __align__(16) uint8_t smem_raw[];
-  T* xs = reinterpret_cast<T*>(smem_raw);
+    bs_prep_forward(const T* __restrict__ x, int64_t rows, int64_t ld, int row_ctas, BandTable tab, Layout L,
+                 float* __restrict__ scale_out, T* __restrict__ packed) {
+  extern __shared__ float chunk_ss[];  // total / CH floats
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
-    const T* xr = x + r * s_row;
-    // total is even for 16-bit bands of 4-element multiples; copy pairs when aligned
-    if ((reinterpret_cast<uintptr_t>(xr) & 3) == 0 && (bc.total & 1) == 0) {
-      const uint32_t* src = reinterpret_cast<const uint32_t*>(xr);
-      uint32_t* dst = reinterpret_cast<uint32_t*>(xs);
-      for (int i = threadIdx.x; i < bc.total / 2; i += kThreads) dst[i] = src[i];
-    } else {
-      for (int i = threadIdx.x; i < bc.total; i += kThreads) xs[i] = xr[i];
-    }
-    __syncthreads();
-    for (int b = warp; b < bc.nb; b += kThreads / 32) {
-      const int w = bc.w[b];
-      const T* xb = xs + bc.off[b];
-      float ss = 0.f;
-      for (int i = lane; i < w; i += 32) {
-        const float v = Elem<T>::to_f(xb[i]);
-        ss += v * v;
+  if ((int)blockIdx.x < row_ctas) {
+    using U = typename Vec<T, CH>::U;
+    const int nchunks = L.total / CH;
+    for (int64_t r = blockIdx.x; r < rows; r += row_ctas) {
+      const U* xr = reinterpret_cast<const U*>(x + r * ld);
+      for (int c = threadIdx.x; c < nchunks; c += kThreads) {
+        const U u = xr[c];
+        const T* e = reinterpret_cast<const T*>(&u);
+        float ss = 0.f;
+#pragma unroll
+        for (int j = 0; j < CH; ++j) {
+          const float v = Elem<T>::to_f(e[j]);
+          ss = fmaf(v, v, ss);
+        }
+        chunk_ss[c] = ss;
       }
-      ss = warp_sum(ss);
-      const float inv = 1.0f / fmaxf(sqrtf(ss), 1.0e-12f);
-      if (lane == 0) inv_norm[r * bc.nb + b] = inv;
-      const float k = inv * sqrtf((float)w);
-      T* nb_ = normed_p + r * bc.total_p + bc.poff[b];
-      for (int i = lane; i < bc.kp[b]; i += 32) nb_[i] = Elem<T>::from_f(i < w ? Elem<T>::to_f(xb[i]) * k : 0.f);
+      __syncthreads();
+      for (int b = warp; b < L.nb; b += kThreads / 32) {
+        const int c0 = L.off[b] / CH, c1 = (L.off[b] + L.w[b]) / CH;
+        float ss = 0.f;
+        for (int c = c0 + lane; c < c1; c += 32) ss += chunk_ss[c];
+        ss = warp_sum(ss);
+        if (lane == 0) scale_out[r * L.nb + b] = 1.0f / fmaxf(sqrtf(ss), 1.0e-12f);
+      }
+      __syncthreads();
     }
-    __syncthreads();
+    return;
   }
-}
-
-// packed[n, poff_b + k] for band b = blockIdx.y: threads over k, rows n strided.
-template <typename T, typename TP>
-__global__ void __launch_bounds__(kThreads)
-    pack_weights_band(BandTable tab, BandCols bc, int64_t O, T* __restrict__ packed) {
-  const int b = blockIdx.y;
-  const int w = bc.w[b], kp = bc.kp[b];
+  // packing: the groups' [rows_g, kp_g] blocks, 8 columns per thread
+  const int64_t e8 = ((int64_t)blockIdx.x - row_ctas) * kThreads + threadIdx.x;
+  int64_t base = 0;
+  int g = 0;
+  for (; g < L.ng; ++g) {
+    const int64_t sz = (int64_t)(L.row[g + 1] - L.row[g]) * (L.kp[g] / 8);
+    if (e8 < base + sz) break;
+    base += sz;
+  }
+  if (g >= L.ng) return;
+  const int64_t local = e8 - base;
+  const int kq = L.kp[g] / 8;
+  const int n = (int)(local / kq), k0 = (int)(local % kq) * 8;
+  const int b = L.first[g] + n / L.O, o = n % L.O;
   const TP* W = static_cast<const TP*>(tab.ptr1[b]);
-  const TP* g = static_cast<const TP*>(tab.ptr0[b]);
-  for (int64_t e = (int64_t)blockIdx.x * kThreads + threadIdx.x; e < O * kp; e += (int64_t)gridDim.x * kThreads) {
-    const int64_t n = e / kp;
-    const int k = (int)(e - n * kp);
-    const float v = k < w ? Elem<TP>::to_f(W[n * w + k]) * Elem<TP>::to_f(g[k]) : 0.f;
-    packed[n * bc.total_p + bc.poff[b] + k] = Elem<T>::from_f(v);
+  const TP* gm = static_cast<const TP*>(tab.ptr0[b]);
+  alignas(16) T vals[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int i = L.a[g] + k0 + j - L.off[b];
+    vals[j] = Elem<T>::from_f(i >= 0 && i < L.w[b] ? Elem<TP>::to_f(W[(int64_t)o * L.w[b] + i]) * Elem<TP>::to_f(gm[i]) : 0.f);
   }
+  *reinterpret_cast<uint4*>(packed + (int64_t)(L.row[g] + n) * L.kpmax + k0) = *reinterpret_cast<const uint4*>(vals);
 }
 
-// out[m, b, n] = acc + bias_b[n]
+// out[m, b, o] = s[m, b] * sqrt(w_b) * acc + bias_b[o] for the group's bands (one band per 32-column chunk).
 template <typename T, typename TP>
 struct BandOutEpi {
   T* out;
-  int nb;
-  int O;
+  const float* inv;
+  int nb, O;
+  int first[kMaxBands];
+  float sqrt_w[kMaxBands];
   const void* bias[kMaxBands];
   template <int BN>
   __device__ void run(const ugemm::Plan&, const ugemm::TileCtx& t) const {
     const int lane = threadIdx.x & 31;
     const int64_t ld = (int64_t)nb * O;
-    T* base = out + (int64_t)t.row0 * ld + (int64_t)t.group * O + t.n0;
-    const TP* bp = static_cast<const TP*>(bias[t.group]);
 #pragma unroll 1
     for (int c0 = 32 * t.sub; c0 < BN; c0 += 32 * ugemm::kSubs) {
       if (c0 >= t.n_valid) break;
       const int ncols = min(32, t.n_valid - c0);
+      const int n = t.n0 + c0;
+      const int b = first[t.group] + n / O, o0 = n % O;
       float v[32];
       umma::tmem_ld32(t.taddr + c0, v);
-      const float bl = (bp != nullptr && lane < ncols) ? Elem<TP>::to_f(bp[t.n0 + c0 + lane]) : 0.f;
+      const float sc = t.row_valid ? inv[(int64_t)t.row * nb + b] * sqrt_w[b] : 0.f;
+      const TP* bp = static_cast<const TP*>(bias[b]);
+      const float bl = (bp != nullptr && lane < ncols) ? Elem<TP>::to_f(bp[o0 + lane]) : 0.f;
 #pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] += __shfl_sync(0xffffffffu, bl, j);
-      ugemm::warp_store<T>(t.stage, v, base + c0, ld, t.rows_valid, ncols);
+      for (int j = 0; j < 32; ++j) v[j] = fmaf(v[j], sc, __shfl_sync(0xffffffffu, bl, j));
+      ugemm::warp_store<T>(t.stage, v, out + (int64_t)t.row0 * ld + (int64_t)b * O + o0, ld, t.rows_valid, ncols);
     }
   }
 };
 
-// G tile (rows o of O, columns i of the band's padded width):
-//   grad_W_b[o, i] = G[o, i] * gamma_b[i]   (i < w_b)
-//   partial[row0 / 32][poff_b + i] = sum over this warp's 32 rows of W_b[o, i] * G[o, i]
+// ------------------------------------------------------------ backward prep
+// CTAs [0, row_ctas): normed[r, c] = x[r, c] * s[r, band(c)] * sqrt(w_band) for the band columns.
+// CTAs [row_ctas, ...): bias partials bpart[chunk][col] = sum over the chunk's 64 rows of dY[r, col].
+template <typename T, int CH>
+__global__ void __launch_bounds__(kThreads)
+    bs_prep_backward(const T* __restrict__ x, int64_t rows, int64_t ld, const float* __restrict__ inv, Layout L,
+                  int row_ctas, T* __restrict__ normed, int64_t nld, const T* __restrict__ dy, int64_t cols,
+                  float* __restrict__ bpart) {
+  extern __shared__ float sc_s[];  // nb scales of the current row, then the chunk -> band map
+  if ((int)blockIdx.x < row_ctas) {
+    using U = typename Vec<T, CH>::U;
+    const int nchunks = L.total / CH;
+    int* band_of_chunk = reinterpret_cast<int*>(sc_s + L.nb);
+    for (int c = threadIdx.x; c < nchunks; c += kThreads) {
+      int lo = 0, hi = L.nb - 1;
+      const int col = c * CH;
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (L.off[mid] <= col) lo = mid; else hi = mid - 1;
+      }
+      band_of_chunk[c] = lo;
+    }
+    for (int64_t r = blockIdx.x; r < rows; r += row_ctas) {
+      __syncthreads();
+      for (int b = threadIdx.x; b < L.nb; b += kThreads) sc_s[b] = inv[r * L.nb + b] * sqrtf((float)L.w[b]);
+      __syncthreads();
+      const U* xr = reinterpret_cast<const U*>(x + r * ld);
+      U* nr = reinterpret_cast<U*>(normed + r * nld);
+      for (int c = threadIdx.x; c < nchunks; c += kThreads) {
+        U u = xr[c];
+        T* e = reinterpret_cast<T*>(&u);
+        const float s = sc_s[band_of_chunk[c]];
+#pragma unroll
+        for (int j = 0; j < CH; ++j) e[j] = Elem<T>::from_f(Elem<T>::to_f(e[j]) * s);
+        nr[c] = u;
+      }
+    }
+    return;
+  }
+  const int64_t bid = (int64_t)blockIdx.x - row_ctas;
+  const int64_t col_blocks = (cols + kThreads - 1) / kThreads;
+  const int64_t chunk = bid / col_blocks;
+  const int64_t c = (bid % col_blocks) * kThreads + threadIdx.x;
+  if (c >= cols) return;
+  const int64_t r0 = chunk * red::kRowsPerChunk;
+  const int64_t r1 = r0 + red::kRowsPerChunk < rows ? r0 + red::kRowsPerChunk : rows;
+  float s = 0.f;
+  for (int64_t r = r0; r < r1; ++r) s += Elem<T>::to_f(dy[r * cols + c]);
+  bpart[chunk * cols + c] = s;
+}
+
+// G tile (rows o of O, columns n of band b's k-range, feature i = n - lead_b):
+//   grad_W_b[o, i] = G[o, n] * gamma_b[i]              (0 <= i < w_b)
+//   gpart[row0 / 32][off_b + i] = sum over this warp's 32 rows of W_b[o, i] * G[o, n]
 template <typename TP>
 struct WGradBandEpi {
-  BandCols bc;
+  int w[kMaxBands], lead[kMaxBands], off[kMaxBands];
+  int total;
   const void* gamma[kMaxBands];
   const void* weight[kMaxBands];
   void* grad_w[kMaxBands];
-  float* partial;
+  float* gpart;
   template <int BN>
   __device__ void run(const ugemm::Plan&, const ugemm::TileCtx& t) const {
     const int lane = threadIdx.x & 31;
     const int b = t.group;
-    const int w = bc.w[b];
+    const int wb = w[b], ld = lead[b];
     const TP* gm = static_cast<const TP*>(gamma[b]);
     const TP* W = static_cast<const TP*>(weight[b]);
     TP* gW = static_cast<TP*>(grad_w[b]);
 #pragma unroll 1
     for (int c0 = 32 * t.sub; c0 < BN; c0 += 32 * ugemm::kSubs) {
-      const int i0 = t.n0 + c0;
-      if (c0 >= t.n_valid || i0 >= w) break;
-      const int ncols = min(32, w - i0);
-      float v[32], wv[32];
+      const int i0 = t.n0 + c0 - ld;  // feature of this chunk's column 0 (may be negative by the lead)
+      if (c0 >= t.n_valid || i0 >= wb) break;
+      const int i = i0 + lane;
+      const bool col_ok = i >= 0 && i < wb;
+      float v[32];
       umma::tmem_ld32(t.taddr + c0, v);
-      ugemm::warp_load<TP>(t.stage, W + (int64_t)t.row0 * w + i0, w, t.rows_valid, ncols, wv);
-      const float gl = lane < ncols ? Elem<TP>::to_f(gm[i0 + lane]) : 0.f;
+      // W rows of this warp, column i per lane (through the staging block: row r, lane = column)
       float* st = reinterpret_cast<float*>(t.stage + lane * ugemm::kStageRowBytes);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) st[j] = wv[j] * v[j];  // W * G, this lane's row
+      for (int j = 0; j < 32; ++j) st[j] = v[j];  // G, this lane's row o = row0 + lane, columns i0 .. i0 + 31
       __syncwarp();
+      const float gl = col_ok ? Elem<TP>::to_f(gm[i]) : 0.f;
       float s = 0.f;
-      for (int r = 0; r < t.rows_valid; ++r) s += reinterpret_cast<const float*>(t.stage + r * ugemm::kStageRowBytes)[lane];
-      if (lane < ncols && t.rows_valid > 0) partial[(int64_t)(t.row0 / 32) * bc.total_p + bc.poff[b] + i0 + lane] = s;
+      for (int r = 0; r < t.rows_valid; ++r) {
+        const float g = reinterpret_cast<const float*>(t.stage + r * ugemm::kStageRowBytes)[lane];
+        if (col_ok) {
+          const int64_t idx = (int64_t)(t.row0 + r) * wb + i;
+          s = fmaf(Elem<TP>::to_f(W[idx]), g, s);
+          gW[idx] = Elem<TP>::from_f(g * gl);
+        }
+      }
+      if (col_ok && t.rows_valid > 0) gpart[(int64_t)(t.row0 / 32) * total + off[b] + i] = s;
       __syncwarp();
-#pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] *= __shfl_sync(0xffffffffu, gl, j);
-      ugemm::warp_store<TP>(t.stage, v, gW + (int64_t)t.row0 * w + i0, w, t.rows_valid, ncols);
     }
   }
 };
 
-// grad_gamma_b[i] = sum_q partial[q][poff_b + i]
+// grad_gamma_b[i] = sum_q gpart[q][off_b + i] for the first `total` threads; grad_bias_b[o] = sum over chunks of
+// bpart[chunk][b * O + o] for the next nb * O.
 template <typename TP>
 __global__ void __launch_bounds__(kThreads)
-    gamma_finalize(const float* __restrict__ partial, int nq, BandCols bc, BandTable gtab) {
-  const int c = blockIdx.x * kThreads + threadIdx.x;
-  if (c >= bc.total_p) return;
-  int lo = 0, hi = bc.nb - 1;
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (bc.poff[mid] <= c) lo = mid; else hi = mid - 1;
+    bs_finalize(const float* __restrict__ gpart, int nq, const float* __restrict__ bpart, int nchunks, Layout L,
+             BandTable gtab, BandTable btab) {
+  const int64_t c = (int64_t)blockIdx.x * kThreads + threadIdx.x;
+  if (c < L.total) {
+    int lo = 0, hi = L.nb - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (L.off[mid] <= c) lo = mid; else hi = mid - 1;
+    }
+    float s = 0.f;
+    for (int q = 0; q < nq; ++q) s += gpart[(int64_t)q * L.total + c];
+    static_cast<TP*>(const_cast<void*>(gtab.ptr0[lo]))[c - L.off[lo]] = Elem<TP>::from_f(s);
+    return;
   }
-  const int b = lo, i = c - bc.poff[b];
-  if (i >= bc.w[b]) return;
+  const int64_t cols = (int64_t)L.nb * L.O;
+  const int64_t k = c - L.total;
+  if (k >= cols || btab.ptr0[0] == nullptr) return;
   float s = 0.f;
-  for (int q = 0; q < nq; ++q) s += partial[(int64_t)q * bc.total_p + c];
-  static_cast<TP*>(const_cast<void*>(gtab.ptr0[b]))[i] = Elem<TP>::from_f(s);
+  for (int q = 0; q < nchunks; ++q) s += bpart[(int64_t)q * cols + k];
+  const int b = (int)(k / L.O);
+  static_cast<TP*>(const_cast<void*>(btab.ptr0[b]))[k - (int64_t)b * L.O] = Elem<TP>::from_f(s);
 }
 
 int64_t align256(int64_t v) { return (v + 255) & ~(int64_t)255; }
 
 struct Sizes {
-  int64_t packed_bytes, normed_bytes, ws_bytes;
-  int64_t ws_gpart, ws_bpart;
+  int64_t packed_bytes, ws_bytes;
+  int64_t ws_gpart, ws_bpart;  // offsets of the partial blocks after the normed copy
 };
 
-Sizes sizes_of(int64_t rows, const BandCols& bc, int64_t O, int es) {
+Sizes sizes_of(int64_t rows, const Layout& L, int es) {
   Sizes z;
-  z.packed_bytes = align256(O * bc.total_p * es);
-  z.normed_bytes = align256(rows * bc.total_p * es);
-  z.ws_gpart = 0;
-  z.ws_bpart = align256(((O + 31) / 32) * bc.total_p * 4);
-  z.ws_bytes = z.ws_bpart + align256((int64_t)red::chunks(rows) * bc.nb * O * 4);
+  z.packed_bytes = align256((int64_t)L.n_total * L.kpmax * es);
+  const int64_t ld = (L.total + kRowAlign - 1) / kRowAlign * kRowAlign;
+  z.ws_gpart = align256(rows * ld * es);
+  z.ws_bpart = z.ws_gpart + align256((int64_t)((L.O + 31) / 32) * L.total * 4);
+  z.ws_bytes = z.ws_bpart + align256((int64_t)red::chunks(rows) * L.nb * L.O * 4);
   return z;
-}
-
-int grid_for(int64_t n, int per) {
-  int64_t g = (n + per - 1) / per;
-  const int64_t cap = (int64_t)num_sms() * 16;
-  return (int)(g > cap ? cap : (g < 1 ? 1 : g));
 }
 
 template <int BN, bool A_MN, bool B_MN, class Epi>
 int run_gemm(const CUtensorMap& ma, const CUtensorMap& mb, ugemm::Plan& plan, const Epi& epi, int fp16,
              cudaStream_t s, const char* name) {
-  constexpr int STAGES = BN == 256 ? 3 : 4;
+  constexpr int STAGES = 4;
   const int tiles = ugemm::build_plan(plan, BN);
   if (tiles == 0) return PMB_OK;
   auto kern = ugemm::umma_gemm_kernel<BN, STAGES, A_MN, B_MN, Epi>;
   const int smem = ugemm::smem_bytes<BN, STAGES>();
   PMB_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem), name);
   kern<<<ugemm::persistent_grid(tiles), ugemm::kThreads, smem, s>>>(ma, mb, plan, epi, fp16);
+  PMB_CHECK_LAUNCH(name);
+  return PMB_OK;
+}
+
+template <typename T, typename TP, int CH>
+int launch_prep_forward(const T* x, int64_t rows, int64_t ld, const BandTable& tab, const Layout& L, float* inv,
+                        T* packed, cudaStream_t s, const char* name) {
+  const int row_ctas = (int)(rows < (int64_t)num_sms() * 8 ? rows : (int64_t)num_sms() * 8);
+  int64_t pack_items = 0;
+  for (int g = 0; g < L.ng; ++g) pack_items += (int64_t)(L.row[g + 1] - L.row[g]) * (L.kp[g] / 8);
+  const int pack_ctas = (int)((pack_items + kThreads - 1) / kThreads);
+  const size_t smem = (size_t)(L.total / CH) * sizeof(float);
+  auto kern = bs_prep_forward<T, TP, CH>;
+  if (smem > 48 * 1024) PMB_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem), name);
+  kern<<<row_ctas + pack_ctas, kThreads, smem, s>>>(x, rows, ld, row_ctas, tab, L, inv, packed);
+  PMB_CHECK_LAUNCH(name);
+  return PMB_OK;
+}
+
+template <typename T, int CH>
+int launch_prep_backward(const T* x, int64_t rows, int64_t ld, const float* inv, const Layout& L, T* normed,
+                         int64_t nld, const T* dy, float* bpart, cudaStream_t s, const char* name) {
+  const int row_ctas = (int)(rows < (int64_t)num_sms() * 8 ? rows : (int64_t)num_sms() * 8);
+  const int64_t cols = (int64_t)L.nb * L.O;
+  const int64_t bias_ctas = bpart ? ((cols + kThreads - 1) / kThreads) * red::chunks(rows) : 0;
+  const size_t smem = (size_t)L.nb * sizeof(float) + (size_t)(L.total / CH) * sizeof(int);
+  auto kern = bs_prep_backward<T, CH>;
+  if (smem > 48 * 1024) PMB_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem), name);
+  kern<<<(unsigned)(row_ctas + bias_ctas), kThreads, smem, s>>>(x, rows, ld, inv, L, row_ctas, normed, nld, dy, cols,
+                                                                 bpart);
   PMB_CHECK_LAUNCH(name);
   return PMB_OK;
 }
@@ -287,164 +415,173 @@ using namespace pmb;
 extern "C" int pmb_band_split_tc_sizes(int64_t rows, int num_bands, const int64_t* widths, int64_t out_features,
                                        int dtype, int64_t* sizes) {
   clear_error();
-  PMB_REQUIRE(num_bands > 0 && num_bands <= kMaxBands && widths && sizes && rows >= 0 && out_features > 0,
-              "pmb_band_split_tc_sizes: bad arguments");
+  PMB_REQUIRE(num_bands > 0 && num_bands <= kMaxBands && widths && sizes && rows >= 0 && out_features > 0 &&
+                  out_features % 64 == 0 && out_features <= 4096,
+              "pmb_band_split_tc_sizes: bad arguments (out_features must be a positive multiple of 64)");
   for (int b = 0; b < num_bands; ++b) PMB_REQUIRE(widths[b] > 0, "pmb_band_split_tc_sizes: band %d is empty", b);
-  const BandCols bc = make_cols(num_bands, widths);
-  const Sizes z = sizes_of(rows, bc, out_features, dtype_size(dtype) > 0 ? dtype_size(dtype) : 2);
+  const Layout L = make_layout(num_bands, widths, (int)out_features);
+  const Sizes z = sizes_of(rows, L, dtype_size(dtype) > 0 ? dtype_size(dtype) : 2);
   sizes[0] = z.packed_bytes;
-  sizes[1] = z.normed_bytes;
-  sizes[2] = z.ws_bytes;
-  sizes[3] = bc.total_p;
+  sizes[1] = z.ws_bytes;
+  sizes[2] = kRowAlign;
+  sizes[3] = L.ng;
   return PMB_OK;
 }
 
-extern "C" int pmb_band_split_tc_forward(const void* x, int64_t rows, int64_t x_stride_row, int64_t x_stride_band,
-                                         int64_t x_stride_feat, int num_bands, const int64_t* widths,
-                                         const void* const* gammas, const void* const* weights,
-                                         const void* const* biases, int64_t out_features, void* packed_weights,
-                                         void* normed_padded, float* inv_norm, void* out, int dtype,
-                                         int param_dtype, void* stream) {
+extern "C" int pmb_band_split_tc_forward(const void* x, int64_t rows, int64_t x_ld, int num_bands,
+                                         const int64_t* widths, const void* const* gammas,
+                                         const void* const* weights, const void* const* biases, int64_t out_features,
+                                         void* packed_weights, float* inv_norm, void* out, int dtype, int param_dtype,
+                                         void* stream) {
   clear_error();
   const char* name = "pmb_band_split_tc_forward";
   PMB_REQUIRE(dtype == PMB_BFLOAT16 || dtype == PMB_FLOAT16, "%s: activations must be bf16 or fp16", name);
   BandTable tab;
   int st = make_band_table(tab, num_bands, widths, gammas, weights, biases, name);
   if (st) return st;
-  PMB_REQUIRE(rows >= 0 && rows < (1ll << 31) && out_features > 0 && out_features % 8 == 0,
-              "%s: bad shape (out_features must be a multiple of 8)", name);
+  PMB_REQUIRE(rows >= 0 && rows < (1ll << 31) && out_features > 0 && out_features % 64 == 0 && out_features <= 4096,
+              "%s: bad shape (out_features must be a positive multiple of 64)", name);
   if (rows == 0) return PMB_OK;
-  PMB_REQUIRE(x && out && inv_norm && packed_weights && normed_padded, "%s: NULL tensor argument", name);
+  PMB_REQUIRE(x && out && inv_norm && packed_weights, "%s: NULL tensor argument", name);
   for (int b = 0; b < num_bands; ++b)
     PMB_REQUIRE(tab.ptr0[b] && tab.ptr1[b], "%s: band %d has a NULL gamma or weight", name, b);
-  PMB_REQUIRE(x_stride_band < 0 || (tab.max_width * num_bands == tab.total),
-              "%s: a band stride requires equal band widths", name);
-  const BandCols bc = make_cols(num_bands, widths);
-  XLayout lx{x_stride_row, x_stride_band, x_stride_feat};
+  const Layout L = make_layout(num_bands, widths, (int)out_features);
+  if (x_ld < L.total || x_ld % kRowAlign != 0 || (reinterpret_cast<uintptr_t>(x) & 15) != 0 ||
+      (reinterpret_cast<uintptr_t>(packed_weights) & 15) != 0) {
+    set_error("%s: x needs a 16-byte aligned base and a row stride that is a multiple of %d elements and at least "
+              "%d (got %lld)", name, kRowAlign, L.total, (long long)x_ld);
+    return PMB_ERR_ALIGNMENT;
+  }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int fp16 = dtype == PMB_FLOAT16;
+  const int ch = chunk_elems(L);
   return PMB_DISPATCH_PARAM(dtype, param_dtype, T, TP, name, [&] {
     if constexpr (sizeof(T) == 4) {
       set_error("%s: fp32 activations are not supported", name);
       return PMB_ERR_UNSUPPORTED_DTYPE;
     } else {
-      const size_t row_smem = (size_t)bc.total * sizeof(T);
-      if (x_stride_band < 0 && x_stride_feat == 1 && row_smem <= 96 * 1024) {
-        if (row_smem > 48 * 1024)
-          PMB_CHECK_CUDA(cudaFuncSetAttribute(norm_padded_rows<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              (int)row_smem),
-                         name);
-        const int g = (int)(rows < (int64_t)num_sms() * 8 ? rows : (int64_t)num_sms() * 8);
-        norm_padded_rows<T><<<g, kThreads, row_smem, s>>>(static_cast<const T*>(x), rows, x_stride_row, bc,
-                                                            static_cast<T*>(normed_padded), inv_norm);
-      } else {
-        norm_padded<T><<<grid_for(rows * num_bands, kThreads / 32), kThreads, 0, s>>>(
-            static_cast<const T*>(x), rows, lx, bc, static_cast<T*>(normed_padded), inv_norm);
-      }
-      PMB_CHECK_LAUNCH(name);
-      {
-        int bx = (int)((out_features * 64 + kThreads - 1) / kThreads);
-        dim3 pg((unsigned)(bx < 1 ? 1 : bx), (unsigned)num_bands);
-        pack_weights_band<T, TP><<<pg, kThreads, 0, s>>>(tab, bc, out_features, static_cast<T*>(packed_weights));
-      }
-      PMB_CHECK_LAUNCH(name);
-      CUtensorMap ma, mb;
-      constexpr int BN = 256;
-      int st2 = tma::make_map_3d(ma, normed_padded, dtype, bc.total_p, 1, rows, bc.total_p * 2, bc.total_p * 2, 64, 1,
-                                 ugemm::BM, name);
+      const T* xt = static_cast<const T*>(x);
+      T* pk = static_cast<T*>(packed_weights);
+      int st2 = ch == 4   ? launch_prep_forward<T, TP, 4>(xt, rows, x_ld, tab, L, inv_norm, pk, s, name)
+                : ch == 2 ? launch_prep_forward<T, TP, 2>(xt, rows, x_ld, tab, L, inv_norm, pk, s, name)
+                          : launch_prep_forward<T, TP, 1>(xt, rows, x_ld, tab, L, inv_norm, pk, s, name);
       if (st2) return st2;
-      st2 = tma::make_map_3d(mb, packed_weights, dtype, bc.total_p, 1, out_features, bc.total_p * 2,
-                             bc.total_p * 2, 64, 1, BN, name);
+      CUtensorMap ma, mb;
+      constexpr int BN = 192;
+      st2 = tma::make_map_3d(ma, x, dtype, L.total, 1, rows, x_ld * 2, x_ld * 2, 64, 1, ugemm::BM, name);
+      if (st2) return st2;
+      st2 = tma::make_map_3d(mb, packed_weights, dtype, L.kpmax, 1, L.n_total, (int64_t)L.kpmax * 2,
+                             (int64_t)L.kpmax * 2, 64, 1, BN, name);
       if (st2) return st2;
       ugemm::Plan plan;
-      plan.num_groups = num_bands;
+      plan.num_groups = L.ng;
       BandOutEpi<T, TP> epi;
       epi.out = static_cast<T*>(out);
+      epi.inv = inv_norm;
       epi.nb = num_bands;
       epi.O = (int)out_features;
       for (int b = 0; b < num_bands; ++b) {
-        plan.g[b] = ugemm::Group{(int)rows, (int)out_features, bc.kp[b], bc.poff[b], 0, 0, bc.poff[b], 0, 0};
+        epi.sqrt_w[b] = sqrtf((float)L.w[b]);
         epi.bias[b] = biases ? biases[b] : nullptr;
+      }
+      for (int g = 0; g < L.ng; ++g) {
+        epi.first[g] = L.first[g];
+        plan.g[g] = ugemm::Group{(int)rows, L.row[g + 1] - L.row[g], L.kp[g], L.a[g], 0, 0, 0, 0, L.row[g]};
       }
       return run_gemm<BN, false, false>(ma, mb, plan, epi, fp16, s, name);
     }
   });
 }
 
-extern "C" int pmb_band_split_tc_backward(const void* grad_out, const void* normed_padded, int64_t rows,
-                                          int num_bands, const int64_t* widths, const void* const* gammas,
-                                          const void* const* weights, int64_t out_features,
-                                          void* const* grad_gammas, void* const* grad_weights,
+extern "C" int pmb_band_split_tc_backward(const void* grad_out, const void* x, int64_t x_ld, const float* inv_norm,
+                                          int64_t rows, int num_bands, const int64_t* widths,
+                                          const void* const* gammas, const void* const* weights,
+                                          int64_t out_features, void* const* grad_gammas, void* const* grad_weights,
                                           void* const* grad_biases, int dtype, int param_dtype, void* workspace,
                                           int64_t workspace_bytes, void* stream) {
   clear_error();
   const char* name = "pmb_band_split_tc_backward";
   PMB_REQUIRE(dtype == PMB_BFLOAT16 || dtype == PMB_FLOAT16, "%s: activations must be bf16 or fp16", name);
-  BandTable wtab, gtab;
+  BandTable wtab, gtab, btab;
   int st = make_band_table(wtab, num_bands, widths, gammas, weights, (const void* const*)grad_weights, name);
   if (st) return st;
   st = make_band_table(gtab, num_bands, widths, (const void* const*)grad_gammas, nullptr, nullptr, name);
   if (st) return st;
-  PMB_REQUIRE(rows > 0 && rows < (1ll << 31) && out_features > 0 && out_features % 8 == 0, "%s: bad shape", name);
-  PMB_REQUIRE(grad_out && normed_padded && grad_gammas && grad_weights && gammas && weights,
+  PMB_REQUIRE(rows > 0 && rows < (1ll << 31) && out_features > 0 && out_features % 64 == 0 && out_features <= 4096,
+              "%s: bad shape", name);
+  PMB_REQUIRE(grad_out && x && inv_norm && grad_gammas && grad_weights && gammas && weights,
               "%s: NULL tensor argument", name);
   for (int b = 0; b < num_bands; ++b)
     PMB_REQUIRE(wtab.ptr0[b] && wtab.ptr1[b] && wtab.ptr2[b] && gtab.ptr0[b] && (!grad_biases || grad_biases[b]),
                 "%s: band %d has a NULL parameter or gradient pointer", name, b);
-  const BandCols bc = make_cols(num_bands, widths);
-  const Sizes z = sizes_of(rows, bc, out_features, dtype_size(dtype));
-  if (workspace == nullptr || workspace_bytes < z.ws_bytes) {
-    set_error("%s: workspace of %lld bytes is smaller than the %lld required", name, (long long)workspace_bytes,
-              (long long)z.ws_bytes);
+  {
+    std::vector<int64_t> ow(num_bands, out_features);
+    st = make_band_table(btab, num_bands, ow.data(), (const void* const*)grad_biases, nullptr, nullptr, name);
+    if (st) return st;
+    if (!grad_biases) btab.ptr0[0] = nullptr;
+  }
+  const Layout L = make_layout(num_bands, widths, (int)out_features);
+  if (x_ld < L.total || x_ld % kRowAlign != 0 || (reinterpret_cast<uintptr_t>(x) & 15) != 0 ||
+      (reinterpret_cast<uintptr_t>(grad_out) & 15) != 0) {
+    set_error("%s: x and grad_out need 16-byte aligned bases and x a row stride that is a multiple of %d "
+              "elements (got %lld)", name, kRowAlign, (long long)x_ld);
+    return PMB_ERR_ALIGNMENT;
+  }
+  const Sizes z = sizes_of(rows, L, dtype_size(dtype));
+  if (workspace == nullptr || workspace_bytes < z.ws_bytes || (reinterpret_cast<uintptr_t>(workspace) & 255) != 0) {
+    set_error("%s: workspace of %lld bytes is smaller than the %lld required (or not 256-byte aligned)", name,
+              (long long)workspace_bytes, (long long)z.ws_bytes);
     return PMB_ERR_WORKSPACE;
   }
+  // row stride of the normed copy in the workspace
+  const int64_t nld = (L.total + kRowAlign - 1) / kRowAlign * kRowAlign;
   float* gpart = reinterpret_cast<float*>(static_cast<char*>(workspace) + z.ws_gpart);
   float* bpart = reinterpret_cast<float*>(static_cast<char*>(workspace) + z.ws_bpart);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int fp16 = dtype == PMB_FLOAT16;
+  const int ch = chunk_elems(L);
   return PMB_DISPATCH_PARAM(dtype, param_dtype, T, TP, name, [&] {
     if constexpr (sizeof(T) == 4) {
       set_error("%s: fp32 activations are not supported", name);
       return PMB_ERR_UNSUPPORTED_DTYPE;
     } else {
-      // G_b = dY_b^T normed_b: A(m = o, k = r) = dY[r, b, o], B(n = i, k = r) = normed_p[r, poff_b + i]
+      const T* xt = static_cast<const T*>(x);
+      T* normed = static_cast<T*>(workspace);
+      const T* dy = static_cast<const T*>(grad_out);
+      float* bp = grad_biases ? bpart : nullptr;
+      int st2 = ch == 4   ? launch_prep_backward<T, 4>(xt, rows, x_ld, inv_norm, L, normed, nld, dy, bp, s, name)
+                : ch == 2 ? launch_prep_backward<T, 2>(xt, rows, x_ld, inv_norm, L, normed, nld, dy, bp, s, name)
+                          : launch_prep_backward<T, 1>(xt, rows, x_ld, inv_norm, L, normed, nld, dy, bp, s, name);
+      if (st2) return st2;
+      // G_b = dY_b^T normed_b: A(m = o, k = r) = dY[r, b, o], B(n, k = r) = normed[r, a_b + n]
       constexpr int BN = 128;
       CUtensorMap ma, mb;
-      int st2 = tma::make_map_3d(ma, grad_out, dtype, out_features, num_bands, rows, out_features * 2,
-                                 (int64_t)num_bands * out_features * 2, 64, 1, 64, name);
+      st2 = tma::make_map_3d(ma, grad_out, dtype, out_features, num_bands, rows, out_features * 2,
+                             (int64_t)num_bands * out_features * 2, 64, 1, 64, name);
       if (st2) return st2;
-      st2 = tma::make_map_3d(mb, normed_padded, dtype, bc.total_p, 1, rows, bc.total_p * 2, bc.total_p * 2, 64, 1, 64,
-                             name);
+      st2 = tma::make_map_3d(mb, normed, dtype, L.total, 1, rows, nld * 2, nld * 2, 64, 1, 64, name);
       if (st2) return st2;
       ugemm::Plan plan;
       plan.num_groups = num_bands;
       WGradBandEpi<TP> epi;
-      epi.bc = bc;
-      epi.partial = gpart;
+      epi.total = L.total;
+      epi.gpart = gpart;
       for (int b = 0; b < num_bands; ++b) {
-        plan.g[b] = ugemm::Group{(int)out_features, bc.kp[b], (int)rows, 0, b, 0, bc.poff[b], 0, 0};
+        const int a = L.off[b] & ~(kRowAlign - 1);
+        epi.w[b] = L.w[b];
+        epi.lead[b] = L.off[b] - a;
+        epi.off[b] = L.off[b];
+        plan.g[b] = ugemm::Group{(int)out_features, L.off[b] - a + L.w[b], (int)rows, 0, b, 0, a, 0, 0};
         epi.gamma[b] = gammas[b];
         epi.weight[b] = weights[b];
         epi.grad_w[b] = grad_weights[b];
       }
       st2 = run_gemm<BN, true, true>(ma, mb, plan, epi, fp16, s, name);
       if (st2) return st2;
-      gamma_finalize<TP><<<(bc.total_p + kThreads - 1) / kThreads, kThreads, 0, s>>>(
-          gpart, (int)((out_features + 31) / 32), bc, gtab);
+      const int64_t items = L.total + (int64_t)num_bands * out_features;
+      bs_finalize<TP><<<(unsigned)((items + kThreads - 1) / kThreads), kThreads, 0, s>>>(
+          gpart, (int)((out_features + 31) / 32), bpart, red::chunks(rows), L, gtab, btab);
       PMB_CHECK_LAUNCH(name);
-      if (grad_biases != nullptr) {
-        BandTable btab;
-        std::vector<int64_t> ow(num_bands, out_features);
-        st2 = make_band_table(btab, num_bands, ow.data(), (const void* const*)grad_biases, nullptr, nullptr, name);
-        if (st2) return st2;
-        const int64_t cols = (int64_t)num_bands * out_features;
-        dim3 gp((unsigned)((cols + 255) / 256), (unsigned)red::chunks(rows));
-        red::colsum_partial<T><<<gp, red::kThreads, 0, s>>>(static_cast<const T*>(grad_out), rows, cols, cols, bpart);
-        PMB_CHECK_LAUNCH(name);
-        red::colsum_finalize_bands<<<(unsigned)((cols + 255) / 256), red::kThreads, 0, s>>>(
-            bpart, red::chunks(rows), cols, btab, Elem<TP>::code);
-        PMB_CHECK_LAUNCH(name);
-      }
       return PMB_OK;
     }
   });

@@ -79,7 +79,10 @@ struct Config {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr uint32_t IDESC_BF16 = umma::idesc_f16(true, A_MN, B_MN, BM, BN);
   static constexpr uint32_t IDESC_F16 = umma::idesc_f16(false, A_MN, B_MN, BM, BN);
-  static constexpr uint32_t TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;  // two accumulators
+  // two accumulators; tcgen05.alloc takes a power of two from 32 to 512 columns
+  static constexpr uint32_t TMEM_COLS = 2 * BN <= 32 ? 32 : 2 * BN <= 64 ? 64 : 2 * BN <= 128 ? 128
+                                      : 2 * BN <= 256 ? 256 : 512;
+  static_assert(2 * BN <= 512, "two accumulators must fit the 512 tensor-memory columns");
 };
 
 template <int BN, int STAGES>

@@ -42,7 +42,22 @@ struct BandInfo {
   void* grad[kMaxBands];         // per-band fp32 gradient destinations (weights)
 };
 
-__device__ __forceinline__ float sigm(float v) { return 1.0f / (1.0f + expf(-v)); }
+// 16-bit activations only, so the hardware approximations (MUFU; relative
+// error around 2^-11, below the 2^-8 / 2^-11 spacing of bf16 / fp16 results)
+// replace the accurate library calls, which made the epilogues issue-bound:
+//   tanh: tanh.approx.f32;   sigmoid(v) = 1 / (1 + 2^(-v log2 e)) with
+//   ex2.approx and rcp.approx (2^+inf -> rcp 0, 2^-inf -> 1: saturates).
+__device__ __forceinline__ float tanh_fast(float v) {
+  float r;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(r) : "f"(v));
+  return r;
+}
+__device__ __forceinline__ float sigm(float v) {
+  float e, r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(v * -1.4426950408889634f));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.0f + e));
+  return r;
+}
 
 template <typename T>
 __device__ __forceinline__ float ld(const void* p, int64_t i) {
@@ -111,7 +126,7 @@ struct TanhEpi {
       umma::tmem_ld32(t.taddr + c0, v);
       const float bl = lane < ncols ? Elem<TP>::to_f(bp[c0 + lane]) : 0.f;
 #pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = tanhf(v[j] + __shfl_sync(0xffffffffu, bl, j));
+      for (int j = 0; j < 32; ++j) v[j] = tanh_fast(v[j] + __shfl_sync(0xffffffffu, bl, j));
       ugemm::warp_store<T>(t.stage, v, o + c0, ld, t.rows_valid, ncols);
     }
   }

@@ -666,17 +666,22 @@ def mask_estimator_final_direct_backward(grad_out, x, pre, weights, dim_inputs, 
 
 # ------------------------------------------------------- band index kernels
 def band_gather(stft: torch.Tensor, tables: dict, out_dtype: torch.dtype = torch.float32) -> torch.Tensor:
-    """stft fp32 [B,S,F,T,2] -> band features [B,T,J*2] (``tables`` from BandIndex.device_tables)."""
+    """stft fp32 [B,S,F,T,2] -> band features [B,T,J*2] (``tables`` from BandIndex.device_tables).
+
+    The result is a view whose rows (one per frame) start 16 bytes apart: the
+    storage is [B, T, ld] with ld = J*2 rounded up to 8 elements, so the
+    tensor-core BandSplit reads it in place with TMA."""
     device = nat.require_cuda(stft, name="band_gather")
     _check(stft.dtype == torch.float32 and stft.dim() == 5 and stft.shape[-1] == 2, "stft must be fp32 [B,S,F,T,2]")
     stft = _contig(stft)
     b, s, f, t, _ = stft.shape
     j = tables["index"].numel()
-    x = torch.empty(b, t, j * 2, dtype=out_dtype, device=device)
+    ld = (2 * j + 7) // 8 * 8
+    x = torch.empty(b, t, ld, dtype=out_dtype, device=device)
     with torch.cuda.device(device):
         nat.call("pmb_band_gather_forward", stft.data_ptr(), tables["index"].data_ptr(), b, s, f, t, j, x.data_ptr(),
-                 nat.dtype_code(out_dtype), nat.stream_handle(device))
-    return x
+                 ld, nat.dtype_code(out_dtype), nat.stream_handle(device))
+    return x[..., : 2 * j]
 
 
 def band_gather_backward(grad_x: torch.Tensor, tables: dict, channels: int, freqs: int) -> torch.Tensor:

@@ -68,38 +68,47 @@ class BandSplitFn(torch.autograd.Function):
 
     16-bit activations whose input needs no gradient (the STFT features of
     training) take the tcgen05 path (pmb_band_split_tc_forward / _backward:
-    zero-padded normalised bands, one grouped tensor-core GEMM each way);
-    otherwise the exact SIMT kernels (pmb_band_split_forward / _backward)."""
+    the GEMM reads the features in place -- rows 16-byte aligned, as the band
+    gather writes them; anything else is first copied into such rows -- and
+    applies the per-(row, band) norm scale in its epilogue; the backward
+    reads the features and the saved inverse norms); otherwise the exact SIMT
+    kernels (pmb_band_split_forward / _backward)."""
 
     @staticmethod
     def forward(ctx, x, widths, out_features, *params):
         nb = len(widths)
         gammas, weights, biases = params[:nb], params[nb : 2 * nb], params[2 * nb :]
         device = nat.require_cuda(x, name="BandSplit")
-        x = x.contiguous()
         rows, total = x.shape
-        out = torch.empty(rows, nb, out_features, dtype=x.dtype, device=device)
         inv = torch.empty(rows, nb, dtype=torch.float32, device=device)
         pdt = weights[0].dtype
         ctx.widths = widths
         ctx.out_features = out_features
         ctx.tc = (x.dtype in (torch.bfloat16, torch.float16) and not ctx.needs_input_grad[0]
-                  and out_features % 8 == 0)
+                  and out_features % 64 == 0)
         if ctx.tc:
             warr = nat.i64_array(widths)
             sizes = (ctypes.c_int64 * 4)()
             nat.call("pmb_band_split_tc_sizes", rows, nb, warr, out_features, nat.dtype_code(x.dtype), sizes)
+            align = int(sizes[2])
+            if not (x.stride(-1) == 1 and x.stride(0) % align == 0 and x.stride(0) >= total
+                    and x.data_ptr() % 16 == 0):
+                ld = (total + align - 1) // align * align
+                buf = torch.empty(rows, ld, dtype=x.dtype, device=device)
+                buf[:, :total].copy_(x)
+                x = buf[:, :total]
+            out = torch.empty(rows, nb, out_features, dtype=x.dtype, device=device)
             packed = nat.workspace(sizes[0], device)
-            normed_p = torch.empty(rows, int(sizes[3]), dtype=x.dtype, device=device)
             nat.call(
-                "pmb_band_split_tc_forward", x.data_ptr(), rows, total, -1, 1, nb, warr, nat.ptr_array(gammas),
-                nat.ptr_array(weights), nat.ptr_array(biases), out_features, packed.data_ptr(), normed_p.data_ptr(),
-                inv.data_ptr(), out.data_ptr(), nat.dtype_code(x.dtype), nat.dtype_code(pdt),
-                nat.stream_handle(device),
+                "pmb_band_split_tc_forward", x.data_ptr(), rows, x.stride(0), nb, warr, nat.ptr_array(gammas),
+                nat.ptr_array(weights), nat.ptr_array(biases), out_features, packed.data_ptr(), inv.data_ptr(),
+                out.data_ptr(), nat.dtype_code(x.dtype), nat.dtype_code(pdt), nat.stream_handle(device),
             )
-            ctx.ws_bytes = int(sizes[2])
-            ctx.save_for_backward(normed_p, *gammas, *weights)
+            ctx.ws_bytes = int(sizes[1])
+            ctx.save_for_backward(x, inv, *gammas, *weights)
             return out
+        x = x.contiguous()
+        out = torch.empty(rows, nb, out_features, dtype=x.dtype, device=device)
         normed = torch.empty_like(x)
         ext.band_split_forward_into(x, rows, (total, -1, 1), widths, gammas, weights, biases, out_features, out,
                                     normed, inv, param_dtype=pdt)
@@ -110,17 +119,17 @@ class BandSplitFn(torch.autograd.Function):
     def backward(ctx, grad):
         nb = len(ctx.widths)
         if ctx.tc:
-            normed_p, *rest = ctx.saved_tensors
+            x, inv, *rest = ctx.saved_tensors
             gammas, weights = rest[:nb], rest[nb:]
-            device = normed_p.device
-            grad = grad.to(normed_p.dtype).contiguous()
+            device = x.device
+            grad = grad.to(x.dtype).contiguous()
             rows = grad.shape[0]
             g_gammas = [torch.empty_like(g) for g in gammas]
             g_weights = [torch.empty_like(w) for w in weights]
             g_biases = [torch.empty(ctx.out_features, dtype=weights[0].dtype, device=device) for _ in weights]
             ws = nat.workspace(ctx.ws_bytes, device)
             nat.call(
-                "pmb_band_split_tc_backward", grad.data_ptr(), normed_p.data_ptr(), rows, nb,
+                "pmb_band_split_tc_backward", grad.data_ptr(), x.data_ptr(), x.stride(0), inv.data_ptr(), rows, nb,
                 nat.i64_array(ctx.widths), nat.ptr_array(gammas), nat.ptr_array(weights), ctx.out_features,
                 nat.ptr_array(g_gammas), nat.ptr_array(g_weights), nat.ptr_array(g_biases),
                 nat.dtype_code(grad.dtype), nat.dtype_code(weights[0].dtype), ws.data_ptr(), ctx.ws_bytes,

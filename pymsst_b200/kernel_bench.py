@@ -28,8 +28,9 @@ SEQ_BATCH, SEQ = 248, 258
 
 
 class _Bench:
-    def __init__(self, device: torch.device, iters: int, warmup: int = 3):
+    def __init__(self, device: torch.device, iters: int, warmup: int = 3, graphs: bool = True):
         self.device = device
+        self.graphs = graphs
         self.iters = iters
         self.warmup = warmup
         self.flush = torch.empty(64 * 1024 * 1024, device=device)
@@ -38,15 +39,30 @@ class _Bench:
         self.peaks = load_peaks()
 
     def time(self, name: str, fn, bytes_: float = 0.0, flops: float = 0.0) -> dict:
+        """Median device time of ``fn``: captured once into a CUDA graph after the warm-up calls and replayed
+        (so host launch work between an op's kernels is not timed), 256 MB written between replays so L2
+        starts cold; ops that cannot be captured are timed as eager calls."""
         for _ in range(self.warmup):
             fn()
         torch.cuda.synchronize(self.device)
+        graph = None
+        if self.graphs:
+            try:
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph):
+                    fn()
+            except Exception:  # not capturable: time eager calls instead
+                graph = None
+                torch.cuda.synchronize(self.device)
         times = []
         for _ in range(self.iters):
             self.flush.zero_()
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record(self.stream)
-            fn()
+            if graph is not None:
+                graph.replay()
+            else:
+                fn()
             b.record(self.stream)
             torch.cuda.synchronize(self.device)
             times.append(a.elapsed_time(b))
@@ -278,7 +294,9 @@ def _op_band_rows(bench: _Bench, rows: int):
     widths = [4 * f for f in DEFAULT_FREQS_PER_BANDS]
     nb, total, D = len(widths), sum(widths), DIM
     sfx = "" if rows == 1032 else f" [{rows} rows]"
-    x = torch.randn(rows, total, device=dev, dtype=bf)
+    ld = (total + 7) // 8 * 8  # the band gather's 16-byte rows
+    xbuf = torch.randn(rows, ld, device=dev, dtype=bf)
+    x = xbuf[:, :total]
     gam = [torch.ones(w, device=dev) for w in widths]
     wts = [torch.randn(D, w, device=dev) / w ** 0.5 for w in widths]
     bss = [torch.zeros(D, device=dev) for _ in widths]
@@ -286,29 +304,32 @@ def _op_band_rows(bench: _Bench, rows: int):
     sizes = (ctypes.c_int64 * 4)()
     nat.call("pmb_band_split_tc_sizes", rows, nb, warr, D, 2, sizes)
     packed = nat.workspace(sizes[0], dev)
-    normed_p = torch.empty(rows, int(sizes[3]), device=dev, dtype=bf)
     inv = torch.empty(rows, nb, device=dev)
     out = torch.empty(rows, nb, D, device=dev, dtype=bf)
     st = nat.stream_handle(dev)
     pg, pw, pb = nat.ptr_array(gam), nat.ptr_array(wts), nat.ptr_array(bss)
     flops = 2.0 * rows * total * D
-    byt = rows * total * 2 * 2 + total * D * 4 + rows * nb * D * 2
+    # algorithmic bytes: x read once, out and inv written once, fp32 W / gamma / bias read once
+    byt = rows * total * 2 + rows * nb * (D * 2 + 4) + (total * (D + 1) + nb * D) * 4
     bench.time("band_split_tc_forward" + sfx, lambda: nat.call(
-        "pmb_band_split_tc_forward", x.data_ptr(), rows, total, -1, 1, nb, warr, pg, pw, pb, D, packed.data_ptr(),
-        normed_p.data_ptr(), inv.data_ptr(), out.data_ptr(), 2, 0, st), byt, flops)
-    normed = torch.empty_like(x)
+        "pmb_band_split_tc_forward", x.data_ptr(), rows, ld, nb, warr, pg, pw, pb, D, packed.data_ptr(),
+        inv.data_ptr(), out.data_ptr(), 2, 0, st), byt, flops)
+    xc = x.contiguous()
+    normed = torch.empty_like(xc)
+    sbyt = rows * total * 2 * 2 + rows * nb * (D * 2 + 4) + (total * (D + 1) + nb * D) * 4
     bench.time("band_split_forward (SIMT)" + sfx, lambda: nat.call(
-        "pmb_band_split_forward", x.data_ptr(), rows, total, -1, 1, nb, warr, pg, pw, pb, D, out.data_ptr(),
-        normed.data_ptr(), inv.data_ptr(), 2, 0, st), byt, flops)
+        "pmb_band_split_forward", xc.data_ptr(), rows, total, -1, 1, nb, warr, pg, pw, pb, D, out.data_ptr(),
+        normed.data_ptr(), inv.data_ptr(), 2, 0, st), sbyt, flops)
     gy = torch.randn(rows, nb, D, device=dev, dtype=bf)
     gg = [torch.empty_like(g) for g in gam]
     gw = [torch.empty_like(w) for w in wts]
     gb = [torch.empty_like(b) for b in bss]
-    ws = nat.workspace(sizes[2], dev)
-    bbyt = rows * nb * D * 2 + rows * total * 2 + total * D * 4 * 2
+    ws = nat.workspace(sizes[1], dev)
+    # dY, x and inv read once; W read, grad W / gamma / bias written (fp32)
+    bbyt = rows * nb * (D * 2 + 4) + rows * total * 2 + (total * D * 2 + 2 * total + 2 * nb * D) * 4
     bench.time("band_split_tc_backward" + sfx, lambda: nat.call(
-        "pmb_band_split_tc_backward", gy.data_ptr(), normed_p.data_ptr(), rows, nb, warr, pg, pw, D,
-        nat.ptr_array(gg), nat.ptr_array(gw), nat.ptr_array(gb), 2, 0, ws.data_ptr(), sizes[2], st), bbyt, flops)
+        "pmb_band_split_tc_backward", gy.data_ptr(), x.data_ptr(), ld, inv.data_ptr(), rows, nb, warr, pg, pw, D,
+        nat.ptr_array(gg), nat.ptr_array(gw), nat.ptr_array(gb), 2, 0, ws.data_ptr(), sizes[1], st), bbyt, flops)
     swsb = nat.library().pmb_band_split_backward_workspace_size(rows, nb, warr, D, 0)
     sws = nat.workspace(swsb, dev)
     bench.time("band_split_backward (SIMT)" + sfx, lambda: nat.call(
@@ -464,12 +485,14 @@ def main(argv=None) -> None:
     p.add_argument("--warmup", type=int, default=3, help="untimed calls per op before timing (0 with --iters 1 "
                    "launches each kernel once, for profiler captures)")
     p.add_argument("--json", default=None)
+    p.add_argument("--eager", action="store_true",
+                   help="time eager calls instead of CUDA-graph replays (host launch time then counts)")
     p.add_argument("--sweep", action="store_true",
                    help="run the config-2 kernel sweep (RMSNorm, rotary, BandSplit, mel at sizes beyond L2) "
                         "instead of the config-3 ops")
     args = p.parse_args(argv)
     device = torch.device("cuda", torch.cuda.current_device())
-    bench = _Bench(device, max(args.iters, 1), args.warmup)
+    bench = _Bench(device, max(args.iters, 1), args.warmup, graphs=not args.eager and args.warmup > 0)
     if args.sweep:
         run_sweep(bench)
     for name in ([] if args.sweep else args.ops or list(OPS)):

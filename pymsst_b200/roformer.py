@@ -418,11 +418,24 @@ class _Roformer(nn.Module):
             b, t, f, d = x.shape
             # rows stay in (b, t, f) order for both axes: the time transformer's sequences are (b, f) pairs
             # over t (inner = f), the frequency transformer's are (b, t) pairs over f
-            x = time_t(x, seq_len=t, inner=f)
-            x = freq_t(x.reshape(b * t, f, d)).reshape(b, t, f, d)
+            x = self._run_transformer(time_t, x, seq_len=t, inner=f)
+            x = self._run_transformer(freq_t, x.reshape(b * t, f, d)).reshape(b, t, f, d)
             if self.skip_connection:
                 store.append(x)
         return self.final_norm(x)
+
+    def _run_transformer(self, transformer, x, **kwargs):
+        """One axial transformer; with ``use_torch_checkpoint`` (training, gradients on) its activations are
+        recomputed in the backward instead of kept (torch.utils.checkpoint, non-reentrant), as pymss-core
+        does per transformer.  Dropout masks are replayed exactly only when dropout is live (the RNG state is
+        then saved, which a captured CUDA graph does not allow)."""
+        if not (self.use_torch_checkpoint and self.training and torch.is_grad_enabled()):
+            return transformer(x, **kwargs)
+        from torch.utils.checkpoint import checkpoint
+
+        dropout_live = any(isinstance(m, nn.Dropout) and m.p > 0 for m in transformer.modules()) or any(
+            getattr(m, "dropout", 0.0) > 0 for m in transformer.modules() if isinstance(m, Attention))
+        return checkpoint(transformer, x, use_reentrant=False, preserve_rng_state=dropout_live, **kwargs)
 
     def _istft(self, spec, window, length):  # spec fp32 [b, n, s, f, t, 2]
         b, n, s, f, t, _ = spec.shape

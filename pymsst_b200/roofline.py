@@ -54,7 +54,7 @@ def work(name: str, a: tuple) -> tuple[float, float]:
         return rows * (3 * h * dh + 2 * dim + h) * ES[dt] + 8 * rows * h + 2 * h * (dim + 1) * ES[pt], \
             4.0 * rows * h * (dim + dh)
     if name == "pmb_band_gather_forward":
-        b, s, f, t, j, xd = a[2], a[3], a[4], a[5], a[6], a[8]
+        b, s, f, t, j, xd = a[2], a[3], a[4], a[5], a[6], a[9]
         return b * t * j * 2 * (4 + ES[xd]) + 4 * j, 0.0
     if name == "pmb_band_recombine_forward":
         b, n, s, f, t, j, mult, md = a[4], a[5], a[6], a[7], a[8], a[9], a[10], a[12]
@@ -96,14 +96,16 @@ def work(name: str, a: tuple) -> tuple[float, float]:
         rows, dim, n, dt = a[4] * a[5], a[6], 3 * a[7] * a[8], a[13]
         return (rows * dim + n * dim + rows * n) * ES[dt] + 2 * a[5] * a[8] // 2 * 4, 2.0 * rows * n * dim
     if name == "pmb_band_split_tc_forward":
-        rows, nb, o, dt, pt = a[1], a[5], a[10], a[15], a[16]
-        total = sum(_widths(a[6], nb))
-        byt = 2 * rows * total * ES[dt] + rows * nb * (o * ES[dt] + 4) + (total * (o + 1) + nb * o) * ES[pt]
+        # x read once, out and inv written once, parameters read once
+        rows, nb, o, dt, pt = a[1], a[3], a[8], a[12], a[13]
+        total = sum(_widths(a[4], nb))
+        byt = rows * total * ES[dt] + rows * nb * (o * ES[dt] + 4) + (total * (o + 1) + nb * o) * ES[pt]
         return byt, 2.0 * rows * total * o
     if name == "pmb_band_split_tc_backward":
-        rows, nb, o, dt, pt = a[2], a[3], a[7], a[11], a[12]
-        total = sum(_widths(a[4], nb))
-        byt = rows * nb * o * ES[dt] + rows * total * ES[dt] + (2 * total * (o + 1) + 2 * nb * o) * ES[pt]
+        # dY, x and inv read once; W read; grad W, gamma, bias written
+        rows, nb, o, dt, pt = a[4], a[5], a[9], a[13], a[14]
+        total = sum(_widths(a[6], nb))
+        byt = rows * nb * (o * ES[dt] + 4) + rows * total * ES[dt] + (2 * total * o + 2 * total + 2 * nb * o) * ES[pt]
         return byt, 2.0 * rows * total * o
     if name in ("pmb_mask_estimator_tc_forward", "pmb_mask_estimator_tc_backward"):
         fwd = name.endswith("forward")
@@ -159,18 +161,25 @@ MEASURED_TRAFFIC = {
 }
 
 
-def roofline(name: str, calls: int, total_ms: float, args_list: list, peaks: dict, traffic=None) -> dict:
-    """Achieved rate of the timed calls against the roof that binds this op."""
+def roofline(name: str, calls: int, total_ms: float, args_list: list, peaks: dict, traffic=None,
+             in_step: bool = True) -> dict:
+    """Achieved rate of the timed calls against the roof that binds this op.
+
+    ``in_step``: the calls were timed inside a long training step, so the tensor roof is the sustained bf16
+    figure (the GPU settles at a lower clock under its power cap); otherwise the burst figure of a kernel
+    timed alone.  HBM has one measured figure for both."""
+    tflops = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]) if in_step else peaks["bf16_tflops"]
     byt = sum(work(name, a)[0] for a in args_list)
     flops = sum(work(name, a)[1] for a in args_list)
     secs = total_ms / 1e3
     t_hbm = byt / (peaks["hbm_gbs"] * 1e9)
-    t_tc = flops / (peaks["bf16_tflops"] * 1e12)
+    t_tc = flops / (tflops * 1e12)
     per_launch_ms = total_ms / max(calls, 1)
     if t_tc > t_hbm:
         achieved = flops / secs / 1e12
-        return {"bound": "tensor", "achieved": round(achieved, 2), "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-                "frac": round(achieved / peaks["bf16_tflops"], 4), "traffic": traffic, "kernel": name,
+        return {"bound": "tensor", "achieved": round(achieved, 2), "peak": tflops, "unit": "TFLOP/s",
+                "frac": round(achieved / tflops, 4), "traffic": traffic, "kernel": name,
+                "peak_kind": "sustained" if in_step else "burst",
                 "calls": calls, "ms_per_call": round(per_launch_ms, 4), "peak_source": peaks["source"],
                 "algorithmic_flops_per_call": flops / max(calls, 1)}
     achieved = byt / secs / 1e9

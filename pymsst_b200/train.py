@@ -1,11 +1,13 @@
 """Training step, benchmark configurations and the seeded loss-curve runner.
 
 ``Trainer.step`` is one training step of the reference's manual loop
-(src/pymsst/validation/direct_compare.py:358-386): forward with the loss under
-autocast (bf16 / fp16 or off), backward, optional gradient clipping, Adam
-step.  Data parallelism is torch DDP over NCCL (the reference trains with
-Lightning ``strategy="ddp"``, src/pymsst/cli.py:357-372): one process per
-GPU, gradients all-reduced in buckets that overlap the backward.
+(src/pymsst/validation/direct_compare.py:350-384): forward with the loss under
+autocast (bf16 / fp16 or off), backward of the (fp16: scaled) loss, optional
+gradient clipping, Adam step through the gradient scaler.  Data parallelism
+follows the reference's Lightning ``strategy="ddp"`` (src/pymsst/cli.py:
+357-372): one process per GPU, gradients averaged over ranks by NCCL -- one
+all-reduce of the flat gradient buffer (optionally in buckets that overlap
+the backward) in the flat / captured step, torch DDP otherwise.
 ``run_loss_curve`` is the ``compare-direct`` analogue: a seeded run that
 records the loss of every step.
 """
@@ -68,23 +70,40 @@ def build_model(bench: BenchConfig, seed: int = 0) -> torch.nn.Module:
 
 
 class Trainer:
-    """Owns the model (optionally data-parallel) and its Adam optimizer.
+    """Owns the model (optionally data-parallel), its Adam optimizer and, for fp16, its gradient scaler.
+
+    One ``step`` is one iteration of the reference's manual loop
+    (src/pymsst/validation/direct_compare.py:350-384): forward and loss under
+    autocast, ``scaler.scale(loss).backward()``, ``scaler.unscale_`` before
+    gradient clipping, ``scaler.step`` / ``scaler.update``.  As there, the
+    ``torch.amp.GradScaler`` is enabled for fp16 autocast (``grad_scaler``
+    None) and off otherwise; bf16 and fp32 steps are plain Adam steps.
+
+    ``flat_params`` (default: on with ``cuda_graph``) makes every parameter a
+    view of one flat fp32 buffer and every gradient a slot of one flat
+    gradient buffer: Adam updates one tensor, and with more than one rank the
+    flat gradients are all-reduced directly (mean over ranks) instead of
+    through DDP, after rank 0's parameters are broadcast to every rank.
+    ``overlap_allreduce`` splits that all-reduce into buckets of about
+    ``bucket_cap_mb`` that start, asynchronously, as soon as the backward has
+    finished every gradient of a bucket; the flat layout is rebuilt after the
+    first backward so each bucket is a contiguous range in the order the
+    gradients become final.
 
     ``cuda_graph=True`` captures the whole training step (forward, backward,
-    gradient all-reduce, Adam) once into a CUDA graph and replays it; the
-    step is then free of per-kernel host launch cost, which otherwise bounds
-    a training step of this size.  The first call runs three untimed
+    gradient all-reduce, scaler and Adam) once into a CUDA graph and replays
+    it; the step is then free of per-kernel host launch cost, which otherwise
+    bounds a training step of this size.  The first call runs three untimed
     forward/backward passes on its batch (no parameter update) so every
     library plan and cached table exists before the capture, initialises the
     Adam state with an update of zero, and then captures; every call,
-    including the first, applies exactly one Adam update.  With more than one
-    rank the graph all-reduces the flattened gradients itself (one NCCL call,
-    mean over ranks) instead of wrapping the model in DDP.  Input shapes must
-    stay fixed; the returned loss tensor is overwritten by the next step."""
+    including the first, applies exactly one update.  Input shapes must stay
+    fixed; the returned loss tensor is overwritten by the next step."""
 
     def __init__(self, model: torch.nn.Module, *, lr: float = 1e-4, amp_dtype: torch.dtype | None = None,
                  grad_clip: float = 0.0, distributed: bool = False, device: torch.device | None = None,
-                 fused_adam: bool = True, bucket_cap_mb: float = 64.0, cuda_graph: bool = False):
+                 fused_adam: bool = True, bucket_cap_mb: float = 64.0, cuda_graph: bool = False,
+                 grad_scaler: bool | None = None, flat_params: bool | None = None, overlap_allreduce: bool = False):
         self.device = device or torch.device("cuda", torch.cuda.current_device())
         self.model = model.to(self.device)
         self.amp_dtype = amp_dtype
@@ -92,55 +111,166 @@ class Trainer:
         self.module = self.model
         self.distributed = distributed
         self.cuda_graph = bool(cuda_graph) and self.device.type == "cuda"
-        if distributed and not self.cuda_graph:
+        on_cuda = self.device.type == "cuda"
+        params = [p for p in self.model.parameters() if p.requires_grad]
+        self.params = params
+        flat = self.cuda_graph if flat_params is None else bool(flat_params)
+        self.flat = flat and bool(params) and all(p.dtype == torch.float32 for p in params)
+        if self.cuda_graph and not self.flat and distributed:
+            raise ValueError("a captured multi-rank step needs fp32 parameters in the flat layout")
+        use_scaler = (amp_dtype == torch.float16) if grad_scaler is None else bool(grad_scaler)
+        self.scaler = torch.amp.GradScaler(self.device.type, enabled=use_scaler)
+        if distributed and not self.flat:
             from torch.nn.parallel import DistributedDataParallel
 
             self.module = DistributedDataParallel(
-                self.model, device_ids=[self.device.index] if self.device.type == "cuda" else None,
+                self.model, device_ids=[self.device.index] if on_cuda else None,
                 bucket_cap_mb=bucket_cap_mb, gradient_as_bucket_view=True, broadcast_buffers=False,
             )
-        params = [p for p in self.model.parameters() if p.requires_grad]
-        self.params = params
-        on_cuda = self.device.type == "cuda"
         self.flat_param = self.flat_grad = self.flat_half = None
         self._half_live = [False]  # True only inside _forward_backward, after the mirror's refresh
+        self.bucket_bytes = int(bucket_cap_mb * 2**20)
+        self.overlap = bool(overlap_allreduce) and distributed and self.flat
+        self._buckets: list[tuple[int, int, list[int]]] = []
+        self._bucket_of: list[int] = []
+        self._pending: list[int] = []
+        self._works: list = []
+        self._launched: list[bool] = []
+        self._relayout_done = not self.overlap
+        self._ready_order: list[int] | None = None
+        self.bucket_launches = 0  # bucketed all-reduces issued so far (host-side count)
+        self._profiling = False
         opt_params = params
-        if self.cuda_graph and params and all(p.dtype == torch.float32 for p in params):
-            # one flat fp32 parameter buffer (the parameters become views of it) and one flat gradient buffer:
-            # Adam then updates a single tensor instead of hundreds of small ones, and the all-reduce works
-            # on the flat gradients in place
-            # every parameter starts on a 128-element boundary (512 bytes fp32, 256 bytes in the 16-bit
-            # mirror below), as a fresh allocation would: libraries pick their kernels by operand alignment,
-            # and a view at an odd offset would get a different (differently rounded) GEMM than the
-            # per-step cast it replaces.  The padding holds zeros, which Adam leaves at zero.
-            offsets = []
-            total = 0
-            for p in params:
-                offsets.append(total)
-                total += (p.numel() + 127) // 128 * 128
-            self.flat_param = torch.zeros(total, dtype=torch.float32, device=self.device)
-            self.flat_grad = torch.zeros(total, dtype=torch.float32, device=self.device)
-            self._grad_views = []
-            with torch.no_grad():
-                for p, off in zip(params, offsets):
-                    n = p.numel()
-                    self.flat_param[off:off + n].copy_(p.reshape(-1))
-                    p.data = self.flat_param[off:off + n].view_as(p)
-                    self._grad_views.append(self.flat_grad[off:off + n].view_as(p))
-            self.flat_param.grad = self.flat_grad
+        if self.flat:
+            self._build_flat(list(range(len(params))))
+            if distributed:
+                # every rank starts from rank 0's parameters (DDP does the same broadcast at construction)
+                dist.broadcast(self.flat_param.data, 0)
             opt_params = [self.flat_param]
-            if amp_dtype in (torch.bfloat16, torch.float16):
-                # the parameters in the activation type, refreshed by one copy kernel per step (the fused ops
-                # read them through fused.lowp_weight instead of casting each weight with its own kernel)
-                self.flat_half = torch.zeros(total, dtype=amp_dtype, device=self.device)
-                for p, off in zip(params, offsets):
-                    p._pmb_half = self.flat_half[off:off + p.numel()].view_as(p)
-                    p._pmb_half_live = self._half_live
+            if self.overlap:
+                for i, p in enumerate(params):
+                    p.register_post_accumulate_grad_hook(self._grad_ready_hook(i))
         self.optimizer = torch.optim.Adam(opt_params, lr=lr, fused=fused_adam and on_cuda,
                                           capturable=self.cuda_graph)
         self._graph = None
         self._static = None
         self.launches_per_step = None  # this package's kernels in one captured step
+
+    # ------------------------------------------------------------- flat layout
+    def _build_flat(self, order: list[int]):
+        """(Re)build the flat fp32 parameter and gradient buffers with the parameters in ``order``.
+
+        Every parameter starts on a 128-element boundary (512 bytes fp32, 256 bytes in the 16-bit mirror), as
+        a fresh allocation would: libraries pick their kernels by operand alignment, and a view at an odd
+        offset would get a different (differently rounded) GEMM than the per-step cast it replaces.  The
+        padding holds zeros, which Adam leaves at zero and the all-reduce averages as zeros."""
+        params = self.params
+        offsets = [0] * len(params)
+        total = 0
+        for i in order:
+            offsets[i] = total
+            total += (params[i].numel() + 127) // 128 * 128
+        flat_param = torch.zeros(total, dtype=torch.float32, device=self.device)
+        flat_grad = torch.zeros(total, dtype=torch.float32, device=self.device)
+        with torch.no_grad():
+            for p, off in zip(params, offsets):
+                flat_param[off:off + p.numel()].copy_(p.reshape(-1))
+        if self.flat_param is None:
+            self.flat_param = torch.nn.Parameter(flat_param)
+        else:
+            self.flat_param.data = flat_param
+        self.flat_grad = flat_grad
+        self.flat_param.grad = flat_grad
+        self._offsets = offsets
+        self._grad_views = []
+        for p, off in zip(params, offsets):
+            n = p.numel()
+            p.data = self.flat_param.data[off:off + n].view_as(p)
+            self._grad_views.append(flat_grad[off:off + n].view_as(p))
+        if self.amp_dtype in (torch.bfloat16, torch.float16) and self.device.type == "cuda":
+            # the parameters in the activation type, refreshed by one copy kernel per step (the fused ops read
+            # them through fused.lowp_weight instead of casting each weight with its own kernel)
+            self.flat_half = torch.zeros(total, dtype=self.amp_dtype, device=self.device)
+            for p, off in zip(params, offsets):
+                p._pmb_half = self.flat_half[off:off + p.numel()].view_as(p)
+                p._pmb_half_live = self._half_live
+        # all-reduce buckets: contiguous ranges of the flat buffer, in layout order
+        self._buckets = []
+        cur: list[int] = []
+        start = 0
+        size = 0
+        for i in order:
+            cur.append(i)
+            size += ((params[i].numel() + 127) // 128 * 128) * 4
+            if size >= self.bucket_bytes:
+                end = offsets[i] + (params[i].numel() + 127) // 128 * 128
+                self._buckets.append((start, end, cur))
+                start, cur, size = end, [], 0
+        if cur:
+            self._buckets.append((start, total, cur))
+        self._bucket_of = [0] * len(params)
+        for b, (_, _, idx) in enumerate(self._buckets):
+            for i in idx:
+                self._bucket_of[i] = b
+
+    def _grad_ready_hook(self, index: int):
+        def hook(p):
+            if self._ready_order is not None:
+                self._ready_order.append(index)
+            if self._relayout_done and self._pending:
+                b = self._bucket_of[index]
+                self._pending[b] -= 1
+                if self._pending[b] == 0:
+                    self._launch_bucket(b)
+        return hook
+
+    def _launch_bucket(self, b: int):
+        start, end, idx = self._buckets[b]
+        pairs = [(self._grad_views[i], self.params[i].grad) for i in idx if self.params[i].grad is not None]
+        if pairs:
+            torch._foreach_copy_([v for v, _ in pairs], [g for _, g in pairs])
+        self._works.append(dist.all_reduce(self.flat_grad[start:end], async_op=True))
+        self._launched[b] = True
+        self.bucket_launches += 1
+
+    def _begin_backward(self):
+        if self.overlap and self._relayout_done and not self._profiling:
+            self._pending = [len(idx) for _, _, idx in self._buckets]
+            self._launched = [False] * len(self._buckets)
+            self._works = []
+
+    def _finish_grads(self):
+        """After the backward: the gradients in the flat buffer, all-reduced (mean) when distributed."""
+        if self.overlap and self._relayout_done and self._pending:
+            for b in range(len(self._buckets)):
+                if not self._launched[b]:  # a bucket with parameters that got no gradient this step
+                    self._launch_bucket(b)
+            for w in self._works:
+                w.wait()
+            self._works = []
+            self._pending = []
+            self.flat_grad.div_(dist.get_world_size())
+            return
+        if self.flat:
+            self._gather_flat_grads()
+        if self.distributed:
+            self._allreduce_grads()
+
+    def _maybe_relayout(self):
+        """First backward with overlap on: lay the flat buffers out in the order the gradients became final."""
+        if self._relayout_done or self._ready_order is None:
+            return
+        seen = []
+        for i in self._ready_order:
+            if i not in seen:
+                seen.append(i)
+        seen += [i for i in range(len(self.params)) if i not in seen]
+        # every rank must use the same layout: take rank 0's order
+        order = torch.tensor(seen, dtype=torch.int64, device=self.device)
+        dist.broadcast(order, 0)
+        self._build_flat([int(i) for i in order.tolist()])
+        self._ready_order = None
+        self._relayout_done = True
 
     # ------------------------------------------------------------- eager
     def _forward_backward(self, mixture, target):
@@ -151,10 +281,11 @@ class Trainer:
                 self.flat_half.copy_(self.flat_param)
             self._half_live[0] = True
         try:
-            with torch.autocast("cuda", dtype=self.amp_dtype or torch.bfloat16, enabled=self.amp_dtype is not None,
-                                cache_enabled=not self.cuda_graph):
+            with torch.autocast(self.device.type, dtype=self.amp_dtype or torch.bfloat16,
+                                enabled=self.amp_dtype is not None, cache_enabled=not self.cuda_graph):
                 loss = self.module(mixture, target)
-            loss.backward()
+            self._begin_backward()
+            self.scaler.scale(loss).backward()
         finally:
             self._half_live[0] = False
         return loss
@@ -166,8 +297,6 @@ class Trainer:
         torch._foreach_copy_([v for v, _ in pairs], [g for _, g in pairs])
 
     def _allreduce_grads(self):
-        import torch.distributed as dist
-
         if self.flat_grad is not None:
             dist.all_reduce(self.flat_grad)
             self.flat_grad.div_(dist.get_world_size())
@@ -182,20 +311,50 @@ class Trainer:
 
     def _update(self):
         if self.grad_clip:
-            if self.flat_param is not None:
-                torch.nn.utils.clip_grad_norm_([self.flat_param], self.grad_clip)
-            else:
-                torch.nn.utils.clip_grad_norm_(self.model.parameters(), self.grad_clip)
-        self.optimizer.step()
+            self.scaler.unscale_(self.optimizer)
+            torch.nn.utils.clip_grad_norm_([self.flat_param] if self.flat else self.model.parameters(),
+                                           self.grad_clip)
+        self.scaler.step(self.optimizer)
+        self.scaler.update()
+
+    def _warm_relayout(self, mixture, target):
+        """One untimed forward/backward that records the order in which gradients become final, then the
+        flat layout in that order (overlap_allreduce only)."""
+        if self._relayout_done:
+            return
+        self._zero_grads()
+        self._ready_order = []
+        self._forward_backward(mixture, target)
+        self._maybe_relayout()
+        self._zero_grads()
 
     def step(self, mixture: torch.Tensor, target: torch.Tensor) -> torch.Tensor:
         """One training step on device tensors; returns the detached loss (device)."""
         if self.cuda_graph:
             return self._graph_step(mixture, target)
-        self.optimizer.zero_grad(set_to_none=True)
+        self._warm_relayout(mixture, target)
+        self._zero_grads()
+        if not self.flat:
+            self.optimizer.zero_grad(set_to_none=True)
         loss = self._forward_backward(mixture, target)
+        self._finish_grads()
         self._update()
         return loss.detach()
+
+    def check_kernels(self) -> None:
+        """Raise if a tensor-core kernel of this package gave up waiting (its outputs would be incomplete).
+
+        Every tcgen05 / TMA wait in the library is bounded; a wait that runs out sets a device flag and the
+        kernel winds down instead of hanging.  Reading the flag synchronises with the device."""
+        from . import _native as nat
+
+        if self.device.type != "cuda":
+            return
+        torch.cuda.synchronize(self.device)
+        code = int(nat.library().pmb_umma_timeout(0))
+        if code:
+            raise nat.KernelError(f"a tensor-core kernel timed out waiting (site code {code:#x}); "
+                                  "the last steps' results are not valid")
 
     # ------------------------------------------------------------- graph
     def _capture(self, mixture, target):
@@ -205,13 +364,11 @@ class Trainer:
         side = torch.cuda.Stream(self.device)
         side.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(side):
+            self._warm_relayout(static_mix, static_tgt)
             for _ in range(3):
                 self._zero_grads()
                 self._forward_backward(static_mix, static_tgt)
-                if self.flat_grad is not None:
-                    self._gather_flat_grads()
-                if self.distributed:
-                    self._allreduce_grads()
+                self._finish_grads()
             # Adam state (moments, device step counters) created by an update of zero
             if self.flat_grad is not None:
                 self.flat_grad.zero_()
@@ -226,18 +383,33 @@ class Trainer:
                         st["step"].zero_()
         torch.cuda.current_stream(self.device).wait_stream(side)
         self._zero_grads()
+        self.check_kernels()
         graph = torch.cuda.CUDAGraph()
         before = nat.library().pmb_launch_count()
         with torch.cuda.graph(graph):
             loss = self._forward_backward(static_mix, static_tgt)
-            if self.flat_grad is not None:
-                self._gather_flat_grads()
-            if self.distributed:
-                self._allreduce_grads()
+            self._finish_grads()
             self._update()
         self.launches_per_step = int(nat.library().pmb_launch_count() - before)
         self._graph = graph
         self._static = (static_mix, static_tgt, loss.detach())
+
+    def profile_graph(self) -> torch.cuda.CUDAGraph:
+        """A second captured graph of this step's forward and backward alone (no collective, no update) on the
+        captured step's static inputs, for per-kernel device timing: entry points called under
+        ``_native.time_entries(..., external=True)`` while it is captured get timing events in the graph."""
+        if self._static is None:
+            raise RuntimeError("profile_graph needs the captured step: run one step first")
+        static_mix, static_tgt, _ = self._static
+        self._zero_grads()
+        graph = torch.cuda.CUDAGraph()
+        self._profiling = True
+        try:
+            with torch.cuda.graph(graph):
+                self._forward_backward(static_mix, static_tgt)
+        finally:
+            self._profiling = False
+        return graph
 
     def _zero_grads(self):
         """Drop the per-parameter gradients (the backward allocates fresh ones); the flat buffer, when there
@@ -257,7 +429,8 @@ class Trainer:
         return loss
 
     def step_host(self, mixture: torch.Tensor, target: torch.Tensor, loss_out: torch.Tensor | None = None):
-        """Step from host tensors (pinned for async copies); the loss is copied back to ``loss_out``."""
+        """Step from host tensors (pinned for async copies); the loss is copied back to ``loss_out``, or
+        returned as a float (after checking the kernels' timeout flag) when no ``loss_out`` is given."""
         if self.cuda_graph and self._static is not None:
             static_mix, static_tgt, _ = self._static
             static_mix.copy_(mixture, non_blocking=True)
@@ -268,18 +441,23 @@ class Trainer:
             tgt = target.to(self.device, non_blocking=True)
             loss = self.step(mix, tgt)
         if loss_out is None:
-            return float(loss)
+            value = float(loss)
+            self.check_kernels()
+            return value
         loss_out.copy_(loss, non_blocking=True)
         return loss_out
 
 
 def run_loss_curve(model: torch.nn.Module, batches, *, lr: float = 1e-4, amp_dtype=None,
-                   device: torch.device | None = None, grad_clip: float = 0.0) -> list[float]:
+                   device: torch.device | None = None, grad_clip: float = 0.0, cuda_graph: bool = False,
+                   grad_scaler: bool | None = None) -> list[float]:
     """Seeded training run; returns the loss of every step (the compare-direct curve)."""
-    trainer = Trainer(model, lr=lr, amp_dtype=amp_dtype, device=device, grad_clip=grad_clip)
+    trainer = Trainer(model, lr=lr, amp_dtype=amp_dtype, device=device, grad_clip=grad_clip, cuda_graph=cuda_graph,
+                      grad_scaler=grad_scaler)
     losses = []
     for mix, tgt in batches:
         losses.append(float(trainer.step(mix.to(trainer.device), tgt.to(trainer.device))))
+    trainer.check_kernels()
     return losses
 
 

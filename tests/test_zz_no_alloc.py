@@ -5,9 +5,10 @@ program binding the C ABI from another language with no device allocator of
 its own, or a training loop that must not allocate mid-step because
 cudaMalloc / cudaFree synchronise the device.  The no-allocation variant keeps
 its scratch in a fixed array inside the library.  These tests call it through
-the C ABI twice in a row (the second call runs on the scratch the first one
-left behind) and compare each result with pmb_rms_norm_backward given a
-caller-allocated workspace, within the tolerances the other RMSNorm tests use.
+the C ABI twice in a row on each case (the second call runs on the scratch the
+first one left behind) and compare each result with pmb_rms_norm_backward
+given a caller-allocated workspace, within the tolerances the other RMSNorm
+tests use; two of the cases fill the array to its last element.
 
 This file is collected last (tests/test_zz_*), so a run that stops at the
 first failure has already run every other test.
@@ -37,7 +38,11 @@ def _noalloc(dy, saved, saved_is_input, inv, gamma, grad_x_dtype, grad_gamma_dty
 
 @pytest.mark.gpu
 def test_noalloc_backward_matches_workspace_version_twice(cuda_device):
-    cases = [(4096, 192, torch.bfloat16, True), (777, 384, torch.float32, False)]
+    # (rows, dim, dtype, saved is the input).  The last two fill the scratch array exactly: dim 1024 with enough
+    # rows for the largest backward grid (592 blocks), each block writing a full 1024-float partial row of
+    # grad_gamma.
+    cases = [(4096, 192, torch.bfloat16, True), (777, 384, torch.float32, False), (8192, 1024, torch.float32, False),
+             (6000, 1024, torch.bfloat16, True)]
     for seed, (rows, dim, dtype, from_input) in enumerate(cases):
         g = torch.Generator().manual_seed(100 + seed)
         x = (torch.randn(rows, dim, generator=g) * 3).to(dtype).to(cuda_device)
@@ -50,11 +55,15 @@ def test_noalloc_backward_matches_workspace_version_twice(cuda_device):
         saved = x if from_input else normed
         ref_gx, ref_gg = rms_norm_backward_into(dy, saved, inv, gamma, saved_is_input=from_input, grad_x_dtype=dtype,
                                                 grad_gamma_dtype=torch.float32)
-        gx, gg = _noalloc(dy, saved, from_input, inv, gamma, dtype, torch.float32)
-        torch.cuda.synchronize()
         rtol, atol = TOL[dtype]
-        torch.testing.assert_close(gx.double().cpu(), ref_gx.double().cpu(), rtol=rtol, atol=atol)
-        torch.testing.assert_close(gg.double().cpu(), ref_gg.double().cpu(), rtol=1e-4, atol=1e-3)
+        for call in range(2):  # the second call runs on the scratch contents the first one left behind
+            gx, gg = _noalloc(dy, saved, from_input, inv, gamma, dtype, torch.float32)
+            torch.cuda.synchronize()
+            msg = f"rows={rows} dim={dim} {dtype} call {call}"
+            torch.testing.assert_close(gx.double().cpu(), ref_gx.double().cpu(), rtol=rtol, atol=atol,
+                                       msg=lambda m: f"{msg}: {m}")
+            torch.testing.assert_close(gg.double().cpu(), ref_gg.double().cpu(), rtol=1e-4, atol=1e-3,
+                                       msg=lambda m: f"{msg}: {m}")
 
 
 def test_noalloc_rejects_dims_beyond_its_scratch():
