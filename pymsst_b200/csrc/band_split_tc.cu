@@ -54,6 +54,8 @@ constexpr int kThreads = 256;
 constexpr int kRowAlign = 8;     // x row stride alignment in elements (16 bytes)
 constexpr int kMaxGroupBands = 8;
 constexpr int kMaxGroupN = 1536;
+constexpr int kBiasRows = 32;  // rows per bias-gradient partial sum
+inline int bias_chunks(int64_t rows) { return (int)((rows + kBiasRows - 1) / kBiasRows); }
 
 struct Layout {
   int nb, ng, O, total, kpmax, n_total;
@@ -63,6 +65,8 @@ struct Layout {
   int a[kMaxBands];        // first column of group g's k-range (multiple of 8)
   int kp[kMaxBands];       // k extent of group g (multiple of 64)
   int row[kMaxBands + 1];  // first row of group g in the packed weight [n_total, kpmax]
+  int gof[kMaxBands];           // weight group of band b
+  int pack_cta[kMaxBands + 1];  // first packing CTA of band b (a CTA packs up to 8 k-chunks of 8 columns)
 };
 
 Layout make_layout(int nb, const int64_t* widths, int O) {
@@ -99,6 +103,12 @@ Layout make_layout(int nb, const int64_t* widths, int O) {
   L.first[L.ng] = nb;
   L.row[L.ng] = rows;
   L.n_total = rows;
+  L.pack_cta[0] = 0;
+  for (int g = 0; g < L.ng; ++g)
+    for (int b = L.first[g]; b < L.first[g + 1]; ++b) {
+      L.gof[b] = g;
+      L.pack_cta[b + 1] = L.pack_cta[b] + (L.kp[g] / 8 + 7) / 8;
+    }
   return L;
 }
 
@@ -164,29 +174,39 @@ __global__ void __launch_bounds__(kThreads)
     }
     return;
   }
-  // packing: the groups' [rows_g, kp_g] blocks, 8 columns per thread
-  const int64_t e8 = ((int64_t)blockIdx.x - row_ctas) * kThreads + threadIdx.x;
-  int64_t base = 0;
-  int g = 0;
-  for (; g < L.ng; ++g) {
-    const int64_t sz = (int64_t)(L.row[g + 1] - L.row[g]) * (L.kp[g] / 8);
-    if (e8 < base + sz) break;
-    base += sz;
+  // packing: CTA = (band b, up to 8 consecutive 8-column k-chunks of its group's k-range); thread = (chunk,
+  // one of 32 row lanes) over the band's O weight rows, so a warp reads four 8-column W row segments and
+  // writes four 16-byte-aligned 128-byte packed row segments
+  const int cta = (int)blockIdx.x - row_ctas;
+  int lo = 0, hi = L.nb - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (L.pack_cta[mid] <= cta) lo = mid; else hi = mid - 1;
   }
-  if (g >= L.ng) return;
-  const int64_t local = e8 - base;
-  const int kq = L.kp[g] / 8;
-  const int n = (int)(local / kq), k0 = (int)(local % kq) * 8;
-  const int b = L.first[g] + n / L.O, o = n % L.O;
-  const TP* W = static_cast<const TP*>(tab.ptr1[b]);
+  const int b = lo, g = L.gof[b];
+  const int c = (cta - L.pack_cta[b]) * 8 + (threadIdx.x & 7);
+  if (c >= L.kp[g] / 8) return;
+  const int wb = L.w[b];
+  const int i0 = L.a[g] + 8 * c - L.off[b];  // band feature of this chunk's first column
+  const TP* Wb = static_cast<const TP*>(tab.ptr1[b]);
   const TP* gm = static_cast<const TP*>(tab.ptr0[b]);
-  alignas(16) T vals[8];
+  T* dst = packed + (int64_t)(L.row[g] + (b - L.first[g]) * L.O) * L.kpmax + 8 * c;
+  float gv[8];
+  unsigned inb = 0;  // bit j: column j of the chunk is a feature of band b
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    const int i = L.a[g] + k0 + j - L.off[b];
-    vals[j] = Elem<T>::from_f(i >= 0 && i < L.w[b] ? Elem<TP>::to_f(W[(int64_t)o * L.w[b] + i]) * Elem<TP>::to_f(gm[i]) : 0.f);
+    const bool in = i0 + j >= 0 && i0 + j < wb;
+    inb |= (unsigned)in << j;
+    gv[j] = in ? Elem<TP>::to_f(gm[i0 + j]) : 0.f;
   }
-  *reinterpret_cast<uint4*>(packed + (int64_t)(L.row[g] + n) * L.kpmax + k0) = *reinterpret_cast<const uint4*>(vals);
+  for (int o = threadIdx.x >> 3; o < L.O; o += kThreads / 8) {
+    const TP* Wr = Wb + (int64_t)o * wb;
+    alignas(16) T vals[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      vals[j] = Elem<T>::from_f((inb >> j) & 1u ? Elem<TP>::to_f(Wr[i0 + j]) * gv[j] : 0.f);
+    *reinterpret_cast<uint4*>(dst + (int64_t)o * L.kpmax) = *reinterpret_cast<const uint4*>(vals);
+  }
 }
 
 // out[m, b, o] = s[m, b] * sqrt(w_b) * acc + bias_b[o] for the group's bands (one band per 32-column chunk).
@@ -200,21 +220,35 @@ struct BandOutEpi {
   const void* bias[kMaxBands];
   template <int BN>
   __device__ void run(const ugemm::Plan&, const ugemm::TileCtx& t) const {
+    constexpr int kMaxChunks = (BN / 32 + ugemm::kSubs - 1) / ugemm::kSubs;
     const int lane = threadIdx.x & 31;
     const int64_t ld = (int64_t)nb * O;
-#pragma unroll 1
-    for (int c0 = 32 * t.sub; c0 < BN; c0 += 32 * ugemm::kSubs) {
-      if (c0 >= t.n_valid) break;
+    // scale and bias of every chunk this warp drains, loaded before the first tensor-memory read so their
+    // latencies overlap (one round trip per tile instead of one per chunk)
+    float sc[kMaxChunks], bl[kMaxChunks];
+#pragma unroll
+    for (int q = 0; q < kMaxChunks; ++q) {
+      const int c0 = 32 * (t.sub + q * ugemm::kSubs);
+      sc[q] = bl[q] = 0.f;
+      if (c0 < BN && c0 < t.n_valid) {
+        const int n = t.n0 + c0;
+        const int b = first[t.group] + n / O, o0 = n % O;
+        const TP* bp = static_cast<const TP*>(bias[b]);
+        sc[q] = t.row_valid ? inv[(int64_t)t.row * nb + b] * sqrt_w[b] : 0.f;
+        bl[q] = (bp != nullptr && lane < t.n_valid - c0) ? Elem<TP>::to_f(bp[o0 + lane]) : 0.f;
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < kMaxChunks; ++q) {
+      const int c0 = 32 * (t.sub + q * ugemm::kSubs);
+      if (c0 >= BN || c0 >= t.n_valid) break;
       const int ncols = min(32, t.n_valid - c0);
       const int n = t.n0 + c0;
       const int b = first[t.group] + n / O, o0 = n % O;
       float v[32];
       umma::tmem_ld32(t.taddr + c0, v);
-      const float sc = t.row_valid ? inv[(int64_t)t.row * nb + b] * sqrt_w[b] : 0.f;
-      const TP* bp = static_cast<const TP*>(bias[b]);
-      const float bl = (bp != nullptr && lane < ncols) ? Elem<TP>::to_f(bp[o0 + lane]) : 0.f;
 #pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = fmaf(v[j], sc, __shfl_sync(0xffffffffu, bl, j));
+      for (int j = 0; j < 32; ++j) v[j] = fmaf(v[j], sc[q], __shfl_sync(0xffffffffu, bl[q], j));
       ugemm::warp_store<T>(t.stage, v, out + (int64_t)t.row0 * ld + (int64_t)b * O + o0, ld, t.rows_valid, ncols);
     }
   }
@@ -264,10 +298,18 @@ __global__ void __launch_bounds__(kThreads)
   const int64_t chunk = bid / col_blocks;
   const int64_t c = (bid % col_blocks) * kThreads + threadIdx.x;
   if (c >= cols) return;
-  const int64_t r0 = chunk * red::kRowsPerChunk;
-  const int64_t r1 = r0 + red::kRowsPerChunk < rows ? r0 + red::kRowsPerChunk : rows;
+  const int64_t r0 = chunk * kBiasRows;
+  const int64_t r1 = r0 + kBiasRows < rows ? r0 + kBiasRows : rows;
+  // eight rows in flight per step (independent loads), summed in a fixed order
   float s = 0.f;
-  for (int64_t r = r0; r < r1; ++r) s += Elem<T>::to_f(dy[r * cols + c]);
+  int64_t r = r0;
+  for (; r + 8 <= r1; r += 8) {
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = Elem<T>::to_f(dy[(r + j) * cols + c]);
+    s += ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
+  }
+  for (; r < r1; ++r) s += Elem<T>::to_f(dy[r * cols + c]);
   bpart[chunk * cols + c] = s;
 }
 
@@ -296,21 +338,29 @@ struct WGradBandEpi {
       if (c0 >= t.n_valid || i0 >= wb) break;
       const int i = i0 + lane;
       const bool col_ok = i >= 0 && i < wb;
-      float v[32];
-      umma::tmem_ld32(t.taddr + c0, v);
-      // W rows of this warp, column i per lane (through the staging block: row r, lane = column)
-      float* st = reinterpret_cast<float*>(t.stage + lane * ugemm::kStageRowBytes);
+      {
+        // transpose G through the staging block: row r = output o = row0 + r, column lane
+        float v[32];
+        umma::tmem_ld32(t.taddr + c0, v);
+        float* st = reinterpret_cast<float*>(t.stage + lane * ugemm::kStageRowBytes);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) st[j] = v[j];  // G, this lane's row o = row0 + lane, columns i0 .. i0 + 31
+        for (int j = 0; j < 32; ++j) st[j] = v[j];
+      }
       __syncwarp();
+      // lane = feature column i: the warp's W rows, 16 loaded together at a time (coalesced along i)
       const float gl = col_ok ? Elem<TP>::to_f(gm[i]) : 0.f;
       float s = 0.f;
-      for (int r = 0; r < t.rows_valid; ++r) {
-        const float g = reinterpret_cast<const float*>(t.stage + r * ugemm::kStageRowBytes)[lane];
-        if (col_ok) {
-          const int64_t idx = (int64_t)(t.row0 + r) * wb + i;
-          s = fmaf(Elem<TP>::to_f(W[idx]), g, s);
-          gW[idx] = Elem<TP>::from_f(g * gl);
+#pragma unroll
+      for (int h = 0; h < 32; h += 16) {
+        float wr[16];
+#pragma unroll
+        for (int r = 0; r < 16; ++r)
+          wr[r] = (col_ok && h + r < t.rows_valid) ? Elem<TP>::to_f(W[(int64_t)(t.row0 + h + r) * wb + i]) : 0.f;
+#pragma unroll
+        for (int r = 0; r < 16; ++r) {
+          const float g = reinterpret_cast<const float*>(t.stage + (h + r) * ugemm::kStageRowBytes)[lane];
+          s = fmaf(wr[r], g, s);
+          if (col_ok && h + r < t.rows_valid) gW[(int64_t)(t.row0 + h + r) * wb + i] = Elem<TP>::from_f(g * gl);
         }
       }
       if (col_ok && t.rows_valid > 0) gpart[(int64_t)(t.row0 / 32) * total + off[b] + i] = s;
@@ -319,31 +369,43 @@ struct WGradBandEpi {
   }
 };
 
-// grad_gamma_b[i] = sum_q gpart[q][off_b + i] for the first `total` threads; grad_bias_b[o] = sum over chunks of
-// bpart[chunk][b * O + o] for the next nb * O.
+// CTAs [0, gamma_ctas): grad_gamma_b[i] = sum_q gpart[q][off_b + i], one column per thread.
+// Other CTAs: grad_bias_b[o] = sum over chunks of bpart[chunk][b * O + o]: 32 columns per CTA, eight threads per
+// column each summing every eighth chunk, combined in shared memory in a fixed order.
 template <typename TP>
 __global__ void __launch_bounds__(kThreads)
     bs_finalize(const float* __restrict__ gpart, int nq, const float* __restrict__ bpart, int nchunks, Layout L,
-             BandTable gtab, BandTable btab) {
-  const int64_t c = (int64_t)blockIdx.x * kThreads + threadIdx.x;
-  if (c < L.total) {
+                int gamma_ctas, BandTable gtab, BandTable btab) {
+  if ((int)blockIdx.x < gamma_ctas) {
+    const int64_t c = (int64_t)blockIdx.x * kThreads + threadIdx.x;
+    if (c >= L.total) return;
     int lo = 0, hi = L.nb - 1;
     while (lo < hi) {
       const int mid = (lo + hi + 1) >> 1;
       if (L.off[mid] <= c) lo = mid; else hi = mid - 1;
     }
     float s = 0.f;
+#pragma unroll 8
     for (int q = 0; q < nq; ++q) s += gpart[(int64_t)q * L.total + c];
     static_cast<TP*>(const_cast<void*>(gtab.ptr0[lo]))[c - L.off[lo]] = Elem<TP>::from_f(s);
     return;
   }
+  __shared__ float part[8][33];
   const int64_t cols = (int64_t)L.nb * L.O;
-  const int64_t k = c - L.total;
-  if (k >= cols || btab.ptr0[0] == nullptr) return;
+  const int cl = threadIdx.x & 31, pl = threadIdx.x >> 5;
+  const int64_t k = ((int64_t)blockIdx.x - gamma_ctas) * 32 + cl;
   float s = 0.f;
-  for (int q = 0; q < nchunks; ++q) s += bpart[(int64_t)q * cols + k];
-  const int b = (int)(k / L.O);
-  static_cast<TP*>(const_cast<void*>(btab.ptr0[b]))[k - (int64_t)b * L.O] = Elem<TP>::from_f(s);
+  if (k < cols)
+    for (int q = pl; q < nchunks; q += 8) s += bpart[(int64_t)q * cols + k];
+  part[pl][cl] = s;
+  __syncthreads();
+  if (pl == 0 && k < cols && btab.ptr0[0] != nullptr) {
+    float t = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) t += part[j][cl];
+    const int b = (int)(k / L.O);
+    static_cast<TP*>(const_cast<void*>(btab.ptr0[b]))[k - (int64_t)b * L.O] = Elem<TP>::from_f(t);
+  }
 }
 
 int64_t align256(int64_t v) { return (v + 255) & ~(int64_t)255; }
@@ -359,7 +421,7 @@ Sizes sizes_of(int64_t rows, const Layout& L, int es) {
   const int64_t ld = (L.total + kRowAlign - 1) / kRowAlign * kRowAlign;
   z.ws_gpart = align256(rows * ld * es);
   z.ws_bpart = z.ws_gpart + align256((int64_t)((L.O + 31) / 32) * L.total * 4);
-  z.ws_bytes = z.ws_bpart + align256((int64_t)red::chunks(rows) * L.nb * L.O * 4);
+  z.ws_bytes = z.ws_bpart + align256((int64_t)bias_chunks(rows) * L.nb * L.O * 4);
   return z;
 }
 
@@ -381,9 +443,7 @@ template <typename T, typename TP, int CH>
 int launch_prep_forward(const T* x, int64_t rows, int64_t ld, const BandTable& tab, const Layout& L, float* inv,
                         T* packed, cudaStream_t s, const char* name) {
   const int row_ctas = (int)(rows < (int64_t)num_sms() * 8 ? rows : (int64_t)num_sms() * 8);
-  int64_t pack_items = 0;
-  for (int g = 0; g < L.ng; ++g) pack_items += (int64_t)(L.row[g + 1] - L.row[g]) * (L.kp[g] / 8);
-  const int pack_ctas = (int)((pack_items + kThreads - 1) / kThreads);
+  const int pack_ctas = L.pack_cta[L.nb];
   const size_t smem = (size_t)(L.total / CH) * sizeof(float);
   auto kern = bs_prep_forward<T, TP, CH>;
   if (smem > 48 * 1024) PMB_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem), name);
@@ -397,7 +457,7 @@ int launch_prep_backward(const T* x, int64_t rows, int64_t ld, const float* inv,
                          int64_t nld, const T* dy, float* bpart, cudaStream_t s, const char* name) {
   const int row_ctas = (int)(rows < (int64_t)num_sms() * 8 ? rows : (int64_t)num_sms() * 8);
   const int64_t cols = (int64_t)L.nb * L.O;
-  const int64_t bias_ctas = bpart ? ((cols + kThreads - 1) / kThreads) * red::chunks(rows) : 0;
+  const int64_t bias_ctas = bpart ? ((cols + kThreads - 1) / kThreads) * bias_chunks(rows) : 0;
   const size_t smem = (size_t)L.nb * sizeof(float) + (size_t)(L.total / CH) * sizeof(int);
   auto kern = bs_prep_backward<T, CH>;
   if (smem > 48 * 1024) PMB_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem), name);
@@ -578,9 +638,10 @@ extern "C" int pmb_band_split_tc_backward(const void* grad_out, const void* x, i
       }
       st2 = run_gemm<BN, true, true>(ma, mb, plan, epi, fp16, s, name);
       if (st2) return st2;
-      const int64_t items = L.total + (int64_t)num_bands * out_features;
-      bs_finalize<TP><<<(unsigned)((items + kThreads - 1) / kThreads), kThreads, 0, s>>>(
-          gpart, (int)((out_features + 31) / 32), bpart, red::chunks(rows), L, gtab, btab);
+      const int gamma_ctas = (L.total + kThreads - 1) / kThreads;
+      const int64_t bias_ctas = grad_biases ? ((int64_t)num_bands * out_features + 31) / 32 : 0;
+      bs_finalize<TP><<<(unsigned)(gamma_ctas + bias_ctas), kThreads, 0, s>>>(
+          gpart, (int)((out_features + 31) / 32), bpart, bias_chunks(rows), L, gamma_ctas, gtab, btab);
       PMB_CHECK_LAUNCH(name);
       return PMB_OK;
     }

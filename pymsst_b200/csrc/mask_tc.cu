@@ -17,6 +17,7 @@
 // per forward (one launch per layer) and reused by the backward.
 // Reference semantics: src/pymsst/training/cuda/fused_band_split.cu:1006-1074,
 // :2284-2367, :2516-2851; fused_roformer.py:527-583.
+#include <algorithm>
 #include <vector>
 
 #include "gemm_umma.cuh"
@@ -32,6 +33,8 @@ constexpr int kThreads = 256;
 constexpr int BN = 128;
 constexpr int STAGES = 4;
 constexpr int kChunk = 64;  // GLU outputs per 128-column tile
+constexpr int kGluRows = 16;  // rows per GLU-backward thread (and per partial row of the final bias gradient)
+inline int glu_chunks(int64_t rows) { return (int)((rows + kGluRows - 1) / kGluRows); }
 
 struct BandInfo {
   int nb;
@@ -252,17 +255,24 @@ __global__ void __launch_bounds__(kThreads)
   const int l = c * kChunk + (j % kChunk);
   const bool valid = l < info.w[b];
   const int64_t pl = info.pbase[b] + c * 128 + (j % kChunk);  // left slot column
-  const int64_t r0 = (int64_t)blockIdx.y * red::kRowsPerChunk;
-  const int64_t r1 = r0 + red::kRowsPerChunk < rows ? r0 + red::kRowsPerChunk : rows;
+  const int64_t r0 = (int64_t)blockIdx.y * kGluRows;
   float acc = 0.f;
-  for (int64_t r = r0; r < r1; ++r) {
-    float v = 0.f;
-    if (valid) {
-      const float a = Elem<T>::to_f(pre[r * P + pl]);
-      const float s = sigm(Elem<T>::to_f(pre[r * P + pl + kChunk]));
-      const float g = Elem<T>::to_f(dy[r * total + info.off[b] + l]);
-      v = is_gate ? g * a * s * (1.0f - s) : g * s;
-    }
+  // all kGluRows rows' loads issued together (one memory round trip per thread)
+  float a[kGluRows], gt[kGluRows], g[kGluRows];
+#pragma unroll
+  for (int j = 0; j < kGluRows; ++j) {
+    const int64_t r = r0 + j;
+    const bool ok = valid && r < rows;
+    a[j] = ok ? Elem<T>::to_f(pre[r * P + pl]) : 0.f;
+    gt[j] = ok ? Elem<T>::to_f(pre[r * P + pl + kChunk]) : 0.f;
+    g[j] = ok ? Elem<T>::to_f(dy[r * total + info.off[b] + l]) : 0.f;
+  }
+#pragma unroll
+  for (int j = 0; j < kGluRows; ++j) {
+    const int64_t r = r0 + j;
+    if (r >= rows) break;
+    const float s = sigm(gt[j]);
+    const float v = valid ? (is_gate ? g[j] * a[j] * s * (1.0f - s) : g[j] * s) : 0.f;
     gp[r * P + p] = Elem<T>::from_f(v);
     acc += v;
   }
@@ -286,7 +296,11 @@ __global__ void __launch_bounds__(kThreads)
   const int l = c * kChunk + (j % kChunk);
   if (l >= info.w[b]) return;
   float s = 0.f;
-  for (int k = 0; k < chunks; ++k) s += partial[(int64_t)k * P + p];
+  int k = 0;
+  for (; k + 4 <= chunks; k += 4)
+    s += (partial[(int64_t)k * P + p] + partial[(int64_t)(k + 1) * P + p]) +
+         (partial[(int64_t)(k + 2) * P + p] + partial[(int64_t)(k + 3) * P + p]);
+  for (; k < chunks; ++k) s += partial[(int64_t)k * P + p];
   TP* dst = static_cast<TP*>(const_cast<void*>(gb.ptr0[b]));
   dst[j < kChunk ? l : info.w[b] + l] = Elem<TP>::from_f(s);
 }
@@ -346,18 +360,22 @@ Layout make_layout(int64_t rows, int nb, int64_t dim, int64_t hidden, int L, con
   y.ws_da = align256(rows * P * 2);
   y.ws_db = y.ws_da + align256(rows * nb * wide * 2);
   y.ws_partial = y.ws_db + align256(rows * nb * wide * 2);
-  const int64_t pcols = P > nb * wide ? P : nb * wide;
-  y.ws_bytes = y.ws_partial + align256((int64_t)red::chunks(rows) * pcols * 4);
+  const int64_t partial_floats = std::max((int64_t)glu_chunks(rows) * P, (int64_t)red::chunks(rows) * nb * wide);
+  y.ws_bytes = y.ws_partial + align256(partial_floats * 4);
   return y;
 }
 
-template <class Epi, bool A_MN, bool B_MN>
+// N tile width per GEMM: 256 where N is the 768-wide hidden layer (A tiles then read 3 rather than 6 times,
+// and the epilogue's 8 column chunks spread 3 / 3 / 2 over the warps of a lane quarter), 192 for the
+// 192-wide model dimension, 128 for the GLU layer (one 64-output chunk and its gates per tile).
+template <int BNT, class Epi, bool A_MN, bool B_MN>
 int run_gemm(const CUtensorMap& ma, const CUtensorMap& mb, ugemm::Plan& plan, const Epi& epi, int fp16,
              cudaStream_t s, const char* name) {
-  const int tiles = ugemm::build_plan(plan, BN);
+  constexpr int NST = BNT >= 256 ? 3 : STAGES;
+  const int tiles = ugemm::build_plan(plan, BNT);
   if (tiles == 0) return PMB_OK;
-  auto kern = ugemm::umma_gemm_kernel<BN, STAGES, A_MN, B_MN, Epi>;
-  const int smem = ugemm::smem_bytes<BN, STAGES>();
+  auto kern = ugemm::umma_gemm_kernel<BNT, NST, A_MN, B_MN, Epi>;
+  const int smem = ugemm::smem_bytes<BNT, NST>();
   PMB_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem), name);
   kern<<<ugemm::persistent_grid(tiles), ugemm::kThreads, smem, s>>>(ma, mb, plan, epi, fp16);
   PMB_CHECK_LAUNCH(name);
@@ -398,7 +416,8 @@ int forward_impl(const void* x, const Layout& y, const void* const* weights, con
     ugemm::Plan plan;
     plan.num_groups = y.nb;
     if (!final) {
-      st = tma::make_map_3d(mb, pk, dtype, in_w, y.nb, y.hidden, y.hidden * in_w * 2, in_w * 2, 64, 1, BN, name);
+      const int hbn = y.hidden % 256 == 0 ? 256 : BN;
+      st = tma::make_map_3d(mb, pk, dtype, in_w, y.nb, y.hidden, y.hidden * in_w * 2, in_w * 2, 64, 1, hbn, name);
       if (st) return st;
       // the packed hidden weight is [nb, H, in_w]: mid = band stride H*in_w, outer = row stride in_w
       for (int b = 0; b < y.nb; ++b) plan.g[b] = ugemm::Group{(int)y.rows, (int)y.hidden, (int)in_w, 0, b, 0, 0, b, 0};
@@ -407,7 +426,8 @@ int forward_impl(const void* x, const Layout& y, const void* const* weights, con
       epi.ld = (int64_t)y.nb * y.hidden;
       epi.h = (int)y.hidden;
       for (int b = 0; b < y.nb; ++b) epi.bias[b] = biases[(int64_t)l * y.nb + b];
-      st = run_gemm<TanhEpi<T, TP>, false, false>(ma, mb, plan, epi, fp16, s, name);
+      st = hbn == 256 ? run_gemm<256, TanhEpi<T, TP>, false, false>(ma, mb, plan, epi, fp16, s, name)
+                      : run_gemm<BN, TanhEpi<T, TP>, false, false>(ma, mb, plan, epi, fp16, s, name);
       if (st) return st;
       in = epi.out;
       pk += (int64_t)y.nb * y.hidden * in_w;
@@ -426,7 +446,7 @@ int forward_impl(const void* x, const Layout& y, const void* const* weights, con
       epi.ld_pre = y.P;
       epi.info = info;
       for (int b = 0; b < y.nb; ++b) epi.info.bias[b] = biases[(int64_t)l * y.nb + b];
-      st = run_gemm<GluEpi<T, TP>, false, false>(ma, mb, plan, epi, fp16, s, name);
+      st = run_gemm<BN, GluEpi<T, TP>, false, false>(ma, mb, plan, epi, fp16, s, name);
       if (st) return st;
     }
   }
@@ -461,7 +481,7 @@ int backward_impl(const void* grad_out, const void* x, const void* acts, const v
   }
   // 1) GLU backward + final bias gradient
   {
-    dim3 g((unsigned)((y.P + kThreads - 1) / kThreads), chunks);
+    dim3 g((unsigned)((y.P + kThreads - 1) / kThreads), glu_chunks(y.rows));
     glu_bwd_packed<T><<<g, kThreads, 0, s>>>(static_cast<const T*>(grad_out), static_cast<const T*>(pre), y.rows,
                                              y.total, y.P, info, gp, partial);
     PMB_CHECK_LAUNCH(name);
@@ -470,8 +490,8 @@ int backward_impl(const void* grad_out, const void* x, const void* acts, const v
     int st = make_band_table(gb, y.nb, ones.data(), (const void* const*)(grad_biases + (int64_t)y.L * y.nb), nullptr,
                              nullptr, name);
     if (st) return st;
-    glu_bias_finalize<TP><<<(unsigned)((y.P + kThreads - 1) / kThreads), kThreads, 0, s>>>(partial, chunks, y.P, info,
-                                                                                           gb);
+    glu_bias_finalize<TP><<<(unsigned)((y.P + kThreads - 1) / kThreads), kThreads, 0, s>>>(
+        partial, glu_chunks(y.rows), y.P, info, gb);
     PMB_CHECK_LAUNCH(name);
   }
   // 2) final weight gradient: dWf_b = gp_b^T h_b   (M = packed rows, N = hin, K = rows)
@@ -492,7 +512,8 @@ int backward_impl(const void* grad_out, const void* x, const void* acts, const v
       plan.g[b] = ugemm::Group{pb, (int)hin, (int)y.rows, info.pbase[b], 0, 0, 0, b, 0};
       epi.info.grad[b] = grad_weights[(int64_t)y.L * y.nb + b];
     }
-    st = run_gemm<WGradEpi<TP>, true, true>(ma, mb, plan, epi, fp16, s, name);
+    st = hin % 256 == 0 ? run_gemm<256, WGradEpi<TP>, true, true>(ma, mb, plan, epi, fp16, s, name)
+                        : run_gemm<BN, WGradEpi<TP>, true, true>(ma, mb, plan, epi, fp16, s, name);
     if (st) return st;
   }
   // 3) dH = gp_b Wf_b (M = rows, N = hin, K = packed rows), tanh' fused
@@ -516,7 +537,8 @@ int backward_impl(const void* grad_out, const void* x, const void* acts, const v
     epi.y = y.L > 0 ? h_last : nullptr;
     epi.ld = (int64_t)y.nb * hin;
     epi.h = (int)hin;
-    st = run_gemm<DActEpi<T>, false, true>(ma, mb, plan, epi, fp16, s, name);
+    st = hin % 256 == 0 ? run_gemm<256, DActEpi<T>, false, true>(ma, mb, plan, epi, fp16, s, name)
+                        : run_gemm<BN, DActEpi<T>, false, true>(ma, mb, plan, epi, fp16, s, name);
     if (st) return st;
   }
   // 4) hidden layers, last to first: dcur holds d(pre-activation) of layer l
@@ -556,7 +578,8 @@ int backward_impl(const void* grad_out, const void* x, const void* acts, const v
         plan.g[b] = ugemm::Group{(int)y.hidden, (int)lin, (int)y.rows, 0, b, 0, 0, b, 0};
         epi.info.grad[b] = grad_weights[(int64_t)l * y.nb + b];
       }
-      st = run_gemm<WGradEpi<TP>, true, true>(ma, mb, plan, epi, fp16, s, name);
+      st = lin % 192 == 0 ? run_gemm<192, WGradEpi<TP>, true, true>(ma, mb, plan, epi, fp16, s, name)
+                          : run_gemm<BN, WGradEpi<TP>, true, true>(ma, mb, plan, epi, fp16, s, name);
       if (st) return st;
     }
     // input gradient: dX_b = dcur_b W_b (M = rows, N = lin, K = H), tanh' of the layer below fused
@@ -578,7 +601,8 @@ int backward_impl(const void* grad_out, const void* x, const void* acts, const v
       epi.y = l > 0 ? lx : nullptr;
       epi.ld = (int64_t)y.nb * lin;
       epi.h = (int)lin;
-      st = run_gemm<DActEpi<T>, false, true>(ma, mb, plan, epi, fp16, s, name);
+      st = lin % 192 == 0 ? run_gemm<192, DActEpi<T>, false, true>(ma, mb, plan, epi, fp16, s, name)
+                          : run_gemm<BN, DActEpi<T>, false, true>(ma, mb, plan, epi, fp16, s, name);
       if (st) return st;
       dcur = next;
     }

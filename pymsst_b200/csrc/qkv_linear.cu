@@ -8,8 +8,10 @@
 // the stored projection of the unfused path) and rotates the interleaved pairs
 // by the row's position angle; the angle tables are passed transposed
 // ([Dh/2, N]) so the 32 rows of a warp read 32 consecutive positions of one
-// pair (coalesced) instead of 32 scattered table rows.  Stores are 16-byte
-// row vectors.  The projection is written once and never re-read for a split
+// pair (coalesced) instead of 32 scattered table rows, and each epilogue warp
+// keeps the 16 angle pairs of its head half in registers across the chunks
+// it drains (see the chunk map in QkvRotaryEpi).  Stores are 16-byte row
+// vectors.  The projection is written once and never re-read for a split
 // or rotary pass; the backward is pmb_qkv_rotary_merge plus the two
 // projection-gradient GEMMs.
 // Reference semantics: to_qkv projection + qkv_to_bnhd + rotary_forward on
@@ -35,24 +37,45 @@ struct QkvRotaryEpi {
     const int q_ = t.row / inner, ii = t.row - q_ * inner;
     const int o = q_ / seq, pos = q_ - o * seq;
     const int64_t prow = (int64_t)(o * inner + ii) * seq + pos;
+    // Chunk -> warp map: with eight 32-column chunks per tile (BN = 256, 64-wide heads) the first warp of a lane
+    // quarter takes the even chunks 0, 2, 4 (pairs 0..15 of a head), the second the odd chunks 1, 3, 5 (pairs
+    // 16..31), the third chunks 6 and 7; so the first two read their 32 angle values once per tile and keep them
+    // in registers.  Other widths use the round-robin map.
+    constexpr int kNch = BN / 32;
+    constexpr bool kPaired = kNch == 8;
+    const int nmine = kPaired ? (t.sub < 2 ? 3 : 2) : (kNch - t.sub + ugemm::kSubs - 1) / ugemm::kSubs;
+    float cc[16], sn[16];
+    int cached = -1;
 #pragma unroll 1
-    for (int c0 = 32 * t.sub; c0 < BN; c0 += 32 * ugemm::kSubs) {
-      if (c0 >= t.n_valid) break;
+    for (int q = 0; q < nmine; ++q) {
+      const int chunk = kPaired ? (t.sub < 2 ? t.sub + 2 * q : 6 + q) : t.sub + q * ugemm::kSubs;
+      const int c0 = 32 * chunk;
+      if (c0 >= t.n_valid) continue;
       const int ncols = min(32, t.n_valid - c0);
-      float v[32];
-      umma::tmem_ld32(t.taddr + c0, v);
       const int n = t.n0 + c0;
       const int which = n / hd, col = n - which * hd;
-      if (rotate && which < 2) {
+      const bool rot = rotate && which < 2;
+      if (rot) {
         const int p0 = (col % dh) / 2;
-        const float* cp = cos_t + (int64_t)p0 * seq + pos;
-        const float* sp = sin_t + (int64_t)p0 * seq + pos;
+        if (p0 != cached) {  // angle loads issued before the accumulator read, so their latency overlaps it
+          const float* cp = cos_t + (int64_t)p0 * seq + pos;
+          const float* sp = sin_t + (int64_t)p0 * seq + pos;
+#pragma unroll
+          for (int u = 0; u < 16; ++u) {
+            cc[u] = cp[(int64_t)u * seq];
+            sn[u] = sp[(int64_t)u * seq];
+          }
+          cached = p0;
+        }
+      }
+      float v[32];
+      umma::tmem_ld32(t.taddr + c0, v);
+      if (rot) {
 #pragma unroll
         for (int u = 0; u < 16; ++u) {
-          const float c = cp[(int64_t)u * seq], sn = sp[(int64_t)u * seq];
           const float e = round_to<T>(v[2 * u]), od = round_to<T>(v[2 * u + 1]);
-          v[2 * u] = e * c - od * sn;
-          v[2 * u + 1] = od * c + e * sn;
+          v[2 * u] = e * cc[u] - od * sn[u];
+          v[2 * u + 1] = od * cc[u] + e * sn[u];
         }
       }
       T* base = which == 0 ? plane[0] : (which == 1 ? plane[1] : plane[2]);

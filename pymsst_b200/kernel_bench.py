@@ -34,7 +34,8 @@ class _Bench:
         self.iters = iters
         self.warmup = warmup
         self.flush = torch.empty(64 * 1024 * 1024, device=device)
-        self.stream = torch.cuda.current_stream(device)
+        # every op runs on this side stream (made current by main), the stream its graphs are captured on
+        self.stream = torch.cuda.Stream(device)
         self.results: dict[str, dict] = {}
         self.peaks = load_peaks()
 
@@ -49,7 +50,7 @@ class _Bench:
         if self.graphs:
             try:
                 graph = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(graph):
+                with torch.cuda.graph(graph, stream=self.stream):
                     fn()
             except Exception:  # not capturable: time eager calls instead
                 graph = None
@@ -493,12 +494,14 @@ def main(argv=None) -> None:
     args = p.parse_args(argv)
     device = torch.device("cuda", torch.cuda.current_device())
     bench = _Bench(device, max(args.iters, 1), args.warmup, graphs=not args.eager and args.warmup > 0)
-    if args.sweep:
-        run_sweep(bench)
-    for name in ([] if args.sweep else args.ops or list(OPS)):
-        if name not in OPS:
-            raise SystemExit(f"unknown op {name!r}; choose from {', '.join(OPS)}")
-        OPS[name](bench)
+    with torch.cuda.stream(bench.stream):
+        if args.sweep:
+            run_sweep(bench)
+        for name in ([] if args.sweep else args.ops or list(OPS)):
+            if name not in OPS:
+                raise SystemExit(f"unknown op {name!r}; choose from {', '.join(OPS)}")
+            OPS[name](bench)
+    torch.cuda.synchronize(device)
     timeout = nat.library().pmb_umma_timeout(1)
     if timeout:
         raise RuntimeError(f"tcgen05 wait timed out (site {timeout:#x})")
