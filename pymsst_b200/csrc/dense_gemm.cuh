@@ -23,7 +23,9 @@ __device__ __forceinline__ float load_dyn(const void* p, int64_t i, int code) {
 }
 
 // C = act(acc + bias) in TC, row stride ldc.  With `slices` set, group g of
-// the plan writes slice g (slice_elems apart): the split-K partials.
+// the plan writes slice g (slice_elems apart): the split-K partials.  16-bit
+// outputs with `use_tma` are written by TMA tile stores through `out_map`
+// (tma::make_store_map_2d over C).
 template <typename TC>
 struct DenseEpi {
   TC* c;
@@ -32,6 +34,8 @@ struct DenseEpi {
   int bias_dtype;
   int act;
   int64_t slice_elems;
+  int use_tma;
+  CUtensorMap out_map;
   template <int BN>
   __device__ void run(const ugemm::Plan&, const ugemm::TileCtx& t) const {
     TC* base = c + (int64_t)t.group * slice_elems + (int64_t)t.row0 * ldc + t.n0;
@@ -51,10 +55,29 @@ struct DenseEpi {
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = tanhf(v[j]);
       }
+      if constexpr (sizeof(TC) == 2) {
+        if (use_tma) {
+          ugemm::warp_tma_store<TC>(t, v, &out_map, t.n0 + c0, t.row0);
+          continue;
+        }
+      }
       ugemm::warp_store<TC>(t.stage, v, base + c0, ldc, t.rows_valid, ncols);
     }
   }
 };
+
+// A DenseEpi for a 16-bit C [m, n] (row stride ldc) that stores through TMA when C's base and pitch allow it.
+template <typename TC>
+inline DenseEpi<TC> dense_epi_tma(TC* c, int64_t ldc, int64_t m, int64_t n, const void* bias, int bias_dtype, int act,
+                                  int c_dtype, const char* name) {
+  DenseEpi<TC> e{c, ldc, bias, bias_dtype, act, 0, 0, {}};
+  if (((reinterpret_cast<uintptr_t>(c) | (uintptr_t)(ldc * 2)) & 15) == 0 &&
+      tma::make_store_map_2d(e.out_map, c, c_dtype, (uint64_t)n, (uint64_t)m, (uint64_t)ldc * 2, name) == PMB_OK)
+    e.use_tma = 1;
+  else
+    clear_error();
+  return e;
+}
 
 // N tile width for an N extent: 256 once N exceeds 128 (the A rows are then
 // read once per 256 columns), else 128 / 64.
@@ -131,10 +154,12 @@ inline int gemm(const void* a, int64_t lda, bool a_mn, const void* b, int64_t ld
                         DenseEpi<float>{static_cast<float*>(c), ldc, bias, bias_dtype, act, 0}, fp16, s, name);
     case PMB_FLOAT16:
       return launch_any(bn, a_mn, b_mn, ma, mb, plan,
-                        DenseEpi<__half>{static_cast<__half*>(c), ldc, bias, bias_dtype, act, 0}, fp16, s, name);
+                        dense_epi_tma<__half>(static_cast<__half*>(c), ldc, m, n, bias, bias_dtype, act, c_dtype, name),
+                        fp16, s, name);
     case PMB_BFLOAT16:
       return launch_any(bn, a_mn, b_mn, ma, mb, plan,
-                        DenseEpi<__nv_bfloat16>{static_cast<__nv_bfloat16*>(c), ldc, bias, bias_dtype, act, 0},
+                        dense_epi_tma<__nv_bfloat16>(static_cast<__nv_bfloat16*>(c), ldc, m, n, bias, bias_dtype, act,
+                                                     c_dtype, name),
                         fp16, s, name);
     default:
       set_error("%s: unsupported output dtype %d", name, c_dtype);

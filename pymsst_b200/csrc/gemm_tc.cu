@@ -92,6 +92,33 @@ int make_map_4d(CUtensorMap& map, const void* base, int dtype, const uint64_t (&
   return PMB_OK;
 }
 
+int make_store_map_2d(CUtensorMap& map, const void* base, int dtype, uint64_t cols, uint64_t rows, uint64_t ld_bytes,
+                      const char* name) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) {
+    set_error("%s: cuTensorMapEncodeTiled is unavailable (driver too old or no GPU)", name);
+    return PMB_ERR_CUDA;
+  }
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (ld_bytes & 15) != 0) {
+    set_error("%s: output store map needs a 16-byte aligned base and row pitch (pitch %llu bytes)", name,
+              (unsigned long long)ld_bytes);
+    return PMB_ERR_ALIGNMENT;
+  }
+  const cuuint64_t d[2] = {cols, rows};
+  const cuuint64_t st[1] = {ld_bytes};
+  const cuuint32_t bx[2] = {32, 32};
+  const cuuint32_t elem[2] = {1, 1};
+  const CUtensorMapDataType t =
+      dtype == PMB_BFLOAT16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const CUresult r = fn(&map, t, 2, const_cast<void*>(base), d, st, bx, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("%s: cuTensorMapEncodeTiled failed (%d) for an output store map", name, (int)r);
+    return PMB_ERR_CUDA;
+  }
+  return PMB_OK;
+}
+
 int make_map_rows_f32(CUtensorMap& map, const void* base, uint64_t cols, uint64_t rows, uint64_t pitch_bytes,
                       uint32_t box_cols, const char* name) {
   EncodeTiledFn fn = encode_fn();

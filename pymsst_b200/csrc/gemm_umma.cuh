@@ -44,6 +44,8 @@ constexpr int kMaxGroups = PMB_MAX_BANDS;
 // Per-warp staging block: 32 rows x (32 fp32 + 16 bytes of padding).
 constexpr int kStageRowBytes = 32 * 4 + 16;
 constexpr int kStageWarpBytes = 32 * kStageRowBytes;
+static_assert(kStageWarpBytes % 512 == 0 && kStageWarpBytes >= 4096,
+              "staging blocks hold two 512-byte-aligned 2 KB TMA store buffers");
 
 struct Group {
   int m, n, k;                  // problem size of this group
@@ -104,6 +106,7 @@ struct TileCtx {
   int n_valid;     // columns of this tile inside the group (<= BN)
   uint32_t taddr;  // TMEM address of this thread's row, column 0 of the tile
   uint8_t* stage;  // this warp's staging block (kStageWarpBytes)
+  int* store_seq;  // this thread's count of TMA tile stores issued so far (picks the staging buffer)
 };
 
 // Locate tile `tile` of the plan: group, M / N origin.
@@ -225,6 +228,46 @@ __device__ __forceinline__ void warp_load(uint8_t* stage, const T* src, int64_t 
 #pragma unroll
   for (int j = 0; j < 32; ++j) v[j] = Elem<T>::to_f(srow[j]);
   __syncwarp();
+}
+
+// TMA tile stores (16-bit outputs).  The warp writes its 32 x 32 block into
+// one of two 2 KB buffers at the start of its staging block (512-byte
+// aligned) in the 64-byte-swizzled layout of the output's tensor map: row r
+// at byte 64 r, its 16-byte chunk c at chunk position c ^ ((r >> 1) & 3), so
+// the 32 lanes' row writes spread over all banks.  One lane then issues the
+// bulk tensor store of the box at (col, row); the tensor map clips rows and
+// columns past the output's extent.  Buffers alternate: before rewriting one,
+// the lane waits until at most one earlier store is still reading shared
+// memory.  This replaces the staged 16-byte global stores (shared-memory
+// reads plus LSU stores per lane) with one asynchronous copy per block.
+// Every output-store map is {32 columns, 32 rows}, 64-byte swizzle
+// (tma::make_store_map_2d).  An epilogue that uses these stores does not use
+// warp_store / warp_load (they share the staging block).
+template <typename T>
+__device__ __forceinline__ void warp_tma_store(const TileCtx& t, const float (&v)[32], const CUtensorMap* map,
+                                               int col, int row) {
+  static_assert(sizeof(T) == 2, "TMA tile stores take 16-bit outputs");
+  const int lane = threadIdx.x & 31;
+  const int buf = (*t.store_seq)++ & 1;
+  uint8_t* box = t.stage + buf * 2048;
+  if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+  __syncwarp();
+  T pack[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) pack[j] = Elem<T>::from_f(v[j]);
+  const int sw = (lane >> 1) & 3;
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    *reinterpret_cast<uint4*>(box + lane * 64 + ((q ^ sw) << 4)) = reinterpret_cast<const uint4*>(pack)[q];
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  __syncwarp();
+  if (lane == 0) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(col), "r"(row), "r"(umma::smem_u32(box))
+                 : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+  }
 }
 
 // ------------------------------------------------------------------ kernel
@@ -359,6 +402,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3;
     const int sub = (warp - 2) / 4;
     uint8_t* stage = staging + (warp - 2) * kStageWarpBytes;
+    int store_seq = 0;
     uint32_t local = 0;
     for (int tile = blockIdx.x; tile < plan.total_tiles; tile += gridDim.x, ++local) {
       if (abort_flag) break;
@@ -385,12 +429,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         t.n_valid = min(BN, G.n - n0);
         t.taddr = tmem + buf * BN + ((uint32_t)(quarter * 32) << 16);
         t.stage = stage;
+        t.store_seq = &store_seq;
         epi.template run<BN>(plan, t);
       }
       umma::tc_fence_before();
       __syncwarp();
       if (lane == 0) umma::mbar_arrive(&tempty[buf]);
     }
+    // TMA tile stores still reading this warp's staging buffers must finish before the CTA releases them
+    if (lane == 0 && store_seq > 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    __syncwarp();
   }
   __syncwarp();
   umma::tc_fence_before();

@@ -10,8 +10,10 @@
 // ([Dh/2, N]) so the 32 rows of a warp read 32 consecutive positions of one
 // pair (coalesced) instead of 32 scattered table rows, and each epilogue warp
 // keeps the 16 angle pairs of its head half in registers across the chunks
-// it drains (see the chunk map in QkvRotaryEpi).  Stores are 16-byte row
-// vectors.  The projection is written once and never re-read for a split
+// it drains (see the chunk map in QkvRotaryEpi).  Where sequences are
+// contiguous rows (inner == 1) each warp's 32 x 32 block goes out as one TMA
+// tile store; with the row map (inner > 1) the rows of a block are scattered
+// over the plane and go out as 16-byte row vectors.  The projection is written once and never re-read for a split
 // or rotary pass; the backward is pmb_qkv_rotary_merge plus the two
 // projection-gradient GEMMs.
 // Reference semantics: to_qkv projection + qkv_to_bnhd + rotary_forward on
@@ -30,6 +32,8 @@ struct QkvRotaryEpi {
   const float* cos_t;  // [Dh/2, seq]
   const float* sin_t;
   int hd, seq, dh, rotate, inner;
+  int use_tma;           // inner == 1 and every plane accepts a TMA store map
+  CUtensorMap maps[3];   // q, k, v planes as [rows, H*Dh] store maps
   template <int BN>
   __device__ void run(const ugemm::Plan&, const ugemm::TileCtx& t) const {
     // x row r = (outer, position, inner index); its plane row is (outer * inner + inner index) * seq + position.
@@ -78,6 +82,10 @@ struct QkvRotaryEpi {
           v[2 * u + 1] = od * cc[u] + e * sn[u];
         }
       }
+      if (use_tma) {
+        ugemm::warp_tma_store<T>(t, v, &maps[which], col, t.row0);
+        continue;
+      }
       T* base = which == 0 ? plane[0] : (which == 1 ? plane[1] : plane[2]);
       if (inner == 1) {
         ugemm::warp_store<T>(t.stage, v, base + (int64_t)t.row0 * hd + col, hd, t.rows_valid, ncols);
@@ -122,7 +130,18 @@ extern "C" int pmb_qkv_linear_rotary_forward(const void* x, const void* weight, 
   auto run = [&](auto tag) {
     using T = decltype(tag);
     QkvRotaryEpi<T> epi{{static_cast<T*>(q), static_cast<T*>(k), static_cast<T*>(v)}, cos_t, sin_t,
-                        (int)(heads * dim_head), (int)seq_len, (int)dim_head, rotate_qk, (int)seq_inner};
+                        (int)(heads * dim_head), (int)seq_len, (int)dim_head, rotate_qk, (int)seq_inner, 0, {}};
+    if (seq_inner == 1 && (heads * dim_head * 2) % 16 == 0) {
+      // planes stored by TMA tiles: rows in x order are plane rows when sequences are contiguous
+      int ok = 1;
+      for (int i = 0; i < 3 && ok; ++i)
+        ok = tma::make_store_map_2d(epi.maps[i], epi.plane[i], dtype, (uint64_t)(heads * dim_head), (uint64_t)rows,
+                                    (uint64_t)(heads * dim_head * 2), name) == PMB_OK;
+      if (ok)
+        epi.use_tma = 1;
+      else
+        clear_error();
+    }
     if (bn == 256) return dense::launch<256, false, false>(ma, mb, plan, epi, fp16, s, name);
     if (bn == 128) return dense::launch<128, false, false>(ma, mb, plan, epi, fp16, s, name);
     return dense::launch<64, false, false>(ma, mb, plan, epi, fp16, s, name);

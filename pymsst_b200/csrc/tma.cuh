@@ -27,6 +27,12 @@ int make_map_3d(CUtensorMap& map, const void* base, int dtype, uint64_t inner, u
 int make_map_4d(CUtensorMap& map, const void* base, int dtype, const uint64_t (&dims)[4],
                 const uint64_t (&stride_bytes)[3], const uint32_t (&box)[4], const char* name);
 
+// Output map for TMA tile stores: a 16-bit [rows, cols] matrix with a row
+// pitch of ld_bytes (a multiple of 16), box {32 columns, 32 rows}, 64-byte
+// swizzle (the layout ugemm::warp_tma_store writes).
+int make_store_map_2d(CUtensorMap& map, const void* base, int dtype, uint64_t cols, uint64_t rows, uint64_t ld_bytes,
+                      const char* name);
+
 // 2-D map over an fp32 matrix [rows, cols] (row pitch in bytes, a multiple of
 // 16), no swizzle, box {box_cols, 1}: one slice of one row per load.
 int make_map_rows_f32(CUtensorMap& map, const void* base, uint64_t cols, uint64_t rows, uint64_t pitch_bytes,

@@ -16,7 +16,8 @@ arrays to cublasGemmGroupedBatchedEx and faulted on this GPU
 (fused_band_split.cu:2258-2279), so it is never called.
 
 Run with ``-s`` to see the table (median of 10 calls after 3 warm-ups, CUDA
-events around each call, outputs allocated inside the call on both sides).
+events around each call queued behind a GPU sleep so they bracket device
+work, outputs allocated inside the call on both sides).
 """
 from __future__ import annotations
 
@@ -38,20 +39,34 @@ def _reference_module():
     return load(path)
 
 
-def _time(fn, iters=10, warmup=3):
+def _time(fn, iters=10, warmup=3, graph=False):
+    """Median device time of fn in microseconds.  Each timed call is queued behind a short GPU sleep, so the
+    host has issued the whole call before the GPU reaches it and the events bracket device work (host-side
+    waits inside the call, such as a synchronous pointer-table upload, still count).  graph=True times replays
+    of fn captured into a CUDA graph (for the training-path autograd Functions)."""
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
+    g = None
+    if graph:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        torch.cuda.synchronize()
     times = []
     for _ in range(iters):
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda._sleep(2_000_000)
         a.record()
-        fn()
+        if g is not None:
+            g.replay()
+        else:
+            fn()
         b.record()
         torch.cuda.synchronize()
         times.append(a.elapsed_time(b))
     times.sort()
-    return times[len(times) // 2] * 1e3  # microseconds
+    return times[len(times) // 2] * 1e3
 
 
 def _cases(device):
@@ -72,7 +87,7 @@ def _cases(device):
     ]
     t = rn(1032, 62, 8, 64)
     ang = torch.arange(62, dtype=torch.float32)[:, None] * (1.0 / 10000 ** (torch.arange(0, 64, 2) / 64))[None]
-    cos, sin = (v.reshape(1, 62, 1, 32).to(device) for v in (ang.cos(), ang.sin()))
+    cos, sin = (v.reshape(1, 62, 1, 32).to(dt).to(device) for v in (ang.cos(), ang.sin()))
     cases.append(("rotary_forward", (t, cos, sin)))
     widths = [4 * f for f in DEFAULT_FREQS_PER_BANDS]
     offsets = torch.tensor([0] + torch.tensor(widths).cumsum(0).tolist(), dtype=torch.int64, device=device)
@@ -123,14 +138,14 @@ def test_training_path_kernels_timed_beside_the_reference(cuda_device):
     params = ([torch.rand(w, generator=g).add(0.5).to(cuda_device) for w in widths]
               + [(torch.randn(192, w, generator=g) * w ** -0.5).to(cuda_device) for w in widths]
               + [torch.zeros(192, device=cuda_device) for _ in widths])
-    t_band = _time(lambda: BandSplitFn.apply(xb, widths, 192, *params))
+    t_band = _time(lambda: BandSplitFn.apply(xb, widths, 192, *params), graph=True)
     hx = torch.randn(1032, 62, 192, generator=g).to(dt).to(cuda_device)
     mparams = []
     for layer, (cin, cout) in enumerate(((192, 768), (768, None))):
         outs = [768] * 62 if cout else [2 * w for w in widths]
         mparams += [(torch.randn(o, cin, generator=g) * cin ** -0.5).to(cuda_device) for o in outs]
         mparams += [torch.zeros(o, device=cuda_device) for o in outs]
-    t_mask = _time(lambda: MaskEstimatorTCFn.apply(hx, widths, 1, 768, *mparams))
+    t_mask = _time(lambda: MaskEstimatorTCFn.apply(hx, widths, 1, 768, *mparams), graph=True)
     print(f"\ntraining path, bf16: BandSplit tcgen05 forward {t_band:.1f} us; "
           f"MaskEstimator tcgen05 forward (both layers) {t_mask:.1f} us")
     assert t_band > 0 and t_mask > 0
