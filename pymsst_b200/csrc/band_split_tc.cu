@@ -215,6 +215,8 @@ struct BandOutEpi {
   T* out;
   const float* inv;
   int nb, O;
+  int use_tma;          // out stored by TMA tiles through out_map ([rows, nb * O])
+  CUtensorMap out_map;
   int first[kMaxBands];
   float sqrt_w[kMaxBands];
   const void* bias[kMaxBands];
@@ -249,6 +251,10 @@ struct BandOutEpi {
       umma::tmem_ld32(t.taddr + c0, v);
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = fmaf(v[j], sc[q], __shfl_sync(0xffffffffu, bl[q], j));
+      if (use_tma) {  // O is a multiple of 64: each 32-column chunk lies inside one band
+        ugemm::warp_tma_store<T>(t, v, &out_map, b * O + o0, t.row0);
+        continue;
+      }
       ugemm::warp_store<T>(t.stage, v, out + (int64_t)t.row0 * ld + (int64_t)b * O + o0, ld, t.rows_valid, ncols);
     }
   }
@@ -540,6 +546,9 @@ extern "C" int pmb_band_split_tc_forward(const void* x, int64_t rows, int64_t x_
       epi.inv = inv_norm;
       epi.nb = num_bands;
       epi.O = (int)out_features;
+      epi.use_tma = tma::make_store_map_2d(epi.out_map, out, dtype, (uint64_t)(num_bands * out_features),
+                                           (uint64_t)rows, (uint64_t)(num_bands * out_features * 2), name) == PMB_OK;
+      if (!epi.use_tma) clear_error();
       for (int b = 0; b < num_bands; ++b) {
         epi.sqrt_w[b] = sqrtf((float)L.w[b]);
         epi.bias[b] = biases ? biases[b] : nullptr;

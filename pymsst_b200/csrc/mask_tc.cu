@@ -116,6 +116,8 @@ struct TanhEpi {
   int64_t ld;  // nb * H
   int h;
   const void* bias[kMaxBands];
+  int use_tma;          // out stored by TMA tiles through out_map ([rows, nb * H])
+  CUtensorMap out_map;
   template <int BNT>
   __device__ void run(const ugemm::Plan&, const ugemm::TileCtx& t) const {
     T* o = out + (int64_t)t.row0 * ld + (int64_t)t.group * h + t.n0;
@@ -130,6 +132,10 @@ struct TanhEpi {
       const float bl = lane < ncols ? Elem<TP>::to_f(bp[c0 + lane]) : 0.f;
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = tanh_fast(v[j] + __shfl_sync(0xffffffffu, bl, j));
+      if (use_tma) {  // hidden widths are multiples of 64: chunks are whole
+        ugemm::warp_tma_store<T>(t, v, &out_map, t.group * h + t.n0 + c0, t.row0);
+        continue;
+      }
       ugemm::warp_store<T>(t.stage, v, o + c0, ld, t.rows_valid, ncols);
     }
   }
@@ -426,6 +432,10 @@ int forward_impl(const void* x, const Layout& y, const void* const* weights, con
       epi.ld = (int64_t)y.nb * y.hidden;
       epi.h = (int)y.hidden;
       for (int b = 0; b < y.nb; ++b) epi.bias[b] = biases[(int64_t)l * y.nb + b];
+      // hidden widths are multiples of 64, so every 32-column chunk lies inside one band: TMA tile stores
+      epi.use_tma = tma::make_store_map_2d(epi.out_map, epi.out, dtype, (uint64_t)(y.nb * y.hidden), (uint64_t)y.rows,
+                                           (uint64_t)(y.nb * y.hidden * 2), name) == PMB_OK;
+      if (!epi.use_tma) clear_error();
       st = hbn == 256 ? run_gemm<256, TanhEpi<T, TP>, false, false>(ma, mb, plan, epi, fp16, s, name)
                       : run_gemm<BN, TanhEpi<T, TP>, false, false>(ma, mb, plan, epi, fp16, s, name);
       if (st) return st;
