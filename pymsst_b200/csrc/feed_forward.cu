@@ -9,12 +9,15 @@
 //           derivative and the grad_b1 column partials in the GEMM epilogue;
 //           grad_W1 = d_pre^T x (split-K); grad_x = d_pre W1.
 // GELU is the exact (erf) form of torch.nn.GELU(): gelu(v) = v * Phi(v),
-// gelu'(v) = Phi(v) + v * phi(v).  Intermediate values are rounded to the
+// gelu'(v) = Phi(v) + v * phi(v), evaluated as in the elementwise passes
+// (gelu.cuh: for 16-bit values the logistic fit that rounds to the exact
+// GELU).  Intermediate values are rounded to the
 // activation dtype where the unfused autocast path stores them (the linear
 // outputs and the GELU output), so both paths see the same bf16 tensors.
 // The reference runs this block through torch (pymss-core FeedForward,
 // called per layer from src/pymsst/training/fused_roformer.py:256-824).
 #include "dense_gemm.cuh"
+#include "gelu.cuh"
 #include "reduce.cuh"
 
 namespace pmb {
@@ -22,16 +25,16 @@ unsigned int timeout_flag_ff(int reset) { return umma::flag_reader(reset); }
 
 namespace {
 
-__device__ __forceinline__ float gelu_cdf(float v) { return 0.5f * (1.0f + erff(v * 0.70710678118654752f)); }
-__device__ __forceinline__ float gelu_pdf(float v) { return 0.39894228040143268f * expf(-0.5f * v * v); }
-
-// pre / act = (acc + b1) / gelu(acc + b1), both stored in T.
+// pre / act = (acc + b1) / gelu(acc + b1), both stored in T (the 16-bit GELU of gelu.cuh, equal to the exact GELU
+// after rounding).  With `use_tma` both go out as TMA tile stores ([rows, hidden] maps; hidden is a multiple of 32).
 template <typename T, typename TP>
 struct GeluEpi {
   T* pre;
   T* act;
   const TP* bias;
   int64_t ld;
+  int use_tma;
+  CUtensorMap pre_map, act_map;
   template <int BN>
   __device__ void run(const ugemm::Plan&, const ugemm::TileCtx& t) const {
     const int lane = threadIdx.x & 31;
@@ -45,9 +48,16 @@ struct GeluEpi {
       const float bl = lane < ncols ? Elem<TP>::to_f(bias[t.n0 + c0 + lane]) : 0.f;
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = round_to<T>(v[j] + __shfl_sync(0xffffffffu, bl, j));
+      if (use_tma) {
+        ugemm::warp_tma_store<T>(t, v, &pre_map, t.n0 + c0, t.row0);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = gelu_of<T>(v[j]);
+        ugemm::warp_tma_store<T>(t, v, &act_map, t.n0 + c0, t.row0);
+        continue;
+      }
       ugemm::warp_store<T>(t.stage, v, pre + base + c0, ld, t.rows_valid, ncols);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = v[j] * gelu_cdf(v[j]);
+      for (int j = 0; j < 32; ++j) v[j] = gelu_of<T>(v[j]);
       ugemm::warp_store<T>(t.stage, v, act + base + c0, ld, t.rows_valid, ncols);
     }
   }
@@ -73,7 +83,7 @@ struct DGeluEpi {
       umma::tmem_ld32(t.taddr + c0, v);
       ugemm::warp_load<T>(t.stage, pre + base + c0, ld, t.rows_valid, ncols, p);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = round_to<T>(v[j]) * (gelu_cdf(p[j]) + p[j] * gelu_pdf(p[j]));
+      for (int j = 0; j < 32; ++j) v[j] = round_to<T>(v[j]) * gelu_grad_of<T>(p[j]);
       ugemm::warp_store<T>(t.stage, v, dpre + base + c0, ld, t.rows_valid, ncols);
       // column sums of the staged (rounded) block, rows in order
       float s = 0.f;
@@ -160,7 +170,11 @@ extern "C" int pmb_feed_forward_forward(const void* x, const void* w1, const voi
       ugemm::Plan plan;
       plan.num_groups = 1;
       plan.g[0] = ugemm::Group{(int)rows, (int)hidden, (int)dim, 0, 0, 0, 0, 0, 0};
-      GeluEpi<T, TP> epi{static_cast<T*>(pre), static_cast<T*>(act), static_cast<const TP*>(b1), hidden};
+      GeluEpi<T, TP> epi{static_cast<T*>(pre), static_cast<T*>(act), static_cast<const TP*>(b1), hidden, 0, {}, {}};
+      epi.use_tma = hidden % 32 == 0 &&
+                    tma::make_store_map_2d(epi.pre_map, pre, dtype, hidden, rows, hidden * 2, name) == PMB_OK &&
+                    tma::make_store_map_2d(epi.act_map, act, dtype, hidden, rows, hidden * 2, name) == PMB_OK;
+      if (!epi.use_tma) clear_error();
       st = bn == 256 ? dense::launch<256, false, false>(ma, mb, plan, epi, fp16, s, name)
                      : (bn == 128 ? dense::launch<128, false, false>(ma, mb, plan, epi, fp16, s, name)
                                   : dense::launch<64, false, false>(ma, mb, plan, epi, fp16, s, name));

@@ -11,67 +11,13 @@
 #include <initializer_list>
 
 #include "common.cuh"
+#include "gelu.cuh"
 #include "reduce.cuh"
 
 namespace pmb {
 namespace {
 
 constexpr int kRowsPerBlock = 128;
-
-__device__ __forceinline__ float phi_cdf(float v) { return 0.5f * (1.0f + erff(v * 0.70710678118654752f)); }
-__device__ __forceinline__ float phi_pdf(float v) { return 0.39894228040143268f * expf(-0.5f * v * v); }
-
-// 16-bit paths.  Phi(x) = 1 / (1 + 2^(-x H(x^2 / 5.5^2))) with H the degree-9
-// polynomial fitted by pymsst_b200/gelu_fit.py to log2(Phi / (1 - Phi)) / x
-// on [0, 5.5] (uniform relative error of the exponent, so of x Phi(x) on both
-// sides of zero); beyond |x| = 5.5 Phi saturates to 0 / 1, as fp32 erf has
-// already rounded to -1 / 1 there.  Two MUFU operations (ex2.approx,
-// rcp.approx) and 14 FMA-pipe ones per value instead of erff's longer
-// sequence, which made these passes issue-bound.  Over every finite bf16
-// input the rounded GELU equals the exact one (float64) rounded; fp16 differs
-// in 32 of 63488 inputs by one unit in the last place.  fp32 keeps erff.
-__constant__ float kPhiH[10] = {2.302230358e+00f, 3.169386864e+00f, -3.889901191e-02f, -4.928254604e+00f,
-                                1.236330509e+01f, -1.772161293e+01f, 1.614952087e+01f, -9.167760849e+00f,
-                                2.937237978e+00f, -4.014779925e-01f};
-
-__device__ __forceinline__ float ex2_approx(float v) {
-  float r;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(v));
-  return r;
-}
-
-__device__ __forceinline__ float rcp_approx(float v) {
-  float r;
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(v));
-  return r;
-}
-
-__device__ __forceinline__ float phi_cdf_fast(float x) {
-  const float t = x * x;
-  const float s = t * (1.0f / 30.25f);
-  float h = kPhiH[9];
-#pragma unroll
-  for (int i = 8; i >= 0; --i) h = fmaf(h, s, kPhiH[i]);
-  h = t > 30.25f ? 1e4f : h;  // |x| > 5.5: the exponent overflows to +-inf, Phi to 0 / 1
-  return rcp_approx(1.0f + ex2_approx(-x * h));
-}
-
-// phi(x) = exp(-x^2 / 2) / sqrt(2 pi) through ex2.approx
-__device__ __forceinline__ float phi_pdf_fast(float x) {
-  return 0.39894228040143268f * ex2_approx(x * x * -0.72134752044448170f);  // -log2(e) / 2
-}
-
-template <typename T>
-__device__ __forceinline__ float gelu_of(float v) {
-  if constexpr (sizeof(T) == 2) return v * phi_cdf_fast(v);
-  else return v * phi_cdf(v);
-}
-
-template <typename T>
-__device__ __forceinline__ float gelu_grad_of(float v) {
-  if constexpr (sizeof(T) == 2) return phi_cdf_fast(v) + v * phi_pdf_fast(v);
-  else return phi_cdf(v) + v * phi_pdf(v);
-}
 
 template <typename T>
 struct V8 {

@@ -1,4 +1,4 @@
-"""Coefficients of the normal-CDF approximation used by the 16-bit GELU kernels (csrc/gelu.cu).
+"""Coefficients of the normal-CDF approximation used by the 16-bit GELU kernels (csrc/gelu.cuh).
 
 The kernels evaluate Phi(x) = 1 / (1 + 2^(-x * H(x^2 / C^2))) for |x| <= C = 5.5 with H a degree-9
 polynomial, and saturate Phi to 0 / 1 beyond C (where fp32 erf has already rounded to -1 / 1).  H is

@@ -91,7 +91,7 @@ def test_gelu_kernels_match_torch(cuda_device, dtype):
 @pytest.mark.gpu
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_gelu_every_16bit_input(cuda_device, dtype):
-    """Every finite 16-bit value through the 16-bit GELU path (logistic form of the normal CDF, csrc/gelu.cu):
+    """Every finite 16-bit value through the 16-bit GELU path (logistic form of the normal CDF, csrc/gelu.cuh):
     forward and derivative within one unit in the last place of torch's erf GELU, equal for almost all."""
     x = torch.arange(0, 65536, dtype=torch.int32).to(torch.int16).view(dtype)
     x = x[torch.isfinite(x.float())]
