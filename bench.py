@@ -58,7 +58,6 @@ TIMED_ENTRIES = [
     "pmb_mask_estimator_tc_backward", "pmb_gemm_tc", "pmb_qkv_linear_rotary_forward", "pmb_band_split_tc_forward",
     "pmb_band_split_tc_backward", "pmb_gelu_forward", "pmb_gelu_backward", "pmb_column_sum",
     "pmb_attention_forward", "pmb_attention_backward", "pmb_stft_frames_forward", "pmb_stft_frames_backward",
-    "pmb_feed_forward_dgelu",
 ]
 
 

@@ -429,23 +429,6 @@ PMB_API int pmb_feed_forward_backward(const void* grad_out, const void* x, const
                                       void* stream);
 
 /* ------------------------------------------------------------------------
- * The feed-forward backward's middle step alone, for callers that keep the
- * weight-gradient and input-gradient GEMMs on a library:
- *   d_pre = round(grad_out w2) * gelu'(pre),   grad_b1 = column sums of d_pre
- * one tcgen05 GEMM (M = rows, N = hidden, K = dim) whose epilogue reads pre,
- * applies the GELU derivative, stores d_pre [rows, hidden] by TMA tile stores
- * and writes per-32-row column partials of d_pre (summed by a second launch
- * into grad_b1, param_dtype).  grad_out [rows, dim], w2 [dim, hidden] in the
- * activation dtype; workspace of pmb_feed_forward_dgelu_workspace_size
- * bytes.  hidden % 32 == 0, dim % 8 == 0.  No counterpart in the reference
- * (its feed-forward block is torch's).
- * ---------------------------------------------------------------------- */
-PMB_API int64_t pmb_feed_forward_dgelu_workspace_size(int64_t rows, int64_t hidden);
-PMB_API int pmb_feed_forward_dgelu(const void* grad_out, const void* w2, const void* pre, int64_t rows, int64_t dim,
-                                   int64_t hidden, void* dpre, void* grad_b1, int dtype, int param_dtype,
-                                   void* workspace, int64_t workspace_bytes, void* stream);
-
-/* ------------------------------------------------------------------------
  * BandSplit on the tcgen05 tensor cores (bf16 / fp16 activations; fp32 or
  * activation-dtype parameters), same math as pmb_band_split_forward:
  *   out[m, b, :] = (x_b * inv * sqrt(w_b) * gamma_b) W_b^T + bias_b,

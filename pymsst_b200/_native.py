@@ -40,8 +40,6 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "pmb_feed_forward_backward_workspace_size": (_i64, [_i64, _i64, _i64, _i]),
     "pmb_feed_forward_backward": (
         _i, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _p, _p, _p, _p, _p, _i, _i, _p, _i64, _p]),
-    "pmb_feed_forward_dgelu_workspace_size": (_i64, [_i64, _i64]),
-    "pmb_feed_forward_dgelu": (_i, [_p, _p, _p, _i64, _i64, _i64, _p, _p, _i, _i, _p, _i64, _p]),
     "pmb_gelu_forward": (_i, [_p, _p, _i64, _i, _p]),
     "pmb_rows_pass_workspace_size": (_i64, [_i64, _i64]),
     "pmb_gelu_backward": (_i, [_p, _p, _p, _i64, _i64, _p, _i, _i, _p, _i64, _p]),

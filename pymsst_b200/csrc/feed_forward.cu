@@ -95,59 +95,6 @@ struct DGeluEpi {
   }
 };
 
-// d_pre = round(acc) * gelu'(pre) stored in T by TMA tile stores, and the
-// column sums of the stored values over this warp's 32 rows to
-// partial[row0 / 32][col]: no staging-block reads or writes besides the TMA
-// store buffers.  Each lane loads its own row of pre (64 bytes) before it
-// reads the accumulator; the column sums come from a transposing butterfly
-// (31 shuffles leave column l's sum in lane l, in a fixed order).  Rows past
-// the end read no pre; their accumulator rows are zero (zero-filled A rows).
-template <typename T>
-struct DGeluTmaEpi {
-  const T* pre;
-  float* partial;
-  int64_t ld;  // hidden
-  CUtensorMap dpre_map;
-  template <int BN>
-  __device__ void run(const ugemm::Plan&, const ugemm::TileCtx& t) const {
-    const int lane = threadIdx.x & 31;
-#pragma unroll 1
-    for (int c0 = 32 * t.sub; c0 < BN; c0 += 32 * ugemm::kSubs) {
-      if (c0 >= t.n_valid) break;
-      float p[32];
-      {
-        uint4 u[4];
-        const uint4* src = reinterpret_cast<const uint4*>(pre + (int64_t)t.row * ld + t.n0 + c0);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) u[q] = t.row_valid ? src[q] : make_uint4(0, 0, 0, 0);
-        const T* e = reinterpret_cast<const T*>(u);
-#pragma unroll
-        for (int j = 0; j < 32; ++j) p[j] = Elem<T>::to_f(e[j]);
-      }
-      float v[32];
-      umma::tmem_ld32(t.taddr + c0, v);
-#pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = round_to<T>(round_to<T>(v[j]) * gelu_grad_of<T>(p[j]));
-      ugemm::warp_tma_store<T>(t, v, &dpre_map, t.n0 + c0, t.row0);
-      // transposing butterfly: after step s each lane keeps half of its columns, summed with its partner's
-#pragma unroll
-      for (int s = 0; s < 5; ++s) {
-        const int off = 16 >> s;
-        const bool upper = (lane & off) != 0;
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          if (j < off) {
-            const float send = upper ? v[j] : v[j + off];
-            const float keep = upper ? v[j + off] : v[j];
-            v[j] = keep + __shfl_xor_sync(0xffffffffu, send, off);
-          }
-        }
-      }
-      if (t.rows_valid > 0) partial[(int64_t)(t.row0 / 32) * ld + t.n0 + c0 + lane] = v[0];
-    }
-  }
-};
-
 // partial[chunk][c] = column sums of a [rows, cols] 16-bit matrix over
 // 64-row chunks, two adjacent columns per thread.
 template <typename T>
@@ -326,54 +273,4 @@ extern "C" int pmb_feed_forward_backward(const void* grad_out, const void* x, co
       return PMB_OK;
     }
   });
-}
-
-extern "C" int64_t pmb_feed_forward_dgelu_workspace_size(int64_t rows, int64_t hidden) {
-  if (rows <= 0 || hidden <= 0) return 0;
-  return align256(((rows + 31) / 32) * hidden * 4);
-}
-
-extern "C" int pmb_feed_forward_dgelu(const void* grad_out, const void* w2, const void* pre, int64_t rows, int64_t dim,
-                                      int64_t hidden, void* dpre, void* grad_b1, int dtype, int param_dtype,
-                                      void* workspace, int64_t workspace_bytes, void* stream) {
-  clear_error();
-  const char* name = "pmb_feed_forward_dgelu";
-  PMB_REQUIRE(dtype == PMB_BFLOAT16 || dtype == PMB_FLOAT16, "%s: activations must be bf16 or fp16", name);
-  PMB_REQUIRE(rows > 0 && rows < (1ll << 31) && dim > 0 && dim % 8 == 0 && hidden > 0 && hidden % 32 == 0,
-              "%s: bad shape (dim a multiple of 8, hidden of 32)", name);
-  PMB_REQUIRE(grad_out && w2 && pre && dpre && grad_b1, "%s: NULL tensor argument", name);
-  PMB_REQUIRE(dtype_size(param_dtype) > 0, "%s: unsupported parameter dtype", name);
-  PMB_REQUIRE(((reinterpret_cast<uintptr_t>(pre) | reinterpret_cast<uintptr_t>(dpre)) & 15) == 0,
-              "%s: pre and d_pre must be 16-byte aligned", name);
-  const int64_t need = pmb_feed_forward_dgelu_workspace_size(rows, hidden);
-  if (workspace == nullptr || workspace_bytes < need) {
-    set_error("%s: workspace of %lld bytes is smaller than the %lld required", name, (long long)workspace_bytes,
-              (long long)need);
-    return PMB_ERR_WORKSPACE;
-  }
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int fp16 = dtype == PMB_FLOAT16;
-  float* partial = static_cast<float*>(workspace);
-  auto run = [&](auto tag) -> int {
-    using T = decltype(tag);
-    const int bn = dense::pick_bn(hidden);
-    CUtensorMap ma, mb;
-    int st = dense::make_maps(ma, mb, grad_out, dim, false, w2, hidden, true, rows, hidden, dim, bn, dtype, name);
-    if (st) return st;
-    ugemm::Plan plan;
-    plan.num_groups = 1;
-    plan.g[0] = ugemm::Group{(int)rows, (int)hidden, (int)dim, 0, 0, 0, 0, 0, 0};
-    DGeluTmaEpi<T> epi{static_cast<const T*>(pre), partial, hidden, {}};
-    st = tma::make_store_map_2d(epi.dpre_map, dpre, dtype, hidden, rows, hidden * 2, name);
-    if (st) return st;
-    st = bn == 256 ? dense::launch<256, false, true>(ma, mb, plan, epi, fp16, s, name)
-                   : (bn == 128 ? dense::launch<128, false, true>(ma, mb, plan, epi, fp16, s, name)
-                                : dense::launch<64, false, true>(ma, mb, plan, epi, fp16, s, name));
-    if (st) return st;
-    red::colsum_rows<<<red::colsum_rows_grid(hidden), red::kThreads, 0, s>>>(partial, (int)((rows + 31) / 32), hidden,
-                                                                             grad_b1, param_dtype);
-    PMB_CHECK_LAUNCH(name);
-    return PMB_OK;
-  };
-  return fp16 ? run(__half()) : run(__nv_bfloat16());
 }

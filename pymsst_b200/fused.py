@@ -392,12 +392,10 @@ class FeedForwardFn(torch.autograd.Function):
 
     The two Linear layers and their weight / input gradients are plain
     library GEMMs (cuBLAS through torch, bias in the GEMM epilogue, operands
-    cast to the activation dtype as autocast does), except the hidden-layer
-    gradient: one tcgen05 GEMM g W2 whose epilogue applies the GELU
-    derivative, stores d_pre and writes the first bias gradient's column
-    partials (pmb_feed_forward_dgelu; pmb_gelu_backward after a library GEMM
-    where the widths do not allow it).  GELU and the second bias gradient
-    (pmb_column_sum) are this package's elementwise kernels.  (The
+    cast to the activation dtype as autocast does); GELU, its derivative and
+    both bias gradients are this package's kernels: the GELU derivative and
+    the first bias gradient come out of one pass over the hidden activations
+    (pmb_gelu_backward), the second bias gradient from pmb_column_sum.  (The
     fused block pmb_feed_forward_forward -- bias and GELU in the tcgen05 GEMM
     epilogue -- measured 118.7 us per call at config-3 shapes against 112 us
     for cuBLAS + the GELU pass, so the step keeps the latter.)"""
@@ -433,20 +431,11 @@ class FeedForwardFn(torch.autograd.Function):
         nat.call("pmb_column_sum", g.data_ptr(), rows, dim, gb2.data_ptr(), nat.dtype_code(dts[3]),
                  nat.dtype_code(dt), ws.data_ptr(), wsb, st)
         gw2 = torch.matmul(g.t(), act).to(dts[2])
+        da = torch.matmul(g, w2c)
         dpre = torch.empty_like(pre)
         gb1 = torch.empty(hidden, dtype=dts[1], device=device)
-        if hidden % 32 == 0 and dim % 8 == 0:
-            # d_pre = (g W2) * gelu'(pre) and its column sums from one tcgen05 GEMM epilogue
-            w2c = w2c.contiguous()
-            wsd = int(nat.library().pmb_feed_forward_dgelu_workspace_size(rows, hidden))
-            wd = nat.workspace(wsd, device)
-            nat.call("pmb_feed_forward_dgelu", g.data_ptr(), w2c.data_ptr(), pre.data_ptr(), rows, dim, hidden,
-                     dpre.data_ptr(), gb1.data_ptr(), nat.dtype_code(dt), nat.dtype_code(dts[1]), wd.data_ptr(), wsd,
-                     st)
-        else:
-            da = torch.matmul(g, w2c)
-            nat.call("pmb_gelu_backward", da.data_ptr(), pre.data_ptr(), dpre.data_ptr(), rows, hidden,
-                     gb1.data_ptr(), nat.dtype_code(dts[1]), nat.dtype_code(dt), ws.data_ptr(), wsb, st)
+        nat.call("pmb_gelu_backward", da.data_ptr(), pre.data_ptr(), dpre.data_ptr(), rows, hidden, gb1.data_ptr(),
+                 nat.dtype_code(dts[1]), nat.dtype_code(dt), ws.data_ptr(), wsb, st)
         gw1 = torch.matmul(dpre.t(), xn).to(dts[0])
         gx = torch.matmul(dpre, w1c) if ctx.needs_input_grad[0] else None
         return gx, gw1, gb1, gw2, gb2

@@ -218,15 +218,6 @@ def op_ff(bench: _Bench):
     bench.time("gelu_backward (+bias grad)", lambda: nat.call(
         "pmb_gelu_backward", act.data_ptr(), pre.data_ptr(), gpre.data_ptr(), ROWS, hid, gb1.data_ptr(), 0, 2,
         gws.data_ptr(), gwsb, st), 3 * ROWS * hid * 2)
-    dsb = int(nat.library().pmb_feed_forward_dgelu_workspace_size(ROWS, hid))
-    dws = nat.workspace(dsb, dev)
-    w2bf = w2.contiguous()
-    bench.time("feed_forward_dgelu (g W2 * gelu', bias grad)", lambda: nat.call(
-        "pmb_feed_forward_dgelu", gy.data_ptr(), w2bf.data_ptr(), pre.data_ptr(), ROWS, DIM, hid, gpre.data_ptr(),
-        gb1.data_ptr(), 2, 0, dws.data_ptr(), dsb, st), (ROWS * (DIM + 2 * hid) + DIM * hid) * 2, flops)
-    bench.time("torch g W2 + gelu_backward (replaced)", lambda: (
-        nat.call("pmb_gelu_backward", torch.matmul(gy, w2bf).data_ptr(), pre.data_ptr(), gpre.data_ptr(), ROWS, hid,
-                 gb1.data_ptr(), 0, 2, gws.data_ptr(), gwsb, st)), (ROWS * (DIM + 2 * hid) + DIM * hid) * 2, flops)
     bench.time("column_sum [rows, dim]", lambda: nat.call(
         "pmb_column_sum", gy.data_ptr(), ROWS, DIM, gb2.data_ptr(), 0, 2, gws.data_ptr(), gwsb, st), ROWS * DIM * 2)
     bwd_bytes = (3 * ROWS * DIM + 4 * ROWS * hid) * 2

@@ -133,10 +133,6 @@ def work(name: str, a: tuple) -> tuple[float, float]:
     if name in ("pmb_stft_frames_forward", "pmb_stft_frames_backward"):
         b, length, n_fft, frames = a[3], a[4], a[5], a[7]
         return 4.0 * (b * length + b * frames * n_fft + n_fft), 1.0 * b * frames * n_fft
-    if name == "pmb_feed_forward_dgelu":
-        # grad_out, W2 and pre read once, d_pre written, bias gradient written
-        rows, dim, hid, dt = a[3], a[4], a[5], a[8]
-        return (rows * (dim + 2 * hid) + dim * hid) * ES[dt] + 4 * hid, 2.0 * rows * dim * hid
     if name == "pmb_gelu_forward":
         return 2.0 * a[2] * ES[a[3]], 0.0
     if name == "pmb_gelu_backward":

@@ -119,35 +119,3 @@ def test_gelu_every_16bit_input(cuda_device, dtype):
              nat.dtype_code(dtype), ws.data_ptr(), wsb, st)
     check(gx, xr.grad)
 
-
-
-@pytest.mark.parametrize("rows,dim,hidden", [(63984, 192, 768), (1000, 192, 768), (77, 384, 1536)])
-def test_dgelu_gemm_epilogue_matches_unfused(cuda_device, rows, dim, hidden):
-    """pmb_feed_forward_dgelu (g W2 on tcgen05, GELU derivative and bias-gradient column partials in the
-    epilogue, d_pre stored by TMA tiles) against the unfused sequence it replaces: the library GEMM rounded to
-    bf16, then the GELU-derivative pass (pmb_gelu_backward) with its bias sums."""
-    torch.manual_seed(rows + hidden)
-    dt = torch.bfloat16
-    g = torch.randn(rows, dim, device=cuda_device).to(dt)
-    w2 = (torch.randn(dim, hidden, device=cuda_device) / hidden ** 0.5).to(dt)
-    pre = (torch.randn(rows, hidden, device=cuda_device) * 2).to(dt)
-    st = nat.stream_handle(cuda_device)
-    dpre = torch.empty_like(pre)
-    gb1 = torch.empty(hidden, device=cuda_device)
-    wsd = int(nat.library().pmb_feed_forward_dgelu_workspace_size(rows, hidden))
-    wd = nat.workspace(wsd, cuda_device)
-    nat.call("pmb_feed_forward_dgelu", g.data_ptr(), w2.data_ptr(), pre.data_ptr(), rows, dim, hidden, dpre.data_ptr(),
-             gb1.data_ptr(), nat.dtype_code(dt), nat.dtype_code(torch.float32), wd.data_ptr(), wsd, st)
-    da = torch.matmul(g, w2)
-    ref = torch.empty_like(pre)
-    ref_b = torch.empty(hidden, device=cuda_device)
-    wsb = nat.library().pmb_rows_pass_workspace_size(rows, hidden)
-    ws = nat.workspace(wsb, cuda_device)
-    nat.call("pmb_gelu_backward", da.data_ptr(), pre.data_ptr(), ref.data_ptr(), rows, hidden, ref_b.data_ptr(),
-             nat.dtype_code(torch.float32), nat.dtype_code(dt), ws.data_ptr(), wsb, st)
-    torch.cuda.synchronize()
-    _close(dpre, ref.double().cpu(), "d_pre")
-    # bias gradient: column sums of the stored d_pre, in the fused kernel's own rows
-    torch.testing.assert_close(gb1.double().cpu(), dpre.double().sum(0).cpu(), rtol=1e-4, atol=1e-3)
-    _close(gb1, ref_b.double().cpu(), "grad_b1", tol=1e-2)
-    assert nat.library().pmb_umma_timeout(1) == 0
