@@ -516,6 +516,23 @@ PMB_API int pmb_attention_backward(const void* q, const void* k, const void* v, 
                                    const float* lse, void* grad_q, void* grad_k, void* grad_v, int64_t sequences,
                                    int64_t seq_len, int64_t heads, int64_t dim_head, const int64_t* strides,
                                    float scale, int dtype, void* workspace, int64_t workspace_bytes, void* stream);
+/* The same backward with the rotary embedding's inverse rotation applied to
+ * grad_q and grad_k before they are stored: with cos / sin the fp32 angle
+ * tables [seq_len, dim_head / 2] (16-byte aligned) the forward rotated q and
+ * k with ((e, o) -> (e c - o s, o c + e s) on interleaved pairs), the
+ * gradients come out as those of the unrotated projections ((e, o) ->
+ * (e c + o s, o c - e s)).  With grad_q / grad_k / grad_v given as strided
+ * views of the [rows, 3 * heads * dim_head] projection gradient, this
+ * writes that gradient directly, replacing the attention backward plus
+ * pmb_qkv_rotary_merge for sequences stored in row order (the reference's
+ * rotary backward, src/pymsst/training/cuda/fused_band_split.cu:1104-1128,
+ * applied after the attention backward of fused_roformer.py:793-818). */
+PMB_API int pmb_attention_backward_rotary(const void* q, const void* k, const void* v, const void* o,
+                                          const void* grad_out, const float* lse, const float* cos, const float* sin,
+                                          void* grad_q, void* grad_k, void* grad_v, int64_t sequences,
+                                          int64_t seq_len, int64_t heads, int64_t dim_head, const int64_t* strides,
+                                          float scale, int dtype, void* workspace, int64_t workspace_bytes,
+                                          void* stream);
 
 /* ------------------------------------------------------------------------
  * STFT framing of the multi-resolution STFT loss: torch.stft (center=True,

@@ -436,6 +436,29 @@ __device__ __forceinline__ void store_row32(T* dst, const uint32_t (&a)[32], flo
   }
 }
 
+// Inverse rotary rotation of a thread's 32 gradient values of position pos
+// (interleaved pairs 16 half .. 16 half + 15 of the head): (e, o) ->
+// (e c + o s, o c - e s), the transpose of the forward's (e c - o s,
+// o c + e s); angles from fp32 tables [N, 32].  The gradient then leaves the
+// kernel in the projection's own (unrotated) space.
+__device__ __forceinline__ void unrotate32(uint32_t (&a)[32], const float* __restrict__ rc,
+                                           const float* __restrict__ rs, int pos, int half) {
+  const float4* c4 = reinterpret_cast<const float4*>(rc + (int64_t)pos * 32 + half * 16);
+  const float4* s4 = reinterpret_cast<const float4*>(rs + (int64_t)pos * 32 + half * 16);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float4 c = __ldg(c4 + i), sn = __ldg(s4 + i);
+    const float cc[4] = {c.x, c.y, c.z, c.w}, ss[4] = {sn.x, sn.y, sn.z, sn.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int e_i = 8 * i + 2 * j;
+      const float e = __uint_as_float(a[e_i]), o = __uint_as_float(a[e_i + 1]);
+      a[e_i] = __float_as_uint(fmaf(e, cc[j], o * ss[j]));
+      a[e_i + 1] = __float_as_uint(fmaf(o, cc[j], -e * ss[j]));
+    }
+  }
+}
+
 // 16 columns of this warp's TMEM lane quarter, without waiting (see tmem_wait16).
 __device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(
@@ -524,7 +547,8 @@ __global__ void __launch_bounds__(kBwdThreads, 2)
     attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmDO,
                    const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                    const T* __restrict__ o, const float* __restrict__ lse, float* __restrict__ delta,
-                   T* __restrict__ dq, Plane po, Plane pdq, int N, int H, int ldl, int nblk, int total, float scale) {
+                   T* __restrict__ dq, Plane po, Plane pdq, int N, int H, int ldl, int nblk, int total, float scale,
+                   const float* __restrict__ rcos, const float* __restrict__ rsin) {
   using namespace bq;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
@@ -730,7 +754,10 @@ __global__ void __launch_bounds__(kBwdThreads, 2)
       asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
       tie32(a0);
       warp_arrive(dq_empty, false);
-      if (valid) store_row32<T>(dq + it.b * pdq.s_b + it.h * pdq.s_h + (int64_t)r * pdq.s_n + half * 32, a0, scale);
+      if (valid) {
+        if (rcos != nullptr) unrotate32(a0, rcos, rsin, r, half);
+        store_row32<T>(dq + it.b * pdq.s_b + it.h * pdq.s_h + (int64_t)r * pdq.s_n + half * 32, a0, scale);
+      }
     }
   }
   umma::tc_fence_before();
@@ -768,7 +795,7 @@ __global__ void __launch_bounds__(kBwdThreads, 2)
                      const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmDO,
                      const __grid_constant__ CUtensorMap tmL, const __grid_constant__ CUtensorMap tmD,
                      T* __restrict__ dk, T* __restrict__ dv, Plane pdk, Plane pdv, int N, int H, int nblk, int total,
-                     float scale) {
+                     float scale, const float* __restrict__ rcos, const float* __restrict__ rsin) {
   using namespace bk;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
@@ -957,6 +984,7 @@ __global__ void __launch_bounds__(kBwdThreads, 2)
       const int r = it.blk * BM + row;
       if (r < N) {
         store_row32<T>(dv + it.b * pdv.s_b + it.h * pdv.s_h + (int64_t)r * pdv.s_n + half * 32, vv, 1.f);
+        if (rcos != nullptr) unrotate32(kv, rcos, rsin, r, half);
         store_row32<T>(dk + it.b * pdk.s_b + it.h * pdk.s_h + (int64_t)r * pdk.s_n + half * 32, kv, scale);
       }
     }
@@ -1256,7 +1284,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                       const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
                       const __grid_constant__ CUtensorMap tmO, const float* __restrict__ lse, T* __restrict__ dq,
                       T* __restrict__ dk, T* __restrict__ dv, Plane pdq, Plane pdk, Plane pdv, int sequences, int N,
-                      int H, int ldl, int total, float scale) {
+                      int H, int ldl, int total, float scale, const float* __restrict__ rcos,
+                      const float* __restrict__ rsin) {
   using namespace bf;
   using L = Layout<kPack>;
   constexpr bool pack = kPack;
@@ -1511,6 +1540,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const int64_t rk = seq * pdk.s_b + h * pdk.s_h + (int64_t)pos * pdk.s_n + half * 32;
         const int64_t rq = seq * pdq.s_b + h * pdq.s_h + (int64_t)pos * pdq.s_n + half * 32;
         store_row32<T>(dv + rv, gv, 1.f);
+        if (rcos != nullptr) {
+          unrotate32(gk, rcos, rsin, pos, half);
+          unrotate32(gq, rcos, rsin, pos, half);
+        }
         store_row32<T>(dk + rk, gk, scale);
         store_row32<T>(dq + rq, gq, scale);
       }
@@ -1640,13 +1673,14 @@ extern "C" int64_t pmb_attention_backward_workspace_size(int64_t sequences, int6
   return (sequences * heads * row_pitch(seq_len) * 4 + 255) / 256 * 256;
 }
 
-extern "C" int pmb_attention_backward(const void* q, const void* k, const void* v, const void* o,
-                                      const void* grad_out, const float* lse, void* grad_q, void* grad_k,
-                                      void* grad_v, int64_t sequences, int64_t seq_len, int64_t heads,
-                                      int64_t dim_head, const int64_t* strides, float scale, int dtype,
-                                      void* workspace, int64_t workspace_bytes, void* stream) {
-  clear_error();
-  const char* name = "pmb_attention_backward";
+namespace pmb {
+namespace {
+// The backward of both entry points; rcos / rsin (fp32 [seq_len, 32], or both NULL) rotate dQ and dK back.
+int attention_backward(const void* q, const void* k, const void* v, const void* o, const void* grad_out,
+                       const float* lse, void* grad_q, void* grad_k, void* grad_v, int64_t sequences, int64_t seq_len,
+                       int64_t heads, int64_t dim_head, const int64_t* strides, float scale, int dtype,
+                       const float* rcos, const float* rsin, void* workspace, int64_t workspace_bytes, void* stream,
+                       const char* name) {
   if (int st = check_shape(name, dtype, sequences, seq_len, heads, dim_head)) return st;
   if (sequences == 0) return PMB_OK;
   PMB_REQUIRE(lse && strides, "%s: NULL argument", name);
@@ -1689,7 +1723,7 @@ extern "C" int pmb_attention_backward(const void* q, const void* k, const void* 
       PMB_CHECK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem), name);
       kernel<<<grid, kBwdThreads, smem, s>>>(mq, mk, mv, mdo, mo, lse, static_cast<T*>(grad_q),
                                                  static_cast<T*>(grad_k), static_cast<T*>(grad_v), pdq, pdk, pdv,
-                                                 (int)sequences, N, H, (int)ldl, (int)items, scale);
+                                                 (int)sequences, N, H, (int)ldl, (int)items, scale, rcos, rsin);
       PMB_CHECK_LAUNCH(name);
       return PMB_OK;
     };
@@ -1716,13 +1750,40 @@ extern "C" int pmb_attention_backward(const void* q, const void* k, const void* 
         cudaFuncSetAttribute(attn_bwd_dkdv_tc<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, bk::SMEM), name);
     attn_bwd_dq_tc<T><<<grid, kBwdThreads, bq::SMEM, s>>>(mq128, mdo128, mk64, mv64, static_cast<const T*>(o), lse,
                                                         delta, static_cast<T*>(grad_q), po, pdq, N, H, (int)ldl, nblk,
-                                                        (int)total, scale);
+                                                        (int)total, scale, rcos, rsin);
     PMB_CHECK_LAUNCH(name);
     attn_bwd_dkdv_tc<T><<<grid, kBwdThreads, bk::SMEM, s>>>(mk128, mv128, mq64, mdo64, ml, md, static_cast<T*>(grad_k),
                                                           static_cast<T*>(grad_v), pdk, pdv, N, H, nblk, (int)total,
-                                                          scale);
+                                                          scale, rcos, rsin);
     PMB_CHECK_LAUNCH(name);
     return PMB_OK;
   };
   return dtype == PMB_BFLOAT16 ? run(__nv_bfloat16()) : run(__half());
+}
+}  // namespace
+}  // namespace pmb
+
+extern "C" int pmb_attention_backward(const void* q, const void* k, const void* v, const void* o,
+                                      const void* grad_out, const float* lse, void* grad_q, void* grad_k,
+                                      void* grad_v, int64_t sequences, int64_t seq_len, int64_t heads,
+                                      int64_t dim_head, const int64_t* strides, float scale, int dtype,
+                                      void* workspace, int64_t workspace_bytes, void* stream) {
+  clear_error();
+  return attention_backward(q, k, v, o, grad_out, lse, grad_q, grad_k, grad_v, sequences, seq_len, heads, dim_head,
+                            strides, scale, dtype, nullptr, nullptr, workspace, workspace_bytes, stream,
+                            "pmb_attention_backward");
+}
+
+extern "C" int pmb_attention_backward_rotary(const void* q, const void* k, const void* v, const void* o,
+                                             const void* grad_out, const float* lse, const float* cos,
+                                             const float* sin, void* grad_q, void* grad_k, void* grad_v,
+                                             int64_t sequences, int64_t seq_len, int64_t heads, int64_t dim_head,
+                                             const int64_t* strides, float scale, int dtype, void* workspace,
+                                             int64_t workspace_bytes, void* stream) {
+  clear_error();
+  const char* name = "pmb_attention_backward_rotary";
+  PMB_REQUIRE(cos && sin && (reinterpret_cast<uintptr_t>(cos) & 15) == 0 && (reinterpret_cast<uintptr_t>(sin) & 15) == 0,
+              "%s: angle tables must be non-NULL and 16-byte aligned", name);
+  return attention_backward(q, k, v, o, grad_out, lse, grad_q, grad_k, grad_v, sequences, seq_len, heads, dim_head,
+                            strides, scale, dtype, cos, sin, workspace, workspace_bytes, stream, name);
 }

@@ -21,7 +21,6 @@
 #include <vector>
 
 #include "gemm_umma.cuh"
-#include "reduce.cuh"
 #include "tma.cuh"
 
 namespace pmb {
@@ -33,8 +32,9 @@ constexpr int kThreads = 256;
 constexpr int BN = 128;
 constexpr int STAGES = 4;
 constexpr int kChunk = 64;  // GLU outputs per 128-column tile
-constexpr int kGluRows = 16;  // rows per GLU-backward thread (and per partial row of the final bias gradient)
-inline int glu_chunks(int64_t rows) { return (int)((rows + kGluRows - 1) / kGluRows); }
+constexpr int kGluRows = 4;    // rows per GLU-backward thread
+constexpr int kPartRows = 32;  // rows per partial row of the bias-gradient column sums (GLU and hidden layers)
+inline int part_chunks(int64_t rows) { return (int)((rows + kPartRows - 1) / kPartRows); }
 
 struct BandInfo {
   int nb;
@@ -183,29 +183,68 @@ struct GluEpi {
 };
 
 // dH epilogue: dst[m, b, n] = acc * (1 - y^2) (tanh derivative with the
-// layer output y) or acc (no activation before this layer).
+// layer output y) or acc (no activation before this layer).  Each lane loads
+// its own row of y (64 bytes) before it reads the accumulator, so the load
+// overlaps the tensor-memory wait.  With `partial`, the column sums of the
+// stored (rounded) values over this warp's 32 rows go to
+// partial[row0 / 32][column] -- the next layer's bias gradient without a
+// separate pass over dst; the sums come from a transposing butterfly (31
+// shuffles leave column l's sum in lane l, fixed order).  Widths are
+// multiples of 64, so every 32-column chunk is whole.
 template <typename T>
 struct DActEpi {
   T* dst;
-  const T* y;  // nullable
+  const T* y;        // nullable
+  float* partial;    // nullable: [ceil(rows / 32), ld] fp32
   int64_t ld;
   int h;
+  int use_tma;       // dst stored by TMA tiles through dst_map ([rows, ld])
+  CUtensorMap dst_map;
   template <int BNT>
   __device__ void run(const ugemm::Plan&, const ugemm::TileCtx& t) const {
-    const int64_t base = (int64_t)t.row0 * ld + (int64_t)t.group * h + t.n0;
+    const int lane = threadIdx.x & 31;
+    const int64_t col0 = (int64_t)t.group * h + t.n0;
 #pragma unroll 1
     for (int c0 = 32 * t.sub; c0 < BNT; c0 += 32 * ugemm::kSubs) {
       if (c0 >= t.n_valid) break;
-      const int ncols = min(32, t.n_valid - c0);
+      uint4 u[4];
+      if (y != nullptr) {
+        const uint4* src = reinterpret_cast<const uint4*>(y + (int64_t)t.row * ld + col0 + c0);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) u[q] = t.row_valid ? src[q] : make_uint4(0, 0, 0, 0);
+      }
       float v[32];
       umma::tmem_ld32(t.taddr + c0, v);
       if (y != nullptr) {
-        float yv[32];
-        ugemm::warp_load<T>(t.stage, y + base + c0, ld, t.rows_valid, ncols, yv);
+        const T* e = reinterpret_cast<const T*>(u);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] *= 1.0f - yv[j] * yv[j];
+        for (int j = 0; j < 32; ++j) {
+          const float yv = Elem<T>::to_f(e[j]);
+          v[j] *= 1.0f - yv * yv;
+        }
       }
-      ugemm::warp_store<T>(t.stage, v, dst + base + c0, ld, t.rows_valid, ncols);
+      if (use_tma)
+        ugemm::warp_tma_store<T>(t, v, &dst_map, (int)(col0 + c0), t.row0);
+      else
+        ugemm::warp_store<T>(t.stage, v, dst + (int64_t)t.row0 * ld + col0 + c0, ld, t.rows_valid, 32);
+      if (partial != nullptr) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = t.row_valid ? round_to<T>(v[j]) : 0.f;
+#pragma unroll
+        for (int s = 0; s < 5; ++s) {
+          const int off = 16 >> s;
+          const bool upper = (lane & off) != 0;
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            if (j < off) {
+              const float send = upper ? v[j] : v[j + off];
+              const float keep = upper ? v[j + off] : v[j];
+              v[j] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+            }
+          }
+        }
+        if (t.rows_valid > 0) partial[(int64_t)(t.row0 / 32) * ld + col0 + c0 + lane] = v[0];
+      }
     }
   }
 };
@@ -243,46 +282,90 @@ struct WGradEpi {
 
 // GLU backward in the packed layout: gp = (g*sig(gate), g*left*sig'(gate)),
 // zero in padding slots; plus column partial sums for the bias gradient.
+// Thread = 8 consecutive left slots of one 64-output chunk (their gates sit
+// 64 columns further) over kGluRows rows: 16-byte loads of left and gate,
+// both results stored from the same thread.  CTA = 32 slot groups x 8 row
+// groups = 256 left slots x kPartRows rows; its column sums (fixed order over
+// the row groups) are one partial row.
+__device__ __forceinline__ int band_of_slot(const BandInfo& info, int64_t q) {
+  int lo = 0, hi = info.nb - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (info.pbase[mid] / 2 <= q) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kThreads)
     glu_bwd_packed(const T* __restrict__ dy, const T* __restrict__ pre, int64_t rows, int64_t total, int64_t P,
                    BandInfo info, T* __restrict__ gp, float* __restrict__ partial) {
-  const int64_t p = (int64_t)blockIdx.x * kThreads + threadIdx.x;
-  if (p >= P) return;
-  int lo = 0, hi = info.nb - 1;
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (info.pbase[mid] <= p) lo = mid; else hi = mid - 1;
-  }
-  const int b = lo;
-  const int q = (int)(p - info.pbase[b]);
-  const int c = q / 128, j = q % 128;
-  const bool is_gate = j >= kChunk;
-  const int l = c * kChunk + (j % kChunk);
-  const bool valid = l < info.w[b];
-  const int64_t pl = info.pbase[b] + c * 128 + (j % kChunk);  // left slot column
-  const int64_t r0 = (int64_t)blockIdx.y * kGluRows;
-  float acc = 0.f;
-  // all kGluRows rows' loads issued together (one memory round trip per thread)
-  float a[kGluRows], gt[kGluRows], g[kGluRows];
+  static_assert(kThreads == 256 && kPartRows == 8 * kGluRows, "CTA = 32 slot groups x 8 row groups");
+  __shared__ float sums[8][32][17];
+  __shared__ int64_t slot_col[32];
+  const int sgi = threadIdx.x & 31, rgi = threadIdx.x >> 5;
+  const int64_t q = ((int64_t)blockIdx.x * 32 + sgi) * 8;  // first left slot of this group (slots = P / 2)
+  float sl[8], sg[8];
 #pragma unroll
-  for (int j = 0; j < kGluRows; ++j) {
-    const int64_t r = r0 + j;
-    const bool ok = valid && r < rows;
-    a[j] = ok ? Elem<T>::to_f(pre[r * P + pl]) : 0.f;
-    gt[j] = ok ? Elem<T>::to_f(pre[r * P + pl + kChunk]) : 0.f;
-    g[j] = ok ? Elem<T>::to_f(dy[r * total + info.off[b] + l]) : 0.f;
+  for (int j = 0; j < 8; ++j) sl[j] = sg[j] = 0.f;
+  if (q < P / 2) {
+    const int b = band_of_slot(info, q);
+    const int qq = (int)(q - info.pbase[b] / 2);
+    const int c = qq / kChunk, jj = qq % kChunk;
+    const int64_t pl = info.pbase[b] + 128 * c + jj;  // left slot column; its gates at pl + kChunk
+    const int l0 = c * kChunk + jj;                   // band output of the first slot
+    const int nvalid = max(0, min(8, info.w[b] - l0));
+    if (rgi == 0) slot_col[sgi] = pl;
+    const T* dyb = dy + info.off[b] + l0;
+    const int64_t r0 = (int64_t)blockIdx.y * kPartRows + rgi * kGluRows;
+    // every row's loads issued before the first use (one memory round trip per thread)
+    uint4 a[kGluRows], gt[kGluRows];
+    float g[kGluRows][8];
+#pragma unroll
+    for (int i = 0; i < kGluRows; ++i) {
+      const int64_t r = r0 + i;
+      const bool ok = r < rows;
+      a[i] = ok ? *reinterpret_cast<const uint4*>(pre + r * P + pl) : make_uint4(0, 0, 0, 0);
+      gt[i] = ok ? *reinterpret_cast<const uint4*>(pre + r * P + pl + kChunk) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) g[i][j] = ok && j < nvalid ? Elem<T>::to_f(dyb[r * total + j]) : 0.f;
+    }
+#pragma unroll
+    for (int i = 0; i < kGluRows; ++i) {
+      const int64_t r = r0 + i;
+      if (r >= rows) break;
+      const T* ea = reinterpret_cast<const T*>(&a[i]);
+      const T* eg = reinterpret_cast<const T*>(&gt[i]);
+      alignas(16) T ol[8], og[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float s = sigm(Elem<T>::to_f(eg[j]));
+        // padding slots (past w) hold arbitrary values: selected away, never multiplied
+        const float vl = j < nvalid ? g[i][j] * s : 0.f;
+        const float vg = j < nvalid ? g[i][j] * Elem<T>::to_f(ea[j]) * s * (1.0f - s) : 0.f;
+        ol[j] = Elem<T>::from_f(vl);
+        og[j] = Elem<T>::from_f(vg);
+        sl[j] += vl;
+        sg[j] += vg;
+      }
+      *reinterpret_cast<uint4*>(gp + r * P + pl) = *reinterpret_cast<const uint4*>(ol);
+      *reinterpret_cast<uint4*>(gp + r * P + pl + kChunk) = *reinterpret_cast<const uint4*>(og);
+    }
   }
 #pragma unroll
-  for (int j = 0; j < kGluRows; ++j) {
-    const int64_t r = r0 + j;
-    if (r >= rows) break;
-    const float s = sigm(gt[j]);
-    const float v = valid ? (is_gate ? g[j] * a[j] * s * (1.0f - s) : g[j] * s) : 0.f;
-    gp[r * P + p] = Elem<T>::from_f(v);
-    acc += v;
+  for (int j = 0; j < 8; ++j) {
+    sums[rgi][sgi][j] = sl[j];
+    sums[rgi][sgi][8 + j] = sg[j];
   }
-  partial[(int64_t)blockIdx.y * P + p] = acc;
+  __syncthreads();
+  for (int k = threadIdx.x; k < 32 * 16; k += kThreads) {
+    const int s = k / 16, j = k % 16;
+    if (((int64_t)blockIdx.x * 32 + s) * 8 >= P / 2) continue;
+    float acc = 0.f;
+#pragma unroll
+    for (int r = 0; r < 8; ++r) acc += sums[r][s][j];
+    partial[(int64_t)blockIdx.y * P + slot_col[s] + (j < 8 ? j : kChunk + j - 8)] = acc;
+  }
 }
 
 // bias grad: packed column p -> original bias index (left l, gate w + l).
@@ -317,8 +400,13 @@ __global__ void __launch_bounds__(kThreads)
     grouped_bias_finalize(const float* __restrict__ partial, int chunks, int nb, int h, BandTable gb) {
   const int64_t c = (int64_t)blockIdx.x * kThreads + threadIdx.x;
   if (c >= (int64_t)nb * h) return;
+  const int64_t cols = (int64_t)nb * h;
   float s = 0.f;
-  for (int k = 0; k < chunks; ++k) s += partial[(int64_t)k * nb * h + c];
+  int k = 0;
+  for (; k + 4 <= chunks; k += 4)
+    s += (partial[(int64_t)k * cols + c] + partial[(int64_t)(k + 1) * cols + c]) +
+         (partial[(int64_t)(k + 2) * cols + c] + partial[(int64_t)(k + 3) * cols + c]);
+  for (; k < chunks; ++k) s += partial[(int64_t)k * cols + c];
   TP* dst = static_cast<TP*>(const_cast<void*>(gb.ptr0[c / h]));
   dst[c % h] = Elem<TP>::from_f(s);
 }
@@ -366,7 +454,7 @@ Layout make_layout(int64_t rows, int nb, int64_t dim, int64_t hidden, int L, con
   y.ws_da = align256(rows * P * 2);
   y.ws_db = y.ws_da + align256(rows * nb * wide * 2);
   y.ws_partial = y.ws_db + align256(rows * nb * wide * 2);
-  const int64_t partial_floats = std::max((int64_t)glu_chunks(rows) * P, (int64_t)red::chunks(rows) * nb * wide);
+  const int64_t partial_floats = (int64_t)part_chunks(rows) * std::max(P, (int64_t)nb * wide);
   y.ws_bytes = y.ws_partial + align256(partial_floats * 4);
   return y;
 }
@@ -475,7 +563,6 @@ int backward_impl(const void* grad_out, const void* x, const void* acts, const v
   T* gp = reinterpret_cast<T*>(ws + y.ws_gp);
   T* buf[2] = {reinterpret_cast<T*>(ws + y.ws_da), reinterpret_cast<T*>(ws + y.ws_db)};
   float* partial = reinterpret_cast<float*>(ws + y.ws_partial);
-  const int chunks = red::chunks(y.rows);
   const int64_t hin = y.L > 0 ? y.hidden : y.dim;
   const T* h_last = y.L > 0 ? static_cast<const T*>(acts) + (int64_t)(y.L - 1) * y.rows * y.nb * y.hidden
                             : static_cast<const T*>(x);
@@ -491,7 +578,7 @@ int backward_impl(const void* grad_out, const void* x, const void* acts, const v
   }
   // 1) GLU backward + final bias gradient
   {
-    dim3 g((unsigned)((y.P + kThreads - 1) / kThreads), glu_chunks(y.rows));
+    dim3 g((unsigned)((y.P / 2 + 255) / 256), part_chunks(y.rows));
     glu_bwd_packed<T><<<g, kThreads, 0, s>>>(static_cast<const T*>(grad_out), static_cast<const T*>(pre), y.rows,
                                              y.total, y.P, info, gp, partial);
     PMB_CHECK_LAUNCH(name);
@@ -501,7 +588,7 @@ int backward_impl(const void* grad_out, const void* x, const void* acts, const v
                              nullptr, name);
     if (st) return st;
     glu_bias_finalize<TP><<<(unsigned)((y.P + kThreads - 1) / kThreads), kThreads, 0, s>>>(
-        partial, glu_chunks(y.rows), y.P, info, gb);
+        partial, part_chunks(y.rows), y.P, info, gb);
     PMB_CHECK_LAUNCH(name);
   }
   // 2) final weight gradient: dWf_b = gp_b^T h_b   (M = packed rows, N = hin, K = rows)
@@ -545,8 +632,12 @@ int backward_impl(const void* grad_out, const void* x, const void* acts, const v
     dcur = y.L > 0 ? buf[0] : static_cast<T*>(grad_x);
     epi.dst = dcur;
     epi.y = y.L > 0 ? h_last : nullptr;
+    epi.partial = y.L > 0 ? partial : nullptr;  // bias gradient of the last hidden layer
     epi.ld = (int64_t)y.nb * hin;
     epi.h = (int)hin;
+    epi.use_tma = tma::make_store_map_2d(epi.dst_map, dcur, dtype, (uint64_t)epi.ld, (uint64_t)y.rows,
+                                         (uint64_t)(epi.ld * 2), name) == PMB_OK;
+    if (!epi.use_tma) clear_error();
     st = hin % 256 == 0 ? run_gemm<256, DActEpi<T>, false, true>(ma, mb, plan, epi, fp16, s, name)
                         : run_gemm<BN, DActEpi<T>, false, true>(ma, mb, plan, epi, fp16, s, name);
     if (st) return st;
@@ -555,19 +646,16 @@ int backward_impl(const void* grad_out, const void* x, const void* acts, const v
   for (int l = y.L - 1; l >= 0; --l) {
     const int64_t lin = l == 0 ? y.dim : y.hidden;
     const T* lx = l == 0 ? static_cast<const T*>(x) : static_cast<const T*>(acts) + (int64_t)(l - 1) * y.rows * y.nb * y.hidden;
-    // bias gradient: column sums of dcur
+    // bias gradient: column sums of dcur (partial rows written by the epilogue that produced dcur)
     {
       const int64_t cols = (int64_t)y.nb * y.hidden;
-      dim3 g((unsigned)((cols + 255) / 256), chunks);
-      red::colsum_partial<T><<<g, red::kThreads, 0, s>>>(dcur, y.rows, cols, cols, partial);
-      PMB_CHECK_LAUNCH(name);
       BandTable gb;
       std::vector<int64_t> ones(y.nb, 1);
       int st = make_band_table(gb, y.nb, ones.data(), (const void* const*)(grad_biases + (int64_t)l * y.nb), nullptr,
                                nullptr, name);
       if (st) return st;
       grouped_bias_finalize<T, TP><<<(unsigned)((cols + kThreads - 1) / kThreads), kThreads, 0, s>>>(
-          partial, chunks, y.nb, (int)y.hidden, gb);
+          partial, part_chunks(y.rows), y.nb, (int)y.hidden, gb);
       PMB_CHECK_LAUNCH(name);
     }
     // weight gradient: dW_b = dcur_b^T lx_b  (M = H, N = lin, K = rows)
@@ -609,8 +697,12 @@ int backward_impl(const void* grad_out, const void* x, const void* acts, const v
       if (next == dcur) next = buf[((y.L - l) + 1) % 2];
       epi.dst = next;
       epi.y = l > 0 ? lx : nullptr;
+      epi.partial = l > 0 ? partial : nullptr;  // bias gradient of layer l - 1
       epi.ld = (int64_t)y.nb * lin;
       epi.h = (int)lin;
+      epi.use_tma = tma::make_store_map_2d(epi.dst_map, next, dtype, (uint64_t)epi.ld, (uint64_t)y.rows,
+                                           (uint64_t)(epi.ld * 2), name) == PMB_OK;
+      if (!epi.use_tma) clear_error();
       st = lin % 192 == 0 ? run_gemm<192, DActEpi<T>, false, true>(ma, mb, plan, epi, fp16, s, name)
                           : run_gemm<BN, DActEpi<T>, false, true>(ma, mb, plan, epi, fp16, s, name);
       if (st) return st;

@@ -235,12 +235,15 @@ class MaskEstimatorTCFn(torch.autograd.Function):
         total = sum(widths)
         out = torch.empty(rows, total, dtype=x.dtype, device=device)
         layers = hidden_layers + 1
-        weights = [params[2 * nb * l + b] for l in range(layers) for b in range(nb)]
-        biases = [params[2 * nb * l + nb + b] for l in range(layers) for b in range(nb)]
+        # inside the trainer's step the 16-bit mirror of the parameters (the values autocast's casts give) is
+        # read instead of the fp32 masters: half the bytes for the weight packing
+        src = live_mirrors(params, x.dtype) or params
+        weights = [src[2 * nb * l + b] for l in range(layers) for b in range(nb)]
+        biases = [src[2 * nb * l + nb + b] for l in range(layers) for b in range(nb)]
         nat.call(
             "pmb_mask_estimator_tc_forward", x.data_ptr(), rows, nb, dim, hidden, hidden_layers, warr,
             nat.ptr_array(weights), nat.ptr_array(biases), packed.data_ptr(), acts.data_ptr(), pre.data_ptr(),
-            out.data_ptr(), nat.dtype_code(x.dtype), nat.dtype_code(params[0].dtype), nat.stream_handle(device),
+            out.data_ptr(), nat.dtype_code(x.dtype), nat.dtype_code(src[0].dtype), nat.stream_handle(device),
         )
         ctx.meta = (widths, hidden_layers, hidden, int(sizes[3]))
         ctx.save_for_backward(x, packed, acts, pre, *params)
@@ -287,6 +290,19 @@ def lowp_weight(p: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
     if half is not None and live is not None and live[0] and half.dtype == dtype:
         return half
     return p.to(dtype)
+
+
+def live_mirrors(params, dtype: torch.dtype):
+    """The trainer's live 16-bit mirrors of all of ``params`` (see lowp_weight), or None when any parameter
+    has none (outside the trainer's step): never a mix, and never a cast."""
+    out = []
+    for p in params:
+        half = getattr(p, "_pmb_half", None)
+        live = getattr(p, "_pmb_half_live", None)
+        if half is None or live is None or not live[0] or half.dtype != dtype:
+            return None
+        out.append(half)
+    return out
 
 
 class OutProjFn(torch.autograd.Function):
@@ -558,6 +574,76 @@ class AttentionFn(torch.autograd.Function):
             ws.data_ptr(), ws_bytes, nat.stream_handle(device),
         )
         return dq, dk, dv
+
+
+class QKVAttentionFn(torch.autograd.Function):
+    """Attention input projection with rotary (QKVRotaryFn's tensor-core path) followed by the own attention
+    kernels (AttentionFn): xn [b, n, D] (rows in sequence order, as on an axial transformer's band axis) ->
+    o [b, h, n, 64], a view of a [b, n, h, 64] plane.  The forward is those two ops.  The backward writes dQ and
+    dK rotated back to the projection's space, and dV, straight into the [b * n, 3 * h * 64] projection gradient
+    (pmb_attention_backward_rotary given strided views of it), so QKVRotaryFn.backward's merge pass and its
+    round trip of that gradient go; the two projection-gradient GEMMs follow as there.  Reference semantics:
+    qkv_to_bnhd + rotary + scaled-dot-product attention of the patched Attention.forward
+    (src/pymsst/training/fused_roformer.py:793-818)."""
+
+    @staticmethod
+    def forward(ctx, xn, weight, cos, sin, cos_t, sin_t, heads):
+        device = nat.require_cuda(xn, weight, name="QKVAttention")
+        b, n, d = xn.shape
+        dh = weight.shape[0] // (3 * heads)
+        if not (xn.dtype in (torch.bfloat16, torch.float16) and d % 8 == 0 and dh == 64):
+            raise ValueError("QKVAttention: 16-bit activations, D % 8 == 0 and 64-element heads only")
+        w = lowp_weight(weight, xn.dtype).contiguous()
+        x2 = xn.reshape(b * n, d).contiguous()
+        rotate = int(cos is not None)
+        if rotate:
+            if tuple(cos.shape) != (n, dh // 2) or tuple(sin.shape) != (n, dh // 2):
+                raise ValueError(f"QKVAttention: angle tables must be [{n}, {dh // 2}], got {tuple(cos.shape)} "
+                                 f"and {tuple(sin.shape)}")
+            cos, sin = cos.float().contiguous(), sin.float().contiguous()
+            if cos_t is None:
+                cos_t, sin_t = cos.t().contiguous(), sin.t().contiguous()
+        planes = [torch.empty(b, n, heads, dh, dtype=xn.dtype, device=device) for _ in range(3)]
+        stream = nat.stream_handle(device)
+        nat.call(
+            "pmb_qkv_linear_rotary_forward", x2.data_ptr(), w.data_ptr(), nat.ptr(cos_t), nat.ptr(sin_t), b, n, d,
+            heads, dh, planes[0].data_ptr(), planes[1].data_ptr(), planes[2].data_ptr(), rotate,
+            nat.dtype_code(xn.dtype), 1, stream,
+        )
+        q, k, v = (pl.transpose(1, 2) for pl in planes)
+        o = _bnhd_empty(b, heads, n, dh, xn.dtype, device)
+        lse = torch.empty(b * heads, (n + 3) // 4 * 4, dtype=torch.float32, device=device)
+        nat.call(
+            "pmb_attention_forward", q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(), b, n,
+            heads, dh, nat.i64_array(_attn_strides(q, k, v, o)), dh ** -0.5, nat.dtype_code(xn.dtype), stream,
+        )
+        ctx.weight_dtype = weight.dtype
+        ctx.save_for_backward(x2, w, cos, sin, q, k, v, o, lse)
+        return o
+
+    @staticmethod
+    def backward(ctx, grad):
+        x2, w, cos, sin, q, k, v, o, lse = ctx.saved_tensors
+        device = q.device
+        b, h, n, dh = q.shape
+        grad = _attn_plane(grad.to(q.dtype))
+        gqkv = torch.empty(b * n, 3 * h * dh, dtype=q.dtype, device=device)
+        parts = gqkv.view(b, n, 3, h, dh)
+        dq, dk, dv = (parts[:, :, i].transpose(1, 2) for i in range(3))
+        ws_bytes = int(nat.library().pmb_attention_backward_workspace_size(b, n, h))
+        ws = nat.workspace(ws_bytes, device)
+        strides = nat.i64_array(_attn_strides(q, k, v, o, grad, dq, dk, dv))
+        head = (q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), grad.data_ptr(), lse.data_ptr())
+        tail = (b, n, h, dh, strides, dh ** -0.5, nat.dtype_code(q.dtype), ws.data_ptr(), ws_bytes,
+                nat.stream_handle(device))
+        if cos is not None:
+            nat.call("pmb_attention_backward_rotary", *head, cos.data_ptr(), sin.data_ptr(), dq.data_ptr(),
+                     dk.data_ptr(), dv.data_ptr(), *tail)
+        else:
+            nat.call("pmb_attention_backward", *head, dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), *tail)
+        gx = torch.matmul(gqkv, w).reshape(b, n, -1) if ctx.needs_input_grad[0] else None
+        gw = torch.matmul(gqkv.t(), x2).to(ctx.weight_dtype) if ctx.needs_input_grad[1] else None
+        return gx, gw, None, None, None, None, None
 
 
 class STFTFramesFn(torch.autograd.Function):

@@ -232,9 +232,15 @@ def op_ff(bench: _Bench):
     def torch_ff():
         with torch.autocast("cuda", dtype=torch.bfloat16):
             y = lin2(torch.nn.functional.gelu(lin1(xr)))
-        y.backward(gy)
+        _grads(y, [xr, *lin1.parameters(), *lin2.parameters()], gy)
 
     bench.time("torch feed-forward fwd+bwd", torch_ff, fwd_bytes + bwd_bytes, 6 * flops)
+
+
+def _grads(y, inputs, gy):
+    """The backward of y for the given inputs without accumulating into their .grad (no accumulation kernels
+    are timed with the op)."""
+    return torch.autograd.grad(y, inputs, gy)
 
 
 def op_sdpa(bench: _Bench):
@@ -251,7 +257,7 @@ def op_sdpa(bench: _Bench):
             def run():
                 with sdpa_kernel(backend):
                     y = torch.nn.functional.scaled_dot_product_attention(*qkv)
-                y.backward(gy)
+                _grads(y, qkv, gy)
             try:
                 bench.time(f"sdpa {backend.name} n={n}", run, 0.0, flops)
             except RuntimeError as e:
@@ -275,7 +281,7 @@ def op_attn(bench: _Bench):
                 AttentionFn.apply(*qkv)
 
         def run():
-            AttentionFn.apply(*qkv).backward(gy)
+            _grads(AttentionFn.apply(*qkv), qkv, gy)
 
         bench.time(f"attention fwd n={n}", fwd, by, fl_f)
         bench.time(f"attention fwd+bwd n={n}", run, by * 3, fl_f * 3.5)
@@ -397,7 +403,7 @@ def op_mask(bench: _Bench):
     gy = torch.randn(rows, sum(widths), device=dev, dtype=torch.bfloat16)
 
     def fwd_bwd():
-        MaskEstimatorTCFn.apply(xr, widths, 1, hid, *params).backward(gy)
+        _grads(MaskEstimatorTCFn.apply(xr, widths, 1, hid, *params), [xr, *params], gy)
 
     bench.time("mask_estimator_tc fwd+bwd", fwd_bwd, 3 * byt, 3 * flops)
 

@@ -26,7 +26,11 @@ The per-layer hot path runs through :mod:`pymsst_b200.fused`:
 * attention core softmax(q k^T / sqrt(dh)) v: :class:`~pymsst_b200.fused.AttentionFn`
   (tcgen05 kernels; 16-bit, head dim 64) on the band axis, cuDNN's
   ``F.scaled_dot_product_attention`` on the longer time axis; any backend can
-  be forced with ``set_cuda_attention_backend``.
+  be forced with ``set_cuda_attention_backend``.  Where the own kernels run
+  on sequences stored in row order (the band axis),
+  :class:`~pymsst_b200.fused.QKVAttentionFn` takes projection, rotary and
+  attention together, so the attention backward writes the projection
+  gradient itself.
 
 The feed-forward projections and the attention output projection are cuBLAS
 GEMMs (the feed-forward GELU and bias gradients run on this package's kernels).
@@ -50,6 +54,7 @@ from .fused import (
     MaskEstimatorFn,
     MaskEstimatorTCFn,
     OutProjFn,
+    QKVAttentionFn,
     QKVRotaryFn,
     RMSNormFn,
     compute_dtype,
@@ -153,9 +158,13 @@ _SHORT_SEQ = 128
 ATTENTION_BACKENDS = ("auto", "default", "pmb", "cudnn", "efficient", "math", "flash")
 
 
+def _own_attention(n, backend):
+    """Whether a sequence of n positions takes the own attention kernels (when they support the shape)."""
+    return backend == "pmb" or (backend in ("auto", "default") and n <= _SHORT_SEQ)
+
+
 def _attention(q, k, v, dropout_p, backend="auto"):
-    if attention_supported(q, dropout_p) and (
-            backend == "pmb" or (backend in ("auto", "default") and q.shape[-2] <= _SHORT_SEQ)):
+    if attention_supported(q, dropout_p) and _own_attention(q.shape[-2], backend):
         return AttentionFn.apply(q, k, v)
     if q.is_cuda:
         from torch.nn.attention import SDPBackend, sdpa_kernel
@@ -208,9 +217,16 @@ class Attention(nn.Module):
         cos = sin = cos_t = sin_t = None
         if self.rotary_embed is not None:
             cos, sin, cos_t, sin_t = self.rotary_embed.tables(n, x.device)
-        q, k, v = QKVRotaryFn.apply(xn.reshape(b, n, d), self.to_qkv.weight, cos, sin, cos_t, sin_t, self.heads,
-                                    inner)
-        attn = _attention(q, k, v, self.dropout if self.training else 0.0, self.attention_backend)
+        dropout_p = self.dropout if self.training else 0.0
+        if (inner == 1 and xn.is_cuda and xn.dtype in (torch.bfloat16, torch.float16) and d % 8 == 0
+                and self.dim_head == 64 and dropout_p == 0.0 and _own_attention(n, self.attention_backend)):
+            # sequences in row order on the own kernels: the attention backward writes the projection gradient
+            attn = QKVAttentionFn.apply(xn.reshape(b, n, d), self.to_qkv.weight, cos, sin, cos_t, sin_t,
+                                        self.heads)
+        else:
+            q, k, v = QKVRotaryFn.apply(xn.reshape(b, n, d), self.to_qkv.weight, cos, sin, cos_t, sin_t,
+                                        self.heads, inner)
+            attn = _attention(q, k, v, dropout_p, self.attention_backend)
         gated = AttentionGateFn.apply(attn, xn.reshape(rows, d), self.to_gates.weight, self.to_gates.bias, inner)
         drop = self.to_out[1]
         if residual is not None and (not self.training or drop.p == 0.0):
