@@ -138,6 +138,20 @@ PMB_API int pmb_rms_norm_backward(const void* grad_out, const void* saved, int s
                           int grad_x_dtype, int grad_gamma_dtype, void* workspace,
                           int64_t workspace_bytes, void* stream);
 
+/* The same backward for a pre-norm residual block y = x + f(norm(x)):
+ *   grad_x += grad_residual   (grad_residual: [rows, dim] in grad_x_dtype, the
+ * gradient reaching x through the residual branch; NULL adds nothing), in the
+ * pass that writes grad_x, so the two gradients of x are not summed by a
+ * separate elementwise pass (the reference's Transformer blocks,
+ * fused_roformer.py:793-818 and pymss-core's `x = attn(x) + x; x = ff(x) + x`).
+ * grad_x must not be NULL when grad_residual is given, and the two must not
+ * overlap. */
+PMB_API int pmb_rms_norm_backward_add(const void* grad_out, const void* saved, int saved_is_input,
+                                      const float* inv_norm, const void* gamma, const void* grad_residual,
+                                      void* grad_x, void* grad_gamma, int64_t rows, int64_t dim, int grad_dtype,
+                                      int gamma_dtype, int grad_x_dtype, int grad_gamma_dtype, void* workspace,
+                                      int64_t workspace_bytes, void* stream);
+
 /*
  * pmb_rms_norm_backward for callers that cannot allocate device memory for
  * the call (a program binding this C ABI from another language with no

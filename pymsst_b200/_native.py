@@ -52,6 +52,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "pmb_rms_norm_forward": (_i, [_p, _p, _p, _p, _p, _i64, _i64, _i, _i, _i, _p]),
     "pmb_rms_norm_backward_workspace_size": (_i64, [_i64, _i64]),
     "pmb_rms_norm_backward": (_i, [_p, _p, _i, _p, _p, _p, _p, _i64, _i64, _i, _i, _i, _i, _p, _i64, _p]),
+    "pmb_rms_norm_backward_add": (
+        _i, [_p, _p, _i, _p, _p, _p, _p, _p, _i64, _i64, _i, _i, _i, _i, _p, _i64, _p]),
     "pmb_rms_norm_backward_noalloc": (_i, [_p, _p, _i, _p, _p, _p, _p, _i64, _i64, _i, _i, _i, _i, _p]),
     "pmb_rotary_forward": (_i, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i, _p]),
     "pmb_rotary_backward": (_i, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i, _p]),

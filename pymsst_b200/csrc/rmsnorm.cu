@@ -129,11 +129,30 @@ __global__ void __launch_bounds__(kThreads)
 }
 
 // --------------------------------------------------------------- backward
+// The residual branch's gradient added to grad_x (nullable: zeros), V values from element i (16-byte aligned).
+template <typename Tdx, int V>
+__device__ __forceinline__ void load_res(const Tdx* __restrict__ dres, int64_t i, float (&add)[V]) {
+  if (dres == nullptr) {
+#pragma unroll
+    for (int e = 0; e < V; ++e) add[e] = 0.f;
+    return;
+  }
+  if constexpr (sizeof(Tdx) * V == 16) {
+    const Pack<Tdx, V> pr = *reinterpret_cast<const Pack<Tdx, V>*>(dres + i);
+#pragma unroll
+    for (int e = 0; e < V; ++e) add[e] = Elem<Tdx>::to_f(pr.v[e]);
+  } else {
+#pragma unroll
+    for (int e = 0; e < V; ++e) add[e] = Elem<Tdx>::to_f(dres[i + e]);
+  }
+}
+
 template <typename Tg, typename Tdx, int V, int NJ>
 __global__ void __launch_bounds__(kThreads)
     rms_bwd_vec(const Tg* __restrict__ dy, const Tg* __restrict__ saved, int saved_is_input,
                 const float* __restrict__ inv_norm, const void* __restrict__ gamma, int gcode,
-                Tdx* __restrict__ dx, float* __restrict__ partial, int64_t rows, int dim) {
+                Tdx* __restrict__ dx, const Tdx* __restrict__ dres, float* __restrict__ partial, int64_t rows,
+                int dim) {
   extern __shared__ float red[];  // [kWarps][dim]
   const int lane = threadIdx.x & 31;
   const int wib = threadIdx.x >> 5;
@@ -185,9 +204,11 @@ __global__ void __launch_bounds__(kThreads)
       for (int j = 0; j < NJ; ++j) {
         const int vi = j * 32 + lane;
         if (vi < nvec) {
+          float add[V];
+          load_res<Tdx, V>(dres, r * dim + (int64_t)vi * V, add);
           Pack<Tdx, V> p;
 #pragma unroll
-          for (int e = 0; e < V; ++e) p.v[e] = Elem<Tdx>::from_f(inv * (gd[j][e] * scale - nv[j][e] * ds));
+          for (int e = 0; e < V; ++e) p.v[e] = Elem<Tdx>::from_f(inv * (gd[j][e] * scale - nv[j][e] * ds) + add[e]);
           *reinterpret_cast<Pack<Tdx, V>*>(dx + r * dim + (int64_t)vi * V) = p;
         }
       }
@@ -215,7 +236,8 @@ template <typename Tg, typename Tdx>
 __global__ void __launch_bounds__(kThreads)
     rms_bwd_generic(const Tg* __restrict__ dy, const Tg* __restrict__ saved, int saved_is_input,
                     const float* __restrict__ inv_norm, const void* __restrict__ gamma, int gcode,
-                    Tdx* __restrict__ dx, float* __restrict__ partial, int64_t rows, int dim) {
+                    Tdx* __restrict__ dx, const Tdx* __restrict__ dres, float* __restrict__ partial, int64_t rows,
+                    int dim) {
   // Column-parallel partials: each thread owns columns c = tid, tid+256, ...
   // and walks this CTA's rows; the row dot product is a CTA reduction.
   __shared__ float sdot[kWarps];
@@ -245,7 +267,8 @@ __global__ void __launch_bounds__(kThreads)
       for (int c = threadIdx.x; c < dim; c += kThreads) {
         const float d = Elem<Tg>::to_f(dy[r * dim + c]);
         const float n = Elem<Tg>::to_f(saved[r * dim + c]) * nk;
-        dx[r * dim + c] = Elem<Tdx>::from_f(inv * (d * ld_dyn(gamma, c, gcode) * scale - n * ds));
+        const float add = dres != nullptr ? Elem<Tdx>::to_f(dres[r * dim + c]) : 0.f;
+        dx[r * dim + c] = Elem<Tdx>::from_f(inv * (d * ld_dyn(gamma, c, gcode) * scale - n * ds) + add);
       }
     }
   }
@@ -385,7 +408,7 @@ template <typename Tg, typename Tdx, int V, int G, int NJ>
 __global__ void __launch_bounds__(kThreads, 3)
     rms_bwd_bulk(const Tg* __restrict__ dy, const Tg* __restrict__ saved, int saved_is_input,
                  const float* __restrict__ inv_norm, const void* __restrict__ gamma, int gcode, Tdx* __restrict__ dx,
-                 float* __restrict__ partial, int64_t rows, int dim, int rpt) {
+                 const Tdx* __restrict__ dres, float* __restrict__ partial, int64_t rows, int dim, int rpt) {
   constexpr int RW = 32 / G;
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kBwdStageBytes * 2);
@@ -469,12 +492,14 @@ __global__ void __launch_bounds__(kThreads, 3)
             const Pack<Tg, V> pd = *reinterpret_cast<const Pack<Tg, V>*>(ds_ + q * dim + vi * V);
             const Pack<Tg, V> ps = *reinterpret_cast<const Pack<Tg, V>*>(ss_ + q * dim + vi * V);
             const float* gv = g_s + vi * V;
+            float add[V];
+            load_res<Tdx, V>(dres, (r0 + q) * dim + (int64_t)vi * V, add);
             Pack<Tdx, V> p;
 #pragma unroll
             for (int e = 0; e < V; ++e) {
               const float d = Elem<Tg>::to_f(pd.v[e]);
               const float nn = Elem<Tg>::to_f(ps.v[e]) * nk;
-              p.v[e] = Elem<Tdx>::from_f(inv * (d * gv[e] * scale - nn * dsc));
+              p.v[e] = Elem<Tdx>::from_f(inv * (d * gv[e] * scale - nn * dsc) + add[e]);
             }
             // dx goes back over this lane's own dy elements (sizeof(Tdx) == sizeof(Tg)), bulk-stored below
             *reinterpret_cast<Pack<Tdx, V>*>(reinterpret_cast<Tdx*>(ds_) + q * dim + vi * V) = p;
@@ -584,17 +609,19 @@ constexpr int kMaxBwdTileRows = kWarps * 32;
 
 template <typename Tg, typename Tdx>
 int launch_bwd(const void* dy, const void* saved, int saved_is_input, const float* inv, const void* gamma,
-               int gcode, void* dx, void* dgamma, int dgcode, int64_t rows, int64_t dim, float* partial,
-               cudaStream_t stream) {
+               int gcode, void* dx, const void* dres, void* dgamma, int dgcode, int64_t rows, int64_t dim,
+               float* partial, cudaStream_t stream) {
   constexpr int V = 16 / sizeof(Tg);
   const int grid = bwd_blocks(rows);
   const int64_t nvec = dim / V;
   const bool vec_ok = dim % V == 0 && aligned16(dy) && aligned16(saved) && (dx == nullptr || aligned16(dx)) &&
+                      (dres == nullptr || aligned16(dres)) &&
                       (dim * (int64_t)sizeof(Tg)) % 16 == 0 && (dim * (int64_t)sizeof(Tdx)) % 16 == 0;
   const int nj = (int)((nvec + 31) / 32);
   const Tg* dyp = static_cast<const Tg*>(dy);
   const Tg* sp = static_cast<const Tg*>(saved);
   Tdx* dxp = static_cast<Tdx*>(dx);
+  const Tdx* drp = static_cast<const Tdx*>(dres);
   const size_t smem = (size_t)kWarps * dim * sizeof(float);
   int used_grid = grid;  // CTAs writing grad_gamma partial rows
   // Register budget: at most 1024 elements of a row per warp in the vector path.
@@ -610,8 +637,8 @@ int launch_bwd(const void* dy, const void* saved, int saved_is_input, const floa
     constexpr int bsm = bulk_smem_bytes<kBwdStageBytes, 2>();
     auto go = [&](auto kern) {
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bsm);
-      kern<<<used_grid, kThreads, bsm, stream>>>(dyp, sp, saved_is_input, inv, gamma, gcode, dxp, partial, rows,
-                                                 (int)dim, rpt);
+      kern<<<used_grid, kThreads, bsm, stream>>>(dyp, sp, saved_is_input, inv, gamma, gcode, dxp, drp, partial,
+                                                 rows, (int)dim, rpt);
     };
     if (nvec <= 8)
       go(rms_bwd_bulk<Tg, Tdx, V, 8, 1>);
@@ -628,19 +655,19 @@ int launch_bwd(const void* dy, const void* saved, int saved_is_input, const floa
   } else if (vec_ok && nj * 32 * V <= 1024 && smem <= 48 * 1024) {
     if (nj <= 1)
       rms_bwd_vec<Tg, Tdx, V, 1><<<grid, kThreads, smem, stream>>>(dyp, sp, saved_is_input, inv, gamma, gcode, dxp,
-                                                                   partial, rows, (int)dim);
+                                                                   drp, partial, rows, (int)dim);
     else if (nj <= 2)
       rms_bwd_vec<Tg, Tdx, V, 2><<<grid, kThreads, smem, stream>>>(dyp, sp, saved_is_input, inv, gamma, gcode, dxp,
-                                                                   partial, rows, (int)dim);
+                                                                   drp, partial, rows, (int)dim);
     else if (nj <= 4)
       rms_bwd_vec<Tg, Tdx, V, 4><<<grid, kThreads, smem, stream>>>(dyp, sp, saved_is_input, inv, gamma, gcode, dxp,
-                                                                   partial, rows, (int)dim);
+                                                                   drp, partial, rows, (int)dim);
     else if constexpr (V == 4)
       rms_bwd_vec<Tg, Tdx, V, 8><<<grid, kThreads, smem, stream>>>(dyp, sp, saved_is_input, inv, gamma, gcode, dxp,
-                                                                   partial, rows, (int)dim);
+                                                                   drp, partial, rows, (int)dim);
   } else {
     rms_bwd_generic<Tg, Tdx><<<grid, kThreads, 0, stream>>>(dyp, sp, saved_is_input, inv, gamma, gcode, dxp,
-                                                            partial, rows, (int)dim);
+                                                            drp, partial, rows, (int)dim);
   }
   PMB_CHECK_LAUNCH("pmb_rms_norm_backward");
   if (dgamma != nullptr) {
@@ -682,36 +709,61 @@ extern "C" int64_t pmb_rms_norm_backward_workspace_size(int64_t rows, int64_t di
   return max_bwd_grid(rows) * dim * (int64_t)sizeof(float);
 }
 
+namespace pmb {
+namespace {
+int rms_backward(const void* grad_out, const void* saved, int saved_is_input, const float* inv_norm,
+                 const void* gamma, const void* grad_residual, void* grad_x, void* grad_gamma, int64_t rows,
+                 int64_t dim, int grad_dtype, int gamma_dtype, int grad_x_dtype, int grad_gamma_dtype, void* workspace,
+                 int64_t workspace_bytes, void* stream, const char* name) {
+  PMB_REQUIRE(rows >= 0 && dim > 0 && dim <= (1 << 20), "%s: bad shape rows=%lld dim=%lld", name, (long long)rows,
+              (long long)dim);
+  PMB_REQUIRE(valid_code(gamma_dtype) && valid_code(grad_gamma_dtype), "%s: unsupported gamma/grad_gamma dtype",
+              name);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (rows == 0) {
+    if (grad_gamma != nullptr) {
+      PMB_CHECK_CUDA(cudaMemsetAsync(grad_gamma, 0, dim * dtype_size(grad_gamma_dtype), s), name);
+    }
+    return PMB_OK;
+  }
+  PMB_REQUIRE(grad_out && saved && inv_norm && gamma, "%s: NULL tensor argument", name);
+  PMB_REQUIRE(grad_residual == nullptr || grad_x != nullptr, "%s: grad_residual needs grad_x", name);
+  const int64_t need = pmb_rms_norm_backward_workspace_size(rows, dim);
+  if (workspace_bytes < need || workspace == nullptr) {
+    set_error("%s: workspace of %lld bytes is smaller than the %lld required", name, (long long)workspace_bytes,
+              (long long)need);
+    return PMB_ERR_WORKSPACE;
+  }
+  float* partial = static_cast<float*>(workspace);
+  return PMB_DISPATCH(grad_dtype, Tg, name, [&] {
+    return PMB_DISPATCH(grad_x_dtype, Tdx, name, [&] {
+      return launch_bwd<Tg, Tdx>(grad_out, saved, saved_is_input, inv_norm, gamma, gamma_dtype, grad_x,
+                                 grad_residual, grad_gamma, grad_gamma_dtype, rows, dim, partial, s);
+    });
+  });
+}
+}  // namespace
+}  // namespace pmb
+
 extern "C" int pmb_rms_norm_backward(const void* grad_out, const void* saved, int saved_is_input,
                                      const float* inv_norm, const void* gamma, void* grad_x, void* grad_gamma,
                                      int64_t rows, int64_t dim, int grad_dtype, int gamma_dtype, int grad_x_dtype,
                                      int grad_gamma_dtype, void* workspace, int64_t workspace_bytes, void* stream) {
   clear_error();
-  PMB_REQUIRE(rows >= 0 && dim > 0 && dim <= (1 << 20), "pmb_rms_norm_backward: bad shape rows=%lld dim=%lld",
-              (long long)rows, (long long)dim);
-  PMB_REQUIRE(valid_code(gamma_dtype) && valid_code(grad_gamma_dtype),
-              "pmb_rms_norm_backward: unsupported gamma/grad_gamma dtype");
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (rows == 0) {
-    if (grad_gamma != nullptr) {
-      PMB_CHECK_CUDA(cudaMemsetAsync(grad_gamma, 0, dim * dtype_size(grad_gamma_dtype), s), "pmb_rms_norm_backward");
-    }
-    return PMB_OK;
-  }
-  PMB_REQUIRE(grad_out && saved && inv_norm && gamma, "pmb_rms_norm_backward: NULL tensor argument");
-  const int64_t need = pmb_rms_norm_backward_workspace_size(rows, dim);
-  if (workspace_bytes < need || workspace == nullptr) {
-    set_error("pmb_rms_norm_backward: workspace of %lld bytes is smaller than the %lld required",
-              (long long)workspace_bytes, (long long)need);
-    return PMB_ERR_WORKSPACE;
-  }
-  float* partial = static_cast<float*>(workspace);
-  return PMB_DISPATCH(grad_dtype, Tg, "pmb_rms_norm_backward", [&] {
-    return PMB_DISPATCH(grad_x_dtype, Tdx, "pmb_rms_norm_backward", [&] {
-      return launch_bwd<Tg, Tdx>(grad_out, saved, saved_is_input, inv_norm, gamma, gamma_dtype, grad_x, grad_gamma,
-                                 grad_gamma_dtype, rows, dim, partial, s);
-    });
-  });
+  return rms_backward(grad_out, saved, saved_is_input, inv_norm, gamma, nullptr, grad_x, grad_gamma, rows, dim,
+                      grad_dtype, gamma_dtype, grad_x_dtype, grad_gamma_dtype, workspace, workspace_bytes, stream,
+                      "pmb_rms_norm_backward");
+}
+
+extern "C" int pmb_rms_norm_backward_add(const void* grad_out, const void* saved, int saved_is_input,
+                                         const float* inv_norm, const void* gamma, const void* grad_residual,
+                                         void* grad_x, void* grad_gamma, int64_t rows, int64_t dim, int grad_dtype,
+                                         int gamma_dtype, int grad_x_dtype, int grad_gamma_dtype, void* workspace,
+                                         int64_t workspace_bytes, void* stream) {
+  clear_error();
+  return rms_backward(grad_out, saved, saved_is_input, inv_norm, gamma, grad_residual, grad_x, grad_gamma, rows, dim,
+                      grad_dtype, gamma_dtype, grad_x_dtype, grad_gamma_dtype, workspace, workspace_bytes, stream,
+                      "pmb_rms_norm_backward_add");
 }
 
 // ---------------------------------------------------------------------------
@@ -805,8 +857,8 @@ extern "C" int pmb_rms_norm_backward_noalloc(const void* grad_out, const void* s
   // every path launches at most kMaxBwdBlocks CTAs, so the partial sums fit the array.
   return PMB_DISPATCH(grad_dtype, Tg, name, [&] {
     return PMB_DISPATCH(grad_x_dtype, Tdx, name, [&] {
-      return launch_bwd<Tg, Tdx>(grad_out, saved, saved_is_input, inv_norm, gamma, gamma_dtype, grad_x, grad_gamma,
-                                 grad_gamma_dtype, rows, dim, partial, s);
+      return launch_bwd<Tg, Tdx>(grad_out, saved, saved_is_input, inv_norm, gamma, gamma_dtype, grad_x, nullptr,
+                                 grad_gamma, grad_gamma_dtype, rows, dim, partial, s);
     });
   });
 }

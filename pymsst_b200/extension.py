@@ -60,9 +60,11 @@ def rms_norm_backward_into(
     saved_is_input: bool,
     grad_x_dtype: torch.dtype | None,
     grad_gamma_dtype: torch.dtype,
+    grad_residual: torch.Tensor | None = None,
     name: str = "rms_norm_backward",
 ):
-    """Shared RMSNorm backward; ``grad_x_dtype=None`` skips grad_x."""
+    """Shared RMSNorm backward; ``grad_x_dtype=None`` skips grad_x.  ``grad_residual`` (same shape as x, in
+    ``grad_x_dtype``) is added to grad_x in the same pass (pmb_rms_norm_backward_add)."""
     device = nat.require_cuda(grad_out, saved, inv_norm, gamma, name=name)
     grad_out = _contig(grad_out)
     saved = _contig(saved)
@@ -73,14 +75,18 @@ def rms_norm_backward_into(
     lib = nat.library()
     ws_bytes = int(lib.pmb_rms_norm_backward_workspace_size(rows, dim))
     workspace = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=device)
-    with torch.cuda.device(device):
-        nat.call(
-            "pmb_rms_norm_backward",
-            grad_out.data_ptr(), saved.data_ptr(), int(saved_is_input), inv_norm.data_ptr(), _contig(gamma).data_ptr(),
-            nat.ptr(grad_x), grad_gamma.data_ptr(), rows, dim, nat.dtype_code(grad_out.dtype),
+    head = (grad_out.data_ptr(), saved.data_ptr(), int(saved_is_input), inv_norm.data_ptr(), _contig(gamma).data_ptr())
+    tail = (nat.ptr(grad_x), grad_gamma.data_ptr(), rows, dim, nat.dtype_code(grad_out.dtype),
             nat.dtype_code(gamma.dtype), nat.dtype_code(grad_x_dtype or grad_out.dtype),
-            nat.dtype_code(grad_gamma_dtype), workspace.data_ptr(), ws_bytes, nat.stream_handle(device),
-        )
+            nat.dtype_code(grad_gamma_dtype), workspace.data_ptr(), ws_bytes, nat.stream_handle(device))
+    with torch.cuda.device(device):
+        if grad_residual is None:
+            nat.call("pmb_rms_norm_backward", *head, *tail)
+        else:
+            _check(grad_x is not None, f"{name}: grad_residual needs grad_x")
+            grad_residual = _contig(grad_residual.to(grad_x_dtype))
+            _check(grad_residual.numel() == grad_out.numel(), f"{name}: grad_residual must match x")
+            nat.call("pmb_rms_norm_backward_add", *head, grad_residual.data_ptr(), *tail)
     return grad_x, grad_gamma
 
 

@@ -62,6 +62,42 @@ class RMSNormFn(torch.autograd.Function):
         return gx, gg
 
 
+class RMSNormResidualFn(torch.autograd.Function):
+    """RMSNormFn for a pre-norm residual block: returns (y, x), the second output being x itself for the block's
+    residual branch.  The backward then receives both gradients of x and writes grad_x = RMSNorm'(grad_y) +
+    grad_residual in the norm's own pass (pmb_rms_norm_backward_add), instead of the norm's pass followed by
+    autograd's elementwise sum of the two gradients."""
+
+    @staticmethod
+    def forward(ctx, x: torch.Tensor, gamma: torch.Tensor):
+        device = nat.require_cuda(x, gamma, name="RMSNormResidual")
+        xc = x.contiguous()
+        dim = xc.shape[-1]
+        rows = _rows(xc)
+        out = torch.empty_like(xc)
+        inv = torch.empty(rows, dtype=torch.float32, device=device)
+        nat.call(
+            "pmb_rms_norm_forward", xc.data_ptr(), gamma.data_ptr(), out.data_ptr(), None, inv.data_ptr(), rows, dim,
+            nat.dtype_code(xc.dtype), nat.dtype_code(gamma.dtype), nat.dtype_code(xc.dtype), nat.stream_handle(device),
+        )
+        ctx.save_for_backward(xc, inv, gamma)
+        return out, x
+
+    @staticmethod
+    def backward(ctx, grad, grad_res):
+        x, inv, gamma = ctx.saved_tensors
+        need_x = ctx.needs_input_grad[0]
+        if grad is None:  # only the residual branch was used
+            return grad_res, None
+        gx, gg = ext.rms_norm_backward_into(
+            grad.to(x.dtype).contiguous(), x, inv, gamma, saved_is_input=True,
+            grad_x_dtype=x.dtype if need_x else None, grad_gamma_dtype=gamma.dtype,
+            grad_residual=grad_res.reshape(x.shape) if need_x and grad_res is not None else None,
+            name="RMSNormResidual.backward",
+        )
+        return gx, gg
+
+
 # ---------------------------------------------------------------- BandSplit
 class BandSplitFn(torch.autograd.Function):
     """feats [rows, total] -> [rows, nb, O]; per band RMSNorm + Linear (ragged).
@@ -235,15 +271,12 @@ class MaskEstimatorTCFn(torch.autograd.Function):
         total = sum(widths)
         out = torch.empty(rows, total, dtype=x.dtype, device=device)
         layers = hidden_layers + 1
-        # inside the trainer's step the 16-bit mirror of the parameters (the values autocast's casts give) is
-        # read instead of the fp32 masters: half the bytes for the weight packing
-        src = live_mirrors(params, x.dtype) or params
-        weights = [src[2 * nb * l + b] for l in range(layers) for b in range(nb)]
-        biases = [src[2 * nb * l + nb + b] for l in range(layers) for b in range(nb)]
+        weights = [params[2 * nb * l + b] for l in range(layers) for b in range(nb)]
+        biases = [params[2 * nb * l + nb + b] for l in range(layers) for b in range(nb)]
         nat.call(
             "pmb_mask_estimator_tc_forward", x.data_ptr(), rows, nb, dim, hidden, hidden_layers, warr,
             nat.ptr_array(weights), nat.ptr_array(biases), packed.data_ptr(), acts.data_ptr(), pre.data_ptr(),
-            out.data_ptr(), nat.dtype_code(x.dtype), nat.dtype_code(src[0].dtype), nat.stream_handle(device),
+            out.data_ptr(), nat.dtype_code(x.dtype), nat.dtype_code(params[0].dtype), nat.stream_handle(device),
         )
         ctx.meta = (widths, hidden_layers, hidden, int(sizes[3]))
         ctx.save_for_backward(x, packed, acts, pre, *params)
@@ -292,19 +325,6 @@ def lowp_weight(p: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
     return p.to(dtype)
 
 
-def live_mirrors(params, dtype: torch.dtype):
-    """The trainer's live 16-bit mirrors of all of ``params`` (see lowp_weight), or None when any parameter
-    has none (outside the trainer's step): never a mix, and never a cast."""
-    out = []
-    for p in params:
-        half = getattr(p, "_pmb_half", None)
-        live = getattr(p, "_pmb_half_live", None)
-        if half is None or live is None or not live[0] or half.dtype != dtype:
-            return None
-        out.append(half)
-    return out
-
-
 class OutProjFn(torch.autograd.Function):
     """residual + gated W^T in one GEMM (torch.addmm with the residual as C), W in the activation type; the
     gradients are those autograd gives through W.to(dtype), with the same products: grad_gated = g W,
@@ -326,6 +346,15 @@ class OutProjFn(torch.autograd.Function):
         return g, g_gated, g_w
 
 
+def _input_grad(gqkv, w, gx_pass, shape):
+    """gqkv W, plus the gradient that reached the input through its pass-through output (the head gate's input
+    gradient) as the GEMM's C operand: one GEMM instead of a GEMM and an elementwise sum."""
+    if gx_pass is None:
+        return torch.matmul(gqkv, w).reshape(shape)
+    c = gx_pass.reshape(gqkv.shape[0], w.shape[1]).to(gqkv.dtype)
+    return torch.addmm(c, gqkv, w).reshape(shape)
+
+
 class QKVRotaryFn(torch.autograd.Function):
     """xn [b, n, D] -> q, k, v [b, h, n, dh]: projection, split, rotary on q/k.
 
@@ -342,10 +371,13 @@ class QKVRotaryFn(torch.autograd.Function):
     Otherwise (fp32, other shapes): a torch projection plus the split kernel.
     The backward merges the three gradients, in whatever layout the attention
     backward produced them, with the inverse rotation (pmb_qkv_rotary_merge)
-    and runs the two projection-gradient GEMMs."""
+    and runs the two projection-gradient GEMMs.  With ``pass_x`` xn is also
+    returned, for another consumer of the same input (the head gate): the
+    gradient coming back through it is the C operand of the input-gradient
+    GEMM, so the two gradients of xn are not summed by a separate pass."""
 
     @staticmethod
-    def forward(ctx, xn, weight, cos, sin, cos_t, sin_t, heads, inner=1):
+    def forward(ctx, xn, weight, cos, sin, cos_t, sin_t, heads, inner=1, pass_x=False):
         device = nat.require_cuda(xn, weight, name="QKVRotary")
         b, n, d = xn.shape
         dh = weight.shape[0] // (3 * heads)
@@ -378,10 +410,10 @@ class QKVRotaryFn(torch.autograd.Function):
         ctx.inner = inner
         ctx.weight_dtype = weight.dtype
         ctx.save_for_backward(x2, w, cos, sin)
-        return q, k, v
+        return (q, k, v, xn) if pass_x else (q, k, v)
 
     @staticmethod
-    def backward(ctx, gq, gk, gv):
+    def backward(ctx, gq, gk, gv, gx_pass=None):
         x2, w, cos, sin = ctx.saved_tensors
         heads = ctx.heads
         device = x2.device
@@ -398,9 +430,9 @@ class QKVRotaryFn(torch.autograd.Function):
             nat.ptr(sin), b, n, heads, dh, gqkv.data_ptr(), int(cos is not None), nat.dtype_code(x2.dtype),
             strides[0], strides[1], strides[2], ctx.inner, nat.stream_handle(device),
         )
-        gx = torch.matmul(gqkv, w).reshape(b, n, -1) if ctx.needs_input_grad[0] else None
+        gx = _input_grad(gqkv, w, gx_pass, (b, n, -1)) if ctx.needs_input_grad[0] else None
         gw = torch.matmul(gqkv.t(), x2).to(ctx.weight_dtype) if ctx.needs_input_grad[1] else None
-        return gx, gw, None, None, None, None, None, None
+        return gx, gw, None, None, None, None, None, None, None
 
 
 class FeedForwardFn(torch.autograd.Function):
@@ -582,12 +614,13 @@ class QKVAttentionFn(torch.autograd.Function):
     o [b, h, n, 64], a view of a [b, n, h, 64] plane.  The forward is those two ops.  The backward writes dQ and
     dK rotated back to the projection's space, and dV, straight into the [b * n, 3 * h * 64] projection gradient
     (pmb_attention_backward_rotary given strided views of it), so QKVRotaryFn.backward's merge pass and its
-    round trip of that gradient go; the two projection-gradient GEMMs follow as there.  Reference semantics:
+    round trip of that gradient go; the two projection-gradient GEMMs follow as there (``pass_x`` as there).
+    Reference semantics:
     qkv_to_bnhd + rotary + scaled-dot-product attention of the patched Attention.forward
     (src/pymsst/training/fused_roformer.py:793-818)."""
 
     @staticmethod
-    def forward(ctx, xn, weight, cos, sin, cos_t, sin_t, heads):
+    def forward(ctx, xn, weight, cos, sin, cos_t, sin_t, heads, pass_x=False):
         device = nat.require_cuda(xn, weight, name="QKVAttention")
         b, n, d = xn.shape
         dh = weight.shape[0] // (3 * heads)
@@ -619,10 +652,10 @@ class QKVAttentionFn(torch.autograd.Function):
         )
         ctx.weight_dtype = weight.dtype
         ctx.save_for_backward(x2, w, cos, sin, q, k, v, o, lse)
-        return o
+        return (o, xn) if pass_x else o
 
     @staticmethod
-    def backward(ctx, grad):
+    def backward(ctx, grad, gx_pass=None):
         x2, w, cos, sin, q, k, v, o, lse = ctx.saved_tensors
         device = q.device
         b, h, n, dh = q.shape
@@ -641,9 +674,9 @@ class QKVAttentionFn(torch.autograd.Function):
                      dk.data_ptr(), dv.data_ptr(), *tail)
         else:
             nat.call("pmb_attention_backward", *head, dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), *tail)
-        gx = torch.matmul(gqkv, w).reshape(b, n, -1) if ctx.needs_input_grad[0] else None
+        gx = _input_grad(gqkv, w, gx_pass, (b, n, -1)) if ctx.needs_input_grad[0] else None
         gw = torch.matmul(gqkv.t(), x2).to(ctx.weight_dtype) if ctx.needs_input_grad[1] else None
-        return gx, gw, None, None, None, None, None
+        return gx, gw, None, None, None, None, None, None
 
 
 class STFTFramesFn(torch.autograd.Function):

@@ -408,7 +408,13 @@ def op_mask(bench: _Bench):
     bench.time("mask_estimator_tc fwd+bwd", fwd_bwd, 3 * byt, 3 * flops)
 
 
-OPS = {"gate": op_gate, "band": op_band, "mel": op_mel, "mask": op_mask, "rms": op_rms, "qkv": op_qkv, "ff": op_ff, "sdpa": op_sdpa, "attn": op_attn}
+def op_band_sweep(bench: _Bench):
+    """BandSplit at the config-2 sweep size (8192 rows), for profiling it alone."""
+    _op_band_rows(bench, 8 * 1024)
+
+
+OPS = {"gate": op_gate, "band": op_band, "band8192": op_band_sweep, "mel": op_mel, "mask": op_mask, "rms": op_rms,
+       "qkv": op_qkv, "ff": op_ff, "sdpa": op_sdpa, "attn": op_attn}
 
 
 # ---------------------------------------------------------------------------

@@ -57,6 +57,7 @@ from .fused import (
     QKVAttentionFn,
     QKVRotaryFn,
     RMSNormFn,
+    RMSNormResidualFn,
     compute_dtype,
     rotary_tables,
     attention_supported,
@@ -120,6 +121,11 @@ class RMSNorm(nn.Module):
 
     def forward(self, x):
         return RMSNormFn.apply(x, self.gamma)
+
+    def with_residual(self, x):
+        """(norm(x), x) for a pre-norm residual block: use the second output for the residual branch, so the
+        backward adds that branch's gradient of x in the norm's own pass."""
+        return RMSNormResidualFn.apply(x, self.gamma)
 
 
 class RotaryEmbedding(nn.Module):
@@ -213,21 +219,27 @@ class Attention(nn.Module):
         n = x.shape[-2] if seq_len is None else seq_len
         rows = x.numel() // d
         b = rows // n
-        xn = self.norm(x)
+        if residual is x:
+            # the residual branch's gradient of x is added in the norm's backward pass
+            xn, residual = self.norm.with_residual(x)
+        else:
+            xn = self.norm(x)
         cos = sin = cos_t = sin_t = None
         if self.rotary_embed is not None:
             cos, sin, cos_t, sin_t = self.rotary_embed.tables(n, x.device)
         dropout_p = self.dropout if self.training else 0.0
+        # the projection passes xn through to the head gate, so the gate's gradient of xn joins the projection's
+        # input gradient in one GEMM
         if (inner == 1 and xn.is_cuda and xn.dtype in (torch.bfloat16, torch.float16) and d % 8 == 0
                 and self.dim_head == 64 and dropout_p == 0.0 and _own_attention(n, self.attention_backend)):
             # sequences in row order on the own kernels: the attention backward writes the projection gradient
-            attn = QKVAttentionFn.apply(xn.reshape(b, n, d), self.to_qkv.weight, cos, sin, cos_t, sin_t,
-                                        self.heads)
+            attn, xg = QKVAttentionFn.apply(xn.reshape(b, n, d), self.to_qkv.weight, cos, sin, cos_t, sin_t,
+                                            self.heads, True)
         else:
-            q, k, v = QKVRotaryFn.apply(xn.reshape(b, n, d), self.to_qkv.weight, cos, sin, cos_t, sin_t,
-                                        self.heads, inner)
+            q, k, v, xg = QKVRotaryFn.apply(xn.reshape(b, n, d), self.to_qkv.weight, cos, sin, cos_t, sin_t,
+                                            self.heads, inner, True)
             attn = _attention(q, k, v, dropout_p, self.attention_backend)
-        gated = AttentionGateFn.apply(attn, xn.reshape(rows, d), self.to_gates.weight, self.to_gates.bias, inner)
+        gated = AttentionGateFn.apply(attn, xg.reshape(rows, d), self.to_gates.weight, self.to_gates.bias, inner)
         drop = self.to_out[1]
         if residual is not None and (not self.training or drop.p == 0.0):
             # residual + gated W^T in one GEMM (C = residual, beta = 1)
@@ -245,9 +257,16 @@ class FeedForward(nn.Module):
             RMSNorm(dim), nn.Linear(dim, inner), nn.GELU(), nn.Dropout(dropout), nn.Linear(inner, dim), nn.Dropout(dropout)
         )
 
-    def forward(self, x):
-        dt = x.dtype
-        h = self.net[0](x)
+    def forward(self, x, add_residual=False):
+        """ff(x), or ff(x) + x with ``add_residual`` (the residual branch's gradient of x then joins the norm's
+        backward pass)."""
+        if add_residual:
+            h, res = self.net[0].with_residual(x)
+            return self._ff(h) + res
+        return self._ff(self.net[0](x))
+
+    def _ff(self, h):
+        dt = h.dtype
         lin1, lin2 = self.net[1], self.net[4]
         dropout_live = self.training and (self.net[3].p > 0 or self.net[5].p > 0)
         if h.dtype in (torch.bfloat16, torch.float16) and not dropout_live and h.shape[-1] % 8 == 0 and \
@@ -284,7 +303,7 @@ class Transformer(nn.Module):
         """x [b, n, d], or rows in (outer, position, inner) order (see Attention.forward)."""
         for attn, ff in self.layers:
             x = attn(x, seq_len, inner, residual=x)
-            x = ff(x) + x
+            x = ff(x, add_residual=True)
         return self.norm(x)
 
 

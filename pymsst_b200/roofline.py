@@ -42,6 +42,9 @@ def work(name: str, a: tuple) -> tuple[float, float]:
         rows, dim, gd, gmd, gxd = a[7], a[8], a[9], a[10], a[11]
         return rows * dim * (2 * ES[gd] + (ES[gxd] if a[5] is not None else 0)) + 4 * rows + 2 * dim * ES[gmd], \
             8.0 * rows * dim
+    if name == "pmb_rms_norm_backward_add":  # dy, x and the residual gradient read, grad_x written
+        rows, dim, gd, gmd, gxd = a[8], a[9], a[10], a[11], a[12]
+        return rows * dim * (2 * ES[gd] + 2 * ES[gxd]) + 4 * rows + 2 * dim * ES[gmd], 9.0 * rows * dim
     if name in ("pmb_qkv_rotary_split", "pmb_qkv_rotary_merge"):
         b, n, h, dh = (a[3], a[4], a[5], a[6]) if name.endswith("split") else (a[5], a[6], a[7], a[8])
         dt = a[11]
@@ -130,6 +133,10 @@ def work(name: str, a: tuple) -> tuple[float, float]:
         plane = seqs * n * h * dh * ES[dt]
         # q, k, v, o, dO read; dQ, dK, dV written; lse read, D written and read back
         return 8.0 * plane + 12.0 * seqs * h * n, 10.0 * seqs * h * n * n * dh
+    if name == "pmb_attention_backward_rotary":  # the same, plus the two fp32 angle tables
+        seqs, n, h, dh, dt = a[11], a[12], a[13], a[14], a[17]
+        plane = seqs * n * h * dh * ES[dt]
+        return 8.0 * plane + 12.0 * seqs * h * n + 2 * 4.0 * n * dh // 2, 10.0 * seqs * h * n * n * dh
     if name in ("pmb_stft_frames_forward", "pmb_stft_frames_backward"):
         b, length, n_fft, frames = a[3], a[4], a[5], a[7]
         return 4.0 * (b * length + b * frames * n_fft + n_fft), 1.0 * b * frames * n_fft

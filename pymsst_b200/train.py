@@ -140,6 +140,7 @@ class Trainer:
         self._ready_order: list[int] | None = None
         self.bucket_launches = 0  # bucketed all-reduces issued so far (host-side count)
         self._profiling = False
+        self._hook_handles: list = []
         opt_params = params
         if self.flat:
             self._build_flat(list(range(len(params))))
@@ -148,13 +149,27 @@ class Trainer:
                 dist.broadcast(self.flat_param.data, 0)
             opt_params = [self.flat_param]
             if self.overlap:
-                for i, p in enumerate(params):
-                    p.register_post_accumulate_grad_hook(self._grad_ready_hook(i))
+                self._hook_handles = [p.register_post_accumulate_grad_hook(self._grad_ready_hook(i))
+                                      for i, p in enumerate(params)]
         self.optimizer = torch.optim.Adam(opt_params, lr=lr, fused=fused_adam and on_cuda,
                                           capturable=self.cuda_graph)
         self._graph = None
         self._static = None
         self.launches_per_step = None  # this package's kernels in one captured step
+
+    def close(self) -> None:
+        """Release the captured step (which holds this trainer's NCCL calls when distributed) and the gradient
+        hooks.  Call it before destroy_process_group: a live graph with captured collectives keeps the process
+        group's teardown waiting, and the hooks (closures over the trainer) keep the trainer, and so its graph,
+        alive until a garbage collection."""
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
+        for h in self._hook_handles:
+            h.remove()
+        self._hook_handles = []
+        self._works = []
+        self._graph = None
+        self._static = None
 
     # ------------------------------------------------------------- flat layout
     def _build_flat(self, order: list[int]):

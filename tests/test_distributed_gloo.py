@@ -117,6 +117,9 @@ def _flat_worker(rank, world, port, out, overlap):
         gathered = [torch.empty_like(params) for _ in range(world)]
         dist.all_gather(gathered, params)
         out[rank] = ([t.tolist() for t in gathered], len(trainer._buckets), trainer.bucket_launches)
+        trainer.close()  # hooks removed: a further backward launches no all-reduce
+        model(torch.randn(2, 8), torch.randn(2, 4)).backward()
+        assert trainer.bucket_launches == out[rank][2]
     finally:
         dist.destroy_process_group()
 

@@ -84,6 +84,57 @@ def test_rms_norm_backward_from_saved_input(cuda_device, dtype):
     torch.testing.assert_close(gg.double().cpu(), r_gg, rtol=1e-4, atol=1e-2)
 
 
+# bulk (rows of 192 / 384), vector (dim 1536 > the bulk limit) and generic (dim 37, unaligned) kernels
+@pytest.mark.parametrize("rows,dim", [(4096, 192), (777, 384), (300, 1536), (65, 37)])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_rms_norm_backward_adds_the_residual_gradient(cuda_device, rows, dim, dtype):
+    """pmb_rms_norm_backward_add: grad_x = RMSNorm'(dy) + grad_residual in the norm's own pass, against the
+    float64 oracle's RMSNorm' plus the residual gradient (one 16-bit rounding of the sum)."""
+    g = torch.Generator().manual_seed(rows + dim)
+    x = torch.randn(rows, dim, generator=g).to(dtype).to(cuda_device)
+    gamma = (torch.rand(dim, generator=g) + 0.5).to(cuda_device)
+    dy = torch.randn(rows, dim, generator=g).to(dtype).to(cuda_device)
+    res = torch.randn(rows, dim, generator=g).to(dtype).to(cuda_device)
+    _, normed32, inv = ops.rms_norm_forward_mixed(x, gamma) if dtype != torch.float32 else ops.rms_norm_forward(x, gamma)
+    gx, gg = rms_norm_backward_into(dy, x, inv, gamma, saved_is_input=True, grad_x_dtype=dtype,
+                                    grad_gamma_dtype=torch.float32, grad_residual=res)
+    plain, gg0 = rms_norm_backward_into(dy, x, inv, gamma, saved_is_input=True, grad_x_dtype=dtype,
+                                        grad_gamma_dtype=torch.float32)
+    r_gx, r_gg = ops_ref.rms_norm_backward(dy.double().cpu(), normed32.double().cpu(), inv.double().cpu(),
+                                           gamma.double().cpu())
+    _close(gx, r_gx + res.double().cpu(), dtype, scale=float(res.abs().max()))
+    assert torch.equal(gg, gg0)  # the gamma gradient does not see the residual
+    if dtype == torch.float32:
+        torch.testing.assert_close(gx, plain + res, rtol=1e-6, atol=1e-6)
+
+
+def test_rms_norm_residual_fn_matches_norm_plus_sum(cuda_device):
+    """RMSNormResidualFn (y, x) used as a pre-norm residual block gives the gradients of RMSNormFn plus an
+    autograd sum."""
+    from pymsst_b200.fused import RMSNormFn, RMSNormResidualFn
+
+    g = torch.Generator().manual_seed(11)
+    x0 = torch.randn(2, 300, 192, generator=g).to(torch.bfloat16).to(cuda_device)
+    gamma0 = (torch.rand(192, generator=g) + 0.5).to(cuda_device)
+    w = torch.randn(192, 192, generator=g).to(torch.bfloat16).to(cuda_device) / 14
+
+    def run(fused):
+        x, gamma = x0.clone().requires_grad_(), gamma0.clone().requires_grad_()
+        if fused:
+            y, r = RMSNormResidualFn.apply(x, gamma)
+        else:
+            y, r = RMSNormFn.apply(x, gamma), x
+        out = (y @ w) + r
+        out.float().square().sum().backward()
+        return out.detach(), x.grad, gamma.grad
+
+    o1, gx1, gg1 = run(True)
+    o2, gx2, gg2 = run(False)
+    assert torch.equal(o1, o2)
+    torch.testing.assert_close(gx1.float(), gx2.float(), rtol=1e-2, atol=1e-2 * float(gx2.abs().max()))
+    torch.testing.assert_close(gg1, gg2, rtol=1e-5, atol=1e-5 * float(gg2.abs().max()))
+
+
 def test_rms_norm_zero_rows_and_zero_vector(cuda_device):
     x = torch.zeros(3, 192, device=cuda_device)
     gamma = torch.ones(192, device=cuda_device)
