@@ -220,26 +220,33 @@ struct BandOutEpi {
   int first[kMaxBands];
   float sqrt_w[kMaxBands];
   const void* bias[kMaxBands];
-  template <int BN>
-  __device__ void run(const ugemm::Plan&, const ugemm::TileCtx& t) const {
-    constexpr int kMaxChunks = (BN / 32 + ugemm::kSubs - 1) / ugemm::kSubs;
-    const int lane = threadIdx.x & 31;
-    const int64_t ld = (int64_t)nb * O;
-    // scale and bias of every chunk this warp drains, loaded before the first tensor-memory read so their
-    // latencies overlap (one round trip per tile instead of one per chunk)
+  // row scale and bias of every chunk a warp drains (BN <= 256: at most 3 chunks per warp), loaded by the
+  // engine one tile ahead (prefetch), so their latency is hidden behind the previous tile's epilogue
+  static constexpr int kMaxChunks = (256 / 32 + ugemm::kSubs - 1) / ugemm::kSubs;
+  struct Pre {
     float sc[kMaxChunks], bl[kMaxChunks];
+  };
+  __device__ void prefetch(const ugemm::Plan&, const ugemm::TileCtx& t, Pre& p) const {
+    const int lane = threadIdx.x & 31;
 #pragma unroll
     for (int q = 0; q < kMaxChunks; ++q) {
       const int c0 = 32 * (t.sub + q * ugemm::kSubs);
-      sc[q] = bl[q] = 0.f;
-      if (c0 < BN && c0 < t.n_valid) {
+      p.sc[q] = p.bl[q] = 0.f;
+      if (c0 < t.n_valid) {
         const int n = t.n0 + c0;
         const int b = first[t.group] + n / O, o0 = n % O;
         const TP* bp = static_cast<const TP*>(bias[b]);
-        sc[q] = t.row_valid ? inv[(int64_t)t.row * nb + b] * sqrt_w[b] : 0.f;
-        bl[q] = (bp != nullptr && lane < t.n_valid - c0) ? Elem<TP>::to_f(bp[o0 + lane]) : 0.f;
+        p.sc[q] = t.row_valid ? inv[(int64_t)t.row * nb + b] * sqrt_w[b] : 0.f;
+        p.bl[q] = (bp != nullptr && lane < t.n_valid - c0) ? Elem<TP>::to_f(bp[o0 + lane]) : 0.f;
       }
     }
+  }
+  template <int BN>
+  __device__ void run(const ugemm::Plan&, const ugemm::TileCtx& t, const Pre& p) const {
+    static_assert(BN <= 256, "at most kMaxChunks chunks per warp");
+    const int64_t ld = (int64_t)nb * O;
+    const float* sc = p.sc;
+    const float* bl = p.bl;
 #pragma unroll
     for (int q = 0; q < kMaxChunks; ++q) {
       const int c0 = 32 * (t.sub + q * ugemm::kSubs);

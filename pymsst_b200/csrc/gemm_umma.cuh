@@ -30,6 +30,8 @@
 // frees its TMEM and exits, leaving the site in g_umma_timeout.
 #pragma once
 
+#include <type_traits>
+
 #include "umma.cuh"
 
 namespace pmb {
@@ -107,6 +109,24 @@ struct TileCtx {
   uint32_t taddr;  // TMEM address of this thread's row, column 0 of the tile
   uint8_t* stage;  // this warp's staging block (kStageWarpBytes)
   int* store_seq;  // this thread's count of TMA tile stores issued so far (picks the staging buffer)
+};
+
+// Epilogues with per-tile global operands (row scales, bias slices) may
+// declare `struct Pre` and `prefetch(plan, ctx, Pre&)`: the epilogue warps
+// then issue tile i+1's loads before they drain tile i, and run(plan, ctx,
+// pre) receives values loaded an epilogue earlier, so the loads' latency is
+// hidden behind the previous tile instead of sitting on every tile.
+template <class E, class = void>
+struct HasPre : std::false_type {};
+template <class E>
+struct HasPre<E, std::void_t<typename E::Pre>> : std::true_type {};
+template <class E, bool = HasPre<E>::value>
+struct PreOf {
+  struct type {};
+};
+template <class E>
+struct PreOf<E, true> {
+  using type = typename E::Pre;
 };
 
 // Locate tile `tile` of the plan: group, M / N origin.
@@ -404,12 +424,38 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* stage = staging + (warp - 2) * kStageWarpBytes;
     int store_seq = 0;
     uint32_t local = 0;
-    for (int tile = blockIdx.x; tile < plan.total_tiles; tile += gridDim.x, ++local) {
-      if (abort_flag) break;
+    auto ctx_of = [&](int tile, uint32_t buf) {
       int gi, m0, n0;
       locate(plan, tile, BN, gi, m0, n0);
       const Group& G = plan.g[gi];
+      TileCtx t;
+      t.group = gi;
+      t.sub = sub;
+      t.m0 = m0;
+      t.n0 = n0;
+      t.row0 = m0 + quarter * 32;
+      t.row = t.row0 + lane;
+      t.row_valid = t.row < G.m;
+      t.rows_valid = max(0, min(32, G.m - t.row0));
+      t.n_valid = min(BN, G.n - n0);
+      t.taddr = tmem + buf * BN + ((uint32_t)(quarter * 32) << 16);
+      t.stage = stage;
+      t.store_seq = &store_seq;
+      return t;
+    };
+    // this tile's prefetched operands and the next tile's (copied over at the end of each tile: no
+    // dynamically indexed register arrays)
+    typename PreOf<Epi>::type pre_cur, pre_next;
+    if constexpr (HasPre<Epi>::value) {
+      if ((int)blockIdx.x < plan.total_tiles) epi.prefetch(plan, ctx_of(blockIdx.x, 0), pre_cur);
+    }
+    for (int tile = blockIdx.x; tile < plan.total_tiles; tile += gridDim.x, ++local) {
+      if (abort_flag) break;
       const uint32_t buf = local & 1, use = local >> 1;
+      if constexpr (HasPre<Epi>::value) {  // the next tile's loads, in flight while this one drains
+        if (tile + (int)gridDim.x < plan.total_tiles)
+          epi.prefetch(plan, ctx_of(tile + gridDim.x, buf ^ 1), pre_next);
+      }
       if (!umma::mbar_wait(&tfull[buf], use & 1, 3)) {
         abort_flag = 1;
         break;
@@ -417,21 +463,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       umma::tc_fence_after();
       __syncwarp();
       if (!abort_flag) {
-        TileCtx t;
-        t.group = gi;
-        t.sub = sub;
-        t.m0 = m0;
-        t.n0 = n0;
-        t.row0 = m0 + quarter * 32;
-        t.row = t.row0 + lane;
-        t.row_valid = t.row < G.m;
-        t.rows_valid = max(0, min(32, G.m - t.row0));
-        t.n_valid = min(BN, G.n - n0);
-        t.taddr = tmem + buf * BN + ((uint32_t)(quarter * 32) << 16);
-        t.stage = stage;
-        t.store_seq = &store_seq;
-        epi.template run<BN>(plan, t);
+        const TileCtx t = ctx_of(tile, buf);
+        if constexpr (HasPre<Epi>::value)
+          epi.template run<BN>(plan, t, pre_cur);
+        else
+          epi.template run<BN>(plan, t);
       }
+      if constexpr (HasPre<Epi>::value) pre_cur = pre_next;
       umma::tc_fence_before();
       __syncwarp();
       if (lane == 0) umma::mbar_arrive(&tempty[buf]);

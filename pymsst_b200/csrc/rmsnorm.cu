@@ -10,6 +10,8 @@
 // :1237-1247 and :1263-1286).
 #include <mutex>
 
+#include <type_traits>
+
 #include "common.cuh"
 #include "reduce.cuh"
 #include "umma.cuh"
@@ -404,15 +406,18 @@ __global__ void __launch_bounds__(kThreads, 4)
   if (threadIdx.x == 0) umma::bulk_wait_all();
 }
 
-template <typename Tg, typename Tdx, int V, int G, int NJ>
-__global__ void __launch_bounds__(kThreads, 3)
+// RES: a third input, the residual branch's gradient (Tdx, same layout as dx), staged through the same ring
+// and added to grad_x.
+template <typename Tg, typename Tdx, int V, int G, int NJ, bool RES>
+__global__ void __launch_bounds__(kThreads, RES ? 2 : 3)
     rms_bwd_bulk(const Tg* __restrict__ dy, const Tg* __restrict__ saved, int saved_is_input,
                  const float* __restrict__ inv_norm, const void* __restrict__ gamma, int gcode, Tdx* __restrict__ dx,
                  const Tdx* __restrict__ dres, float* __restrict__ partial, int64_t rows, int dim, int rpt) {
   constexpr int RW = 32 / G;
+  constexpr int IN = RES ? 3 : 2;  // staged inputs per ring slot
   extern __shared__ __align__(128) uint8_t smem[];
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kBwdStageBytes * 2);
-  float* g_s = reinterpret_cast<float*>(smem + kStages * kBwdStageBytes * 2 + 128);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kBwdStageBytes * IN);
+  float* g_s = reinterpret_cast<float*>(smem + kStages * kBwdStageBytes * IN + 128);
   float* red = reinterpret_cast<float*>(smem);  // reused after the ring drains: [kWarps * RW][dim]
   const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
   const int gl = lane % G, sub = lane / G;
@@ -429,10 +434,11 @@ __global__ void __launch_bounds__(kThreads, 3)
     const int64_t r0 = tile * rpt;
     const int64_t n = rows - r0 < rpt ? rows - r0 : rpt;
     const uint32_t bytes = (uint32_t)(n * dim * (int64_t)sizeof(Tg));
-    uint8_t* base = smem + st * kBwdStageBytes * 2;
-    umma::mbar_arrive_expect_tx(&full[st], 2 * bytes);
+    uint8_t* base = smem + st * kBwdStageBytes * IN;
+    umma::mbar_arrive_expect_tx(&full[st], IN * bytes);
     umma::bulk_load(base, dy + r0 * dim, bytes, &full[st]);
     umma::bulk_load(base + kBwdStageBytes, saved + r0 * dim, bytes, &full[st]);
+    if constexpr (RES) umma::bulk_load(base + 2 * kBwdStageBytes, dres + r0 * dim, bytes, &full[st]);
   };
   if (threadIdx.x == 0)
     for (int st = 0; st < kStages; ++st) {
@@ -454,8 +460,9 @@ __global__ void __launch_bounds__(kThreads, 3)
     const float inv_l = qi < n ? inv_norm[r0 + qi] : 0.f;
     // every thread takes the same decision, so no thread is left at a barrier
     if (__syncthreads_or(!umma::mbar_wait(&full[st], (it / kStages) & 1, 0x22))) break;
-    Tg* ds_ = reinterpret_cast<Tg*>(smem + st * kBwdStageBytes * 2);
-    const Tg* ss_ = reinterpret_cast<const Tg*>(smem + st * kBwdStageBytes * 2 + kBwdStageBytes);
+    Tg* ds_ = reinterpret_cast<Tg*>(smem + st * kBwdStageBytes * IN);
+    const Tg* ss_ = reinterpret_cast<const Tg*>(smem + st * kBwdStageBytes * IN + kBwdStageBytes);
+    const Tdx* rs_ = reinterpret_cast<const Tdx*>(smem + st * kBwdStageBytes * IN + 2 * kBwdStageBytes);
     int step = 0;
     for (int qb = wib * RW; qb < n; qb += kWarps * RW, ++step) {
       const int q = qb + sub;
@@ -493,7 +500,14 @@ __global__ void __launch_bounds__(kThreads, 3)
             const Pack<Tg, V> ps = *reinterpret_cast<const Pack<Tg, V>*>(ss_ + q * dim + vi * V);
             const float* gv = g_s + vi * V;
             float add[V];
-            load_res<Tdx, V>(dres, (r0 + q) * dim + (int64_t)vi * V, add);
+            if constexpr (RES) {
+              const Pack<Tdx, V> pr = *reinterpret_cast<const Pack<Tdx, V>*>(rs_ + q * dim + vi * V);
+#pragma unroll
+              for (int e = 0; e < V; ++e) add[e] = Elem<Tdx>::to_f(pr.v[e]);
+            } else {
+#pragma unroll
+              for (int e = 0; e < V; ++e) add[e] = 0.f;
+            }
             Pack<Tdx, V> p;
 #pragma unroll
             for (int e = 0; e < V; ++e) {
@@ -630,28 +644,36 @@ int launch_bwd(const void* dy, const void* saved, int saved_is_input, const floa
       (int64_t)kWarps * 4 * dim * 4 <= (int64_t)kStages * kBwdStageBytes * 2) {
     const int rpt = (int)(kBwdStageBytes / row_bytes < kMaxBwdTileRows ? kBwdStageBytes / row_bytes : kMaxBwdTileRows);
     const int64_t tiles = (rows + rpt - 1) / rpt;
-    int64_t g = (int64_t)num_sms() * 3;  // 3 CTAs of 64 KB shared memory per SM
+    // 3 CTAs of 68 KB shared memory per SM (2 of 100 KB with the residual gradient staged as a third input)
+    int64_t g = (int64_t)num_sms() * (drp ? 2 : 3);
     if (g > kMaxBwdBlocks) g = kMaxBwdBlocks;
     if (g > tiles) g = tiles;
     used_grid = (int)g;
-    constexpr int bsm = bulk_smem_bytes<kBwdStageBytes, 2>();
-    auto go = [&](auto kern) {
+    auto go = [&](auto kern, int bsm) {
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bsm);
       kern<<<used_grid, kThreads, bsm, stream>>>(dyp, sp, saved_is_input, inv, gamma, gcode, dxp, drp, partial,
                                                  rows, (int)dim, rpt);
     };
-    if (nvec <= 8)
-      go(rms_bwd_bulk<Tg, Tdx, V, 8, 1>);
-    else if (nvec <= 24)
-      go(rms_bwd_bulk<Tg, Tdx, V, 8, 3>);
-    else if (nvec <= 48)
-      go(rms_bwd_bulk<Tg, Tdx, V, 16, 3>);
-    else if (nvec <= 64)
-      go(rms_bwd_bulk<Tg, Tdx, V, 32, 2>);
-    else if (nvec <= 128)
-      go(rms_bwd_bulk<Tg, Tdx, V, 32, 4>);
-    else if constexpr (V == 4)
-      go(rms_bwd_bulk<Tg, Tdx, V, 32, 8>);
+    auto pick = [&](auto res) {
+      constexpr bool R = decltype(res)::value;
+      constexpr int bsm = bulk_smem_bytes<kBwdStageBytes, R ? 3 : 2>();
+      if (nvec <= 8)
+        go(rms_bwd_bulk<Tg, Tdx, V, 8, 1, R>, bsm);
+      else if (nvec <= 24)
+        go(rms_bwd_bulk<Tg, Tdx, V, 8, 3, R>, bsm);
+      else if (nvec <= 48)
+        go(rms_bwd_bulk<Tg, Tdx, V, 16, 3, R>, bsm);
+      else if (nvec <= 64)
+        go(rms_bwd_bulk<Tg, Tdx, V, 32, 2, R>, bsm);
+      else if (nvec <= 128)
+        go(rms_bwd_bulk<Tg, Tdx, V, 32, 4, R>, bsm);
+      else if constexpr (V == 4)
+        go(rms_bwd_bulk<Tg, Tdx, V, 32, 8, R>, bsm);
+    };
+    if (drp != nullptr)
+      pick(std::true_type());
+    else
+      pick(std::false_type());
   } else if (vec_ok && nj * 32 * V <= 1024 && smem <= 48 * 1024) {
     if (nj <= 1)
       rms_bwd_vec<Tg, Tdx, V, 1><<<grid, kThreads, smem, stream>>>(dyp, sp, saved_is_input, inv, gamma, gcode, dxp,

@@ -139,6 +139,11 @@ def op_rms(bench: _Bench):
     bench.time("rms_norm_backward", lambda: nat.call(
         "pmb_rms_norm_backward", dy.data_ptr(), x.data_ptr(), 1, inv.data_ptr(), g.data_ptr(), gx.data_ptr(),
         gg.data_ptr(), ROWS, DIM, 2, 2, 2, 2, ws.data_ptr(), wsb, st), ROWS * DIM * 2 * 3 + ROWS * 4)
+    res = torch.randn_like(x)
+    bench.time("rms_norm_backward_add (+ residual gradient)", lambda: nat.call(
+        "pmb_rms_norm_backward_add", dy.data_ptr(), x.data_ptr(), 1, inv.data_ptr(), g.data_ptr(), res.data_ptr(),
+        gx.data_ptr(), gg.data_ptr(), ROWS, DIM, 2, 2, 2, 2, ws.data_ptr(), wsb, st), ROWS * DIM * 2 * 4 + ROWS * 4)
+    bench.time("torch add (the residual sum it replaces)", lambda: torch.add(gx, res, out=out), ROWS * DIM * 2 * 3)
 
 
 def op_qkv(bench: _Bench):
@@ -285,6 +290,33 @@ def op_attn(bench: _Bench):
 
         bench.time(f"attention fwd n={n}", fwd, by, fl_f)
         bench.time(f"attention fwd+bwd n={n}", run, by * 3, fl_f * 3.5)
+    _op_qkv_attention(bench)
+
+
+def _op_qkv_attention(bench: _Bench):
+    """Projection + rotary + attention on the band axis (62 positions), fwd+bwd: QKVAttentionFn (the attention
+    backward writes the projection gradient, rotated back) against QKVRotaryFn + AttentionFn (merge pass)."""
+    from .fused import AttentionFn, QKVAttentionFn, QKVRotaryFn, rotary_tables
+
+    dev, bf = bench.device, torch.bfloat16
+    nb, n = ROWS // 62, 62
+    x = torch.randn(nb, n, DIM, device=dev, dtype=bf).requires_grad_()
+    w = (torch.randn(3 * HEADS * DHEAD, DIM, device=dev) / DIM ** 0.5).requires_grad_()
+    freqs = 1.0 / (10000 ** (torch.arange(0, DHEAD, 2, device=dev).float() / DHEAD))
+    cos, sin = rotary_tables(freqs, n, dev)
+    cos_t, sin_t = cos.t().contiguous(), sin.t().contiguous()
+    gy = torch.randn(nb, HEADS, n, DHEAD, device=dev, dtype=bf)
+    by = ROWS * (DIM + 3 * HEADS * DHEAD) * 2 * 3
+
+    def fused():
+        _grads(QKVAttentionFn.apply(x, w, cos, sin, cos_t, sin_t, HEADS), [x, w], gy)
+
+    def split():
+        q, k, v = QKVRotaryFn.apply(x, w, cos, sin, cos_t, sin_t, HEADS)
+        _grads(AttentionFn.apply(q, k, v), [x, w], gy)
+
+    bench.time(f"qkv+attention fwd+bwd n={n} (QKVAttentionFn)", fused, by)
+    bench.time(f"qkv+attention fwd+bwd n={n} (QKVRotaryFn + AttentionFn)", split, by)
 
 
 def op_band(bench: _Bench):
