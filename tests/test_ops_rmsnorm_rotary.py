@@ -103,7 +103,8 @@ def test_rms_norm_backward_adds_the_residual_gradient(cuda_device, rows, dim, dt
     r_gx, r_gg = ops_ref.rms_norm_backward(dy.double().cpu(), normed32.double().cpu(), inv.double().cpu(),
                                            gamma.double().cpu())
     _close(gx, r_gx + res.double().cpu(), dtype, scale=float(res.abs().max()))
-    assert torch.equal(gg, gg0)  # the gamma gradient does not see the residual
+    # the gamma gradient does not see the residual (summed over a different grid: the same up to fp32 ordering)
+    torch.testing.assert_close(gg, gg0, rtol=1e-5, atol=1e-5 * float(gg0.abs().max()))
     if dtype == torch.float32:
         torch.testing.assert_close(gx, plain + res, rtol=1e-6, atol=1e-6)
 
