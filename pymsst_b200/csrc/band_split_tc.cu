@@ -137,38 +137,63 @@ struct Vec<T, 1> {
 };
 
 // ------------------------------------------------------------- forward prep
-// CTAs [0, row_ctas): s for rows r = blockIdx.x, + row_ctas, ...
+// CTAs [0, row_ctas): s for blocks of kPrepRows rows r0 = kPrepRows * blockIdx.x, + kPrepRows * row_ctas, ...
 // CTAs [row_ctas, ...): packed[row_g + n, k] = W_b[o, i] * gamma_b[i] (or 0)
 // for 8 consecutive k per thread.
+// Rows go kPrepRows at a time: every thread's loads of all of them are in
+// flight together, and one pass of the per-band warp reductions serves all of
+// them (a lane sums the band's chunk partials of every row, the warp reduces
+// them in a fixed order, and lanes 0..kPrepRows-1 finish one row each), so
+// the reduction overhead and the final reciprocal square roots are shared.
+constexpr int kPrepRows = 4;
+
 template <typename T, typename TP, int CH>
 __global__ void __launch_bounds__(kThreads)
     bs_prep_forward(const T* __restrict__ x, int64_t rows, int64_t ld, int row_ctas, BandTable tab, Layout L,
                  float* __restrict__ scale_out, T* __restrict__ packed) {
-  extern __shared__ float chunk_ss[];  // total / CH floats
+  extern __shared__ float chunk_ss[];  // [kPrepRows][total / CH]
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   if ((int)blockIdx.x < row_ctas) {
     using U = typename Vec<T, CH>::U;
     const int nchunks = L.total / CH;
-    for (int64_t r = blockIdx.x; r < rows; r += row_ctas) {
-      const U* xr = reinterpret_cast<const U*>(x + r * ld);
+    for (int64_t r0 = (int64_t)blockIdx.x * kPrepRows; r0 < rows; r0 += (int64_t)row_ctas * kPrepRows) {
+      const int nr = rows - r0 < kPrepRows ? (int)(rows - r0) : kPrepRows;
       for (int c = threadIdx.x; c < nchunks; c += kThreads) {
-        const U u = xr[c];
-        const T* e = reinterpret_cast<const T*>(&u);
-        float ss = 0.f;
+        U u[kPrepRows];
 #pragma unroll
-        for (int j = 0; j < CH; ++j) {
-          const float v = Elem<T>::to_f(e[j]);
-          ss = fmaf(v, v, ss);
+        for (int i = 0; i < kPrepRows; ++i)
+          if (i < nr) u[i] = reinterpret_cast<const U*>(x + (r0 + i) * ld)[c];
+#pragma unroll
+        for (int i = 0; i < kPrepRows; ++i) {
+          float ss = 0.f;
+          if (i < nr) {
+            const T* e = reinterpret_cast<const T*>(&u[i]);
+#pragma unroll
+            for (int j = 0; j < CH; ++j) {
+              const float v = Elem<T>::to_f(e[j]);
+              ss = fmaf(v, v, ss);
+            }
+          }
+          chunk_ss[i * nchunks + c] = ss;
         }
-        chunk_ss[c] = ss;
       }
       __syncthreads();
       for (int b = warp; b < L.nb; b += kThreads / 32) {
         const int c0 = L.off[b] / CH, c1 = (L.off[b] + L.w[b]) / CH;
-        float ss = 0.f;
-        for (int c = c0 + lane; c < c1; c += 32) ss += chunk_ss[c];
-        ss = warp_sum(ss);
-        if (lane == 0) scale_out[r * L.nb + b] = 1.0f / fmaxf(sqrtf(ss), 1.0e-12f);
+        float ss[kPrepRows];
+#pragma unroll
+        for (int i = 0; i < kPrepRows; ++i) ss[i] = 0.f;
+        for (int c = c0 + lane; c < c1; c += 32)
+#pragma unroll
+          for (int i = 0; i < kPrepRows; ++i) ss[i] += chunk_ss[i * nchunks + c];
+        float mine = 0.f;  // lane i ends with row i's band sum
+#pragma unroll
+        for (int i = 0; i < kPrepRows; ++i) {
+          const float t = warp_sum(ss[i]);
+          if (lane == i) mine = t;
+        }
+        // 1 / max(||x||, 1e-12) as min(rsqrt(ss), 1e12) (rsqrt(0) = inf)
+        if (lane < nr) scale_out[(r0 + lane) * L.nb + b] = fminf(rsqrtf(mine), 1.0e12f);
       }
       __syncthreads();
     }
@@ -268,18 +293,20 @@ struct BandOutEpi {
 };
 
 // ------------------------------------------------------------ backward prep
-// CTAs [0, row_ctas): normed[r, c] = x[r, c] * s[r, band(c)] * sqrt(w_band) for the band columns.
-// CTAs [row_ctas, ...): bias partials bpart[chunk][col] = sum over the chunk's 64 rows of dY[r, col].
+// CTAs [0, row_ctas): normed[r, c] = x[r, c] * s[r, band(c)] * sqrt(w_band) for the band columns, kPrepRows
+// rows per pass (all of their loads in flight together, one barrier pair per pass).
+// CTAs [row_ctas, ...): bias partials bpart[chunk][col] = sum over the chunk's kBiasRows rows of dY[r, col],
+// eight adjacent columns per thread (16-byte loads), eight rows in flight.
 template <typename T, int CH>
 __global__ void __launch_bounds__(kThreads)
     bs_prep_backward(const T* __restrict__ x, int64_t rows, int64_t ld, const float* __restrict__ inv, Layout L,
                   int row_ctas, T* __restrict__ normed, int64_t nld, const T* __restrict__ dy, int64_t cols,
                   float* __restrict__ bpart) {
-  extern __shared__ float sc_s[];  // nb scales of the current row, then the chunk -> band map
+  extern __shared__ float sc_s[];  // [kPrepRows][nb] scales of the pass's rows, then the chunk -> band map
   if ((int)blockIdx.x < row_ctas) {
     using U = typename Vec<T, CH>::U;
     const int nchunks = L.total / CH;
-    int* band_of_chunk = reinterpret_cast<int*>(sc_s + L.nb);
+    int* band_of_chunk = reinterpret_cast<int*>(sc_s + kPrepRows * L.nb);
     for (int c = threadIdx.x; c < nchunks; c += kThreads) {
       int lo = 0, hi = L.nb - 1;
       const int col = c * CH;
@@ -289,41 +316,64 @@ __global__ void __launch_bounds__(kThreads)
       }
       band_of_chunk[c] = lo;
     }
-    for (int64_t r = blockIdx.x; r < rows; r += row_ctas) {
+    for (int64_t r0 = (int64_t)blockIdx.x * kPrepRows; r0 < rows; r0 += (int64_t)row_ctas * kPrepRows) {
+      const int nr = rows - r0 < kPrepRows ? (int)(rows - r0) : kPrepRows;
       __syncthreads();
-      for (int b = threadIdx.x; b < L.nb; b += kThreads) sc_s[b] = inv[r * L.nb + b] * sqrtf((float)L.w[b]);
+      for (int k = threadIdx.x; k < nr * L.nb; k += kThreads) {
+        const int i = k / L.nb, b = k - i * L.nb;
+        sc_s[k] = inv[(r0 + i) * L.nb + b] * sqrtf((float)L.w[b]);
+      }
       __syncthreads();
-      const U* xr = reinterpret_cast<const U*>(x + r * ld);
-      U* nr = reinterpret_cast<U*>(normed + r * nld);
       for (int c = threadIdx.x; c < nchunks; c += kThreads) {
-        U u = xr[c];
-        T* e = reinterpret_cast<T*>(&u);
-        const float s = sc_s[band_of_chunk[c]];
+        U u[kPrepRows];
 #pragma unroll
-        for (int j = 0; j < CH; ++j) e[j] = Elem<T>::from_f(Elem<T>::to_f(e[j]) * s);
-        nr[c] = u;
+        for (int i = 0; i < kPrepRows; ++i)
+          if (i < nr) u[i] = reinterpret_cast<const U*>(x + (r0 + i) * ld)[c];
+        const int b = band_of_chunk[c];
+#pragma unroll
+        for (int i = 0; i < kPrepRows; ++i) {
+          if (i >= nr) break;
+          T* e = reinterpret_cast<T*>(&u[i]);
+          const float sc = sc_s[i * L.nb + b];
+#pragma unroll
+          for (int j = 0; j < CH; ++j) e[j] = Elem<T>::from_f(Elem<T>::to_f(e[j]) * sc);
+          reinterpret_cast<U*>(normed + (r0 + i) * nld)[c] = u[i];
+        }
       }
     }
     return;
   }
   const int64_t bid = (int64_t)blockIdx.x - row_ctas;
-  const int64_t col_blocks = (cols + kThreads - 1) / kThreads;
+  const int64_t col_blocks = (cols / 8 + kThreads - 1) / kThreads;
   const int64_t chunk = bid / col_blocks;
-  const int64_t c = (bid % col_blocks) * kThreads + threadIdx.x;
+  const int64_t c = ((bid % col_blocks) * kThreads + threadIdx.x) * 8;
   if (c >= cols) return;
   const int64_t r0 = chunk * kBiasRows;
   const int64_t r1 = r0 + kBiasRows < rows ? r0 + kBiasRows : rows;
-  // eight rows in flight per step (independent loads), summed in a fixed order
-  float s = 0.f;
+  float s[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) s[j] = 0.f;
   int64_t r = r0;
   for (; r + 8 <= r1; r += 8) {
-    float v[8];
+    uint4 v[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] = Elem<T>::to_f(dy[(r + j) * cols + c]);
-    s += ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
+    for (int k = 0; k < 8; ++k) v[k] = *reinterpret_cast<const uint4*>(dy + (r + k) * cols + c);
+    // rows summed pairwise in a fixed order
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float t[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) t[k] = Elem<T>::to_f(reinterpret_cast<const T*>(&v[k])[j]);
+      s[j] += ((t[0] + t[1]) + (t[2] + t[3])) + ((t[4] + t[5]) + (t[6] + t[7]));
+    }
   }
-  for (; r < r1; ++r) s += Elem<T>::to_f(dy[r * cols + c]);
-  bpart[chunk * cols + c] = s;
+  for (; r < r1; ++r) {
+    const uint4 v = *reinterpret_cast<const uint4*>(dy + r * cols + c);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s[j] += Elem<T>::to_f(reinterpret_cast<const T*>(&v)[j]);
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) bpart[chunk * cols + c + j] = s[j];
 }
 
 // G tile (rows o of O, columns n of band b's k-range, feature i = n - lead_b):
@@ -455,9 +505,10 @@ int run_gemm(const CUtensorMap& ma, const CUtensorMap& mb, ugemm::Plan& plan, co
 template <typename T, typename TP, int CH>
 int launch_prep_forward(const T* x, int64_t rows, int64_t ld, const BandTable& tab, const Layout& L, float* inv,
                         T* packed, cudaStream_t s, const char* name) {
-  const int row_ctas = (int)(rows < (int64_t)num_sms() * 8 ? rows : (int64_t)num_sms() * 8);
+  const int64_t blocks = (rows + kPrepRows - 1) / kPrepRows;
+  const int row_ctas = (int)(blocks < (int64_t)num_sms() * 8 ? blocks : (int64_t)num_sms() * 8);
   const int pack_ctas = L.pack_cta[L.nb];
-  const size_t smem = (size_t)(L.total / CH) * sizeof(float);
+  const size_t smem = (size_t)kPrepRows * (L.total / CH) * sizeof(float);
   auto kern = bs_prep_forward<T, TP, CH>;
   if (smem > 48 * 1024) PMB_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem), name);
   kern<<<row_ctas + pack_ctas, kThreads, smem, s>>>(x, rows, ld, row_ctas, tab, L, inv, packed);
@@ -468,10 +519,11 @@ int launch_prep_forward(const T* x, int64_t rows, int64_t ld, const BandTable& t
 template <typename T, int CH>
 int launch_prep_backward(const T* x, int64_t rows, int64_t ld, const float* inv, const Layout& L, T* normed,
                          int64_t nld, const T* dy, float* bpart, cudaStream_t s, const char* name) {
-  const int row_ctas = (int)(rows < (int64_t)num_sms() * 8 ? rows : (int64_t)num_sms() * 8);
-  const int64_t cols = (int64_t)L.nb * L.O;
-  const int64_t bias_ctas = bpart ? ((cols + kThreads - 1) / kThreads) * bias_chunks(rows) : 0;
-  const size_t smem = (size_t)L.nb * sizeof(float) + (size_t)(L.total / CH) * sizeof(int);
+  const int64_t blocks = (rows + kPrepRows - 1) / kPrepRows;
+  const int row_ctas = (int)(blocks < (int64_t)num_sms() * 8 ? blocks : (int64_t)num_sms() * 8);
+  const int64_t cols = (int64_t)L.nb * L.O;  // a multiple of 64 (O is)
+  const int64_t bias_ctas = bpart ? ((cols / 8 + kThreads - 1) / kThreads) * bias_chunks(rows) : 0;
+  const size_t smem = (size_t)kPrepRows * L.nb * sizeof(float) + (size_t)(L.total / CH) * sizeof(int);
   auto kern = bs_prep_backward<T, CH>;
   if (smem > 48 * 1024) PMB_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem), name);
   kern<<<(unsigned)(row_ctas + bias_ctas), kThreads, smem, s>>>(x, rows, ld, inv, L, row_ctas, normed, nld, dy, cols,
