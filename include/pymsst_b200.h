@@ -541,6 +541,30 @@ PMB_API int pmb_attention_backward(const void* q, const void* k, const void* v, 
  * pmb_qkv_rotary_merge for sequences stored in row order (the reference's
  * rotary backward, src/pymsst/training/cuda/fused_band_split.cu:1104-1128,
  * applied after the attention backward of fused_roformer.py:793-818). */
+/* Attention with the BS-/Mel-RoFormer head gate folded in (sequences of up
+ * to 64 positions, the band axis): gated = softmax(q k^T scale) v *
+ * sigmoid(gate_logits[seq * seq_len + pos, head]) written in place of o
+ * (gate_logits: [sequences * seq_len, heads] in the activation type, rows
+ * in sequence order).  The backward takes the gated output and its gradient
+ * where pmb_attention_backward_rotary takes o and grad_out (dO = gate *
+ * grad_gated), writes dQ / dK (rotated back when cos / sin are given; both
+ * NULL otherwise) and dV, and the gate logits' gradient
+ * grad_logits[row * grad_logits_ld + head] = rowsum(grad_gated * gated) *
+ * (1 - gate); all in one pass.  Replaces the attention core plus the separate
+ * gate pass of the patched Attention.forward
+ * (src/pymsst/training/fused_roformer.py:793-818; gate kernels
+ * cuda/fused_band_split.cu:1778-2036). */
+PMB_API int pmb_attention_forward_gated(const void* q, const void* k, const void* v, const void* gate_logits,
+                                        void* gated, float* lse, int64_t sequences, int64_t seq_len, int64_t heads,
+                                        int64_t dim_head, const int64_t* strides, float scale, int dtype,
+                                        void* stream);
+PMB_API int pmb_attention_backward_gated(const void* q, const void* k, const void* v, const void* gated,
+                                         const void* grad_gated, const float* lse, const void* gate_logits,
+                                         const float* cos, const float* sin, void* grad_q, void* grad_k,
+                                         void* grad_v, void* grad_logits, int64_t grad_logits_ld, int64_t sequences,
+                                         int64_t seq_len, int64_t heads, int64_t dim_head, const int64_t* strides,
+                                         float scale, int dtype, void* workspace, int64_t workspace_bytes,
+                                         void* stream);
 PMB_API int pmb_attention_backward_rotary(const void* q, const void* k, const void* v, const void* o,
                                           const void* grad_out, const float* lse, const float* cos, const float* sin,
                                           void* grad_q, void* grad_k, void* grad_v, int64_t sequences,

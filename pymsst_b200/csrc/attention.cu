@@ -436,6 +436,12 @@ __device__ __forceinline__ void store_row32(T* dst, const uint32_t (&a)[32], flo
   }
 }
 
+// Head gate sigma(logit) of one (row, head), from the 16-bit logit the gate projection produced.
+template <typename T>
+__device__ __forceinline__ float gate_of(T logit) {
+  return 1.0f / (1.0f + __expf(-Elem<T>::to_f(logit)));
+}
+
 // Inverse rotary rotation of a thread's 32 gradient values of position pos
 // (interleaved pairs 16 half .. 16 half + 15 of the head): (e, o) ->
 // (e c + o s, o c - e s), the transpose of the forward's (e c - o s,
@@ -1029,7 +1035,7 @@ template <typename T, bool kPack>
 __global__ void __launch_bounds__(kThreads, 2)
     attn_fwd_short_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmV, T* __restrict__ o, float* __restrict__ lse, Plane po,
-                      int sequences, int N, int H, int ldl, int total, float scale) {
+                      int sequences, int N, int H, int ldl, int total, float scale, const T* __restrict__ glogit) {
   using namespace fs;
   constexpr bool pack = kPack;
   extern __shared__ uint8_t smem_raw[];
@@ -1220,8 +1226,10 @@ __global__ void __launch_bounds__(kThreads, 2)
       tmem_wait2(oa, ob);
       warp_arrive(o_empty, false);
       if (seq < sequences && pos < N) {
+        // with the head gate: gated = o * sigma(logit[seq * N + pos, h]) in place of o
+        const float mul = glogit != nullptr ? gate_of(glogit[((int64_t)seq * N + pos) * H + h]) / l : 1.f / l;
         store_row64<T>(o + seq * po.s_b + h * po.s_h + (int64_t)pos * po.s_n,
-                       *reinterpret_cast<float(*)[32]>(oa), *reinterpret_cast<float(*)[32]>(ob), 1.f / l);
+                       *reinterpret_cast<float(*)[32]>(oa), *reinterpret_cast<float(*)[32]>(ob), mul);
         lse[((int64_t)seq * H + h) * ldl + pos] = (m + log2f(l)) * kLn2;
       }
     }
@@ -1270,9 +1278,11 @@ struct Layout {
   static constexpr int OFF_PT = kStages * STAGE;
   static constexpr int OFF_DST = OFF_PT + kOp;
   static constexpr int OFF_BAR = OFF_DST + kOp;
-  static constexpr int OFF_X = OFF_BAR + 128;  // per buffer: [2][128] partial D, then [128] lse * log2e
+  // per buffer: [2][128] partial D, [128] lse * log2e, and (packed pairs) [128] head gates
+  static constexpr int OFF_X = OFF_BAR + 128;
   static constexpr int kXBufs = kPack ? 2 : 1;
-  static constexpr int kXBytes = 3 * BM * 4;
+  static constexpr int kXFloats = (kPack ? 4 : 3) * BM;
+  static constexpr int kXBytes = kXFloats * 4;
   static constexpr int SMEM = OFF_X + kXBufs * kXBytes + 1024;
   static_assert(SMEM <= 232448 - 64, "fused backward shared memory");
 };
@@ -1285,7 +1295,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                       const __grid_constant__ CUtensorMap tmO, const float* __restrict__ lse, T* __restrict__ dq,
                       T* __restrict__ dk, T* __restrict__ dv, Plane pdq, Plane pdk, Plane pdv, int sequences, int N,
                       int H, int ldl, int total, float scale, const float* __restrict__ rcos,
-                      const float* __restrict__ rsin) {
+                      const float* __restrict__ rsin, const T* __restrict__ glogit, T* __restrict__ dlogit,
+                      int64_t dl_ld) {
   using namespace bf;
   using L = Layout<kPack>;
   constexpr bool pack = kPack;
@@ -1447,8 +1458,21 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 #pragma unroll
         for (int e = 0; e < 8; ++e) part = fmaf(Elem<T>::to_f(oe[e]), Elem<T>::to_f(de[e]), part);
       }
-      xb[half * BM + row] = part;
-      if (half == 0) xb[2 * BM + row] = seq_of(item) < sequences && pos < N ? lse_v * kLog2e : 0.f;
+      // With the head gate g of query `row` folded in, the staged "o" / "dO" tiles are the gated output and
+      // its gradient: dO = g dGated, so D = rowsum(dO * O) = rowsum(dGated * gated) = part, dP^T's column of
+      // this query carries g, and so must the P^T operand of dV = P^T dO.  Staging D / g and
+      // lse log2e - log2 g instead of D and lse log2e makes the softmax loop give P^T g and
+      // P^T g (dP^T_raw - D / g) = P^T (g dP^T_raw - D) = dS^T unchanged; g itself is kept for dlogit.
+      float g = 1.f;
+      if constexpr (pack) {
+        const int seq = seq_of(item), h = (int)(item % H);
+        if (glogit != nullptr && seq < sequences && pos < N)
+          g = fmaxf(gate_of(glogit[((int64_t)seq * N + pos) * H + h]), 1e-30f);
+        if (half == 0) xb[3 * BM + row] = g;
+      }
+      xb[half * BM + row] = part / g;
+      if (half == 0)
+        xb[2 * BM + row] = seq_of(item) < sequences && pos < N ? lse_v * kLog2e - (pack ? log2f(g) : 0.f) : 0.f;
       warp_arrive(x_full, false);
       return umma::mbar_wait(x_full, tt & 1, 0x77);
     };
@@ -1462,7 +1486,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     for (int item = blockIdx.x; ok && item < total && !abort_flag; item += gridDim.x, ++t) {
       const int h = item % H, seq = seq_of(item);
       const bool valid = seq < sequences && pos < N;  // as a key and as a query
-      float* xb = xbuf + (pack ? (t & 1) : 0) * 3 * BM;
+      float* xb = xbuf + (pack ? (t & 1) : 0) * L::kXFloats;
       if (!pack) {
         if (!stage_d(t, item, lse_pf, xb)) {
           ok = false;
@@ -1515,7 +1539,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       if (pack && item + (int64_t)gridDim.x < total) {
         // every row warp has finished this item's softmax (ps_full waited by the MMA lane before acc_full, and
         // the other buffer's last readers were item t - 1's): stage the next item's D now
-        if (!stage_d(t + 1, (int64_t)item + gridDim.x, lse_pf, xbuf + ((t + 1) & 1) * 3 * BM)) {
+        if (!stage_d(t + 1, (int64_t)item + gridDim.x, lse_pf, xbuf + ((t + 1) & 1) * L::kXFloats)) {
           ok = false;
           break;
         }
@@ -1546,6 +1570,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
         store_row32<T>(dk + rk, gk, scale);
         store_row32<T>(dq + rq, gq, scale);
+        if constexpr (pack) {
+          // gradient of the gate logit of query `row`: sum_d dGated * o * g (1 - g) = D (1 - g), D = g * staged
+          if (dlogit != nullptr && half == 0) {
+            const float g = xs[3 * BM + row];
+            dlogit[((int64_t)seq * N + pos) * dl_ld + h] = Elem<T>::from_f((xs[row] + xs[BM + row]) * g * (1.f - g));
+          }
+        }
       }
     }
     if (!ok) abort_flag = 1;
@@ -1616,11 +1647,12 @@ using namespace pmb;
 
 extern "C" int64_t pmb_attention_row_pitch(int64_t seq_len) { return seq_len > 0 ? row_pitch(seq_len) : 0; }
 
-extern "C" int pmb_attention_forward(const void* q, const void* k, const void* v, void* o, float* lse,
-                                     int64_t sequences, int64_t seq_len, int64_t heads, int64_t dim_head,
-                                     const int64_t* strides, float scale, int dtype, void* stream) {
-  clear_error();
-  const char* name = "pmb_attention_forward";
+namespace pmb {
+namespace {
+// The forward of both entry points; glogit (16-bit [sequences * seq_len, heads], or NULL) gates the output.
+int attention_forward(const void* q, const void* k, const void* v, void* o, float* lse, int64_t sequences,
+                      int64_t seq_len, int64_t heads, int64_t dim_head, const int64_t* strides, float scale, int dtype,
+                      const void* glogit, void* stream, const char* name) {
   if (int st = check_shape(name, dtype, sequences, seq_len, heads, dim_head)) return st;
   if (sequences == 0) return PMB_OK;
   PMB_REQUIRE(lse && strides, "%s: NULL argument", name);
@@ -1648,7 +1680,8 @@ extern "C" int pmb_attention_forward(const void* q, const void* k, const void* v
       auto kernel = pack ? attn_fwd_short_tc<T, true> : attn_fwd_short_tc<T, false>;
       PMB_CHECK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fs::SMEM), name);
       kernel<<<grid_for(items), kThreads, fs::SMEM, s>>>(mq, mk, mv, static_cast<T*>(o), lse, po, (int)sequences, N,
-                                                         H, (int)row_pitch(N), (int)items, scale);
+                                                         H, (int)row_pitch(N), (int)items, scale,
+                                                         static_cast<const T*>(glogit));
       PMB_CHECK_LAUNCH(name);
       return PMB_OK;
     };
@@ -1667,6 +1700,29 @@ extern "C" int pmb_attention_forward(const void* q, const void* k, const void* v
   };
   return dtype == PMB_BFLOAT16 ? run(__nv_bfloat16()) : run(__half());
 }
+}  // namespace
+}  // namespace pmb
+
+extern "C" int pmb_attention_forward(const void* q, const void* k, const void* v, void* o, float* lse,
+                                     int64_t sequences, int64_t seq_len, int64_t heads, int64_t dim_head,
+                                     const int64_t* strides, float scale, int dtype, void* stream) {
+  clear_error();
+  return attention_forward(q, k, v, o, lse, sequences, seq_len, heads, dim_head, strides, scale, dtype, nullptr,
+                           stream, "pmb_attention_forward");
+}
+
+extern "C" int pmb_attention_forward_gated(const void* q, const void* k, const void* v, const void* gate_logits,
+                                           void* gated, float* lse, int64_t sequences, int64_t seq_len,
+                                           int64_t heads, int64_t dim_head, const int64_t* strides, float scale,
+                                           int dtype, void* stream) {
+  clear_error();
+  const char* name = "pmb_attention_forward_gated";
+  PMB_REQUIRE(gate_logits != nullptr, "%s: NULL gate logits", name);
+  PMB_REQUIRE(seq_len <= 64, "%s: the gated kernels take sequences of up to 64 positions (got %lld)", name,
+              (long long)seq_len);
+  return attention_forward(q, k, v, gated, lse, sequences, seq_len, heads, dim_head, strides, scale, dtype,
+                           gate_logits, stream, name);
+}
 
 extern "C" int64_t pmb_attention_backward_workspace_size(int64_t sequences, int64_t seq_len, int64_t heads) {
   if (sequences <= 0 || seq_len <= 0 || heads <= 0) return 0;
@@ -1680,7 +1736,7 @@ int attention_backward(const void* q, const void* k, const void* v, const void* 
                        const float* lse, void* grad_q, void* grad_k, void* grad_v, int64_t sequences, int64_t seq_len,
                        int64_t heads, int64_t dim_head, const int64_t* strides, float scale, int dtype,
                        const float* rcos, const float* rsin, void* workspace, int64_t workspace_bytes, void* stream,
-                       const char* name) {
+                       const char* name, const void* glogit = nullptr, void* dlogit = nullptr, int64_t dl_ld = 0) {
   if (int st = check_shape(name, dtype, sequences, seq_len, heads, dim_head)) return st;
   if (sequences == 0) return PMB_OK;
   PMB_REQUIRE(lse && strides, "%s: NULL argument", name);
@@ -1723,12 +1779,16 @@ int attention_backward(const void* q, const void* k, const void* v, const void* 
       PMB_CHECK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem), name);
       kernel<<<grid, kBwdThreads, smem, s>>>(mq, mk, mv, mdo, mo, lse, static_cast<T*>(grad_q),
                                                  static_cast<T*>(grad_k), static_cast<T*>(grad_v), pdq, pdk, pdv,
-                                                 (int)sequences, N, H, (int)ldl, (int)items, scale, rcos, rsin);
+                                                 (int)sequences, N, H, (int)ldl, (int)items, scale, rcos, rsin,
+                                                 static_cast<const T*>(glogit), static_cast<T*>(dlogit), dl_ld);
       PMB_CHECK_LAUNCH(name);
       return PMB_OK;
     };
     return dtype == PMB_BFLOAT16 ? run(__nv_bfloat16()) : run(__half());
   }
+  // the gate is folded into the one-pass kernel only
+  PMB_REQUIRE(glogit == nullptr, "%s: the gated output must be laid out like q (non-overlapping plane strides)",
+              name);
   float* delta = static_cast<float*>(workspace);
   CUtensorMap mq128, mdo128, mk64, mv64, mk128, mv128, mq64, mdo64, ml, md;  // *64: 32-row chunk maps
   if (int st = plane_map(mq128, q, pq, dtype, sequences, N, H, BM, name)) return st;
@@ -1786,4 +1846,25 @@ extern "C" int pmb_attention_backward_rotary(const void* q, const void* k, const
               "%s: angle tables must be non-NULL and 16-byte aligned", name);
   return attention_backward(q, k, v, o, grad_out, lse, grad_q, grad_k, grad_v, sequences, seq_len, heads, dim_head,
                             strides, scale, dtype, cos, sin, workspace, workspace_bytes, stream, name);
+}
+
+extern "C" int pmb_attention_backward_gated(const void* q, const void* k, const void* v, const void* gated,
+                                            const void* grad_gated, const float* lse, const void* gate_logits,
+                                            const float* cos, const float* sin, void* grad_q, void* grad_k,
+                                            void* grad_v, void* grad_logits, int64_t grad_logits_ld,
+                                            int64_t sequences, int64_t seq_len, int64_t heads, int64_t dim_head,
+                                            const int64_t* strides, float scale, int dtype, void* workspace,
+                                            int64_t workspace_bytes, void* stream) {
+  clear_error();
+  const char* name = "pmb_attention_backward_gated";
+  PMB_REQUIRE(gate_logits && grad_logits && grad_logits_ld >= heads, "%s: gate logits and their gradient needed",
+              name);
+  PMB_REQUIRE(seq_len <= 64, "%s: the gated kernels take sequences of up to 64 positions (got %lld)", name,
+              (long long)seq_len);
+  PMB_REQUIRE((cos == nullptr) == (sin == nullptr) &&
+                  (reinterpret_cast<uintptr_t>(cos) & 15) == 0 && (reinterpret_cast<uintptr_t>(sin) & 15) == 0,
+              "%s: angle tables must both be given (16-byte aligned) or both be NULL", name);
+  return attention_backward(q, k, v, gated, grad_gated, lse, grad_q, grad_k, grad_v, sequences, seq_len, heads,
+                            dim_head, strides, scale, dtype, cos, sin, workspace, workspace_bytes, stream, name,
+                            gate_logits, grad_logits, grad_logits_ld);
 }

@@ -679,6 +679,92 @@ class QKVAttentionFn(torch.autograd.Function):
         return gx, gw, None, None, None, None, None, None
 
 
+class QKVAttentionGateFn(torch.autograd.Function):
+    """QKVAttentionFn with the head gate folded into the attention kernels, for sequences of up to 64 positions
+    in row order (the band axis): xn [b, n, D] -> gated [b * n, h * 64] = attention * sigmoid(xn W_g^T + b_g)
+    per head, the AttentionGateFn output.
+
+    Forward: the gate logits come from one small GEMM in the activation type (as autocast computes the gate
+    Linear), and the attention kernel writes the gated output in place of o (pmb_attention_forward_gated).
+    Backward: pmb_attention_backward_gated writes dQ / dK rotated back, dV and the logits' gradient
+    rowsum(dGated * gated) (1 - gate) into one [b * n, 3 h 64 + h] buffer E, so the input gradient
+    E [W_qkv; W_g] and the weight gradients E^T xn are one GEMM each and the gate has no pass of its own.
+    Reference semantics: the patched Attention.forward, src/pymsst/training/fused_roformer.py:793-818."""
+
+    @staticmethod
+    def forward(ctx, xn, weight, cos, sin, cos_t, sin_t, heads, w_gate, b_gate):
+        device = nat.require_cuda(xn, weight, w_gate, b_gate, name="QKVAttentionGate")
+        b, n, d = xn.shape
+        dh = weight.shape[0] // (3 * heads)
+        if not (xn.dtype in (torch.bfloat16, torch.float16) and d % 8 == 0 and dh == 64 and n <= 64):
+            raise ValueError("QKVAttentionGate: 16-bit activations, D % 8 == 0, 64-element heads and at most 64 "
+                             "positions only")
+        dt = xn.dtype
+        w = lowp_weight(weight, dt).contiguous()
+        wg = lowp_weight(w_gate, dt).contiguous()
+        bg = lowp_weight(b_gate, dt)
+        x2 = xn.reshape(b * n, d).contiguous()
+        rotate = int(cos is not None)
+        if rotate:
+            if tuple(cos.shape) != (n, dh // 2) or tuple(sin.shape) != (n, dh // 2):
+                raise ValueError(f"QKVAttentionGate: angle tables must be [{n}, {dh // 2}], got {tuple(cos.shape)} "
+                                 f"and {tuple(sin.shape)}")
+            cos, sin = cos.float().contiguous(), sin.float().contiguous()
+            if cos_t is None:
+                cos_t, sin_t = cos.t().contiguous(), sin.t().contiguous()
+        planes = [torch.empty(b, n, heads, dh, dtype=dt, device=device) for _ in range(3)]
+        stream = nat.stream_handle(device)
+        nat.call(
+            "pmb_qkv_linear_rotary_forward", x2.data_ptr(), w.data_ptr(), nat.ptr(cos_t), nat.ptr(sin_t), b, n, d,
+            heads, dh, planes[0].data_ptr(), planes[1].data_ptr(), planes[2].data_ptr(), rotate, nat.dtype_code(dt),
+            1, stream,
+        )
+        q, k, v = (pl.transpose(1, 2) for pl in planes)
+        logits = torch.addmm(bg, x2, wg.t())  # [b * n, heads]
+        gated = torch.empty(b * n, heads * dh, dtype=dt, device=device)
+        gp = gated.view(b, n, heads, dh).transpose(1, 2)
+        lse = torch.empty(b * heads, (n + 3) // 4 * 4, dtype=torch.float32, device=device)
+        nat.call(
+            "pmb_attention_forward_gated", q.data_ptr(), k.data_ptr(), v.data_ptr(), logits.data_ptr(),
+            gated.data_ptr(), lse.data_ptr(), b, n, heads, dh, nat.i64_array(_attn_strides(q, k, v, gp)), dh ** -0.5,
+            nat.dtype_code(dt), stream,
+        )
+        ctx.dtypes = (weight.dtype, w_gate.dtype, b_gate.dtype)
+        ctx.save_for_backward(x2, w, wg, cos, sin, q, k, v, gated, lse, logits)
+        return gated
+
+    @staticmethod
+    def backward(ctx, grad):
+        x2, w, wg, cos, sin, q, k, v, gated, lse, logits = ctx.saved_tensors
+        device = q.device
+        b, h, n, dh = q.shape
+        rows, inner = b * n, h * dh
+        g2 = grad.to(q.dtype).contiguous()
+        ext = torch.empty(rows, 3 * inner + h, dtype=q.dtype, device=device)
+        dq, dk, dv = (ext[:, i * inner:(i + 1) * inner].view(b, n, h, dh).transpose(1, 2) for i in range(3))
+        gp = gated.view(b, n, h, dh).transpose(1, 2)
+        dgp = g2.view(b, n, h, dh).transpose(1, 2)
+        ws_bytes = int(nat.library().pmb_attention_backward_workspace_size(b, n, h))
+        ws = nat.workspace(ws_bytes, device)
+        nat.call(
+            "pmb_attention_backward_gated", q.data_ptr(), k.data_ptr(), v.data_ptr(), gated.data_ptr(),
+            g2.data_ptr(), lse.data_ptr(), logits.data_ptr(), nat.ptr(cos), nat.ptr(sin), dq.data_ptr(),
+            dk.data_ptr(), dv.data_ptr(), ext[:, 3 * inner:].data_ptr(), 3 * inner + h, b, n, h, dh,
+            nat.i64_array(_attn_strides(q, k, v, gp, dgp, dq, dk, dv)), dh ** -0.5, nat.dtype_code(q.dtype),
+            ws.data_ptr(), ws_bytes, nat.stream_handle(device),
+        )
+        gx = gw = gwg = gbg = None
+        if ctx.needs_input_grad[0]:
+            gx = torch.matmul(ext, torch.cat([w, wg], 0)).reshape(b, n, -1)
+        if ctx.needs_input_grad[1] or ctx.needs_input_grad[7]:
+            gw_ext = torch.matmul(ext.t(), x2)
+            gw = gw_ext[:3 * inner].to(ctx.dtypes[0])
+            gwg = gw_ext[3 * inner:].to(ctx.dtypes[1])
+        if ctx.needs_input_grad[8]:
+            gbg = ext[:, 3 * inner:].float().sum(0).to(ctx.dtypes[2])
+        return gx, gw, None, None, None, None, None, gwg, gbg
+
+
 class STFTFramesFn(torch.autograd.Function):
     """x [B, L] fp32 -> windowed frames [B, T, n_fft] of the centred, reflect-padded signal, as torch.stft frames
     it (window: n_fft values, zero-padded as torch.stft pads a shorter window).  Forward: one kernel writes the

@@ -318,6 +318,23 @@ def _op_qkv_attention(bench: _Bench):
     bench.time(f"qkv+attention fwd+bwd n={n} (QKVAttentionFn)", fused, by)
     bench.time(f"qkv+attention fwd+bwd n={n} (QKVRotaryFn + AttentionFn)", split, by)
 
+    from .fused import AttentionGateFn, QKVAttentionGateFn
+
+    wg = (torch.randn(HEADS, DIM, device=dev) / DIM ** 0.5).requires_grad_()
+    bg = torch.zeros(HEADS, device=dev).requires_grad_()
+    gg = torch.randn(ROWS, HEADS * DHEAD, device=dev, dtype=bf)
+    byg = by + ROWS * HEADS * DHEAD * 2 * 3
+
+    def gated():
+        _grads(QKVAttentionGateFn.apply(x, w, cos, sin, cos_t, sin_t, HEADS, wg, bg), [x, w, wg, bg], gg)
+
+    def gate_apart():
+        o = QKVAttentionFn.apply(x, w, cos, sin, cos_t, sin_t, HEADS)
+        _grads(AttentionGateFn.apply(o, x.reshape(ROWS, DIM), wg, bg, 1), [x, w, wg, bg], gg)
+
+    bench.time(f"qkv+attention+gate fwd+bwd n={n} (QKVAttentionGateFn)", gated, byg)
+    bench.time(f"qkv+attention+gate fwd+bwd n={n} (QKVAttentionFn + AttentionGateFn)", gate_apart, byg)
+
 
 def op_band(bench: _Bench):
     """BandSplit (config-3 bands: 62 bands over 1025 stereo complex bins, 1032 rows, D = 192)."""

@@ -55,6 +55,7 @@ from .fused import (
     MaskEstimatorTCFn,
     OutProjFn,
     QKVAttentionFn,
+    QKVAttentionGateFn,
     QKVRotaryFn,
     RMSNormFn,
     RMSNormResidualFn,
@@ -228,18 +229,26 @@ class Attention(nn.Module):
         if self.rotary_embed is not None:
             cos, sin, cos_t, sin_t = self.rotary_embed.tables(n, x.device)
         dropout_p = self.dropout if self.training else 0.0
-        # the projection passes xn through to the head gate, so the gate's gradient of xn joins the projection's
-        # input gradient in one GEMM
-        if (inner == 1 and xn.is_cuda and xn.dtype in (torch.bfloat16, torch.float16) and d % 8 == 0
-                and self.dim_head == 64 and dropout_p == 0.0 and _own_attention(n, self.attention_backend)):
-            # sequences in row order on the own kernels: the attention backward writes the projection gradient
-            attn, xg = QKVAttentionFn.apply(xn.reshape(b, n, d), self.to_qkv.weight, cos, sin, cos_t, sin_t,
-                                            self.heads, True)
+        own = (inner == 1 and xn.is_cuda and xn.dtype in (torch.bfloat16, torch.float16) and d % 8 == 0
+               and self.dim_head == 64 and dropout_p == 0.0 and _own_attention(n, self.attention_backend))
+        if own and n <= 64:
+            # short sequences in row order (the band axis): projection, attention and head gate in one Function;
+            # the attention backward writes the projection gradient and the gate logits' gradient
+            gated = QKVAttentionGateFn.apply(xn.reshape(b, n, d), self.to_qkv.weight, cos, sin, cos_t, sin_t,
+                                             self.heads, self.to_gates.weight, self.to_gates.bias)
         else:
-            q, k, v, xg = QKVRotaryFn.apply(xn.reshape(b, n, d), self.to_qkv.weight, cos, sin, cos_t, sin_t,
-                                            self.heads, inner, True)
-            attn = _attention(q, k, v, dropout_p, self.attention_backend)
-        gated = AttentionGateFn.apply(attn, xg.reshape(rows, d), self.to_gates.weight, self.to_gates.bias, inner)
+            # the projection passes xn through to the head gate, so the gate's gradient of xn joins the
+            # projection's input gradient in one GEMM
+            if own:
+                # sequences in row order on the own kernels: the attention backward writes the projection gradient
+                attn, xg = QKVAttentionFn.apply(xn.reshape(b, n, d), self.to_qkv.weight, cos, sin, cos_t, sin_t,
+                                                self.heads, True)
+            else:
+                q, k, v, xg = QKVRotaryFn.apply(xn.reshape(b, n, d), self.to_qkv.weight, cos, sin, cos_t, sin_t,
+                                                self.heads, inner, True)
+                attn = _attention(q, k, v, dropout_p, self.attention_backend)
+            gated = AttentionGateFn.apply(attn, xg.reshape(rows, d), self.to_gates.weight, self.to_gates.bias,
+                                          inner)
         drop = self.to_out[1]
         if residual is not None and (not self.training or drop.p == 0.0):
             # residual + gated W^T in one GEMM (C = residual, beta = 1)

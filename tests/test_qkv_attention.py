@@ -14,7 +14,7 @@ import pytest
 import torch
 
 from pymsst_b200 import _native as nat
-from pymsst_b200.fused import AttentionFn, QKVAttentionFn, QKVRotaryFn, rotary_tables
+from pymsst_b200.fused import AttentionFn, QKVAttentionFn, QKVAttentionGateFn, QKVRotaryFn, rotary_tables
 
 pytestmark = pytest.mark.gpu
 
@@ -125,4 +125,70 @@ def test_rotary_backward_entry_matches_merge(cuda_device):
     assert torch.equal(direct[:, 2 * h * 64:], merged[:, 2 * h * 64:])
     scale = float(merged.float().abs().max())
     torch.testing.assert_close(direct.float(), merged.float(), rtol=1e-2, atol=2e-2 * scale)
+    assert nat.library().pmb_umma_timeout(1) == 0
+
+
+# ------------------------------------------------------------------ head gate folded into the attention kernels
+def _gate_params(device, d, heads, seed):
+    g = torch.Generator().manual_seed(seed)
+    wg = (torch.randn(heads, d, generator=g) / d ** 0.5).to(device)
+    bg = (torch.randn(heads, generator=g) * 0.5).to(device)
+    return wg, bg
+
+
+@pytest.mark.parametrize("b,n,d,heads", [(33, 62, 192, 8), (6, 60, 384, 8), (5, 17, 192, 4)])
+@pytest.mark.parametrize("rotate", [True, False])
+def test_qkv_attention_gate_matches_separate_gate(cuda_device, b, n, d, heads, rotate):
+    """QKVAttentionGateFn against QKVAttentionFn + AttentionGateFn on the same inputs.  The two compute the gate
+    logits differently (a 16-bit GEMM as autocast does, against the gate kernel's fp32 dot products with the fp32
+    weight), so outputs and gradients agree at the 16-bit bar (2e-2 of the scale)."""
+    from pymsst_b200.fused import AttentionGateFn
+
+    x, w, gy, cos, sin = _inputs(cuda_device, b, n, d, heads, seed=3 * b + n)
+    wg, bg = _gate_params(cuda_device, d, heads, seed=n)
+    gy = gy.transpose(1, 2).reshape(b * n, heads * 64)
+    if not rotate:
+        cos = sin = None
+
+    def run(fused):
+        xr, wr, wgr, bgr = (t.clone().requires_grad_() for t in (x, w, wg, bg))
+        if fused:
+            out = QKVAttentionGateFn.apply(xr, wr, cos, sin, None, None, heads, wgr, bgr)
+        else:
+            o = QKVAttentionFn.apply(xr, wr, cos, sin, None, None, heads)
+            out = AttentionGateFn.apply(o, xr.reshape(b * n, d), wgr, bgr, 1)
+        grads = torch.autograd.grad(out, (xr, wr, wgr, bgr), gy)
+        return (out.detach(), *grads)
+
+    got, exp = run(True), run(False)
+    for a, e, name in zip(got, exp, ("out", "grad_x", "grad_w", "grad_w_gate", "grad_b_gate")):
+        scale = float(e.abs().max())
+        torch.testing.assert_close(a.float(), e.float(), rtol=2e-2, atol=2e-2 * scale, msg=lambda m: f"{name}: {m}")
+    assert nat.library().pmb_umma_timeout(1) == 0
+
+
+def test_qkv_attention_gate_matches_float64(cuda_device):
+    from pymsst_b200.fused import QKVAttentionGateFn
+
+    b, n, d, heads = 9, 62, 192, 8
+    x, w, gy, cos, sin = _inputs(cuda_device, b, n, d, heads, seed=21)
+    wg, bg = _gate_params(cuda_device, d, heads, seed=22)
+    gy = gy.transpose(1, 2).reshape(b * n, heads * 64)
+    xr, wr, wgr, bgr = (t.clone().requires_grad_() for t in (x, w, wg, bg))
+    out = QKVAttentionGateFn.apply(xr, wr, cos, sin, None, None, heads, wgr, bgr)
+    grads = torch.autograd.grad(out, (xr, wr, wgr, bgr), gy)
+    # float64: the kernels read W, W_g and b_g in bf16
+    x64 = x.double().cpu().requires_grad_()
+    w64, wg64, bg64 = (t.double().cpu().to(torch.bfloat16).double().requires_grad_() for t in (w, wg, bg))
+    p = (x64.reshape(b * n, d) @ w64.t()).reshape(b, n, 3, heads, 64).permute(2, 0, 3, 1, 4)
+    c64, s64 = cos.double().cpu(), sin.double().cpu()
+    q, k, v = _rotate_ref(p[0], c64, s64), _rotate_ref(p[1], c64, s64), p[2]
+    att = torch.softmax(q @ k.transpose(-1, -2) / 8.0, dim=-1) @ v  # [b, h, n, 64]
+    gate = torch.sigmoid(x64.reshape(b * n, d) @ wg64.t() + bg64)  # [b * n, h]
+    ref = (att.transpose(1, 2).reshape(b * n, heads, 64) * gate[:, :, None]).reshape(b * n, heads * 64)
+    rgrads = torch.autograd.grad(ref, (x64, w64, wg64, bg64), gy.double().cpu())
+    for a, e, name in zip((out, *grads), (ref, *rgrads), ("out", "grad_x", "grad_w", "grad_w_gate", "grad_b_gate")):
+        scale = float(e.abs().max())
+        torch.testing.assert_close(a.double().cpu(), e.detach(), rtol=3e-2, atol=3e-2 * scale,
+                                   msg=lambda m: f"{name}: {m}")
     assert nat.library().pmb_umma_timeout(1) == 0
