@@ -43,11 +43,16 @@ constexpr int kSubs = 3;                 // epilogue warps per TMEM lane quarter
 constexpr int kEpiWarps = 4 * kSubs;
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kMaxGroups = PMB_MAX_BANDS;
-// Per-warp staging block: 32 rows x (32 fp32 + 16 bytes of padding).
+// Per-warp staging block: 32 rows x (32 fp32 + 16 bytes of padding) for the
+// row-vector stores, or kStoreBufs 2 KB buffers for the TMA tile stores
+// (a warp keeps up to kStoreBufs - 1 stores reading shared memory while it
+// fills the next buffer).
 constexpr int kStageRowBytes = 32 * 4 + 16;
-constexpr int kStageWarpBytes = 32 * kStageRowBytes;
-static_assert(kStageWarpBytes % 512 == 0 && kStageWarpBytes >= 4096,
-              "staging blocks hold two 512-byte-aligned 2 KB TMA store buffers");
+constexpr int kStoreBufs = 3;
+constexpr int kStageWarpBytes = 32 * kStageRowBytes > kStoreBufs * 2048 ? 32 * kStageRowBytes : kStoreBufs * 2048;
+static_assert(kStageWarpBytes % 512 == 0 && kStageWarpBytes >= kStoreBufs * 2048,
+              "staging blocks hold kStoreBufs 512-byte-aligned 2 KB TMA store buffers");
+constexpr int kMaxSmemBytes = 232448;  // per CTA on sm_100a
 
 struct Group {
   int m, n, k;                  // problem size of this group
@@ -268,9 +273,10 @@ __device__ __forceinline__ void warp_tma_store(const TileCtx& t, const float (&v
                                                int col, int row) {
   static_assert(sizeof(T) == 2, "TMA tile stores take 16-bit outputs");
   const int lane = threadIdx.x & 31;
-  const int buf = (*t.store_seq)++ & 1;
+  const int buf = (*t.store_seq)++ % kStoreBufs;
   uint8_t* box = t.stage + buf * 2048;
-  if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+  // the store that last used this buffer (kStoreBufs stores ago) has finished reading it
+  if (lane == 0) asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(kStoreBufs - 1) : "memory");
   __syncwarp();
   T pack[32];
 #pragma unroll
@@ -296,6 +302,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     umma_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ Plan plan, const __grid_constant__ Epi epi, int fp16) {
   using C = Config<BN, A_MN, B_MN>;
+  static_assert(smem_bytes<BN, STAGES>() <= kMaxSmemBytes, "stage ring + staging blocks exceed shared memory");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* staging = smem + STAGES * C::STAGE_BYTES;

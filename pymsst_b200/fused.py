@@ -740,7 +740,9 @@ class QKVAttentionGateFn(torch.autograd.Function):
         b, h, n, dh = q.shape
         rows, inner = b * n, h * dh
         g2 = grad.to(q.dtype).contiguous()
-        ext = torch.empty(rows, 3 * inner + h, dtype=q.dtype, device=device)
+        width = 3 * inner + h
+        # rows padded to 8 elements: the kernels take plane strides that are multiples of 8
+        ext = torch.empty(rows, (width + 7) // 8 * 8, dtype=q.dtype, device=device)[:, :width]
         dq, dk, dv = (ext[:, i * inner:(i + 1) * inner].view(b, n, h, dh).transpose(1, 2) for i in range(3))
         gp = gated.view(b, n, h, dh).transpose(1, 2)
         dgp = g2.view(b, n, h, dh).transpose(1, 2)
@@ -749,7 +751,7 @@ class QKVAttentionGateFn(torch.autograd.Function):
         nat.call(
             "pmb_attention_backward_gated", q.data_ptr(), k.data_ptr(), v.data_ptr(), gated.data_ptr(),
             g2.data_ptr(), lse.data_ptr(), logits.data_ptr(), nat.ptr(cos), nat.ptr(sin), dq.data_ptr(),
-            dk.data_ptr(), dv.data_ptr(), ext[:, 3 * inner:].data_ptr(), 3 * inner + h, b, n, h, dh,
+            dk.data_ptr(), dv.data_ptr(), ext[:, 3 * inner:].data_ptr(), ext.stride(0), b, n, h, dh,
             nat.i64_array(_attn_strides(q, k, v, gp, dgp, dq, dk, dv)), dh ** -0.5, nat.dtype_code(q.dtype),
             ws.data_ptr(), ws_bytes, nat.stream_handle(device),
         )
