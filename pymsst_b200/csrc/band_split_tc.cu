@@ -491,7 +491,7 @@ Sizes sizes_of(int64_t rows, const Layout& L, int es) {
 template <int BN, bool A_MN, bool B_MN, class Epi>
 int run_gemm(const CUtensorMap& ma, const CUtensorMap& mb, ugemm::Plan& plan, const Epi& epi, int fp16,
              cudaStream_t s, const char* name) {
-  constexpr int STAGES = BN >= 192 ? 3 : 4;  // the ring and the epilogue staging share the shared memory
+  constexpr int STAGES = 4;
   const int tiles = ugemm::build_plan(plan, BN);
   if (tiles == 0) return PMB_OK;
   auto kern = ugemm::umma_gemm_kernel<BN, STAGES, A_MN, B_MN, Epi>;

@@ -48,7 +48,7 @@ constexpr int kMaxGroups = PMB_MAX_BANDS;
 // (a warp keeps up to kStoreBufs - 1 stores reading shared memory while it
 // fills the next buffer).
 constexpr int kStageRowBytes = 32 * 4 + 16;
-constexpr int kStoreBufs = 3;
+constexpr int kStoreBufs = 2;  // measured: a third buffer changed no GEMM's time
 constexpr int kStageWarpBytes = 32 * kStageRowBytes > kStoreBufs * 2048 ? 32 * kStageRowBytes : kStoreBufs * 2048;
 static_assert(kStageWarpBytes % 512 == 0 && kStageWarpBytes >= kStoreBufs * 2048,
               "staging blocks hold kStoreBufs 512-byte-aligned 2 KB TMA store buffers");

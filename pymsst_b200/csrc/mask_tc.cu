@@ -465,7 +465,7 @@ Layout make_layout(int64_t rows, int nb, int64_t dim, int64_t hidden, int L, con
 template <int BNT, class Epi, bool A_MN, bool B_MN>
 int run_gemm(const CUtensorMap& ma, const CUtensorMap& mb, ugemm::Plan& plan, const Epi& epi, int fp16,
              cudaStream_t s, const char* name) {
-  constexpr int NST = BNT >= 192 ? 3 : STAGES;
+  constexpr int NST = BNT >= 256 ? 3 : STAGES;
   const int tiles = ugemm::build_plan(plan, BNT);
   if (tiles == 0) return PMB_OK;
   auto kern = ugemm::umma_gemm_kernel<BNT, NST, A_MN, B_MN, Epi>;
