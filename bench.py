@@ -58,7 +58,8 @@ TIMED_ENTRIES = [
     "pmb_mask_estimator_tc_backward", "pmb_gemm_tc", "pmb_qkv_linear_rotary_forward", "pmb_band_split_tc_forward",
     "pmb_band_split_tc_backward", "pmb_gelu_forward", "pmb_gelu_backward", "pmb_column_sum",
     "pmb_attention_forward", "pmb_attention_backward", "pmb_attention_backward_rotary", "pmb_rms_norm_backward_add",
-    "pmb_stft_frames_forward", "pmb_stft_frames_backward",
+    "pmb_stft_frames_forward", "pmb_stft_frames_backward", "pmb_spectral_l1_forward", "pmb_spectral_l1_backward",
+    "pmb_attention_forward_gated", "pmb_attention_backward_gated",
 ]
 
 

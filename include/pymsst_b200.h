@@ -573,6 +573,27 @@ PMB_API int pmb_attention_backward_rotary(const void* q, const void* k, const vo
                                           void* stream);
 
 /* ------------------------------------------------------------------------
+ * One resolution of the multi-resolution STFT loss: mean |Y_recon - Y_target|
+ * over `count` complex values (fp32, interleaved re / im; 16-byte aligned),
+ * the F.l1_loss of two onesided spectra.  The forward writes the mean to
+ * loss[0] (deterministic: per-CTA partials in the workspace,
+ * pmb_spectral_l1_workspace_size bytes, summed in fp64 in a fixed order).
+ * The backward writes grad_recon = grad_loss[0] * (Y_recon - Y_target) /
+ * |Y_recon - Y_target| / count (0 where they agree) times the inverse real
+ * FFT's bin weight (0.5 for bins strictly between 0 and n_fft / 2, `bins` =
+ * n_fft / 2 + 1 per row), so an inverse real FFT of it is the gradient of the
+ * frames: one pass replaces the elementwise difference, abs, mean, their
+ * backward and the rfft backward's bin weighting.  grad_loss is a device
+ * pointer.  Replaces F.l1_loss over torch.stft spectra in pymss-core's
+ * multi-resolution STFT loss (trained unchanged by the reference,
+ * src/pymsst/training/module.py:221-224). */
+PMB_API int64_t pmb_spectral_l1_workspace_size(int64_t count);
+PMB_API int pmb_spectral_l1_forward(const float* y_recon, const float* y_target, int64_t count, float* loss,
+                                    void* workspace, int64_t workspace_bytes, void* stream);
+PMB_API int pmb_spectral_l1_backward(const float* y_recon, const float* y_target, int64_t count, int64_t bins,
+                                     int64_t n_fft, const float* grad_loss, float* grad_recon, void* stream);
+
+/* ------------------------------------------------------------------------
  * STFT framing of the multi-resolution STFT loss: torch.stft (center=True,
  * reflect padding by n_fft/2) frames x [batch, length] into frames [batch,
  * frames, n_fft] = reflect_pad(x)[f*hop + k] * window[k].  The forward

@@ -830,6 +830,57 @@ class RealFFTFn(torch.autograd.Function):
         return torch.fft.irfft(g * w, n=n, dim=-1, norm=_INVERSE_NORM[ctx.norm]), None
 
 
+class SpectralL1Fn(torch.autograd.Function):
+    """mean |rfft(frames) - target_spec| (F.l1_loss of two onesided spectra) with the rfft inside.  Forward:
+    torch.fft.rfft, then one pass for the mean (pmb_spectral_l1_forward, deterministic).  Backward: one pass
+    writes (Y - T) / |Y - T| times the upstream gradient / count and the inverse real FFT's bin weights
+    (pmb_spectral_l1_backward), then the inverse real FFT: the elementwise difference, abs, mean, their
+    backward and RealFFTFn's bin weighting in two passes over the spectrum."""
+
+    @staticmethod
+    def forward(ctx, frames, target_spec, norm):
+        device = nat.require_cuda(frames, target_spec, name="SpectralL1")
+        y = torch.fft.rfft(frames, dim=-1, norm=norm)
+        t = target_spec.contiguous()
+        if t.shape != y.shape or t.dtype != y.dtype:
+            raise ValueError(f"SpectralL1: target spectrum {tuple(t.shape)} {t.dtype} must match {tuple(y.shape)} "
+                             f"{y.dtype}")
+        count = y.numel()
+        wsb = int(nat.library().pmb_spectral_l1_workspace_size(count))
+        ws = nat.workspace(wsb, device)
+        loss = torch.empty((), dtype=torch.float32, device=device)
+        nat.call("pmb_spectral_l1_forward", torch.view_as_real(y).data_ptr(), torch.view_as_real(t).data_ptr(), count,
+                 loss.data_ptr(), ws.data_ptr(), wsb, nat.stream_handle(device))
+        ctx.n = frames.shape[-1]
+        ctx.norm = norm
+        ctx.save_for_backward(y, t)
+        return loss
+
+    @staticmethod
+    def backward(ctx, g):
+        y, t = ctx.saved_tensors
+        gl = g.float().reshape(1).contiguous()
+        gy = torch.empty_like(y)
+        nat.call("pmb_spectral_l1_backward", torch.view_as_real(y).data_ptr(), torch.view_as_real(t).data_ptr(),
+                 y.numel(), y.shape[-1], ctx.n, gl.data_ptr(), torch.view_as_real(gy).data_ptr(),
+                 nat.stream_handle(y.device))
+        return torch.fft.irfft(gy, n=ctx.n, dim=-1, norm=_INVERSE_NORM[ctx.norm]), None, None
+
+
+def stft_l1_loss(recon: torch.Tensor, target: torch.Tensor, n_fft: int, hop: int, window: torch.Tensor,
+                 normalized: bool) -> torch.Tensor:
+    """F.l1_loss(stft(recon), stft(target)) for fp32 CUDA signals [B, L] (torch.stft's spectra, frames first):
+    the framing kernels, the rfft, and SpectralL1Fn's one-pass mean and gradient.  The target's spectrum carries no
+    gradient (a training target); with a target that needs one, the two spectra go through F.l1_loss."""
+    norm = "ortho" if normalized else "backward"
+    if target.requires_grad:
+        return F.l1_loss(stft_loss_spectrum(recon, n_fft, hop, window, normalized),
+                         stft_loss_spectrum(target, n_fft, hop, window, normalized))
+    with torch.no_grad():
+        ty = stft_loss_spectrum(target, n_fft, hop, window, normalized)
+    return SpectralL1Fn.apply(STFTFramesFn.apply(recon, window, n_fft, hop), ty, norm)
+
+
 def stft_loss_spectrum(x: torch.Tensor, n_fft: int, hop: int, window: torch.Tensor, normalized: bool) -> torch.Tensor:
     """torch.stft(x, n_fft, hop, window=window, center=True, pad_mode="reflect", onesided, return_complex) for
     fp32 CUDA x [B, L], as [B, T, F] (frames first); window already zero-padded to n_fft."""

@@ -62,7 +62,7 @@ from .fused import (
     compute_dtype,
     rotary_tables,
     attention_supported,
-    stft_loss_spectrum,
+    stft_l1_loss,
     tensor_core_ok,
 )
 
@@ -508,14 +508,14 @@ class _Roformer(nn.Module):
                     # first); the L1 mean does not depend on the layout
                     window = self._loss_window(win, n_fft, recon.device)
                     hop, norm = self.multi_stft_kwargs["hop_length"], self.multi_stft_kwargs["normalized"]
-                    ry = stft_loss_spectrum(recon.reshape(-1, recon.shape[-1]), n_fft, hop, window, norm)
-                    ty = stft_loss_spectrum(target.reshape(-1, target.shape[-1]), n_fft, hop, window, norm)
+                    res = res + stft_l1_loss(recon.reshape(-1, recon.shape[-1]), target.reshape(-1, target.shape[-1]),
+                                             n_fft, hop, window, norm)
                 else:
                     kw = dict(n_fft=n_fft, win_length=win, return_complex=True,
                               window=self._window(win, recon.device), **self.multi_stft_kwargs)
                     ry = torch.stft(recon.reshape(-1, recon.shape[-1]), **kw)
                     ty = torch.stft(target.reshape(-1, target.shape[-1]), **kw)
-                res = res + F.l1_loss(ry, ty)
+                    res = res + F.l1_loss(ry, ty)
         return loss + res * self.multi_stft_resolution_loss_weight
 
     def _separate(self, raw_audio, length):

@@ -140,6 +140,18 @@ def work(name: str, a: tuple) -> tuple[float, float]:
     if name in ("pmb_stft_frames_forward", "pmb_stft_frames_backward"):
         b, length, n_fft, frames = a[3], a[4], a[5], a[7]
         return 4.0 * (b * length + b * frames * n_fft + n_fft), 1.0 * b * frames * n_fft
+    if name == "pmb_spectral_l1_forward":  # two complex64 spectra read
+        return 16.0 * a[2], 4.0 * a[2]
+    if name == "pmb_spectral_l1_backward":  # two read, the gradient written
+        return 24.0 * a[2], 8.0 * a[2]
+    if name == "pmb_attention_forward_gated":  # the attention forward plus the [rows, heads] logits
+        seqs, n, h, dh, dt = a[6], a[7], a[8], a[9], a[12]
+        plane = seqs * n * h * dh * ES[dt]
+        return 4.0 * plane + 4.0 * seqs * h * n + seqs * n * h * ES[dt], 4.0 * seqs * h * n * n * dh
+    if name == "pmb_attention_backward_gated":  # the backward plus logits read and their gradient written
+        seqs, n, h, dh, dt = a[14], a[15], a[16], a[17], a[20]
+        plane = seqs * n * h * dh * ES[dt]
+        return 8.0 * plane + 12.0 * seqs * h * n + 2.0 * seqs * n * h * ES[dt], 10.0 * seqs * h * n * n * dh
     if name == "pmb_gelu_forward":
         return 2.0 * a[2] * ES[a[3]], 0.0
     if name == "pmb_gelu_backward":

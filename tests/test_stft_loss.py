@@ -96,3 +96,45 @@ def test_real_fft_backward_matches_torch(n, norm):
     got, = torch.autograd.grad(RealFFTFn.apply(x, norm), x, gy)
     assert got.is_contiguous()
     torch.testing.assert_close(got, want, rtol=1e-12, atol=1e-12)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("win", [4096, 2048, 256])
+@pytest.mark.parametrize("normalized", [False, True])
+def test_stft_l1_loss_matches_torch(cuda_device, win, normalized):
+    """stft_l1_loss (framing kernels + rfft + SpectralL1Fn's one-pass mean and gradient) against
+    F.l1_loss(torch.stft(recon), torch.stft(target)): value and the recon gradient to 1e-5 relative."""
+    from pymsst_b200.fused import stft_l1_loss
+
+    n_fft = max(win, 2048)
+    g = torch.Generator().manual_seed(win + int(normalized))
+    x = torch.randn(3, 9000, generator=g).to(cuda_device)
+    t = torch.randn(3, 9000, generator=g).to(cuda_device)
+    w = torch.hann_window(win, device=cuda_device)
+    xa = x.clone().requires_grad_()
+    ours = stft_l1_loss(xa, t, n_fft, HOP, _window(win, n_fft, cuda_device), normalized)
+    (gx,) = torch.autograd.grad(ours, xa, torch.tensor(1.7, device=cuda_device))
+    xb = x.clone().requires_grad_()
+    kw = dict(n_fft=n_fft, hop_length=HOP, win_length=win, window=w, normalized=normalized, return_complex=True)
+    ref = torch.nn.functional.l1_loss(torch.stft(xb, **kw), torch.stft(t, **kw))
+    (gr,) = torch.autograd.grad(ref, xb, torch.tensor(1.7, device=cuda_device))
+    torch.testing.assert_close(ours, ref, rtol=1e-5, atol=0)
+    torch.testing.assert_close(gx, gr, rtol=1e-5, atol=1e-5 * float(gr.abs().max()))
+
+
+@pytest.mark.gpu
+def test_spectral_l1_zero_difference_and_odd_count(cuda_device):
+    """Equal spectra give loss 0 and gradient 0 (torch's convention for |z| at 0); an odd element count takes the
+    scalar tail of the vectorised sum."""
+    from pymsst_b200.fused import SpectralL1Fn
+
+    frames = torch.randn(3, 1, 2048, device=cuda_device).requires_grad_()  # 3 x 1025 = odd count
+    with torch.no_grad():
+        same = torch.fft.rfft(frames, dim=-1)
+    loss = SpectralL1Fn.apply(frames, same, "backward")
+    (g,) = torch.autograd.grad(loss, frames)
+    assert float(loss) == 0.0 and torch.count_nonzero(g) == 0
+    other = torch.randn(3, 1, 1025, dtype=torch.complex64, device=cuda_device)
+    loss = SpectralL1Fn.apply(frames, other, "backward")
+    ref = torch.nn.functional.l1_loss(torch.fft.rfft(frames.detach(), dim=-1), other)
+    torch.testing.assert_close(loss, ref, rtol=1e-5, atol=0)
