@@ -550,7 +550,11 @@ PMB_API int pmb_attention_backward(const void* q, const void* k, const void* v, 
  * grad_gated), writes dQ / dK (rotated back when cos / sin are given; both
  * NULL otherwise) and dV, and the gate logits' gradient
  * grad_logits[row * grad_logits_ld + head] = rowsum(grad_gated * gated) *
- * (1 - gate); all in one pass.  Replaces the attention core plus the separate
+ * (1 - gate); all in one pass.  With grad_bias_partials (fp32,
+ * pmb_attention_gate_bias_partials(sequences, heads) values, or NULL) it also
+ * writes the sums of the stored logit gradients over groups of 32 rows:
+ * partial[(pair * heads + head) * 4 + quarter], pair = sequence / 2, whose
+ * sum over pairs and quarters is the gate bias gradient of each head.  Replaces the attention core plus the separate
  * gate pass of the patched Attention.forward
  * (src/pymsst/training/fused_roformer.py:793-818; gate kernels
  * cuda/fused_band_split.cu:1778-2036). */
@@ -558,13 +562,14 @@ PMB_API int pmb_attention_forward_gated(const void* q, const void* k, const void
                                         void* gated, float* lse, int64_t sequences, int64_t seq_len, int64_t heads,
                                         int64_t dim_head, const int64_t* strides, float scale, int dtype,
                                         void* stream);
+PMB_API int64_t pmb_attention_gate_bias_partials(int64_t sequences, int64_t heads);
 PMB_API int pmb_attention_backward_gated(const void* q, const void* k, const void* v, const void* gated,
                                          const void* grad_gated, const float* lse, const void* gate_logits,
                                          const float* cos, const float* sin, void* grad_q, void* grad_k,
-                                         void* grad_v, void* grad_logits, int64_t grad_logits_ld, int64_t sequences,
-                                         int64_t seq_len, int64_t heads, int64_t dim_head, const int64_t* strides,
-                                         float scale, int dtype, void* workspace, int64_t workspace_bytes,
-                                         void* stream);
+                                         void* grad_v, void* grad_logits, int64_t grad_logits_ld,
+                                         float* grad_bias_partials, int64_t sequences, int64_t seq_len,
+                                         int64_t heads, int64_t dim_head, const int64_t* strides, float scale,
+                                         int dtype, void* workspace, int64_t workspace_bytes, void* stream);
 PMB_API int pmb_attention_backward_rotary(const void* q, const void* k, const void* v, const void* o,
                                           const void* grad_out, const float* lse, const float* cos, const float* sin,
                                           void* grad_q, void* grad_k, void* grad_v, int64_t sequences,

@@ -94,9 +94,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "pmb_attention_backward": (
         _i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _pi64, _f32, _i, _p, _i64, _p]),
     "pmb_attention_forward_gated": (_i, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _pi64, _f32, _i, _p]),
+    "pmb_attention_gate_bias_partials": (_i64, [_i64, _i64]),
     "pmb_attention_backward_gated": (
-        _i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _pi64, _f32, _i, _p,
-             _i64, _p]),
+        _i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _p, _i64, _i64, _i64, _i64, _pi64, _f32, _i,
+             _p, _i64, _p]),
     "pmb_attention_backward_rotary": (
         _i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _pi64, _f32, _i, _p, _i64, _p]),
     "pmb_spectral_l1_workspace_size": (_i64, [_i64]),

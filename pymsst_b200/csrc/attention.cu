@@ -1296,7 +1296,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                       T* __restrict__ dk, T* __restrict__ dv, Plane pdq, Plane pdk, Plane pdv, int sequences, int N,
                       int H, int ldl, int total, float scale, const float* __restrict__ rcos,
                       const float* __restrict__ rsin, const T* __restrict__ glogit, T* __restrict__ dlogit,
-                      int64_t dl_ld) {
+                      int64_t dl_ld, float* __restrict__ dbias) {
   using namespace bf;
   using L = Layout<kPack>;
   constexpr bool pack = kPack;
@@ -1570,11 +1570,22 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
         store_row32<T>(dk + rk, gk, scale);
         store_row32<T>(dq + rq, gq, scale);
-        if constexpr (pack) {
-          // gradient of the gate logit of query `row`: sum_d dGated * o * g (1 - g) = D (1 - g), D = g * staged
-          if (dlogit != nullptr && half == 0) {
+      }
+      if constexpr (pack) {
+        // gradient of the gate logit of query `row`: sum_d dGated * o * g (1 - g) = D (1 - g), D = g * staged;
+        // and, per warp, the sum of the stored values over its 32 queries (the gate bias gradient's partial of
+        // this item and lane quarter, summed in a fixed order by the caller)
+        if (dlogit != nullptr && half == 0) {  // warp-uniform
+          float dl = 0.f;
+          if (valid) {
             const float g = xs[3 * BM + row];
-            dlogit[((int64_t)seq * N + pos) * dl_ld + h] = Elem<T>::from_f((xs[row] + xs[BM + row]) * g * (1.f - g));
+            const T v = Elem<T>::from_f((xs[row] + xs[BM + row]) * g * (1.f - g));
+            dlogit[((int64_t)seq * N + pos) * dl_ld + h] = v;
+            dl = Elem<T>::to_f(v);
+          }
+          if (dbias != nullptr) {
+            dl = warp_sum(dl);
+            if (lane == 0) dbias[(int64_t)item * 4 + quarter] = dl;
           }
         }
       }
@@ -1736,7 +1747,8 @@ int attention_backward(const void* q, const void* k, const void* v, const void* 
                        const float* lse, void* grad_q, void* grad_k, void* grad_v, int64_t sequences, int64_t seq_len,
                        int64_t heads, int64_t dim_head, const int64_t* strides, float scale, int dtype,
                        const float* rcos, const float* rsin, void* workspace, int64_t workspace_bytes, void* stream,
-                       const char* name, const void* glogit = nullptr, void* dlogit = nullptr, int64_t dl_ld = 0) {
+                       const char* name, const void* glogit = nullptr, void* dlogit = nullptr, int64_t dl_ld = 0,
+                       float* dbias = nullptr) {
   if (int st = check_shape(name, dtype, sequences, seq_len, heads, dim_head)) return st;
   if (sequences == 0) return PMB_OK;
   PMB_REQUIRE(lse && strides, "%s: NULL argument", name);
@@ -1780,7 +1792,8 @@ int attention_backward(const void* q, const void* k, const void* v, const void* 
       kernel<<<grid, kBwdThreads, smem, s>>>(mq, mk, mv, mdo, mo, lse, static_cast<T*>(grad_q),
                                                  static_cast<T*>(grad_k), static_cast<T*>(grad_v), pdq, pdk, pdv,
                                                  (int)sequences, N, H, (int)ldl, (int)items, scale, rcos, rsin,
-                                                 static_cast<const T*>(glogit), static_cast<T*>(dlogit), dl_ld);
+                                                 static_cast<const T*>(glogit), static_cast<T*>(dlogit), dl_ld,
+                                                 dbias);
       PMB_CHECK_LAUNCH(name);
       return PMB_OK;
     };
@@ -1848,13 +1861,17 @@ extern "C" int pmb_attention_backward_rotary(const void* q, const void* k, const
                             strides, scale, dtype, cos, sin, workspace, workspace_bytes, stream, name);
 }
 
+extern "C" int64_t pmb_attention_gate_bias_partials(int64_t sequences, int64_t heads) {
+  return sequences > 0 && heads > 0 ? (sequences + 1) / 2 * heads * 4 : 0;
+}
+
 extern "C" int pmb_attention_backward_gated(const void* q, const void* k, const void* v, const void* gated,
                                             const void* grad_gated, const float* lse, const void* gate_logits,
                                             const float* cos, const float* sin, void* grad_q, void* grad_k,
                                             void* grad_v, void* grad_logits, int64_t grad_logits_ld,
-                                            int64_t sequences, int64_t seq_len, int64_t heads, int64_t dim_head,
-                                            const int64_t* strides, float scale, int dtype, void* workspace,
-                                            int64_t workspace_bytes, void* stream) {
+                                            float* grad_bias_partials, int64_t sequences, int64_t seq_len,
+                                            int64_t heads, int64_t dim_head, const int64_t* strides, float scale,
+                                            int dtype, void* workspace, int64_t workspace_bytes, void* stream) {
   clear_error();
   const char* name = "pmb_attention_backward_gated";
   PMB_REQUIRE(gate_logits && grad_logits && grad_logits_ld >= heads, "%s: gate logits and their gradient needed",
@@ -1866,5 +1883,5 @@ extern "C" int pmb_attention_backward_gated(const void* q, const void* k, const 
               "%s: angle tables must both be given (16-byte aligned) or both be NULL", name);
   return attention_backward(q, k, v, gated, grad_gated, lse, grad_q, grad_k, grad_v, sequences, seq_len, heads,
                             dim_head, strides, scale, dtype, cos, sin, workspace, workspace_bytes, stream, name,
-                            gate_logits, grad_logits, grad_logits_ld);
+                            gate_logits, grad_logits, grad_logits_ld, grad_bias_partials);
 }

@@ -748,10 +748,13 @@ class QKVAttentionGateFn(torch.autograd.Function):
         dgp = g2.view(b, n, h, dh).transpose(1, 2)
         ws_bytes = int(nat.library().pmb_attention_backward_workspace_size(b, n, h))
         ws = nat.workspace(ws_bytes, device)
+        # per (sequence pair, head, 32-row group) sums of the logit gradient: the gate bias gradient's partials
+        bpart = torch.empty(int(nat.library().pmb_attention_gate_bias_partials(b, h)), dtype=torch.float32,
+                            device=device)
         nat.call(
             "pmb_attention_backward_gated", q.data_ptr(), k.data_ptr(), v.data_ptr(), gated.data_ptr(),
             g2.data_ptr(), lse.data_ptr(), logits.data_ptr(), nat.ptr(cos), nat.ptr(sin), dq.data_ptr(),
-            dk.data_ptr(), dv.data_ptr(), ext[:, 3 * inner:].data_ptr(), ext.stride(0), b, n, h, dh,
+            dk.data_ptr(), dv.data_ptr(), ext[:, 3 * inner:].data_ptr(), ext.stride(0), bpart.data_ptr(), b, n, h, dh,
             nat.i64_array(_attn_strides(q, k, v, gp, dgp, dq, dk, dv)), dh ** -0.5, nat.dtype_code(q.dtype),
             ws.data_ptr(), ws_bytes, nat.stream_handle(device),
         )
@@ -763,7 +766,7 @@ class QKVAttentionGateFn(torch.autograd.Function):
             gw = gw_ext[:3 * inner].to(ctx.dtypes[0])
             gwg = gw_ext[3 * inner:].to(ctx.dtypes[1])
         if ctx.needs_input_grad[8]:
-            gbg = ext[:, 3 * inner:].float().sum(0).to(ctx.dtypes[2])
+            gbg = bpart.view(-1, h, 4).sum((0, 2)).to(ctx.dtypes[2])
         return gx, gw, None, None, None, None, None, gwg, gbg
 
 

@@ -149,7 +149,7 @@ def work(name: str, a: tuple) -> tuple[float, float]:
         plane = seqs * n * h * dh * ES[dt]
         return 4.0 * plane + 4.0 * seqs * h * n + seqs * n * h * ES[dt], 4.0 * seqs * h * n * n * dh
     if name == "pmb_attention_backward_gated":  # the backward plus logits read and their gradient written
-        seqs, n, h, dh, dt = a[14], a[15], a[16], a[17], a[20]
+        seqs, n, h, dh, dt = a[15], a[16], a[17], a[18], a[21]
         plane = seqs * n * h * dh * ES[dt]
         return 8.0 * plane + 12.0 * seqs * h * n + 2.0 * seqs * n * h * ES[dt], 10.0 * seqs * h * n * n * dh
     if name == "pmb_gelu_forward":
