@@ -578,6 +578,28 @@ PMB_API int pmb_attention_backward_rotary(const void* q, const void* k, const vo
                                           void* stream);
 
 /* ------------------------------------------------------------------------
+ * The overlap-add of torch.istft (center=True), after the inverse real FFT
+ * of each frame: y[b, i] = sum_t frames[b, k, t] w[k] / env[i + n/2] with
+ * k = i + n/2 - t*hop over the frames that cover that position, env the
+ * overlap-added squared window, i < length (zeros past the signal's end, as
+ * torch.istft pads to `length`).  frames [batch, n_fft, num_frames] fp32 at
+ * any element strides (frame_strides = {batch, k, t}: the inverse FFT along
+ * the frequency axis of a [F, T] spectrum leaves time fastest), window fp32
+ * [n_fft] (zero-padded to n_fft, centred).  The backward writes the frames'
+ * gradient grad_frames[b, k, t] (contiguous [batch, n_fft, num_frames]) =
+ * grad_y[b, t*hop + k - n/2] w[k] / env (0 outside the trimmed range).  One
+ * pass each, replacing the window multiply, the overlap-add, the envelope
+ * division, the trim and their backward (pymss-core's torch.istft at the end
+ * of the BS-/Mel-RoFormer forward, reached from
+ * src/pymsst/training/module.py:221-224). */
+PMB_API int pmb_istft_overlap_add_forward(const float* frames, const int64_t* frame_strides, const float* window,
+                                          float* y, int64_t batch, int64_t n_fft, int64_t num_frames, int64_t hop,
+                                          int64_t length, void* stream);
+PMB_API int pmb_istft_overlap_add_backward(const float* grad_y, const float* window, float* grad_frames,
+                                           int64_t batch, int64_t n_fft, int64_t num_frames, int64_t hop,
+                                           int64_t length, void* stream);
+
+/* ------------------------------------------------------------------------
  * One resolution of the multi-resolution STFT loss: mean |Y_recon - Y_target|
  * over `count` complex values (fp32, interleaved re / im; 16-byte aligned),
  * the F.l1_loss of two onesided spectra.  The forward writes the mean to

@@ -100,6 +100,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
              _p, _i64, _p]),
     "pmb_attention_backward_rotary": (
         _i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _pi64, _f32, _i, _p, _i64, _p]),
+    "pmb_istft_overlap_add_forward": (_i, [_p, _pi64, _p, _p, _i64, _i64, _i64, _i64, _i64, _p]),
+    "pmb_istft_overlap_add_backward": (_i, [_p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p]),
     "pmb_spectral_l1_workspace_size": (_i64, [_i64]),
     "pmb_spectral_l1_forward": (_i, [_p, _p, _i64, _p, _p, _i64, _p]),
     "pmb_spectral_l1_backward": (_i, [_p, _p, _i64, _i64, _i64, _p, _p, _p]),

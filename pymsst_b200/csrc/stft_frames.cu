@@ -89,10 +89,102 @@ __global__ void __launch_bounds__(kThreads)
   *reinterpret_cast<float4*>(frames + (int64_t)bt * n + k0) = o;
 }
 
+// ------------------------------------------------------------------ iSTFT
+// Overlap-add of the inverse-FFT frames of torch.istft (center=True):
+//   y[i] = sum_t frames[t][p - t*hop] w[p - t*hop] / env[p],  p = i + n/2,
+//   env[p] = sum_t w[p - t*hop]^2   (the overlap-added squared window)
+// over the frames t with 0 <= p - t*hop < n, for the trimmed output i < len
+// (zeros past the untrimmed end, as torch.istft pads to `length`).  The
+// frames are the inverse real FFT along the frequency axis of a [F, T]
+// spectrum, element (k, t) of batch b at frames[b * sb + k * sk + t * st]
+// (the layout the transform returned).  One thread per output sample; the
+// envelope is summed in the same loop (no buffer).
+__global__ void __launch_bounds__(kThreads)
+    istft_ola_fwd(const float* __restrict__ frames, int64_t sb, int64_t sk, int64_t st,
+                  const float* __restrict__ window, float* __restrict__ y, int n, int T, int hop, int len) {
+  const int i = blockIdx.x * kThreads + threadIdx.x;
+  if (i >= len) return;
+  const float* fb = frames + (int64_t)blockIdx.y * sb;
+  const int p = i + n / 2;
+  const int t_lo = p - n + 1 > 0 ? (p - n + hop) / hop : 0;
+  int t_hi = p / hop;
+  if (t_hi > T - 1) t_hi = T - 1;
+  float acc = 0.f, env = 0.f;
+  for (int t = t_lo; t <= t_hi; ++t) {
+    const int k = p - t * hop;
+    const float w = window[k];
+    acc = fmaf(fb[k * sk + t * st], w, acc);
+    env = fmaf(w, w, env);
+  }
+  y[(int64_t)blockIdx.y * len + i] = t_lo <= t_hi ? acc / env : 0.f;
+}
+
+// Its gradient with respect to the frames: each frame element (k, t) was
+// added into exactly one output sample, p = t*hop + k:
+//   grad_frames[k * T + t] = grad_y[p - n/2] w[k] / env[p]  (0 outside the trimmed range)
+// grid (n * T / 256, batch), consecutive threads take consecutive t.
+__global__ void __launch_bounds__(kThreads)
+    istft_ola_bwd(const float* __restrict__ grad_y, const float* __restrict__ window, float* __restrict__ grad_frames,
+                  int n, int T, int hop, int len) {
+  const int e = blockIdx.x * kThreads + threadIdx.x;
+  if (e >= n * T) return;
+  const int k = e / T, t = e - k * T;
+  const int p = t * hop + k, i = p - n / 2;
+  float g = 0.f;
+  if (i >= 0 && i < len) {
+    const int t_lo = p - n + 1 > 0 ? (p - n + hop) / hop : 0;
+    int t_hi = p / hop;
+    if (t_hi > T - 1) t_hi = T - 1;
+    float env = 0.f;
+    for (int u = t_lo; u <= t_hi; ++u) {
+      const float w = window[p - u * hop];
+      env = fmaf(w, w, env);
+    }
+    g = grad_y[(int64_t)blockIdx.y * len + i] * window[k] / env;
+  }
+  grad_frames[(int64_t)blockIdx.y * n * T + e] = g;
+}
+
 }  // namespace
 }  // namespace pmb
 
 using namespace pmb;
+
+extern "C" int pmb_istft_overlap_add_forward(const float* frames, const int64_t* frame_strides, const float* window,
+                                             float* y, int64_t batch, int64_t n_fft, int64_t num_frames, int64_t hop,
+                                             int64_t length, void* stream) {
+  clear_error();
+  const char* name = "pmb_istft_overlap_add_forward";
+  PMB_REQUIRE(batch >= 0 && n_fft > 0 && num_frames > 0 && hop > 0 && hop <= n_fft && length > 0,
+              "%s: bad shape", name);
+  PMB_REQUIRE(n_fft * num_frames < ((int64_t)1 << 31) && length < (1 << 30) && batch <= 65535, "%s: too large", name);
+  if (batch == 0) return PMB_OK;
+  PMB_REQUIRE(frames && frame_strides && window && y, "%s: NULL argument", name);
+  PMB_REQUIRE(frame_strides[0] >= 0 && frame_strides[1] >= 0 && frame_strides[2] >= 0, "%s: bad strides", name);
+  const dim3 grid((unsigned)((length + kThreads - 1) / kThreads), (unsigned)batch);
+  istft_ola_fwd<<<grid, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      frames, frame_strides[0], frame_strides[1], frame_strides[2], window, y, (int)n_fft, (int)num_frames, (int)hop,
+      (int)length);
+  PMB_CHECK_LAUNCH(name);
+  return PMB_OK;
+}
+
+extern "C" int pmb_istft_overlap_add_backward(const float* grad_y, const float* window, float* grad_frames,
+                                              int64_t batch, int64_t n_fft, int64_t num_frames, int64_t hop,
+                                              int64_t length, void* stream) {
+  clear_error();
+  const char* name = "pmb_istft_overlap_add_backward";
+  PMB_REQUIRE(batch >= 0 && n_fft > 0 && num_frames > 0 && hop > 0 && hop <= n_fft && length > 0,
+              "%s: bad shape", name);
+  PMB_REQUIRE(n_fft * num_frames < ((int64_t)1 << 31) && length < (1 << 30) && batch <= 65535, "%s: too large", name);
+  if (batch == 0) return PMB_OK;
+  PMB_REQUIRE(grad_y && window && grad_frames, "%s: NULL argument", name);
+  const dim3 grid((unsigned)((n_fft * num_frames + kThreads - 1) / kThreads), (unsigned)batch);
+  istft_ola_bwd<<<grid, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(grad_y, window, grad_frames, (int)n_fft,
+                                                                          (int)num_frames, (int)hop, (int)length);
+  PMB_CHECK_LAUNCH(name);
+  return PMB_OK;
+}
 
 extern "C" int pmb_stft_frames_forward(const float* x, const float* window, float* frames, int64_t batch,
                                        int64_t length, int64_t n_fft, int64_t hop, int64_t num_frames, void* stream) {

@@ -833,6 +833,36 @@ class RealFFTFn(torch.autograd.Function):
         return torch.fft.irfft(g * w, n=n, dim=-1, norm=_INVERSE_NORM[ctx.norm]), None
 
 
+class ISTFTOverlapAddFn(torch.autograd.Function):
+    """The overlap-add of torch.istft (center=True) after the per-frame inverse real FFT: frames fp32
+    [B, n_fft, T] (any strides, e.g. torch.fft.irfft along dim -2 of a [B, F, T] spectrum) -> y [B, length] =
+    the window-weighted overlap-add divided by the overlap-added squared window, centre-trimmed, zero past the
+    signal's end.  One kernel each way (pmb_istft_overlap_add_forward / _backward)."""
+
+    @staticmethod
+    def forward(ctx, frames, window, hop, length):
+        device = nat.require_cuda(frames, window, name="ISTFTOverlapAdd")
+        frames = frames.float()
+        window = window.float().contiguous()
+        b, n, t = frames.shape
+        y = torch.empty(b, length, dtype=torch.float32, device=device)
+        nat.call("pmb_istft_overlap_add_forward", frames.data_ptr(), nat.i64_array(list(frames.stride())),
+                 window.data_ptr(), y.data_ptr(), b, n, t, hop, length, nat.stream_handle(device))
+        ctx.save_for_backward(window)
+        ctx.meta = (b, n, t, hop, length)
+        return y
+
+    @staticmethod
+    def backward(ctx, g):
+        (window,) = ctx.saved_tensors
+        b, n, t, hop, length = ctx.meta
+        g = g.float().contiguous()
+        gf = torch.empty(b, n, t, dtype=torch.float32, device=g.device)
+        nat.call("pmb_istft_overlap_add_backward", g.data_ptr(), window.data_ptr(), gf.data_ptr(), b, n, t, hop,
+                 length, nat.stream_handle(g.device))
+        return gf, None, None, None
+
+
 class SpectralL1Fn(torch.autograd.Function):
     """mean |rfft(frames) - target_spec| (F.l1_loss of two onesided spectra) with the rfft inside.  Forward:
     torch.fft.rfft, then one pass for the mean (pmb_spectral_l1_forward, deterministic).  Backward: one pass

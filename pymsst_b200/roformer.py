@@ -51,6 +51,7 @@ from .fused import (
     BandRecombineFn,
     BandSplitFn,
     FeedForwardFn,
+    ISTFTOverlapAddFn,
     MaskEstimatorFn,
     MaskEstimatorTCFn,
     OutProjFn,
@@ -100,6 +101,9 @@ def _istft_overlap_add(z, n_fft, hop, window, normalized, length):
         win = F.pad(win, (left, n_fft - win.shape[0] - left))
     t = frames.shape[-1]
     total = n_fft + hop * (t - 1)
+    if frames.is_cuda:
+        # window, overlap-add, envelope division and trim in one kernel each way
+        return ISTFTOverlapAddFn.apply(frames, win, hop, length if length is not None else total - n_fft)
     y = _overlap_add(frames * win[:, None], hop)
     key = (n_fft, hop, t, win.device, win.data_ptr(), win._version)
     env = _ENVELOPES.get(key)
