@@ -59,7 +59,8 @@ TIMED_ENTRIES = [
     "pmb_band_split_tc_backward", "pmb_gelu_forward", "pmb_gelu_backward", "pmb_column_sum",
     "pmb_attention_forward", "pmb_attention_backward", "pmb_attention_backward_rotary", "pmb_rms_norm_backward_add",
     "pmb_stft_frames_forward", "pmb_stft_frames_backward", "pmb_spectral_l1_forward", "pmb_spectral_l1_backward",
-    "pmb_attention_forward_gated", "pmb_attention_backward_gated",
+    "pmb_attention_forward_gated", "pmb_attention_backward_gated", "pmb_istft_overlap_add_forward",
+    "pmb_istft_overlap_add_backward",
 ]
 
 

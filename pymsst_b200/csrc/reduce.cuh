@@ -74,34 +74,47 @@ __global__ void __launch_bounds__(kThreads)
 }
 
 // Column sums of a [nrows, cols] fp32 partial matrix with many rows: each CTA
-// covers 8 columns with 32 row lanes (a warp reads 4 rows x 32 bytes per
-// load, four loads in flight per thread); the row lanes are combined in
-// shared memory in a fixed order.  Launch: grid ceil(cols / 8), 256 threads.
-// out[c] stored as out_code.
-inline int colsum_rows_grid(int64_t cols) { return (int)((cols + 7) / 8); }
+// covers 4 columns with 64 row lanes (a warp reads 8 rows x 16 bytes per
+// load, four loads in flight per thread), so even a 192-column matrix spreads
+// over 48 CTAs; the row lanes are combined in shared memory in a fixed order.
+// Launch: grid colsum_rows_grid(cols), 256 threads.  out[c] stored as out_code.
+constexpr int kColsumCols = 4;
+constexpr int kColsumRowLanes = kThreads / kColsumCols;
+inline int colsum_rows_grid(int64_t cols) { return (int)((cols + kColsumCols - 1) / kColsumCols); }
 
 __global__ void __launch_bounds__(kThreads)
     colsum_rows(const float* __restrict__ partial, int nrows, int64_t cols, void* __restrict__ out, int out_code) {
-  __shared__ float red_s[32][9];
-  const int cl = threadIdx.x & 7, rl = threadIdx.x >> 3;
-  const int64_t c = (int64_t)blockIdx.x * 8 + cl;
+  __shared__ float red_s[kColsumRowLanes][kColsumCols + 1];
+  __shared__ float red8[8][kColsumCols];
+  const int cl = threadIdx.x % kColsumCols, rl = threadIdx.x / kColsumCols;
+  const int64_t c = (int64_t)blockIdx.x * kColsumCols + cl;
+  constexpr int R = kColsumRowLanes;
   float s = 0.f;
   if (c < cols) {
     int r = rl;
-    for (; r + 96 < nrows; r += 128) {
-      const float a = partial[(int64_t)r * cols + c], b = partial[(int64_t)(r + 32) * cols + c];
-      const float d = partial[(int64_t)(r + 64) * cols + c], e = partial[(int64_t)(r + 96) * cols + c];
+    for (; r + 3 * R < nrows; r += 4 * R) {
+      const float a = partial[(int64_t)r * cols + c], b = partial[(int64_t)(r + R) * cols + c];
+      const float d = partial[(int64_t)(r + 2 * R) * cols + c], e = partial[(int64_t)(r + 3 * R) * cols + c];
       s += (a + b) + (d + e);
     }
-    for (; r < nrows; r += 32) s += partial[(int64_t)r * cols + c];
+    for (; r < nrows; r += R) s += partial[(int64_t)r * cols + c];
   }
   red_s[rl][cl] = s;
   __syncthreads();
-  if (threadIdx.x < 8 && (int64_t)blockIdx.x * 8 + threadIdx.x < cols) {
+  // 64 row lanes -> 8 per column in fixed pairs, then the 8 summed by one thread
+  if (threadIdx.x < 8 * kColsumCols) {
+    const int col = threadIdx.x % kColsumCols, part = threadIdx.x / kColsumCols;
     float t = 0.f;
-#pragma unroll 8
-    for (int k = 0; k < 32; ++k) t += red_s[k][threadIdx.x];
-    store_dyn(out, (int64_t)blockIdx.x * 8 + threadIdx.x, out_code, t);
+#pragma unroll
+    for (int k = 0; k < R / 8; ++k) t += red_s[part * (R / 8) + k][col];
+    red8[part][col] = t;
+  }
+  __syncthreads();
+  if (threadIdx.x < kColsumCols && (int64_t)blockIdx.x * kColsumCols + threadIdx.x < cols) {
+    float t = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t += red8[k][threadIdx.x];
+    store_dyn(out, (int64_t)blockIdx.x * kColsumCols + threadIdx.x, out_code, t);
   }
 }
 

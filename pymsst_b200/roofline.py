@@ -140,6 +140,12 @@ def work(name: str, a: tuple) -> tuple[float, float]:
     if name in ("pmb_stft_frames_forward", "pmb_stft_frames_backward"):
         b, length, n_fft, frames = a[3], a[4], a[5], a[7]
         return 4.0 * (b * length + b * frames * n_fft + n_fft), 1.0 * b * frames * n_fft
+    if name == "pmb_istft_overlap_add_forward":  # frames read once, the signal written
+        b, n, t, length = a[4], a[5], a[6], a[8]
+        return 4.0 * b * (n * t + length), 3.0 * b * n * t
+    if name == "pmb_istft_overlap_add_backward":  # the signal's gradient read, the frames' written
+        b, n, t, length = a[3], a[4], a[5], a[7]
+        return 4.0 * b * (n * t + length), 2.0 * b * n * t
     if name == "pmb_spectral_l1_forward":  # two complex64 spectra read
         return 16.0 * a[2], 4.0 * a[2]
     if name == "pmb_spectral_l1_backward":  # two read, the gradient written
