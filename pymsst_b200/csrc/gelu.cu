@@ -31,8 +31,18 @@ __global__ void __launch_bounds__(256) gelu_fwd_kernel(const T* __restrict__ x, 
   for (int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x; i < nv; i += (int64_t)gridDim.x * 256) {
     uint4 u = reinterpret_cast<const uint4*>(x)[i];
     T* e = reinterpret_cast<T*>(&u);
+    if constexpr (sizeof(T) == 2) {  // two values per packed instruction
 #pragma unroll
-    for (int j = 0; j < N; ++j) e[j] = Elem<T>::from_f(gelu_of<T>(Elem<T>::to_f(e[j])));
+      for (int j = 0; j < N; j += 2) {
+        float a, b;
+        gelu_fast2(Elem<T>::to_f(e[j]), Elem<T>::to_f(e[j + 1]), a, b);
+        e[j] = Elem<T>::from_f(a);
+        e[j + 1] = Elem<T>::from_f(b);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < N; ++j) e[j] = Elem<T>::from_f(gelu_of<T>(Elem<T>::to_f(e[j])));
+    }
     reinterpret_cast<uint4*>(y)[i] = u;
   }
   // tail (n not a multiple of the vector width)
@@ -84,11 +94,24 @@ __global__ void __launch_bounds__(256, 3)
           const T* g = reinterpret_cast<const T*>(&ug[k]);
           uint4 uo;
           T* o = reinterpret_cast<T*>(&uo);
+          if constexpr (sizeof(T) == 2) {  // two values per packed instruction
 #pragma unroll
-          for (int j = 0; j < N; ++j) {
-            const float v = Elem<T>::to_f(e[j]);
-            o[j] = Elem<T>::from_f(Elem<T>::to_f(g[j]) * gelu_grad_of<T>(v));
-            acc[j] += Elem<T>::to_f(o[j]);
+            for (int j = 0; j < N; j += 2) {
+              float d0, d1, q0, q1;
+              gelu_grad_fast2(Elem<T>::to_f(e[j]), Elem<T>::to_f(e[j + 1]), d0, d1);
+              unpk2(mul2(pk2(Elem<T>::to_f(g[j]), Elem<T>::to_f(g[j + 1])), pk2(d0, d1)), q0, q1);
+              o[j] = Elem<T>::from_f(q0);
+              o[j + 1] = Elem<T>::from_f(q1);
+              acc[j] += Elem<T>::to_f(o[j]);
+              acc[j + 1] += Elem<T>::to_f(o[j + 1]);
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < N; ++j) {
+              const float v = Elem<T>::to_f(e[j]);
+              o[j] = Elem<T>::from_f(Elem<T>::to_f(g[j]) * gelu_grad_of<T>(v));
+              acc[j] += Elem<T>::to_f(o[j]);
+            }
           }
           *reinterpret_cast<uint4*>(gx + r * cols + c) = uo;
         }

@@ -285,12 +285,16 @@ __global__ void __launch_bounds__(kThreads)
 constexpr int kStages = 4;
 constexpr int kFwdStageBytes = 12288;
 constexpr int kBwdStageBytes = 8192;  // per input (dy, saved)
+// With the residual gradient as a third input: 3 stages of 12 KB per input, so a tile of the model's 192-wide
+// 16-bit rows holds 32 rows (every row slot of the 8 warps busy) at 2 CTAs per SM.
+constexpr int kBwdStageBytesRes = 12288;
+constexpr int kBwdStagesRes = 3;
 
 constexpr int kMaxBulkDim = 1024;  // gamma staged as fp32 after the ring and the barriers
 
-template <int STAGE_BYTES, int INPUTS>
+template <int STAGE_BYTES, int INPUTS, int STAGES = kStages>
 constexpr int bulk_smem_bytes() {
-  return kStages * STAGE_BYTES * INPUTS + 128 + kMaxBulkDim * 4;
+  return STAGES * STAGE_BYTES * INPUTS + 128 + kMaxBulkDim * 4;
 }
 
 // gamma as fp32 into shared memory (whole CTA; followed by the caller's barrier)
@@ -415,9 +419,11 @@ __global__ void __launch_bounds__(kThreads, RES ? 2 : 3)
                  const Tdx* __restrict__ dres, float* __restrict__ partial, int64_t rows, int dim, int rpt) {
   constexpr int RW = 32 / G;
   constexpr int IN = RES ? 3 : 2;  // staged inputs per ring slot
+  constexpr int SB = RES ? kBwdStageBytesRes : kBwdStageBytes;  // bytes per input per slot
+  constexpr int NS = RES ? kBwdStagesRes : kStages;              // ring slots
   extern __shared__ __align__(128) uint8_t smem[];
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kBwdStageBytes * IN);
-  float* g_s = reinterpret_cast<float*>(smem + kStages * kBwdStageBytes * IN + 128);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + NS * SB * IN);
+  float* g_s = reinterpret_cast<float*>(smem + NS * SB * IN + 128);
   float* red = reinterpret_cast<float*>(smem);  // reused after the ring drains: [kWarps * RW][dim]
   const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
   const int gl = lane % G, sub = lane / G;
@@ -426,7 +432,7 @@ __global__ void __launch_bounds__(kThreads, RES ? 2 : 3)
   const float scale = sqrtf((float)dim);
   const int64_t tiles = (rows + rpt - 1) / rpt;
   if (threadIdx.x == 0) {
-    for (int st = 0; st < kStages; ++st) umma::mbar_init(&full[st], 1);
+    for (int st = 0; st < NS; ++st) umma::mbar_init(&full[st], 1);
     umma::fence_barrier_init();
   }
   __syncthreads();
@@ -434,14 +440,14 @@ __global__ void __launch_bounds__(kThreads, RES ? 2 : 3)
     const int64_t r0 = tile * rpt;
     const int64_t n = rows - r0 < rpt ? rows - r0 : rpt;
     const uint32_t bytes = (uint32_t)(n * dim * (int64_t)sizeof(Tg));
-    uint8_t* base = smem + st * kBwdStageBytes * IN;
+    uint8_t* base = smem + st * SB * IN;
     umma::mbar_arrive_expect_tx(&full[st], IN * bytes);
     umma::bulk_load(base, dy + r0 * dim, bytes, &full[st]);
-    umma::bulk_load(base + kBwdStageBytes, saved + r0 * dim, bytes, &full[st]);
-    if constexpr (RES) umma::bulk_load(base + 2 * kBwdStageBytes, dres + r0 * dim, bytes, &full[st]);
+    umma::bulk_load(base + SB, saved + r0 * dim, bytes, &full[st]);
+    if constexpr (RES) umma::bulk_load(base + 2 * SB, dres + r0 * dim, bytes, &full[st]);
   };
   if (threadIdx.x == 0)
-    for (int st = 0; st < kStages; ++st) {
+    for (int st = 0; st < NS; ++st) {
       const int64_t t = blockIdx.x + (int64_t)st * gridDim.x;
       if (t < tiles) issue(t, st);
     }
@@ -452,17 +458,17 @@ __global__ void __launch_bounds__(kThreads, RES ? 2 : 3)
     for (int e = 0; e < V; ++e) acc[j][e] = 0.f;
   int it = 0;
   for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++it) {
-    const int st = it % kStages;
+    const int st = it % NS;
     const int64_t r0 = tile * rpt;
     const int n = rows - r0 < rpt ? (int)(rows - r0) : rpt;
     // this warp's row norms for the tile, one load per lane, before the wait
     const int qi = wib * RW + (lane / RW) * kWarps * RW + (lane % RW);
     const float inv_l = qi < n ? inv_norm[r0 + qi] : 0.f;
     // every thread takes the same decision, so no thread is left at a barrier
-    if (__syncthreads_or(!umma::mbar_wait(&full[st], (it / kStages) & 1, 0x22))) break;
-    Tg* ds_ = reinterpret_cast<Tg*>(smem + st * kBwdStageBytes * IN);
-    const Tg* ss_ = reinterpret_cast<const Tg*>(smem + st * kBwdStageBytes * IN + kBwdStageBytes);
-    const Tdx* rs_ = reinterpret_cast<const Tdx*>(smem + st * kBwdStageBytes * IN + 2 * kBwdStageBytes);
+    if (__syncthreads_or(!umma::mbar_wait(&full[st], (it / NS) & 1, 0x22))) break;
+    Tg* ds_ = reinterpret_cast<Tg*>(smem + st * SB * IN);
+    const Tg* ss_ = reinterpret_cast<const Tg*>(smem + st * SB * IN + SB);
+    const Tdx* rs_ = reinterpret_cast<const Tdx*>(smem + st * SB * IN + 2 * SB);
     int step = 0;
     for (int qb = wib * RW; qb < n; qb += kWarps * RW, ++step) {
       const int q = qb + sub;
@@ -528,7 +534,7 @@ __global__ void __launch_bounds__(kThreads, RES ? 2 : 3)
         umma::bulk_store(dx + r0 * dim, ds_, (uint32_t)(n * dim * (int64_t)sizeof(Tdx)));
         umma::bulk_commit();
       }
-      const int64_t nt = tile + (int64_t)kStages * gridDim.x;
+      const int64_t nt = tile + (int64_t)NS * gridDim.x;
       if (nt < tiles) {
         if (dx != nullptr) umma::bulk_wait_read_all();
         issue(nt, st);
@@ -640,9 +646,10 @@ int launch_bwd(const void* dy, const void* saved, int saved_is_input, const floa
   int used_grid = grid;  // CTAs writing grad_gamma partial rows
   // Register budget: at most 1024 elements of a row per warp in the vector path.
   const int64_t row_bytes = dim * (int64_t)sizeof(Tg);
-  if (vec_ok && sizeof(Tg) == sizeof(Tdx) && dim <= kMaxBulkDim && row_bytes <= kBwdStageBytes &&
-      (int64_t)kWarps * 4 * dim * 4 <= (int64_t)kStages * kBwdStageBytes * 2) {
-    const int rpt = (int)(kBwdStageBytes / row_bytes < kMaxBwdTileRows ? kBwdStageBytes / row_bytes : kMaxBwdTileRows);
+  const int64_t sb = dres ? kBwdStageBytesRes : kBwdStageBytes, ns = dres ? kBwdStagesRes : kStages;
+  if (vec_ok && sizeof(Tg) == sizeof(Tdx) && dim <= kMaxBulkDim && row_bytes <= sb &&
+      (int64_t)kWarps * 4 * dim * 4 <= ns * sb * 2) {
+    const int rpt = (int)(sb / row_bytes < kMaxBwdTileRows ? sb / row_bytes : kMaxBwdTileRows);
     const int64_t tiles = (rows + rpt - 1) / rpt;
     // 3 CTAs of 68 KB shared memory per SM (2 of 100 KB with the residual gradient staged as a third input)
     int64_t g = (int64_t)num_sms() * (drp ? 2 : 3);
@@ -656,7 +663,8 @@ int launch_bwd(const void* dy, const void* saved, int saved_is_input, const floa
     };
     auto pick = [&](auto res) {
       constexpr bool R = decltype(res)::value;
-      constexpr int bsm = bulk_smem_bytes<kBwdStageBytes, R ? 3 : 2>();
+      constexpr int bsm = R ? bulk_smem_bytes<kBwdStageBytesRes, 3, kBwdStagesRes>()
+                            : bulk_smem_bytes<kBwdStageBytes, 2>();
       if (nvec <= 8)
         go(rms_bwd_bulk<Tg, Tdx, V, 8, 1, R>, bsm);
       else if (nvec <= 24)
