@@ -102,13 +102,7 @@ __device__ __forceinline__ void phi_cdf_fast2(float x0, float x1, float& p0, flo
   p1 = rcp_approx(d1);
 }
 
-// 16-bit paths, two values at a time: x * Phi(x) and Phi(x) + x phi(x)
-__device__ __forceinline__ void gelu_fast2(float x0, float x1, float& y0, float& y1) {
-  float p0, p1;
-  uint64_t t;
-  phi_cdf_fast2(x0, x1, p0, p1, t);
-  unpk2(mul2(pk2(x0, x1), pk2(p0, p1)), y0, y1);
-}
+// 16-bit path, two values at a time: Phi(x) + x phi(x)
 __device__ __forceinline__ void gelu_grad_fast2(float x0, float x1, float& g0, float& g1) {
   float p0, p1;
   uint64_t t;
