@@ -457,13 +457,50 @@ def op_mask(bench: _Bench):
     bench.time("mask_estimator_tc fwd+bwd", fwd_bwd, 3 * byt, 3 * flops)
 
 
+def op_stft(bench: _Bench):
+    """Loss and output transforms of config 3: one resolution of the multi-resolution STFT loss (8 signals of
+    131584 samples, n_fft 2048, hop 147: spectral L1 forward and backward) and the iSTFT overlap-add of the model
+    output (8 signals, n_fft 2048, hop 512, 258 frames)."""
+    dev = bench.device
+    st = nat.stream_handle(dev)
+    nsig, length, n_fft = 8, 131584, 2048
+    frames = 1 + length // 147
+    count = nsig * frames * (n_fft // 2 + 1)
+    yr = torch.randn(count * 2, device=dev)
+    yt = torch.randn(count * 2, device=dev)
+    gy = torch.empty_like(yr)
+    loss = torch.empty((), device=dev)
+    one = torch.ones(1, device=dev)
+    wsb = int(nat.library().pmb_spectral_l1_workspace_size(count))
+    ws = nat.workspace(wsb, dev)
+    bench.time("spectral_l1_forward [8, 896, 1025]", lambda: nat.call(
+        "pmb_spectral_l1_forward", yr.data_ptr(), yt.data_ptr(), count, loss.data_ptr(), ws.data_ptr(), wsb, st),
+        16.0 * count)
+    bench.time("spectral_l1_backward [8, 896, 1025]", lambda: nat.call(
+        "pmb_spectral_l1_backward", yr.data_ptr(), yt.data_ptr(), count, n_fft // 2 + 1, n_fft, one.data_ptr(),
+        gy.data_ptr(), st), 24.0 * count)
+    hop, t = 512, 258
+    fr = torch.randn(nsig, n_fft, t, device=dev)
+    win = torch.hann_window(n_fft, device=dev)
+    y = torch.empty(nsig, length, device=dev)
+    gfr = torch.empty_like(fr)
+    strides = nat.i64_array(list(fr.stride()))
+    byt = 4.0 * nsig * (n_fft * t + length)
+    bench.time("istft_overlap_add_forward [8, 2048, 258]", lambda: nat.call(
+        "pmb_istft_overlap_add_forward", fr.data_ptr(), strides, win.data_ptr(), y.data_ptr(), nsig, n_fft, t, hop,
+        length, st), byt)
+    bench.time("istft_overlap_add_backward [8, 2048, 258]", lambda: nat.call(
+        "pmb_istft_overlap_add_backward", y.data_ptr(), win.data_ptr(), gfr.data_ptr(), nsig, n_fft, t, hop, length,
+        st), byt)
+
+
 def op_band_sweep(bench: _Bench):
     """BandSplit at the config-2 sweep size (8192 rows), for profiling it alone."""
     _op_band_rows(bench, 8 * 1024)
 
 
 OPS = {"gate": op_gate, "band": op_band, "band8192": op_band_sweep, "mel": op_mel, "mask": op_mask, "rms": op_rms,
-       "qkv": op_qkv, "ff": op_ff, "sdpa": op_sdpa, "attn": op_attn}
+       "qkv": op_qkv, "ff": op_ff, "sdpa": op_sdpa, "attn": op_attn, "stft": op_stft}
 
 
 # ---------------------------------------------------------------------------

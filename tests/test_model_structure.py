@@ -83,3 +83,37 @@ def test_synthetic_generator_is_seeded():
     mix4, tgt4 = synthetic.make_batch(1, 1024, seed=0, stems=4)
     assert tgt4.shape == (1, 4, 2, 1024)
     torch.testing.assert_close(mix4, tgt4.sum(1))
+
+
+@pytest.mark.parametrize("model_type,kwargs", [("bs_roformer", TINY_BSR), ("mel_band_roformer", TINY_MBR)])
+def test_checkpoint_package_round_trip(tmp_path, model_type, kwargs):
+    """The reference's export package (src/pymsst/export/checkpoint.py:10-31): written from this package's model,
+    loaded back (model rebuilt from the package's config) and into the oracle (pymss-core's layout), and one
+    written from the oracle's model loaded here; every tensor survives bit for bit."""
+    from pymsst_b200.checkpoint import export_core_checkpoint, load_core_checkpoint
+
+    torch.manual_seed(3)
+    ours, ref = _pair(model_type, kwargs)
+    conf = {"model": dict(kwargs), "training": {"batch_size": 2}}
+    path = export_core_checkpoint(ours, tmp_path / "ours.ckpt", model_type=model_type, config=conf,
+                                  metadata={"epoch": 1})
+    package = torch.load(path, map_location="cpu", weights_only=True)
+    assert set(package) == {"state_dict", "model_type", "config", "metadata"}
+    assert package["model_type"] == model_type and package["metadata"] == {"epoch": 1}
+    assert all(t.device.type == "cpu" for t in package["state_dict"].values())
+    back, _ = load_core_checkpoint(path)
+    ref.load_state_dict(package["state_dict"], strict=True)
+    want = ours.state_dict()
+    for k, v in back.state_dict().items():
+        assert torch.equal(v, want[k]), k
+    for k, v in ref.state_dict().items():
+        assert torch.equal(v, want[k]), k
+    # the other direction: the oracle's weights exported in the same layout load into this package's model
+    torch.manual_seed(4)
+    _, ref2 = _pair(model_type, kwargs)
+    path2 = export_core_checkpoint(ref2, tmp_path / "ref.ckpt", model_type=model_type)
+    mine, _ = load_core_checkpoint(path2, model=cfg.build_model(model_type, **kwargs))
+    for k, v in ref2.state_dict().items():
+        assert torch.equal(mine.state_dict()[k], v), k
+    with pytest.raises(ValueError, match="no config"):
+        load_core_checkpoint(path2)
