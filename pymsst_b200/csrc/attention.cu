@@ -1286,6 +1286,36 @@ struct Layout {
   static constexpr int SMEM = OFF_X + kXBufs * kXBytes + 1024;
   static_assert(SMEM <= 232448 - 64, "fused backward shared memory");
 };
+
+// Packed pairs keep the rotary angles of a thread's own row in the free TMEM
+// columns: every item puts position row & 63 in TMEM lane `row`, so lane
+// `row` holds cos of pairs 0..31 at columns kTmemRot.. and sin at
+// kTmemRot + 32..; a thread's half reads its 16 pairs of each.
+constexpr uint32_t kTmemRot = 448;
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+      "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+      "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15]))
+      : "memory");
+}
+
+// unrotate32 with the thread's 16 angle pairs already loaded (c, s)
+__device__ __forceinline__ void unrotate32_regs(uint32_t (&a)[32], const uint32_t (&c)[16], const uint32_t (&sn)[16]) {
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const float cc = __uint_as_float(c[j]), ss = __uint_as_float(sn[j]);
+    const float e = __uint_as_float(a[2 * j]), o = __uint_as_float(a[2 * j + 1]);
+    a[2 * j] = __float_as_uint(fmaf(e, cc, o * ss));
+    a[2 * j + 1] = __float_as_uint(fmaf(o, cc, -e * ss));
+  }
+}
 }  // namespace bf
 
 template <typename T, bool kPack>
@@ -1432,6 +1462,18 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         *reinterpret_cast<uint4*>(smem + L::OFF_PT + off) = make_uint4(0, 0, 0, 0);
         *reinterpret_cast<uint4*>(smem + L::OFF_DST + off) = make_uint4(0, 0, 0, 0);
       }
+      if (rcos != nullptr) {  // this row's angle pairs into its TMEM lane, once for all items
+        float cv[16], sv[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const bool ok = pos < N;
+          cv[j] = ok ? __ldg(rcos + pos * 32 + half * 16 + j) : 1.f;
+          sv[j] = ok ? __ldg(rsin + pos * 32 + half * 16 + j) : 0.f;
+        }
+        tmem_st16(tmem + lane_off + kTmemRot + half * 16, cv);
+        tmem_st16(tmem + lane_off + kTmemRot + 32 + half * 16, sv);
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      }
     }
     // query columns of this thread: packed, 32 of its own sequence's block; otherwise 64 in two passes
     constexpr int npass = pack ? 1 : 2;
@@ -1565,8 +1607,17 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const int64_t rq = seq * pdq.s_b + h * pdq.s_h + (int64_t)pos * pdq.s_n + half * 32;
         store_row32<T>(dv + rv, gv, 1.f);
         if (rcos != nullptr) {
-          unrotate32(gk, rcos, rsin, pos, half);
-          unrotate32(gq, rcos, rsin, pos, half);
+          if constexpr (pack) {
+            uint32_t cr[16], sr[16];
+            tmem_ld16_nowait(tmem + lane_off + kTmemRot + half * 16, cr);
+            tmem_ld16_nowait(tmem + lane_off + kTmemRot + 32 + half * 16, sr);
+            tmem_wait16(cr, sr);
+            unrotate32_regs(gk, cr, sr);
+            unrotate32_regs(gq, cr, sr);
+          } else {
+            unrotate32(gk, rcos, rsin, pos, half);
+            unrotate32(gq, rcos, rsin, pos, half);
+          }
         }
         store_row32<T>(dk + rk, gk, scale);
         store_row32<T>(dq + rq, gq, scale);
