@@ -122,13 +122,13 @@ __global__ void __launch_bounds__(kThreads)
 // Its gradient with respect to the frames: each frame element (k, t) was
 // added into exactly one output sample, p = t*hop + k:
 //   grad_frames[k * T + t] = grad_y[p - n/2] w[k] / env[p]  (0 outside the trimmed range)
-// grid (n * T / 256, batch), consecutive threads take consecutive t.
+// grid (T / 256, n, batch): consecutive threads take consecutive t of one k (no index division).
 __global__ void __launch_bounds__(kThreads)
     istft_ola_bwd(const float* __restrict__ grad_y, const float* __restrict__ window, float* __restrict__ grad_frames,
                   int n, int T, int hop, int len) {
-  const int e = blockIdx.x * kThreads + threadIdx.x;
-  if (e >= n * T) return;
-  const int k = e / T, t = e - k * T;
+  const int t = blockIdx.x * kThreads + threadIdx.x, k = blockIdx.y;
+  if (t >= T) return;
+  const int64_t e = (int64_t)k * T + t;
   const int p = t * hop + k, i = p - n / 2;
   float g = 0.f;
   if (i >= 0 && i < len) {
@@ -140,9 +140,9 @@ __global__ void __launch_bounds__(kThreads)
       const float w = window[p - u * hop];
       env = fmaf(w, w, env);
     }
-    g = grad_y[(int64_t)blockIdx.y * len + i] * window[k] / env;
+    g = grad_y[(int64_t)blockIdx.z * len + i] * window[k] / env;
   }
-  grad_frames[(int64_t)blockIdx.y * n * T + e] = g;
+  grad_frames[(int64_t)blockIdx.z * n * T + e] = g;
 }
 
 }  // namespace
@@ -179,7 +179,8 @@ extern "C" int pmb_istft_overlap_add_backward(const float* grad_y, const float* 
   PMB_REQUIRE(n_fft * num_frames < ((int64_t)1 << 31) && length < (1 << 30) && batch <= 65535, "%s: too large", name);
   if (batch == 0) return PMB_OK;
   PMB_REQUIRE(grad_y && window && grad_frames, "%s: NULL argument", name);
-  const dim3 grid((unsigned)((n_fft * num_frames + kThreads - 1) / kThreads), (unsigned)batch);
+  PMB_REQUIRE(n_fft <= 65535, "%s: n_fft above 65535", name);
+  const dim3 grid((unsigned)((num_frames + kThreads - 1) / kThreads), (unsigned)n_fft, (unsigned)batch);
   istft_ola_bwd<<<grid, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(grad_y, window, grad_frames, (int)n_fft,
                                                                           (int)num_frames, (int)hop, (int)length);
   PMB_CHECK_LAUNCH(name);
