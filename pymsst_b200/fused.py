@@ -346,6 +346,14 @@ class OutProjFn(torch.autograd.Function):
         return g, g_gated, g_w
 
 
+def _weight_grad(a: torch.Tensor, b: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    """a @ b as the gradient of a parameter of type ``dtype``: for fp32 parameters and 16-bit operands one GEMM
+    with an fp32 result (cuBLAS accumulates in fp32 either way), instead of a 16-bit product and a cast kernel."""
+    if dtype == torch.float32 and a.dtype in (torch.bfloat16, torch.float16) and a.is_cuda:
+        return torch.mm(a, b, out_dtype=torch.float32)
+    return torch.matmul(a, b).to(dtype)
+
+
 def _input_grad(gqkv, w, gx_pass, shape):
     """gqkv W, plus the gradient that reached the input through its pass-through output (the head gate's input
     gradient) as the GEMM's C operand: one GEMM instead of a GEMM and an elementwise sum."""
@@ -431,7 +439,7 @@ class QKVRotaryFn(torch.autograd.Function):
             strides[0], strides[1], strides[2], ctx.inner, nat.stream_handle(device),
         )
         gx = _input_grad(gqkv, w, gx_pass, (b, n, -1)) if ctx.needs_input_grad[0] else None
-        gw = torch.matmul(gqkv.t(), x2).to(ctx.weight_dtype) if ctx.needs_input_grad[1] else None
+        gw = _weight_grad(gqkv.t(), x2, ctx.weight_dtype) if ctx.needs_input_grad[1] else None
         return gx, gw, None, None, None, None, None, None, None
 
 
@@ -478,13 +486,13 @@ class FeedForwardFn(torch.autograd.Function):
         ws = nat.workspace(wsb, device)
         nat.call("pmb_column_sum", g.data_ptr(), rows, dim, gb2.data_ptr(), nat.dtype_code(dts[3]),
                  nat.dtype_code(dt), ws.data_ptr(), wsb, st)
-        gw2 = torch.matmul(g.t(), act).to(dts[2])
+        gw2 = _weight_grad(g.t(), act, dts[2])
         da = torch.matmul(g, w2c)
         dpre = torch.empty_like(pre)
         gb1 = torch.empty(hidden, dtype=dts[1], device=device)
         nat.call("pmb_gelu_backward", da.data_ptr(), pre.data_ptr(), dpre.data_ptr(), rows, hidden, gb1.data_ptr(),
                  nat.dtype_code(dts[1]), nat.dtype_code(dt), ws.data_ptr(), wsb, st)
-        gw1 = torch.matmul(dpre.t(), xn).to(dts[0])
+        gw1 = _weight_grad(dpre.t(), xn, dts[0])
         gx = torch.matmul(dpre, w1c) if ctx.needs_input_grad[0] else None
         return gx, gw1, gb1, gw2, gb2
 
@@ -675,7 +683,7 @@ class QKVAttentionFn(torch.autograd.Function):
         else:
             nat.call("pmb_attention_backward", *head, dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), *tail)
         gx = _input_grad(gqkv, w, gx_pass, (b, n, -1)) if ctx.needs_input_grad[0] else None
-        gw = torch.matmul(gqkv.t(), x2).to(ctx.weight_dtype) if ctx.needs_input_grad[1] else None
+        gw = _weight_grad(gqkv.t(), x2, ctx.weight_dtype) if ctx.needs_input_grad[1] else None
         return gx, gw, None, None, None, None, None, None
 
 
@@ -762,8 +770,8 @@ class QKVAttentionGateFn(torch.autograd.Function):
         if ctx.needs_input_grad[0]:
             gx = torch.matmul(ext, torch.cat([w, wg], 0)).reshape(b, n, -1)
         if ctx.needs_input_grad[1] or ctx.needs_input_grad[7]:
-            gw_ext = torch.matmul(ext.t(), x2)
-            gw = gw_ext[:3 * inner].to(ctx.dtypes[0])
+            gw_ext = _weight_grad(ext.t(), x2, ctx.dtypes[0])
+            gw = gw_ext[:3 * inner]
             gwg = gw_ext[3 * inner:].to(ctx.dtypes[1])
         if ctx.needs_input_grad[8]:
             gbg = bpart.view(-1, h, 4).sum((0, 2)).to(ctx.dtypes[2])
