@@ -1603,22 +1603,26 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       warp_arrive(acc_empty, false);
       if (valid) {
         const int64_t rv = seq * pdv.s_b + h * pdv.s_h + (int64_t)pos * pdv.s_n + half * 32;
+        store_row32<T>(dv + rv, gv, 1.f);
+      }
+      if (rcos != nullptr) {
+        if constexpr (pack) {
+          // tcgen05.ld is warp-collective: every lane loads (rows past the sequence read the
+          // identity angles the prologue wrote), only the valid rows store below
+          uint32_t cr[16], sr[16];
+          tmem_ld16_nowait(tmem + lane_off + kTmemRot + half * 16, cr);
+          tmem_ld16_nowait(tmem + lane_off + kTmemRot + 32 + half * 16, sr);
+          tmem_wait16(cr, sr);
+          unrotate32_regs(gk, cr, sr);
+          unrotate32_regs(gq, cr, sr);
+        } else if (valid) {
+          unrotate32(gk, rcos, rsin, pos, half);
+          unrotate32(gq, rcos, rsin, pos, half);
+        }
+      }
+      if (valid) {
         const int64_t rk = seq * pdk.s_b + h * pdk.s_h + (int64_t)pos * pdk.s_n + half * 32;
         const int64_t rq = seq * pdq.s_b + h * pdq.s_h + (int64_t)pos * pdq.s_n + half * 32;
-        store_row32<T>(dv + rv, gv, 1.f);
-        if (rcos != nullptr) {
-          if constexpr (pack) {
-            uint32_t cr[16], sr[16];
-            tmem_ld16_nowait(tmem + lane_off + kTmemRot + half * 16, cr);
-            tmem_ld16_nowait(tmem + lane_off + kTmemRot + 32 + half * 16, sr);
-            tmem_wait16(cr, sr);
-            unrotate32_regs(gk, cr, sr);
-            unrotate32_regs(gq, cr, sr);
-          } else {
-            unrotate32(gk, rcos, rsin, pos, half);
-            unrotate32(gq, rcos, rsin, pos, half);
-          }
-        }
         store_row32<T>(dk + rk, gk, scale);
         store_row32<T>(dq + rq, gq, scale);
       }
