@@ -104,12 +104,27 @@ inline int make_maps(CUtensorMap& ma, CUtensorMap& mb, const void* a, int64_t ld
   return st;
 }
 
+// Resident-B variant (gemm_umma.cuh): 256-wide N blocks with K <= 192, the whole B block of a CTA (96 KB) kept
+// in shared memory beside a 4-slot ring of A; operand traffic per tile drops from 144 KB to 48 KB at K = 192.
+constexpr int kResKB = 3;
+constexpr int kResStages = 4;
+
 template <int BN, bool A_MN, bool B_MN, class Epi>
 int launch(const CUtensorMap& ma, const CUtensorMap& mb, ugemm::Plan& plan, const Epi& epi, int fp16,
            cudaStream_t stream, const char* name) {
   constexpr int STAGES = stages_for<BN>();
   const int tiles = ugemm::build_plan(plan, BN);
   if (tiles == 0) return PMB_OK;
+  if constexpr (BN == 256) {
+    if (plan.num_groups == 1 && plan.g[0].k <= kResKB * ugemm::BK) {
+      auto kern = ugemm::umma_gemm_kernel<BN, kResStages, A_MN, B_MN, Epi, kResKB>;
+      const int smem = ugemm::smem_bytes<BN, kResStages, kResKB>();
+      PMB_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem), name);
+      kern<<<ugemm::persistent_grid(tiles), ugemm::kThreads, smem, stream>>>(ma, mb, plan, epi, fp16);
+      PMB_CHECK_LAUNCH(name);
+      return PMB_OK;
+    }
+  }
   auto kern = ugemm::umma_gemm_kernel<BN, STAGES, A_MN, B_MN, Epi>;
   const int smem = ugemm::smem_bytes<BN, STAGES>();
   PMB_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem), name);

@@ -94,10 +94,20 @@ struct Config {
   static_assert(2 * BN <= 512, "two accumulators must fit the 512 tensor-memory columns");
 };
 
-template <int BN, int STAGES>
+// RES_KB > 0: B resident in shared memory (RES_KB k-blocks of one N block), ring slots hold A only.
+template <int BN, int STAGES, int RES_KB = 0>
 constexpr int smem_bytes() {
-  return STAGES * (BM * BK * 2 + BN * BK * 2) + kEpiWarps * kStageWarpBytes + 1024 /*alignment slack*/ +
-         256 /*barriers*/;
+  return STAGES * (BM * BK * 2 + (RES_KB > 0 ? 0 : BN * BK * 2)) + RES_KB * BN * BK * 2 +
+         kEpiWarps * kStageWarpBytes + 1024 /*alignment slack*/ + 256 /*barriers*/;
+}
+
+// Resident-B schedule: CTA c serves N block c % ntn only (ntn = N blocks of the single group) and walks the M
+// tiles of that block; its tiles are c, c + step, ... with step = (CTAs on that block) * ntn, so every tile of
+// the plan is covered once.  Every role of the CTA computes the same step.
+__device__ __forceinline__ int resident_step(const Plan& plan, int bn) {
+  const int ntn = (plan.g[0].n + bn - 1) / bn;
+  const int nb = (int)blockIdx.x % ntn;
+  return ((int)gridDim.x - nb + ntn - 1) / ntn * ntn;
 }
 
 // Per-warp view handed to epilogues.  Each thread owns one accumulator row;
@@ -297,23 +307,31 @@ __device__ __forceinline__ void warp_tma_store(const TileCtx& t, const float (&v
 }
 
 // ------------------------------------------------------------------ kernel
-template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi>
+// RES_KB > 0 (single-group plans with K <= RES_KB * BK, the host checks): each CTA loads the B block of its N
+// block once (resident_step schedule) and the ring streams only A, so a tile moves 128 x K instead of
+// (128 + BN) x K operand bytes from L2; for K = 192, BN = 256 a third.
+template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi, int RES_KB = 0>
 __global__ void __launch_bounds__(kThreads, 1)
     umma_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ Plan plan, const __grid_constant__ Epi epi, int fp16) {
   using C = Config<BN, A_MN, B_MN>;
-  static_assert(smem_bytes<BN, STAGES>() <= kMaxSmemBytes, "stage ring + staging blocks exceed shared memory");
+  static_assert(smem_bytes<BN, STAGES, RES_KB>() <= kMaxSmemBytes, "stage ring + staging blocks exceed shared memory");
+  constexpr int SLOT = RES_KB > 0 ? C::A_BYTES : C::STAGE_BYTES;  // bytes a ring slot carries
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* staging = smem + STAGES * C::STAGE_BYTES;
+  uint8_t* bres_smem = smem + STAGES * SLOT;  // resident B: RES_KB k-blocks of C::B_BYTES
+  uint8_t* staging = bres_smem + RES_KB * C::B_BYTES;
   uint64_t* full = reinterpret_cast<uint64_t*>(staging + kEpiWarps * kStageWarpBytes);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;  // [2] accumulator ready (MMA -> epilogue)
   uint64_t* tempty = tfull + 2;      // [2] accumulator drained (epilogue -> MMA)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* bres = tempty + 2;       // resident B loaded (producer -> MMA)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bres + 1);
   __shared__ volatile int abort_flag;
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  int step = gridDim.x;  // tile stride of this CTA
+  if constexpr (RES_KB > 0) step = resident_step(plan, BN);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -324,6 +342,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       umma::mbar_init(&tfull[b], 1);
       umma::mbar_init(&tempty[b], kEpiWarps);
     }
+    umma::mbar_init(bres, 1);
     umma::fence_barrier_init();
     abort_flag = 0;
     umma::tma_prefetch(&tmA);
@@ -338,8 +357,29 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- TMA producer
+      // B block (k-block kb at b_dst) of the N block at n0
+      auto load_b = [&](uint8_t* b_dst, uint64_t* bar, const Group& G, int k0, int n0) {
+        if (!B_MN) {
+          umma::tma_load_3d(b_dst, &tmB, bar, k0 + G.b_inner, G.b_mid, n0 + G.b_outer);
+        } else {
+#pragma unroll
+          for (int c = 0; c < BN / 64; ++c)
+            umma::tma_load_3d(b_dst + c * 64 * BK * 2, &tmB, bar, n0 + c * 64 + G.b_inner, G.b_mid,
+                              k0 + G.b_outer);
+        }
+      };
+      if constexpr (RES_KB > 0) {
+        if ((int)blockIdx.x < plan.total_tiles) {
+          int gi, m0, n0;
+          locate(plan, blockIdx.x, BN, gi, m0, n0);
+          const Group& G = plan.g[gi];
+          const int kblocks = (G.k + BK - 1) / BK;  // <= RES_KB
+          umma::mbar_arrive_expect_tx(bres, kblocks * C::B_BYTES);
+          for (int kb = 0; kb < kblocks; ++kb) load_b(bres_smem + kb * C::B_BYTES, bres, G, kb * BK, n0);
+        }
+      }
       uint32_t it = 0;
-      for (int tile = blockIdx.x; tile < plan.total_tiles && !abort_flag; tile += gridDim.x) {
+      for (int tile = blockIdx.x; tile < plan.total_tiles && !abort_flag; tile += step) {
         int gi, m0, n0;
         locate(plan, tile, BN, gi, m0, n0);
         const Group& G = plan.g[gi];
@@ -351,9 +391,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             abort_flag = 1;
             break;
           }
-          uint8_t* a_dst = smem + s * C::STAGE_BYTES;
-          uint8_t* b_dst = a_dst + C::A_BYTES;
-          umma::mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
+          uint8_t* a_dst = smem + s * SLOT;
+          umma::mbar_arrive_expect_tx(&full[s], SLOT);
           const int k0 = kb * BK;
           if (!A_MN) {
             umma::tma_load_3d(a_dst, &tmA, &full[s], k0 + G.a_inner, G.a_mid, m0 + G.a_outer);
@@ -363,14 +402,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               umma::tma_load_3d(a_dst + c * 64 * BK * 2, &tmA, &full[s], m0 + c * 64 + G.a_inner, G.a_mid,
                                 k0 + G.a_outer);
           }
-          if (!B_MN) {
-            umma::tma_load_3d(b_dst, &tmB, &full[s], k0 + G.b_inner, G.b_mid, n0 + G.b_outer);
-          } else {
-#pragma unroll
-            for (int c = 0; c < BN / 64; ++c)
-              umma::tma_load_3d(b_dst + c * 64 * BK * 2, &tmB, &full[s], n0 + c * 64 + G.b_inner, G.b_mid,
-                                k0 + G.b_outer);
-          }
+          if constexpr (RES_KB == 0) load_b(a_dst + C::A_BYTES, &full[s], G, k0, n0);
         }
       }
     }
@@ -378,8 +410,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       // ---------------- MMA issuer
       const uint32_t idesc = fp16 ? C::IDESC_F16 : C::IDESC_BF16;
+      if constexpr (RES_KB > 0) {
+        if ((int)blockIdx.x < plan.total_tiles && !umma::mbar_wait(bres, 0, 5)) abort_flag = 1;
+      }
       uint32_t it = 0, local = 0;
-      for (int tile = blockIdx.x; tile < plan.total_tiles && !abort_flag; tile += gridDim.x, ++local) {
+      for (int tile = blockIdx.x; tile < plan.total_tiles && !abort_flag; tile += step, ++local) {
         int gi, m0, n0;
         locate(plan, tile, BN, gi, m0, n0);
         const int kblocks = (plan.g[gi].k + BK - 1) / BK;
@@ -400,8 +435,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           umma::tc_fence_after();
-          const uint32_t a_base = umma::smem_u32(smem + s * C::STAGE_BYTES);
-          const uint32_t b_base = a_base + C::A_BYTES;
+          const uint32_t a_base = umma::smem_u32(smem + s * SLOT);
+          const uint32_t b_base = RES_KB > 0 ? umma::smem_u32(bres_smem + kb * C::B_BYTES) : a_base + C::A_BYTES;
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
             uint64_t da, db;
@@ -456,12 +491,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     if constexpr (HasPre<Epi>::value) {
       if ((int)blockIdx.x < plan.total_tiles) epi.prefetch(plan, ctx_of(blockIdx.x, 0), pre_cur);
     }
-    for (int tile = blockIdx.x; tile < plan.total_tiles; tile += gridDim.x, ++local) {
+    for (int tile = blockIdx.x; tile < plan.total_tiles; tile += step, ++local) {
       if (abort_flag) break;
       const uint32_t buf = local & 1, use = local >> 1;
       if constexpr (HasPre<Epi>::value) {  // the next tile's loads, in flight while this one drains
-        if (tile + (int)gridDim.x < plan.total_tiles)
-          epi.prefetch(plan, ctx_of(tile + gridDim.x, buf ^ 1), pre_next);
+        if (tile + step < plan.total_tiles) epi.prefetch(plan, ctx_of(tile + step, buf ^ 1), pre_next);
       }
       if (!umma::mbar_wait(&tfull[buf], use & 1, 3)) {
         abort_flag = 1;

@@ -30,7 +30,10 @@ def _padded(t, device):
     return store.to(device)[:, : t.shape[1]]
 
 
-@pytest.mark.parametrize("m,n,k", [(128, 128, 64), (1000, 192, 768), (130, 70, 100), (4096, 1536, 192), (64, 8, 16)])
+# (4096, 1536, 192), (9000, 768, 192), (1000, 600, 72) and (300, 129, 40) run the resident-B schedule (K <= 192,
+# 256-wide N blocks): N blocks that do not divide the 148-CTA grid, ragged M / N tails, K below one k-block
+@pytest.mark.parametrize("m,n,k", [(128, 128, 64), (1000, 192, 768), (130, 70, 100), (4096, 1536, 192), (64, 8, 16),
+                                   (9000, 768, 192), (1000, 600, 72), (300, 129, 40)])
 @pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, False), (True, True)])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_gemm_tc_matches_reference(cuda_device, m, n, k, a_mn, b_mn, dtype):
