@@ -22,12 +22,38 @@ __device__ __forceinline__ float load_dyn(const void* p, int64_t i, int code) {
   }
 }
 
+// Bias values of a tile, loaded one tile ahead through the engine's prefetch hook (gemm_umma.cuh: `Pre`,
+// `prefetch`): lane l of a warp holds bias[n0 + c0 + l] for each of the warp's 32-column chunks c0 = 32 * (sub +
+// q * kSubs), q < kBiasChunks, so no chunk waits on a global load after its accumulator read.
+constexpr int kBiasChunks = (256 / 32 + ugemm::kSubs - 1) / ugemm::kSubs;
+struct BiasPre {
+  float b[kBiasChunks];
+};
+template <class Load>
+__device__ __forceinline__ void prefetch_bias(const ugemm::TileCtx& t, BiasPre& p, Load&& load) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int q = 0; q < kBiasChunks; ++q) {
+    const int c = 32 * (t.sub + q * ugemm::kSubs) + lane;  // column within the tile
+    p.b[q] = c < t.n_valid ? load(t.n0 + c) : 0.f;
+  }
+}
+// chunk q's value (q < kBiasChunks) without a dynamically indexed register array
+__device__ __forceinline__ float bias_of(const BiasPre& p, int q) {
+  static_assert(kBiasChunks == 3, "bias_of selects among three chunks");
+  return q == 0 ? p.b[0] : (q == 1 ? p.b[1] : p.b[2]);
+}
+
 // C = act(acc + bias) in TC, row stride ldc.  With `slices` set, group g of
 // the plan writes slice g (slice_elems apart): the split-K partials.  16-bit
 // outputs with `use_tma` are written by TMA tile stores through `out_map`
 // (tma::make_store_map_2d over C).
 template <typename TC>
 struct DenseEpi {
+  // the resident-B schedule (dense::launch) measured 57.4 -> 51.2 us on [63984 x 192] x [192 x 1536]; epilogues
+  // without this member keep the interleaved schedule (the rotary QKV epilogue measured 79.9 -> 88.1 us under it:
+  // its rotating N blocks all landed on two thirds of the CTAs)
+  static constexpr bool kResidentB = true;
   TC* c;
   int64_t ldc;
   const void* bias;
@@ -36,18 +62,22 @@ struct DenseEpi {
   int64_t slice_elems;
   int use_tma;
   CUtensorMap out_map;
+  using Pre = BiasPre;
+  __device__ void prefetch(const ugemm::Plan&, const ugemm::TileCtx& t, Pre& p) const {
+    prefetch_bias(t, p, [&](int64_t col) { return bias ? load_dyn(bias, col, bias_dtype) : 0.f; });
+  }
   template <int BN>
-  __device__ void run(const ugemm::Plan&, const ugemm::TileCtx& t) const {
+  __device__ void run(const ugemm::Plan&, const ugemm::TileCtx& t, const Pre& pre) const {
     TC* base = c + (int64_t)t.group * slice_elems + (int64_t)t.row0 * ldc + t.n0;
-    const int lane = threadIdx.x & 31;
+    int q = 0;
 #pragma unroll 1
-    for (int c0 = 32 * t.sub; c0 < BN; c0 += 32 * ugemm::kSubs) {
+    for (int c0 = 32 * t.sub; c0 < BN; c0 += 32 * ugemm::kSubs, ++q) {
       if (c0 >= t.n_valid) break;
       const int ncols = min(32, t.n_valid - c0);
       float v[32];
       umma::tmem_ld32(t.taddr + c0, v);
       if (bias) {
-        const float bl = lane < ncols ? load_dyn(bias, t.n0 + c0 + lane, bias_dtype) : 0.f;
+        const float bl = bias_of(pre, q);
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] += __shfl_sync(0xffffffffu, bl, j);
       }
@@ -106,8 +136,14 @@ inline int make_maps(CUtensorMap& ma, CUtensorMap& mb, const void* a, int64_t ld
 
 // Resident-B variant (gemm_umma.cuh): 256-wide N blocks with K <= 192, the whole B block of a CTA (96 KB) kept
 // in shared memory beside a 4-slot ring of A; operand traffic per tile drops from 144 KB to 48 KB at K = 192.
+// Taken for epilogues that declare `static constexpr bool kResidentB = true`.
 constexpr int kResKB = 3;
 constexpr int kResStages = 4;
+
+template <class E, class = void>
+struct WantsResidentB : std::false_type {};
+template <class E>
+struct WantsResidentB<E, std::void_t<decltype(E::kResidentB)>> : std::bool_constant<E::kResidentB> {};
 
 template <int BN, bool A_MN, bool B_MN, class Epi>
 int launch(const CUtensorMap& ma, const CUtensorMap& mb, ugemm::Plan& plan, const Epi& epi, int fp16,
@@ -115,7 +151,7 @@ int launch(const CUtensorMap& ma, const CUtensorMap& mb, ugemm::Plan& plan, cons
   constexpr int STAGES = stages_for<BN>();
   const int tiles = ugemm::build_plan(plan, BN);
   if (tiles == 0) return PMB_OK;
-  if constexpr (BN == 256) {
+  if constexpr (BN == 256 && WantsResidentB<Epi>::value) {
     if (plan.num_groups == 1 && plan.g[0].k <= kResKB * ugemm::BK) {
       auto kern = ugemm::umma_gemm_kernel<BN, kResStages, A_MN, B_MN, Epi, kResKB>;
       const int smem = ugemm::smem_bytes<BN, kResStages, kResKB>();

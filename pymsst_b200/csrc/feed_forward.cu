@@ -35,17 +35,21 @@ struct GeluEpi {
   int64_t ld;
   int use_tma;
   CUtensorMap pre_map, act_map;
+  using Pre = dense::BiasPre;  // the bias slice, loaded a tile ahead
+  __device__ void prefetch(const ugemm::Plan&, const ugemm::TileCtx& t, Pre& p) const {
+    dense::prefetch_bias(t, p, [&](int64_t col) { return Elem<TP>::to_f(bias[col]); });
+  }
   template <int BN>
-  __device__ void run(const ugemm::Plan&, const ugemm::TileCtx& t) const {
-    const int lane = threadIdx.x & 31;
+  __device__ void run(const ugemm::Plan&, const ugemm::TileCtx& t, const Pre& bp) const {
     const int64_t base = (int64_t)t.row0 * ld + t.n0;
+    int q = 0;
 #pragma unroll 1
-    for (int c0 = 32 * t.sub; c0 < BN; c0 += 32 * ugemm::kSubs) {
+    for (int c0 = 32 * t.sub; c0 < BN; c0 += 32 * ugemm::kSubs, ++q) {
       if (c0 >= t.n_valid) break;
       const int ncols = min(32, t.n_valid - c0);
       float v[32];
       umma::tmem_ld32(t.taddr + c0, v);
-      const float bl = lane < ncols ? Elem<TP>::to_f(bias[t.n0 + c0 + lane]) : 0.f;
+      const float bl = dense::bias_of(bp, q);
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = round_to<T>(v[j] + __shfl_sync(0xffffffffu, bl, j));
       if (use_tma) {
