@@ -32,12 +32,22 @@ struct Elem<__half> {
   static constexpr int code = PMB_FLOAT16;
   __device__ __forceinline__ static float to_f(__half v) { return __half2float(v); }
   __device__ __forceinline__ static __half from_f(float v) { return __float2half_rn(v); }
+  // (a, b) rounded to nearest even in one instruction, a in the low half (memory order)
+  __device__ __forceinline__ static uint32_t pack2(float a, float b) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
 };
 template <>
 struct Elem<__nv_bfloat16> {
   static constexpr int code = PMB_BFLOAT16;
   __device__ __forceinline__ static float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
   __device__ __forceinline__ static __nv_bfloat16 from_f(float v) { return __float2bfloat16_rn(v); }
+  // (a, b) rounded to nearest even in one instruction, a in the low half (memory order)
+  __device__ __forceinline__ static uint32_t pack2(float a, float b) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
 };
 
 template <typename T>

@@ -53,7 +53,8 @@ struct DenseEpi {
   // the resident-B schedule (dense::launch) measured 57.4 -> 51.2 us on [63984 x 192] x [192 x 1536]; epilogues
   // without this member keep the interleaved schedule (the rotary QKV epilogue measured 79.9 -> 88.1 us under it:
   // its rotating N blocks all landed on two thirds of the CTAs)
-  static constexpr bool kResidentB = true;
+  // (16-bit outputs only: the fp32 variant spilled 4 bytes under the resident schedule)
+  static constexpr bool kResidentB = sizeof(TC) == 2;
   TC* c;
   int64_t ldc;
   const void* bias;

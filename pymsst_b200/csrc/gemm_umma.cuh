@@ -288,13 +288,14 @@ __device__ __forceinline__ void warp_tma_store(const TileCtx& t, const float (&v
   // the store that last used this buffer (kStoreBufs stores ago) has finished reading it
   if (lane == 0) asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(kStoreBufs - 1) : "memory");
   __syncwarp();
-  T pack[32];
+  uint32_t pk[16];  // two values per conversion instruction
 #pragma unroll
-  for (int j = 0; j < 32; ++j) pack[j] = Elem<T>::from_f(v[j]);
+  for (int j = 0; j < 16; ++j) pk[j] = Elem<T>::pack2(v[2 * j], v[2 * j + 1]);
   const int sw = (lane >> 1) & 3;
 #pragma unroll
   for (int q = 0; q < 4; ++q)
-    *reinterpret_cast<uint4*>(box + lane * 64 + ((q ^ sw) << 4)) = reinterpret_cast<const uint4*>(pack)[q];
+    *reinterpret_cast<uint4*>(box + lane * 64 + ((q ^ sw) << 4)) =
+        make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   __syncwarp();
   if (lane == 0) {
