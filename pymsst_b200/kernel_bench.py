@@ -336,6 +336,26 @@ def _op_qkv_attention(bench: _Bench):
     bench.time(f"qkv+attention+gate fwd+bwd n={n} (QKVAttentionFn + AttentionGateFn)", gate_apart, byg)
 
 
+def op_attn_gated(bench: _Bench):
+    """The band-axis attention of the training step alone: projection, rotary, attention and head gate forward and
+    backward through QKVAttentionGateFn (62 positions); its first backward launch is the gated one-pass kernel."""
+    from .fused import QKVAttentionGateFn, rotary_tables
+
+    dev, bf = bench.device, torch.bfloat16
+    nb, n = ROWS // 62, 62
+    x = torch.randn(nb, n, DIM, device=dev, dtype=bf).requires_grad_()
+    w = (torch.randn(3 * HEADS * DHEAD, DIM, device=dev) / DIM ** 0.5).requires_grad_()
+    wg = (torch.randn(HEADS, DIM, device=dev) / DIM ** 0.5).requires_grad_()
+    bg = torch.zeros(HEADS, device=dev).requires_grad_()
+    freqs = 1.0 / (10000 ** (torch.arange(0, DHEAD, 2, device=dev).float() / DHEAD))
+    cos, sin = rotary_tables(freqs, n, dev)
+    cos_t, sin_t = cos.t().contiguous(), sin.t().contiguous()
+    gg = torch.randn(ROWS, HEADS * DHEAD, device=dev, dtype=bf)
+    byg = ROWS * (DIM + 3 * HEADS * DHEAD) * 2 * 3 + ROWS * HEADS * DHEAD * 2 * 3
+    bench.time(f"qkv+attention+gate fwd+bwd n={n} (QKVAttentionGateFn)", lambda: _grads(
+        QKVAttentionGateFn.apply(x, w, cos, sin, cos_t, sin_t, HEADS, wg, bg), [x, w, wg, bg], gg), byg)
+
+
 def op_band(bench: _Bench):
     """BandSplit (config-3 bands: 62 bands over 1025 stereo complex bins, 1032 rows, D = 192)."""
     _op_band_rows(bench, 1032)
@@ -500,7 +520,9 @@ def op_band_sweep(bench: _Bench):
 
 
 OPS = {"gate": op_gate, "band": op_band, "band8192": op_band_sweep, "mel": op_mel, "mask": op_mask, "rms": op_rms,
-       "qkv": op_qkv, "ff": op_ff, "sdpa": op_sdpa, "attn": op_attn, "stft": op_stft}
+       "qkv": op_qkv, "ff": op_ff, "sdpa": op_sdpa, "attn": op_attn, "attn_gated": op_attn_gated, "stft": op_stft}
+# ops that only isolate one case of another op (for profiler captures); run when named
+NAMED_ONLY = {"attn_gated"}
 
 
 # ---------------------------------------------------------------------------
@@ -595,7 +617,7 @@ def main(argv=None) -> None:
     with torch.cuda.stream(bench.stream):
         if args.sweep:
             run_sweep(bench)
-        for name in ([] if args.sweep else args.ops or list(OPS)):
+        for name in ([] if args.sweep else args.ops or [k for k in OPS if k not in NAMED_ONLY]):
             if name not in OPS:
                 raise SystemExit(f"unknown op {name!r}; choose from {', '.join(OPS)}")
             OPS[name](bench)
