@@ -8,6 +8,10 @@
 //             partial row; red::colsum_rows sums the partial rows in order.
 // The values are computed in fp32 from the stored 16-bit tensors and rounded
 // once, as torch's elementwise kernels do; the bias sums add the rounded gx.
+// Reference semantics: the nn.GELU() of pymss-core's FeedForward; the
+// reference's patch set (src/pymsst/training/fused_roformer.py:256-824:
+// BandSplit, rotary, RMSNorm, attention gates, MaskEstimator) leaves the
+// feed-forward block on torch.
 #include <initializer_list>
 
 #include "common.cuh"
