@@ -37,8 +37,15 @@ __global__ void __launch_bounds__(256) gelu_fwd_kernel(const T* __restrict__ x, 
     T* e = reinterpret_cast<T*>(&u);
     // (the packed two-value form measured 2 us slower here than the scalar one: unlike the derivative, the
     // forward has too little arithmetic per value to pay for the register pairing)
+    if constexpr (sizeof(T) == 2) {  // outputs rounded in pairs (one conversion instruction per two values)
+      uint32_t* w = reinterpret_cast<uint32_t*>(&u);
 #pragma unroll
-    for (int j = 0; j < N; ++j) e[j] = Elem<T>::from_f(gelu_of<T>(Elem<T>::to_f(e[j])));
+      for (int j = 0; j < N; j += 2)
+        w[j / 2] = Elem<T>::pack2(gelu_of<T>(Elem<T>::to_f(e[j])), gelu_of<T>(Elem<T>::to_f(e[j + 1])));
+    } else {
+#pragma unroll
+      for (int j = 0; j < N; ++j) e[j] = Elem<T>::from_f(gelu_of<T>(Elem<T>::to_f(e[j])));
+    }
     reinterpret_cast<uint4*>(y)[i] = u;
   }
   // tail (n not a multiple of the vector width)
@@ -96,8 +103,7 @@ __global__ void __launch_bounds__(256, 3)
               float d0, d1, q0, q1;
               gelu_grad_fast2(Elem<T>::to_f(e[j]), Elem<T>::to_f(e[j + 1]), d0, d1);
               unpk2(mul2(pk2(Elem<T>::to_f(g[j]), Elem<T>::to_f(g[j + 1])), pk2(d0, d1)), q0, q1);
-              o[j] = Elem<T>::from_f(q0);
-              o[j + 1] = Elem<T>::from_f(q1);
+              reinterpret_cast<uint32_t*>(&uo)[j / 2] = Elem<T>::pack2(q0, q1);  // rounded as a pair
               acc[j] += Elem<T>::to_f(o[j]);
               acc[j + 1] += Elem<T>::to_f(o[j + 1]);
             }
