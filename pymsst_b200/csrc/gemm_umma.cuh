@@ -10,7 +10,8 @@
 //
 // Persistent, warp-specialised CTA of 448 threads, one per SM; CTA i takes
 // tiles i, i + grid, ... (tiles enumerated group by group, N fastest, so the
-// CTAs in flight share their A rows through L2):
+// CTAs in flight share their A rows through L2), or, with RES_KB > 0, only
+// the tiles of one N block whose B stays in shared memory (resident_step):
 //   warp 0 (one lane)   TMA producer into a STAGES-deep shared-memory ring
 //                       (full / empty mbarriers, running across tiles);
 //   warp 1 (one lane)   tcgen05.mma issuer (M = 128, N = BN, K = 16 per
