@@ -95,6 +95,9 @@ def work(name: str, a: tuple) -> tuple[float, float]:
         rows, nb, h, dt, pt = a[3], a[4], a[5], a[11], a[12]
         total = sum(_widths(a[6], nb))
         return rows * (2 * nb * h + 3 * total) * ES[dt] + 2 * 2 * total * (h + 1) * ES[pt], 8.0 * rows * h * total
+    if name == "pmb_gemm_tc":  # A [m, k] and B [n, k] read, C [m, n] written, the bias slice read
+        m, n, k, cd, bd, dt = a[12], a[13], a[14], a[8], a[10], a[15]
+        return (m * k + n * k) * ES[dt] + m * n * ES[cd] + (n * ES[bd] if a[9] else 0), 2.0 * m * n * k
     if name == "pmb_qkv_linear_rotary_forward":
         rows, dim, n, dt = a[4] * a[5], a[6], 3 * a[7] * a[8], a[13]
         return (rows * dim + n * dim + rows * n) * ES[dt] + 2 * a[5] * a[8] // 2 * 4, 2.0 * rows * n * dim
