@@ -153,7 +153,9 @@ int launch(const CUtensorMap& ma, const CUtensorMap& mb, ugemm::Plan& plan, cons
   const int tiles = ugemm::build_plan(plan, BN);
   if (tiles == 0) return PMB_OK;
   if constexpr (BN == 256 && WantsResidentB<Epi>::value) {
-    if (plan.num_groups == 1 && plan.g[0].k <= kResKB * ugemm::BK) {
+    // every N block needs a CTA of its own: more N blocks than CTAs keep the interleaved schedule
+    const int ntn = (plan.g[0].n + BN - 1) / BN;
+    if (plan.num_groups == 1 && plan.g[0].k <= kResKB * ugemm::BK && ntn <= ugemm::persistent_grid(tiles)) {
       auto kern = ugemm::umma_gemm_kernel<BN, kResStages, A_MN, B_MN, Epi, kResKB>;
       const int smem = ugemm::smem_bytes<BN, kResStages, kResKB>();
       PMB_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem), name);
