@@ -157,7 +157,8 @@ extern "C" int pmb_istft_overlap_add_forward(const float* frames, const int64_t*
   const char* name = "pmb_istft_overlap_add_forward";
   PMB_REQUIRE(batch >= 0 && n_fft > 0 && num_frames > 0 && hop > 0 && hop <= n_fft && length > 0,
               "%s: bad shape", name);
-  PMB_REQUIRE(n_fft * num_frames < ((int64_t)1 << 31) && length < (1 << 30) && batch <= 65535, "%s: too large", name);
+  PMB_REQUIRE((num_frames + 1) * n_fft < ((int64_t)1 << 31) && length < (1 << 30) && batch <= 65535,
+              "%s: too large", name);
   if (batch == 0) return PMB_OK;
   PMB_REQUIRE(frames && frame_strides && window && y, "%s: NULL argument", name);
   PMB_REQUIRE(frame_strides[0] >= 0 && frame_strides[1] >= 0 && frame_strides[2] >= 0, "%s: bad strides", name);
@@ -176,7 +177,9 @@ extern "C" int pmb_istft_overlap_add_backward(const float* grad_y, const float* 
   const char* name = "pmb_istft_overlap_add_backward";
   PMB_REQUIRE(batch >= 0 && n_fft > 0 && num_frames > 0 && hop > 0 && hop <= n_fft && length > 0,
               "%s: bad shape", name);
-  PMB_REQUIRE(n_fft * num_frames < ((int64_t)1 << 31) && length < (1 << 30) && batch <= 65535, "%s: too large", name);
+  // (num_frames + 1) * n_fft bounds the sample index t * hop + k of every frame element in 32 bits
+  PMB_REQUIRE((num_frames + 1) * n_fft < ((int64_t)1 << 31) && length < (1 << 30) && batch <= 65535,
+              "%s: too large", name);
   if (batch == 0) return PMB_OK;
   PMB_REQUIRE(grad_y && window && grad_frames, "%s: NULL argument", name);
   PMB_REQUIRE(n_fft <= 65535, "%s: n_fft above 65535", name);
